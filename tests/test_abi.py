@@ -1,0 +1,48 @@
+"""CPU: the C-ABI library builds, loads, and exports every entry point include/xtg_cuda.h declares; the session API
+mirrors npu/xtg_npu.h's (same names after the prefix, same arities); open fails cleanly (NULL + message) without a
+usable GPU. No compute call is made here."""
+import ctypes as C
+import re
+
+import pytest
+
+NPU_ABI = {  # npu/xtg_npu.h:23-47, name -> number of parameters
+    "open": 4, "info": 3, "forward": 8, "pos": 1, "rewind": 2, "snapshot_slots": 1, "snapshot_pos": 2,
+    "snapshot": 2, "restore": 2, "grow": 4, "debug_cache": 5, "close": 1,
+}
+
+
+def test_every_declared_symbol_is_exported(xtg):
+    L = xtg.lib()
+    declared = xtg.declared_symbols()
+    assert len(declared) >= 24
+    missing = [s for s in declared if not hasattr(L, s)]
+    assert not missing, missing
+
+
+def test_session_abi_mirrors_npu_plugin(xtg):
+    text = open(xtg.HEADER).read()
+    for name, nargs in NPU_ABI.items():
+        m = re.search(r"XTG_CUDA_API\s+[\w\*\s]+?\bxtg_cuda_%s\s*\(([^)]*)\)" % name, text)
+        assert m, name
+        args = [a for a in m.group(1).split(",") if a.strip()]
+        assert len(args) == nargs, (name, args)
+
+
+def test_open_without_gpu_reports_an_error(xtg):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: the GPU tests cover open")
+    err = C.create_string_buffer(512)
+    h = xtg.lib().xtg_cuda_open(b"synthetic", b"{}", err, len(err))
+    assert not h
+    assert err.value
+
+
+def test_open_rejects_unknown_models_and_bad_options(xtg):
+    L = xtg.lib()
+    err = C.create_string_buffer(512)
+    assert not L.xtg_cuda_open(b"/no/such/model", b"{}", err, len(err))
+    assert b"synthetic" in err.value
+    assert not L.xtg_cuda_open(b"synthetic", b"{\"kv_dtype\": \"bf16\"", err, len(err))
+    assert err.value

@@ -1,0 +1,272 @@
+"""GPU: the sm_100a kernels against the oracle (CPU restatement, itself pinned to the reference's outputs).
+
+Bars: integer / byte work bit-exact (generators, quantizer, int8 / FP8 KV encode); NVFP4
+GEMV and attention within 2e-3 relative error per output, floored by the outputs' RMS:
+    |gpu - oracle| <= 2e-3 * max(|oracle|, rms(oracle)).
+"""
+import math
+import os
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+import make_golden as G  # noqa: E402
+import oracle as O  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+TOL = 2e-3
+
+
+def close_rel(got, ref, tol=TOL):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    rms = math.sqrt((ref ** 2).mean())
+    bound = tol * np.maximum(np.abs(ref), rms)
+    worst = (np.abs(got - ref) / np.maximum(np.abs(ref), rms)).max()
+    return bool(np.all(np.abs(got - ref) <= bound)), worst
+
+
+@pytest.fixture(scope="module")
+def torch_mod():
+    import torch
+    assert torch.cuda.is_available()
+    return torch
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+# ---- generators and the quantizer: bit-exact ----
+
+def test_generators_bit_exact(cuda, xtg, torch_mod):
+    torch = torch_mod
+    n = 1 << 20
+    g = torch.empty(n, dtype=torch.int16, device="cuda")
+    xtg.gen(0, 3, 1234, 0.02, 0.0, g)
+    assert np.array_equal(g.cpu().numpy().view(np.uint16), O.gen_normal_bf16(3, 1234, 0.02, n))
+    u = torch.empty(n, dtype=torch.float32, device="cuda")
+    xtg.gen(1, 3, 77, 0.005, 0.02, u)
+    assert np.array_equal(u.cpu().numpy().view(np.uint32), O.gen_uniform(3, 77, 0.005, 0.02, n).view(np.uint32))
+    i8 = torch.empty(n, dtype=torch.int8, device="cuda")
+    xtg.gen(2, 5, 9, 0, 0, i8)
+    assert np.array_equal(i8.cpu().numpy(), O.gen_int8(5, 9, n))
+
+
+@pytest.mark.parametrize("n,k", [(96, 512), (9216, 3072), (3072, 9216), (70, 256)])
+def test_quantizer_bit_exact(cuda, xtg, torch_mod, n, k):
+    torch = torch_mod
+    raw, codes, scales, g = O.synth_weight(0, 30 + n, n, k)
+    dc, ds, dg = xtg.quantize_nvfp4(dev(torch, raw.view(np.int16)))
+    assert np.array_equal(dc.cpu().numpy(), codes)
+    assert np.array_equal(ds.cpu().numpy(), scales)
+    assert np.float32(dg.item()) == np.float32(g)
+
+
+# ---- the NVFP4 GEMV (matmul_nvfp4) ----
+
+def run_linear(xtg, torch, weights, x):
+    k = x.shape[1]
+    dw = [(dev(torch, c), dev(torch, s), g) for c, s, g in weights]
+    L = xtg.Linear(dw, k)
+    ys = L(dev(torch, x.astype(np.float32)))
+    out = [y.cpu().numpy() for y in ys]
+    L.close()
+    return out
+
+
+def test_gemv_reference_recipe(cuda, xtg, torch_mod):
+    """kernels_test.cpp:57-87's case (two fused weights 70x256 and 33x256, m in 1, 2, 7) against the reference's own
+    outputs (golden) and the oracle."""
+    gold = np.load(os.path.join(HERE, "golden", "nvfp4.npz"))
+    ws, x = G.fused_inputs()
+    for m in G.NVFP4_FUSED["ms"]:
+        ya, yb = run_linear(xtg, torch_mod, ws, x[:m])
+        ok, worst = close_rel(np.concatenate([ya.ravel(), yb.ravel()]),
+                              np.concatenate([gold[f"fused_m{m}_a"].ravel(), gold[f"fused_m{m}_b"].ravel()]))
+        assert ok, (m, worst)
+
+
+@pytest.mark.parametrize("n,k", [(9216, 3072), (3072, 9216)])
+@pytest.mark.parametrize("m", [1, 8])
+def test_gemv_config0(cuda, xtg, torch_mod, n, k, m):
+    """W ~ N(0, 0.02) quantized, x bf16 ~ N(0, 1)."""
+    raw, codes, scales, g = O.synth_weight(0, 7000 + n, n, k)
+    x = O.bf16_to_f32(O.gen_normal_bf16(0, 7100 + k, 1.0, 8 * k)).reshape(8, k)[:m]
+    got = run_linear(xtg, torch_mod, [(codes, scales, g)], x)[0]
+    ref = O.matmul_nvfp4([(codes, scales, g)], x)[0]
+    ok, worst = close_rel(got, ref)
+    assert ok, worst
+
+
+@pytest.mark.parametrize("m", [1, 8])
+def test_gemv_config1_projection_set(cuda, xtg, torch_mod, m):
+    """QKV (4608, fused), QKVG (7680), O, gate+up (fused), down; hidden 3072."""
+    H, F, Q, KV = 3072, 9216, 3072, 768
+    x = O.bf16_to_f32(O.gen_normal_bf16(1, 7200, 1.0, 8 * F)).reshape(8, F)
+    sets = {
+        "qkvg": ([(Q, H), (KV, H), (KV, H), (Q, H)], H),
+        "o": ([(H, Q)], Q),
+        "gate_up": ([(F, H), (F, H)], H),
+        "down": ([(H, F)], F),
+    }
+    for name, (shapes, k) in sets.items():
+        ws = [O.synth_weight(1, 7300 + 16 * i + len(name), n, kk)[1:] for i, (n, kk) in enumerate(shapes)]
+        got = run_linear(xtg, torch_mod, ws, x[:m, :k])
+        ref = O.matmul_nvfp4(ws, x[:m, :k])
+        ok, worst = close_rel(np.concatenate([g_.ravel() for g_ in got]), np.concatenate([r.ravel() for r in ref]))
+        assert ok, (name, worst)
+
+
+def test_gemv_ragged_shapes(cuda, xtg, torch_mod):
+    """Rows not a multiple of 16 and inputs not a multiple of 64 (padding), fused with uneven weights."""
+    k = 336
+    ws = [O.synth_weight(2, 7400 + i, n, k)[1:] for i, n in enumerate((1, 17, 100))]
+    x = O.gen_uniform(2, 7500, -1.0, 1.0, 5 * k).reshape(5, k)
+    got = run_linear(xtg, torch_mod, ws, x)
+    ref = O.matmul_nvfp4(ws, x)
+    ok, worst = close_rel(np.concatenate([g_.ravel() for g_ in got]), np.concatenate([r.ravel() for r in ref]))
+    assert ok, worst
+
+
+def test_gemv_deterministic(cuda, xtg, torch_mod):
+    torch = torch_mod
+    raw, codes, scales, g = O.synth_weight(4, 7600, 3072, 9216)
+    x = dev(torch, O.gen_uniform(4, 7601, -1.0, 1.0, 8 * 9216).reshape(8, 9216))
+    L = xtg.Linear([(dev(torch, codes), dev(torch, scales), g)], 9216)
+    a = L(x)[0].cpu().numpy()
+    b = L(x)[0].cpu().numpy()
+    L.close()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+# ---- attention ----
+
+def cache_to_device(torch, codes_k, codes_v, ks, vs):
+    """Oracle layout [slots][kv_heads][128] / [slots][kv_heads] -> the library's K [h][slots][128], V [h][128][slots],
+    scales [h][slots]."""
+    kc = np.ascontiguousarray(codes_k.transpose(1, 0, 2))
+    vc = np.ascontiguousarray(codes_v.transpose(1, 2, 0))
+    return dev(torch, kc), dev(torch, vc), dev(torch, np.ascontiguousarray(ks.T)), dev(torch, np.ascontiguousarray(vs.T))
+
+
+def rope_rows(x, pos0, theta):
+    x = np.ascontiguousarray(x, np.float32).copy()
+    L = O.lib()
+    L.xo_rope(O.ptr(x, O.f32p), x.shape[0], x.shape[1], x.shape[2], pos0, theta)
+    return x
+
+
+def config2_inputs(seed, slots, n_q, ring):
+    heads, kvh, d = 24, 6, 128
+    ck = O.gen_int8(seed, 1, slots * kvh * d).view(np.uint8).reshape(slots, kvh, d)
+    cv = O.gen_int8(seed, 2, slots * kvh * d).view(np.uint8).reshape(slots, kvh, d)
+    ks = O.gen_uniform(seed, 3, 0.005, 0.02, slots * kvh).reshape(slots, kvh)
+    vs = O.gen_uniform(seed, 4, 0.005, 0.02, slots * kvh).reshape(slots, kvh)
+    q = O.bf16_to_f32(O.gen_normal_bf16(seed, 5, 1.0, n_q * heads * d)).reshape(n_q, heads, d)
+    k = O.bf16_to_f32(O.gen_normal_bf16(seed, 6, 1.0, n_q * kvh * d)).reshape(n_q, kvh, d)
+    v = O.bf16_to_f32(O.gen_normal_bf16(seed, 7, 1.0, n_q * kvh * d)).reshape(n_q, kvh, d)
+    return ck, cv, ks, vs, q, k, v
+
+
+@pytest.mark.parametrize("L", [4096, 8192, 32768])
+def test_attention_config2_global(cuda, xtg, torch_mod, L):
+    """BASELINE config 2, global layer: 8 rows at p = L - 8 over L - 8 cached positions (slot = position)."""
+    torch = torch_mod
+    pos0, n_q = L - 8, 8
+    ck, cv, ks, vs, q, k, v = config2_inputs(20 + L, L, n_q, False)
+    q = rope_rows(q, pos0, 1e6)
+    k = rope_rows(k, pos0, 1e6)
+    scale = 1.0 / math.sqrt(128)
+    ref = O.attention(q, k, v, ck, cv, ks, vs, pos0, 0, scale)
+    kc, vc, kss, vss = cache_to_device(torch, ck, cv, ks, vs)
+    for splits in (1, 24):
+        got = xtg.attention(dev(torch, q), dev(torch, k), dev(torch, v), kc, vc, kss, vss, pos0, 0, scale,
+                            splits=splits).cpu().numpy()
+        ok, worst = close_rel(got, ref)
+        assert ok, (splits, worst)
+
+
+def test_attention_config2_sliding_ring(cuda, xtg, torch_mod):
+    """BASELINE config 2, sliding layer: a 1088-slot ring holding the most recent 1088 positions in rotated slot
+    order, window 1024; the mask comes from the slot -> position table."""
+    torch = torch_mod
+    ring, window, n_q = 1088, 1024, 8
+    pos0 = 8192 - 8 + 37
+    ck, cv, ks, vs, q, k, v = config2_inputs(99, ring, n_q, True)
+    ring_pos = np.array([pos0 - 1 - ((pos0 - 1 - s) % ring) for s in range(ring)], np.int64)
+    q = rope_rows(q, pos0, 1e6)
+    k = rope_rows(k, pos0, 1e6)
+    scale = 1.0 / math.sqrt(128)
+    ref = O.attention(q, k, v, ck, cv, ks, vs, pos0, window, scale, ring_pos=ring_pos)
+    kc, vc, kss, vss = cache_to_device(torch, ck, cv, ks, vs)
+    rp = dev(torch, ring_pos.astype(np.int32))
+    for splits in (1, 8, 17):
+        got = xtg.attention(dev(torch, q), dev(torch, k), dev(torch, v), kc, vc, kss, vss, pos0, window, scale,
+                            ring_pos=rp, splits=splits).cpu().numpy()
+        ok, worst = close_rel(got, ref)
+        assert ok, (splits, worst)
+
+
+@pytest.mark.parametrize("dtype", [O.KV_I8, O.KV_FP8])
+@pytest.mark.parametrize("case", [(300, 1, 0), (5000, 1, 0), (300, 1, 64), (100, 7, 0), (100, 8, 16), (0, 8, 0),
+                                  (900, 3, 128), (64, 1, 0), (1, 2, 0)])
+def test_attention_reference_cases(cuda, xtg, torch_mod, dtype, case):
+    """kernels_test.cpp:139-141's cases (cached, n_q, window) with head_dim 128, 8 q / 2 KV heads, scale 0.7; n_q
+    capped at the 8 rows of a verify step. Window cases run as a ring of window + 64 slots holding the latest
+    positions, with stale slots marked -1."""
+    torch = torch_mod
+    cached, n_q, window = case
+    heads, kvh, d = 8, 2, 128
+    total = cached + n_q
+    K = O.gen_uniform(31, 1, -1.0, 1.0, total * kvh * d).reshape(total, kvh, d)
+    V = O.gen_uniform(31, 2, -1.0, 1.0, total * kvh * d).reshape(total, kvh, d)
+    q = O.gen_uniform(31, 3, -1.0, 1.0, n_q * heads * d).reshape(n_q, heads, d)
+    ring = window > 0
+    slots = (window + 64) if ring else max(64, (total + 63) // 64 * 64)
+    ck = np.zeros((slots, kvh, d), np.uint8)
+    cv = np.zeros_like(ck)
+    ks = np.zeros((slots, kvh), np.float32)
+    vs = np.zeros_like(ks)
+    rp = np.full(slots, -1, np.int64)
+    for p in range(cached):
+        s = p % slots
+        (ck[s], ks[s]), (cv[s], vs[s]) = O.kv_encode(dtype, K[p]), O.kv_encode(dtype, V[p])
+        rp[s] = p
+    ref = O.attention(q, K[cached:], V[cached:], ck, cv, ks, vs, cached, window, 0.7,
+                      ring_pos=rp if ring else None, dtype=dtype)
+    kc, vc, kss, vss = cache_to_device(torch, ck, cv, ks, vs)
+    got = xtg.attention(dev(torch, q), dev(torch, K[cached:]), dev(torch, V[cached:]), kc, vc, kss, vss, cached,
+                        window, 0.7, ring_pos=dev(torch, rp.astype(np.int32)) if ring else None, dtype=dtype,
+                        splits=3).cpu().numpy()
+    ok, worst = close_rel(got, ref)
+    assert ok, worst
+
+
+# ---- KV store: bit-exact encode ----
+
+@pytest.mark.parametrize("dtype", [O.KV_I8, O.KV_FP8])
+@pytest.mark.parametrize("ring", [False, True])
+def test_kv_store_bit_exact(cuda, xtg, torch_mod, dtype, ring):
+    torch = torch_mod
+    kvh, slots, n, pos = 3, 128, 70 if not ring else 200, 30
+    k = O.gen_uniform(41, 1, -3.0, 3.0, n * kvh * 128).reshape(n, kvh, 128)
+    v = O.gen_uniform(41, 2, -0.2, 0.2, n * kvh * 128).reshape(n, kvh, 128)
+    k[5, 1] = 0.0
+    kc = torch.zeros((kvh, slots, 128), dtype=torch.uint8, device="cuda")
+    vc = torch.zeros((kvh, 128, slots), dtype=torch.uint8, device="cuda")
+    kss = torch.zeros((kvh, slots), dtype=torch.float32, device="cuda")
+    vss = torch.zeros((kvh, slots), dtype=torch.float32, device="cuda")
+    xtg.kv_store(dev(torch, k), dev(torch, v), pos, slots, ring, dtype, kc, vc, kss, vss)
+    kc, vc, kss, vss = kc.cpu().numpy(), vc.cpu().numpy(), kss.cpu().numpy(), vss.cpu().numpy()
+    first = pos + n - slots if ring and n > slots else pos
+    for p in range(first, pos + n):
+        s = p % slots if ring else p
+        for h in range(kvh):
+            c, sc = O.kv_encode(dtype, k[p - pos, h][None])
+            assert np.array_equal(kc[h, s], c[0]) and kss[h, s] == sc[0]
+            c, sc = O.kv_encode(dtype, v[p - pos, h][None])
+            assert np.array_equal(vc[h, :, s], c[0]) and vss[h, s] == sc[0]

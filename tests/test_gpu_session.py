@@ -1,0 +1,146 @@
+"""GPU: the session behind the C ABI (xtg_cuda_open / forward / rewind / snapshot / restore / grow / debug_cache)
+against the oracle's step (packs/dory/dory.cpp:467-578 order) and the NPU plugin's state rules
+(npu/xtg_npu.cpp:346-447): full-step parity (identical argmax, max |d logit| <= 5e-2), verify vs sequential
+agreement, rewind / snapshot / restore / tier moves, and the error paths (-1 with the state unchanged)."""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 5e-2
+
+
+@pytest.fixture(scope="module")
+def cfg(xtg):
+    return dict(xtg.SMALL)
+
+
+def logits_of(out, n):
+    return np.stack([out[i] for i in range(n)])
+
+
+def test_steps_match_oracle(cuda, xtg, cfg):
+    steps = [[5, 17, 900, 3, 44, 1023, 0, 256], [8, 9, 10, 11, 12, 13, 14, 15], [600, 601, 2], [4095]]
+    ref = O.SynthDory(cfg, ctx=512, n_prefill=100)
+    with xtg.Session(cfg, context=512) as s:
+        s.prefill_synthetic(100)
+        for toks in steps:
+            got = logits_of(s.forward(toks, want=2), len(toks))
+            want = ref.step(toks)
+            assert np.array_equal(got.argmax(1), want.argmax(1))
+            assert np.abs(got - want).max() <= LOGIT_TOL, np.abs(got - want).max()
+            assert s.argmax(8) == list(want.argmax(1))
+        assert s.pos() == ref.n_past == 100 + 8 + 8 + 3 + 1
+        # the prefilled part of the caches is the oracle's, byte for byte; the new rows decode close to it
+        for inst in (0, 1):
+            kc, vc, ks, vs, ring = ref.cache(inst)
+            dk = s.debug_cache(inst, 0).transpose(2, 0, 1)   # [slots][h][d]
+            dv = s.debug_cache(inst, 1).transpose(1, 0, 2)
+            dks = s.debug_cache(inst, 2).T
+            if not ring:
+                assert np.array_equal(dk[:100], kc[:100]) and np.array_equal(dv[:100], vc[:100])
+                assert np.array_equal(dks[:100], ks[:100])
+                new = slice(100, 120)
+                kd = dk[new].view(np.int8).astype(np.float32) * dks[new][..., None]
+                kr = kc[new].view(np.int8).astype(np.float32) * ks[new][..., None]
+                assert np.abs(kd - kr).max() < 0.05
+
+
+def test_verify_matches_sequential(cuda, xtg, cfg):
+    toks = [31, 32, 33, 34, 35, 36, 37, 38]
+    with xtg.Session(cfg, context=512) as a, xtg.Session(cfg, context=512) as b:
+        a.prefill_synthetic(200)
+        b.prefill_synthetic(200)
+        va = logits_of(a.forward(toks, want=2), 8)
+        vb = np.stack([b.forward([t], want=1)[0] for t in toks])
+        assert np.array_equal(va.argmax(1), vb.argmax(1))
+        assert np.abs(va - vb).max() <= LOGIT_TOL
+
+
+def test_forward_is_deterministic_and_rewind_replays(cuda, xtg, cfg):
+    with xtg.Session(cfg, context=512) as s:
+        s.prefill_synthetic(150)
+        a = logits_of(s.forward([1, 2, 3, 4, 5, 6, 7, 8], want=2), 8)
+        assert s.rewind(150)
+        b = logits_of(s.forward([1, 2, 3, 4, 5, 6, 7, 8], want=2), 8)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_rewind_rules(cuda, xtg, cfg):
+    ring, window = cfg["ring"], cfg["window"]
+    with xtg.Session(cfg, context=512) as s:
+        s.prefill_synthetic(300)
+        for _ in range(3):
+            s.forward([7] * 8, want=0)
+        n = s.pos()
+        assert not s.rewind(n + 1) and s.pos() == n
+        assert not s.rewind(-1) and s.pos() == n
+        lowest = n - ring + window - 1   # the ring still holds window - 1 positions before it
+        assert not s.rewind(lowest - 1) and s.pos() == n
+        assert s.rewind(lowest) and s.pos() == lowest
+        assert s.rewind(lowest)
+
+
+def test_snapshot_restore(cuda, xtg, cfg):
+    with xtg.Session(cfg, context=512, snapshots=2) as s:
+        assert s.snapshot_slots() == 2 and s.snapshot_pos(0) == -1 and s.snapshot_pos(5) == -1
+        assert not s.restore(0)
+        s.prefill_synthetic(120)
+        s.forward([9] * 8, want=0)
+        s.snapshot(1)
+        p = s.pos()
+        assert s.snapshot_pos(1) == p
+        after = logits_of(s.forward(list(range(40, 48)), want=2), 8)
+        for _ in range(20):   # far past the ring's slack: only the snapshot brings position p back
+            s.forward([3] * 8, want=0)
+        assert not s.rewind(p)
+        assert s.restore(1) and s.pos() == p
+        again = logits_of(s.forward(list(range(40, 48)), want=2), 8)
+        assert np.array_equal(after.view(np.uint32), again.view(np.uint32))
+        # a forward below a snapshot's position drops it
+        s.snapshot(0)
+        q = s.pos()
+        assert s.rewind(q - 4)
+        s.forward([1], want=0)
+        assert s.snapshot_pos(0) == -1
+
+
+def test_grow_moves_tier_bit_exactly(cuda, xtg, cfg):
+    toks1, toks2 = list(range(100, 108)), list(range(200, 208))
+    with xtg.Session(cfg, context=256) as small, xtg.Session(cfg, context=1024) as big:
+        small.prefill_synthetic(180)
+        big.prefill_synthetic(180)
+        small.forward(toks1, want=0)
+        big.forward(toks1, want=0)
+        with pytest.raises(xtg.XtgError):
+            small.grow("128")                    # cannot hold pos(): the session keeps its tier
+        assert small.info()["context"] == 256
+        small.grow("1k")
+        assert small.info()["context"] == 1024 and small.pos() == big.pos()
+        a = logits_of(small.forward(toks2, want=2), 8)
+        b = logits_of(big.forward(toks2, want=2), 8)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        g_small = small.debug_cache(1, 0)
+        g_big = big.debug_cache(1, 0)
+        assert np.array_equal(g_small[:, :, :204], g_big[:, :, :204])
+
+
+def test_error_paths_leave_state_unchanged(cuda, xtg, cfg):
+    with xtg.Session(cfg, context=128) as s:
+        s.prefill_synthetic(100)
+        with pytest.raises(xtg.XtgError, match="out of range"):
+            s.forward([1, cfg["vocab"]], want=0)
+        assert s.pos() == 100
+        with pytest.raises(xtg.XtgError, match="context full"):
+            s.forward([1] * 29, want=0)
+        assert s.pos() == 100
+        s.forward([1] * 28, want=0)
+        assert s.pos() == 128
+        assert s.debug_cache(999, 0) is None
+        info = s.info()
+        assert info["decode_ar"] == 8 and info["ring_slots"] == cfg["ring"] and info["sliding_window"] == cfg["window"]
+    with pytest.raises(xtg.XtgError):
+        xtg.Session(cfg, context=100)            # not a multiple of 64
+    with pytest.raises(xtg.XtgError):
+        xtg.Session(dict(cfg, head_dim=64))      # the kernels are written for head_dim 128

@@ -1,0 +1,239 @@
+// Kernel-level entry points of include/xtg_cuda.h: the device forms of the reference's CPU kernels on caller-owned
+// device memory (matmul_nvfp4, attention, KvCache::store, the quantizer, the generators).
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/xtg_cuda.h"
+#include "attention.h"
+#include "common.cuh"
+#include "elementwise.h"
+#include "kernels.h"
+
+using namespace xtg;
+
+struct xtg_cuda_linear {
+  int device = 0;
+  int k = 0, nw = 0, tiles = 0, blocks = 0, grid = 0;
+  std::vector<int> n_out, tile0;
+  std::vector<float> globals;
+  uint8_t* w = nullptr;
+  TileOut* outs = nullptr;          // device, rewritten per call (the ys pointers)
+  std::vector<TileOut> outs_host;
+  uint32_t* x16 = nullptr;
+  float* partial = nullptr;
+  int* counters = nullptr;
+  int* m_dev = nullptr;
+  int64_t bytes = 0;
+
+  ~xtg_cuda_linear() {
+    cudaFree(w);
+    cudaFree(outs);
+    cudaFree(x16);
+    cudaFree(partial);
+    cudaFree(counters);
+    cudaFree(m_dev);
+  }
+};
+
+namespace {
+
+void set_err(char* err, int len, const char* what) {
+  if (err && len > 0) std::snprintf(err, (size_t)len, "%s", what);
+}
+
+template <class F>
+int guarded(char* err, int err_len, F&& f) {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(err, err_len, e.what());
+    return -1;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+xtg_cuda_linear* xtg_cuda_linear_new(int nw, const uint8_t* const* codes, const uint8_t* const* scales,
+                                     const float* globals, const int* n_out, int k, char* err, int err_len) {
+  std::unique_ptr<xtg_cuda_linear> L;
+  try {
+    XTG_REQUIRE(nw >= 1 && k >= 16 && k % 16 == 0, "linear: at least one weight, k a positive multiple of 16");
+    L = std::make_unique<xtg_cuda_linear>();
+    XTG_CUDA(cudaGetDevice(&L->device));
+    int sms = 0;
+    XTG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, L->device));
+    L->k = k;
+    L->nw = nw;
+    L->blocks = packed_blocks(k);
+    for (int i = 0; i < nw; ++i) {
+      XTG_REQUIRE(n_out[i] > 0, "linear: n_out must be positive");
+      L->n_out.push_back(n_out[i]);
+      L->globals.push_back(globals[i]);
+      L->tile0.push_back(L->tiles);
+      L->tiles += packed_tiles(n_out[i], false);
+    }
+    L->bytes = (int64_t)L->tiles * L->blocks * kBlockBytes;
+    XTG_CUDA(cudaMalloc(&L->w, L->bytes));
+    for (int i = 0; i < nw; ++i)
+      pack_nvfp4(codes[i], scales[i], nullptr, nullptr, n_out[i], k, false,
+                 L->w + (int64_t)L->tile0[i] * L->blocks * kBlockBytes, nullptr);
+    XTG_CUDA(cudaMalloc(&L->outs, sizeof(TileOut) * L->tiles));
+    L->outs_host.resize(L->tiles);
+    XTG_CUDA(cudaMalloc(&L->x16, (size_t)L->blocks * 4 * 64 * sizeof(uint32_t)));
+    L->grid = gemv_grid(sms);
+    XTG_CUDA(cudaMalloc(&L->partial, gemv_partial_floats(L->grid) * sizeof(float)));
+    XTG_CUDA(cudaMalloc(&L->counters, sizeof(int) * L->tiles));
+    XTG_CUDA(cudaMemset(L->counters, 0, sizeof(int) * L->tiles));
+    XTG_CUDA(cudaMalloc(&L->m_dev, sizeof(int)));
+    XTG_CUDA(cudaDeviceSynchronize());
+  } catch (const std::exception& e) {
+    set_err(err, err_len, e.what());
+    return nullptr;
+  }
+  return L.release();
+}
+
+int xtg_cuda_linear_forward(xtg_cuda_linear* L, const float* x, int m, float* const* ys, void* stream, char* err,
+                            int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_REQUIRE(m >= 1 && m <= kMaxRows, "linear: 1..8 rows");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int i = 0; i < L->nw; ++i) {
+      const int t0 = L->tile0[i], nt = packed_tiles(L->n_out[i], false);
+      for (int t = 0; t < nt; ++t)
+        L->outs_host[t0 + t] = TileOut{ys[i] + 16 * t, L->n_out[i], std::min(16, L->n_out[i] - 16 * t), L->globals[i], 0};
+    }
+    XTG_CUDA(cudaMemcpyAsync(L->outs, L->outs_host.data(), sizeof(TileOut) * L->tiles, cudaMemcpyHostToDevice, s));
+    pack_activations(x, m, L->k, L->x16, s);
+    GemvArgs a = {};
+    a.w = L->w;
+    a.tiles = L->tiles;
+    a.blocks = L->blocks;
+    a.x16 = L->x16;
+    a.m = m;
+    a.partial = L->partial;
+    a.counters = L->counters;
+    a.outs = L->outs;
+    launch_gemv(kEpiStore, a, L->grid, s, false);
+    // outs_host is read by the copy above before this call returns to the caller's next forward
+    XTG_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+int64_t xtg_cuda_linear_bytes(xtg_cuda_linear* L) { return L ? L->bytes : -1; }
+
+void xtg_cuda_linear_free(xtg_cuda_linear* L) { delete L; }
+
+int xtg_cuda_quantize_nvfp4(const uint16_t* w_bf16, int n_out, int k, uint8_t* codes, uint8_t* scales,
+                            float* global, void* stream, char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned int* amax = nullptr;
+    XTG_CUDA(cudaMalloc(&amax, sizeof(unsigned int)));
+    try {
+      quantize_nvfp4(w_bf16, n_out, k, codes, scales, global, amax, s);
+      XTG_CUDA(cudaStreamSynchronize(s));
+    } catch (...) {
+      cudaFree(amax);
+      throw;
+    }
+    cudaFree(amax);
+  });
+}
+
+int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_REQUIRE(p->head_dim == 128, "attention: head_dim 128");
+    XTG_REQUIRE(p->n_q >= 1 && p->n_q <= kMaxRows, "attention: 1..8 query rows");
+    XTG_REQUIRE(splits >= 1, "attention: at least one split");
+    XTG_REQUIRE(p->ring == 0 || p->ring_pos != nullptr, "attention: a ring needs its slot -> position table");
+    XTG_REQUIRE(p->ring != 0 || p->pos0 <= p->slots, "attention: pos0 beyond the cache");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    float* part = nullptr;
+    XTG_CUDA(cudaMalloc(&part, attention_part_floats(p->kv_heads, splits) * sizeof(float)));
+    try {
+      AttnArgs a = {};
+      a.q = p->q;
+      a.k = p->k;
+      a.v = p->v;
+      a.kc = const_cast<uint8_t*>(p->k_codes);
+      a.vc = const_cast<uint8_t*>(p->v_codes);
+      a.ks = const_cast<float*>(p->k_scales);
+      a.vs = const_cast<float*>(p->v_scales);
+      a.slots = p->slots;
+      a.ring = p->ring;
+      a.ring_pos = p->ring_pos;
+      a.dtype = p->dtype;
+      a.window = p->window;
+      a.scale = p->scale;
+      a.m = p->n_q;
+      a.pos0 = p->pos0;
+      a.heads = p->heads;
+      a.kv_heads = p->kv_heads;
+      a.splits = splits;
+      a.part = part;
+      launch_attention(a, s, false);
+      CombineArgs cb = {};
+      cb.part = part;
+      cb.splits = splits;
+      cb.heads = p->heads;
+      cb.kv_heads = p->kv_heads;
+      cb.m = p->n_q;
+      cb.out = p->out;
+      launch_attn_combine(cb, s, false);
+      XTG_CUDA(cudaStreamSynchronize(s));
+    } catch (...) {
+      cudaFree(part);
+      throw;
+    }
+    cudaFree(part);
+  });
+}
+
+int xtg_cuda_kv_store(const float* k, const float* v, int64_t pos, int n, int kv_heads, int64_t slots, int ring,
+                      int dtype, uint8_t* k_codes, uint8_t* v_codes, float* k_scales, float* v_scales, void* stream,
+                      char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_REQUIRE(ring || pos + n <= slots, "KV cache full");
+    KvStoreArgs a = {};
+    a.k = k;
+    a.v = v;
+    a.pos = pos;
+    a.n = n;
+    a.kv_heads = kv_heads;
+    a.slots = slots;
+    a.ring = ring;
+    a.dtype = dtype;
+    a.kc = k_codes;
+    a.vc = v_codes;
+    a.ks = k_scales;
+    a.vs = v_scales;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    launch_kv_store(a, s);
+    XTG_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+int xtg_cuda_gen(int what, uint64_t seed, uint64_t stream_id, float a, float b, void* out, int64_t n, void* stream,
+                 char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (what == 0)
+      gen_normal_bf16(seed, stream_id, a, static_cast<uint16_t*>(out), n, s);
+    else if (what == 1)
+      gen_uniform(seed, stream_id, a, b, static_cast<float*>(out), n, s);
+    else if (what == 2)
+      gen_int8(seed, stream_id, static_cast<int8_t*>(out), n, s);
+    else
+      throw CudaError("gen: what must be 0, 1 or 2");
+    XTG_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+}  // extern "C"

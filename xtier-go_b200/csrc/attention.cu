@@ -1,0 +1,493 @@
+// K3: GQA decode / verify attention over an int8 (or FP8) KV cache, split-KV with a log-sum-exp combine
+// (engine/src/kv.cpp:166-286 semantics; the visibility rule of npu/xtg_npu.cpp:236-258).
+//
+// Cache layout of one instance (HBM, written by this file and by the host's tier / snapshot copies):
+//   K codes [kv_heads][slots][128]   one row per slot, so a slot range of one head is contiguous
+//   V codes [kv_heads][128][slots]   transposed, so the PV operand is read as 16 contiguous slots per lane
+//   K / V scales f32 [kv_heads][slots]  (one per position and KV head: amax / 127 for int8, amax / 448 for FP8)
+// A global instance's slot is the position; a ring's slot s holds position ring_pos[s] (-1 empty). A cached key at
+// position p is visible to the row at t when 0 <= p < pos0 (and t - p < window for a sliding layer); this call's
+// own key j is visible to own row i when j <= i (and i - j < window).
+//
+// One CTA per (split of the slots, KV head), 4 warps: warp w takes query rows 16 (w & 1) .. +15 -- a query row is
+// (activation row, q head of this KV head), 8 x 4 = 32 rows, so the 4 q heads sharing a KV head read it once -- and
+// 64-slot chunks w >> 1, +2, ... of the split. Both products run on mma.m16n8k16: int8 codes become f16 exactly
+// (1152 + b as a half, less 1152), FP8 codes by cvt.rn.f16x2.e4m3x2; Q (after RoPE, justnorm, q scale) is rounded
+// once to fp16; scores are scaled per key by its K scale in FP32, probabilities times the key's V scale are the
+// fp16 A operand of PV. Two permutations make every load contiguous: the head dimension inside a k16 step (lane tq
+// reads 32 contiguous bytes of a K row, Q's fragments use the same order) and the slots inside a 64-slot chunk
+// (lane tq owns slots 16 tq .. 16 tq + 15 in both products).
+#include "attention.h"
+#include "common.cuh"
+
+namespace xtg {
+
+namespace {
+
+constexpr int kD = 128;
+constexpr int kThreads = 128;
+constexpr int kQRows = 32;
+constexpr int kPartStride = kD + 2;   // m, l, acc[128]
+
+__device__ __forceinline__ void rope_norm_vec(float (&x)[4], const float* cosv, const float* sinv, int lane,
+                                              bool rope) {
+  // x[0] = e, x[1] = e + 64, x[2] = e + 32, x[3] = e + 96 for e = lane
+  if (rope) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int e = lane + 32 * h;
+      const float c = cosv[e], s = sinv[e];
+      const float x1 = x[2 * h], x2 = x[2 * h + 1];
+      x[2 * h] = x1 * c - x2 * s;
+      x[2 * h + 1] = x2 * c + x1 * s;
+    }
+  }
+  const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+  const float f = 1.f / sqrtf(ss + 1e-6f);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) x[j] *= f;
+}
+
+// Encode one row of 128 (a warp, 4 values per lane at e, e + 64, e + 32, e + 96) into codes and a scale.
+__device__ __forceinline__ void encode_row(const float (&x)[4], int dtype, int lane, uint8_t* row_k,
+                                           uint8_t* col_v, int64_t v_stride, float* scale_out) {
+  float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+  amax = warp_max(amax);
+  const float top = dtype == kKvFp8 ? 448.f : 127.f;
+  const float sc = amax > 0.f ? __fdiv_rn(amax, top) : 1.f;
+  const float inv = __fdiv_rn(1.f, sc);
+  const int idx[4] = {lane, lane + 64, lane + 32, lane + 96};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float t = __fmul_rn(x[j], inv);
+    uint8_t c;
+    if (dtype == kKvFp8) {
+      c = f32_to_e4m3(t);
+    } else {
+      float r = rintf(t);
+      r = fminf(fmaxf(r, -127.f), 127.f);
+      c = (uint8_t)(int8_t)(int)r;
+    }
+    if (row_k) row_k[idx[j]] = c;
+    if (col_v) col_v[(int64_t)idx[j] * v_stride] = c;
+  }
+  if (lane == 0) *scale_out = sc;
+}
+
+__device__ __forceinline__ void codes_to_f16(uint32_t word, int dtype, uint32_t& lo, uint32_t& hi) {
+  if (dtype == kKvFp8) {
+    lo = e4m3x2_to_f16x2(word & 0xffff);
+    hi = e4m3x2_to_f16x2(word >> 16);
+  } else {
+    const uint32_t biased = word ^ 0x80808080u;
+    lo = s8x2_to_f16x2(biased, 0x4140);
+    hi = s8x2_to_f16x2(biased, 0x4342);
+  }
+}
+
+struct Smem {
+  float q[kQRows][kD + 4];        // prepared queries (query row = 4 * activation row + head in group)
+  float k[kMaxRows][kD + 4];      // this call's keys / values (prepared)
+  float v[kMaxRows][kD + 4];
+  float mrg_m[2][16];             // half-1 warps' softmax state for the merge
+  float mrg_l[2][16];
+  float mrg_acc[2][16][kD + 4];
+};
+
+__global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = lane >> 2, tq = lane & 3;
+  const int split = blockIdx.x, kvh = blockIdx.y;
+  const int m = a.params ? a.params->m : a.m;
+  const int pos0 = (int)(a.params ? a.params->pos0 : a.pos0);   // positions stay below 2^31
+  const int64_t slots = a.slots;
+  const int group = a.heads / a.kv_heads;
+
+  // this CTA's 64-slot chunks: a global cache holds [0, pos0), a ring every slot
+  const int64_t span = a.ring ? slots : pos0;
+  const int64_t nchunks = (span + 63) / 64;
+  const int64_t cb = nchunks * split / a.splits, ce = nchunks * (split + 1) / a.splits;
+  const uint8_t* kc = a.kc + (int64_t)kvh * slots * kD;
+  const uint8_t* vc = a.vc + (int64_t)kvh * kD * slots;
+  const float* ks = a.ks + (int64_t)kvh * slots;
+  const float* vs = a.vs + (int64_t)kvh * slots;
+  if (ce > cb && threadIdx.x == 0) {   // the cache rows this CTA reads do not depend on the previous kernel
+    prefetch_l2(kc + cb * 64 * kD, (uint32_t)((ce - cb) * 64 * kD));
+  }
+  if (ce > cb && threadIdx.x < kD && !a.ring) {
+    prefetch_l2(vc + (int64_t)threadIdx.x * slots + cb * 64, (uint32_t)((ce - cb) * 64));
+  }
+  if (a.pdl) pdl_wait();
+
+  // ---- prepare Q and this call's K / V (RoPE + justnorm + q scale in the fused step) ----
+  for (int task = warp; task < kMaxRows * (group + 2); task += kThreads / 32) {
+    const int i = task / (group + 2), which = task % (group + 2);   // which < group: q head; group: k; +1: v
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    if (i < m) {
+      const float* src;
+      if (a.proj) {
+        const float* row = a.proj + (int64_t)i * a.proj_ld;
+        src = which < group ? row + (int64_t)(kvh * group + which) * kD
+                            : row + (int64_t)a.heads * kD + (int64_t)(which - group) * a.kv_heads * kD + kvh * kD;
+      } else {
+        src = which < group ? a.q + ((int64_t)i * a.heads + kvh * group + which) * kD
+                            : (which == group ? a.k : a.v) + ((int64_t)i * a.kv_heads + kvh) * kD;
+      }
+      x[0] = src[lane];
+      x[1] = src[lane + 64];
+      x[2] = src[lane + 32];
+      x[3] = src[lane + 96];
+      if (a.proj && which <= group) {   // q and k: RoPE then justnorm per head
+        rope_norm_vec(x, a.rope_cos + i * (kD / 2), a.rope_sin + i * (kD / 2), lane, true);
+        if (which < group) {
+          const float* qs = a.qscale + (int64_t)(kvh * group + which) * kD;
+          x[0] *= qs[lane];
+          x[1] *= qs[lane + 64];
+          x[2] *= qs[lane + 32];
+          x[3] *= qs[lane + 96];
+        }
+      }
+      if (a.store && split == 0 && which >= group) {   // this call's rows into the cache
+        const int64_t p = pos0 + i, slot = a.ring ? p % slots : p;
+        if (which == group)
+          encode_row(x, a.dtype, lane, a.kc + ((int64_t)kvh * slots + slot) * kD, nullptr, 0,
+                     a.ks + (int64_t)kvh * slots + slot);
+        else
+          encode_row(x, a.dtype, lane, nullptr, a.vc + (int64_t)kvh * kD * slots + slot, slots,
+                     a.vs + (int64_t)kvh * slots + slot);
+      }
+    }
+    float* dst = which < group ? sm.q[i * group + which] : (which == group ? sm.k[i] : sm.v[i]);
+    dst[lane] = x[0];
+    dst[lane + 64] = x[1];
+    dst[lane + 32] = x[2];
+    dst[lane + 96] = x[3];
+  }
+  __syncthreads();
+  if (a.pdl) pdl_launch_next();
+
+  const int mt = warp & 1, half = warp >> 1;
+  const bool active = (16 * mt) / group < m;   // this warp's query rows hold at least one activation row
+  // A fragments of Q: step s, lane tq reads head dims 32 tq + 4 s + {0, 1} (a0, a1) and + {2, 3} (a2, a3)
+  uint32_t qa[8][4];
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    const int d0 = 32 * tq + 4 * s;
+    const float* r0 = sm.q[16 * mt + g];
+    const float* r1 = sm.q[16 * mt + g + 8];
+    qa[s][0] = pack_f16x2(r0[d0], r0[d0 + 1]);
+    qa[s][1] = pack_f16x2(r1[d0], r1[d0 + 1]);
+    qa[s][2] = pack_f16x2(r0[d0 + 2], r0[d0 + 3]);
+    qa[s][3] = pack_f16x2(r1[d0 + 2], r1[d0 + 3]);
+  }
+  // the activation rows of this lane's two query rows and their positions
+  const int arow0 = (16 * mt + g) / group, arow1 = (16 * mt + g + 8) / group;
+  const int t0 = pos0 + arow0, t1 = pos0 + arow1;
+  const bool live0 = arow0 < m, live1 = arow1 < m;
+
+  float acc[16][4];
+#pragma unroll
+  for (int dt = 0; dt < 16; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.f;
+  float run_m0 = -INFINITY, run_m1 = -INFINITY, run_l0 = 0.f, run_l1 = 0.f;
+
+  // one 64-key chunk: keys come from the cache (own = false, slot base c0) or this call's rows (own = true)
+  auto chunk = [&](int64_t c0, bool own) {
+    // ---- S = Q K^T: 8 n8-tiles, tile T = 2 j + ab holds slots c0 + 16 (n >> 1) + 4 j + (n & 1) + 2 ab ----
+    float s[8][4];
+#pragma unroll
+    for (int T = 0; T < 8; ++T) {
+      const int j = T >> 1, ab = T & 1;
+      const int key = 16 * (g >> 1) + 4 * j + (g & 1) + 2 * ab;   // the key this lane supplies (n = g)
+      uint32_t kw[8];
+      if (!own) {
+        const uint4* kr = reinterpret_cast<const uint4*>(kc + (c0 + key) * kD + 32 * tq);
+        const uint4 k0 = __ldg(kr), k1 = __ldg(kr + 1);
+        kw[0] = k0.x; kw[1] = k0.y; kw[2] = k0.z; kw[3] = k0.w;
+        kw[4] = k1.x; kw[5] = k1.y; kw[6] = k1.z; kw[7] = k1.w;
+      }
+      s[T][0] = s[T][1] = s[T][2] = s[T][3] = 0.f;
+#pragma unroll
+      for (int st = 0; st < 8; ++st) {
+        uint32_t b0, b1;
+        if (own) {
+          const int d0 = 32 * tq + 4 * st;
+          const bool ok = key < m;
+          const float* kr = sm.k[key < kMaxRows ? key : 0];
+          b0 = ok ? pack_f16x2(kr[d0], kr[d0 + 1]) : 0u;
+          b1 = ok ? pack_f16x2(kr[d0 + 2], kr[d0 + 3]) : 0u;
+        } else {
+          codes_to_f16(kw[st], a.dtype, b0, b1);
+        }
+        mma_f16(s[T], qa[st][0], qa[st][1], qa[st][2], qa[st][3], b0, b1);
+      }
+    }
+    // ---- scale, mask, online softmax: this lane's keys are slots c0 + 16 tq + kk, kk = 4 j + 2 ab + {0, 1} ----
+    float ksc[16], vsc[16];
+    int kpos[16];
+    if (own) {
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) {
+        ksc[kk] = 1.f;
+        vsc[kk] = 1.f;
+        kpos[kk] = 16 * tq + kk;   // own key index j
+      }
+    } else {
+      const float4* k4 = reinterpret_cast<const float4*>(ks + c0 + 16 * tq);
+      const float4* v4 = reinterpret_cast<const float4*>(vs + c0 + 16 * tq);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 kq = __ldg(k4 + q), vq = __ldg(v4 + q);
+        ksc[4 * q] = kq.x; ksc[4 * q + 1] = kq.y; ksc[4 * q + 2] = kq.z; ksc[4 * q + 3] = kq.w;
+        vsc[4 * q] = vq.x; vsc[4 * q + 1] = vq.y; vsc[4 * q + 2] = vq.z; vsc[4 * q + 3] = vq.w;
+      }
+      if (a.ring) {
+        const int4* p4 = reinterpret_cast<const int4*>(a.ring_pos + c0 + 16 * tq);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int4 pq = __ldg(p4 + q);
+          kpos[4 * q] = pq.x; kpos[4 * q + 1] = pq.y; kpos[4 * q + 2] = pq.z; kpos[4 * q + 3] = pq.w;
+        }
+      } else {
+#pragma unroll
+        for (int kk = 0; kk < 16; ++kk) kpos[kk] = (int)c0 + 16 * tq + kk;
+      }
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int T = 0; T < 8; ++T) {
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
+        const int p = kpos[kk];
+        bool vis0, vis1;
+        if (own) {
+          vis0 = live0 && p < m && p <= arow0 && (a.window == 0 || arow0 - p < a.window);
+          vis1 = live1 && p < m && p <= arow1 && (a.window == 0 || arow1 - p < a.window);
+        } else {
+          const bool ok = p >= 0 && p < pos0;
+          vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
+          vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
+        }
+        const float f = ksc[kk] * a.scale;
+        s[T][c] = vis0 ? s[T][c] * f : -INFINITY;
+        s[T][2 + c] = vis1 ? s[T][2 + c] * f : -INFINITY;
+        mx0 = fmaxf(mx0, s[T][c]);
+        mx1 = fmaxf(mx1, s[T][2 + c]);
+      }
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float new_m0 = fmaxf(run_m0, mx0), new_m1 = fmaxf(run_m1, mx1);
+    const float corr0 = new_m0 == -INFINITY ? 1.f : expf(run_m0 - new_m0);
+    const float corr1 = new_m1 == -INFINITY ? 1.f : expf(run_m1 - new_m1);
+    run_m0 = new_m0;
+    run_m1 = new_m1;
+    run_l0 *= corr0;
+    run_l1 *= corr1;
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      acc[dt][0] *= corr0;
+      acc[dt][1] *= corr0;
+      acc[dt][2] *= corr1;
+      acc[dt][3] *= corr1;
+    }
+    uint32_t pa[4][4];   // A fragments of P' (probability times V scale), per key step j
+#pragma unroll
+    for (int T = 0; T < 8; ++T) {
+      float p[4];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
+        p[c] = s[T][c] == -INFINITY ? 0.f : expf(s[T][c] - new_m0);
+        p[2 + c] = s[T][2 + c] == -INFINITY ? 0.f : expf(s[T][2 + c] - new_m1);
+        run_l0 += p[c];
+        run_l1 += p[2 + c];
+        p[c] *= vsc[kk];
+        p[2 + c] *= vsc[kk];
+      }
+      const int j = T >> 1;
+      if ((T & 1) == 0) {
+        pa[j][0] = pack_f16x2(p[0], p[1]);
+        pa[j][1] = pack_f16x2(p[2], p[3]);
+      } else {
+        pa[j][2] = pack_f16x2(p[0], p[1]);
+        pa[j][3] = pack_f16x2(p[2], p[3]);
+      }
+    }
+    // ---- O += P' V: V^T row d = 8 dt + g, lane tq reads slots c0 + 16 tq .. + 15 ----
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      const int d = 8 * dt + g;
+      uint32_t vw[4];
+      if (own) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          // slots 16 tq + 4 j + {0, 1, 2, 3}: own rows only exist for tq = 0
+          const int k0 = 16 * tq + 4 * j;
+          float f[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) f[q] = (k0 + q < m) ? sm.v[k0 + q < kMaxRows ? k0 + q : 0][d] : 0.f;
+          const uint32_t lo = pack_f16x2(f[0], f[1]), hi = pack_f16x2(f[2], f[3]);
+          mma_f16(acc[dt], pa[j][0], pa[j][1], pa[j][2], pa[j][3], lo, hi);
+        }
+        (void)vw;
+      } else {
+        const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vc + (int64_t)d * slots + c0 + 16 * tq));
+        vw[0] = vv.x; vw[1] = vv.y; vw[2] = vv.z; vw[3] = vv.w;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t b0, b1;
+          codes_to_f16(vw[j], a.dtype, b0, b1);
+          mma_f16(acc[dt], pa[j][0], pa[j][1], pa[j][2], pa[j][3], b0, b1);
+        }
+      }
+    }
+  };
+
+  if (active) {
+    for (int64_t c = cb + half; c < ce; c += 2) chunk(c * 64, false);
+    // this call's own keys: the last split, the first half
+    if (split == a.splits - 1 && half == 0) chunk(0, true);
+  }
+  // the row sums live spread over the 4 lanes of a row
+  run_l0 += __shfl_xor_sync(0xffffffffu, run_l0, 1);
+  run_l0 += __shfl_xor_sync(0xffffffffu, run_l0, 2);
+  run_l1 += __shfl_xor_sync(0xffffffffu, run_l1, 1);
+  run_l1 += __shfl_xor_sync(0xffffffffu, run_l1, 2);
+
+  // ---- merge the two halves (warps mt and mt + 2), then write the CTA's partial per query row ----
+  if (half == 1) {
+    if (tq == 0) {
+      sm.mrg_m[mt][g] = run_m0;
+      sm.mrg_m[mt][g + 8] = run_m1;
+      sm.mrg_l[mt][g] = run_l0;
+      sm.mrg_l[mt][g + 8] = run_l1;
+    }
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      const int d = 8 * dt + 2 * tq;
+      sm.mrg_acc[mt][g][d] = acc[dt][0];
+      sm.mrg_acc[mt][g][d + 1] = acc[dt][1];
+      sm.mrg_acc[mt][g + 8][d] = acc[dt][2];
+      sm.mrg_acc[mt][g + 8][d + 1] = acc[dt][3];
+    }
+  }
+  __syncthreads();
+  if (half == 0) {
+    const float om0 = sm.mrg_m[mt][g], om1 = sm.mrg_m[mt][g + 8];
+    const float ol0 = sm.mrg_l[mt][g], ol1 = sm.mrg_l[mt][g + 8];
+    const float M0 = fmaxf(run_m0, om0), M1 = fmaxf(run_m1, om1);
+    const float w0a = run_m0 == -INFINITY ? 0.f : expf(run_m0 - M0), w0b = om0 == -INFINITY ? 0.f : expf(om0 - M0);
+    const float w1a = run_m1 == -INFINITY ? 0.f : expf(run_m1 - M1), w1b = om1 == -INFINITY ? 0.f : expf(om1 - M1);
+    const int qr0 = 16 * mt + g, qr1 = qr0 + 8;
+    float* p0 = a.part + (((int64_t)kvh * a.splits + split) * kQRows + qr0) * kPartStride;
+    float* p1 = a.part + (((int64_t)kvh * a.splits + split) * kQRows + qr1) * kPartStride;
+    if (tq == 0) {
+      if (live0) {
+        p0[0] = M0;
+        p0[1] = run_l0 * w0a + ol0 * w0b;
+      }
+      if (live1) {
+        p1[0] = M1;
+        p1[1] = run_l1 * w1a + ol1 * w1b;
+      }
+    }
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      const int d = 8 * dt + 2 * tq;
+      if (live0) {
+        p0[2 + d] = acc[dt][0] * w0a + sm.mrg_acc[mt][g][d] * w0b;
+        p0[3 + d] = acc[dt][1] * w0a + sm.mrg_acc[mt][g][d + 1] * w0b;
+      }
+      if (live1) {
+        p1[2 + d] = acc[dt][2] * w1a + sm.mrg_acc[mt][g + 8][d] * w1b;
+        p1[3 + d] = acc[dt][3] * w1a + sm.mrg_acc[mt][g + 8][d + 1] * w1b;
+      }
+    }
+  }
+}
+
+// Combine the splits of (activation row, q head) by log-sum-exp; then either the plain output (API) or the Dory
+// output gate, fp16 fragments for the O projection and the per-head sum of squares (the step).
+__global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
+  __shared__ float red[32];
+  const int i = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  if (a.pdl) pdl_wait();
+  if (a.pdl) pdl_launch_next();
+  const int m = a.params ? a.params->m : a.m;
+  if (i >= m) return;
+  const int group = a.heads / a.kv_heads, kvh = h / group, qr = i * group + h % group;
+  float M = -INFINITY;
+  for (int s = 0; s < a.splits; ++s)
+    M = fmaxf(M, a.part[(((int64_t)kvh * a.splits + s) * kQRows + qr) * kPartStride]);
+  float L = 0.f, o = 0.f;
+  for (int s = 0; s < a.splits; ++s) {
+    const float* p = a.part + (((int64_t)kvh * a.splits + s) * kQRows + qr) * kPartStride;
+    if (p[0] == -INFINITY) continue;
+    const float w = expf(p[0] - M);
+    L += p[1] * w;
+    o += p[2 + d] * w;
+  }
+  o = L > 0.f ? o / L : 0.f;
+  if (a.out) {
+    a.out[((int64_t)i * a.heads + h) * kD + d] = o;
+    return;
+  }
+  const int col = h * kD + d;
+  const float gt = a.gate[(int64_t)i * a.gate_ld + col];
+  o *= 1.f / (1.f + expf(-gt * a.gscale[col]));
+  a.a16[frag_offset_halves(col, i)] = __half_as_ushort(__float2half_rn(o));
+  const float ss = block_sum(o * o, red);
+  if (d == 0) a.asum[h * kMaxRows + i] = ss;
+}
+
+}  // namespace
+
+size_t attention_smem_bytes() { return sizeof(Smem); }
+
+int64_t attention_part_floats(int kv_heads, int splits) { return (int64_t)kv_heads * splits * kQRows * kPartStride; }
+
+void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
+  AttnArgs a = a_in;
+  a.pdl = pdl ? 1 : 0;
+  XTG_REQUIRE(a.heads % a.kv_heads == 0 && a.heads / a.kv_heads <= 4, "attention: at most 4 q heads per KV head");
+  XTG_REQUIRE(a.slots % 64 == 0, "attention: cache slots must be a multiple of 64");
+  static bool attr_set = false;
+  if (!attr_set) {
+    XTG_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sizeof(Smem)));
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.splits, a.kv_heads);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = sizeof(Smem);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, attention_kernel, a));
+}
+
+void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
+  CombineArgs a = a_in;
+  a.pdl = pdl ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kMaxRows, a.heads);
+  cfg.blockDim = dim3(kD);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_kernel, a));
+}
+
+}  // namespace xtg

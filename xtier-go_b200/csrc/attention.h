@@ -1,0 +1,70 @@
+// Internal interface of the attention kernels (attention.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace xtg {
+
+enum KvDtype { kKvInt8 = 0, kKvFp8 = 1 };
+
+// The per-step values a replayable graph reads on the device.
+struct StepParams {
+  int32_t tokens[8];
+  int32_t m;
+  int32_t pad;
+  int64_t pos0;
+};
+
+struct AttnArgs {
+  // this call's rows: the fused step reads the QKV(G) projection rows [m][proj_ld] (q, k, v, g) and applies RoPE,
+  // justnorm and the q scale; the API form reads prepared q [m][heads][128], k / v [m][kv_heads][128]
+  const float* proj;
+  int proj_ld;
+  const float* q;
+  const float* k;
+  const float* v;
+  const float* qscale;      // [heads * 128]
+  const float* rope_cos;    // [8][64] for positions pos0 .. pos0 + 7
+  const float* rope_sin;
+  // the cache (layout in attention.cu)
+  uint8_t* kc;
+  uint8_t* vc;
+  float* ks;
+  float* vs;
+  int64_t slots;
+  int ring;
+  const int32_t* ring_pos;  // [slots] for a ring
+  int dtype;
+  int store;                // write this call's K / V rows (fused step)
+  int window;
+  float scale;
+  const StepParams* params; // m and pos0 on the device, or null: m, pos0
+  int m;
+  int64_t pos0;
+  int heads, kv_heads;
+  int splits;
+  float* part;              // [kv_heads][splits][32][130]
+  int pdl;
+};
+
+struct CombineArgs {
+  const float* part;
+  int splits, heads, kv_heads;
+  const StepParams* params;
+  int m;
+  float* out;               // API: [m][heads][128]; null in the step
+  const float* gate;        // step: g rows [m][gate_ld] (the projection's g columns)
+  int gate_ld;
+  const float* gscale;      // [heads * 128]
+  uint16_t* a16;            // step: fp16 fragments of the gated output (K = heads * 128)
+  float* asum;              // step: [heads][8] sum of squares per head and activation row
+  int pdl;
+};
+
+size_t attention_smem_bytes();
+int64_t attention_part_floats(int kv_heads, int splits);
+void launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+void launch_attn_combine(const CombineArgs& a, cudaStream_t s, bool pdl);
+
+}  // namespace xtg

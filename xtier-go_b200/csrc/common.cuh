@@ -1,0 +1,211 @@
+// Shared device helpers of libxtg_cuda: number formats, the seeded generators, programmatic-dependent-launch hooks,
+// warp reductions. sm_100a only.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+namespace xtg {
+
+// ---- host error handling: an exception inside the library, a -1 + message at the C ABI ----
+struct CudaError : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+#define XTG_CUDA(call)                                                                                   \
+  do {                                                                                                   \
+    cudaError_t e_ = (call);                                                                             \
+    if (e_ != cudaSuccess)                                                                               \
+      throw ::xtg::CudaError(std::string(#call) + ": " + cudaGetErrorString(e_) + " (" __FILE__ ":" +  \
+                             std::to_string(__LINE__) + ")");                                            \
+  } while (0)
+
+#define XTG_REQUIRE(cond, msg)                       \
+  do {                                               \
+    if (!(cond)) throw ::xtg::CudaError(std::string(msg)); \
+  } while (0)
+
+// ---- programmatic dependent launch: a kernel waits for its predecessor's results only where it reads them ----
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// Prefetch [p, p + bytes) into L2 (no shared memory, no completion to wait for). p and bytes 16-byte aligned.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// ---- number formats ----
+// E4M3 decode (bias 7, subnormal steps of 2^-9, 0x7f NaN), FP32 exact.
+__device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
+  const int e = (b >> 3) & 15, m = b & 7;
+  float mag;
+  if ((b & 0x7f) == 0x7f)
+    mag = __int_as_float(0x7fc00000);
+  else if (e == 0)
+    mag = __int2float_rn(m) * 0.001953125f;   // 2^-9
+  else
+    mag = __int2float_rn(8 + m) * __int_as_float((e - 10 + 127) << 23);
+  return (b & 0x80) ? -mag : mag;
+}
+
+// FP32 -> E4M3, round to nearest even, saturating to 448 (the rule of the reference's f32_to_e4m3 / e4m3_bits).
+__device__ __forceinline__ uint8_t f32_to_e4m3(float f) {
+  const uint32_t u = __float_as_uint(f);
+  const uint8_t sign = (u >> 24) & 0x80;
+  const uint32_t a = u & 0x7fffffffu;
+  if (a > 0x7f800000u) return sign | 0x7f;
+  if (a >= 0x43e00000u) return sign | 0x7e;            // >= 448 (and infinity)
+  if (a < 0x3c800000u) {                                // below 2^-6: multiples of 2^-9
+    const float t = __fmul_rn(__uint_as_float(a), 512.f);
+    return sign | (uint8_t)__float2int_rn(t);
+  }
+  const int e = (int)(a >> 23) - 127;                   // -6 .. 8
+  const float t = __fmul_rn(__uint_as_float(a), __int_as_float((127 + 3 - e) << 23));   // [8, 16)
+  int mant = __float2int_rn(t);
+  int exp = e + 7;
+  if (mant == 16) {
+    mant = 8;
+    ++exp;
+  }
+  int code = (exp << 3) | (mant - 8);
+  return sign | (uint8_t)(code > 0x7e ? 0x7e : code);
+}
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);
+  return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+__device__ __forceinline__ float e2m1_to_f32(uint32_t nib) {
+  const uint32_t m = nib & 7;
+  // 0, 0.5, 1, 1.5, 2, 3, 4, 6
+  const float v = m < 4 ? 0.5f * (float)m : (float)(2u << ((m - 4) >> 1)) * ((m & 1) ? 1.5f : 1.f);
+  return (nib & 8) ? -v : v;
+}
+
+// Nearest E2M1 code, ties to the even code, saturating to 6 (the quantizer's rounding).
+__device__ __forceinline__ uint8_t e2m1_code(float q) {
+  const float a = fabsf(q);
+  int c = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) + (a >= 3.5f) + (a > 5.f);
+  if (q < 0.f) c |= 8;
+  return (uint8_t)c;
+}
+
+// Two E2M1 codes of a byte -> f16x2 (low nibble in the low half); exact.
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+  uint32_t r;
+  asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(r) : "r"(byte));
+  return r;
+}
+
+// Two E4M3 bytes (low, high of a 16-bit value) -> f16x2; exact.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two) {
+  uint32_t r;
+  const uint16_t h = (uint16_t)two;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(h));
+  return r;
+}
+
+// Two signed bytes (low, high of a 16-bit value in bits 0-15 of w) -> f16x2, exact: 1024 + 128 + b as a half, less
+// 1152.
+__device__ __forceinline__ uint32_t s8x2_to_f16x2(uint32_t biased_word, uint32_t sel) {
+  uint32_t r = __byte_perm(biased_word, 0x64646464u, sel);
+  const __half2 h = __hsub2(*reinterpret_cast<const __half2*>(&r), __halves2half2(__ushort_as_half(0x6480),
+                                                                                   __ushort_as_half(0x6480)));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// D = A(16x16, row) * B(16x8, col) + D, f16 inputs, f32 accumulation.
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ---- seeded generators, bit-identical to the oracle's xo_rand_bits / xo_gen_* ----
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z ^= z >> 30;
+  z *= 0xbf58476d1ce4e5b9ull;
+  z ^= z >> 27;
+  z *= 0x94d049bb133111ebull;
+  z ^= z >> 31;
+  return z;
+}
+
+__host__ __device__ __forceinline__ uint64_t rand_key(uint64_t seed, uint64_t stream) {
+  return mix64(seed + 0x9e3779b97f4a7c15ull * (stream + 1));
+}
+
+__host__ __device__ __forceinline__ uint64_t rand_bits(uint64_t key, uint64_t index) {
+  return mix64(key + 0x9e3779b97f4a7c15ull * (index + 1));
+}
+
+__device__ __forceinline__ float normal_from_bits(uint64_t b) {
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) s = __fadd_rn(s, __fadd_rn((float)((b >> (16 * j)) & 0xffff), 0.5f));
+  const float c = __fsub_rn(__fmul_rn(s, 1.f / 65536.f), 2.f);
+  return __fmul_rn(c, 1.7320508f);
+}
+
+__device__ __forceinline__ float uniform_from_bits(uint64_t b, float lo, float span) {
+  const float u = __fmul_rn((float)(b >> 40), 0x1p-24f);
+  return __fadd_rn(lo, __fmul_rn(span, u));
+}
+
+// ---- reductions ----
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum in a fixed order (deterministic), every thread gets the result. red: >= 32 floats of shared memory.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
+  t = warp_sum(t);
+  return t;
+}
+
+// ---- the activation operand of the NVFP4 GEMV: fp16 in the B-fragment order of mma.m16n8k16 ----
+// Element (k, n) of x^T (k < K, activation row n < 8) lives at byte offset:
+//   (k / 16) * 256 + (n * 4 + tq) * 8 + reg * 4 + (k & 1) * 2,  with w = k % 16, reg = w >= 8, tq = (w & 7) / 2
+__host__ __device__ __forceinline__ uint32_t frag_offset_halves(int k, int n) {
+  const int w = k & 15, reg = w >> 3, tq = (w & 7) >> 1;
+  return (uint32_t)((k >> 4) * 128 + (n * 4 + tq) * 4 + reg * 2 + (k & 1));
+}
+
+constexpr int kMaxRows = 8;   // activation rows of a verify step (mma N = 8)
+
+}  // namespace xtg

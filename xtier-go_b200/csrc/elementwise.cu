@@ -1,0 +1,324 @@
+// K4 / K5 helpers of the step: the embedding of a tied NVFP4 head (nvfp4_row, engine/src/kernels.cpp:34-45) with the
+// step's RoPE tables and ring bookkeeping, the nGPT residual updates (slerp_residual and the loop norms,
+// kernels.cpp:177-189 and packs/dory/dory.cpp:530-542), the argmax over the head's tile candidates
+// (engine/src/sampler.cpp:8-13), and the KV writes outside the attention kernel (KvCache::store, kv.cpp:75-112, in
+// this library's layout) plus the seeded KV prefill.
+#include "attention.h"
+#include "common.cuh"
+#include "elementwise.h"
+#include "kernels.h"
+
+namespace xtg {
+
+namespace {
+
+__device__ __forceinline__ float packed_weight(const uint8_t* w, int blocks, float global, int row, int k) {
+  const int t = row >> 4, rr = row & 15, g = rr & 7, hi = rr >> 3;
+  const int b = k >> 6, j = (k >> 4) & 3, w16 = k & 15, q = w16 >> 1, nib = w16 & 1;
+  const int tq = q & 3, part = hi + ((q >> 2) << 1);
+  const uint8_t* blk = w + ((int64_t)t * blocks + b) * kBlockBytes;
+  const uint8_t byte = blk[(g * 4 + tq) * 16 + 4 * j + part];
+  const uint8_t sc = blk[512 + g * 8 + 2 * j + hi];
+  const float s = __fmul_rn(e4m3_to_f32(sc), global);
+  return __fmul_rn(e2m1_to_f32(nib ? byte >> 4 : byte & 15), s);
+}
+
+__global__ void embed_kernel(const EmbedArgs a) {
+  const int r = blockIdx.x;
+  if (a.pdl) pdl_wait();
+  if (a.pdl) pdl_launch_next();
+  const StepParams* p = a.params;
+  const int m = p->m;
+  const int64_t pos0 = p->pos0;
+  if (r < m) {
+    const int tok = p->tokens[r];
+    for (int k2 = threadIdx.x * 2; k2 < a.hidden; k2 += blockDim.x * 2) {
+      const float v0 = packed_weight(a.head, a.blocks, a.global, tok, k2);
+      const float v1 = packed_weight(a.head, a.blocks, a.global, tok, k2 + 1);
+      a.h[(int64_t)r * a.hidden + k2] = v0;
+      a.h[(int64_t)r * a.hidden + k2 + 1] = v1;
+      a.x16[frag_offset_halves(k2, r) >> 1] = pack_f16x2(v0, v1);
+    }
+  } else {
+    for (int k2 = threadIdx.x * 2; k2 < a.hidden; k2 += blockDim.x * 2) a.x16[frag_offset_halves(k2, r) >> 1] = 0u;
+  }
+  // RoPE tables of this step's positions (FP32(pos) * inv_freq, then cos / sin), one per theta
+  if (r < a.n_thetas) {
+    for (int idx = threadIdx.x; idx < kMaxRows * 64; idx += blockDim.x) {
+      const int i = idx / 64, e = idx % 64;
+      const float ang = __fmul_rn((float)(pos0 + i), a.inv_freq[r * 64 + e]);
+      float s, c;
+      sincosf(ang, &s, &c);
+      a.rope_cos[(r * kMaxRows + i) * 64 + e] = c;
+      a.rope_sin[(r * kMaxRows + i) * 64 + e] = s;
+    }
+  }
+  // the ring's slot -> position table gains this step's rows (attention masks positions >= pos0 anyway)
+  if (r == 0 && a.ring_pos && threadIdx.x < m) {
+    const int64_t q = pos0 + threadIdx.x;
+    a.ring_pos[q % a.ring] = (int32_t)q;
+  }
+}
+
+// One CTA per activation row: the residual updates. All norms are justnorm: x / sqrt(sum x^2 + 1e-6).
+__global__ void resid_kernel(const ResidArgs a) {
+  __shared__ float red[32];
+  const int r = blockIdx.x, H = a.hidden;
+  if (a.pdl) pdl_wait();
+  if (a.pdl) pdl_launch_next();
+  const int m = a.params ? a.params->m : a.m;
+  float* h = a.h + (int64_t)r * H;
+  if (r >= m) {
+    for (int k2 = threadIdx.x * 2; k2 < H; k2 += blockDim.x * 2) a.x16[frag_offset_halves(k2, r) >> 1] = 0u;
+    return;
+  }
+  constexpr int kPer = 8;   // H <= kPer * blockDim
+  float v[kPer];
+  const int n = (H + blockDim.x - 1) / blockDim.x;
+  if (a.mode == kResidSlerp) {
+    const float* o = a.o + (int64_t)r * H;
+    float sa = 0.f, sb = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const int k = threadIdx.x + j * blockDim.x;
+      if (k < H) {
+        sa += h[k] * h[k];
+        sb += o[k] * o[k];
+      }
+    }
+    const float fa = 1.f / sqrtf(block_sum(sa, red) + 1e-6f);
+    const float fb = 1.f / sqrtf(block_sum(sb, red) + 1e-6f);
+    float s = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const int k = threadIdx.x + j * blockDim.x;
+      v[j] = 0.f;
+      if (k < H) {
+        const float ya = h[k] * fa, yb = o[k] * fb;
+        v[j] = ya + a.lr[k] * (yb - ya);
+        s += v[j] * v[j];
+      }
+    }
+    const float f = 1.f / sqrtf(block_sum(s, red) + 1e-6f);
+    for (int j = 0; j < n; ++j) v[j] *= f;
+  } else {
+    float* st = a.state + (int64_t)r * H;
+    float* in = a.input + (int64_t)r * H;
+    if (a.mode == kResidLoopBegin) {   // input = state = h
+      for (int j = 0; j < n; ++j) {
+        const int k = threadIdx.x + j * blockDim.x;
+        if (k < H) {
+          st[k] = h[k];
+          in[k] = h[k];
+        }
+      }
+    } else {   // the loop that ends: state = justnorm(h)
+      float s = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const int k = threadIdx.x + j * blockDim.x;
+        if (k < H) s += h[k] * h[k];
+      }
+      const float f = 1.f / sqrtf(block_sum(s, red) + 1e-6f);
+      for (int j = 0; j < n; ++j) {
+        const int k = threadIdx.x + j * blockDim.x;
+        if (k < H) st[k] = h[k] * f;
+      }
+    }
+    if (a.mode == kResidLoopEnd) {   // h = state
+      for (int j = 0; j < n; ++j) {
+        const int k = threadIdx.x + j * blockDim.x;
+        v[j] = k < H ? st[k] : 0.f;
+      }
+    } else {   // a loop begins: h = justnorm(state + input)
+      float s = 0.f;
+      for (int j = 0; j < n; ++j) {
+        const int k = threadIdx.x + j * blockDim.x;
+        v[j] = k < H ? st[k] + in[k] : 0.f;
+        s += v[j] * v[j];
+      }
+      const float f = 1.f / sqrtf(block_sum(s, red) + 1e-6f);
+      for (int j = 0; j < n; ++j) v[j] *= f;
+    }
+  }
+  // write h and its fp16 fragments (pairs of inputs through shared memory would cost a sync; write halves)
+  uint16_t* x16h = reinterpret_cast<uint16_t*>(a.x16);
+  for (int j = 0; j < n; ++j) {
+    const int k = threadIdx.x + j * blockDim.x;
+    if (k < H) {
+      h[k] = v[j];
+      x16h[frag_offset_halves(k, r)] = __half_as_ushort(__float2half_rn(v[j]));
+    }
+  }
+}
+
+__global__ void argmax_kernel(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out,
+                              float* out_val, int pdl) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const int n = blockIdx.x;
+  if (pdl) pdl_wait();
+  if (pdl) pdl_launch_next();
+  if (n >= params->m) return;
+  float v = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
+    const ArgCand c = cand[t * kMaxRows + n];
+    if (c.v > v || (c.v == v && c.i < idx)) {
+      v = c.v;
+      idx = c.i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    bv[warp] = v;
+    bi[warp] = idx;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    v = lane < nw ? bv[lane] : -INFINITY;
+    idx = lane < nw ? bi[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > v || (ov == v && oi < idx)) {
+        v = ov;
+        idx = oi;
+      }
+    }
+    if (lane == 0) {
+      out[n] = idx;
+      if (out_val) out_val[n] = v;
+    }
+  }
+}
+
+// KvCache::store in this library's layout: rows [n][kv_heads][128] at positions pos .. pos + n - 1 (a ring keeps
+// the last `slots`); one warp per (row, head, K or V).
+__global__ void kv_store_kernel(const KvStoreArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t task = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t total = (int64_t)a.n * a.kv_heads * 2;
+  if (task >= total) return;
+  const int kv = (int)(task % 2), h = (int)((task / 2) % a.kv_heads);
+  const int64_t r = task / (2 * a.kv_heads);
+  if (a.ring && r < a.n - a.slots) return;   // a long chunk leaves only its last `slots` rows in a ring
+  const int64_t p = a.pos + r, slot = a.ring ? p % a.slots : p;
+  const float* src = (kv ? a.v : a.k) + (r * a.kv_heads + h) * 128;
+  const float x[4] = {src[lane], src[lane + 64], src[lane + 32], src[lane + 96]};
+  float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+  amax = warp_max(amax);
+  const float top = a.dtype == kKvFp8 ? 448.f : 127.f;
+  const float sc = amax > 0.f ? __fdiv_rn(amax, top) : 1.f;
+  const float inv = __fdiv_rn(1.f, sc);
+  const int idx[4] = {lane, lane + 64, lane + 32, lane + 96};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float t = __fmul_rn(x[j], inv);
+    uint8_t c;
+    if (a.dtype == kKvFp8) {
+      c = f32_to_e4m3(t);
+    } else {
+      float q = fminf(fmaxf(rintf(t), -127.f), 127.f);
+      c = (uint8_t)(int8_t)(int)q;
+    }
+    if (kv)
+      a.vc[((int64_t)h * 128 + idx[j]) * a.slots + slot] = c;
+    else
+      a.kc[((int64_t)h * a.slots + slot) * 128 + idx[j]] = c;
+  }
+  if (lane == 0) (kv ? a.vs : a.ks)[(int64_t)h * a.slots + slot] = sc;
+}
+
+// The seeded prefill of one instance (the oracle's xo_synth_state_new): element (slot, head, e) of K / V codes is
+// draw (slot * kv_heads + head) * 128 + e of its stream, scales draw slot * kv_heads + head; `filled` slots.
+__global__ void kv_prefill_kernel(uint64_t key_k, uint64_t key_v, uint64_t key_ks, uint64_t key_vs, float lo,
+                                  float span, int64_t filled, int kv_heads, int64_t slots, uint8_t* kc, uint8_t* vc,
+                                  float* ks, float* vs) {
+  const int64_t total = filled * kv_heads * 128;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int e = (int)(i % 128);
+    const int64_t sh = i / 128;   // slot * kv_heads + head
+    const int h = (int)(sh % kv_heads);
+    const int64_t s = sh / kv_heads;
+    kc[((int64_t)h * slots + s) * 128 + e] = (uint8_t)(int8_t)((int)(rand_bits(key_k, i) % 255u) - 127);
+    vc[((int64_t)h * 128 + e) * slots + s] = (uint8_t)(int8_t)((int)(rand_bits(key_v, i) % 255u) - 127);
+    if (e == 0) {
+      ks[(int64_t)h * slots + s] = uniform_from_bits(rand_bits(key_ks, sh), lo, span);
+      vs[(int64_t)h * slots + s] = uniform_from_bits(rand_bits(key_vs, sh), lo, span);
+    }
+  }
+}
+
+template <class Args>
+void launch_pdl(void (*kernel)(Args), dim3 grid, dim3 block, const Args& args, cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, kernel, args));
+}
+
+}  // namespace
+
+void launch_embed(const EmbedArgs& a_in, cudaStream_t s, bool pdl) {
+  EmbedArgs a = a_in;
+  a.pdl = pdl ? 1 : 0;
+  launch_pdl(embed_kernel, dim3(kMaxRows), dim3(256), a, s, pdl);
+}
+
+void launch_resid(const ResidArgs& a_in, cudaStream_t s, bool pdl) {
+  ResidArgs a = a_in;
+  a.pdl = pdl ? 1 : 0;
+  XTG_REQUIRE(a.hidden <= 8 * 1024, "resid: hidden above 8192");
+  launch_pdl(resid_kernel, dim3(kMaxRows), dim3(1024), a, s, pdl);
+}
+
+void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out, float* out_val,
+                   cudaStream_t s, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kMaxRows);
+  cfg.blockDim = dim3(1024);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, argmax_kernel, cand, tiles, params, out, out_val, pdl ? 1 : 0));
+}
+
+void launch_kv_store(const KvStoreArgs& a, cudaStream_t s) {
+  const int64_t tasks = (int64_t)a.n * a.kv_heads * 2;
+  if (tasks == 0) return;
+  const int grid = (int)((tasks + 7) / 8);
+  kv_store_kernel<<<grid, 256, 0, s>>>(a);
+  XTG_CUDA(cudaGetLastError());
+}
+
+void kv_prefill(uint64_t seed, uint64_t stream_base, float lo, float hi, int64_t filled, int kv_heads, int64_t slots,
+                uint8_t* kc, uint8_t* vc, float* ks, float* vs, cudaStream_t s) {
+  if (filled <= 0) return;
+  const int64_t total = filled * kv_heads * 128;
+  const int64_t g = (total + 255) / 256;
+  const int grid = (int)(g < 148 * 16 ? g : 148 * 16);
+  kv_prefill_kernel<<<grid, 256, 0, s>>>(rand_key(seed, stream_base + 0), rand_key(seed, stream_base + 1),
+                                         rand_key(seed, stream_base + 2), rand_key(seed, stream_base + 3), lo,
+                                         hi - lo, filled, kv_heads, slots, kc, vc, ks, vs);
+  XTG_CUDA(cudaGetLastError());
+}
+
+}  // namespace xtg

@@ -1,0 +1,68 @@
+// Internal interface of the step's small kernels (elementwise.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "attention.h"
+#include "kernels.h"
+
+namespace xtg {
+
+struct EmbedArgs {
+  const StepParams* params;
+  const uint8_t* head;      // the tied NVFP4 head in the streaming layout
+  int blocks;               // 64-input blocks per row tile
+  float global;
+  int hidden;
+  float* h;                 // [8][hidden]
+  uint32_t* x16;            // fragments of h
+  const float* inv_freq;    // [n_thetas][64]
+  int n_thetas;
+  float* rope_cos;          // [n_thetas][8][64]
+  float* rope_sin;
+  int32_t* ring_pos;        // null without sliding layers
+  int64_t ring;
+  int pdl;
+};
+
+enum ResidMode { kResidSlerp = 0, kResidLoopBegin = 1, kResidLoopNext = 2, kResidLoopEnd = 3 };
+
+struct ResidArgs {
+  int mode;
+  const StepParams* params;
+  int m;
+  int hidden;
+  float* h;                 // [8][hidden]: the residual stream, updated in place
+  const float* o;           // slerp: the sublayer output [8][hidden]
+  const float* lr;          // slerp: [hidden]
+  float* state;             // loops: [8][hidden]
+  float* input;
+  uint32_t* x16;            // fragments of the new h
+  int pdl;
+};
+
+struct KvStoreArgs {
+  const float* k;           // [n][kv_heads][128]
+  const float* v;
+  int64_t pos;
+  int n;
+  int kv_heads;
+  int64_t slots;
+  int ring;
+  int dtype;
+  uint8_t* kc;
+  uint8_t* vc;
+  float* ks;
+  float* vs;
+};
+
+void launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
+void launch_resid(const ResidArgs& a, cudaStream_t s, bool pdl);
+void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out, float* out_val,
+                   cudaStream_t s, bool pdl);
+void launch_kv_store(const KvStoreArgs& a, cudaStream_t s);
+void kv_prefill(uint64_t seed, uint64_t stream_base, float lo, float hi, int64_t filled, int kv_heads, int64_t slots,
+                uint8_t* kc, uint8_t* vc, float* ks, float* vs, cudaStream_t s);
+
+}  // namespace xtg

@@ -1,0 +1,1073 @@
+// The session behind include/xtg_cuda.h: what npu/xtg_npu.cpp does for the Hexagon NPU (KV instances, the ring's
+// slot -> position table, rewinds, snapshots, context tiers, logits out through a callback), done on one B200 with
+// the step of packs/dory/dory.cpp:467-578 as a chain of sm_100a kernels captured once into a CUDA graph.
+//
+// HBM layout of a session:
+//   weight arena   every NVFP4 weight in the GEMV streaming layout (weights.cu), in execution order: per attention
+//                  evaluation the fused q|k|v|g weight then o; per MLP evaluation the interleaved gate/up weight then
+//                  down; the tied head last. The step streams it front to back once.
+//   KV instances   one per attention evaluation (loops unrolled, per_loop): global ones hold `context` slots (slot =
+//                  position), sliding ones a ring of `ring` slots; layouts in attention.cu.
+//   activations    the residual stream h (f32 [8][hidden]) and its fp16 fragments, the loop state and input, the
+//                  projection rows, attention partials, the gated attention / SwiGLU fragments, logits.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/xtg_cuda.h"
+#include "attention.h"
+#include "common.cuh"
+#include "elementwise.h"
+#include "json.h"
+#include "kernels.h"
+
+namespace xtg {
+
+namespace {
+
+struct Config {
+  int hidden = 3072, ffn = 9216, heads = 24, kv_heads = 6, head_dim = 128, vocab = 131072;
+  int n_in = 4, n_rec = 40, n_out = 4, loops = 2;
+  int window = 1024, ring = 1088, global_every = 4;
+  float theta_sliding = 1e4f, theta_global = 1e7f, weight_std = 0.02f;
+  float lr_lo = 0.05f, lr_hi = 0.2f, qs_lo = 48.f, qs_hi = 80.f, gs_lo = 25.f, gs_hi = 75.f;
+  float suv_lo = 25.f, suv_hi = 75.f, ls_lo = 100.f, ls_hi = 200.f, kvs_lo = 0.0008f, kvs_hi = 0.0016f;
+  uint64_t seed = 3;
+  // session options
+  int64_t context = 8192;
+  int kv_dtype = kKvInt8;
+  int snapshots = 2;
+  int decode_rows = 8;
+  int device = 0;
+  bool graph = true, pdl = true;
+  int splits_global = 0, splits_ring = 0;   // 0: chosen from the SM count
+
+  int n_evals() const { return n_in + n_rec * loops + n_out; }
+  int phys(int e) const {
+    if (e < n_in) return e;
+    e -= n_in;
+    if (e < n_rec * loops) return n_in + e % n_rec;
+    return n_in + n_rec + (e - n_rec * loops);
+  }
+  // 0 MLP, 1 sliding attention, 2 global attention (the oracle's xo_synth_kind)
+  int kind(int e) const {
+    const int l = phys(e);
+    if (l % 2) return 0;
+    const int a = l / 2;
+    return (global_every > 0 && a % global_every == global_every - 1) ? 2 : 1;
+  }
+};
+
+int64_t parse_tier(const std::string& s) {
+  if (s.empty()) throw CudaError("tier: empty");
+  char* end = nullptr;
+  const long long v = std::strtoll(s.c_str(), &end, 10);
+  if (end == s.c_str() || v <= 0) throw CudaError("tier: " + s + " is not a context length");
+  int64_t n = v;
+  if (*end == 'k' || *end == 'K') {
+    n *= 1024;
+    ++end;
+  }
+  if (*end) throw CudaError("tier: " + s + " is not a context length");
+  return n;
+}
+
+Config parse_config(const std::string& options) {
+  Config c;
+  Json o = options.empty() ? Json() : Json::parse(options);
+  if (o.kind != Json::Null && o.kind != Json::Object) throw CudaError("options: not a JSON object");
+  const Json& m = o.at("model");
+  auto I = [&](const char* k, int& v) { v = (int)m.number(k, v); };
+  auto F = [&](const char* k, float& v) { v = (float)m.number(k, v); };
+  I("hidden", c.hidden);
+  I("ffn", c.ffn);
+  I("heads", c.heads);
+  I("kv_heads", c.kv_heads);
+  I("head_dim", c.head_dim);
+  I("vocab", c.vocab);
+  I("n_in", c.n_in);
+  I("n_rec", c.n_rec);
+  I("n_out", c.n_out);
+  I("loops", c.loops);
+  I("window", c.window);
+  c.ring = c.window + 64;
+  I("ring", c.ring);
+  I("global_every", c.global_every);
+  F("theta_sliding", c.theta_sliding);
+  F("theta_global", c.theta_global);
+  F("weight_std", c.weight_std);
+  F("lr_lo", c.lr_lo);
+  F("lr_hi", c.lr_hi);
+  F("qs_lo", c.qs_lo);
+  F("qs_hi", c.qs_hi);
+  F("gs_lo", c.gs_lo);
+  F("gs_hi", c.gs_hi);
+  F("suv_lo", c.suv_lo);
+  F("suv_hi", c.suv_hi);
+  F("ls_lo", c.ls_lo);
+  F("ls_hi", c.ls_hi);
+  F("kvs_lo", c.kvs_lo);
+  F("kvs_hi", c.kvs_hi);
+  c.seed = (uint64_t)m.number("seed", (double)c.seed);
+  const Json& ctx = o.at("context");
+  if (ctx.kind == Json::String)
+    c.context = parse_tier(ctx.str);
+  else
+    c.context = (int64_t)o.number("context", (double)c.context);
+  const std::string dt = o.string("kv_dtype", "int8");
+  if (dt != "int8" && dt != "fp8") throw CudaError("kv_dtype: " + dt + " (int8 | fp8)");
+  c.kv_dtype = dt == "fp8" ? kKvFp8 : kKvInt8;
+  c.snapshots = (int)o.number("snapshots", c.snapshots);
+  c.decode_rows = (int)o.number("decode_rows", c.decode_rows);
+  c.device = (int)o.number("device", c.device);
+  c.graph = o.number("graph", 1) != 0;
+  c.pdl = o.number("pdl", 1) != 0;
+  c.splits_global = (int)o.number("splits_global", 0);
+  c.splits_ring = (int)o.number("splits_ring", 0);
+  if (c.head_dim != 128) throw CudaError("model: head_dim must be 128");
+  if (c.heads % c.kv_heads || c.heads / c.kv_heads > 4) throw CudaError("model: at most 4 q heads per KV head");
+  if (c.hidden % 64 || c.ffn % 64 || c.hidden > 8192) throw CudaError("model: hidden, ffn multiples of 64, hidden <= 8192");
+  if (c.vocab <= 0 || c.n_in < 0 || c.n_rec < 0 || c.n_out < 0 || c.loops < 0 || c.n_evals() <= 0)
+    throw CudaError("model: bad layer counts");
+  if (c.window <= 0 || c.ring % 64 || c.ring < c.window + kMaxRows)
+    throw CudaError("model: the ring needs window + 8 slots or more, a multiple of 64");
+  if (c.context < 64 || c.context % 64) throw CudaError("context: a multiple of 64");
+  if (c.decode_rows < 1 || c.decode_rows > kMaxRows) throw CudaError("decode_rows: 1..8");
+  if (c.snapshots < 0 || c.snapshots > 8) throw CudaError("snapshots: 0..8");
+  return c;
+}
+
+// A packed weight (or fused set) and where its tiles go.
+struct Linear {
+  uint8_t* w = nullptr;   // inside the arena
+  int tiles = 0, blocks = 0;
+  int64_t bytes = 0;
+  int64_t alg_bytes = 0;  // codes + scales + globals of the NVFP4 weights
+  int n_total = 0, k = 0;
+  TileOut* outs = nullptr;   // device, kEpiStore
+  float g0 = 1.f, g1 = 1.f;  // gate / up globals (kEpiSwiglu), head global
+};
+
+struct Eval {
+  int kind = 0;
+  Linear qkvg, o, gu, down;
+  float *lr = nullptr, *qscale = nullptr, *gscale = nullptr, *sg = nullptr, *su = nullptr;
+  int theta = 0;   // 0 sliding, 1 global
+  int cache = -1;
+};
+
+struct KvInst {
+  uint8_t *kc = nullptr, *vc = nullptr;
+  float *ks = nullptr, *vs = nullptr;
+  int64_t slots = 0;
+  bool ring = false;
+};
+
+struct Snap {
+  int64_t pos = -1;
+  std::vector<KvInst> rings;   // device copies of the ring instances
+  std::vector<int64_t> ring_pos;
+};
+
+enum KernelClass { kClsGemv = 0, kClsAttn = 1, kClsCombine = 2, kClsSmall = 3, kClasses = 4 };
+
+}  // namespace
+
+}  // namespace xtg
+
+using namespace xtg;
+
+struct xtg_cuda {
+  Config c;
+  cudaStream_t stream = nullptr;
+  int num_sms = 148;
+  std::vector<void*> allocs;   // freed at close
+  // model
+  uint8_t* arena = nullptr;
+  int64_t arena_bytes = 0;
+  std::vector<Eval> evals;
+  Linear head;
+  float* logit_scale = nullptr;
+  float* inv_freq = nullptr;   // [2][64]
+  // session
+  std::vector<KvInst> kv;
+  int32_t* ring_pos_dev = nullptr;
+  std::vector<int64_t> ring_pos;
+  int64_t n_past = 0;
+  std::vector<Snap> snaps;
+  int last_rows = 0;
+  // activations and scratch
+  StepParams* params_dev = nullptr;
+  StepParams* params_host = nullptr;
+  float *h = nullptr, *state = nullptr, *input = nullptr, *o = nullptr, *proj = nullptr, *part = nullptr;
+  uint32_t *x16 = nullptr, *a16 = nullptr, *v16 = nullptr;
+  float *asum = nullptr, *vsum = nullptr, *logits = nullptr, *logits_host = nullptr, *argmax_val = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  int32_t* argmax = nullptr;
+  ArgCand* cand = nullptr;
+  float* gemv_partial = nullptr;
+  int* gemv_counters = nullptr;
+  int gemv_grid_ = 0;
+  int splits_g = 1, splits_r = 1;
+  int proj_ld = 0;
+  // graph
+  cudaGraphExec_t exec = nullptr;
+  // profiling
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>>* prof = nullptr;
+  std::vector<int>* prof_cls = nullptr;
+
+  template <class T>
+  T* dalloc(size_t n, bool zero = true) {
+    void* p = nullptr;
+    XTG_CUDA(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    allocs.push_back(p);
+    if (zero) XTG_CUDA(cudaMemsetAsync(p, 0, std::max<size_t>(n, 1) * sizeof(T), stream));
+    return static_cast<T*>(p);
+  }
+
+  ~xtg_cuda() {
+    if (stream) cudaStreamSynchronize(stream);
+    if (exec) cudaGraphExecDestroy(exec);
+    free_kv(kv);
+    for (auto& s : snaps) free_kv(s.rings);
+    for (void* p : allocs) cudaFree(p);
+    if (params_host) cudaFreeHost(params_host);
+    if (logits_host) cudaFreeHost(logits_host);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  static void free_kv(std::vector<KvInst>& v) {
+    for (auto& k : v) {
+      cudaFree(k.kc);
+      cudaFree(k.vc);
+      cudaFree(k.ks);
+      cudaFree(k.vs);
+    }
+    v.clear();
+  }
+
+  static KvInst alloc_kv(int kv_heads, int64_t slots, bool ring, cudaStream_t s) {
+    KvInst k;
+    k.slots = slots;
+    k.ring = ring;
+    const size_t codes = (size_t)kv_heads * slots * 128, sc = (size_t)kv_heads * slots * sizeof(float);
+    cudaError_t e = cudaMalloc(&k.kc, codes);
+    if (e == cudaSuccess) e = cudaMalloc(&k.vc, codes);
+    if (e == cudaSuccess) e = cudaMalloc(&k.ks, sc);
+    if (e == cudaSuccess) e = cudaMalloc(&k.vs, sc);
+    if (e != cudaSuccess) {
+      cudaFree(k.kc);
+      cudaFree(k.vc);
+      cudaFree(k.ks);
+      cudaFree(k.vs);
+      cudaGetLastError();
+      throw CudaError(std::string("KV cache allocation: ") + cudaGetErrorString(e));
+    }
+    // zero codes: no stale FP8 NaN pattern is ever read, even under a mask
+    XTG_CUDA(cudaMemsetAsync(k.kc, 0, codes, s));
+    XTG_CUDA(cudaMemsetAsync(k.vc, 0, codes, s));
+    XTG_CUDA(cudaMemsetAsync(k.ks, 0, sc, s));
+    XTG_CUDA(cudaMemsetAsync(k.vs, 0, sc, s));
+    return k;
+  }
+
+  static void copy_kv(const KvInst& src, KvInst& dst, int kv_heads, int64_t used, cudaStream_t s) {
+    if (used <= 0) return;
+    // K [kv_heads][slots][128]: rows of used * 128 bytes
+    XTG_CUDA(cudaMemcpy2DAsync(dst.kc, dst.slots * 128, src.kc, src.slots * 128, used * 128, kv_heads,
+                               cudaMemcpyDeviceToDevice, s));
+    // V [kv_heads * 128][slots]: rows of used bytes
+    XTG_CUDA(cudaMemcpy2DAsync(dst.vc, dst.slots, src.vc, src.slots, used, (size_t)kv_heads * 128,
+                               cudaMemcpyDeviceToDevice, s));
+    XTG_CUDA(cudaMemcpy2DAsync(dst.ks, dst.slots * 4, src.ks, src.slots * 4, used * 4, kv_heads,
+                               cudaMemcpyDeviceToDevice, s));
+    XTG_CUDA(cudaMemcpy2DAsync(dst.vs, dst.slots * 4, src.vs, src.slots * 4, used * 4, kv_heads,
+                               cudaMemcpyDeviceToDevice, s));
+  }
+
+  // ---- model construction (the seeded synthetic Dory; the oracle's stream map) ----
+
+  void build_model() {
+    const int H = c.hidden, F = c.ffn, Q = c.heads * c.head_dim, KV = c.kv_heads * c.head_dim;
+    const int ne = c.n_evals();
+    // arena size
+    int64_t total = 0;
+    for (int e = 0; e < ne; ++e) {
+      if (c.kind(e) == 0)
+        total += packed_bytes(F, H, true) + packed_bytes(H, F, false);
+      else
+        total += packed_bytes(2 * Q + 2 * KV, H, false) + packed_bytes(H, Q, false);
+    }
+    total += packed_bytes(c.vocab, H, false);
+    // the fused q|k|v|g weight packs each projection in whole tiles
+    for (int e = 0; e < ne; ++e)
+      if (c.kind(e) != 0) {
+        total -= packed_bytes(2 * Q + 2 * KV, H, false);
+        total += (int64_t)(packed_tiles(Q, false) * 2 + packed_tiles(KV, false) * 2) * packed_blocks(H) * kBlockBytes;
+      }
+    arena_bytes = total;
+    arena = dalloc<uint8_t>((size_t)total, false);
+    // temporaries: the largest weight (the head) in bf16, ModelOpt codes / scales for two weights
+    const int64_t max_elems = std::max<int64_t>((int64_t)c.vocab * H, (int64_t)F * H);
+    uint16_t* raw = nullptr;
+    uint8_t *codes_a = nullptr, *scales_a = nullptr, *codes_b = nullptr, *scales_b = nullptr;
+    float* gdev = nullptr;
+    unsigned int* amax = nullptr;
+    XTG_CUDA(cudaMalloc(&raw, max_elems * 2));
+    XTG_CUDA(cudaMalloc(&codes_a, max_elems / 2));
+    XTG_CUDA(cudaMalloc(&scales_a, max_elems / 16));
+    XTG_CUDA(cudaMalloc(&codes_b, (int64_t)F * H / 2));
+    XTG_CUDA(cudaMalloc(&scales_b, (int64_t)F * H / 16));
+    XTG_CUDA(cudaMalloc(&gdev, 2 * sizeof(float)));
+    XTG_CUDA(cudaMalloc(&amax, sizeof(unsigned int)));
+    auto make = [&](uint64_t stream_id, int n_out, int k, uint8_t* codes, uint8_t* scales) {
+      gen_normal_bf16(c.seed, stream_id, c.weight_std, raw, (int64_t)n_out * k, stream);
+      quantize_nvfp4(raw, n_out, k, codes, scales, gdev, amax, stream);
+      float g = 0.f;
+      XTG_CUDA(cudaMemcpyAsync(&g, gdev, sizeof(float), cudaMemcpyDeviceToHost, stream));
+      XTG_CUDA(cudaStreamSynchronize(stream));
+      return g;
+    };
+    auto vec = [&](uint64_t stream_id, float lo, float hi, int n) {
+      float* v = dalloc<float>(n, false);
+      gen_uniform(c.seed, stream_id, lo, hi, v, n, stream);
+      return v;
+    };
+    uint8_t* cursor = arena;
+    auto place = [&](Linear& L, int tiles, int blocks) {
+      L.w = cursor;
+      L.tiles = tiles;
+      L.blocks = blocks;
+      L.bytes = (int64_t)tiles * blocks * kBlockBytes;
+      cursor += L.bytes;
+    };
+    auto alg = [](int n, int k) { return (int64_t)n * k / 2 + (int64_t)n * k / 16 + 4; };
+    proj_ld = 2 * Q + 2 * KV;
+    int n_attn = 0;
+    evals.resize(ne);
+    for (int e = 0; e < ne; ++e) {
+      Eval& E = evals[e];
+      E.kind = c.kind(e);
+      const uint64_t base = 1000 + 16 * (uint64_t)e;
+      E.lr = vec(base + 8, c.lr_lo, c.lr_hi, H);
+      if (E.kind == 0) {
+        E.sg = vec(base + 11, c.suv_lo, c.suv_hi, F);
+        E.su = vec(base + 12, c.suv_lo, c.suv_hi, F);
+        place(E.gu, packed_tiles(F, true), packed_blocks(H));
+        E.gu.g0 = make(base + 0, F, H, codes_a, scales_a);
+        E.gu.g1 = make(base + 1, F, H, codes_b, scales_b);
+        pack_nvfp4(codes_a, scales_a, codes_b, scales_b, F, H, true, E.gu.w, stream);
+        E.gu.alg_bytes = 2 * alg(F, H);
+        E.gu.n_total = 2 * F;
+        E.gu.k = H;
+        place(E.down, packed_tiles(H, false), packed_blocks(F));
+        const float gd = make(base + 2, H, F, codes_a, scales_a);
+        pack_nvfp4(codes_a, scales_a, nullptr, nullptr, H, F, false, E.down.w, stream);
+        E.down.alg_bytes = alg(H, F);
+        E.down.n_total = H;
+        E.down.k = F;
+        std::vector<TileOut> outs(E.down.tiles);
+        for (int t = 0; t < E.down.tiles; ++t) outs[t] = TileOut{o + 16 * t, H, std::min(16, H - 16 * t), gd, 0};
+        E.down.outs = upload(outs);
+      } else {
+        E.qscale = vec(base + 9, c.qs_lo, c.qs_hi, Q);
+        E.gscale = vec(base + 10, c.gs_lo, c.gs_hi, Q);
+        E.theta = E.kind == 2 ? 1 : 0;
+        E.cache = n_attn++;
+        const int tq = packed_tiles(Q, false), tk = packed_tiles(KV, false), blocks = packed_blocks(H);
+        place(E.qkvg, 2 * tq + 2 * tk, blocks);
+        std::vector<TileOut> outs;
+        const int n_out[4] = {Q, KV, KV, Q};
+        const int col[4] = {0, Q, Q + KV, Q + 2 * KV};
+        int tile0 = 0;
+        for (int j = 0; j < 4; ++j) {
+          const float gj = make(base + j, n_out[j], H, codes_a, scales_a);
+          pack_nvfp4(codes_a, scales_a, nullptr, nullptr, n_out[j], H, false,
+                     E.qkvg.w + (int64_t)tile0 * blocks * kBlockBytes, stream);
+          const int tj = packed_tiles(n_out[j], false);
+          for (int t = 0; t < tj; ++t)
+            outs.push_back(TileOut{proj + col[j] + 16 * t, proj_ld, std::min(16, n_out[j] - 16 * t), gj, 0});
+          tile0 += tj;
+          E.qkvg.alg_bytes += alg(n_out[j], H);
+        }
+        E.qkvg.outs = upload(outs);
+        E.qkvg.n_total = 2 * Q + 2 * KV;
+        E.qkvg.k = H;
+        place(E.o, packed_tiles(H, false), packed_blocks(Q));
+        const float go = make(base + 4, H, Q, codes_a, scales_a);
+        pack_nvfp4(codes_a, scales_a, nullptr, nullptr, H, Q, false, E.o.w, stream);
+        E.o.alg_bytes = alg(H, Q);
+        E.o.n_total = H;
+        E.o.k = Q;
+        std::vector<TileOut> oo(E.o.tiles);
+        for (int t = 0; t < E.o.tiles; ++t) oo[t] = TileOut{o + 16 * t, H, std::min(16, H - 16 * t), go, 0};
+        E.o.outs = upload(oo);
+      }
+    }
+    place(head, packed_tiles(c.vocab, false), packed_blocks(H));
+    head.g0 = make(1, c.vocab, H, codes_a, scales_a);
+    pack_nvfp4(codes_a, scales_a, nullptr, nullptr, c.vocab, H, false, head.w, stream);
+    head.alg_bytes = alg(c.vocab, H);
+    head.n_total = c.vocab;
+    head.k = H;
+    logit_scale = vec(2, c.ls_lo, c.ls_hi, c.vocab);
+    XTG_REQUIRE(cursor == arena + arena_bytes, "weight arena size mismatch");
+    // RoPE inverse frequencies, computed as the reference does on the host: 1 / theta^(2i / d) in FP32
+    std::vector<float> inv(128);
+    const float th[2] = {c.theta_sliding, c.theta_global};
+    for (int t = 0; t < 2; ++t)
+      for (int i = 0; i < 64; ++i) inv[t * 64 + i] = 1.f / std::pow(th[t], float(2 * i) / float(c.head_dim));
+    inv_freq = upload(inv);
+    XTG_CUDA(cudaStreamSynchronize(stream));
+    cudaFree(raw);
+    cudaFree(codes_a);
+    cudaFree(scales_a);
+    cudaFree(codes_b);
+    cudaFree(scales_b);
+    cudaFree(gdev);
+    cudaFree(amax);
+  }
+
+  template <class T>
+  T* upload(const std::vector<T>& v) {
+    T* p = dalloc<T>(v.size(), false);
+    XTG_CUDA(cudaMemcpyAsync(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, stream));
+    XTG_CUDA(cudaStreamSynchronize(stream));   // the host vector goes out of scope
+    return p;
+  }
+
+  void alloc_activations() {
+    const int H = c.hidden, F = c.ffn, Q = c.heads * c.head_dim, KV = c.kv_heads * c.head_dim;
+    (void)KV;
+    params_dev = dalloc<StepParams>(1);
+    XTG_CUDA(cudaMallocHost(&params_host, sizeof(StepParams)));
+    std::memset(params_host, 0, sizeof(StepParams));
+    h = dalloc<float>((size_t)kMaxRows * H);
+    state = dalloc<float>((size_t)kMaxRows * H);
+    input = dalloc<float>((size_t)kMaxRows * H);
+    o = dalloc<float>((size_t)kMaxRows * H);
+    proj = dalloc<float>((size_t)kMaxRows * (2 * Q + 2 * KV));
+    x16 = dalloc<uint32_t>((size_t)packed_blocks(H) * 4 * 64);
+    a16 = dalloc<uint32_t>((size_t)packed_blocks(Q) * 4 * 64);
+    v16 = dalloc<uint32_t>((size_t)packed_blocks(F) * 4 * 64);
+    asum = dalloc<float>((size_t)c.heads * kMaxRows);
+    vsum = dalloc<float>((size_t)packed_tiles(F, true) * kMaxRows);
+    logits = dalloc<float>((size_t)kMaxRows * c.vocab);
+    XTG_CUDA(cudaMallocHost(&logits_host, (size_t)kMaxRows * c.vocab * sizeof(float)));
+    cand = dalloc<ArgCand>((size_t)packed_tiles(c.vocab, false) * kMaxRows);
+    argmax = dalloc<int32_t>(kMaxRows);
+    argmax_val = dalloc<float>(kMaxRows);
+    rope_cos = dalloc<float>(2 * kMaxRows * 64);
+    rope_sin = dalloc<float>(2 * kMaxRows * 64);
+    gemv_grid_ = gemv_grid(num_sms);
+    gemv_partial = dalloc<float>((size_t)gemv_partial_floats(gemv_grid_));
+    gemv_counters = dalloc<int>((size_t)packed_tiles(c.vocab, false) + 4096);
+    splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, (num_sms + c.kv_heads - 1) / c.kv_heads);
+    splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, std::min<int>(c.ring / 64, 8));
+    part = dalloc<float>((size_t)attention_part_floats(c.kv_heads, std::max(splits_g, splits_r)));
+    ring_pos_dev = dalloc<int32_t>(c.ring);
+    ring_pos.assign(c.ring, -1);
+    std::vector<int32_t> neg(c.ring, -1);
+    XTG_CUDA(cudaMemcpyAsync(ring_pos_dev, neg.data(), neg.size() * 4, cudaMemcpyHostToDevice, stream));
+    XTG_CUDA(cudaStreamSynchronize(stream));
+  }
+
+  void alloc_caches() {
+    for (int e = 0; e < c.n_evals(); ++e)
+      if (evals[e].kind != 0)
+        kv.push_back(alloc_kv(c.kv_heads, evals[e].kind == 1 ? c.ring : c.context, evals[e].kind == 1, stream));
+    snaps.resize(c.snapshots);
+  }
+
+  // ---- the step ----
+
+  void mark(int cls, bool begin) {
+    if (!prof) return;
+    if (begin) {
+      cudaEvent_t a, b;
+      XTG_CUDA(cudaEventCreate(&a));
+      XTG_CUDA(cudaEventCreate(&b));
+      prof->push_back({a, b});
+      prof_cls->push_back(cls);
+      XTG_CUDA(cudaEventRecord(a, stream));
+    } else {
+      XTG_CUDA(cudaEventRecord(prof->back().second, stream));
+    }
+  }
+
+  void gemv(const Linear& L, int epi, const uint32_t* xin, const float* sumsq, int nparts, bool pdl) {
+    GemvArgs a = {};
+    a.w = L.w;
+    a.tiles = L.tiles;
+    a.blocks = L.blocks;
+    a.x16 = xin;
+    a.m_dev = &params_dev->m;
+    a.partial = gemv_partial;
+    a.counters = gemv_counters;
+    a.outs = L.outs;
+    a.sumsq = sumsq;
+    a.nparts = nparts;
+    mark(kClsGemv, true);
+    launch_gemv(epi, a, gemv_grid_, stream, pdl);
+    mark(kClsGemv, false);
+  }
+
+  void enqueue_step(bool pdl) {
+    const int H = c.hidden, F = c.ffn, Q = c.heads * c.head_dim;
+    mark(kClsSmall, true);
+    EmbedArgs ea = {};
+    ea.params = params_dev;
+    ea.head = head.w;
+    ea.blocks = head.blocks;
+    ea.global = head.g0;
+    ea.hidden = H;
+    ea.h = h;
+    ea.x16 = x16;
+    ea.inv_freq = inv_freq;
+    ea.n_thetas = 2;
+    ea.rope_cos = rope_cos;
+    ea.rope_sin = rope_sin;
+    ea.ring_pos = ring_pos_dev;
+    ea.ring = c.ring;
+    launch_embed(ea, stream, false);
+    mark(kClsSmall, false);
+    auto resid = [&](int mode, const float* lr) {
+      ResidArgs r = {};
+      r.mode = mode;
+      r.params = params_dev;
+      r.hidden = H;
+      r.h = h;
+      r.o = o;
+      r.lr = lr;
+      r.state = state;
+      r.input = input;
+      r.x16 = x16;
+      mark(kClsSmall, true);
+      launch_resid(r, stream, pdl);
+      mark(kClsSmall, false);
+    };
+    auto sublayer = [&](int e) {
+      const Eval& E = evals[e];
+      if (E.kind == 0) {
+        GemvArgs a = {};
+        a.w = E.gu.w;
+        a.tiles = E.gu.tiles;
+        a.blocks = E.gu.blocks;
+        a.x16 = x16;
+        a.m_dev = &params_dev->m;
+        a.partial = gemv_partial;
+        a.counters = gemv_counters;
+        a.g_gate = E.gu.g0;
+        a.g_up = E.gu.g1;
+        a.sg = E.sg;
+        a.su = E.su;
+        a.features = F;
+        a.v16 = reinterpret_cast<uint16_t*>(v16);
+        a.vsum = vsum;
+        mark(kClsGemv, true);
+        launch_gemv(kEpiSwiglu, a, gemv_grid_, stream, pdl);
+        mark(kClsGemv, false);
+        gemv(E.down, kEpiStore, v16, vsum, E.gu.tiles, pdl);
+        resid(kResidSlerp, E.lr);
+        return;
+      }
+      gemv(E.qkvg, kEpiStore, x16, nullptr, 0, pdl);
+      const KvInst& K = kv[E.cache];
+      AttnArgs at = {};
+      at.proj = proj;
+      at.proj_ld = proj_ld;
+      at.qscale = E.qscale;
+      at.rope_cos = rope_cos + E.theta * kMaxRows * 64;
+      at.rope_sin = rope_sin + E.theta * kMaxRows * 64;
+      at.kc = K.kc;
+      at.vc = K.vc;
+      at.ks = K.ks;
+      at.vs = K.vs;
+      at.slots = K.slots;
+      at.ring = K.ring ? 1 : 0;
+      at.ring_pos = ring_pos_dev;
+      at.dtype = c.kv_dtype;
+      at.store = 1;
+      at.window = K.ring ? c.window : 0;
+      at.scale = 1.f / std::sqrt((float)c.head_dim);
+      at.params = params_dev;
+      at.heads = c.heads;
+      at.kv_heads = c.kv_heads;
+      at.splits = K.ring ? splits_r : splits_g;
+      at.part = part;
+      mark(kClsAttn, true);
+      launch_attention(at, stream, pdl);
+      mark(kClsAttn, false);
+      CombineArgs cb = {};
+      cb.part = part;
+      cb.splits = at.splits;
+      cb.heads = c.heads;
+      cb.kv_heads = c.kv_heads;
+      cb.params = params_dev;
+      cb.gate = proj + Q + 2 * c.kv_heads * c.head_dim;
+      cb.gate_ld = proj_ld;
+      cb.gscale = E.gscale;
+      cb.a16 = reinterpret_cast<uint16_t*>(a16);
+      cb.asum = asum;
+      mark(kClsCombine, true);
+      launch_attn_combine(cb, stream, pdl);
+      mark(kClsCombine, false);
+      gemv(E.o, kEpiStore, a16, asum, c.heads, pdl);
+      resid(kResidSlerp, E.lr);
+    };
+    int e = 0;
+    for (int l = 0; l < c.n_in; ++l) sublayer(e++);
+    if (c.loops > 0) {
+      resid(kResidLoopBegin, nullptr);
+      for (int i = 0; i < c.loops; ++i) {
+        for (int r = 0; r < c.n_rec; ++r) sublayer(e++);
+        resid(i + 1 < c.loops ? kResidLoopNext : kResidLoopEnd, nullptr);
+      }
+    }
+    for (int l = 0; l < c.n_out; ++l) sublayer(e++);
+    GemvArgs a = {};
+    a.w = head.w;
+    a.tiles = head.tiles;
+    a.blocks = head.blocks;
+    a.x16 = x16;
+    a.m_dev = &params_dev->m;
+    a.partial = gemv_partial;
+    a.counters = gemv_counters;
+    a.g_head = head.g0;
+    a.logit_scale = logit_scale;
+    a.logits = logits;
+    a.vocab = c.vocab;
+    a.cand = cand;
+    mark(kClsGemv, true);
+    launch_gemv(kEpiHead, a, gemv_grid_, stream, pdl);
+    mark(kClsGemv, false);
+    mark(kClsSmall, true);
+    launch_argmax(cand, head.tiles, params_dev, argmax, argmax_val, stream, pdl);
+    mark(kClsSmall, false);
+  }
+
+  void capture() {
+    if (exec) return;
+    cudaGraph_t g = nullptr;
+    XTG_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      XTG_CUDA(cudaMemcpyAsync(params_dev, params_host, sizeof(StepParams), cudaMemcpyHostToDevice, stream));
+      enqueue_step(c.pdl);
+    } catch (...) {
+      cudaStreamEndCapture(stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    XTG_CUDA(cudaStreamEndCapture(stream, &g));
+    cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    XTG_CUDA(e);
+  }
+
+  // One step of m rows at n_past (params_host filled), without the host bookkeeping.
+  void launch_step() {
+    if (c.graph) {
+      capture();
+      XTG_CUDA(cudaGraphLaunch(exec, stream));
+    } else {
+      XTG_CUDA(cudaMemcpyAsync(params_dev, params_host, sizeof(StepParams), cudaMemcpyHostToDevice, stream));
+      enqueue_step(c.pdl);
+    }
+  }
+
+  void set_params(const int32_t* tokens, int m) {
+    std::memset(params_host, 0, sizeof(StepParams));
+    for (int i = 0; i < m; ++i) params_host->tokens[i] = tokens[i];
+    params_host->m = m;
+    params_host->pos0 = n_past;
+  }
+
+  void commit(int m) {
+    for (int r = 0; r < m; ++r) ring_pos[(n_past + r) % c.ring] = n_past + r;
+    n_past += m;
+  }
+
+  void forward(const int32_t* tokens, int n, int want, xtg_cuda_logits_fn fn, void* user) {
+    if (n <= 0) return;
+    for (int i = 0; i < n; ++i)
+      if (tokens[i] < 0 || tokens[i] >= c.vocab)
+        throw CudaError("token " + std::to_string(tokens[i]) + " out of range");
+    if (n_past + n > c.context)
+      throw CudaError("context full: " + std::to_string(n_past) + " + " + std::to_string(n) + " tokens (" +
+                      std::to_string(c.context) + ")");
+    for (Snap& s : snaps)   // a snapshot past this point no longer matches what the caches will hold
+      if (s.pos > n_past) s.pos = -1;
+    for (int off = 0; off < n; off += c.decode_rows) {
+      const int m = std::min(c.decode_rows, n - off);
+      set_params(tokens + off, m);
+      launch_step();
+      const int r0 = want == 2 ? 0 : (want == 1 && off + m == n ? m - 1 : m);
+      if (r0 < m && fn)
+        XTG_CUDA(cudaMemcpyAsync(logits_host + (size_t)r0 * c.vocab, logits + (size_t)r0 * c.vocab,
+                                 (size_t)(m - r0) * c.vocab * sizeof(float), cudaMemcpyDeviceToHost, stream));
+      XTG_CUDA(cudaStreamSynchronize(stream));
+      commit(m);
+      last_rows = m;
+      if (fn)
+        for (int i = r0; i < m; ++i) fn(off + i, logits_host + (size_t)i * c.vocab, user);
+    }
+  }
+
+  bool rewind(int64_t to) {
+    if (to < 0 || to > n_past) return false;
+    for (int64_t q = std::max<int64_t>(0, to - c.window + 1); q < to; ++q)
+      if (ring_pos[q % c.ring] != q) return false;
+    n_past = to;
+    return true;
+  }
+
+  void snapshot(int slot) {
+    if (slot < 0 || slot >= (int)snaps.size()) return;
+    Snap& s = snaps[slot];
+    if (s.rings.empty())
+      for (const KvInst& k : kv)
+        if (k.ring) s.rings.push_back(alloc_kv(c.kv_heads, k.slots, true, stream));
+    size_t i = 0;
+    for (const KvInst& k : kv)
+      if (k.ring) copy_kv(k, s.rings[i++], c.kv_heads, k.slots, stream);
+    XTG_CUDA(cudaStreamSynchronize(stream));
+    s.ring_pos = ring_pos;
+    s.pos = n_past;
+  }
+
+  bool restore(int slot) {
+    if (slot < 0 || slot >= (int)snaps.size() || snaps[slot].pos < 0) return false;
+    Snap& s = snaps[slot];
+    size_t i = 0;
+    for (KvInst& k : kv)
+      if (k.ring) copy_kv(s.rings[i++], k, c.kv_heads, k.slots, stream);
+    ring_pos = s.ring_pos;
+    upload_ring_pos();
+    n_past = s.pos;
+    return true;
+  }
+
+  void upload_ring_pos() {
+    std::vector<int32_t> rp(ring_pos.begin(), ring_pos.end());
+    XTG_CUDA(cudaMemcpyAsync(ring_pos_dev, rp.data(), rp.size() * 4, cudaMemcpyHostToDevice, stream));
+    XTG_CUDA(cudaStreamSynchronize(stream));
+  }
+
+  void grow(int64_t ctx) {
+    if (ctx < 64 || ctx % 64) throw CudaError("tier: a context of a multiple of 64 positions");
+    if (ctx < n_past) throw CudaError("tier " + std::to_string(ctx) + " cannot hold " + std::to_string(n_past) +
+                                      " positions");
+    if (ctx == c.context) return;
+    std::vector<KvInst> next;
+    try {
+      for (const KvInst& k : kv) {
+        if (k.ring) continue;
+        next.push_back(alloc_kv(c.kv_heads, ctx, false, stream));
+        copy_kv(k, next.back(), c.kv_heads, n_past, stream);
+      }
+      XTG_CUDA(cudaStreamSynchronize(stream));
+    } catch (...) {
+      free_kv(next);
+      throw;
+    }
+    size_t i = 0;
+    for (KvInst& k : kv) {
+      if (k.ring) continue;
+      cudaFree(k.kc);
+      cudaFree(k.vc);
+      cudaFree(k.ks);
+      cudaFree(k.vs);
+      k = next[i++];
+    }
+    c.context = ctx;
+    for (Snap& s : snaps)   // a smaller tier drops what it cannot hold
+      if (s.pos > ctx) s.pos = -1;
+    if (exec) {   // the graph holds the old caches' addresses
+      cudaGraphExecDestroy(exec);
+      exec = nullptr;
+    }
+  }
+
+  void prefill_synthetic(int64_t n) {
+    if (n < 0 || n > c.context) throw CudaError("prefill: " + std::to_string(n) + " positions do not fit the tier");
+    for (size_t i = 0; i < kv.size(); ++i) {
+      KvInst& k = kv[i];
+      const int64_t filled = k.ring ? std::min<int64_t>(n, k.slots) : n;
+      kv_prefill(c.seed, 500000 + 8 * (uint64_t)i, c.kvs_lo, c.kvs_hi, filled, c.kv_heads, k.slots, k.kc, k.vc, k.ks,
+                 k.vs, stream);
+    }
+    for (int r = 0; r < c.ring; ++r) {
+      int64_t p = -1;
+      if (n > 0) {
+        const int64_t last = n - 1;
+        p = last - ((last - r) % c.ring + c.ring) % c.ring;
+      }
+      ring_pos[r] = p;
+    }
+    upload_ring_pos();
+    n_past = n;
+    for (Snap& s : snaps) s.pos = -1;
+  }
+
+  int64_t kv_bytes() const {
+    int64_t b = 0;
+    for (const KvInst& k : kv) b += (int64_t)c.kv_heads * k.slots * (2 * 128 + 8);
+    return b;
+  }
+
+  int64_t step_bytes(int what, int m) const {
+    const int H = c.hidden, Q = c.heads * c.head_dim;
+    int64_t gemv = 0, attn = 0;
+    auto act = [&](const Linear& L) { return (int64_t)m * L.k * 2 + (int64_t)m * L.n_total * 4; };
+    for (const Eval& E : evals) {
+      if (E.kind == 0) {
+        gemv += E.gu.alg_bytes + act(E.gu) + E.down.alg_bytes + act(E.down);
+      } else {
+        gemv += E.qkvg.alg_bytes + act(E.qkvg) + E.o.alg_bytes + act(E.o);
+        const int64_t keys = E.kind == 1 ? c.ring : n_past;
+        attn += keys * c.kv_heads * (2 * 128 + 8) + (int64_t)m * Q * 4 * 2;
+      }
+    }
+    gemv += head.alg_bytes + act(head);
+    (void)H;
+    return what == 1 ? gemv : what == 2 ? attn : gemv + attn;
+  }
+};
+
+namespace {
+
+void set_err(char* err, int len, const char* what) {
+  if (err && len > 0) std::snprintf(err, (size_t)len, "%s", what);
+}
+
+template <class F>
+int guarded(char* err, int err_len, F&& f) {
+  try {
+    f();
+    return 0;
+  } catch (const std::exception& e) {
+    set_err(err, err_len, e.what());
+    return -1;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+xtg_cuda* xtg_cuda_open(const char* model_path, const char* options, char* err, int err_len) {
+  std::unique_ptr<xtg_cuda> h;
+  try {
+    const std::string path = model_path ? model_path : "";
+    if (path != "synthetic")
+      throw CudaError("model " + path + ": only \"synthetic\" (the seeded synthetic Dory) is supported");
+    h = std::make_unique<xtg_cuda>();
+    h->c = parse_config(options ? options : "");
+    int ndev = 0;
+    XTG_CUDA(cudaGetDeviceCount(&ndev));
+    XTG_REQUIRE(h->c.device >= 0 && h->c.device < ndev, "device: no CUDA device " + std::to_string(h->c.device));
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    cudaDeviceProp prop;
+    XTG_CUDA(cudaGetDeviceProperties(&prop, h->c.device));
+    XTG_REQUIRE(prop.major == 10, std::string("libxtg_cuda is built for sm_100a; device is ") + prop.name);
+    h->num_sms = prop.multiProcessorCount;
+    XTG_CUDA(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+    h->alloc_activations();
+    h->build_model();
+    h->alloc_caches();
+    XTG_CUDA(cudaStreamSynchronize(h->stream));
+  } catch (const std::exception& e) {
+    set_err(err, err_len, e.what());
+    return nullptr;
+  }
+  return h.release();
+}
+
+int xtg_cuda_info(xtg_cuda* h, char* out, int out_len) {
+  int rings = 0;
+  for (const KvInst& k : h->kv) rings += k.ring;
+  const int len = std::snprintf(
+      out, (size_t)(out_len > 0 ? out_len : 0),
+      "{\"vocab\":%d,\"context\":%lld,\"max_position\":%lld,\"prefill_ar\":%d,\"decode_ar\":%d,"
+      "\"kv_instances\":%d,\"ring_instances\":%d,\"ring_slots\":%d,\"sliding_window\":%d,\"kv_bytes\":%lld,"
+      "\"snapshots\":%d,\"kvmap\":false,\"kv_dtype\":\"%s\",\"weight_bytes\":%lld,\"hidden\":%d,\"evaluations\":%d,"
+      "\"sm_count\":%d,\"graph\":%s,\"pdl\":%s,\"splits_global\":%d,\"splits_ring\":%d}",
+      h->c.vocab, (long long)h->c.context, (long long)h->c.context - 1, h->c.decode_rows, h->c.decode_rows,
+      (int)h->kv.size(), rings, h->c.ring, h->c.window, (long long)h->kv_bytes(), (int)h->snaps.size(),
+      h->c.kv_dtype == kKvFp8 ? "fp8" : "int8", (long long)h->arena_bytes, h->c.hidden, h->c.n_evals(), h->num_sms,
+      h->c.graph ? "true" : "false", h->c.pdl ? "true" : "false", h->splits_g, h->splits_r);
+  return len < out_len ? len : -1;
+}
+
+int xtg_cuda_forward(xtg_cuda* h, const int32_t* tokens, int n, int want, xtg_cuda_logits_fn fn, void* user,
+                     char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    h->forward(tokens, n, want, fn, user);
+  });
+}
+
+int64_t xtg_cuda_pos(xtg_cuda* h) { return h->n_past; }
+
+int xtg_cuda_rewind(xtg_cuda* h, int64_t n) { return h->rewind(n) ? 0 : -1; }
+
+int xtg_cuda_snapshot_slots(xtg_cuda* h) { return (int)h->snaps.size(); }
+
+int64_t xtg_cuda_snapshot_pos(xtg_cuda* h, int slot) {
+  return slot >= 0 && slot < (int)h->snaps.size() ? h->snaps[slot].pos : -1;
+}
+
+void xtg_cuda_snapshot(xtg_cuda* h, int slot) {
+  try {
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    h->snapshot(slot);
+  } catch (const std::exception&) {
+    if (slot >= 0 && slot < (int)h->snaps.size()) h->snaps[slot].pos = -1;
+  }
+}
+
+int xtg_cuda_restore(xtg_cuda* h, int slot) {
+  try {
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    return h->restore(slot) ? 0 : -1;
+  } catch (const std::exception&) {
+    return -1;
+  }
+}
+
+int xtg_cuda_grow(xtg_cuda* h, const char* tier, char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    h->grow(parse_tier(tier ? tier : ""));
+  });
+}
+
+int64_t xtg_cuda_debug_cache(xtg_cuda* h, int instance, int value, void* out, int64_t len) {
+  if (instance < 0 || instance >= (int)h->kv.size() || value < 0 || value > 3) return -1;
+  const KvInst& k = h->kv[instance];
+  const int kvh = h->c.kv_heads;
+  const int64_t codes = (int64_t)kvh * k.slots * 128, scales = (int64_t)kvh * k.slots * 4;
+  const int64_t bytes = value < 2 ? codes : scales;
+  if (!out || len < bytes) return bytes;
+  try {
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    if (value >= 2) {
+      XTG_CUDA(cudaMemcpy(out, value == 2 ? k.ks : k.vs, bytes, cudaMemcpyDeviceToHost));
+      return bytes;
+    }
+    std::vector<uint8_t> tmp(bytes);
+    XTG_CUDA(cudaMemcpy(tmp.data(), value == 0 ? k.kc : k.vc, bytes, cudaMemcpyDeviceToHost));
+    uint8_t* o = static_cast<uint8_t*>(out);
+    // K: ours [h][slot][d] -> [h][d][slot]; V: ours [h][d][slot] -> [h][slot][d]
+    for (int hh = 0; hh < kvh; ++hh)
+      for (int64_t s = 0; s < k.slots; ++s)
+        for (int d = 0; d < 128; ++d) {
+          if (value == 0)
+            o[((int64_t)hh * 128 + d) * k.slots + s] = tmp[((int64_t)hh * k.slots + s) * 128 + d];
+          else
+            o[((int64_t)hh * k.slots + s) * 128 + d] = tmp[((int64_t)hh * 128 + d) * k.slots + s];
+        }
+  } catch (const std::exception&) {
+    return -1;
+  }
+  return bytes;
+}
+
+void xtg_cuda_close(xtg_cuda* h) {
+  if (!h) return;
+  cudaSetDevice(h->c.device);
+  delete h;
+}
+
+int xtg_cuda_argmax(xtg_cuda* h, int32_t* out, int n) {
+  try {
+    const int rows = std::min(n, h->last_rows);
+    if (rows <= 0) return -1;
+    XTG_CUDA(cudaMemcpy(out, h->argmax, rows * sizeof(int32_t), cudaMemcpyDeviceToHost));
+    return rows;
+  } catch (const std::exception&) {
+    return -1;
+  }
+}
+
+int xtg_cuda_prefill_synthetic(xtg_cuda* h, int64_t n_past, char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    h->prefill_synthetic(n_past);
+  });
+}
+
+int xtg_cuda_bench(xtg_cuda* h, const int32_t* tokens, int m, int steps, int profile, double* out_ms,
+                   double* out_class_ms, int64_t* out_class_launches, char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    XTG_REQUIRE(m >= 1 && m <= h->c.decode_rows, "bench: 1..decode_rows rows");
+    XTG_REQUIRE(steps >= 1, "bench: at least one step");
+    for (int i = 0; i < m; ++i) XTG_REQUIRE(tokens[i] >= 0 && tokens[i] < h->c.vocab, "bench: token out of range");
+    XTG_REQUIRE(h->n_past + m <= h->c.context, "bench: context full");
+    h->set_params(tokens, m);
+    if (!profile) {
+      h->launch_step();   // capture / warm
+      cudaEvent_t a, b;
+      XTG_CUDA(cudaEventCreate(&a));
+      XTG_CUDA(cudaEventCreate(&b));
+      XTG_CUDA(cudaEventRecord(a, h->stream));
+      for (int s = 0; s < steps; ++s) h->launch_step();
+      XTG_CUDA(cudaEventRecord(b, h->stream));
+      XTG_CUDA(cudaEventSynchronize(b));
+      float ms = 0.f;
+      XTG_CUDA(cudaEventElapsedTime(&ms, a, b));
+      cudaEventDestroy(a);
+      cudaEventDestroy(b);
+      if (out_ms) *out_ms = ms / steps;
+    } else {
+      std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
+      std::vector<int> cls;
+      double cms[kClasses] = {0, 0, 0, 0};
+      int64_t cl[kClasses] = {0, 0, 0, 0};
+      double total = 0;
+      for (int s = 0; s < steps; ++s) {
+        h->prof = &ev;
+        h->prof_cls = &cls;
+        XTG_CUDA(cudaMemcpyAsync(h->params_dev, h->params_host, sizeof(StepParams), cudaMemcpyHostToDevice,
+                                 h->stream));
+        try {
+          h->enqueue_step(false);
+        } catch (...) {
+          h->prof = nullptr;
+          h->prof_cls = nullptr;
+          throw;
+        }
+        h->prof = nullptr;
+        h->prof_cls = nullptr;
+        XTG_CUDA(cudaStreamSynchronize(h->stream));
+        for (size_t i = 0; i < ev.size(); ++i) {
+          float ms = 0.f;
+          XTG_CUDA(cudaEventElapsedTime(&ms, ev[i].first, ev[i].second));
+          cms[cls[i]] += ms;
+          cl[cls[i]] += 1;
+          total += ms;
+          cudaEventDestroy(ev[i].first);
+          cudaEventDestroy(ev[i].second);
+        }
+        ev.clear();
+        cls.clear();
+      }
+      if (out_ms) *out_ms = total / steps;
+      for (int c = 0; c < kClasses; ++c) {
+        if (out_class_ms) out_class_ms[c] = cms[c] / steps;
+        if (out_class_launches) out_class_launches[c] = cl[c] / steps;
+      }
+    }
+    // the steps wrote positions n_past .. n_past + m - 1 into the rings: the state of a forward rewound to n_past
+    for (int r = 0; r < m; ++r) h->ring_pos[(h->n_past + r) % h->c.ring] = h->n_past + r;
+    h->last_rows = m;
+  });
+}
+
+int64_t xtg_cuda_step_bytes(xtg_cuda* h, int what, int m) { return h->step_bytes(what, m); }
+
+}  // extern "C"
