@@ -1,0 +1,382 @@
+"""Benchmark of the Dory verify step on B200s, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...    (one rank per GPU, NCCL only for the barrier / max)
+
+A step is one 8-row verify step of the synthetic Dory-3072 model (4 + 40 x 2 + 4 sublayers, NVFP4 weights with
+g_proj and a tied NVFP4 head, int8 KV, 8K tier with 8184 positions prefilled): 3.35 GB streamed per step, far
+larger than the 126 MB L2, so no flush is needed between steps. Every rank runs its own independent sequence
+(weak scaling, no collective on the data path). `value` is rows verified per second over all ranks with the inputs
+resident (CUDA events on the session's stream, max over ranks); `e2e` is the same through the C ABI forward()
+with host token buffers and every row's logits copied back (wall clock around the call).
+
+--impl reference times XTier Go's own CPU kernels (oracle/_ref/libxtgref.so, compiled from the reference sources)
+on the same config: a bounded sample per step (one global attention, one sliding attention and one MLP sublayer in
+DorySession::sublayer order with FP8 KvCaches, plus 1/16 of the head) scaled to the full step's 11 + 33 + 44
+sublayers and the whole head; all host cores.
+"""
+import argparse
+import ctypes as C
+import importlib.util
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+METRIC = "decode tok/s per B200 (NVFP4 Dory-shape, 8K ctx) and % of HBM roofline"
+UNIT = "tok/s"
+TOKENS = [17, 4242, 99, 131071, 5, 70000, 123, 2048]
+PREFILL = 8184
+FALLBACK_HBM = 6650.0
+
+
+def package():
+    pkg = os.path.join(ROOT, "xtier-go_b200")
+    spec = importlib.util.spec_from_file_location("xtier_go_b200", os.path.join(pkg, "__init__.py"),
+                                                  submodule_search_locations=[pkg])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["xtier_go_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM, "fallback"
+
+
+def ncu_traffic():
+    """dram bytes per GEMV launch from the committed ncu summary (profiles/), or None."""
+    p = os.path.join(ROOT, "profiles", "gemv_nvfp4_dory3072.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(float(line.split(":", 1)[1]))
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# the reference's CPU implementation (oracle/_ref), a bounded sample of the step
+# ------------------------------------------------------------------------------------------------------------------
+
+def reference_sample(model, threads, reps, warmup):
+    """Seconds per full step estimated from the reference's kernels; returns (step_s, detail)."""
+    import numpy as np
+    import oracle as O
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    from make_golden import XrShape, XrSublayer  # the ctypes mirrors of ref_shim.cpp's structs
+    R = O.ref()
+    if R is None:
+        raise RuntimeError("oracle/_ref/libxtgref.so is not built")
+    f32p, u8p = O.f32p, O.u8p
+    R.xr_sublayer.argtypes = [C.c_void_p, C.POINTER(XrShape), C.POINTER(XrSublayer), f32p, C.c_int, C.c_int64,
+                              C.c_int, f32p]
+    R.xr_head.argtypes = [C.c_void_p, u8p, u8p, C.c_float, C.c_int, C.c_int, f32p, C.c_int, f32p, f32p]
+    H, F, heads, kvh, d = model["hidden"], model["ffn"], model["heads"], model["kv_heads"], model["head_dim"]
+    Q, KV = heads * d, kvh * d
+    seed = model["seed"]
+    keep = []
+
+    def w(stream, n, k):
+        _, codes, scales, g = O.synth_weight(seed, stream, n, k, model["weight_std"])
+        keep.extend([codes, scales])
+        return codes, scales, g
+
+    def vec(stream, lo, hi, n):
+        v = O.gen_uniform(seed, stream, lo, hi, n)
+        keep.append(v)
+        return v
+
+    pool = R.xr_pool_new(threads)
+    shape = XrShape(H, F, heads, kvh, d)
+
+    def attn_sub(kind, base):
+        s = XrSublayer()
+        s.kind = kind
+        for j, (n, k) in enumerate([(Q, H), (KV, H), (KV, H), (Q, H), (H, Q)]):
+            c, sc, g = w(base + j, n, k)
+            s.codes[j] = O.ptr(c, u8p)
+            s.scales[j] = O.ptr(sc, u8p)
+            s.globals[j] = g
+        s.lr = O.ptr(vec(base + 8, model["lr_lo"], model["lr_hi"], H), f32p)
+        s.qscale = O.ptr(vec(base + 9, model["qs_lo"], model["qs_hi"], Q), f32p)
+        s.gscale = O.ptr(vec(base + 10, model["gs_lo"], model["gs_hi"], Q), f32p)
+        s.theta = model["theta_global"] if kind == 2 else model["theta_sliding"]
+        s.window = model["window"] if kind == 1 else 0
+        # an FP8 KvCache (the reference has no int8 one) with the prefill stored; a sliding layer's ring is the
+        # reference's own window + 16 slots
+        cache = R.xr_kv_new(kvh, d, 8192, model["window"] + 16 if kind == 1 else 0, 1)
+        first = 0 if kind == 2 else PREFILL - (model["window"] + 16)
+        for p in range(first, PREFILL, 512):
+            n = min(512, PREFILL - p)
+            kk = O.gen_uniform(seed, base + 14, -0.1, 0.1, n * kvh * d)
+            vv = O.gen_uniform(seed, base + 15, -0.1, 0.1, n * kvh * d)
+            assert R.xr_kv_store(cache, p, n, O.ptr(kk, f32p), O.ptr(vv, f32p)) == 0
+        s.cache = cache
+        return s
+
+    def mlp_sub(base):
+        s = XrSublayer()
+        s.kind = 0
+        for j, (n, k) in enumerate([(F, H), (F, H), (H, F)]):
+            c, sc, g = w(base + j, n, k)
+            s.codes[j] = O.ptr(c, u8p)
+            s.scales[j] = O.ptr(sc, u8p)
+            s.globals[j] = g
+        s.lr = O.ptr(vec(base + 8, model["lr_lo"], model["lr_hi"], H), f32p)
+        s.sg = O.ptr(vec(base + 11, model["suv_lo"], model["suv_hi"], F), f32p)
+        s.su = O.ptr(vec(base + 12, model["suv_lo"], model["suv_hi"], F), f32p)
+        return s
+
+    subs = {"global": attn_sub(2, 1000 + 16 * 6), "sliding": attn_sub(1, 1000), "mlp": mlp_sub(1000 + 16)}
+    head_rows = model["vocab"] // 16
+    hc, hs, hg = w(1, head_rows, H)
+    ls = vec(2, model["ls_lo"], model["ls_hi"], head_rows)
+    x0 = O.gen_uniform(seed, 9, -0.03, 0.03, 8 * H).reshape(8, H)
+    work = np.zeros(8 * (4 * H + 3 * Q + 2 * F) + 64, np.float32)
+    logits = np.zeros((8, head_rows), np.float32)
+    times = {k: [] for k in ("global", "sliding", "mlp", "head")}
+    for rep in range(warmup + reps):
+        for name, s in subs.items():
+            x = np.ascontiguousarray(x0)
+            t0 = time.perf_counter()
+            assert R.xr_sublayer(pool, C.byref(shape), C.byref(s), O.ptr(x, f32p), 8, PREFILL, 1,
+                                 O.ptr(work, f32p)) == 0, R.xr_last_error()
+            if rep >= warmup:
+                times[name].append(time.perf_counter() - t0)
+        x = np.ascontiguousarray(x0)
+        t0 = time.perf_counter()
+        assert R.xr_head(pool, O.ptr(hc, u8p), O.ptr(hs, u8p), hg, head_rows, H, O.ptr(x, f32p), 8, O.ptr(ls, f32p),
+                         O.ptr(logits, f32p)) == 0
+        if rep >= warmup:
+            times["head"].append(time.perf_counter() - t0)
+    for s in subs.values():
+        if s.kind:
+            R.xr_kv_free(s.cache)
+    R.xr_pool_free(pool)
+    ev = [e for e in range(model["n_in"] + model["n_rec"] * model["loops"] + model["n_out"])]
+    kinds = O.kinds(model)
+    n_g, n_s, n_m = kinds.count(2), kinds.count(1), kinds.count(0)
+    del ev
+    med = {k: statistics.median(v) for k, v in times.items()}
+    step = n_g * med["global"] + n_s * med["sliding"] + n_m * med["mlp"] + 16 * med["head"]
+    detail = {k: round(v * 1e3, 3) for k, v in med.items()}
+    return step, detail, (n_g, n_s, n_m)
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    x = package()
+    model = dict(x.DORY_3072)
+    threads = os.cpu_count() or 1
+    step_s, detail, counts = reference_sample(model, threads, max(1, args.steps), max(0, args.warmup))
+    value = 8.0 / step_s
+    sample = (f"per step: 1 global + 1 sliding attention + 1 MLP sublayer (8 rows, 8184 cached, FP8 KvCache: "
+              f"the reference has no int8 cache) and 1/16 of the NVFP4 head, scaled by {counts[0]} / {counts[1]} / "
+              f"{counts[2]} sublayers and 16; medians ms {detail}")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations, NVFP4 weights", "data": "synthetic",
+            "config": config_block(args.gpus),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_block(n):
+    return {"workload": "config3: synthetic Dory-3072 NVFP4 8-row verify step, 8K tier, 8184 positions prefilled, "
+                        "batch 1 per GPU",
+            "model": "Dory-3072 synthetic (hidden 3072, 24q/6kv x 128, ffn 9216, vocab 131072, 4+40x2+4, g_proj, "
+                     "tied NVFP4 head)",
+            "global_batch": n, "seq_len": 8192, "rows_per_step": 8, "kv_dtype": "int8",
+            "l2": "inputs larger than L2 (3.35 GB streamed per step)",
+            "parallelism": f"replicas x{n} (independent sequences, no collective)"}
+
+
+# ------------------------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------------------------
+
+def run_ours(args, rank, world, local_rank, dist):
+    import torch
+    x = package()
+    torch.cuda.set_device(local_rank)
+    model = dict(x.DORY_3072)
+    s = x.Session(model, context=8192, device=local_rank)
+    s.prefill_synthetic(PREFILL)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up (graph capture included), then the timed device region
+    s.bench(TOKENS, max(1, args.warmup))
+    barrier()
+    with Clocks(local_rank) as clk:
+        ms, _, _ = s.bench(TOKENS, args.steps)
+    barrier()
+    ms = max_over_ranks(ms)
+    value = world * 8.0 / (ms / 1e3)
+    # end to end through the C ABI: host token buffer in, every row's logits out, the rewind a verify step does
+    for _ in range(2):
+        s.forward(TOKENS, want=2)
+        s.rewind(PREFILL)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        s.forward(TOKENS, want=2)
+        s.rewind(PREFILL)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    barrier()
+    e2e_s = max_over_ranks(e2e_s)
+    # per-kernel-class device time (eager launches with events), for the roofline of the dominant kernel
+    pms, cms, cl = s.bench(TOKENS, 3, profile=True)
+    gemv_bytes = s.step_bytes(1, 8)
+    step_bytes = s.step_bytes(0, 8)
+    peak, peak_kind = peaks()
+    gemv_launches = max(1, cl[0])
+    achieved = gemv_bytes / (cms[0] / 1e3) / 1e9
+    traffic = ncu_traffic()
+    info = s.info()
+    s.close()
+    if rank != 0:
+        return
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "nvfp4 weights x fp16 activations, f32 accumulate; int8 KV",
+            "data": "synthetic (seeded random-init weights, random prefilled KV)", "config": config_block(world),
+            "e2e": {"value": world * 8.0 / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 48,
+                    "d2h_bytes_per_step": 8 * model["vocab"] * 4, "ms_per_step": e2e_s * 1e3},
+            "roofline": {"bound": "hbm", "kernel": "gemv_nvfp4 (all NVFP4 GEMVs of the step)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": peak_kind, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": gemv_bytes / gemv_launches,
+                         "launch_ms": cms[0] / gemv_launches},
+            "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
+                              "frac": step_bytes / (ms / 1e3) / 1e9 / peak, "peak": peak},
+            "kernel_ms_per_step": {"gemv": cms[0], "attention": cms[1], "combine": cms[2], "small": cms[3],
+                                   "eager_total": pms},
+            "gpu_launches": int(sum(cl)) * args.steps,
+            "clocks": clk.summary(),
+            "library": {"splits_global": info.get("splits_global"), "splits_ring": info.get("splits_ring"),
+                        "graph": info.get("graph"), "pdl": info.get("pdl")}}
+    if world == 1 and not args.no_cpu_baseline:
+        try:
+            step_s, detail, counts = reference_sample(model, os.cpu_count() or 1, 1, 0)
+            line["cpu_baseline"] = {"value": 8.0 / step_s, "unit": UNIT, "cores": os.cpu_count() or 1,
+                                    "kind": "reference",
+                                    "sample": f"1 global + 1 sliding + 1 MLP sublayer + 1/16 head, scaled to the "
+                                              f"step; medians ms {detail}"}
+        except Exception as e:  # the baseline is reported, never the target
+            line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "reference",
+                                    "sample": f"unavailable: {e}"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist = tdist
+    try:
+        run_ours(args, rank, world, local_rank, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

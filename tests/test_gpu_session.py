@@ -20,6 +20,22 @@ def logits_of(out, n):
     return np.stack([out[i] for i in range(n)])
 
 
+@pytest.mark.parametrize("layers", [dict(n_in=1, n_rec=0, n_out=0, loops=0), dict(n_in=2, n_rec=0, n_out=0, loops=0),
+                                    dict(n_in=2, n_rec=2, n_out=0, loops=1), dict(n_in=0, n_rec=4, n_out=2, loops=2)])
+def test_partial_models_match_oracle(cuda, xtg, cfg, layers):
+    """One attention sublayer; attention + MLP; a loop; loops without input layers: each against the oracle."""
+    c = dict(cfg, **layers)
+    toks = [5, 17, 900, 3, 44, 1023, 0, 256]
+    ref = O.SynthDory(c, ctx=256, n_prefill=70)
+    with xtg.Session(c, context=256) as s:
+        s.prefill_synthetic(70)
+        got = logits_of(s.forward(toks, want=2), 8)
+    want = ref.step(toks)
+    ref.close()
+    assert np.array_equal(got.argmax(1), want.argmax(1))
+    assert np.abs(got - want).max() <= LOGIT_TOL, np.abs(got - want).max()
+
+
 def test_steps_match_oracle(cuda, xtg, cfg):
     steps = [[5, 17, 900, 3, 44, 1023, 0, 256], [8, 9, 10, 11, 12, 13, 14, 15], [600, 601, 2], [4095]]
     ref = O.SynthDory(cfg, ctx=512, n_prefill=100)

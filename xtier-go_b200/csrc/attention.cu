@@ -86,7 +86,8 @@ __device__ __forceinline__ void codes_to_f16(uint32_t word, int dtype, uint32_t&
 }
 
 struct Smem {
-  float q[kQRows][kD + 4];        // prepared queries (query row = 4 * activation row + head in group)
+  uint4 qf[2][2][8][32];          // Q A fragments [m-tile][hi, lo][k16 step][lane]: q = hi + lo, both fp16
+  float q[kQRows][kD + 4];        // prepared queries (query row = group * activation row + head in group)
   float k[kMaxRows][kD + 4];      // this call's keys / values (prepared)
   float v[kMaxRows][kD + 4];
   float mrg_m[2][16];             // half-1 warps' softmax state for the merge
@@ -170,18 +171,25 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
 
   const int mt = warp & 1, half = warp >> 1;
   const bool active = (16 * mt) / group < m;   // this warp's query rows hold at least one activation row
-  // A fragments of Q: step s, lane tq reads head dims 32 tq + 4 s + {0, 1} (a0, a1) and + {2, 3} (a2, a3)
-  uint32_t qa[8][4];
+  // A fragments of Q, split q = hi + lo (both fp16) so that the scores keep ~22 bits: step st, lane tq reads head
+  // dims 32 tq + 4 st + {0, 1} (a0, a1) and + {2, 3} (a2, a3)
+  for (int idx = threadIdx.x; idx < 2 * 8 * 32; idx += kThreads) {
+    const int l = idx & 31, st = (idx >> 5) & 7, t2 = idx >> 8;
+    const int gg = l >> 2, tt = l & 3, d0 = 32 * tt + 4 * st;
+    const float* r0 = sm.q[16 * t2 + gg];
+    const float* r1 = sm.q[16 * t2 + gg + 8];
+    const float v[8] = {r0[d0], r0[d0 + 1], r1[d0], r1[d0 + 1], r0[d0 + 2], r0[d0 + 3], r1[d0 + 2], r1[d0 + 3]};
+    uint32_t hi[4], lo[4];
 #pragma unroll
-  for (int s = 0; s < 8; ++s) {
-    const int d0 = 32 * tq + 4 * s;
-    const float* r0 = sm.q[16 * mt + g];
-    const float* r1 = sm.q[16 * mt + g + 8];
-    qa[s][0] = pack_f16x2(r0[d0], r0[d0 + 1]);
-    qa[s][1] = pack_f16x2(r1[d0], r1[d0 + 1]);
-    qa[s][2] = pack_f16x2(r0[d0 + 2], r0[d0 + 3]);
-    qa[s][3] = pack_f16x2(r1[d0 + 2], r1[d0 + 3]);
+    for (int j = 0; j < 4; ++j) {
+      const __half h0 = __float2half_rn(v[2 * j]), h1 = __float2half_rn(v[2 * j + 1]);
+      hi[j] = pack_f16x2(__half2float(h0), __half2float(h1));
+      lo[j] = pack_f16x2(v[2 * j] - __half2float(h0), v[2 * j + 1] - __half2float(h1));
+    }
+    sm.qf[t2][0][st][l] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    sm.qf[t2][1][st][l] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
+  __syncthreads();
   // the activation rows of this lane's two query rows and their positions
   const int arow0 = (16 * mt + g) / group, arow1 = (16 * mt + g + 8) / group;
   const int t0 = pos0 + arow0, t1 = pos0 + arow1;
@@ -196,31 +204,36 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
   auto chunk = [&](int64_t c0, bool own) {
     // ---- S = Q K^T: 8 n8-tiles, tile T = 2 j + ab holds slots c0 + 16 (n >> 1) + 4 j + (n & 1) + 2 ab ----
     float s[8][4];
+    uint32_t kw[8][8];   // the K row this lane supplies to each tile: 32 bytes (head dims 32 tq ..)
 #pragma unroll
     for (int T = 0; T < 8; ++T) {
-      const int j = T >> 1, ab = T & 1;
-      const int key = 16 * (g >> 1) + 4 * j + (g & 1) + 2 * ab;   // the key this lane supplies (n = g)
-      uint32_t kw[8];
+      const int key = 16 * (g >> 1) + 4 * (T >> 1) + (g & 1) + 2 * (T & 1);
+      s[T][0] = s[T][1] = s[T][2] = s[T][3] = 0.f;
       if (!own) {
         const uint4* kr = reinterpret_cast<const uint4*>(kc + (c0 + key) * kD + 32 * tq);
         const uint4 k0 = __ldg(kr), k1 = __ldg(kr + 1);
-        kw[0] = k0.x; kw[1] = k0.y; kw[2] = k0.z; kw[3] = k0.w;
-        kw[4] = k1.x; kw[5] = k1.y; kw[6] = k1.z; kw[7] = k1.w;
+        kw[T][0] = k0.x; kw[T][1] = k0.y; kw[T][2] = k0.z; kw[T][3] = k0.w;
+        kw[T][4] = k1.x; kw[T][5] = k1.y; kw[T][6] = k1.z; kw[T][7] = k1.w;
       }
-      s[T][0] = s[T][1] = s[T][2] = s[T][3] = 0.f;
+    }
 #pragma unroll
-      for (int st = 0; st < 8; ++st) {
+    for (int st = 0; st < 8; ++st) {
+      const uint4 qh = sm.qf[mt][0][st][lane], ql = sm.qf[mt][1][st][lane];
+#pragma unroll
+      for (int T = 0; T < 8; ++T) {
         uint32_t b0, b1;
         if (own) {
+          const int key = 16 * (g >> 1) + 4 * (T >> 1) + (g & 1) + 2 * (T & 1);
           const int d0 = 32 * tq + 4 * st;
           const bool ok = key < m;
           const float* kr = sm.k[key < kMaxRows ? key : 0];
           b0 = ok ? pack_f16x2(kr[d0], kr[d0 + 1]) : 0u;
           b1 = ok ? pack_f16x2(kr[d0 + 2], kr[d0 + 3]) : 0u;
         } else {
-          codes_to_f16(kw[st], a.dtype, b0, b1);
+          codes_to_f16(kw[T][st], a.dtype, b0, b1);
         }
-        mma_f16(s[T], qa[st][0], qa[st][1], qa[st][2], qa[st][3], b0, b1);
+        mma_f16(s[T], qh.x, qh.y, qh.z, qh.w, b0, b1);
+        mma_f16(s[T], ql.x, ql.y, ql.z, ql.w, b0, b1);
       }
     }
     // ---- scale, mask, online softmax: this lane's keys are slots c0 + 16 tq + kk, kk = 4 j + 2 ab + {0, 1} ----

@@ -151,7 +151,9 @@ __device__ __noinline__ void finish_part(const GemvArgs& a, int t, const float (
   const int64_t wa = owner_of(tile_begin, units, total_warps), wb = owner_of(tile_end - 1, units, total_warps);
   float sum[4] = {0.f, 0.f, 0.f, 0.f};
   for (int64_t w = wa; w <= wb; ++w) {
-    const int64_t w_first_tile = (w * units / total_warps) / a.blocks;
+    const int64_t wu0 = w * units / total_warps, wu1 = (w + 1) * units / total_warps;
+    if (wu1 <= wu0) continue;   // a warp without blocks parked nothing
+    const int64_t w_first_tile = wu0 / a.blocks;
     const int s2 = (t == w_first_tile) ? 0 : 1;
     const float4 p = __ldcg(reinterpret_cast<const float4*>(a.partial) + (w * 2 + s2) * 32 + lane);
     sum[0] += p.x;
@@ -269,9 +271,13 @@ int gemv_grid(int num_sms) { return num_sms * 2; }
 
 int64_t gemv_partial_floats(int grid) { return (int64_t)grid * kWarps * 2 * 32 * 4; }
 
-void launch_gemv(int epi, const GemvArgs& a_in, int grid, cudaStream_t s, bool pdl) {
+void launch_gemv(int epi, const GemvArgs& a_in, int max_grid, cudaStream_t s, bool pdl) {
   GemvArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
+  // at least 8 blocks per warp where the weight is small; never more CTAs than the scratch was sized for
+  const int64_t units = (int64_t)a.tiles * a.blocks;
+  const int64_t want = (units + kWarps * 8 - 1) / (kWarps * 8);
+  const int grid = (int)(want < max_grid ? (want > 0 ? want : 1) : max_grid);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kWarps * 32);

@@ -71,7 +71,7 @@ struct GemvArgs {
 
 int gemv_grid(int num_sms);
 int64_t gemv_partial_floats(int grid);
-void launch_gemv(int epi, const GemvArgs& a, int grid, cudaStream_t s, bool pdl);
+void launch_gemv(int epi, const GemvArgs& a, int max_grid, cudaStream_t s, bool pdl);
 
 // x f32 [m][k] -> fp16 fragments (rows >= m zero); k padded to the blocks of 64.
 void pack_activations(const float* x, int m, int k, uint32_t* x16, cudaStream_t s);
