@@ -226,7 +226,7 @@ def test_attention_reference_cases(cuda, xtg, torch_mod, dtype, case):
     V = O.gen_uniform(31, 2, -1.0, 1.0, total * kvh * d).reshape(total, kvh, d)
     q = O.gen_uniform(31, 3, -1.0, 1.0, n_q * heads * d).reshape(n_q, heads, d)
     ring = window > 0
-    slots = (window + 64) if ring else max(64, (total + 63) // 64 * 64)
+    slots = (window + 64 + 63) // 64 * 64 if ring else max(64, (total + 63) // 64 * 64)
     ck = np.zeros((slots, kvh, d), np.uint8)
     cv = np.zeros_like(ck)
     ks = np.zeros((slots, kvh), np.float32)
