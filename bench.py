@@ -356,7 +356,21 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-steps", type=int, default=0,
+                    help="profiling driver: run this many eager steps (no graph, no JSON) for ncu, then exit")
+    ap.add_argument("--ncu-model", default="full", choices=["full", "small"],
+                    help="small: the same shapes with 2 + 2 + 2 sublayers (about 0.5 GB on the device)")
     args = ap.parse_args()
+    if args.ncu_steps:
+        x = package()
+        model = dict(x.DORY_3072)
+        if args.ncu_model == "small":
+            model.update(n_in=2, n_rec=2, n_out=2, loops=1)
+        s = x.Session(model, context=8192, graph=False)
+        s.prefill_synthetic(PREFILL)
+        s.bench(TOKENS, args.ncu_steps)
+        s.close()
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
