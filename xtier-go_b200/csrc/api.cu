@@ -119,6 +119,7 @@ int xtg_cuda_linear_forward(xtg_cuda_linear* L, const float* x, int m, float* co
     a.m = m;
     a.partial = L->partial;
     a.counters = L->counters;
+    a.err = nullptr;
     a.outs = L->outs;
     launch_gemv(kEpiStore, a, L->grid, s, false);
     // outs_host is read by the copy above before this call returns to the caller's next forward

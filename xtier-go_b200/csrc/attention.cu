@@ -29,25 +29,6 @@ constexpr int kThreads = 128;
 constexpr int kQRows = 32;
 constexpr int kPartStride = kD + 2;   // m, l, acc[128]
 
-__device__ __forceinline__ void rope_norm_vec(float (&x)[4], const float* cosv, const float* sinv, int lane,
-                                              bool rope) {
-  // x[0] = e, x[1] = e + 64, x[2] = e + 32, x[3] = e + 96 for e = lane
-  if (rope) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int e = lane + 32 * h;
-      const float c = cosv[e], s = sinv[e];
-      const float x1 = x[2 * h], x2 = x[2 * h + 1];
-      x[2 * h] = x1 * c - x2 * s;
-      x[2 * h + 1] = x2 * c + x1 * s;
-    }
-  }
-  const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
-  const float f = 1.f / sqrtf(ss + 1e-6f);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) x[j] *= f;
-}
-
 // Encode one row of 128 (a warp, 4 values per lane at e, e + 64, e + 32, e + 96) into codes and a scale.
 __device__ __forceinline__ void encode_row(const float (&x)[4], int dtype, int lane, uint8_t* row_k,
                                            uint8_t* col_v, int64_t v_stride, float* scale_out) {
@@ -120,54 +101,94 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
   if (ce > cb && threadIdx.x < kD && !a.ring) {
     prefetch_l2(vc + (int64_t)threadIdx.x * slots + cb * 64, (uint32_t)((ce - cb) * 64));
   }
-  if (a.pdl) pdl_wait();
+  if (a.pdl) {
+    pdl_launch_next();
+    pdl_wait();
+  }
 
   // ---- prepare Q and this call's K / V (RoPE + justnorm + q scale in the fused step) ----
-  for (int task = warp; task < kMaxRows * (group + 2); task += kThreads / 32) {
-    const int i = task / (group + 2), which = task % (group + 2);   // which < group: q head; group: k; +1: v
-    float x[4] = {0.f, 0.f, 0.f, 0.f};
-    if (i < m) {
-      const float* src;
-      if (a.proj) {
-        const float* row = a.proj + (int64_t)i * a.proj_ld;
-        src = which < group ? row + (int64_t)(kvh * group + which) * kD
-                            : row + (int64_t)a.heads * kD + (int64_t)(which - group) * a.kv_heads * kD + kvh * kD;
-      } else {
-        src = which < group ? a.q + ((int64_t)i * a.heads + kvh * group + which) * kD
-                            : (which == group ? a.k : a.v) + ((int64_t)i * a.kv_heads + kvh) * kD;
-      }
-      x[0] = src[lane];
-      x[1] = src[lane + 64];
-      x[2] = src[lane + 32];
-      x[3] = src[lane + 96];
-      if (a.proj && which <= group) {   // q and k: RoPE then justnorm per head
-        rope_norm_vec(x, a.rope_cos + i * (kD / 2), a.rope_sin + i * (kD / 2), lane, true);
-        if (which < group) {
-          const float* qs = a.qscale + (int64_t)(kvh * group + which) * kD;
-          x[0] *= qs[lane];
-          x[1] *= qs[lane + 64];
-          x[2] *= qs[lane + 32];
-          x[3] *= qs[lane + 96];
+  // task = (activation row i, vector: q heads of the group, then k, then v); a warp takes tasks warp, warp + 4, ...
+  // in batches whose loads are all issued before any is used (one round trip per batch, not one per task)
+  const int ntask = kMaxRows * (group + 2);
+  constexpr int kBatchT = 6;
+  for (int t0 = warp; t0 < ntask; t0 += 4 * kBatchT) {
+    float xs[kBatchT][4], cs[kBatchT][4], qs4[kBatchT][4];
+#pragma unroll
+    for (int j = 0; j < kBatchT; ++j) {
+      const int task = t0 + 4 * j;
+      const int i = task / (group + 2), which = task % (group + 2);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xs[j][q] = cs[j][q] = qs4[j][q] = 0.f;
+      if (task < ntask && i < m) {
+        const float* src;
+        if (a.proj) {
+          const float* row = a.proj + (int64_t)i * a.proj_ld;
+          src = which < group ? row + (int64_t)(kvh * group + which) * kD
+                              : row + (int64_t)a.heads * kD + (int64_t)(which - group) * a.kv_heads * kD + kvh * kD;
+        } else {
+          src = which < group ? a.q + ((int64_t)i * a.heads + kvh * group + which) * kD
+                              : (which == group ? a.k : a.v) + ((int64_t)i * a.kv_heads + kvh) * kD;
+        }
+        xs[j][0] = src[lane];
+        xs[j][1] = src[lane + 64];
+        xs[j][2] = src[lane + 32];
+        xs[j][3] = src[lane + 96];
+        if (a.proj && which <= group) {
+          cs[j][0] = a.rope_cos[i * (kD / 2) + lane];
+          cs[j][1] = a.rope_sin[i * (kD / 2) + lane];
+          cs[j][2] = a.rope_cos[i * (kD / 2) + lane + 32];
+          cs[j][3] = a.rope_sin[i * (kD / 2) + lane + 32];
+          if (which < group) {
+            const float* qsp = a.qscale + (int64_t)(kvh * group + which) * kD;
+            qs4[j][0] = qsp[lane];
+            qs4[j][1] = qsp[lane + 64];
+            qs4[j][2] = qsp[lane + 32];
+            qs4[j][3] = qsp[lane + 96];
+          }
         }
       }
-      if (a.store && split == 0 && which >= group) {   // this call's rows into the cache
+    }
+#pragma unroll
+    for (int j = 0; j < kBatchT; ++j) {
+      const int task = t0 + 4 * j;
+      if (task >= ntask) break;
+      const int i = task / (group + 2), which = task % (group + 2);
+      float* x = xs[j];
+      if (i < m && a.proj && which <= group) {   // q and k: RoPE, then justnorm per head (q also times q scale)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float c = cs[j][2 * h], sn = cs[j][2 * h + 1];
+          const float x1 = x[2 * h], x2 = x[2 * h + 1];
+          x[2 * h] = x1 * c - x2 * sn;
+          x[2 * h + 1] = x2 * c + x1 * sn;
+        }
+        const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
+        const float f = 1.f / sqrtf(ss + 1e-6f);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) x[q] *= f;
+        if (which < group) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) x[q] *= qs4[j][q];
+        }
+      }
+      if (i < m && a.store && split == 0 && which >= group) {   // this call's rows into the cache
         const int64_t p = pos0 + i, slot = a.ring ? p % slots : p;
+        const float xv[4] = {x[0], x[1], x[2], x[3]};
         if (which == group)
-          encode_row(x, a.dtype, lane, a.kc + ((int64_t)kvh * slots + slot) * kD, nullptr, 0,
+          encode_row(xv, a.dtype, lane, a.kc + ((int64_t)kvh * slots + slot) * kD, nullptr, 0,
                      a.ks + (int64_t)kvh * slots + slot);
         else
-          encode_row(x, a.dtype, lane, nullptr, a.vc + (int64_t)kvh * kD * slots + slot, slots,
+          encode_row(xv, a.dtype, lane, nullptr, a.vc + (int64_t)kvh * kD * slots + slot, slots,
                      a.vs + (int64_t)kvh * slots + slot);
       }
+      float* dst = which < group ? sm.q[i * group + which] : (which == group ? sm.k[i] : sm.v[i]);
+      dst[lane] = x[0];
+      dst[lane + 64] = x[1];
+      dst[lane + 32] = x[2];
+      dst[lane + 96] = x[3];
     }
-    float* dst = which < group ? sm.q[i * group + which] : (which == group ? sm.k[i] : sm.v[i]);
-    dst[lane] = x[0];
-    dst[lane + 64] = x[1];
-    dst[lane + 32] = x[2];
-    dst[lane + 96] = x[3];
   }
   __syncthreads();
-  if (a.pdl) pdl_launch_next();
 
   const int mt = warp & 1, half = warp >> 1;
   const bool active = (16 * mt) / group < m;   // this warp's query rows hold at least one activation row
@@ -425,27 +446,52 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
 }
 
 // Combine the splits of (activation row, q head) by log-sum-exp; then either the plain output (API) or the Dory
-// output gate, fp16 fragments for the O projection and the per-head sum of squares (the step).
+// output gate, fp16 fragments for the O projection and the per-head sum of squares (the step). One CTA per (row,
+// head), one thread per head dimension; the split weights are computed once, every partial is loaded in one wave.
+constexpr int kMaxSplits = 256;
+
 __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   __shared__ float red[32];
+  __shared__ float wgt[kMaxSplits];
+  __shared__ float inv_l;
   const int i = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-  if (a.pdl) pdl_wait();
-  if (a.pdl) pdl_launch_next();
+  if (a.pdl) {
+    pdl_launch_next();
+    pdl_wait();
+  }
   const int m = a.params ? a.params->m : a.m;
   if (i >= m) return;
   const int group = a.heads / a.kv_heads, kvh = h / group, qr = i * group + h % group;
-  float M = -INFINITY;
-  for (int s = 0; s < a.splits; ++s)
-    M = fmaxf(M, a.part[(((int64_t)kvh * a.splits + s) * kQRows + qr) * kPartStride]);
-  float L = 0.f, o = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
-    const float* p = a.part + (((int64_t)kvh * a.splits + s) * kQRows + qr) * kPartStride;
-    if (p[0] == -INFINITY) continue;
-    const float w = expf(p[0] - M);
-    L += p[1] * w;
-    o += p[2 + d] * w;
+  const float* base = a.part + ((int64_t)kvh * a.splits * kQRows + qr) * kPartStride;
+  const int64_t sstride = (int64_t)kQRows * kPartStride;
+  // split weights exp(m_s - M) and 1 / sum_s l_s exp(m_s - M), by the first warp in a fixed order
+  if (threadIdx.x < 32) {
+    float mx = -INFINITY;
+    for (int s = threadIdx.x; s < a.splits; s += 32) mx = fmaxf(mx, base[s * sstride]);
+    mx = warp_max(mx);
+    float l = 0.f;
+    for (int s = threadIdx.x; s < a.splits; s += 32) {
+      const float ms = base[s * sstride];
+      const float w = ms == -INFINITY ? 0.f : expf(ms - mx);
+      wgt[s] = w;
+      l += w == 0.f ? 0.f : base[s * sstride + 1] * w;
+    }
+    l = warp_sum(l);
+    if (threadIdx.x == 0) inv_l = l > 0.f ? 1.f / l : 0.f;
   }
-  o = L > 0.f ? o / L : 0.f;
+  __syncthreads();
+  float o = 0.f;
+  int s = 0;
+  for (; s + 8 <= a.splits; s += 8) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = wgt[s + j] != 0.f ? base[(s + j) * sstride + 2 + d] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o += v[j] * wgt[s + j];
+  }
+  for (; s < a.splits; ++s)
+    if (wgt[s] != 0.f) o += base[s * sstride + 2 + d] * wgt[s];
+  o *= inv_l;
   if (a.out) {
     a.out[((int64_t)i * a.heads + h) * kD + d] = o;
     return;
@@ -469,6 +515,7 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
   a.pdl = pdl ? 1 : 0;
   XTG_REQUIRE(a.heads % a.kv_heads == 0 && a.heads / a.kv_heads <= 4, "attention: at most 4 q heads per KV head");
   XTG_REQUIRE(a.slots % 64 == 0, "attention: cache slots must be a multiple of 64");
+  XTG_REQUIRE(a.splits >= 1 && a.splits <= kMaxSplits, "attention: 1..256 splits");
   static bool attr_set = false;
   if (!attr_set) {
     XTG_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

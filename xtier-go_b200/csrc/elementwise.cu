@@ -25,8 +25,10 @@ __device__ __forceinline__ float packed_weight(const uint8_t* w, int blocks, flo
 
 __global__ void embed_kernel(const EmbedArgs a) {
   const int r = blockIdx.x;
-  if (a.pdl) pdl_wait();
-  if (a.pdl) pdl_launch_next();
+  if (a.pdl) {
+    pdl_launch_next();
+    pdl_wait();
+  }
   const StepParams* p = a.params;
   const int m = p->m;
   const int64_t pos0 = p->pos0;
@@ -60,88 +62,118 @@ __global__ void embed_kernel(const EmbedArgs a) {
   }
 }
 
-// One CTA per activation row: the residual updates. All norms are justnorm: x / sqrt(sum x^2 + 1e-6).
-__global__ void resid_kernel(const ResidArgs a) {
-  __shared__ float red[32];
+// Block-wide sums of two values at once (fixed order, deterministic).
+__device__ __forceinline__ float2 block_sum2(float x, float y, float2* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  x = warp_sum(x);
+  y = warp_sum(y);
+  __syncthreads();
+  if (lane == 0) red[warp] = make_float2(x, y);
+  __syncthreads();
+  float2 t = lane < nw ? red[lane] : make_float2(0.f, 0.f);
+  t.x = warp_sum(t.x);
+  t.y = warp_sum(t.y);
+  return t;
+}
+
+// One CTA per activation row: the residual updates. All norms are justnorm: x / sqrt(sum x^2 + 1e-6). Each thread
+// holds kPer elements (k = thread + j * blockDim) in registers.
+constexpr int kResidThreads = 512;
+constexpr int kPer = 16;   // hidden <= 8192
+
+__global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a) {
+  __shared__ float2 red[32];
   const int r = blockIdx.x, H = a.hidden;
-  if (a.pdl) pdl_wait();
-  if (a.pdl) pdl_launch_next();
+  if (a.pdl) {
+    pdl_launch_next();
+    pdl_wait();
+  }
   const int m = a.params ? a.params->m : a.m;
   float* h = a.h + (int64_t)r * H;
+  uint16_t* x16h = reinterpret_cast<uint16_t*>(a.x16);
   if (r >= m) {
-    for (int k2 = threadIdx.x * 2; k2 < H; k2 += blockDim.x * 2) a.x16[frag_offset_halves(k2, r) >> 1] = 0u;
+    for (int k = threadIdx.x; k < H; k += blockDim.x) x16h[frag_offset_halves(k, r)] = 0;
     return;
   }
-  constexpr int kPer = 8;   // H <= kPer * blockDim
   float v[kPer];
-  const int n = (H + blockDim.x - 1) / blockDim.x;
   if (a.mode == kResidSlerp) {
     const float* o = a.o + (int64_t)r * H;
+    float hv[kPer], ov[kPer];
     float sa = 0.f, sb = 0.f;
-    for (int j = 0; j < n; ++j) {
-      const int k = threadIdx.x + j * blockDim.x;
-      if (k < H) {
-        sa += h[k] * h[k];
-        sb += o[k] * o[k];
-      }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int k = threadIdx.x + j * kResidThreads;
+      hv[j] = k < H ? h[k] : 0.f;
+      ov[j] = k < H ? o[k] : 0.f;
     }
-    const float fa = 1.f / sqrtf(block_sum(sa, red) + 1e-6f);
-    const float fb = 1.f / sqrtf(block_sum(sb, red) + 1e-6f);
-    float s = 0.f;
-    for (int j = 0; j < n; ++j) {
-      const int k = threadIdx.x + j * blockDim.x;
-      v[j] = 0.f;
-      if (k < H) {
-        const float ya = h[k] * fa, yb = o[k] * fb;
-        v[j] = ya + a.lr[k] * (yb - ya);
-        s += v[j] * v[j];
-      }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      sa += hv[j] * hv[j];
+      sb += ov[j] * ov[j];
     }
-    const float f = 1.f / sqrtf(block_sum(s, red) + 1e-6f);
-    for (int j = 0; j < n; ++j) v[j] *= f;
+    const float2 n2 = block_sum2(sa, sb, red);
+    const float fa = 1.f / sqrtf(n2.x + 1e-6f), fb = 1.f / sqrtf(n2.y + 1e-6f);
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int k = threadIdx.x + j * kResidThreads;
+      const float ya = hv[j] * fa, yb = ov[j] * fb;
+      v[j] = k < H ? ya + a.lr[k] * (yb - ya) : 0.f;
+      ss += v[j] * v[j];
+    }
+    const float f = 1.f / sqrtf(block_sum2(ss, 0.f, red).x + 1e-6f);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) v[j] *= f;
   } else {
     float* st = a.state + (int64_t)r * H;
     float* in = a.input + (int64_t)r * H;
+    float hv[kPer], iv[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int k = threadIdx.x + j * kResidThreads;
+      hv[j] = k < H ? h[k] : 0.f;
+      iv[j] = (k < H && a.mode != kResidLoopBegin) ? in[k] : 0.f;
+    }
     if (a.mode == kResidLoopBegin) {   // input = state = h
-      for (int j = 0; j < n; ++j) {
-        const int k = threadIdx.x + j * blockDim.x;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int k = threadIdx.x + j * kResidThreads;
         if (k < H) {
-          st[k] = h[k];
-          in[k] = h[k];
+          st[k] = hv[j];
+          in[k] = hv[j];
         }
+        iv[j] = hv[j];
       }
     } else {   // the loop that ends: state = justnorm(h)
       float s = 0.f;
-      for (int j = 0; j < n; ++j) {
-        const int k = threadIdx.x + j * blockDim.x;
-        if (k < H) s += h[k] * h[k];
-      }
-      const float f = 1.f / sqrtf(block_sum(s, red) + 1e-6f);
-      for (int j = 0; j < n; ++j) {
-        const int k = threadIdx.x + j * blockDim.x;
-        if (k < H) st[k] = h[k] * f;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) s += hv[j] * hv[j];
+      const float f = 1.f / sqrtf(block_sum2(s, 0.f, red).x + 1e-6f);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int k = threadIdx.x + j * kResidThreads;
+        hv[j] *= f;
+        if (k < H) st[k] = hv[j];
       }
     }
     if (a.mode == kResidLoopEnd) {   // h = state
-      for (int j = 0; j < n; ++j) {
-        const int k = threadIdx.x + j * blockDim.x;
-        v[j] = k < H ? st[k] : 0.f;
-      }
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) v[j] = hv[j];
     } else {   // a loop begins: h = justnorm(state + input)
       float s = 0.f;
-      for (int j = 0; j < n; ++j) {
-        const int k = threadIdx.x + j * blockDim.x;
-        v[j] = k < H ? st[k] + in[k] : 0.f;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        v[j] = hv[j] + iv[j];
         s += v[j] * v[j];
       }
-      const float f = 1.f / sqrtf(block_sum(s, red) + 1e-6f);
-      for (int j = 0; j < n; ++j) v[j] *= f;
+      const float f = 1.f / sqrtf(block_sum2(s, 0.f, red).x + 1e-6f);
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) v[j] *= f;
     }
   }
-  // write h and its fp16 fragments (pairs of inputs through shared memory would cost a sync; write halves)
-  uint16_t* x16h = reinterpret_cast<uint16_t*>(a.x16);
-  for (int j = 0; j < n; ++j) {
-    const int k = threadIdx.x + j * blockDim.x;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int k = threadIdx.x + j * kResidThreads;
     if (k < H) {
       h[k] = v[j];
       x16h[frag_offset_halves(k, r)] = __half_as_ushort(__float2half_rn(v[j]));
@@ -154,8 +186,10 @@ __global__ void argmax_kernel(const ArgCand* cand, int tiles, const StepParams* 
   __shared__ float bv[32];
   __shared__ int bi[32];
   const int n = blockIdx.x;
-  if (pdl) pdl_wait();
-  if (pdl) pdl_launch_next();
+  if (pdl) {
+    pdl_launch_next();
+    pdl_wait();
+  }
   if (n >= params->m) return;
   float v = -INFINITY;
   int idx = 0x7fffffff;
@@ -283,8 +317,8 @@ void launch_embed(const EmbedArgs& a_in, cudaStream_t s, bool pdl) {
 void launch_resid(const ResidArgs& a_in, cudaStream_t s, bool pdl) {
   ResidArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
-  XTG_REQUIRE(a.hidden <= 8 * 1024, "resid: hidden above 8192");
-  launch_pdl(resid_kernel, dim3(kMaxRows), dim3(1024), a, s, pdl);
+  XTG_REQUIRE(a.hidden <= kPer * kResidThreads, "resid: hidden above 8192");
+  launch_pdl(resid_kernel, dim3(kMaxRows), dim3(kResidThreads), a, s, pdl);
 }
 
 void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out, float* out_val,

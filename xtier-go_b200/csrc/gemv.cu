@@ -11,10 +11,14 @@
 // rounding of the sums differs, and the activations are rounded once to fp16.
 //
 // Work split: the weight is a stream of 576-byte blocks (weights.cu). Every warp of the grid takes an equal
-// contiguous run of blocks (split-K inside a tile when a run starts or ends mid-tile). A tile's parts land in a
-// scratch slot each; the warp whose atomic increment completes the tile sums the parts in warp order (the same
-// order every launch: deterministic) and runs the epilogue. Weight loads of a warp's first batch and an L2
-// prefetch of its whole run are issued before griddepcontrol.wait, so they overlap the previous kernel.
+// contiguous run of blocks (split-K inside a tile when a run starts or ends mid-tile), so the warps of a CTA cover
+// one contiguous run and the grid covers the weight exactly once. Each warp streams its run through its own ring
+// of shared-memory stages with bulk copies (cp.async.bulk global -> shared, completion on an mbarrier; no
+// multicast); the first stages are issued before griddepcontrol.wait, since the weights do not depend on the
+// previous kernel, and the kernel lets its dependent launch at once, so the next kernel's copies start while this
+// one finishes. A tile split between warps of one CTA is summed in shared memory in warp order; a tile split
+// between CTAs goes through a global scratch slot per CTA, and the CTA whose atomic increment completes the tile
+// sums the CTA parts in CTA order. Every sum has a fixed order, so results are the same every launch.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -23,15 +27,60 @@ namespace xtg {
 namespace {
 
 constexpr int kWarps = 8;
-constexpr int kBatch = 4;   // blocks in flight per warp
+constexpr int kStageBlocks = 4;                           // blocks per bulk copy
+constexpr int kStages = 3;                                // copies in flight per warp
+constexpr int kStageBytes = kStageBlocks * kBlockBytes;   // 2304
+constexpr uint32_t kMaxSpins = 1u << 24;                  // bound on every mbarrier wait
+
+struct GemvSmem {
+  unsigned char ring[kWarps][kStages][kStageBytes];
+  uint64_t bar[kWarps][kStages];
+  float4 part[kWarps][2][32];   // split-tile parts of each warp: [0] its first tile, [1] its last
+  float rowscale[kMaxRows];
+  float red[32][kMaxRows];
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// global -> shared bulk copy completing on `bar` (16-byte aligned addresses, a multiple of 16 bytes)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 __device__ __forceinline__ int64_t owner_of(int64_t u, int64_t units, int64_t total_warps) {
   return ((u + 1) * total_warps - 1) / units;
 }
-
-struct Frag {
-  float c[4];
-};
 
 template <int EPI>
 __device__ __forceinline__ void epilogue(const GemvArgs& a, int t, const float (&acc)[4], int m, const float* rowscale,
@@ -111,9 +160,14 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int t, const float (
   }
 }
 
-// One block: 4 k16 steps, each an MMA of 16 rows x 16 inputs x 8 activation rows.
-__device__ __forceinline__ void block_mma(float (&acc)[4], const uint4 w, const uint2 s, const uint2* xb) {
+// One block: 4 k16 steps, each an MMA of 16 rows x 16 inputs x 8 activation rows; even steps accumulate into acc,
+// odd steps into acc2 (two independent MMA chains).
+__device__ __forceinline__ void block_mma2(float (&acc)[4], float (&acc2)[4], const uint4 w, const uint2 s,
+                                           const uint2* xb) {
   const uint32_t wr[4] = {w.x, w.y, w.z, w.w};
+  uint2 b[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) b[j] = xb[j * 32];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t sc = e4m3x2_to_f16x2(j < 2 ? (s.x >> (16 * j)) : (s.y >> (16 * (j - 2))));
@@ -123,132 +177,180 @@ __device__ __forceinline__ void block_mma(float (&acc)[4], const uint4 w, const 
     const uint32_t a1 = hmul2_u32(e2m1x2_to_f16x2((q >> 8) & 0xff), s_hi);
     const uint32_t a2 = hmul2_u32(e2m1x2_to_f16x2((q >> 16) & 0xff), s_lo);
     const uint32_t a3 = hmul2_u32(e2m1x2_to_f16x2(q >> 24), s_hi);
-    const uint2 b = xb[j * 32];
-    mma_f16(acc, a0, a1, a2, a3, b.x, b.y);
+    if (j & 1)
+      mma_f16(acc2, a0, a1, a2, a3, b[j].x, b[j].y);
+    else
+      mma_f16(acc, a0, a1, a2, a3, b[j].x, b[j].y);
   }
 }
 
-
-// The end of a warp's part of tile t (nb blocks): the epilogue when the part is the whole tile, else park it and,
-// if this part completes the tile, sum all parts in warp order and run the epilogue.
-template <int EPI>
-__device__ __noinline__ void finish_part(const GemvArgs& a, int t, const float (&acc)[4], int nb, int64_t u0,
-                                         int64_t gw, int64_t units, int64_t total_warps, int m,
-                                         const float* rowscale, int lane) {
-  if (nb == a.blocks) {
-    epilogue<EPI>(a, t, acc, m, rowscale, lane);
-    return;
+// The parts of tile t held by CTA warps wa..wb (warp indices within the CTA), summed in warp order. A warp's part
+// of t sits in slot 0 when t is the first tile of its run, else in slot 1.
+__device__ __forceinline__ float4 cta_sum(const GemvSmem& sm, int t, int wa, int wb, int64_t cta_warp0,
+                                          int64_t units, int64_t total_warps, int blocks, int lane) {
+  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int v = wa; v <= wb; ++v) {
+    const int64_t g = cta_warp0 + v;
+    const int64_t v0 = g * units / total_warps, v1 = (g + 1) * units / total_warps;
+    if (v1 <= v0) continue;
+    const float4 p = sm.part[v][(t == (int)(v0 / blocks)) ? 0 : 1][lane];
+    s.x += p.x;
+    s.y += p.y;
+    s.z += p.z;
+    s.w += p.w;
   }
-  const int64_t tile_begin = (int64_t)t * a.blocks, tile_end = tile_begin + a.blocks;
-  const int slot = (t == (int)(u0 / a.blocks)) ? 0 : 1;
-  reinterpret_cast<float4*>(a.partial)[(gw * 2 + slot) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-  __threadfence();
-  int old = 0;
-  if (lane == 0) old = atomicAdd(&a.counters[t], nb);
-  old = __shfl_sync(0xffffffffu, old, 0);
-  if (old + nb != a.blocks) return;
-  __threadfence();
-  const int64_t wa = owner_of(tile_begin, units, total_warps), wb = owner_of(tile_end - 1, units, total_warps);
-  float sum[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int64_t w = wa; w <= wb; ++w) {
-    const int64_t wu0 = w * units / total_warps, wu1 = (w + 1) * units / total_warps;
-    if (wu1 <= wu0) continue;   // a warp without blocks parked nothing
-    const int64_t w_first_tile = wu0 / a.blocks;
-    const int s2 = (t == w_first_tile) ? 0 : 1;
-    const float4 p = __ldcg(reinterpret_cast<const float4*>(a.partial) + (w * 2 + s2) * 32 + lane);
-    sum[0] += p.x;
-    sum[1] += p.y;
-    sum[2] += p.z;
-    sum[3] += p.w;
-  }
-  if (lane == 0) a.counters[t] = 0;
-  epilogue<EPI>(a, t, sum, m, rowscale, lane);
+  return s;
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  GemvSmem& sm = *reinterpret_cast<GemvSmem*>(smem_raw);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t total_warps = (int64_t)gridDim.x * kWarps;
-  const int64_t gw = (int64_t)blockIdx.x * kWarps + warp;
+  const int64_t cta_warp0 = (int64_t)blockIdx.x * kWarps;
+  const int64_t gw = cta_warp0 + warp;
   const int64_t units = (int64_t)a.tiles * a.blocks;
   const int64_t u0 = gw * units / total_warps, u1 = (gw + 1) * units / total_warps;
-  __shared__ float rowscale[kMaxRows];
-  __shared__ float red[32][kMaxRows];
-
-  // issue the first batch of weight loads and an L2 prefetch of the whole run before waiting on the producer
-  if (u1 > u0 && lane == 0) prefetch_l2(a.w + u0 * kBlockBytes, (uint32_t)((u1 - u0) * kBlockBytes));
-  uint4 cw[kBatch];
-  uint2 cs[kBatch];
-  {
+  const int64_t cta_u0 = cta_warp0 * units / total_warps, cta_u1 = (cta_warp0 + kWarps) * units / total_warps;
+  const int n = (int)(u1 - u0);   // this warp's blocks
+  const int nst = (n + kStageBlocks - 1) / kStageBlocks;
+  const uint8_t* src = a.w + u0 * kBlockBytes;
+  uint64_t* bars = sm.bar[warp];
+  auto issue = [&](int st) {   // lane 0: stage st of the run into its ring slot
+    const int slot = st % kStages;
+    const int cnt = n - st * kStageBlocks < kStageBlocks ? n - st * kStageBlocks : kStageBlocks;
+    const uint32_t bytes = (uint32_t)cnt * kBlockBytes;
+    mbar_expect_tx(&bars[slot], bytes);
+    bulk_g2s(sm.ring[warp][slot], src + (int64_t)st * kStageBytes, bytes, &bars[slot]);
+  };
+  // the weights do not depend on the previous kernel: start streaming before waiting on it
+  if (lane == 0 && n > 0) {
 #pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      const int64_t u = u0 + i;
-      if (u < u1) {
-        const uint8_t* blk = a.w + u * kBlockBytes;
-        cw[i] = __ldg(reinterpret_cast<const uint4*>(blk) + lane);
-        cs[i] = __ldg(reinterpret_cast<const uint2*>(blk + 512) + (lane >> 2));
-      }
-    }
+    for (int j = 0; j < kStages; ++j) mbar_init(&bars[j], 1);
+    mbar_init_fence();
+    for (int st = 0; st < kStages && st < nst; ++st) issue(st);
   }
-  if (a.pdl) pdl_wait();
+  __syncwarp();
+  if (a.pdl) {
+    pdl_launch_next();
+    pdl_wait();
+  }
   const int m = a.m_dev ? *a.m_dev : a.m;
   if constexpr (EPI == kEpiStore) {
     if (a.sumsq) {
-      const int n = threadIdx.x & 7, j0 = threadIdx.x >> 3;
-      float s = 0.f;
-      for (int p = j0; p < a.nparts; p += 32) s += a.sumsq[p * kMaxRows + n];
-      red[j0][n] = s;
+      const int r = threadIdx.x & 7, j0 = threadIdx.x >> 3;
+      float acc = 0.f;
+      for (int p = j0; p < a.nparts; p += 32) acc += a.sumsq[p * kMaxRows + r];
+      sm.red[j0][r] = acc;
       __syncthreads();
       if (threadIdx.x < kMaxRows) {
         float t = 0.f;
-        for (int j = 0; j < 32; ++j) t += red[j][threadIdx.x];
-        rowscale[threadIdx.x] = 1.f / sqrtf(t + 1e-6f);
+        for (int j = 0; j < 32; ++j) t += sm.red[j][threadIdx.x];
+        sm.rowscale[threadIdx.x] = 1.f / sqrtf(t + 1e-6f);
       }
     } else if (threadIdx.x < kMaxRows) {
-      rowscale[threadIdx.x] = 1.f;
+      sm.rowscale[threadIdx.x] = 1.f;
     }
     __syncthreads();
   }
-  if (a.pdl) pdl_launch_next();
-
+  const float* rowscale = sm.rowscale;
   const uint2* x16 = reinterpret_cast<const uint2*>(a.x16);
-  if (u1 <= u0) return;
-  int t = (int)(u0 / a.blocks);             // the tile of the current part
-  int64_t tile_begin = (int64_t)t * a.blocks, first = u0;
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int64_t base = u0; base < u1; base += kBatch) {
-    uint4 nw[kBatch];
-    uint2 ns[kBatch];
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {   // the next batch, in flight while this one is multiplied
-      const int64_t v = base + kBatch + i;
-      if (v < u1) {
-        const uint8_t* blk = a.w + v * kBlockBytes;
-        nw[i] = __ldg(reinterpret_cast<const uint4*>(blk) + lane);
-        ns[i] = __ldg(reinterpret_cast<const uint2*>(blk + 512) + (lane >> 2));
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      const int64_t v = base + i;
-      if (v < u1) {
-        if (v == tile_begin + a.blocks) {   // a tile ends inside the batch: finish its part, start the next
-          finish_part<EPI>(a, t, acc, (int)(v - first), u0, gw, units, total_warps, m, rowscale, lane);
-          ++t;
-          tile_begin = v;
-          first = v;
-          acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+  const int first_tile = n > 0 ? (int)(u0 / a.blocks) : -1;
+  if (n > 0) {
+    int t = first_tile;
+    int kb = (int)(u0 - (int64_t)t * a.blocks);   // block index inside tile t
+    int part_kb0 = kb;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t parity = 0;
+    for (int st = 0; st < nst; ++st) {
+      const int slot = st % kStages;
+      uint32_t spins = 0;
+      while (!mbar_try_wait(&bars[slot], (parity >> slot) & 1u)) {
+        if (++spins > kMaxSpins) {   // never expected: report and stop instead of hanging
+          if (lane == 0 && a.err) atomicExch(a.err, 1);
+          break;
         }
-        block_mma(acc, cw[i], cs[i], x16 + (v - tile_begin) * 4 * 32 + lane);
+      }
+      parity ^= 1u << slot;
+      const unsigned char* buf = sm.ring[warp][slot];
+      const int cnt = n - st * kStageBlocks < kStageBlocks ? n - st * kStageBlocks : kStageBlocks;
+#pragma unroll
+      for (int i = 0; i < kStageBlocks; ++i) {
+        if (i < cnt) {
+          const uint4 w = *reinterpret_cast<const uint4*>(buf + i * kBlockBytes + lane * 16);
+          const uint2 sc = *reinterpret_cast<const uint2*>(buf + i * kBlockBytes + 512 + (lane >> 2) * 8);
+          block_mma2(acc, acc2, w, sc, x16 + kb * 128 + lane);
+          if (++kb == a.blocks) {   // the part reaches the end of tile t
+            float f[4] = {acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]};
+            if (part_kb0 == 0)
+              epilogue<EPI>(a, t, f, m, rowscale, lane);
+            else
+              sm.part[warp][t == first_tile ? 0 : 1][lane] = make_float4(f[0], f[1], f[2], f[3]);
+            ++t;
+            kb = 0;
+            part_kb0 = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[q] = acc2[q] = 0.f;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0 && st + kStages < nst) {   // the slot was read: refill it with the run's next stage
+        fence_proxy_async_smem();
+        issue(st + kStages);
       }
     }
-#pragma unroll
-    for (int i = 0; i < kBatch; ++i) {
-      cw[i] = nw[i];
-      cs[i] = ns[i];
-    }
+    if (kb > 0)   // the run ends inside tile t
+      sm.part[warp][t == first_tile ? 0 : 1][lane] =
+          make_float4(acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]);
   }
-  finish_part<EPI>(a, t, acc, (int)(u1 - first), u0, gw, units, total_warps, m, rowscale, lane);
+  __syncthreads();
+  if (n <= 0) return;
+  // ---- split tiles: the last warp of the CTA that covers a tile sums the CTA's parts of it ----
+  const int last_tile = (int)((u1 - 1) / a.blocks);
+  for (int which = 0; which < 2; ++which) {
+    const int t = which == 0 ? first_tile : last_tile;
+    if (which == 1 && last_tile == first_tile) break;
+    const int64_t tb = (int64_t)t * a.blocks, te = tb + a.blocks;
+    const int64_t pb = u0 > tb ? u0 : tb, pe = u1 < te ? u1 : te;   // this warp's part of t
+    if (pb == tb && pe == te) continue;                              // whole tile: done in the loop
+    if (!(pe == te || u1 == cta_u1)) continue;                        // a later warp of the CTA continues t
+    const int64_t owner_first = ((tb + 1) * total_warps - 1) / units;
+    const int wa = (int)((owner_first > cta_warp0 ? owner_first : cta_warp0) - cta_warp0);
+    const float4 s4 = cta_sum(sm, t, wa, warp, cta_warp0, units, total_warps, a.blocks, lane);
+    float f[4] = {s4.x, s4.y, s4.z, s4.w};
+    if (tb >= cta_u0 && te <= cta_u1) {   // every part of t is in this CTA
+      epilogue<EPI>(a, t, f, m, rowscale, lane);
+      continue;
+    }
+    // t continues in another CTA: park this CTA's sum; the CTA completing t sums the CTA parts in CTA order
+    const int cta_first_tile = (int)(cta_u0 / a.blocks);
+    const int cslot = t == cta_first_tile ? 0 : 1;
+    reinterpret_cast<float4*>(a.partial)[((int64_t)blockIdx.x * 2 + cslot) * 32 + lane] = s4;
+    __threadfence();
+    const int covered = (int)((te < cta_u1 ? te : cta_u1) - (tb > cta_u0 ? tb : cta_u0));
+    int old = 0;
+    if (lane == 0) old = atomicAdd(&a.counters[t], covered);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + covered != a.blocks) continue;
+    __threadfence();
+    const int64_t ca = (((tb + 1) * total_warps - 1) / units) / kWarps;
+    const int64_t cb = (((te) * total_warps - 1) / units) / kWarps;
+    float sum[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t c = ca; c <= cb; ++c) {
+      const int64_t c0 = c * kWarps * units / total_warps, c1 = (c + 1) * kWarps * units / total_warps;
+      if (c1 <= c0) continue;
+      const int cs2 = t == (int)(c0 / a.blocks) ? 0 : 1;
+      const float4 p = __ldcg(reinterpret_cast<const float4*>(a.partial) + (c * 2 + cs2) * 32 + lane);
+      sum[0] += p.x;
+      sum[1] += p.y;
+      sum[2] += p.z;
+      sum[3] += p.w;
+    }
+    if (lane == 0) a.counters[t] = 0;
+    epilogue<EPI>(a, t, sum, m, rowscale, lane);
+  }
 }
 
 // x f32 [m][k] -> fragments; one thread per (k pair, row).
@@ -267,9 +369,9 @@ __global__ void pack_activations_kernel(const float* x, int m, int k, int kp, ui
 
 }  // namespace
 
-int gemv_grid(int num_sms) { return num_sms * 2; }
+int gemv_grid(int num_sms) { return num_sms; }
 
-int64_t gemv_partial_floats(int grid) { return (int64_t)grid * kWarps * 2 * 32 * 4; }
+int64_t gemv_partial_floats(int grid) { return (int64_t)grid * 2 * 32 * 4; }
 
 void launch_gemv(int epi, const GemvArgs& a_in, int max_grid, cudaStream_t s, bool pdl) {
   GemvArgs a = a_in;
@@ -278,9 +380,16 @@ void launch_gemv(int epi, const GemvArgs& a_in, int max_grid, cudaStream_t s, bo
   const int64_t units = (int64_t)a.tiles * a.blocks;
   const int64_t want = (units + kWarps * 8 - 1) / (kWarps * 8);
   const int grid = (int)(want < max_grid ? (want > 0 ? want : 1) : max_grid);
+  static bool attr_set[3] = {false, false, false};
+  if (!attr_set[epi]) {
+    auto* k = epi == kEpiStore ? gemv_kernel<kEpiStore> : epi == kEpiSwiglu ? gemv_kernel<kEpiSwiglu> : gemv_kernel<kEpiHead>;
+    XTG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(GemvSmem)));
+    attr_set[epi] = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = sizeof(GemvSmem);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

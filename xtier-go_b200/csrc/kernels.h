@@ -66,6 +66,7 @@ struct GemvArgs {
   float* logits;             // [n][vocab]
   int vocab;
   ArgCand* cand;             // [tiles][8]
+  int* err;                  // set to 1 if a bounded wait gave up (never expected); may be null
   int pdl;                   // launched as a programmatic dependent
 };
 

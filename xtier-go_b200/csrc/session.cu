@@ -210,6 +210,7 @@ struct xtg_cuda {
   ArgCand* cand = nullptr;
   float* gemv_partial = nullptr;
   int* gemv_counters = nullptr;
+  int* dev_err = nullptr;   // bounded device waits that gave up (never expected)
   int gemv_grid_ = 0;
   int splits_g = 1, splits_r = 1;
   int proj_ld = 0;
@@ -465,6 +466,7 @@ struct xtg_cuda {
     gemv_grid_ = gemv_grid(num_sms);
     gemv_partial = dalloc<float>((size_t)gemv_partial_floats(gemv_grid_));
     gemv_counters = dalloc<int>((size_t)packed_tiles(c.vocab, false) + 4096);
+    dev_err = dalloc<int>(1);
     splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, (num_sms + c.kv_heads - 1) / c.kv_heads);
     splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, std::min<int>(c.ring / 64, 8));
     part = dalloc<float>((size_t)attention_part_floats(c.kv_heads, std::max(splits_g, splits_r)));
@@ -507,6 +509,7 @@ struct xtg_cuda {
     a.m_dev = &params_dev->m;
     a.partial = gemv_partial;
     a.counters = gemv_counters;
+    a.err = dev_err;
     a.outs = L.outs;
     a.sumsq = sumsq;
     a.nparts = nparts;
@@ -636,6 +639,7 @@ struct xtg_cuda {
     a.m_dev = &params_dev->m;
     a.partial = gemv_partial;
     a.counters = gemv_counters;
+    a.err = dev_err;
     a.g_head = head.g0;
     a.logit_scale = logit_scale;
     a.logits = logits;
