@@ -221,38 +221,27 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
   for (int dt = 0; dt < 16; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.f;
   float run_m0 = -INFINITY, run_m1 = -INFINITY, run_l0 = 0.f, run_l1 = 0.f;
 
-  // one 64-key chunk: keys come from the cache (own = false, slot base c0) or this call's rows (own = true)
-  auto chunk = [&](int64_t c0, bool own) {
+  // one 64-key chunk of the cache at slot base c0
+  auto chunk = [&](int64_t c0) {
     // ---- S = Q K^T: 8 n8-tiles, tile T = 2 j + ab holds slots c0 + 16 (n >> 1) + 4 j + (n & 1) + 2 ab ----
     float s[8][4];
-    uint32_t kw[8][8];   // the K row this lane supplies to each tile: 32 bytes (head dims 32 tq ..)
+    const uint8_t* krow[8];   // the K row this lane supplies to each tile, at head dims 32 tq ..
 #pragma unroll
     for (int T = 0; T < 8; ++T) {
       const int key = 16 * (g >> 1) + 4 * (T >> 1) + (g & 1) + 2 * (T & 1);
+      krow[T] = kc + (c0 + key) * kD + 32 * tq;
       s[T][0] = s[T][1] = s[T][2] = s[T][3] = 0.f;
-      if (!own) {
-        const uint4* kr = reinterpret_cast<const uint4*>(kc + (c0 + key) * kD + 32 * tq);
-        const uint4 k0 = __ldg(kr), k1 = __ldg(kr + 1);
-        kw[T][0] = k0.x; kw[T][1] = k0.y; kw[T][2] = k0.z; kw[T][3] = k0.w;
-        kw[T][4] = k1.x; kw[T][5] = k1.y; kw[T][6] = k1.z; kw[T][7] = k1.w;
-      }
     }
-#pragma unroll
+#pragma unroll 2
     for (int st = 0; st < 8; ++st) {
       const uint4 qh = sm.qf[mt][0][st][lane], ql = sm.qf[mt][1][st][lane];
+      uint32_t kw[8];
+#pragma unroll
+      for (int T = 0; T < 8; ++T) kw[T] = __ldg(reinterpret_cast<const uint32_t*>(krow[T] + 4 * st));
 #pragma unroll
       for (int T = 0; T < 8; ++T) {
         uint32_t b0, b1;
-        if (own) {
-          const int key = 16 * (g >> 1) + 4 * (T >> 1) + (g & 1) + 2 * (T & 1);
-          const int d0 = 32 * tq + 4 * st;
-          const bool ok = key < m;
-          const float* kr = sm.k[key < kMaxRows ? key : 0];
-          b0 = ok ? pack_f16x2(kr[d0], kr[d0 + 1]) : 0u;
-          b1 = ok ? pack_f16x2(kr[d0 + 2], kr[d0 + 3]) : 0u;
-        } else {
-          codes_to_f16(kw[T][st], a.dtype, b0, b1);
-        }
+        codes_to_f16(kw[T], a.dtype, b0, b1);
         mma_f16(s[T], qh.x, qh.y, qh.z, qh.w, b0, b1);
         mma_f16(s[T], ql.x, ql.y, ql.z, ql.w, b0, b1);
       }
@@ -260,14 +249,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     // ---- scale, mask, online softmax: this lane's keys are slots c0 + 16 tq + kk, kk = 4 j + 2 ab + {0, 1} ----
     float ksc[16], vsc[16];
     int kpos[16];
-    if (own) {
-#pragma unroll
-      for (int kk = 0; kk < 16; ++kk) {
-        ksc[kk] = 1.f;
-        vsc[kk] = 1.f;
-        kpos[kk] = 16 * tq + kk;   // own key index j
-      }
-    } else {
+    {
       const float4* k4 = reinterpret_cast<const float4*>(ks + c0 + 16 * tq);
       const float4* v4 = reinterpret_cast<const float4*>(vs + c0 + 16 * tq);
 #pragma unroll
@@ -295,15 +277,9 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
       for (int c = 0; c < 2; ++c) {
         const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
         const int p = kpos[kk];
-        bool vis0, vis1;
-        if (own) {
-          vis0 = live0 && p < m && p <= arow0 && (a.window == 0 || arow0 - p < a.window);
-          vis1 = live1 && p < m && p <= arow1 && (a.window == 0 || arow1 - p < a.window);
-        } else {
-          const bool ok = p >= 0 && p < pos0;
-          vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
-          vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
-        }
+        const bool ok = p >= 0 && p < pos0;
+        const bool vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
+        const bool vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
         const float f = ksc[kk] * a.scale;
         s[T][c] = vis0 ? s[T][c] * f : -INFINITY;
         s[T][2 + c] = vis1 ? s[T][2 + c] * f : -INFINITY;
@@ -355,37 +331,89 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     // ---- O += P' V: V^T row d = 8 dt + g, lane tq reads slots c0 + 16 tq .. + 15 ----
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) {
-      const int d = 8 * dt + g;
-      uint32_t vw[4];
-      if (own) {
+      const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vc + (int64_t)(8 * dt + g) * slots + c0 + 16 * tq));
+      const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          // slots 16 tq + 4 j + {0, 1, 2, 3}: own rows only exist for tq = 0
-          const int k0 = 16 * tq + 4 * j;
-          float f[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) f[q] = (k0 + q < m) ? sm.v[k0 + q < kMaxRows ? k0 + q : 0][d] : 0.f;
-          const uint32_t lo = pack_f16x2(f[0], f[1]), hi = pack_f16x2(f[2], f[3]);
-          mma_f16(acc[dt], pa[j][0], pa[j][1], pa[j][2], pa[j][3], lo, hi);
-        }
-        (void)vw;
-      } else {
-        const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vc + (int64_t)d * slots + c0 + 16 * tq));
-        vw[0] = vv.x; vw[1] = vv.y; vw[2] = vv.z; vw[3] = vv.w;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t b0, b1;
-          codes_to_f16(vw[j], a.dtype, b0, b1);
-          mma_f16(acc[dt], pa[j][0], pa[j][1], pa[j][2], pa[j][3], b0, b1);
-        }
+      for (int j = 0; j < 4; ++j) {
+        uint32_t b0, b1;
+        codes_to_f16(vw[j], a.dtype, b0, b1);
+        mma_f16(acc[dt], pa[j][0], pa[j][1], pa[j][2], pa[j][3], b0, b1);
       }
     }
   };
 
+  // this call's own keys j < m, exactly in FP32 on the CUDA cores (the reference attends to them unquantized):
+  // lane (g, tq) owns query rows 16 mt + g, + 8 and head dims 8 dt + 2 tq + {0, 1} of the accumulators
+  auto own_rows = [&]() {
+    const float* q0 = sm.q[16 * mt + g];
+    const float* q1 = sm.q[16 * mt + g + 8];
+    float s0[kMaxRows], s1[kMaxRows];
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) {
+      float d0 = 0.f, d1 = 0.f;
+      if (j < m) {
+        const float* kr = sm.k[j];
+#pragma unroll 8
+        for (int e = 32 * tq; e < 32 * tq + 32; ++e) {
+          d0 += q0[e] * kr[e];
+          d1 += q1[e] * kr[e];
+        }
+      }
+      d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
+      d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
+      d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
+      d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
+      const bool vis0 = live0 && j < m && j <= arow0 && (a.window == 0 || arow0 - j < a.window);
+      const bool vis1 = live1 && j < m && j <= arow1 && (a.window == 0 || arow1 - j < a.window);
+      s0[j] = vis0 ? d0 * a.scale : -INFINITY;
+      s1[j] = vis1 ? d1 * a.scale : -INFINITY;
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) {
+      mx0 = fmaxf(mx0, s0[j]);
+      mx1 = fmaxf(mx1, s1[j]);
+    }
+    const float new_m0 = fmaxf(run_m0, mx0), new_m1 = fmaxf(run_m1, mx1);
+    const float corr0 = new_m0 == -INFINITY ? 1.f : expf(run_m0 - new_m0);
+    const float corr1 = new_m1 == -INFINITY ? 1.f : expf(run_m1 - new_m1);
+    run_m0 = new_m0;
+    run_m1 = new_m1;
+    // the row sums are kept spread over the 4 lanes of a row: lane tq = 0 adds this call's keys
+    run_l0 *= corr0;
+    run_l1 *= corr1;
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) {
+      s0[j] = s0[j] == -INFINITY ? 0.f : expf(s0[j] - new_m0);
+      s1[j] = s1[j] == -INFINITY ? 0.f : expf(s1[j] - new_m1);
+      if (tq == 0) {
+        run_l0 += s0[j];
+        run_l1 += s1[j];
+      }
+    }
+#pragma unroll
+    for (int dt = 0; dt < 16; ++dt) {
+      const int d = 8 * dt + 2 * tq;
+      float o00 = acc[dt][0] * corr0, o01 = acc[dt][1] * corr0, o10 = acc[dt][2] * corr1, o11 = acc[dt][3] * corr1;
+#pragma unroll
+      for (int j = 0; j < kMaxRows; ++j) {
+        const float v0 = sm.v[j][d], v1 = sm.v[j][d + 1];
+        o00 += s0[j] * v0;
+        o01 += s0[j] * v1;
+        o10 += s1[j] * v0;
+        o11 += s1[j] * v1;
+      }
+      acc[dt][0] = o00;
+      acc[dt][1] = o01;
+      acc[dt][2] = o10;
+      acc[dt][3] = o11;
+    }
+  };
+
   if (active) {
-    for (int64_t c = cb + half; c < ce; c += 2) chunk(c * 64, false);
+    for (int64_t c = cb + half; c < ce; c += 2) chunk(c * 64);
     // this call's own keys: the last split, the first half
-    if (split == a.splits - 1 && half == 0) chunk(0, true);
+    if (split == a.splits - 1 && half == 0) own_rows();
   }
   // the row sums live spread over the 4 lanes of a row
   run_l0 += __shfl_xor_sync(0xffffffffu, run_l0, 1);

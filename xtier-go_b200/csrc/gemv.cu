@@ -161,26 +161,30 @@ __device__ __forceinline__ void epilogue(const GemvArgs& a, int t, const float (
 }
 
 // One block: 4 k16 steps, each an MMA of 16 rows x 16 inputs x 8 activation rows; even steps accumulate into acc,
-// odd steps into acc2 (two independent MMA chains).
+// odd steps into acc2 (two independent MMA chains). xb: this block's activation fragments (two uint4, a pair of
+// steps each).
 __device__ __forceinline__ void block_mma2(float (&acc)[4], float (&acc2)[4], const uint4 w, const uint2 s,
-                                           const uint2* xb) {
+                                           const uint4* xb) {
+  const uint4 b01 = xb[0], b23 = xb[32];
+  const uint32_t bx[4] = {b01.x, b01.z, b23.x, b23.z}, by[4] = {b01.y, b01.w, b23.y, b23.w};
   const uint32_t wr[4] = {w.x, w.y, w.z, w.w};
-  uint2 b[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) b[j] = xb[j * 32];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const uint32_t sc = e4m3x2_to_f16x2(j < 2 ? (s.x >> (16 * j)) : (s.y >> (16 * (j - 2))));
-    const uint32_t s_lo = __byte_perm(sc, 0, 0x1010), s_hi = __byte_perm(sc, 0, 0x3232);
-    const uint32_t q = wr[j];
-    const uint32_t a0 = hmul2_u32(e2m1x2_to_f16x2(q & 0xff), s_lo);
-    const uint32_t a1 = hmul2_u32(e2m1x2_to_f16x2((q >> 8) & 0xff), s_hi);
-    const uint32_t a2 = hmul2_u32(e2m1x2_to_f16x2((q >> 16) & 0xff), s_lo);
-    const uint32_t a3 = hmul2_u32(e2m1x2_to_f16x2(q >> 24), s_hi);
+    const __half2 sh = *reinterpret_cast<const __half2*>(&sc);
+    const __half2 s_lo = __low2half2(sh), s_hi = __high2half2(sh);
+    uint32_t c[4];
+    e2m1x8_to_f16x2x4(wr[j], c);
+    const __half2 h0 = __hmul2(*reinterpret_cast<const __half2*>(&c[0]), s_lo);
+    const __half2 h1 = __hmul2(*reinterpret_cast<const __half2*>(&c[1]), s_hi);
+    const __half2 h2 = __hmul2(*reinterpret_cast<const __half2*>(&c[2]), s_lo);
+    const __half2 h3 = __hmul2(*reinterpret_cast<const __half2*>(&c[3]), s_hi);
+    const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&h0), a1 = *reinterpret_cast<const uint32_t*>(&h1);
+    const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&h2), a3 = *reinterpret_cast<const uint32_t*>(&h3);
     if (j & 1)
-      mma_f16(acc2, a0, a1, a2, a3, b[j].x, b[j].y);
+      mma_f16(acc2, a0, a1, a2, a3, bx[j], by[j]);
     else
-      mma_f16(acc, a0, a1, a2, a3, b[j].x, b[j].y);
+      mma_f16(acc, a0, a1, a2, a3, bx[j], by[j]);
   }
 }
 
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     __syncthreads();
   }
   const float* rowscale = sm.rowscale;
-  const uint2* x16 = reinterpret_cast<const uint2*>(a.x16);
+  const uint4* x16 = reinterpret_cast<const uint4*>(a.x16);
   const int first_tile = n > 0 ? (int)(u0 / a.blocks) : -1;
   if (n > 0) {
     int t = first_tile;
@@ -263,6 +267,19 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     int part_kb0 = kb;
     float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
     uint32_t parity = 0;
+    // the end of tile t's part: the epilogue for a whole tile, else a shared-memory slot
+    auto tile_done = [&]() {
+      float f[4] = {acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]};
+      if (part_kb0 == 0)
+        epilogue<EPI>(a, t, f, m, rowscale, lane);
+      else
+        sm.part[warp][t == first_tile ? 0 : 1][lane] = make_float4(f[0], f[1], f[2], f[3]);
+      ++t;
+      kb = 0;
+      part_kb0 = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[q] = acc2[q] = 0.f;
+    };
     for (int st = 0; st < nst; ++st) {
       const int slot = st % kStages;
       uint32_t spins = 0;
@@ -273,26 +290,22 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
         }
       }
       parity ^= 1u << slot;
-      const unsigned char* buf = sm.ring[warp][slot];
+      const unsigned char* buf = sm.ring[warp][slot] + lane * 16;
+      const unsigned char* sbuf = sm.ring[warp][slot] + 512 + (lane >> 2) * 8;
       const int cnt = n - st * kStageBlocks < kStageBlocks ? n - st * kStageBlocks : kStageBlocks;
+      if (cnt == kStageBlocks && kb + kStageBlocks <= a.blocks) {   // the common case: no boundary inside
+        const uint4* xb = x16 + kb * 64 + lane;
 #pragma unroll
-      for (int i = 0; i < kStageBlocks; ++i) {
-        if (i < cnt) {
-          const uint4 w = *reinterpret_cast<const uint4*>(buf + i * kBlockBytes + lane * 16);
-          const uint2 sc = *reinterpret_cast<const uint2*>(buf + i * kBlockBytes + 512 + (lane >> 2) * 8);
-          block_mma2(acc, acc2, w, sc, x16 + kb * 128 + lane);
-          if (++kb == a.blocks) {   // the part reaches the end of tile t
-            float f[4] = {acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]};
-            if (part_kb0 == 0)
-              epilogue<EPI>(a, t, f, m, rowscale, lane);
-            else
-              sm.part[warp][t == first_tile ? 0 : 1][lane] = make_float4(f[0], f[1], f[2], f[3]);
-            ++t;
-            kb = 0;
-            part_kb0 = 0;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) acc[q] = acc2[q] = 0.f;
-          }
+        for (int i = 0; i < kStageBlocks; ++i)
+          block_mma2(acc, acc2, *reinterpret_cast<const uint4*>(buf + i * kBlockBytes),
+                     *reinterpret_cast<const uint2*>(sbuf + i * kBlockBytes), xb + i * 64);
+        kb += kStageBlocks;
+        if (kb == a.blocks) tile_done();
+      } else {
+        for (int i = 0; i < cnt; ++i) {
+          block_mma2(acc, acc2, *reinterpret_cast<const uint4*>(buf + i * kBlockBytes),
+                     *reinterpret_cast<const uint2*>(sbuf + i * kBlockBytes), x16 + kb * 64 + lane);
+          if (++kb == a.blocks) tile_done();
         }
       }
       __syncwarp();
@@ -369,7 +382,7 @@ __global__ void pack_activations_kernel(const float* x, int m, int k, int kp, ui
 
 }  // namespace
 
-int gemv_grid(int num_sms) { return num_sms; }
+int gemv_grid(int num_sms) { return num_sms * 2; }
 
 int64_t gemv_partial_floats(int grid) { return (int64_t)grid * 2 * 32 * 4; }
 
