@@ -71,6 +71,9 @@ struct Smem {
   float q[kQRows][kD + 4];        // prepared queries (query row = group * activation row + head in group)
   float k[kMaxRows][kD + 4];      // this call's keys / values (prepared)
   float v[kMaxRows][kD + 4];
+  float rc[kMaxRows][64];          // this step's RoPE cos / sin rows
+  float rs[kMaxRows][64];
+  float qsc[4][kD];               // the q scales of this KV head's q heads
   float mrg_m[2][16];             // half-1 warps' softmax state for the merge
   float mrg_l[2][16];
   float mrg_acc[2][16][kD + 4];
@@ -107,19 +110,15 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
   }
 
   // ---- prepare Q and this call's K / V (RoPE + justnorm + q scale in the fused step) ----
-  // task = (activation row i, vector: q heads of the group, then k, then v); a warp takes tasks warp, warp + 4, ...
-  // in batches whose loads are all issued before any is used (one round trip per batch, not one per task)
-  const int ntask = kMaxRows * (group + 2);
-  constexpr int kBatchT = 6;
-  for (int t0 = warp; t0 < ntask; t0 += 4 * kBatchT) {
-    float xs[kBatchT][4], cs[kBatchT][4], qs4[kBatchT][4];
-#pragma unroll
-    for (int j = 0; j < kBatchT; ++j) {
-      const int task = t0 + 4 * j;
-      const int i = task / (group + 2), which = task % (group + 2);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) xs[j][q] = cs[j][q] = qs4[j][q] = 0.f;
-      if (task < ntask && i < m) {
+  // (1) every vector this CTA needs lands in shared memory in one coalesced wave of 16-byte loads
+  {
+    const int nvec = kMaxRows * (group + 2);
+#pragma unroll 4
+    for (int idx = threadIdx.x; idx < nvec * 32; idx += kThreads) {
+      const int vec = idx >> 5, f4 = idx & 31;
+      const int i = vec / (group + 2), which = vec % (group + 2);
+      float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < m) {
         const float* src;
         if (a.proj) {
           const float* row = a.proj + (int64_t)i * a.proj_ld;
@@ -129,51 +128,54 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
           src = which < group ? a.q + ((int64_t)i * a.heads + kvh * group + which) * kD
                               : (which == group ? a.k : a.v) + ((int64_t)i * a.kv_heads + kvh) * kD;
         }
-        xs[j][0] = src[lane];
-        xs[j][1] = src[lane + 64];
-        xs[j][2] = src[lane + 32];
-        xs[j][3] = src[lane + 96];
-        if (a.proj && which <= group) {
-          cs[j][0] = a.rope_cos[i * (kD / 2) + lane];
-          cs[j][1] = a.rope_sin[i * (kD / 2) + lane];
-          cs[j][2] = a.rope_cos[i * (kD / 2) + lane + 32];
-          cs[j][3] = a.rope_sin[i * (kD / 2) + lane + 32];
-          if (which < group) {
-            const float* qsp = a.qscale + (int64_t)(kvh * group + which) * kD;
-            qs4[j][0] = qsp[lane];
-            qs4[j][1] = qsp[lane + 64];
-            qs4[j][2] = qsp[lane + 32];
-            qs4[j][3] = qsp[lane + 96];
-          }
-        }
+        val = reinterpret_cast<const float4*>(src)[f4];
       }
+      float* dst = which < group ? sm.q[i * group + which] : (which == group ? sm.k[i] : sm.v[i]);
+      reinterpret_cast<float4*>(dst)[f4] = val;
     }
-#pragma unroll
-    for (int j = 0; j < kBatchT; ++j) {
-      const int task = t0 + 4 * j;
-      if (task >= ntask) break;
-      const int i = task / (group + 2), which = task % (group + 2);
-      float* x = xs[j];
-      if (i < m && a.proj && which <= group) {   // q and k: RoPE, then justnorm per head (q also times q scale)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const float c = cs[j][2 * h], sn = cs[j][2 * h + 1];
-          const float x1 = x[2 * h], x2 = x[2 * h + 1];
-          x[2 * h] = x1 * c - x2 * sn;
-          x[2 * h + 1] = x2 * c + x1 * sn;
-        }
-        const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
-        const float f = 1.f / sqrtf(ss + 1e-6f);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) x[q] *= f;
-        if (which < group) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) x[q] *= qs4[j][q];
-        }
+    if (a.proj) {
+      for (int idx = threadIdx.x; idx < kMaxRows * 16; idx += kThreads) {
+        reinterpret_cast<float4*>(&sm.rc[0][0])[idx] = reinterpret_cast<const float4*>(a.rope_cos)[idx];
+        reinterpret_cast<float4*>(&sm.rs[0][0])[idx] = reinterpret_cast<const float4*>(a.rope_sin)[idx];
       }
-      if (i < m && a.store && split == 0 && which >= group) {   // this call's rows into the cache
+      for (int idx = threadIdx.x; idx < group * 32; idx += kThreads)
+        reinterpret_cast<float4*>(&sm.qsc[0][0])[idx] =
+            reinterpret_cast<const float4*>(a.qscale + (int64_t)kvh * group * kD)[idx];
+    }
+  }
+  __syncthreads();
+  // (2) per vector (a warp each): RoPE and justnorm for q and k, q times its scales; this call's K / V rows into the
+  // cache (the first split)
+  if (a.proj || a.store) {
+    const int nvec = kMaxRows * (group + 2);
+    for (int vec = warp; vec < nvec; vec += kThreads / 32) {
+      const int i = vec / (group + 2), which = vec % (group + 2);
+      if (i >= m) continue;
+      float* x = which < group ? sm.q[i * group + which] : (which == group ? sm.k[i] : sm.v[i]);
+      float v0 = x[lane], v1 = x[lane + 64], v2 = x[lane + 32], v3 = x[lane + 96];
+      if (a.proj && which <= group) {
+        const float c0 = sm.rc[i][lane], s0 = sm.rs[i][lane], c1 = sm.rc[i][lane + 32], s1 = sm.rs[i][lane + 32];
+        const float r0 = v0 * c0 - v1 * s0, r1 = v1 * c0 + v0 * s0;
+        const float r2 = v2 * c1 - v3 * s1, r3 = v3 * c1 + v2 * s1;
+        const float f = 1.f / sqrtf(warp_sum(r0 * r0 + r1 * r1 + r2 * r2 + r3 * r3) + 1e-6f);
+        v0 = r0 * f;
+        v1 = r1 * f;
+        v2 = r2 * f;
+        v3 = r3 * f;
+        if (which < group) {
+          v0 *= sm.qsc[which][lane];
+          v1 *= sm.qsc[which][lane + 64];
+          v2 *= sm.qsc[which][lane + 32];
+          v3 *= sm.qsc[which][lane + 96];
+        }
+        x[lane] = v0;
+        x[lane + 64] = v1;
+        x[lane + 32] = v2;
+        x[lane + 96] = v3;
+      }
+      if (a.store && split == 0 && which >= group) {
         const int64_t p = pos0 + i, slot = a.ring ? p % slots : p;
-        const float xv[4] = {x[0], x[1], x[2], x[3]};
+        const float xv[4] = {v0, v1, v2, v3};
         if (which == group)
           encode_row(xv, a.dtype, lane, a.kc + ((int64_t)kvh * slots + slot) * kD, nullptr, 0,
                      a.ks + (int64_t)kvh * slots + slot);
@@ -181,17 +183,9 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
           encode_row(xv, a.dtype, lane, nullptr, a.vc + (int64_t)kvh * kD * slots + slot, slots,
                      a.vs + (int64_t)kvh * slots + slot);
       }
-      float* dst = which < group ? sm.q[i * group + which] : (which == group ? sm.k[i] : sm.v[i]);
-      dst[lane] = x[0];
-      dst[lane + 64] = x[1];
-      dst[lane + 32] = x[2];
-      dst[lane + 96] = x[3];
     }
   }
   __syncthreads();
-
-  const int mt = warp & 1, half = warp >> 1;
-  const bool active = (16 * mt) / group < m;   // this warp's query rows hold at least one activation row
   // A fragments of Q, split q = hi + lo (both fp16) so that the scores keep ~22 bits: step st, lane tq reads head
   // dims 32 tq + 4 st + {0, 1} (a0, a1) and + {2, 3} (a2, a3)
   for (int idx = threadIdx.x; idx < 2 * 8 * 32; idx += kThreads) {
@@ -211,6 +205,8 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     sm.qf[t2][1][st][l] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
   __syncthreads();
+  const int mt = warp & 1, half = warp >> 1;
+  const bool active = (16 * mt) / group < m;   // this warp's query rows hold at least one activation row
   // the activation rows of this lane's two query rows and their positions
   const int arow0 = (16 * mt + g) / group, arow1 = (16 * mt + g + 8) / group;
   const int t0 = pos0 + arow0, t1 = pos0 + arow1;
@@ -342,71 +338,59 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     }
   };
 
-  // this call's own keys j < m, exactly in FP32 on the CUDA cores (the reference attends to them unquantized):
-  // lane (g, tq) owns query rows 16 mt + g, + 8 and head dims 8 dt + 2 tq + {0, 1} of the accumulators
+  // this call's own keys j < m: scores in FP32 from the prepared rows (the reference attends to them unquantized);
+  // lane (g, tq) scores keys 2 tq, 2 tq + 1 for query rows 16 mt + g and + 8, then P V on the tensor cores (keys
+  // 0..15 of one k16 step, the upper 8 empty)
   auto own_rows = [&]() {
     const float* q0 = sm.q[16 * mt + g];
     const float* q1 = sm.q[16 * mt + g + 8];
-    float s0[kMaxRows], s1[kMaxRows];
+    float sc[2][2];
 #pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) {
+    for (int c = 0; c < 2; ++c) {
+      const int j = 2 * tq + c;
+      const float* kr = sm.k[j];
       float d0 = 0.f, d1 = 0.f;
-      if (j < m) {
-        const float* kr = sm.k[j];
-#pragma unroll 8
-        for (int e = 32 * tq; e < 32 * tq + 32; ++e) {
-          d0 += q0[e] * kr[e];
-          d1 += q1[e] * kr[e];
-        }
+#pragma unroll 4
+      for (int e = 0; e < kD; e += 4) {
+        const float4 kv = *reinterpret_cast<const float4*>(kr + e);
+        const float4 a4 = *reinterpret_cast<const float4*>(q0 + e);
+        const float4 b4 = *reinterpret_cast<const float4*>(q1 + e);
+        d0 += a4.x * kv.x + a4.y * kv.y + a4.z * kv.z + a4.w * kv.w;
+        d1 += b4.x * kv.x + b4.y * kv.y + b4.z * kv.z + b4.w * kv.w;
       }
-      d0 += __shfl_xor_sync(0xffffffffu, d0, 1);
-      d0 += __shfl_xor_sync(0xffffffffu, d0, 2);
-      d1 += __shfl_xor_sync(0xffffffffu, d1, 1);
-      d1 += __shfl_xor_sync(0xffffffffu, d1, 2);
       const bool vis0 = live0 && j < m && j <= arow0 && (a.window == 0 || arow0 - j < a.window);
       const bool vis1 = live1 && j < m && j <= arow1 && (a.window == 0 || arow1 - j < a.window);
-      s0[j] = vis0 ? d0 * a.scale : -INFINITY;
-      s1[j] = vis1 ? d1 * a.scale : -INFINITY;
+      sc[0][c] = vis0 ? d0 * a.scale : -INFINITY;
+      sc[1][c] = vis1 ? d1 * a.scale : -INFINITY;
     }
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) {
-      mx0 = fmaxf(mx0, s0[j]);
-      mx1 = fmaxf(mx1, s1[j]);
-    }
+    float mx0 = fmaxf(sc[0][0], sc[0][1]), mx1 = fmaxf(sc[1][0], sc[1][1]);
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
     const float new_m0 = fmaxf(run_m0, mx0), new_m1 = fmaxf(run_m1, mx1);
     const float corr0 = new_m0 == -INFINITY ? 1.f : expf(run_m0 - new_m0);
     const float corr1 = new_m1 == -INFINITY ? 1.f : expf(run_m1 - new_m1);
     run_m0 = new_m0;
     run_m1 = new_m1;
-    // the row sums are kept spread over the 4 lanes of a row: lane tq = 0 adds this call's keys
-    run_l0 *= corr0;
-    run_l1 *= corr1;
+    float p[2][2];
 #pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) {
-      s0[j] = s0[j] == -INFINITY ? 0.f : expf(s0[j] - new_m0);
-      s1[j] = s1[j] == -INFINITY ? 0.f : expf(s1[j] - new_m1);
-      if (tq == 0) {
-        run_l0 += s0[j];
-        run_l1 += s1[j];
-      }
+    for (int c = 0; c < 2; ++c) {
+      p[0][c] = sc[0][c] == -INFINITY ? 0.f : expf(sc[0][c] - new_m0);
+      p[1][c] = sc[1][c] == -INFINITY ? 0.f : expf(sc[1][c] - new_m1);
     }
+    run_l0 = run_l0 * corr0 + p[0][0] + p[0][1];
+    run_l1 = run_l1 * corr1 + p[1][0] + p[1][1];
+    const uint32_t pa0 = pack_f16x2(p[0][0], p[0][1]), pa1 = pack_f16x2(p[1][0], p[1][1]);
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) {
-      const int d = 8 * dt + 2 * tq;
-      float o00 = acc[dt][0] * corr0, o01 = acc[dt][1] * corr0, o10 = acc[dt][2] * corr1, o11 = acc[dt][3] * corr1;
-#pragma unroll
-      for (int j = 0; j < kMaxRows; ++j) {
-        const float v0 = sm.v[j][d], v1 = sm.v[j][d + 1];
-        o00 += s0[j] * v0;
-        o01 += s0[j] * v1;
-        o10 += s1[j] * v0;
-        o11 += s1[j] * v1;
-      }
-      acc[dt][0] = o00;
-      acc[dt][1] = o01;
-      acc[dt][2] = o10;
-      acc[dt][3] = o11;
+      const int d = 8 * dt + g;
+      acc[dt][0] *= corr0;
+      acc[dt][1] *= corr0;
+      acc[dt][2] *= corr1;
+      acc[dt][3] *= corr1;
+      const uint32_t b0 = pack_f16x2(sm.v[2 * tq][d], sm.v[2 * tq + 1][d]);
+      mma_f16(acc[dt], pa0, pa1, 0u, 0u, b0, 0u);
     }
   };
 

@@ -78,8 +78,8 @@ __device__ __forceinline__ float2 block_sum2(float x, float y, float2* red) {
 
 // One CTA per activation row: the residual updates. All norms are justnorm: x / sqrt(sum x^2 + 1e-6). Each thread
 // holds kPer elements (k = thread + j * blockDim) in registers.
-constexpr int kResidThreads = 512;
-constexpr int kPer = 16;   // hidden <= 8192
+constexpr int kResidThreads = 1024;
+constexpr int kPer = 8;   // hidden <= 8192
 
 __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a) {
   __shared__ float2 red[32];
