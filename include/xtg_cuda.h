@@ -116,9 +116,13 @@ XTG_CUDA_API int xtg_cuda_quantize_nvfp4(const uint16_t* w_bf16, int n_out, int 
                             float* global, void* stream, char* err, int err_len);
 
 // attention(pool, AttnArgs) (engine/include/xtg/kv.h:64-79, engine/src/kv.cpp:166-286) over a device KV cache in this
-// library's layout: K codes [kv_heads][slots][128], V codes [kv_heads][128][slots], scales f32 [kv_heads][slots];
+// library's layout (slots a multiple of 64; 16-byte aligned buffers):
+//   K codes [kv_heads][slots][128]: the 16-byte unit u of slot s's row lies at unit u ^ ((s % 64) ^ (s % 64 >> 3)) & 7;
+//   V codes [kv_heads][slots / 64][128][64]: per 64-slot chunk, head dim d's row of 64 slots, its 16-byte unit u at
+//     unit u ^ ((d >> 1) & 3);
+//   scales f32 [kv_heads][slots].
 // ring != 0: slot s holds position ring_pos[s] (int32, -1 empty), else slot = position. head_dim 128, at most 4 q
-// heads per KV head, n_q <= 8, slots a multiple of 64.
+// heads per KV head, n_q <= 8.
 typedef struct {
   int n_q;
   int64_t pos0;
@@ -139,7 +143,7 @@ typedef struct {
 } xtg_cuda_attn_args;
 XTG_CUDA_API int xtg_cuda_attention(const xtg_cuda_attn_args* a, int splits, void* stream, char* err, int err_len);
 
-// KvCache::store (engine/src/kv.cpp:75-112) into this layout: rows k, v [n][kv_heads][128] (device f32) at positions
+// KvCache::store (engine/src/kv.cpp:75-112) into the layout above: rows k, v [n][kv_heads][128] (device f32) at positions
 // pos .. pos + n - 1; a ring keeps the last `slots`. int8: scale amax / 127; FP8: amax / 448 (the reference's rule).
 XTG_CUDA_API int xtg_cuda_kv_store(const float* k, const float* v, int64_t pos, int n, int kv_heads, int64_t slots, int ring,
                       int dtype, uint8_t* k_codes, uint8_t* v_codes, float* k_scales, float* v_scales, void* stream,

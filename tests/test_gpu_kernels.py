@@ -145,11 +145,30 @@ def test_gemv_deterministic(cuda, xtg, torch_mod):
 
 # ---- attention ----
 
+def swz_k(s64):
+    return (s64 ^ (s64 >> 3)) & 7
+
+
+def k_index(kvh, slots):
+    """Flat position of element (h, s, d) of K in the library's layout (include/xtg_cuda.h), shape [h][s][d]."""
+    h, sl, d = np.meshgrid(np.arange(kvh), np.arange(slots), np.arange(128), indexing="ij")
+    return (h * slots + sl) * 128 + 16 * ((d >> 4) ^ swz_k(sl & 63)) + (d & 15)
+
+
+def v_index(kvh, slots):
+    """Flat position of element (h, d, s) of V, shape [h][d][s]."""
+    h, d, sl = np.meshgrid(np.arange(kvh), np.arange(128), np.arange(slots), indexing="ij")
+    return ((h * (slots // 64) + sl // 64) * 128 + d) * 64 + 16 * (((sl & 63) >> 4) ^ ((d >> 1) & 3)) + (sl & 15)
+
+
 def cache_to_device(torch, codes_k, codes_v, ks, vs):
-    """Oracle layout [slots][kv_heads][128] / [slots][kv_heads] -> the library's K [h][slots][128], V [h][128][slots],
-    scales [h][slots]."""
-    kc = np.ascontiguousarray(codes_k.transpose(1, 0, 2))
-    vc = np.ascontiguousarray(codes_v.transpose(1, 2, 0))
+    """Oracle layout [slots][kv_heads][128] / [slots][kv_heads] -> the library's K and V layouts and scales
+    [h][slots]."""
+    slots, kvh, _ = codes_k.shape
+    kc = np.zeros(kvh * slots * 128, np.uint8)
+    vc = np.zeros_like(kc)
+    kc[k_index(kvh, slots)] = codes_k.transpose(1, 0, 2)
+    vc[v_index(kvh, slots)] = codes_v.transpose(1, 2, 0)
     return dev(torch, kc), dev(torch, vc), dev(torch, np.ascontiguousarray(ks.T)), dev(torch, np.ascontiguousarray(vs.T))
 
 
@@ -256,12 +275,14 @@ def test_kv_store_bit_exact(cuda, xtg, torch_mod, dtype, ring):
     k = O.gen_uniform(41, 1, -3.0, 3.0, n * kvh * 128).reshape(n, kvh, 128)
     v = O.gen_uniform(41, 2, -0.2, 0.2, n * kvh * 128).reshape(n, kvh, 128)
     k[5, 1] = 0.0
-    kc = torch.zeros((kvh, slots, 128), dtype=torch.uint8, device="cuda")
-    vc = torch.zeros((kvh, 128, slots), dtype=torch.uint8, device="cuda")
+    kc = torch.zeros(kvh * slots * 128, dtype=torch.uint8, device="cuda")
+    vc = torch.zeros(kvh * slots * 128, dtype=torch.uint8, device="cuda")
     kss = torch.zeros((kvh, slots), dtype=torch.float32, device="cuda")
     vss = torch.zeros((kvh, slots), dtype=torch.float32, device="cuda")
     xtg.kv_store(dev(torch, k), dev(torch, v), pos, slots, ring, dtype, kc, vc, kss, vss)
     kc, vc, kss, vss = kc.cpu().numpy(), vc.cpu().numpy(), kss.cpu().numpy(), vss.cpu().numpy()
+    kc = kc[k_index(kvh, slots)]          # [h][s][d]
+    vc = vc[v_index(kvh, slots)]          # [h][d][s]
     first = pos + n - slots if ring and n > slots else pos
     for p in range(first, pos + n):
         s = p % slots if ring else p

@@ -339,7 +339,7 @@ def attention(q, k, v, k_codes, v_codes, k_scales, v_scales, pos0, window, scale
     out = torch.empty_like(q)
     a = AttnArgs(n_q, pos0, heads, kvh, d, window, scale, q.data_ptr(), k.data_ptr(), v.data_ptr(),
                  k_codes.data_ptr(), v_codes.data_ptr(), k_scales.data_ptr(), v_scales.data_ptr(),
-                 k_codes.shape[1], 1 if ring_pos is not None else 0,
+                 k_scales.shape[1], 1 if ring_pos is not None else 0,
                  ring_pos.data_ptr() if ring_pos is not None else None, dtype, out.data_ptr())
     err = _err()
     _check(lib().xtg_cuda_attention(C.byref(a), splits, _stream(), err, len(err)), err)

@@ -179,6 +179,7 @@ int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, ch
       a.kv_heads = p->kv_heads;
       a.splits = splits;
       a.part = part;
+      a.err = nullptr;
       launch_attention(a, s, false);
       CombineArgs cb = {};
       cb.part = part;

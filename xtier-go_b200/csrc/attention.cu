@@ -1,17 +1,18 @@
 // K3: GQA decode / verify attention over an int8 (or FP8) KV cache, split-KV with a log-sum-exp combine
 // (engine/src/kv.cpp:166-286 semantics; the visibility rule of npu/xtg_npu.cpp:236-258).
 //
-// Cache layout of one instance (HBM, written by this file and by the host's tier / snapshot copies):
-//   K codes [kv_heads][slots][128]   one row per slot, so a slot range of one head is contiguous
-//   V codes [kv_heads][128][slots]   transposed, so the PV operand is read as 16 contiguous slots per lane
-//   K / V scales f32 [kv_heads][slots]  (one per position and KV head: amax / 127 for int8, amax / 448 for FP8)
+// Cache layout of one instance: attention.h (k_offset / v_offset). A 64-slot chunk of one KV head is three
+// contiguous pieces -- 8 KB of K rows, 8 KB of V (head dim major), 256 B of each scale row -- streamed into shared
+// memory by bulk copies (cp.async.bulk, completion on an mbarrier, no multicast) before the kernel waits on the
+// previous one: the cached keys and values do not depend on it. Scales: one f32 per (position, KV head), amax / 127
+// for int8, amax / 448 for FP8.
 // A global instance's slot is the position; a ring's slot s holds position ring_pos[s] (-1 empty). A cached key at
 // position p is visible to the row at t when 0 <= p < pos0 (and t - p < window for a sliding layer); this call's
 // own key j is visible to own row i when j <= i (and i - j < window).
 //
 // One CTA per (split of the slots, KV head), 4 warps: warp w takes query rows 16 (w & 1) .. +15 -- a query row is
 // (activation row, q head of this KV head), 8 x 4 = 32 rows, so the 4 q heads sharing a KV head read it once -- and
-// 64-slot chunks w >> 1, +2, ... of the split. Both products run on mma.m16n8k16: int8 codes become f16 exactly
+// the warp pair w >> 1 takes 64-slot chunks pair, pair + 2, ... of the split through its own 2-stage ring. Both products run on mma.m16n8k16: int8 codes become f16 exactly
 // (1152 + b as a half, less 1152), FP8 codes by cvt.rn.f16x2.e4m3x2; Q (after RoPE, justnorm, q scale) is rounded
 // once to fp16; scores are scaled per key by its K scale in FP32, probabilities times the key's V scale are the
 // fp16 A operand of PV. Two permutations make every load contiguous: the head dimension inside a k16 step (lane tq
@@ -29,9 +30,10 @@ constexpr int kThreads = 128;
 constexpr int kQRows = 32;
 constexpr int kPartStride = kD + 2;   // m, l, acc[128]
 
-// Encode one row of 128 (a warp, 4 values per lane at e, e + 64, e + 32, e + 96) into codes and a scale.
-__device__ __forceinline__ void encode_row(const float (&x)[4], int dtype, int lane, uint8_t* row_k,
-                                           uint8_t* col_v, int64_t v_stride, float* scale_out) {
+// Encode one row of 128 (a warp, 4 values per lane at e, e + 64, e + 32, e + 96) into codes and a scale; value
+// rows go to V, key rows to K (attention.h layouts).
+__device__ __forceinline__ void encode_row(const float (&x)[4], int dtype, int lane, bool value, uint8_t* kc,
+                                           uint8_t* vc, float* scales, int h, int64_t slot, int64_t slots) {
   float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
   amax = warp_max(amax);
   const float top = dtype == kKvFp8 ? 448.f : 127.f;
@@ -49,10 +51,12 @@ __device__ __forceinline__ void encode_row(const float (&x)[4], int dtype, int l
       r = fminf(fmaxf(r, -127.f), 127.f);
       c = (uint8_t)(int8_t)(int)r;
     }
-    if (row_k) row_k[idx[j]] = c;
-    if (col_v) col_v[(int64_t)idx[j] * v_stride] = c;
+    if (value)
+      vc[v_offset(h, idx[j], slot, slots)] = c;
+    else
+      kc[k_offset(h, slot, idx[j], slots)] = c;
   }
-  if (lane == 0) *scale_out = sc;
+  if (lane == 0) scales[(int64_t)h * slots + slot] = sc;
 }
 
 __device__ __forceinline__ void codes_to_f16(uint32_t word, int dtype, uint32_t& lo, uint32_t& hi) {
@@ -66,7 +70,17 @@ __device__ __forceinline__ void codes_to_f16(uint32_t word, int dtype, uint32_t&
   }
 }
 
+struct Stage {                    // one 64-slot chunk of one KV head, as it lies in the cache
+  uint8_t k[64 * kD];
+  uint8_t v[kD * 64];
+  float ks[64];
+  float vs[64];
+  int32_t pos[64];
+};
+
 struct Smem {
+  Stage stage[2][2];              // [warp pair][ring slot]
+  uint64_t bar[2][2];
   uint4 qf[2][2][8][32];          // Q A fragments [m-tile][hi, lo][k16 step][lane]: q = hi + lo, both fp16
   float q[kQRows][kD + 4];        // prepared queries (query row = group * activation row + head in group)
   float k[kMaxRows][kD + 4];      // this call's keys / values (prepared)
@@ -98,11 +112,31 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
   const uint8_t* vc = a.vc + (int64_t)kvh * kD * slots;
   const float* ks = a.ks + (int64_t)kvh * slots;
   const float* vs = a.vs + (int64_t)kvh * slots;
-  if (ce > cb && threadIdx.x == 0) {   // the cache rows this CTA reads do not depend on the previous kernel
-    prefetch_l2(kc + cb * 64 * kD, (uint32_t)((ce - cb) * 64 * kD));
+  const int pair = warp >> 1;
+  const uint32_t stage_bytes = 2 * 64 * kD + 2 * 64 * 4 + (a.ring ? 64 * 4 : 0);
+  // chunk c of this head into ring slot j of `pair` (its first warp's lane 0)
+  auto issue = [&](int pr, int j, int64_t c) {
+    Stage& st = sm.stage[pr][j];
+    uint64_t* bar = &sm.bar[pr][j];
+    mbar_expect_tx(bar, stage_bytes);
+    bulk_g2s(st.k, kc + c * 64 * kD, 64 * kD, bar);
+    bulk_g2s(st.v, vc + c * 64 * kD, 64 * kD, bar);
+    bulk_g2s(st.ks, ks + c * 64, 64 * 4, bar);
+    bulk_g2s(st.vs, vs + c * 64, 64 * 4, bar);
+    if (a.ring) bulk_g2s(st.pos, a.ring_pos + c * 64, 64 * 4, bar);
+  };
+  // the cached keys and values do not depend on the previous kernel: start both pairs' first two chunks now
+  if (threadIdx.x == 0) {
+    for (int pr = 0; pr < 2; ++pr)
+      for (int j = 0; j < 2; ++j) mbar_init(&sm.bar[pr][j], 1);
+    mbar_init_fence();
   }
-  if (ce > cb && threadIdx.x < kD && !a.ring) {
-    prefetch_l2(vc + (int64_t)threadIdx.x * slots + cb * 64, (uint32_t)((ce - cb) * 64));
+  __syncthreads();
+  if (lane == 0 && (warp & 1) == 0) {
+    for (int j = 0; j < 2; ++j) {
+      const int64_t c = cb + pair + 2 * j;
+      if (c < ce) issue(pair, j, c);
+    }
   }
   if (a.pdl) {
     pdl_launch_next();
@@ -176,12 +210,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
       if (a.store && split == 0 && which >= group) {
         const int64_t p = pos0 + i, slot = a.ring ? p % slots : p;
         const float xv[4] = {v0, v1, v2, v3};
-        if (which == group)
-          encode_row(xv, a.dtype, lane, a.kc + ((int64_t)kvh * slots + slot) * kD, nullptr, 0,
-                     a.ks + (int64_t)kvh * slots + slot);
-        else
-          encode_row(xv, a.dtype, lane, nullptr, a.vc + (int64_t)kvh * kD * slots + slot, slots,
-                     a.vs + (int64_t)kvh * slots + slot);
+        encode_row(xv, a.dtype, lane, which != group, a.kc, a.vc, which == group ? a.ks : a.vs, kvh, slot, slots);
       }
     }
   }
@@ -205,7 +234,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     sm.qf[t2][1][st][l] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
   __syncthreads();
-  const int mt = warp & 1, half = warp >> 1;
+  const int mt = warp & 1, half = pair;
   const bool active = (16 * mt) / group < m;   // this warp's query rows hold at least one activation row
   // the activation rows of this lane's two query rows and their positions
   const int arow0 = (16 * mt + g) / group, arow1 = (16 * mt + g + 8) / group;
@@ -217,53 +246,49 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
   for (int dt = 0; dt < 16; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.f;
   float run_m0 = -INFINITY, run_m1 = -INFINITY, run_l0 = 0.f, run_l1 = 0.f;
 
-  // one 64-key chunk of the cache at slot base c0
-  auto chunk = [&](int64_t c0) {
-    // ---- S = Q K^T: 8 n8-tiles, tile T = 2 j + ab holds slots c0 + 16 (n >> 1) + 4 j + (n & 1) + 2 ab ----
+  // one 64-key chunk of the cache (slot base c0) from its shared-memory stage
+  auto chunk = [&](const Stage& stg, int64_t c0) {
+    // ---- S = Q K^T: 8 n8-tiles, tile T = 2 j + ab holds chunk slots 16 (n >> 1) + 4 j + (n & 1) + 2 ab ----
     float s[8][4];
-    const uint8_t* krow[8];   // the K row this lane supplies to each tile, at head dims 32 tq ..
 #pragma unroll
-    for (int T = 0; T < 8; ++T) {
-      const int key = 16 * (g >> 1) + 4 * (T >> 1) + (g & 1) + 2 * (T & 1);
-      krow[T] = kc + (c0 + key) * kD + 32 * tq;
-      s[T][0] = s[T][1] = s[T][2] = s[T][3] = 0.f;
-    }
-#pragma unroll 2
-    for (int st = 0; st < 8; ++st) {
-      const uint4 qh = sm.qf[mt][0][st][lane], ql = sm.qf[mt][1][st][lane];
-      uint32_t kw[8];
+    for (int T = 0; T < 8; ++T) s[T][0] = s[T][1] = s[T][2] = s[T][3] = 0.f;
 #pragma unroll
-      for (int T = 0; T < 8; ++T) kw[T] = __ldg(reinterpret_cast<const uint32_t*>(krow[T] + 4 * st));
+    for (int hs = 0; hs < 2; ++hs) {   // head dims 32 tq + 16 hs .. + 15: k16 steps 4 hs .. 4 hs + 3
+      uint4 kw[8];
 #pragma unroll
       for (int T = 0; T < 8; ++T) {
-        uint32_t b0, b1;
-        codes_to_f16(kw[T], a.dtype, b0, b1);
-        mma_f16(s[T], qh.x, qh.y, qh.z, qh.w, b0, b1);
-        mma_f16(s[T], ql.x, ql.y, ql.z, ql.w, b0, b1);
+        const int key = 16 * (g >> 1) + 4 * (T >> 1) + (g & 1) + 2 * (T & 1);
+        kw[T] = *reinterpret_cast<const uint4*>(stg.k + key * kD + 16 * ((2 * tq + hs) ^ swz_k(key)));
+      }
+#pragma unroll
+      for (int sub = 0; sub < 4; ++sub) {
+        const int st = 4 * hs + sub;
+        const uint4 qh = sm.qf[mt][0][st][lane], ql = sm.qf[mt][1][st][lane];
+#pragma unroll
+        for (int T = 0; T < 8; ++T) {
+          const uint32_t word = sub == 0 ? kw[T].x : sub == 1 ? kw[T].y : sub == 2 ? kw[T].z : kw[T].w;
+          uint32_t b0, b1;
+          codes_to_f16(word, a.dtype, b0, b1);
+          mma_f16(s[T], qh.x, qh.y, qh.z, qh.w, b0, b1);
+          mma_f16(s[T], ql.x, ql.y, ql.z, ql.w, b0, b1);
+        }
       }
     }
-    // ---- scale, mask, online softmax: this lane's keys are slots c0 + 16 tq + kk, kk = 4 j + 2 ab + {0, 1} ----
+    // ---- scale, mask, online softmax: this lane's keys are chunk slots 16 tq + kk, kk = 4 j + 2 ab + {0, 1} ----
     float ksc[16], vsc[16];
     int kpos[16];
-    {
-      const float4* k4 = reinterpret_cast<const float4*>(ks + c0 + 16 * tq);
-      const float4* v4 = reinterpret_cast<const float4*>(vs + c0 + 16 * tq);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 kq = __ldg(k4 + q), vq = __ldg(v4 + q);
-        ksc[4 * q] = kq.x; ksc[4 * q + 1] = kq.y; ksc[4 * q + 2] = kq.z; ksc[4 * q + 3] = kq.w;
-        vsc[4 * q] = vq.x; vsc[4 * q + 1] = vq.y; vsc[4 * q + 2] = vq.z; vsc[4 * q + 3] = vq.w;
-      }
+    for (int q = 0; q < 4; ++q) {
+      const float4 kq = *reinterpret_cast<const float4*>(stg.ks + 16 * tq + 4 * q);
+      const float4 vq = *reinterpret_cast<const float4*>(stg.vs + 16 * tq + 4 * q);
+      ksc[4 * q] = kq.x; ksc[4 * q + 1] = kq.y; ksc[4 * q + 2] = kq.z; ksc[4 * q + 3] = kq.w;
+      vsc[4 * q] = vq.x; vsc[4 * q + 1] = vq.y; vsc[4 * q + 2] = vq.z; vsc[4 * q + 3] = vq.w;
       if (a.ring) {
-        const int4* p4 = reinterpret_cast<const int4*>(a.ring_pos + c0 + 16 * tq);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int4 pq = __ldg(p4 + q);
-          kpos[4 * q] = pq.x; kpos[4 * q + 1] = pq.y; kpos[4 * q + 2] = pq.z; kpos[4 * q + 3] = pq.w;
-        }
+        const int4 pq = *reinterpret_cast<const int4*>(stg.pos + 16 * tq + 4 * q);
+        kpos[4 * q] = pq.x; kpos[4 * q + 1] = pq.y; kpos[4 * q + 2] = pq.z; kpos[4 * q + 3] = pq.w;
       } else {
 #pragma unroll
-        for (int kk = 0; kk < 16; ++kk) kpos[kk] = (int)c0 + 16 * tq + kk;
+        for (int r = 0; r < 4; ++r) kpos[4 * q + r] = (int)c0 + 16 * tq + 4 * q + r;
       }
     }
     float mx0 = -INFINITY, mx1 = -INFINITY;
@@ -324,10 +349,11 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
         pa[j][3] = pack_f16x2(p[2], p[3]);
       }
     }
-    // ---- O += P' V: V^T row d = 8 dt + g, lane tq reads slots c0 + 16 tq .. + 15 ----
+    // ---- O += P' V: V row d = 8 dt + g of the chunk, lane tq reads its slots 16 tq .. + 15 ----
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) {
-      const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vc + (int64_t)(8 * dt + g) * slots + c0 + 16 * tq));
+      const int d = 8 * dt + g;
+      const uint4 vv = *reinterpret_cast<const uint4*>(stg.v + d * 64 + 16 * (tq ^ ((d >> 1) & 3)));
       const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -394,10 +420,22 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     }
   };
 
-  if (active) {
-    for (int64_t c = cb + half; c < ce; c += 2) chunk(c * 64);
-    // this call's own keys: the last split, the first half
-    if (split == a.splits - 1 && half == 0) own_rows();
+  // the pair's chunks cb + pair, + 2, ... through its 2-slot ring; both warps of the pair finish a slot before its
+  // refill (a 64-thread named barrier per pair), the pair's first warp refills it
+  {
+    const int count = ce > cb + pair ? (int)((ce - cb - pair + 1) / 2) : 0;
+    for (int i = 0; i < count; ++i) {
+      const int j = i & 1;
+      mbar_wait_bounded(&sm.bar[pair][j], (uint32_t)((i >> 1) & 1), lane == 0 ? a.err : nullptr);
+      if (active) chunk(sm.stage[pair][j], (cb + pair + 2 * (int64_t)i) * 64);
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
+      if (lane == 0 && mt == 0 && i + 2 < count) {
+        fence_proxy_async_smem();
+        issue(pair, j, cb + pair + 2 * (int64_t)(i + 2));
+      }
+    }
+    // this call's own keys: the last split, the first pair
+    if (active && split == a.splits - 1 && pair == 0) own_rows();
   }
   // the row sums live spread over the 4 lanes of a row
   run_l0 += __shfl_xor_sync(0xffffffffu, run_l0, 1);

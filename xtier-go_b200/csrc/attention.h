@@ -8,6 +8,23 @@ namespace xtg {
 
 enum KvDtype { kKvInt8 = 0, kKvFp8 = 1 };
 
+// ---- the cache layout of one instance (slots a multiple of 64; codes 8-bit, scales f32 [kv_heads][slots]) ----
+// K: [kv_heads][slots][128], the 16-byte unit u of slot s's row stored at unit u ^ swz_k(s % 64);
+// V: [kv_heads][slots / 64][128][64] (a 64-slot chunk of a head is one contiguous 8 KB block, head dim d its row),
+//    the 16-byte unit u (slots 16 u .. 16 u + 15 of the chunk) of row d stored at unit u ^ ((d >> 1) & 3).
+// The XORs make the attention kernel's fragment reads from shared memory bank-conflict free; a chunk of K, V and
+// its scales are contiguous so that each arrives in one bulk copy.
+__host__ __device__ __forceinline__ int swz_k(int s64) { return (s64 ^ (s64 >> 3)) & 7; }
+
+__host__ __device__ __forceinline__ int64_t k_offset(int h, int64_t slot, int d, int64_t slots) {
+  return ((int64_t)h * slots + slot) * 128 + 16 * ((d >> 4) ^ swz_k((int)(slot & 63))) + (d & 15);
+}
+
+__host__ __device__ __forceinline__ int64_t v_offset(int h, int d, int64_t slot, int64_t slots) {
+  return (((int64_t)h * (slots / 64) + slot / 64) * 128 + d) * 64 + 16 * ((int)((slot & 63) >> 4) ^ ((d >> 1) & 3)) +
+         (slot & 15);
+}
+
 // The per-step values a replayable graph reads on the device.
 struct StepParams {
   int32_t tokens[8];
@@ -45,6 +62,7 @@ struct AttnArgs {
   int heads, kv_heads;
   int splits;
   float* part;              // [kv_heads][splits][32][130]
+  int* err;                 // set if a bounded wait gave up (never expected); may be null
   int pdl;
 };
 

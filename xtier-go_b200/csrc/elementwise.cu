@@ -265,9 +265,9 @@ __global__ void kv_store_kernel(const KvStoreArgs a) {
       c = (uint8_t)(int8_t)(int)q;
     }
     if (kv)
-      a.vc[((int64_t)h * 128 + idx[j]) * a.slots + slot] = c;
+      a.vc[v_offset(h, idx[j], slot, a.slots)] = c;
     else
-      a.kc[((int64_t)h * a.slots + slot) * 128 + idx[j]] = c;
+      a.kc[k_offset(h, slot, idx[j], a.slots)] = c;
   }
   if (lane == 0) (kv ? a.vs : a.ks)[(int64_t)h * a.slots + slot] = sc;
 }
@@ -283,8 +283,8 @@ __global__ void kv_prefill_kernel(uint64_t key_k, uint64_t key_v, uint64_t key_k
     const int64_t sh = i / 128;   // slot * kv_heads + head
     const int h = (int)(sh % kv_heads);
     const int64_t s = sh / kv_heads;
-    kc[((int64_t)h * slots + s) * 128 + e] = (uint8_t)(int8_t)((int)(rand_bits(key_k, i) % 255u) - 127);
-    vc[((int64_t)h * 128 + e) * slots + s] = (uint8_t)(int8_t)((int)(rand_bits(key_v, i) % 255u) - 127);
+    kc[k_offset(h, s, e, slots)] = (uint8_t)(int8_t)((int)(rand_bits(key_k, i) % 255u) - 127);
+    vc[v_offset(h, e, s, slots)] = (uint8_t)(int8_t)((int)(rand_bits(key_v, i) % 255u) - 127);
     if (e == 0) {
       ks[(int64_t)h * slots + s] = uniform_from_bits(rand_bits(key_ks, sh), lo, span);
       vs[(int64_t)h * slots + s] = uniform_from_bits(rand_bits(key_vs, sh), lo, span);

@@ -30,7 +30,6 @@ constexpr int kWarps = 8;
 constexpr int kStageBlocks = 4;                           // blocks per bulk copy
 constexpr int kStages = 3;                                // copies in flight per warp
 constexpr int kStageBytes = kStageBlocks * kBlockBytes;   // 2304
-constexpr uint32_t kMaxSpins = 1u << 24;                  // bound on every mbarrier wait
 
 struct GemvSmem {
   unsigned char ring[kWarps][kStages][kStageBytes];
@@ -39,44 +38,6 @@ struct GemvSmem {
   float rowscale[kMaxRows];
   float red[32][kMaxRows];
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_init_fence() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// global -> shared bulk copy completing on `bar` (16-byte aligned addresses, a multiple of 16 bytes)
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 
 __device__ __forceinline__ int64_t owner_of(int64_t u, int64_t units, int64_t total_warps) {
   return ((u + 1) * total_warps - 1) / units;
@@ -282,13 +243,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_const
     };
     for (int st = 0; st < nst; ++st) {
       const int slot = st % kStages;
-      uint32_t spins = 0;
-      while (!mbar_try_wait(&bars[slot], (parity >> slot) & 1u)) {
-        if (++spins > kMaxSpins) {   // never expected: report and stop instead of hanging
-          if (lane == 0 && a.err) atomicExch(a.err, 1);
-          break;
-        }
-      }
+      mbar_wait_bounded(&bars[slot], (parity >> slot) & 1u, lane == 0 ? a.err : nullptr);
       parity ^= 1u << slot;
       const unsigned char* buf = sm.ring[warp][slot] + lane * 16;
       const unsigned char* sbuf = sm.ring[warp][slot] + 512 + (lane >> 2) * 8;

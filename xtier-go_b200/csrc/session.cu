@@ -280,8 +280,9 @@ struct xtg_cuda {
     // K [kv_heads][slots][128]: rows of used * 128 bytes
     XTG_CUDA(cudaMemcpy2DAsync(dst.kc, dst.slots * 128, src.kc, src.slots * 128, used * 128, kv_heads,
                                cudaMemcpyDeviceToDevice, s));
-    // V [kv_heads * 128][slots]: rows of used bytes
-    XTG_CUDA(cudaMemcpy2DAsync(dst.vc, dst.slots, src.vc, src.slots, used, (size_t)kv_heads * 128,
+    // V [kv_heads][slots / 64][128][64]: the whole 64-slot chunks that hold the first `used` slots
+    const int64_t vbytes = (used + 63) / 64 * 64 * 128;
+    XTG_CUDA(cudaMemcpy2DAsync(dst.vc, dst.slots * 128, src.vc, src.slots * 128, vbytes, kv_heads,
                                cudaMemcpyDeviceToDevice, s));
     XTG_CUDA(cudaMemcpy2DAsync(dst.ks, dst.slots * 4, src.ks, src.slots * 4, used * 4, kv_heads,
                                cudaMemcpyDeviceToDevice, s));
@@ -467,7 +468,8 @@ struct xtg_cuda {
     gemv_partial = dalloc<float>((size_t)gemv_partial_floats(gemv_grid_));
     gemv_counters = dalloc<int>((size_t)packed_tiles(c.vocab, false) + 4096);
     dev_err = dalloc<int>(1);
-    splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, (num_sms + c.kv_heads - 1) / c.kv_heads);
+    // one CTA per SM: a global layer's splits fill the SMs once
+    splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, num_sms / c.kv_heads);
     splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, std::min<int>(c.ring / 64, 8));
     part = dalloc<float>((size_t)attention_part_floats(c.kv_heads, std::max(splits_g, splits_r)));
     ring_pos_dev = dalloc<int32_t>(c.ring);
@@ -601,6 +603,7 @@ struct xtg_cuda {
       at.kv_heads = c.kv_heads;
       at.splits = K.ring ? splits_r : splits_g;
       at.part = part;
+      at.err = dev_err;
       mark(kClsAttn, true);
       launch_attention(at, stream, pdl);
       mark(kClsAttn, false);
@@ -965,14 +968,14 @@ int64_t xtg_cuda_debug_cache(xtg_cuda* h, int instance, int value, void* out, in
     std::vector<uint8_t> tmp(bytes);
     XTG_CUDA(cudaMemcpy(tmp.data(), value == 0 ? k.kc : k.vc, bytes, cudaMemcpyDeviceToHost));
     uint8_t* o = static_cast<uint8_t*>(out);
-    // K: ours [h][slot][d] -> [h][d][slot]; V: ours [h][d][slot] -> [h][slot][d]
+    // this library's layouts (attention.h) -> K [h][d][slot], V [h][slot][d]
     for (int hh = 0; hh < kvh; ++hh)
       for (int64_t s = 0; s < k.slots; ++s)
         for (int d = 0; d < 128; ++d) {
           if (value == 0)
-            o[((int64_t)hh * 128 + d) * k.slots + s] = tmp[((int64_t)hh * k.slots + s) * 128 + d];
+            o[((int64_t)hh * 128 + d) * k.slots + s] = tmp[k_offset(hh, s, d, k.slots)];
           else
-            o[((int64_t)hh * k.slots + s) * 128 + d] = tmp[((int64_t)hh * 128 + d) * k.slots + s];
+            o[((int64_t)hh * k.slots + s) * 128 + d] = tmp[v_offset(hh, d, s, k.slots)];
         }
   } catch (const std::exception&) {
     return -1;
