@@ -211,6 +211,7 @@ struct xtg_cuda {
   float* gemv_partial = nullptr;
   int* gemv_counters = nullptr;
   int* dev_err = nullptr;   // bounded device waits that gave up (never expected)
+  int* err_host = nullptr;  // pinned copy of dev_err
   int gemv_grid_ = 0;
   int splits_g = 1, splits_r = 1;
   int proj_ld = 0;
@@ -237,6 +238,7 @@ struct xtg_cuda {
     for (void* p : allocs) cudaFree(p);
     if (params_host) cudaFreeHost(params_host);
     if (logits_host) cudaFreeHost(logits_host);
+    if (err_host) cudaFreeHost(err_host);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -468,6 +470,8 @@ struct xtg_cuda {
     gemv_partial = dalloc<float>((size_t)gemv_partial_floats(gemv_grid_));
     gemv_counters = dalloc<int>((size_t)packed_tiles(c.vocab, false) + 4096);
     dev_err = dalloc<int>(1);
+    XTG_CUDA(cudaMallocHost(&err_host, sizeof(int)));
+    *err_host = 0;
     // one CTA per SM: a global layer's splits fill the SMs once
     splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, num_sms / c.kv_heads);
     splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, std::min<int>(c.ring / 64, 8));
@@ -715,7 +719,13 @@ struct xtg_cuda {
       if (r0 < m && fn)
         XTG_CUDA(cudaMemcpyAsync(logits_host + (size_t)r0 * c.vocab, logits + (size_t)r0 * c.vocab,
                                  (size_t)(m - r0) * c.vocab * sizeof(float), cudaMemcpyDeviceToHost, stream));
+      XTG_CUDA(cudaMemcpyAsync(err_host, dev_err, sizeof(int), cudaMemcpyDeviceToHost, stream));
       XTG_CUDA(cudaStreamSynchronize(stream));
+      if (*err_host) {   // a bounded device wait gave up: the step's results are not to be trusted
+        *err_host = 0;
+        XTG_CUDA(cudaMemsetAsync(dev_err, 0, sizeof(int), stream));
+        throw CudaError("a device wait timed out during the step (results discarded)");
+      }
       commit(m);
       last_rows = m;
       if (fn)
@@ -1068,6 +1078,12 @@ int xtg_cuda_bench(xtg_cuda* h, const int32_t* tokens, int m, int steps, int pro
         if (out_class_ms) out_class_ms[c] = cms[c] / steps;
         if (out_class_launches) out_class_launches[c] = cl[c] / steps;
       }
+    }
+    XTG_CUDA(cudaMemcpy(h->err_host, h->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (*h->err_host) {
+      *h->err_host = 0;
+      XTG_CUDA(cudaMemset(h->dev_err, 0, sizeof(int)));
+      throw CudaError("a device wait timed out during the timed steps");
     }
     // the steps wrote positions n_past .. n_past + m - 1 into the rings: the state of a forward rewound to n_past
     for (int r = 0; r < m; ++r) h->ring_pos[(h->n_past + r) % h->c.ring] = h->n_past + r;
