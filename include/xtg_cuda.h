@@ -143,6 +143,17 @@ typedef struct {
 } xtg_cuda_attn_args;
 XTG_CUDA_API int xtg_cuda_attention(const xtg_cuda_attn_args* a, int splits, void* stream, char* err, int err_len);
 
+// No counterpart in the reference. xtg_cuda_attention for callers that cannot call cudaMalloc: a host runtime that
+// reserved the GPU's memory for its own arena at start-up, or a path on which an allocation may not block or
+// synchronise the device. The same kernels and results; the split-KV partials live in a fixed 4,259,840-byte array
+// of this library, so kv_heads x splits must be at most 256 (larger requests fail with an error). It allocates
+// nothing, enqueues both kernels on `stream` and returns without waiting. The array is held on every GPU that loads
+// the library until the process exits; the first call on a device looks up its address there (make that call
+// before any stream capture). Every call shares the array and it keeps the last call's contents: calls that
+// overlap on the GPU (on different streams, or from several threads at once) race and corrupt each other's results.
+XTG_CUDA_API int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* a, int splits, void* stream, char* err,
+                                            int err_len);
+
 // KvCache::store (engine/src/kv.cpp:75-112) into the layout above: rows k, v [n][kv_heads][128] (device f32) at positions
 // pos .. pos + n - 1; a ring keeps the last `slots`. int8: scale amax / 127; FP8: amax / 448 (the reference's rule).
 XTG_CUDA_API int xtg_cuda_kv_store(const float* k, const float* v, int64_t pos, int n, int kv_heads, int64_t slots, int ring,

@@ -95,6 +95,8 @@ def lib():
                                               C.c_void_p, E, C.c_int]
         L.xtg_cuda_attention.restype = C.c_int
         L.xtg_cuda_attention.argtypes = [C.POINTER(AttnArgs), C.c_int, C.c_void_p, E, C.c_int]
+        L.xtg_cuda_attention_noalloc.restype = C.c_int
+        L.xtg_cuda_attention_noalloc.argtypes = [C.POINTER(AttnArgs), C.c_int, C.c_void_p, E, C.c_int]
         L.xtg_cuda_kv_store.restype = C.c_int
         L.xtg_cuda_kv_store.argtypes = [C.c_void_p, C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_int64, C.c_int,
                                         C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, E,
@@ -343,6 +345,24 @@ def attention(q, k, v, k_codes, v_codes, k_scales, v_scales, pos0, window, scale
                  ring_pos.data_ptr() if ring_pos is not None else None, dtype, out.data_ptr())
     err = _err()
     _check(lib().xtg_cuda_attention(C.byref(a), splits, _stream(), err, len(err)), err)
+    return out
+
+
+def attention_noalloc(q, k, v, k_codes, v_codes, k_scales, v_scales, pos0, window, scale, ring_pos=None, dtype=0,
+                      splits=4, out=None):
+    """xtg_cuda_attention_noalloc: attention() with the split partials in the library's fixed scratch (nothing
+    allocated by the library; kv_heads x splits <= 256). Enqueued on the current stream, not waited for."""
+    import torch
+    n_q, heads, d = q.shape
+    kvh = k.shape[1]
+    if out is None:
+        out = torch.empty_like(q)
+    a = AttnArgs(n_q, pos0, heads, kvh, d, window, scale, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                 k_codes.data_ptr(), v_codes.data_ptr(), k_scales.data_ptr(), v_scales.data_ptr(),
+                 k_scales.shape[1], 1 if ring_pos is not None else 0,
+                 ring_pos.data_ptr() if ring_pos is not None else None, dtype, out.data_ptr())
+    err = _err()
+    _check(lib().xtg_cuda_attention_noalloc(C.byref(a), splits, _stream(), err, len(err)), err)
     return out
 
 

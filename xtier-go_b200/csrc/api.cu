@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -195,6 +196,93 @@ int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, ch
       throw;
     }
     cudaFree(part);
+  });
+}
+
+}  // extern "C"
+
+// ---- attention without allocation ----
+// Some callers cannot call cudaMalloc: a host runtime that reserved the GPU's memory for its own arena at start-up
+// (a fresh allocation then fails, or fragments that arena), and code on a path where an allocation may not block
+// or synchronise the device. xtg_cuda_attention allocates its split-KV partials per call; for those callers
+// xtg_cuda_attention_noalloc keeps them in the fixed array below instead: 4,259,840 bytes, room for 256 KV-head x
+// split pairs (32 query rows x 130 floats each). Every GPU that loads this library holds the array until the process
+// exits. All calls share it, and it keeps the last call's contents.
+namespace {
+constexpr int kNoAllocPairs = 256;
+constexpr int64_t kNoAllocFloats = (int64_t)kNoAllocPairs * 32 * 130;
+}  // namespace
+
+// In host code this name is only a host-side stand-in for the array; its device address comes from
+// cudaGetSymbolAddress, once per device.
+__device__ __align__(256) float g_noalloc_attn_part[kNoAllocFloats];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// The array's device address on the current device; the first call on a device looks it up with that device current.
+float* noalloc_scratch() {
+  int device = 0;
+  XTG_CUDA(cudaGetDevice(&device));
+  XTG_REQUIRE(device >= 0 && device < kNoAllocMaxDevices, "attention_noalloc: device index above 63");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[device]) {
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_attn_part);
+    if (e != cudaSuccess)
+      throw CudaError(std::string("attention_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    g_noalloc_ptr[device] = static_cast<float*>(ptr);
+  }
+  return g_noalloc_ptr[device];
+}
+}  // namespace
+
+extern "C" {
+
+int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* p, int splits, void* stream, char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_REQUIRE(p->head_dim == 128, "attention: head_dim 128");
+    XTG_REQUIRE(p->n_q >= 1 && p->n_q <= kMaxRows, "attention: 1..8 query rows");
+    XTG_REQUIRE(splits >= 1, "attention: at least one split");
+    XTG_REQUIRE(p->ring == 0 || p->ring_pos != nullptr, "attention: a ring needs its slot -> position table");
+    XTG_REQUIRE(p->ring != 0 || p->pos0 <= p->slots, "attention: pos0 beyond the cache");
+    XTG_REQUIRE(p->kv_heads >= 1 && attention_part_floats(p->kv_heads, splits) <= kNoAllocFloats,
+                "attention_noalloc: kv_heads x splits above 256, the fixed scratch's limit (4,259,840 bytes)");
+    float* part = noalloc_scratch();
+    // every split writes the partial of every live query row that the combine reads: nothing needs clearing
+    AttnArgs a = {};
+    a.q = p->q;
+    a.k = p->k;
+    a.v = p->v;
+    a.kc = const_cast<uint8_t*>(p->k_codes);
+    a.vc = const_cast<uint8_t*>(p->v_codes);
+    a.ks = const_cast<float*>(p->k_scales);
+    a.vs = const_cast<float*>(p->v_scales);
+    a.slots = p->slots;
+    a.ring = p->ring;
+    a.ring_pos = p->ring_pos;
+    a.dtype = p->dtype;
+    a.window = p->window;
+    a.scale = p->scale;
+    a.m = p->n_q;
+    a.pos0 = p->pos0;
+    a.heads = p->heads;
+    a.kv_heads = p->kv_heads;
+    a.splits = splits;
+    a.part = part;
+    a.err = nullptr;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    launch_attention(a, s, false);
+    CombineArgs cb = {};
+    cb.part = part;
+    cb.splits = splits;
+    cb.heads = p->heads;
+    cb.kv_heads = p->kv_heads;
+    cb.m = p->n_q;
+    cb.out = p->out;
+    launch_attn_combine(cb, s, false);
   });
 }
 
