@@ -11,31 +11,29 @@
 #include "attention.h"
 #include "common.cuh"
 #include "elementwise.h"
+#include "fp4mma.cuh"
 #include "kernels.h"
 
 using namespace xtg;
 
 struct xtg_cuda_linear {
   int device = 0;
-  int k = 0, nw = 0, tiles = 0, blocks = 0, grid = 0;
+  int k = 0, nw = 0, tiles = 0, kblocks = 0;
   std::vector<int> n_out, tile0;
   std::vector<float> globals;
   uint8_t* w = nullptr;
   TileOut* outs = nullptr;          // device, rewritten per call (the ys pointers)
   std::vector<TileOut> outs_host;
-  uint32_t* x16 = nullptr;
-  float* partial = nullptr;
-  int* counters = nullptr;
-  int* m_dev = nullptr;
+  uint8_t* xb = nullptr;            // the input's B digits
+  float* xb_pre = nullptr;
+  GemvPlan plan;
   int64_t bytes = 0;
 
   ~xtg_cuda_linear() {
     cudaFree(w);
     cudaFree(outs);
-    cudaFree(x16);
-    cudaFree(partial);
-    cudaFree(counters);
-    cudaFree(m_dev);
+    cudaFree(xb);
+    cudaFree(xb_pre);
   }
 };
 
@@ -71,7 +69,7 @@ xtg_cuda_linear* xtg_cuda_linear_new(int nw, const uint8_t* const* codes, const 
     XTG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, L->device));
     L->k = k;
     L->nw = nw;
-    L->blocks = packed_blocks(k);
+    L->kblocks = packed_kblocks(k);
     for (int i = 0; i < nw; ++i) {
       XTG_REQUIRE(n_out[i] > 0, "linear: n_out must be positive");
       L->n_out.push_back(n_out[i]);
@@ -79,19 +77,21 @@ xtg_cuda_linear* xtg_cuda_linear_new(int nw, const uint8_t* const* codes, const 
       L->tile0.push_back(L->tiles);
       L->tiles += packed_tiles(n_out[i], false);
     }
-    L->bytes = (int64_t)L->tiles * L->blocks * kBlockBytes;
+    L->bytes = (int64_t)L->tiles * L->kblocks * kPackUnitBytes;
     XTG_CUDA(cudaMalloc(&L->w, L->bytes));
     for (int i = 0; i < nw; ++i)
       pack_nvfp4(codes[i], scales[i], nullptr, nullptr, n_out[i], k, false,
-                 L->w + (int64_t)L->tile0[i] * L->blocks * kBlockBytes, nullptr);
+                 L->w + (int64_t)L->tile0[i] * L->kblocks * kPackUnitBytes, nullptr);
     XTG_CUDA(cudaMalloc(&L->outs, sizeof(TileOut) * L->tiles));
     L->outs_host.resize(L->tiles);
-    XTG_CUDA(cudaMalloc(&L->x16, (size_t)L->blocks * 4 * 64 * sizeof(uint32_t)));
-    L->grid = gemv_grid(sms);
-    XTG_CUDA(cudaMalloc(&L->partial, gemv_partial_floats(L->grid) * sizeof(float)));
-    XTG_CUDA(cudaMalloc(&L->counters, sizeof(int) * L->tiles));
-    XTG_CUDA(cudaMemset(L->counters, 0, sizeof(int) * L->tiles));
-    XTG_CUDA(cudaMalloc(&L->m_dev, sizeof(int)));
+    L->plan = plan_gemv(L->tiles, L->kblocks, sms, 8, 1 << 20);
+    XTG_CUDA(cudaMalloc(&L->xb, (size_t)digit_bytes(k)));
+    XTG_CUDA(cudaMalloc(&L->xb_pre, (size_t)packed_kblocks(k) * 4 * kMaxRows * sizeof(float)));
+    XTG_CUDA(cudaMemset(L->xb, 0, (size_t)digit_bytes(k)));
+    {
+      const std::vector<float> ones((size_t)packed_kblocks(k) * 4 * kMaxRows, kEmptyPrescale);
+      XTG_CUDA(cudaMemcpy(L->xb_pre, ones.data(), ones.size() * sizeof(float), cudaMemcpyHostToDevice));
+    }
     XTG_CUDA(cudaDeviceSynchronize());
   } catch (const std::exception& e) {
     set_err(err, err_len, e.what());
@@ -108,21 +108,21 @@ int xtg_cuda_linear_forward(xtg_cuda_linear* L, const float* x, int m, float* co
     for (int i = 0; i < L->nw; ++i) {
       const int t0 = L->tile0[i], nt = packed_tiles(L->n_out[i], false);
       for (int t = 0; t < nt; ++t)
-        L->outs_host[t0 + t] = TileOut{ys[i] + 16 * t, L->n_out[i], std::min(16, L->n_out[i] - 16 * t), L->globals[i], 0};
+        L->outs_host[t0 + t] = TileOut{ys[i] + 128 * t, L->n_out[i], std::min(128, L->n_out[i] - 128 * t),
+                                       L->globals[i], L->globals[i]};
     }
     XTG_CUDA(cudaMemcpyAsync(L->outs, L->outs_host.data(), sizeof(TileOut) * L->tiles, cudaMemcpyHostToDevice, s));
-    pack_activations(x, m, L->k, L->x16, s);
+    digitize_rows(x, m, L->k, L->xb, L->xb_pre, s);
     GemvArgs a = {};
     a.w = L->w;
     a.tiles = L->tiles;
-    a.blocks = L->blocks;
-    a.x16 = L->x16;
+    a.kblocks = L->kblocks;
+    a.xb = L->xb;
+    a.xb_pre = L->xb_pre;
     a.m = m;
-    a.partial = L->partial;
-    a.counters = L->counters;
     a.err = nullptr;
     a.outs = L->outs;
-    launch_gemv(kEpiStore, a, L->grid, s, false);
+    launch_gemv(kEpiStore, a, L->plan, s, false);
     // outs_host is read by the copy above before this call returns to the caller's next forward
     XTG_CUDA(cudaStreamSynchronize(s));
   });

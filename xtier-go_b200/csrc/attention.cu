@@ -20,6 +20,7 @@
 // (lane tq owns slots 16 tq .. 16 tq + 15 in both products).
 #include "attention.h"
 #include "common.cuh"
+#include "fp4mma.cuh"
 
 namespace xtg {
 
@@ -549,9 +550,20 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   const int col = h * kD + d;
   const float gt = a.gate[(int64_t)i * a.gate_ld + col];
   o *= 1.f / (1.f + expf(-gt * a.gscale[col]));
-  a.a16[frag_offset_halves(col, i)] = __half_as_ushort(__float2half_rn(o));
   const float ss = block_sum(o * o, red);
   if (d == 0) a.asum[h * kMaxRows + i] = ss;
+  // the O projection's input: this head's 8 groups of 16 as B digits (warp 0, a quad per group)
+  __shared__ float ov[kD];
+  ov[d] = o;
+  __syncthreads();
+  if (d < 32) {
+    const int gl = d >> 2, t = d & 3, G = h * (kD / 16) + gl;
+    const float v[4] = {ov[16 * gl + 4 * t], ov[16 * gl + 4 * t + 1], ov[16 * gl + 4 * t + 2], ov[16 * gl + 4 * t + 3]};
+    uint32_t code[kDigits], sf[kDigits];
+    const float p = digitize16_quad(v, code, sf);
+    store_digits_quad(a.ab + (int64_t)(G >> 2) * kBBlockBytes, i, G & 3, t, code, sf);
+    if (t == 0) a.ab_pre[(int64_t)G * 8 + i] = p;
+  }
 }
 
 }  // namespace

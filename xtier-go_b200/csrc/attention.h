@@ -75,7 +75,8 @@ struct CombineArgs {
   const float* gate;        // step: g rows [m][gate_ld] (the projection's g columns)
   int gate_ld;
   const float* gscale;      // [heads * 128]
-  uint16_t* a16;            // step: fp16 fragments of the gated output (K = heads * 128)
+  uint8_t* ab;              // step: the gated output as B digits (the O projection's input, K = heads * 128)
+  float* ab_pre;            // [heads * 8][8] their prescales
   float* asum;              // step: [heads][8] sum of squares per head and activation row
   int pdl;
 };

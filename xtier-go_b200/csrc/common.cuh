@@ -159,16 +159,11 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   return r;
 }
 
-// The four bytes of a word (8 E2M1 codes) -> four f16x2 (byte i -> out[i], low nibble in the low half); exact.
-__device__ __forceinline__ void e2m1x8_to_f16x2x4(uint32_t q, uint32_t (&out)[4]) {
-  asm("{ .reg .b8 b0, b1, b2, b3;\n"
-      "mov.b32 {b0, b1, b2, b3}, %4;\n"
-      "cvt.rn.f16x2.e2m1x2 %0, b0;\n"
-      "cvt.rn.f16x2.e2m1x2 %1, b1;\n"
-      "cvt.rn.f16x2.e2m1x2 %2, b2;\n"
-      "cvt.rn.f16x2.e2m1x2 %3, b3; }"
-      : "=r"(out[0]), "=r"(out[1]), "=r"(out[2]), "=r"(out[3])
-      : "r"(q));
+// Two floats -> a byte of two E2M1 codes (lo in the low nibble), nearest, saturating to +-6.
+__device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{ .reg .b8 t; cvt.rn.satfinite.e2m1x2.f32 t, %2, %1; cvt.u32.u8 %0, t; }" : "=r"(r) : "f"(lo), "f"(hi));
+  return r;
 }
 
 // Two E4M3 bytes (low, high of a 16-bit value) -> f16x2; exact.
@@ -263,15 +258,6 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-// ---- the activation operand of the NVFP4 GEMV: fp16 in the B-fragment order of mma.m16n8k16 ----
-// Two consecutive k16 steps of a lane are 16 contiguous bytes (one 128-bit load per pair of steps). Element (k, n) of
-// x^T (k < K, activation row n < 8) is half number
-//   ((s / 2) * 32 + lane) * 8 + (s & 1) * 4 + reg * 2 + (k & 1),  s = k / 16, w = k % 16, reg = w >= 8,
-//   lane = n * 4 + (w & 7) / 2
-__host__ __device__ __forceinline__ uint32_t frag_offset_halves(int k, int n) {
-  const int s = k >> 4, w = k & 15, reg = w >> 3, tq = (w & 7) >> 1;
-  return (uint32_t)((((s >> 1) * 32 + n * 4 + tq) * 8) + (s & 1) * 4 + reg * 2 + (k & 1));
-}
 
 constexpr int kMaxRows = 8;   // activation rows of a verify step (mma N = 8)
 

@@ -6,24 +6,48 @@
 #include "attention.h"
 #include "common.cuh"
 #include "elementwise.h"
+#include "fp4mma.cuh"
 #include "kernels.h"
 
 namespace xtg {
 
 namespace {
 
-__device__ __forceinline__ float packed_weight(const uint8_t* w, int blocks, float global, int row, int k) {
-  const int t = row >> 4, rr = row & 15, g = rr & 7, hi = rr >> 3;
-  const int b = k >> 6, j = (k >> 4) & 3, w16 = k & 15, q = w16 >> 1, nib = w16 & 1;
-  const int tq = q & 3, part = hi + ((q >> 2) << 1);
-  const uint8_t* blk = w + ((int64_t)t * blocks + b) * kBlockBytes;
-  const uint8_t byte = blk[(g * 4 + tq) * 16 + 4 * j + part];
-  const uint8_t sc = blk[512 + g * 8 + 2 * j + hi];
+__device__ __forceinline__ float packed_weight(const uint8_t* w, int kblocks, float global, int row, int k) {
+  const int t = row / kTileRows, r = row % kTileRows, b = k / kKBlock, kk = k % kKBlock;
+  const uint8_t* unit = w + ((int64_t)t * kblocks + b) * kUnitBytes;
+  const uint8_t byte = unit[a_code_offset(r, kk & ~1)];
+  const uint8_t sc = unit[kUnitCodeBytes + sf_offset(r, kk >> 4)];
   const float s = __fmul_rn(e4m3_to_f32(sc), global);
-  return __fmul_rn(e2m1_to_f32(nib ? byte >> 4 : byte & 15), s);
+  return __fmul_rn(e2m1_to_f32((kk & 1) ? byte >> 4 : byte & 15), s);
+}
+
+// Activation row i (hidden values in shared memory) -> its B digits in xb and the prescale of every 16-input group
+// in xb_pre (zero digits for zero rows); every thread of the CTA takes part (a quad per group). The other rows' bytes
+// of xb are left alone.
+__device__ __forceinline__ void digitize_row(const float* row, int hidden, int i, bool zero, uint8_t* xb,
+                                             float* xb_pre, float fixed) {
+  const int groups = (hidden + 15) / 16;
+  for (int q0 = 0; q0 < groups * 4; q0 += blockDim.x) {
+    const int q = q0 + (int)threadIdx.x, g = q >> 2, t = q & 3;
+    const bool active = g < groups;
+    float v[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int k = 16 * g + 4 * t + c;
+      v[c] = (active && !zero && k < hidden) ? row[k] : 0.f;
+    }
+    uint32_t code[kDigits], sf[kDigits];
+    const float p = digitize16_quad(v, code, sf, fixed);   // whole warps take part
+    if (active) {
+      store_digits_quad(xb + (int64_t)(g >> 2) * kBBlockBytes, i, g & 3, t, code, sf);
+      if (t == 0) xb_pre[(int64_t)g * 8 + i] = p;
+    }
+  }
 }
 
 __global__ void embed_kernel(const EmbedArgs a) {
+  extern __shared__ float rowbuf[];   // [hidden]
   const int r = blockIdx.x;
   if (a.pdl) {
     pdl_launch_next();
@@ -34,16 +58,14 @@ __global__ void embed_kernel(const EmbedArgs a) {
   const int64_t pos0 = p->pos0;
   if (r < m) {
     const int tok = p->tokens[r];
-    for (int k2 = threadIdx.x * 2; k2 < a.hidden; k2 += blockDim.x * 2) {
-      const float v0 = packed_weight(a.head, a.blocks, a.global, tok, k2);
-      const float v1 = packed_weight(a.head, a.blocks, a.global, tok, k2 + 1);
-      a.h[(int64_t)r * a.hidden + k2] = v0;
-      a.h[(int64_t)r * a.hidden + k2 + 1] = v1;
-      a.x16[frag_offset_halves(k2, r) >> 1] = pack_f16x2(v0, v1);
+    for (int k = threadIdx.x; k < a.hidden; k += blockDim.x) {
+      const float v = packed_weight(a.head, a.kblocks, a.global, tok, k);
+      a.h[(int64_t)r * a.hidden + k] = v;
+      rowbuf[k] = v;
     }
-  } else {
-    for (int k2 = threadIdx.x * 2; k2 < a.hidden; k2 += blockDim.x * 2) a.x16[frag_offset_halves(k2, r) >> 1] = 0u;
   }
+  __syncthreads();
+  digitize_row(rowbuf, a.hidden, r, r >= m, a.xb, a.xb_pre, 0.f);
   // RoPE tables of this step's positions (FP32(pos) * inv_freq, then cos / sin), one per theta
   if (r < a.n_thetas) {
     for (int idx = threadIdx.x; idx < kMaxRows * 64; idx += blockDim.x) {
@@ -61,6 +83,9 @@ __global__ void embed_kernel(const EmbedArgs a) {
     a.ring_pos[q % a.ring] = (int32_t)q;
   }
 }
+
+// the residual stream is unit-norm after every update (|h| <= 1): one prescale for all its groups (2^11)
+constexpr float kUnitNorm = 2048.f;
 
 // Block-wide sums of two values at once (fixed order, deterministic).
 __device__ __forceinline__ float2 block_sum2(float x, float y, float2* red) {
@@ -83,6 +108,7 @@ constexpr int kPer = 8;   // hidden <= 8192
 
 __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a) {
   __shared__ float2 red[32];
+  extern __shared__ float rowbuf[];   // [hidden]
   const int r = blockIdx.x, H = a.hidden;
   if (a.pdl) {
     pdl_launch_next();
@@ -90,9 +116,8 @@ __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a)
   }
   const int m = a.params ? a.params->m : a.m;
   float* h = a.h + (int64_t)r * H;
-  uint16_t* x16h = reinterpret_cast<uint16_t*>(a.x16);
   if (r >= m) {
-    for (int k = threadIdx.x; k < H; k += blockDim.x) x16h[frag_offset_halves(k, r)] = 0;
+    digitize_row(rowbuf, H, r, true, a.xb, a.xb_pre, kUnitNorm);
     return;
   }
   float v[kPer];
@@ -176,9 +201,11 @@ __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a)
     const int k = threadIdx.x + j * kResidThreads;
     if (k < H) {
       h[k] = v[j];
-      x16h[frag_offset_halves(k, r)] = __half_as_ushort(__float2half_rn(v[j]));
+      rowbuf[k] = v[j];
     }
   }
+  __syncthreads();
+  digitize_row(rowbuf, H, r, false, a.xb, a.xb_pre, kUnitNorm);
 }
 
 __global__ void argmax_kernel(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out,
@@ -293,10 +320,12 @@ __global__ void kv_prefill_kernel(uint64_t key_k, uint64_t key_v, uint64_t key_k
 }
 
 template <class Args>
-void launch_pdl(void (*kernel)(Args), dim3 grid, dim3 block, const Args& args, cudaStream_t s, bool pdl) {
+void launch_pdl(void (*kernel)(Args), dim3 grid, dim3 block, const Args& args, cudaStream_t s, bool pdl,
+                size_t smem = 0) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -311,14 +340,15 @@ void launch_pdl(void (*kernel)(Args), dim3 grid, dim3 block, const Args& args, c
 void launch_embed(const EmbedArgs& a_in, cudaStream_t s, bool pdl) {
   EmbedArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
-  launch_pdl(embed_kernel, dim3(kMaxRows), dim3(256), a, s, pdl);
+  XTG_REQUIRE(a.hidden <= 8192, "embed: hidden above 8192");
+  launch_pdl(embed_kernel, dim3(kMaxRows), dim3(256), a, s, pdl, (size_t)a.hidden * sizeof(float));
 }
 
 void launch_resid(const ResidArgs& a_in, cudaStream_t s, bool pdl) {
   ResidArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
   XTG_REQUIRE(a.hidden <= kPer * kResidThreads, "resid: hidden above 8192");
-  launch_pdl(resid_kernel, dim3(kMaxRows), dim3(kResidThreads), a, s, pdl);
+  launch_pdl(resid_kernel, dim3(kMaxRows), dim3(kResidThreads), a, s, pdl, (size_t)a.hidden * sizeof(float));
 }
 
 void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out, float* out_val,

@@ -11,12 +11,13 @@ namespace xtg {
 
 struct EmbedArgs {
   const StepParams* params;
-  const uint8_t* head;      // the tied NVFP4 head in the streaming layout
-  int blocks;               // 64-input blocks per row tile
+  const uint8_t* head;      // the tied NVFP4 head in tensor-core units
+  int kblocks;              // 64-input blocks per row tile
   float global;
   int hidden;
   float* h;                 // [8][hidden]
-  uint32_t* x16;            // fragments of h
+  uint8_t* xb;              // B digits of h
+  float* xb_pre;            // [hidden / 16][8] their prescales
   const float* inv_freq;    // [n_thetas][64]
   int n_thetas;
   float* rope_cos;          // [n_thetas][8][64]
@@ -38,7 +39,8 @@ struct ResidArgs {
   const float* lr;          // slerp: [hidden]
   float* state;             // loops: [8][hidden]
   float* input;
-  uint32_t* x16;            // fragments of the new h
+  uint8_t* xb;              // B digits of the new h
+  float* xb_pre;            // [hidden / 16][8] their prescales
   int pdl;
 };
 

@@ -1,382 +1,517 @@
-// K1: NVFP4 weight x fp16 activation GEMV for the 1..8-row decode / verify step (the hot loop of
-// engine/src/kernels.cpp:84-138 matmul_nvfp4, m <= 8).
+// K1: NVFP4 weight x activation GEMV for the 1..8-row decode / verify step (matmul_nvfp4's hot loop,
+// engine/src/kernels.cpp:84-138, m <= 8) on the block-scaled FP4 tensor cores of sm_100a.
 //
-// Why tensor cores at m = 8: streaming NVFP4 at HBM speed is ~23 weight bytes per clock per SM, and each code byte
-// holds 2 weights used by 8 rows: 32 FMAs per byte, ~340 FP32 FMAs per clock per SM against the 128 the CUDA cores
-// issue. So every E2M1 code pair is converted to f16x2 (cvt.rn.f16x2.e2m1x2) and multiplied by its E4M3 block
-// scale (cvt.rn.f16x2.e4m3x2, hmul2) -- e2m1 x e4m3 has at most 6 significant bits and lies in [2^-10, 2688], so
-// this product is EXACT in fp16 -- and fed to mma.m16n8k16 (f32 accumulation) as the A operand, 16 weight rows x 16
-// inputs; the activations (<= 8 rows, zero padded) are the B operand. The per-tensor global scale is applied in
-// the epilogue. Compared with the reference's order (per-16 group sum in FP32, times the scale) only the FP32
-// rounding of the sums differs, and the activations are rounded once to fp16.
+// Why tensor cores, and why this form: at 8 rows the weights are read once and used 8 times, far below any
+// tensor-core ridge, so the kernel must stream NVFP4 at HBM speed. Converting the E2M1 codes and E4M3 scales on the
+// CUDA cores costs ~95 instructions per 576 weight bytes, which alone fills the SM's issue slots at HBM rate.
+// tcgen05.mma kind::mxf4nvf4 takes the codes and the per-16 E4M3 scales as they are stored, so the weights go from
+// HBM to shared memory (bulk copies) to the tensor core untouched. The activations become the FP4 B operand as
+// 6 scaled E2M1 digits per value (fp4mma.cuh): N = 48 digit rows, the epilogue adds each row's 6 digit columns.
+// One MMA is 128 weight rows x 64 inputs; its accumulator lives in TMEM.
 //
-// Work split: the weight is a stream of 576-byte blocks (weights.cu). Every warp of the grid takes an equal
-// contiguous run of blocks (split-K inside a tile when a run starts or ends mid-tile), so the warps of a CTA cover
-// one contiguous run and the grid covers the weight exactly once. Each warp streams its run through its own ring
-// of shared-memory stages with bulk copies (cp.async.bulk global -> shared, completion on an mbarrier; no
-// multicast); the first stages are issued before griddepcontrol.wait, since the weights do not depend on the
-// previous kernel, and the kernel lets its dependent launch at once, so the next kernel's copies start while this
-// one finishes. A tile split between warps of one CTA is summed in shared memory in warp order; a tile split
-// between CTAs goes through a global scratch slot per CTA, and the CTA whose atomic increment completes the tile
-// sums the CTA parts in CTA order. Every sum has a fixed order, so results are the same every launch.
+// Work split: tiles of 128 rows. A GEMV with fewer tiles than CTA slots splits each tile's K blocks over a cluster
+// of `split` CTAs, whose partial sums meet in distributed shared memory (summed in cluster-rank order, no atomics);
+// otherwise each CTA takes whole tiles. In every CTA one thread streams weight units through a ring of shared-memory
+// stages (cp.async.bulk, completion on mbarriers; the first stages are issued before griddepcontrol.wait, since the
+// weights do not depend on the previous kernel), one thread issues the MMAs, and four warps drain the TMEM
+// accumulator (double-buffered across tiles) into the epilogue: a plain store (with an optional justnorm row scale),
+// SwiGLU, or the lm_head with its per-tile argmax candidates. Every sum has a fixed order: results are the same on
+// every launch.
+#include <algorithm>
+
 #include "common.cuh"
+#include "fp4mma.cuh"
 #include "kernels.h"
 
 namespace xtg {
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kStageBlocks = 4;                           // blocks per bulk copy
-constexpr int kStages = 3;                                // copies in flight per warp
-constexpr int kStageBytes = kStageBlocks * kBlockBytes;   // 2304
+constexpr int kThreads = 256;
+constexpr int kStageUnits = 4;
+constexpr int kMaxRing = 6;
+constexpr int kAccCols = 64;   // TMEM columns per accumulator (48 used)
 
-struct GemvSmem {
-  unsigned char ring[kWarps][kStages][kStageBytes];
-  uint64_t bar[kWarps][kStages];
-  float4 part[kWarps][2][32];   // split-tile parts of each warp: [0] its first tile, [1] its last
-  float rowscale[kMaxRows];
-  float red[32][kMaxRows];
+struct Params {
+  GemvArgs a;
+  int split, tpc, ring, slice_max, rpr;
+  uint32_t tmem_cols;
+  uint32_t off_b, off_pre, off_red, off_vsq, off_cand, off_bar, off_misc;
 };
 
-__device__ __forceinline__ int64_t owner_of(int64_t u, int64_t units, int64_t total_warps) {
-  return ((u + 1) * total_warps - 1) / units;
-}
+struct SmemPlan {
+  uint32_t off_b, off_pre, off_red, off_vsq, off_cand, off_bar, off_misc, total;
+  int rpr;   // partial-row slots per source CTA in the cluster reduction
+};
 
-template <int EPI>
-__device__ __forceinline__ void epilogue(const GemvArgs& a, int t, const float (&acc)[4], int m, const float* rowscale,
-                                         int lane) {
-  const int g = lane >> 2, tq = lane & 3;
-  const int n0 = 2 * tq, n1 = 2 * tq + 1;
-  if constexpr (EPI == kEpiStore) {
-    const TileOut o = a.outs[t];
-    const float s0 = o.global * rowscale[n0], s1 = o.global * rowscale[n1];
-    if (g < o.rows) {
-      if (n0 < m) o.y[(int64_t)n0 * o.ld + g] = acc[0] * s0;
-      if (n1 < m) o.y[(int64_t)n1 * o.ld + g] = acc[1] * s1;
-    }
-    if (g + 8 < o.rows) {
-      if (n0 < m) o.y[(int64_t)n0 * o.ld + g + 8] = acc[2] * s0;
-      if (n1 < m) o.y[(int64_t)n1 * o.ld + g + 8] = acc[3] * s1;
-    }
-  } else if constexpr (EPI == kEpiSwiglu) {
-    const int f = t * 8 + g;
-    float v0 = 0.f, v1 = 0.f;
-    if (f < a.features) {
-      const float sg = a.sg[f], su = a.su[f];
-      const float z0 = acc[0] * a.g_gate * sg, z1 = acc[1] * a.g_gate * sg;
-      v0 = z0 / (1.f + expf(-z0)) * (acc[2] * a.g_up * su);
-      v1 = z1 / (1.f + expf(-z1)) * (acc[3] * a.g_up * su);
-      if (n0 >= m) v0 = 0.f;
-      if (n1 >= m) v1 = 0.f;
-      a.v16[frag_offset_halves(f, n0)] = __half_as_ushort(__float2half_rn(v0));
-      a.v16[frag_offset_halves(f, n1)] = __half_as_ushort(__float2half_rn(v1));
-      if (a.vout) {
-        if (n0 < m) a.vout[(int64_t)n0 * a.features + f] = v0;
-        if (n1 < m) a.vout[(int64_t)n1 * a.features + f] = v1;
-      }
-    }
-    // sum of squares over the tile's 8 features, per activation row (fixed shuffle order)
-    float q0 = v0 * v0, q1 = v1 * v1;
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      q0 += __shfl_xor_sync(0xffffffffu, q0, o);
-      q1 += __shfl_xor_sync(0xffffffffu, q1, o);
-    }
-    if (g == 0) {
-      a.vsum[t * 8 + n0] = q0;
-      a.vsum[t * 8 + n1] = q1;
-    }
-  } else {   // kEpiHead
-    const int r0 = t * 16 + g, r1 = r0 + 8;
-    float l[4];
-    l[0] = r0 < a.vocab ? acc[0] * a.g_head * a.logit_scale[r0] : -INFINITY;
-    l[1] = r0 < a.vocab ? acc[1] * a.g_head * a.logit_scale[r0] : -INFINITY;
-    l[2] = r1 < a.vocab ? acc[2] * a.g_head * a.logit_scale[r1] : -INFINITY;
-    l[3] = r1 < a.vocab ? acc[3] * a.g_head * a.logit_scale[r1] : -INFINITY;
-    if (r0 < a.vocab) {
-      if (n0 < m) a.logits[(int64_t)n0 * a.vocab + r0] = l[0];
-      if (n1 < m) a.logits[(int64_t)n1 * a.vocab + r0] = l[1];
-    }
-    if (r1 < a.vocab) {
-      if (n0 < m) a.logits[(int64_t)n0 * a.vocab + r1] = l[2];
-      if (n1 < m) a.logits[(int64_t)n1 * a.vocab + r1] = l[3];
-    }
-    // the tile's best row per activation row; ties go to the lower vocabulary index
-    float bv0 = l[0], bv1 = l[1];
-    int bi0 = r0, bi1 = r0;
-    if (l[2] > bv0) { bv0 = l[2]; bi0 = r1; }
-    if (l[3] > bv1) { bv1 = l[3]; bi1 = r1; }
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      const float ov0 = __shfl_xor_sync(0xffffffffu, bv0, o), ov1 = __shfl_xor_sync(0xffffffffu, bv1, o);
-      const int oi0 = __shfl_xor_sync(0xffffffffu, bi0, o), oi1 = __shfl_xor_sync(0xffffffffu, bi1, o);
-      if (ov0 > bv0 || (ov0 == bv0 && oi0 < bi0)) { bv0 = ov0; bi0 = oi0; }
-      if (ov1 > bv1 || (ov1 == bv1 && oi1 < bi1)) { bv1 = ov1; bi1 = oi1; }
-    }
-    if (g == 0) {
-      a.cand[t * 8 + n0] = ArgCand{bv0, bi0};
-      a.cand[t * 8 + n1] = ArgCand{bv1, bi1};
-    }
-  }
-}
-
-// One block: 4 k16 steps, each an MMA of 16 rows x 16 inputs x 8 activation rows; even steps accumulate into acc,
-// odd steps into acc2 (two independent MMA chains). xb: this block's activation fragments (two uint4, a pair of
-// steps each).
-__device__ __forceinline__ void block_mma2(float (&acc)[4], float (&acc2)[4], const uint4 w, const uint2 s,
-                                           const uint4* xb) {
-  const uint4 b01 = xb[0], b23 = xb[32];
-  const uint32_t bx[4] = {b01.x, b01.z, b23.x, b23.z}, by[4] = {b01.y, b01.w, b23.y, b23.w};
-  const uint32_t wr[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t sc = e4m3x2_to_f16x2(j < 2 ? (s.x >> (16 * j)) : (s.y >> (16 * (j - 2))));
-    const __half2 sh = *reinterpret_cast<const __half2*>(&sc);
-    const __half2 s_lo = __low2half2(sh), s_hi = __high2half2(sh);
-    uint32_t c[4];
-    e2m1x8_to_f16x2x4(wr[j], c);
-    const __half2 h0 = __hmul2(*reinterpret_cast<const __half2*>(&c[0]), s_lo);
-    const __half2 h1 = __hmul2(*reinterpret_cast<const __half2*>(&c[1]), s_hi);
-    const __half2 h2 = __hmul2(*reinterpret_cast<const __half2*>(&c[2]), s_lo);
-    const __half2 h3 = __hmul2(*reinterpret_cast<const __half2*>(&c[3]), s_hi);
-    const uint32_t a0 = *reinterpret_cast<const uint32_t*>(&h0), a1 = *reinterpret_cast<const uint32_t*>(&h1);
-    const uint32_t a2 = *reinterpret_cast<const uint32_t*>(&h2), a3 = *reinterpret_cast<const uint32_t*>(&h3);
-    if (j & 1)
-      mma_f16(acc2, a0, a1, a2, a3, bx[j], by[j]);
-    else
-      mma_f16(acc, a0, a1, a2, a3, bx[j], by[j]);
-  }
-}
-
-// The parts of tile t held by CTA warps wa..wb (warp indices within the CTA), summed in warp order. A warp's part
-// of t sits in slot 0 when t is the first tile of its run, else in slot 1.
-__device__ __forceinline__ float4 cta_sum(const GemvSmem& sm, int t, int wa, int wb, int64_t cta_warp0,
-                                          int64_t units, int64_t total_warps, int blocks, int lane) {
-  float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int v = wa; v <= wb; ++v) {
-    const int64_t g = cta_warp0 + v;
-    const int64_t v0 = g * units / total_warps, v1 = (g + 1) * units / total_warps;
-    if (v1 <= v0) continue;
-    const float4 p = sm.part[v][(t == (int)(v0 / blocks)) ? 0 : 1][lane];
-    s.x += p.x;
-    s.y += p.y;
-    s.z += p.z;
-    s.w += p.w;
-  }
+SmemPlan smem_plan(int ring, int slice, int split) {
+  SmemPlan s;
+  // STORE: ceil(128 / split) rows per rank; SwiGLU: 2 x 16 x ceil(4 / split) (gate and up of its feature groups)
+  s.rpr = std::max((kTileRows + split - 1) / split, 32 * ((4 + split - 1) / split));
+  uint32_t o = (uint32_t)(ring * kStageUnits * kUnitBytes);
+  s.off_b = o;
+  o += (uint32_t)slice * kBBlockBytes;
+  s.off_pre = o;
+  o += (uint32_t)slice * 4 * 8 * 4;
+  s.off_red = o;
+  o += (uint32_t)(split * s.rpr * 8 * 4);
+  s.off_vsq = o;
+  o += 8 * 64 * 4;
+  s.off_cand = o;
+  o += 4 * 8 * 8;
+  s.off_bar = o;
+  o += (2 * kMaxRing + 8) * 8;
+  s.off_misc = o;
+  o += 128;
+  s.total = o;
   return s;
 }
 
+// TMEM: the accumulator (two when a CTA takes several tiles), the slice's activation scales, the ring's weight scales
+int tmem_columns(int tiles_per_cta, int slice, int ring) {
+  return (tiles_per_cta > 1 ? 2 : 1) * kAccCols + 4 * slice + 4 * ring * kStageUnits;
+}
+
+__device__ __forceinline__ void wait_bar(uint64_t* bar, uint32_t parity, int* err) {
+  mbar_wait_bounded(bar, parity, err);
+}
+
+// first row (STORE) or 16-feature group (SwiGLU) a cluster rank finishes: ceil(n * rank / split)
+__device__ __forceinline__ int share_begin(int n, int rank, int split) { return (n * rank + split - 1) / split; }
+
 template <int EPI>
-__global__ void __launch_bounds__(kWarps * 32, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  GemvSmem& sm = *reinterpret_cast<GemvSmem*>(smem_raw);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t total_warps = (int64_t)gridDim.x * kWarps;
-  const int64_t cta_warp0 = (int64_t)blockIdx.x * kWarps;
-  const int64_t gw = cta_warp0 + warp;
-  const int64_t units = (int64_t)a.tiles * a.blocks;
-  const int64_t u0 = gw * units / total_warps, u1 = (gw + 1) * units / total_warps;
-  const int64_t cta_u0 = cta_warp0 * units / total_warps, cta_u1 = (cta_warp0 + kWarps) * units / total_warps;
-  const int n = (int)(u1 - u0);   // this warp's blocks
-  const int nst = (n + kStageBlocks - 1) / kStageBlocks;
-  const uint8_t* src = a.w + u0 * kBlockBytes;
-  uint64_t* bars = sm.bar[warp];
-  auto issue = [&](int st) {   // lane 0: stage st of the run into its ring slot
-    const int slot = st % kStages;
-    const int cnt = n - st * kStageBlocks < kStageBlocks ? n - st * kStageBlocks : kStageBlocks;
-    const uint32_t bytes = (uint32_t)cnt * kBlockBytes;
-    mbar_expect_tx(&bars[slot], bytes);
-    bulk_g2s(sm.ring[warp][slot], src + (int64_t)st * kStageBytes, bytes, &bars[slot]);
-  };
-  // the weights do not depend on the previous kernel: start streaming before waiting on it
-  if (lane == 0 && n > 0) {
-#pragma unroll
-    for (int j = 0; j < kStages; ++j) mbar_init(&bars[j], 1);
-    mbar_init_fence();
-    for (int st = 0; st < kStages && st < nst; ++st) issue(st);
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ Params P) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const GemvArgs& a = P.a;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KB = a.kblocks, S = P.split, ring = P.ring;
+  // this CTA's job: tiles [t0, t0 + nt) x K blocks [k0, k0 + nkb)
+  int t0, nt, k0, nkb, srank;
+  if (S > 1) {
+    t0 = blockIdx.x / S;
+    nt = 1;
+    srank = (int)(blockIdx.x % S);
+    k0 = KB * srank / S;
+    nkb = KB * (srank + 1) / S - k0;
+  } else {
+    t0 = blockIdx.x * P.tpc;
+    nt = min(P.tpc, a.tiles - t0);
+    srank = 0;
+    k0 = 0;
+    nkb = KB;
   }
+  const int nunits = nt * nkb, nstages = (nunits + kStageUnits - 1) / kStageUnits;
+  uint8_t* ringbuf = smem;
+  uint8_t* bbuf = smem + P.off_b;
+  float* pre_s = reinterpret_cast<float*>(smem + P.off_pre);   // [nkb * 4][8]
+  float* red = reinterpret_cast<float*>(smem + P.off_red);     // [S][rpr][8]
+  float* vsq = reinterpret_cast<float*>(smem + P.off_vsq);
+  ArgCand* cand_s = reinterpret_cast<ArgCand*>(smem + P.off_cand);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P.off_bar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + ring;
+  uint64_t* bfull = bars + 2 * ring;
+  uint64_t* accfull = bars + 2 * ring + 1;    // [2]
+  uint64_t* accempty = bars + 2 * ring + 3;   // [2]
+  uint64_t* done = bars + 2 * ring + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + P.off_misc);
+  float* pslice = reinterpret_cast<float*>(smem + P.off_misc + 16);   // [8] the rows' common prescale
+  float* rowscale = reinterpret_cast<float*>(smem + P.off_misc + 48);   // [8]
+
+  // ---- set-up: TMEM before the dependent launch (a dependent CTA on this SM may wait for our columns) ----
+  if (warp == 2) tmem_alloc(tmem_slot, P.tmem_cols);
+  if (tid == 0) {
+    for (int i = 0; i < ring; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(bfull, 1);
+    mbar_init(&accfull[0], 1);
+    mbar_init(&accfull[1], 1);
+    mbar_init(&accempty[0], kTileRows);
+    mbar_init(&accempty[1], kTileRows);
+    mbar_init(done, 1);
+    mbar_init_fence();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  // A stage's units are contiguous in the weight (consecutive K blocks of one tile, or whole tiles when the K blocks
+  // are not split), so a stage is one bulk copy: the bulk copies of one thread complete one after another, and a
+  // few large copies stream far faster than many small ones.
+  auto unit_src = [&](int u) {
+    const int t = t0 + u / nkb, kb = k0 + u % nkb;
+    return a.w + ((int64_t)t * KB + kb) * kUnitBytes;
+  };
+  auto issue_stage = [&](int st) {
+    const int slot = st % ring, first = st * kStageUnits;
+    const int cnt = min(kStageUnits, nunits - first);
+    mbar_expect_tx(&full[slot], (uint32_t)cnt * kUnitBytes);
+    bulk_g2s(ringbuf + slot * kStageUnits * kUnitBytes, unit_src(first), (uint32_t)cnt * kUnitBytes, &full[slot]);
+  };
+  if (tid == 0)
+    for (int st = 0; st < ring && st < nstages; ++st) issue_stage(st);
   __syncwarp();
+
   if (a.pdl) {
     pdl_launch_next();
     pdl_wait();
   }
   const int m = a.m_dev ? *a.m_dev : a.m;
-  if constexpr (EPI == kEpiStore) {
-    if (a.sumsq) {
-      const int r = threadIdx.x & 7, j0 = threadIdx.x >> 3;
-      float acc = 0.f;
-      for (int p = j0; p < a.nparts; p += 32) acc += a.sumsq[p * kMaxRows + r];
-      sm.red[j0][r] = acc;
-      __syncthreads();
-      if (threadIdx.x < kMaxRows) {
-        float t = 0.f;
-        for (int j = 0; j < 32; ++j) t += sm.red[j][threadIdx.x];
-        sm.rowscale[threadIdx.x] = 1.f / sqrtf(t + 1e-6f);
-      }
-    } else if (threadIdx.x < kMaxRows) {
-      sm.rowscale[threadIdx.x] = 1.f;
-    }
-    __syncthreads();
+
+  // ---- the B operand of this CTA's K slice: the producer's digits, brought to one prescale per row ----
+  // (a thread other than the weight producer issues the copy, so that it does not queue behind the weight stages)
+  if (tid == 96) {
+    mbar_expect_tx(bfull, (uint32_t)nkb * kBBlockBytes);
+    bulk_g2s(bbuf, a.xb + (int64_t)k0 * kBBlockBytes, (uint32_t)nkb * kBBlockBytes, bfull);
   }
-  const float* rowscale = sm.rowscale;
-  const uint4* x16 = reinterpret_cast<const uint4*>(a.x16);
-  const int first_tile = n > 0 ? (int)(u0 / a.blocks) : -1;
-  if (n > 0) {
-    int t = first_tile;
-    int kb = (int)(u0 - (int64_t)t * a.blocks);   // block index inside tile t
-    int part_kb0 = kb;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f}, acc2[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t parity = 0;
-    // the end of tile t's part: the epilogue for a whole tile, else a shared-memory slot
-    auto tile_done = [&]() {
-      float f[4] = {acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]};
-      if (part_kb0 == 0)
-        epilogue<EPI>(a, t, f, m, rowscale, lane);
-      else
-        sm.part[warp][t == first_tile ? 0 : 1][lane] = make_float4(f[0], f[1], f[2], f[3]);
-      ++t;
-      kb = 0;
-      part_kb0 = 0;
+  __syncwarp();
+  {
+    const int i = warp;   // warp i: activation row i
+    float pmin = 3.0e38f;
+    for (int b = lane; b < nkb * 4; b += 32) {
+      const float pb = a.xb_pre[((int64_t)k0 * 4 + b) * 8 + i];
+      pre_s[b * 8 + i] = pb;
+      pmin = fminf(pmin, pb);
+    }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[q] = acc2[q] = 0.f;
-    };
-    for (int st = 0; st < nst; ++st) {
-      const int slot = st % kStages;
-      mbar_wait_bounded(&bars[slot], (parity >> slot) & 1u, lane == 0 ? a.err : nullptr);
-      parity ^= 1u << slot;
-      const unsigned char* buf = sm.ring[warp][slot] + lane * 16;
-      const unsigned char* sbuf = sm.ring[warp][slot] + 512 + (lane >> 2) * 8;
-      const int cnt = n - st * kStageBlocks < kStageBlocks ? n - st * kStageBlocks : kStageBlocks;
-      if (cnt == kStageBlocks && kb + kStageBlocks <= a.blocks) {   // the common case: no boundary inside
-        const uint4* xb = x16 + kb * 64 + lane;
+    for (int o = 16; o > 0; o >>= 1) pmin = fminf(pmin, __shfl_xor_sync(0xffffffffu, pmin, o));
+    if (lane == 0) pslice[i] = pmin;
+  }
+  if (EPI == kEpiStore && tid < 8) {
+    float t = 1.f;
+    if (a.sumsq) {
+      t = 0.f;
+      for (int q = 0; q < a.nparts; ++q) t += a.sumsq[q * 8 + tid];
+      t = 1.f / sqrtf(t + 1e-6f);
+    }
+    rowscale[tid] = t;
+  }
+  wait_bar(bfull, 0, a.err);
+  __syncthreads();
+  for (int e = tid; e < nkb * 4 * 8; e += kThreads) {   // (group, row): its 6 digit scales
+    const int b = e >> 3, i = e & 7;
+    const int k = (__float_as_int(pre_s[b * 8 + i]) - __float_as_int(pslice[i])) >> 23;
+    if (k > 0) {
+      uint8_t* sfb = bbuf + (b >> 2) * kBBlockBytes + kBCodeBytes;
 #pragma unroll
-        for (int i = 0; i < kStageBlocks; ++i)
-          block_mma2(acc, acc2, *reinterpret_cast<const uint4*>(buf + i * kBlockBytes),
-                     *reinterpret_cast<const uint2*>(sbuf + i * kBlockBytes), xb + i * 64);
-        kb += kStageBlocks;
-        if (kb == a.blocks) tile_done();
+      for (int d = 0; d < kDigits; ++d) sfb[sf_offset(8 * d + i, b & 3)] = (uint8_t)ue4m3_scale_down(sfb[sf_offset(8 * d + i, b & 3)], k);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncthreads();
+
+  if (warp == 0) {
+    // ---- producer ----
+    if (lane == 0) {
+      for (int st = ring; st < nstages; ++st) {
+        const int slot = st % ring;
+        wait_bar(&empty[slot], (uint32_t)((st / ring) - 1) & 1u, a.err);
+        issue_stage(st);
+      }
+      // every issued copy has landed before the CTA may exit (normally long since)
+      for (int slot = 0; slot < ring && slot < nstages; ++slot) {
+        const int last = slot + ((nstages - 1 - slot) / ring) * ring;
+        wait_bar(&full[slot], (uint32_t)(last / ring) & 1u, a.err);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA issuer: the slice's activation scales go to TMEM once; per unit the weight scales, then the MMA.
+    // One thread issues everything, so the per-unit work is kept to a few instructions: indices advance
+    // incrementally and the descriptors by their start-address field (16-byte units, no carry out of 14 bits). ----
+    if (lane == 0) {
+      tc_fence_after();
+      const uint32_t ring_addr = smem_u32(ringbuf), b_addr = smem_u32(bbuf);
+      const uint32_t acc_cols = nt > 1 ? 2 * kAccCols : kAccCols;
+      const uint32_t sfb0 = tbase + acc_cols, sfa0 = sfb0 + 4 * (uint32_t)nkb;
+      for (int kb = 0; kb < nkb; ++kb) tc_cp_sf(sfb0 + 4 * kb, sf_desc(b_addr + (uint32_t)(kb * kBBlockBytes + kBCodeBytes)));
+      const uint64_t da0 = a_desc(ring_addr), dsfa0 = sf_desc(ring_addr + kUnitCodeBytes), db0 = a_desc(b_addr);
+      int j = 0, kb = 0;
+      for (int st = 0; st < nstages; ++st) {
+        const int slot = st % ring, cnt = min(kStageUnits, nunits - st * kStageUnits);
+        wait_bar(&full[slot], (uint32_t)(st / ring) & 1u, a.err);
+        tc_fence_after();
+        const uint32_t u0 = (uint32_t)(slot * kStageUnits);
+        for (int idx = 0; idx < cnt; ++idx) {
+          if (kb == 0 && j >= 2) {
+            wait_bar(&accempty[j & 1], (uint32_t)((j >> 1) - 1) & 1u, a.err);
+            tc_fence_after();
+          }
+          const uint32_t ui = u0 + (uint32_t)idx;
+          const uint32_t sfa = sfa0 + 4 * ui;
+          tc_cp_sf(sfa, dsfa0 + ui * (kUnitBytes >> 4));
+          tc_mma_fp4(tbase + (uint32_t)((j & 1) * kAccCols), da0 + ui * (kUnitBytes >> 4),
+                     db0 + (uint32_t)kb * (kBBlockBytes >> 4), sfa, sfb0 + 4 * (uint32_t)kb, kb > 0 ? 1u : 0u);
+          if (++kb == nkb) {
+            tc_commit(&accfull[j & 1]);
+            kb = 0;
+            ++j;
+          }
+        }
+        tc_commit(&empty[slot]);
+      }
+      tc_commit(done);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ---- epilogue: TMEM lane quarter q = warp - 4 holds tile rows 32 q .. 32 q + 31 ----
+    const int q = warp - 4, r = 32 * q + lane;
+    float inv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) inv[i] = 1.f / pslice[i];
+    for (int j = 0; j < nt; ++j) {
+      const int acc = j & 1, t = t0 + j;
+      wait_bar(&accfull[acc], (uint32_t)(j >> 1) & 1u, a.err);
+      tc_fence_after();
+      float d[kDigitRows];
+      const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * kAccCols);
+      tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(&d[0]));
+      tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(&d[16]));
+      tmem_ld16(taddr + 32, *reinterpret_cast<float(*)[16]>(&d[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&accempty[acc]);
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        y[i] = ((((d[i] + d[8 + i]) + d[16 + i]) + d[24 + i]) + (d[32 + i] + d[40 + i])) * inv[i];
+      if constexpr (EPI == kEpiHead) {
+        const int row = t * kTileRows + r;
+        const bool ok = row < a.vocab;
+        const float ls = ok ? a.logit_scale[row] * a.g_head : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float l = ok ? y[i] * ls : -INFINITY;
+          if (ok && i < m) a.logits[(int64_t)i * a.vocab + row] = l;
+          int li = row;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, l, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, li, o);
+            if (ov > l || (ov == l && oi < li)) {
+              l = ov;
+              li = oi;
+            }
+          }
+          if (lane == 0) cand_s[q * 8 + i] = ArgCand{l, li};
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (q == 0 && lane < 8) {
+          ArgCand best = cand_s[lane];
+          for (int qq = 1; qq < 4; ++qq) {
+            const ArgCand c = cand_s[qq * 8 + lane];
+            if (c.v > best.v || (c.v == best.v && c.i < best.i)) best = c;
+          }
+          a.cand[t * 8 + lane] = best;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
       } else {
-        for (int i = 0; i < cnt; ++i) {
-          block_mma2(acc, acc2, *reinterpret_cast<const uint4*>(buf + i * kBlockBytes),
-                     *reinterpret_cast<const uint2*>(sbuf + i * kBlockBytes), x16 + kb * 64 + lane);
-          if (++kb == a.blocks) tile_done();
+        const TileOut o = a.outs ? a.outs[t] : TileOut{};
+        float g;
+        if constexpr (EPI == kEpiSwiglu)
+          g = r < 64 ? a.g_gate : a.g_up;
+        else
+          g = r < 64 ? o.global_lo : o.global_hi;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] *= g;
+        if (EPI == kEpiStore && S == 1) {
+          if (r < o.rows)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              if (i < m) o.y[(int64_t)i * o.ld + r] = y[i] * rowscale[i];
+        } else {
+          // push this CTA's part of row r to the cluster rank that finishes it
+          int owner, slot;
+          if constexpr (EPI == kEpiStore) {
+            owner = (r * S) / kTileRows;
+            slot = r - share_begin(kTileRows, owner, S);
+          } else {
+            const int f = r & 63;
+            owner = ((f >> 4) * S) / 4;
+            const int g0 = share_begin(4, owner, S), g1 = share_begin(4, owner + 1, S);
+            slot = (r >= 64 ? 16 * (g1 - g0) : 0) + f - 16 * g0;
+          }
+          float* dst = red + (srank * P.rpr + slot) * 8;
+          if (S == 1) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = y[i];
+          } else {
+            st_cluster_f32x8(dst, (uint32_t)owner, y);
+          }
         }
       }
-      __syncwarp();
-      if (lane == 0 && st + kStages < nst) {   // the slot was read: refill it with the run's next stage
-        fence_proxy_async_smem();
-        issue(st + kStages);
+    }
+  }
+  // ---- split tiles meet in the cluster; SwiGLU pairs gate and up rows ----
+  __syncthreads();
+  if (EPI != kEpiHead && (S > 1 || EPI == kEpiSwiglu)) {
+    if (S > 1) cluster_sync();
+    const int t = t0;
+    auto total = [&](int slot, int i) {
+      float v = 0.f;
+      for (int c = 0; c < S; ++c) v += red[(c * P.rpr + slot) * 8 + i];
+      return v;
+    };
+    if constexpr (EPI == kEpiStore) {
+      const TileOut o = a.outs[t];
+      const int r0 = share_begin(kTileRows, srank, S), nr = share_begin(kTileRows, srank + 1, S) - r0;
+      for (int p = tid; p < nr * 8; p += kThreads) {
+        const int i = p / nr, rl = p % nr, r = r0 + rl;
+        if (i < m && r < o.rows) o.y[(int64_t)i * o.ld + r] = total(rl, i) * rowscale[i];
+      }
+    } else {
+      // quad (group g, row i): lane t holds features 16 g + 4 t .. + 3 of the tile; v -> digits of the next GEMV
+      const int g0 = share_begin(4, srank, S), g1 = share_begin(4, srank + 1, S), nf = 16 * (g1 - g0);
+      const int quad = tid >> 2, qt = tid & 3;
+      const bool active = quad < (g1 - g0) * 8;
+      const int gl = quad >> 3, i = quad & 7, g = g0 + gl;
+      float v[4] = {0.f, 0.f, 0.f, 0.f}, sq = 0.f;
+      if (active) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int fl = 16 * gl + 4 * qt + c, f = t * 64 + 16 * g + 4 * qt + c;
+          if (f < a.features && i < m) {
+            const float z = total(fl, i) * a.sg[f];
+            const float u = total(nf + fl, i) * a.su[f];
+            v[c] = z / (1.f + expf(-z)) * u;
+          }
+          sq += v[c] * v[c];
+        }
+      }
+      if (tid < 8 * 64 / 4) vsq[i * 16 + ((gl * 4 + qt) & 15)] = active ? sq : 0.f;
+      uint32_t code[kDigits], sf[kDigits];
+      const float pb = digitize16_quad(v, code, sf);   // every lane of the warp takes part
+      if (active) {
+        store_digits_quad(a.vb + (int64_t)t * kBBlockBytes, i, g, qt, code, sf);
+        if (qt == 0) a.vb_pre[((int64_t)t * 4 + g) * 8 + i] = pb;
+      }
+      __syncthreads();
+      if (tid < 8) {
+        float s2 = 0.f;
+        for (int e = 0; e < 4 * (g1 - g0); ++e) s2 += vsq[tid * 16 + e];
+        a.vsum[((int64_t)t * S + srank) * 8 + tid] = s2;
       }
     }
-    if (kb > 0)   // the run ends inside tile t
-      sm.part[warp][t == first_tile ? 0 : 1][lane] =
-          make_float4(acc[0] + acc2[0], acc[1] + acc2[1], acc[2] + acc2[2], acc[3] + acc2[3]);
   }
-  __syncthreads();
-  if (n <= 0) return;
-  // ---- split tiles: the last warp of the CTA that covers a tile sums the CTA's parts of it ----
-  const int last_tile = (int)((u1 - 1) / a.blocks);
-  for (int which = 0; which < 2; ++which) {
-    const int t = which == 0 ? first_tile : last_tile;
-    if (which == 1 && last_tile == first_tile) break;
-    const int64_t tb = (int64_t)t * a.blocks, te = tb + a.blocks;
-    const int64_t pb = u0 > tb ? u0 : tb, pe = u1 < te ? u1 : te;   // this warp's part of t
-    if (pb == tb && pe == te) continue;                              // whole tile: done in the loop
-    if (!(pe == te || u1 == cta_u1)) continue;                        // a later warp of the CTA continues t
-    const int64_t owner_first = ((tb + 1) * total_warps - 1) / units;
-    const int wa = (int)((owner_first > cta_warp0 ? owner_first : cta_warp0) - cta_warp0);
-    const float4 s4 = cta_sum(sm, t, wa, warp, cta_warp0, units, total_warps, a.blocks, lane);
-    float f[4] = {s4.x, s4.y, s4.z, s4.w};
-    if (tb >= cta_u0 && te <= cta_u1) {   // every part of t is in this CTA
-      epilogue<EPI>(a, t, f, m, rowscale, lane);
-      continue;
-    }
-    // t continues in another CTA: park this CTA's sum; the CTA completing t sums the CTA parts in CTA order
-    const int cta_first_tile = (int)(cta_u0 / a.blocks);
-    const int cslot = t == cta_first_tile ? 0 : 1;
-    reinterpret_cast<float4*>(a.partial)[((int64_t)blockIdx.x * 2 + cslot) * 32 + lane] = s4;
-    __threadfence();
-    const int covered = (int)((te < cta_u1 ? te : cta_u1) - (tb > cta_u0 ? tb : cta_u0));
-    int old = 0;
-    if (lane == 0) old = atomicAdd(&a.counters[t], covered);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + covered != a.blocks) continue;
-    __threadfence();
-    const int64_t ca = (((tb + 1) * total_warps - 1) / units) / kWarps;
-    const int64_t cb = (((te) * total_warps - 1) / units) / kWarps;
-    float sum[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int64_t c = ca; c <= cb; ++c) {
-      const int64_t c0 = c * kWarps * units / total_warps, c1 = (c + 1) * kWarps * units / total_warps;
-      if (c1 <= c0) continue;
-      const int cs2 = t == (int)(c0 / a.blocks) ? 0 : 1;
-      const float4 p = __ldcg(reinterpret_cast<const float4*>(a.partial) + (c * 2 + cs2) * 32 + lane);
-      sum[0] += p.x;
-      sum[1] += p.y;
-      sum[2] += p.z;
-      sum[3] += p.w;
-    }
-    if (lane == 0) a.counters[t] = 0;
-    epilogue<EPI>(a, t, sum, m, rowscale, lane);
+  // ---- teardown: every tcgen05 operation has completed before the columns go back ----
+  if (warp == 2) {
+    if (lane == 0) wait_bar(done, 0, a.err);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tbase, P.tmem_cols);
   }
 }
 
-// x f32 [m][k] -> fragments; one thread per (k pair, row).
-__global__ void pack_activations_kernel(const float* x, int m, int k, int kp, uint32_t* x16) {
-  const int64_t total = (int64_t)(kp / 2) * kMaxRows;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int n = (int)(i % kMaxRows), kk = (int)(i / kMaxRows) * 2;
-    float v0 = 0.f, v1 = 0.f;
-    if (n < m && kk < k) {
-      v0 = x[(int64_t)n * k + kk];
-      v1 = kk + 1 < k ? x[(int64_t)n * k + kk + 1] : 0.f;
-    }
-    x16[frag_offset_halves(kk, n) >> 1] = pack_f16x2(v0, v1);
+// x f32 [m][k] -> digits: one quad per (16-input group, row)
+__global__ void digitize_rows_kernel(const float* x, int m, int k, uint8_t* xb, float* xb_pre) {
+  const int64_t quad = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 2;
+  const int qt = threadIdx.x & 3;
+  const int groups = (k + 63) / 64 * 4;   // every group of the padded K blocks
+  const bool active = quad < (int64_t)groups * 8;
+  const int g = active ? (int)(quad / 8) : 0, i = (int)(quad % 8);
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  if (active && i < m && 16 * g < k) {
+    const float4 q = *reinterpret_cast<const float4*>(x + (int64_t)i * k + 16 * g + 4 * qt);
+    v[0] = q.x;
+    v[1] = q.y;
+    v[2] = q.z;
+    v[3] = q.w;
+  }
+  uint32_t code[kDigits], sf[kDigits];
+  const float pb = digitize16_quad(v, code, sf);
+  if (active) {
+    store_digits_quad(xb + (int64_t)(g >> 2) * kBBlockBytes, i, g & 3, qt, code, sf);
+    if (qt == 0) xb_pre[(int64_t)g * 8 + i] = pb;
   }
 }
 
 }  // namespace
 
-int gemv_grid(int num_sms) { return num_sms * 2; }
+GemvPlan plan_gemv(int tiles, int kblocks, int num_sms, int max_split, int max_tiles_per_cta) {
+  constexpr int64_t kSmPerSm = 233472, kPerCtaReserve = 1024, kMaxSmem = 232448;
+  GemvPlan p;
+  for (int cps = 2; cps >= 1; --cps) {
+    const int slots = num_sms * cps;
+    if (tiles >= slots || max_split <= 1) {
+      p.split = 1;
+      p.tiles_per_cta = std::max(1, std::min(max_tiles_per_cta, (tiles + slots - 1) / slots));
+      p.grid = (tiles + p.tiles_per_cta - 1) / p.tiles_per_cta;
+    } else {
+      p.split = std::max(1, std::min(std::min(max_split, kblocks), slots / tiles));
+      p.tiles_per_cta = 1;
+      p.grid = tiles * p.split;
+    }
+    const int slice = (kblocks + p.split - 1) / p.split;
+    p.ring = cps == 2 ? 3 : kMaxRing;
+    p.smem = smem_plan(p.ring, slice, p.split).total;
+    if (cps == 2 && 2 * (p.smem + kPerCtaReserve) > kSmPerSm) continue;
+    if (cps == 2 && tmem_columns(p.tiles_per_cta, slice, p.ring) > 256) continue;
+    XTG_REQUIRE(p.smem <= kMaxSmem, "gemv: the K slice does not fit in shared memory");
+    return p;
+  }
+  return p;
+}
 
-int64_t gemv_partial_floats(int grid) { return (int64_t)grid * 2 * 32 * 4; }
-
-void launch_gemv(int epi, const GemvArgs& a_in, int max_grid, cudaStream_t s, bool pdl) {
-  GemvArgs a = a_in;
-  a.pdl = pdl ? 1 : 0;
-  // at least 8 blocks per warp where the weight is small; never more CTAs than the scratch was sized for
-  const int64_t units = (int64_t)a.tiles * a.blocks;
-  const int64_t want = (units + kWarps * 8 - 1) / (kWarps * 8);
-  const int grid = (int)(want < max_grid ? (want > 0 ? want : 1) : max_grid);
+void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bool pdl) {
+  XTG_REQUIRE(epi != kEpiHead || p.split == 1, "gemv: the head epilogue takes whole tiles");
+  XTG_REQUIRE(epi != kEpiSwiglu || p.tiles_per_cta == 1, "gemv: the SwiGLU epilogue takes one tile per CTA");
+  XTG_REQUIRE(p.split >= 1 && p.split <= 8 && p.ring >= 1 && p.ring <= kMaxRing, "gemv: bad plan");
+  Params P = {};
+  P.a = a;
+  P.a.pdl = pdl ? 1 : 0;
+  P.split = p.split;
+  P.tpc = p.tiles_per_cta;
+  P.ring = p.ring;
+  P.slice_max = (a.kblocks + p.split - 1) / p.split;
+  const SmemPlan sp = smem_plan(p.ring, P.slice_max, p.split);
+  P.rpr = sp.rpr;
+  P.off_b = sp.off_b;
+  P.off_pre = sp.off_pre;
+  P.off_red = sp.off_red;
+  P.off_vsq = sp.off_vsq;
+  P.off_cand = sp.off_cand;
+  P.off_bar = sp.off_bar;
+  P.off_misc = sp.off_misc;
+  const int cols = tmem_columns(p.tiles_per_cta, P.slice_max, p.ring);
+  XTG_REQUIRE(cols <= 512, "gemv: the K slice's scales do not fit in TMEM");
+  P.tmem_cols = cols <= 256 ? 256 : 512;
   static bool attr_set[3] = {false, false, false};
+  auto* k = epi == kEpiStore ? gemv_kernel<kEpiStore> : epi == kEpiSwiglu ? gemv_kernel<kEpiSwiglu> : gemv_kernel<kEpiHead>;
   if (!attr_set[epi]) {
-    auto* k = epi == kEpiStore ? gemv_kernel<kEpiStore> : epi == kEpiSwiglu ? gemv_kernel<kEpiSwiglu> : gemv_kernel<kEpiHead>;
-    XTG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(GemvSmem)));
+    XTG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
     attr_set[epi] = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kWarps * 32);
-  cfg.dynamicSmemBytes = sizeof(GemvSmem);
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = sp.total;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (p.split > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = p.split;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  if (epi == kEpiStore)
-    XTG_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<kEpiStore>, a));
-  else if (epi == kEpiSwiglu)
-    XTG_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<kEpiSwiglu>, a));
-  else
-    XTG_CUDA(cudaLaunchKernelEx(&cfg, gemv_kernel<kEpiHead>, a));
+  cfg.numAttrs = n;
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, k, P));
 }
 
-void pack_activations(const float* x, int m, int k, uint32_t* x16, cudaStream_t s) {
-  const int kp = packed_blocks(k) * 64;
-  const int64_t total = (int64_t)(kp / 2) * kMaxRows;
-  const int grid = (int)((total + 255) / 256);
-  pack_activations_kernel<<<grid, 256, 0, s>>>(x, m, k, kp, x16);
+void digitize_rows(const float* x, int m, int k, uint8_t* xb, float* xb_pre, cudaStream_t s) {
+  XTG_REQUIRE(k % 16 == 0 && m >= 0 && m <= 8, "digitize: k a multiple of 16, at most 8 rows");
+  const int64_t threads = (int64_t)((k + 63) / 64 * 4) * 8 * 4;
+  digitize_rows_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, s>>>(x, m, k, xb, xb_pre);
   XTG_CUDA(cudaGetLastError());
 }
 

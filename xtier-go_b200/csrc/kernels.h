@@ -6,13 +6,20 @@
 
 namespace xtg {
 
-// ---- the NVFP4 streaming layout (weights.cu) ----
-constexpr int kBlockBytes = 576;   // 16 rows x 64 inputs: 512 code bytes + 64 scale bytes
-inline int packed_blocks(int k) { return (k + 63) / 64; }
-inline int packed_tiles(int n_out, bool interleave) { return interleave ? (n_out + 7) / 8 : (n_out + 15) / 16; }
+// ---- NVFP4 weights in tensor-core units (weights.cu; layouts in fp4mma.cuh) ----
+// A weight [n_out][k] is cut into tiles of 128 rows and K blocks of 64 inputs; unit (t, b) is 4608 contiguous bytes
+// (4096 code bytes in the MMA's A layout, 512 bytes of E4M3 scales in the scale-factor atom), units in tile-major
+// order. An interleaved pack holds two weights of n_out rows (gate, up): tile t has rows 64 t .. 64 t + 63 of the
+// first in tile rows 0-63 and the same rows of the second in tile rows 64-127.
+constexpr int kPackTileRows = 128;
+constexpr int kPackUnitBytes = 4608;
+inline int packed_kblocks(int k) { return (k + 63) / 64; }
+inline int packed_tiles(int n_out, bool interleave) { return interleave ? (n_out + 63) / 64 : (n_out + 127) / 128; }
 inline int64_t packed_bytes(int n_out, int k, bool interleave) {
-  return (int64_t)packed_tiles(n_out, interleave) * packed_blocks(k) * kBlockBytes;
+  return (int64_t)packed_tiles(n_out, interleave) * packed_kblocks(k) * kPackUnitBytes;
 }
+// activations as B digits (fp4mma.cuh): 2048 bytes per 64 inputs
+inline int64_t digit_bytes(int k) { return (int64_t)packed_kblocks(k) * 2048; }
 
 void gen_normal_bf16(uint64_t seed, uint64_t stream, float stddev, uint16_t* out, int64_t n, cudaStream_t s);
 void gen_uniform(uint64_t seed, uint64_t stream, float lo, float hi, float* out, int64_t n, cudaStream_t s);
@@ -21,16 +28,15 @@ void quantize_nvfp4(const uint16_t* w, int n_out, int k, uint8_t* codes, uint8_t
                     unsigned int* amax_scratch, cudaStream_t s);
 void pack_nvfp4(const uint8_t* codes_a, const uint8_t* scales_a, const uint8_t* codes_b, const uint8_t* scales_b,
                 int n_out, int k, bool interleave, uint8_t* dst, cudaStream_t s);
-void unpack_nvfp4(const uint8_t* src, int n_out, int k, uint8_t* codes, uint8_t* scales, cudaStream_t s);
 
 // ---- the GEMV (gemv.cu) ----
-// Where a tile's 16 output rows go (STORE epilogue): y[n * ld + r] for activation row n, tile row r < rows.
+// Where a tile's 128 output rows go (STORE epilogue): y[n * ld + r] for activation row n, tile row r < rows; global
+// scales of tile rows 0-63 and 64-127.
 struct TileOut {
   float* y;
   int ld;
   int rows;
-  float global;
-  int pad;
+  float global_lo, global_hi;
 };
 
 enum GemvEpi { kEpiStore = 0, kEpiSwiglu = 1, kEpiHead = 2 };
@@ -41,25 +47,26 @@ struct ArgCand {   // the best logit of a tile for one activation row
 };
 
 struct GemvArgs {
-  const uint8_t* w;          // streaming-layout blocks
-  int tiles, blocks;         // tiles of 16 rows, 64-input blocks per tile
-  const uint32_t* x16;       // activations, fp16 B fragments: [blocks * 4 steps][32 lanes][2 words]
+  const uint8_t* w;          // units [tiles][kblocks]
+  int tiles, kblocks;
+  // input: the B digits of the activations ([kblocks][2048], fp4mma.cuh) and the power-of-two prescale of every
+  // 16-input group and row ([kblocks * 4][8])
+  const uint8_t* xb;
+  const float* xb_pre;
   const int* m_dev;          // activation rows (1..8) read on the device (a replayable graph), or null: m
   int m;
-  float* partial;            // [total warps][2][32 lanes][4] split-K parts
-  int* counters;             // [tiles], zero between launches (the finishing warp resets its tile's)
   // kEpiStore
   const TileOut* outs;       // [tiles]
   const float* sumsq;        // optional: y *= 1 / sqrt(sum_p sumsq[p][n] + 1e-6), p < nparts (a justnorm of x)
   int nparts;
-  // kEpiSwiglu (interleaved gate / up tiles of 8 features)
+  // kEpiSwiglu (interleaved gate / up tiles): v = silu(g * sg) * (u * su) as the next GEMV's digits (K = F)
   float g_gate, g_up;
   const float* sg;
   const float* su;
   int features;              // F
-  uint16_t* v16;             // fragments of v = silu(g * sg) * (u * su) for the next GEMV (K = F)
-  float* vsum;               // [tiles][8] sum over the tile's features of v^2
-  float* vout;               // optional f32 v [n][F]
+  uint8_t* vb;               // [tiles][2048]
+  float* vb_pre;             // [tiles * 4][8]
+  float* vsum;               // [tiles * split][8]: sums of v^2 over the features each CTA finishes
   // kEpiHead
   float g_head;
   const float* logit_scale;  // [vocab]
@@ -70,11 +77,15 @@ struct GemvArgs {
   int pdl;                   // launched as a programmatic dependent
 };
 
-int gemv_grid(int num_sms);
-int64_t gemv_partial_floats(int grid);
-void launch_gemv(int epi, const GemvArgs& a, int max_grid, cudaStream_t s, bool pdl);
-
-// x f32 [m][k] -> fp16 fragments (rows >= m zero); k padded to the blocks of 64.
-void pack_activations(const float* x, int m, int k, uint32_t* x16, cudaStream_t s);
+// How a GEMV is spread over the GPU: `split` CTAs (one cluster) share each tile's K blocks, or (split 1) each CTA
+// takes tiles_per_cta whole tiles. ring: shared-memory stages of 4 units.
+struct GemvPlan {
+  int split = 1, tiles_per_cta = 1, grid = 1, ring = 3;
+  int64_t smem = 0;
+};
+GemvPlan plan_gemv(int tiles, int kblocks, int num_sms, int max_split, int max_tiles_per_cta);
+void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bool pdl);
+// x f32 [m][k] (k a multiple of 16; rows m..7 zero) -> B digits xb [kblocks][2048] and prescales xb_pre [k / 16][8]
+void digitize_rows(const float* x, int m, int k, uint8_t* xb, float* xb_pre, cudaStream_t s);
 
 }  // namespace xtg

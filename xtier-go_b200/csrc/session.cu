@@ -21,6 +21,7 @@
 #include "attention.h"
 #include "common.cuh"
 #include "elementwise.h"
+#include "fp4mma.cuh"
 #include "json.h"
 #include "kernels.h"
 
@@ -143,12 +144,13 @@ Config parse_config(const std::string& options) {
 // A packed weight (or fused set) and where its tiles go.
 struct Linear {
   uint8_t* w = nullptr;   // inside the arena
-  int tiles = 0, blocks = 0;
+  int tiles = 0, kblocks = 0;
   int64_t bytes = 0;
   int64_t alg_bytes = 0;  // codes + scales + globals of the NVFP4 weights
   int n_total = 0, k = 0;
   TileOut* outs = nullptr;   // device, kEpiStore
   float g0 = 1.f, g1 = 1.f;  // gate / up globals (kEpiSwiglu), head global
+  GemvPlan plan;
 };
 
 struct Eval {
@@ -203,16 +205,16 @@ struct xtg_cuda {
   StepParams* params_dev = nullptr;
   StepParams* params_host = nullptr;
   float *h = nullptr, *state = nullptr, *input = nullptr, *o = nullptr, *proj = nullptr, *part = nullptr;
-  uint32_t *x16 = nullptr, *a16 = nullptr, *v16 = nullptr;
+  // GEMV inputs as B digits with their per-group prescales: h (the residual's output), the gated attention output
+  // (the O projection's input), v (the down projection's input)
+  uint8_t *xb = nullptr, *ab = nullptr, *vb = nullptr;
+  float *xb_pre = nullptr, *ab_pre = nullptr, *vb_pre = nullptr;
   float *asum = nullptr, *vsum = nullptr, *logits = nullptr, *logits_host = nullptr, *argmax_val = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   int32_t* argmax = nullptr;
   ArgCand* cand = nullptr;
-  float* gemv_partial = nullptr;
-  int* gemv_counters = nullptr;
   int* dev_err = nullptr;   // bounded device waits that gave up (never expected)
   int* err_host = nullptr;  // pinned copy of dev_err
-  int gemv_grid_ = 0;
   int splits_g = 1, splits_r = 1;
   int proj_ld = 0;
   // graph
@@ -310,7 +312,8 @@ struct xtg_cuda {
     for (int e = 0; e < ne; ++e)
       if (c.kind(e) != 0) {
         total -= packed_bytes(2 * Q + 2 * KV, H, false);
-        total += (int64_t)(packed_tiles(Q, false) * 2 + packed_tiles(KV, false) * 2) * packed_blocks(H) * kBlockBytes;
+        total += (int64_t)(packed_tiles(Q, false) * 2 + packed_tiles(KV, false) * 2) * packed_kblocks(H) *
+                 kPackUnitBytes;
       }
     arena_bytes = total;
     arena = dalloc<uint8_t>((size_t)total, false);
@@ -341,12 +344,19 @@ struct xtg_cuda {
       return v;
     };
     uint8_t* cursor = arena;
-    auto place = [&](Linear& L, int tiles, int blocks) {
+    // the head takes whole tiles (its argmax candidates), SwiGLU one tile per CTA
+    auto place = [&](Linear& L, int tiles, int kblocks, int max_split = 8, int max_tpc = 1 << 20) {
       L.w = cursor;
       L.tiles = tiles;
-      L.blocks = blocks;
-      L.bytes = (int64_t)tiles * blocks * kBlockBytes;
+      L.kblocks = kblocks;
+      L.bytes = (int64_t)tiles * kblocks * kPackUnitBytes;
+      L.plan = plan_gemv(tiles, kblocks, num_sms, max_split, max_tpc);
       cursor += L.bytes;
+    };
+    auto tile_outs = [&](float* y, int ld, int n, float g) {
+      std::vector<TileOut> v(packed_tiles(n, false));
+      for (int t = 0; t < (int)v.size(); ++t) v[t] = TileOut{y + 128 * t, ld, std::min(128, n - 128 * t), g, g};
+      return v;
     };
     auto alg = [](int n, int k) { return (int64_t)n * k / 2 + (int64_t)n * k / 16 + 4; };
     proj_ld = 2 * Q + 2 * KV;
@@ -360,29 +370,27 @@ struct xtg_cuda {
       if (E.kind == 0) {
         E.sg = vec(base + 11, c.suv_lo, c.suv_hi, F);
         E.su = vec(base + 12, c.suv_lo, c.suv_hi, F);
-        place(E.gu, packed_tiles(F, true), packed_blocks(H));
+        place(E.gu, packed_tiles(F, true), packed_kblocks(H), 8, 1);
         E.gu.g0 = make(base + 0, F, H, codes_a, scales_a);
         E.gu.g1 = make(base + 1, F, H, codes_b, scales_b);
         pack_nvfp4(codes_a, scales_a, codes_b, scales_b, F, H, true, E.gu.w, stream);
         E.gu.alg_bytes = 2 * alg(F, H);
         E.gu.n_total = 2 * F;
         E.gu.k = H;
-        place(E.down, packed_tiles(H, false), packed_blocks(F));
+        place(E.down, packed_tiles(H, false), packed_kblocks(F));
         const float gd = make(base + 2, H, F, codes_a, scales_a);
         pack_nvfp4(codes_a, scales_a, nullptr, nullptr, H, F, false, E.down.w, stream);
         E.down.alg_bytes = alg(H, F);
         E.down.n_total = H;
         E.down.k = F;
-        std::vector<TileOut> outs(E.down.tiles);
-        for (int t = 0; t < E.down.tiles; ++t) outs[t] = TileOut{o + 16 * t, H, std::min(16, H - 16 * t), gd, 0};
-        E.down.outs = upload(outs);
+        E.down.outs = upload(tile_outs(o, H, H, gd));
       } else {
         E.qscale = vec(base + 9, c.qs_lo, c.qs_hi, Q);
         E.gscale = vec(base + 10, c.gs_lo, c.gs_hi, Q);
         E.theta = E.kind == 2 ? 1 : 0;
         E.cache = n_attn++;
-        const int tq = packed_tiles(Q, false), tk = packed_tiles(KV, false), blocks = packed_blocks(H);
-        place(E.qkvg, 2 * tq + 2 * tk, blocks);
+        const int tq = packed_tiles(Q, false), tk = packed_tiles(KV, false), kblocks = packed_kblocks(H);
+        place(E.qkvg, 2 * tq + 2 * tk, kblocks);
         std::vector<TileOut> outs;
         const int n_out[4] = {Q, KV, KV, Q};
         const int col[4] = {0, Q, Q + KV, Q + 2 * KV};
@@ -390,28 +398,25 @@ struct xtg_cuda {
         for (int j = 0; j < 4; ++j) {
           const float gj = make(base + j, n_out[j], H, codes_a, scales_a);
           pack_nvfp4(codes_a, scales_a, nullptr, nullptr, n_out[j], H, false,
-                     E.qkvg.w + (int64_t)tile0 * blocks * kBlockBytes, stream);
+                     E.qkvg.w + (int64_t)tile0 * kblocks * kPackUnitBytes, stream);
           const int tj = packed_tiles(n_out[j], false);
-          for (int t = 0; t < tj; ++t)
-            outs.push_back(TileOut{proj + col[j] + 16 * t, proj_ld, std::min(16, n_out[j] - 16 * t), gj, 0});
+          for (const TileOut& t : tile_outs(proj + col[j], proj_ld, n_out[j], gj)) outs.push_back(t);
           tile0 += tj;
           E.qkvg.alg_bytes += alg(n_out[j], H);
         }
         E.qkvg.outs = upload(outs);
         E.qkvg.n_total = 2 * Q + 2 * KV;
         E.qkvg.k = H;
-        place(E.o, packed_tiles(H, false), packed_blocks(Q));
+        place(E.o, packed_tiles(H, false), packed_kblocks(Q));
         const float go = make(base + 4, H, Q, codes_a, scales_a);
         pack_nvfp4(codes_a, scales_a, nullptr, nullptr, H, Q, false, E.o.w, stream);
         E.o.alg_bytes = alg(H, Q);
         E.o.n_total = H;
         E.o.k = Q;
-        std::vector<TileOut> oo(E.o.tiles);
-        for (int t = 0; t < E.o.tiles; ++t) oo[t] = TileOut{o + 16 * t, H, std::min(16, H - 16 * t), go, 0};
-        E.o.outs = upload(oo);
+        E.o.outs = upload(tile_outs(o, H, H, go));
       }
     }
-    place(head, packed_tiles(c.vocab, false), packed_blocks(H));
+    place(head, packed_tiles(c.vocab, false), packed_kblocks(H), 1);
     head.g0 = make(1, c.vocab, H, codes_a, scales_a);
     pack_nvfp4(codes_a, scales_a, nullptr, nullptr, c.vocab, H, false, head.w, stream);
     head.alg_bytes = alg(c.vocab, H);
@@ -454,11 +459,18 @@ struct xtg_cuda {
     input = dalloc<float>((size_t)kMaxRows * H);
     o = dalloc<float>((size_t)kMaxRows * H);
     proj = dalloc<float>((size_t)kMaxRows * (2 * Q + 2 * KV));
-    x16 = dalloc<uint32_t>((size_t)packed_blocks(H) * 4 * 64);
-    a16 = dalloc<uint32_t>((size_t)packed_blocks(Q) * 4 * 64);
-    v16 = dalloc<uint32_t>((size_t)packed_blocks(F) * 4 * 64);
+    xb = dalloc<uint8_t>((size_t)digit_bytes(H));
+    ab = dalloc<uint8_t>((size_t)digit_bytes(Q));
+    vb = dalloc<uint8_t>((size_t)digit_bytes(F));
+    auto empty_pre = [&](int k) {   // rows never written: all-zero digits that never set a slice's prescale
+      const std::vector<float> v((size_t)packed_kblocks(k) * 4 * kMaxRows, kEmptyPrescale);
+      return upload(v);
+    };
+    xb_pre = empty_pre(H);
+    ab_pre = empty_pre(Q);
+    vb_pre = empty_pre(F);
     asum = dalloc<float>((size_t)c.heads * kMaxRows);
-    vsum = dalloc<float>((size_t)packed_tiles(F, true) * kMaxRows);
+    vsum = dalloc<float>((size_t)packed_tiles(F, true) * 8 * kMaxRows);
     logits = dalloc<float>((size_t)kMaxRows * c.vocab);
     XTG_CUDA(cudaMallocHost(&logits_host, (size_t)kMaxRows * c.vocab * sizeof(float)));
     cand = dalloc<ArgCand>((size_t)packed_tiles(c.vocab, false) * kMaxRows);
@@ -466,9 +478,6 @@ struct xtg_cuda {
     argmax_val = dalloc<float>(kMaxRows);
     rope_cos = dalloc<float>(2 * kMaxRows * 64);
     rope_sin = dalloc<float>(2 * kMaxRows * 64);
-    gemv_grid_ = gemv_grid(num_sms);
-    gemv_partial = dalloc<float>((size_t)gemv_partial_floats(gemv_grid_));
-    gemv_counters = dalloc<int>((size_t)packed_tiles(c.vocab, false) + 4096);
     dev_err = dalloc<int>(1);
     XTG_CUDA(cudaMallocHost(&err_host, sizeof(int)));
     *err_host = 0;
@@ -506,21 +515,26 @@ struct xtg_cuda {
     }
   }
 
-  void gemv(const Linear& L, int epi, const uint32_t* xin, const float* sumsq, int nparts, bool pdl) {
+  GemvArgs gemv_args(const Linear& L) {
     GemvArgs a = {};
     a.w = L.w;
     a.tiles = L.tiles;
-    a.blocks = L.blocks;
-    a.x16 = xin;
+    a.kblocks = L.kblocks;
     a.m_dev = &params_dev->m;
-    a.partial = gemv_partial;
-    a.counters = gemv_counters;
     a.err = dev_err;
     a.outs = L.outs;
+    return a;
+  }
+
+  // a GEMV of activation digits (xb, xb_pre), with an optional justnorm row scale from sumsq (STORE)
+  void gemv(const Linear& L, int epi, GemvArgs a, const uint8_t* in, const float* in_pre, bool pdl,
+            const float* sumsq = nullptr, int nparts = 0) {
+    a.xb = in;
+    a.xb_pre = in_pre;
     a.sumsq = sumsq;
     a.nparts = nparts;
     mark(kClsGemv, true);
-    launch_gemv(epi, a, gemv_grid_, stream, pdl);
+    launch_gemv(epi, a, L.plan, stream, pdl);
     mark(kClsGemv, false);
   }
 
@@ -530,11 +544,12 @@ struct xtg_cuda {
     EmbedArgs ea = {};
     ea.params = params_dev;
     ea.head = head.w;
-    ea.blocks = head.blocks;
+    ea.kblocks = head.kblocks;
     ea.global = head.g0;
     ea.hidden = H;
     ea.h = h;
-    ea.x16 = x16;
+    ea.xb = xb;
+    ea.xb_pre = xb_pre;
     ea.inv_freq = inv_freq;
     ea.n_thetas = 2;
     ea.rope_cos = rope_cos;
@@ -553,7 +568,8 @@ struct xtg_cuda {
       r.lr = lr;
       r.state = state;
       r.input = input;
-      r.x16 = x16;
+      r.xb = xb;
+      r.xb_pre = xb_pre;
       mark(kClsSmall, true);
       launch_resid(r, stream, pdl);
       mark(kClsSmall, false);
@@ -561,29 +577,21 @@ struct xtg_cuda {
     auto sublayer = [&](int e) {
       const Eval& E = evals[e];
       if (E.kind == 0) {
-        GemvArgs a = {};
-        a.w = E.gu.w;
-        a.tiles = E.gu.tiles;
-        a.blocks = E.gu.blocks;
-        a.x16 = x16;
-        a.m_dev = &params_dev->m;
-        a.partial = gemv_partial;
-        a.counters = gemv_counters;
+        GemvArgs a = gemv_args(E.gu);
         a.g_gate = E.gu.g0;
         a.g_up = E.gu.g1;
         a.sg = E.sg;
         a.su = E.su;
         a.features = F;
-        a.v16 = reinterpret_cast<uint16_t*>(v16);
+        a.vb = vb;
+        a.vb_pre = vb_pre;
         a.vsum = vsum;
-        mark(kClsGemv, true);
-        launch_gemv(kEpiSwiglu, a, gemv_grid_, stream, pdl);
-        mark(kClsGemv, false);
-        gemv(E.down, kEpiStore, v16, vsum, E.gu.tiles, pdl);
+        gemv(E.gu, kEpiSwiglu, a, xb, xb_pre, pdl);
+        gemv(E.down, kEpiStore, gemv_args(E.down), vb, vb_pre, pdl, vsum, E.gu.tiles * E.gu.plan.split);
         resid(kResidSlerp, E.lr);
         return;
       }
-      gemv(E.qkvg, kEpiStore, x16, nullptr, 0, pdl);
+      gemv(E.qkvg, kEpiStore, gemv_args(E.qkvg), xb, xb_pre, pdl);
       const KvInst& K = kv[E.cache];
       AttnArgs at = {};
       at.proj = proj;
@@ -620,12 +628,13 @@ struct xtg_cuda {
       cb.gate = proj + Q + 2 * c.kv_heads * c.head_dim;
       cb.gate_ld = proj_ld;
       cb.gscale = E.gscale;
-      cb.a16 = reinterpret_cast<uint16_t*>(a16);
+      cb.ab = ab;
+      cb.ab_pre = ab_pre;
       cb.asum = asum;
       mark(kClsCombine, true);
       launch_attn_combine(cb, stream, pdl);
       mark(kClsCombine, false);
-      gemv(E.o, kEpiStore, a16, asum, c.heads, pdl);
+      gemv(E.o, kEpiStore, gemv_args(E.o), ab, ab_pre, pdl, asum, c.heads);
       resid(kResidSlerp, E.lr);
     };
     int e = 0;
@@ -638,23 +647,14 @@ struct xtg_cuda {
       }
     }
     for (int l = 0; l < c.n_out; ++l) sublayer(e++);
-    GemvArgs a = {};
-    a.w = head.w;
-    a.tiles = head.tiles;
-    a.blocks = head.blocks;
-    a.x16 = x16;
-    a.m_dev = &params_dev->m;
-    a.partial = gemv_partial;
-    a.counters = gemv_counters;
-    a.err = dev_err;
+    GemvArgs a = gemv_args(head);
+    a.outs = nullptr;
     a.g_head = head.g0;
     a.logit_scale = logit_scale;
     a.logits = logits;
     a.vocab = c.vocab;
     a.cand = cand;
-    mark(kClsGemv, true);
-    launch_gemv(kEpiHead, a, gemv_grid_, stream, pdl);
-    mark(kClsGemv, false);
+    gemv(head, kEpiHead, a, xb, xb_pre, pdl);
     mark(kClsSmall, true);
     launch_argmax(cand, head.tiles, params_dev, argmax, argmax_val, stream, pdl);
     mark(kClsSmall, false);

@@ -1,17 +1,12 @@
 // NVFP4 weights on the device: the seeded synthetic generators, the NVFP4 quantizer, and the repack from ModelOpt's
 // row layout (engine/include/xtg/kernels.h:13-20) into the GEMV's streaming layout.
 //
-// Streaming layout. A weight [n_out][k] is cut into tiles of 16 output rows and blocks of 64 inputs; block (t, b)
-// is 576 contiguous bytes, blocks in tile-major order, so that any run of blocks is one contiguous byte range:
-//   bytes   0..511  codes, 16 per lane of a warp: lane L = 4 g + tq holds, for each k16 step j = 0..3 of the block,
-//                   [row g byte tq, row g+8 byte tq, row g byte tq+4, row g+8 byte tq+4] of that step's 8 code bytes
-//                   (byte q of a step holds inputs 2q (low nibble) and 2q+1), i.e. exactly the A fragment of
-//                   mma.m16n8k16 after an e2m1x2 -> f16x2 conversion per byte;
-//   bytes 512..575  E4M3 scales, 8 per lane group g: for j = 0..3, [scale(row g, step j), scale(row g+8, step j)].
-// Rows past n_out and inputs past k are zero codes with zero scales. An interleaved pack puts 8 rows of weight A
-// (gate) in tile rows 0-7 and the same 8 rows of weight B (up) in rows 8-15, so that one lane holds gate and up of
-// the same feature after the MMA.
+// The packed layout is the tensor-core unit of fp4mma.cuh: per (128-row tile, 64-input block) 4096 code bytes in
+// the MMA's A layout and 512 E4M3 scale bytes in the scale-factor atom, units in tile-major order. Rows past n_out
+// and inputs past k are zero codes with zero scales. An interleaved pack puts 64 rows of weight A (gate) in tile rows
+// 0-63 and the same 64 rows of weight B (up) in rows 64-127, so that gate and up of a feature finish in one tile.
 #include "common.cuh"
+#include "fp4mma.cuh"
 #include "kernels.h"
 
 namespace xtg {
@@ -108,101 +103,52 @@ void quantize_nvfp4(const uint16_t* w, int n_out, int k, uint8_t* codes, uint8_t
   XTG_CUDA(cudaGetLastError());
 }
 
-// ---- repack ModelOpt rows -> streaming layout ----
+// ---- repack ModelOpt rows -> tensor-core units ----
 
-// One thread per (tile, block, lane): 16 code bytes, and for lanes 0..7 the 8 scale bytes of row group `lane`.
+// One thread per (tile, K block, tile row): the row's 32 code bytes (two 16-byte halves of the A layout) and its 4
+// scale bytes in the scale-factor atom.
 __global__ void pack_nvfp4_kernel(const uint8_t* codes_a, const uint8_t* scales_a, const uint8_t* codes_b,
-                                  const uint8_t* scales_b, int n_out, int k, int interleave, int tiles, int blocks,
+                                  const uint8_t* scales_b, int n_out, int k, int interleave, int tiles, int kblocks,
                                   uint8_t* dst) {
-  const int64_t total = (int64_t)tiles * blocks * 32;
+  const int64_t total = (int64_t)tiles * kblocks * kTileRows;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int lane = (int)(i & 31);
-    const int64_t tb = i >> 5;
-    const int t = (int)(tb / blocks), b = (int)(tb % blocks);
-    uint8_t* out = dst + tb * kBlockBytes;
-    // the source of tile row r
-    auto src = [&](int r, const uint8_t*& c, const uint8_t*& s, int& row) {
-      if (interleave) {
-        row = t * 8 + (r & 7);
-        c = r < 8 ? codes_a : codes_b;
-        s = r < 8 ? scales_a : scales_b;
-      } else {
-        row = t * 16 + r;
-        c = codes_a;
-        s = scales_a;
-      }
-    };
-    const int g = lane >> 2, tq = lane & 3;
-    uint8_t bytes[16];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int kk = b * 64 + j * 16;   // first input of the step
-#pragma unroll
-      for (int part = 0; part < 4; ++part) {
-        const int r = g + ((part & 1) ? 8 : 0);
-        const int q = tq + ((part & 2) ? 4 : 0);
-        const uint8_t* c;
-        const uint8_t* s;
-        int row;
-        src(r, c, s, row);
-        uint8_t v = 0;
-        if (row < n_out && kk + 2 * q < k) v = c[(int64_t)row * (k / 2) + kk / 2 + q];
-        (void)s;
-        bytes[4 * j + part] = v;
+    const int r = (int)(i % kTileRows);
+    const int64_t tb = i / kTileRows;
+    const int t = (int)(tb / kblocks), b = (int)(tb % kblocks);
+    const uint8_t* c = codes_a;
+    const uint8_t* sc = scales_a;
+    int row = t * kTileRows + r;
+    if (interleave) {
+      row = t * 64 + (r & 63);
+      if (r >= 64) {
+        c = codes_b;
+        sc = scales_b;
       }
     }
-    *reinterpret_cast<uint4*>(out + lane * 16) = *reinterpret_cast<const uint4*>(bytes);
-    if (lane < 8) {
-      uint8_t sb[8];
+    uint8_t* unit = dst + tb * kUnitBytes;
+    uint8_t bytes[32];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int grp = b * 4 + j;
+    for (int q = 0; q < 32; ++q) {
+      const int kk = b * kKBlock + 2 * q;
+      bytes[q] = (row < n_out && kk < k) ? c[(int64_t)row * (k / 2) + kk / 2] : 0;
+    }
+    *reinterpret_cast<uint4*>(unit + a_code_offset(r, 0)) = *reinterpret_cast<const uint4*>(bytes);
+    *reinterpret_cast<uint4*>(unit + a_code_offset(r, 32)) = *reinterpret_cast<const uint4*>(bytes + 16);
 #pragma unroll
-        for (int hi = 0; hi < 2; ++hi) {
-          const uint8_t* c;
-          const uint8_t* s;
-          int row;
-          src(lane + 8 * hi, c, s, row);
-          (void)c;
-          sb[2 * j + hi] = (row < n_out && grp * 16 < k) ? s[(int64_t)row * (k / 16) + grp] : 0;
-        }
-      }
-      *reinterpret_cast<uint2*>(out + 512 + lane * 8) = *reinterpret_cast<const uint2*>(sb);
+    for (int j = 0; j < 4; ++j) {
+      const int grp = b * 4 + j;
+      unit[kUnitCodeBytes + sf_offset(r, j)] = (row < n_out && grp * 16 < k) ? sc[(int64_t)row * (k / 16) + grp] : 0;
     }
   }
 }
 
 void pack_nvfp4(const uint8_t* codes_a, const uint8_t* scales_a, const uint8_t* codes_b, const uint8_t* scales_b,
                 int n_out, int k, bool interleave, uint8_t* dst, cudaStream_t s) {
-  const int tiles = packed_tiles(n_out, interleave), blocks = packed_blocks(k);
-  const int64_t total = (int64_t)tiles * blocks * 32;
+  XTG_REQUIRE(k % 16 == 0, "pack_nvfp4: k must be a multiple of 16");
+  const int tiles = packed_tiles(n_out, interleave), kblocks = packed_kblocks(k);
+  const int64_t total = (int64_t)tiles * kblocks * kTileRows;
   pack_nvfp4_kernel<<<grid_for(total, 256), 256, 0, s>>>(codes_a, scales_a, codes_b, scales_b, n_out, k,
-                                                         interleave ? 1 : 0, tiles, blocks, dst);
-  XTG_CUDA(cudaGetLastError());
-}
-
-// The inverse: tile rows back to ModelOpt codes / scales (debug exports, tests).
-__global__ void unpack_nvfp4_kernel(const uint8_t* src, int n_out, int k, int tiles, int blocks, uint8_t* codes,
-                                    uint8_t* scales) {
-  const int64_t total = (int64_t)n_out * (k / 16);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int row = (int)(i / (k / 16)), grp = (int)(i % (k / 16));
-    const int t = row / 16, r = row % 16, g = r & 7, hi = r >> 3;
-    const int b = grp / 4, j = grp % 4;
-    const uint8_t* blk = src + ((int64_t)t * blocks + b) * kBlockBytes;
-    scales[i] = blk[512 + g * 8 + 2 * j + hi];
-    for (int q = 0; q < 8; ++q) {
-      const int tq = q & 3, part = hi + ((q >> 2) << 1);
-      codes[(int64_t)row * (k / 2) + grp * 8 + q] = blk[(g * 4 + tq) * 16 + 4 * j + part];
-    }
-  }
-  (void)tiles;
-}
-
-void unpack_nvfp4(const uint8_t* src, int n_out, int k, uint8_t* codes, uint8_t* scales, cudaStream_t s) {
-  const int tiles = packed_tiles(n_out, false), blocks = packed_blocks(k);
-  const int64_t total = (int64_t)n_out * (k / 16);
-  unpack_nvfp4_kernel<<<grid_for(total, 256), 256, 0, s>>>(src, n_out, k, tiles, blocks, codes, scales);
+                                                         interleave ? 1 : 0, tiles, kblocks, dst);
   XTG_CUDA(cudaGetLastError());
 }
 
