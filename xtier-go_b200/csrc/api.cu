@@ -184,6 +184,11 @@ int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, ch
       launch_attention(a, s, false);
       CombineArgs cb = {};
       cb.part = part;
+      cb.q = p->q;
+      cb.k = p->k;
+      cb.v = p->v;
+      cb.scale = p->scale;
+      cb.window = p->window;
       cb.splits = splits;
       cb.heads = p->heads;
       cb.kv_heads = p->kv_heads;
@@ -277,6 +282,11 @@ int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* p, int splits, void* st
     launch_attention(a, s, false);
     CombineArgs cb = {};
     cb.part = part;
+    cb.q = p->q;
+    cb.k = p->k;
+    cb.v = p->v;
+    cb.scale = p->scale;
+    cb.window = p->window;
     cb.splits = splits;
     cb.heads = p->heads;
     cb.kv_heads = p->kv_heads;

@@ -27,38 +27,10 @@ namespace xtg {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;   // 4 warp pairs
+constexpr int kPairs = 4;
 constexpr int kQRows = 32;
 constexpr int kPartStride = kD + 2;   // m, l, acc[128]
-
-// Encode one row of 128 (a warp, 4 values per lane at e, e + 64, e + 32, e + 96) into codes and a scale; value
-// rows go to V, key rows to K (attention.h layouts).
-__device__ __forceinline__ void encode_row(const float (&x)[4], int dtype, int lane, bool value, uint8_t* kc,
-                                           uint8_t* vc, float* scales, int h, int64_t slot, int64_t slots) {
-  float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
-  amax = warp_max(amax);
-  const float top = dtype == kKvFp8 ? 448.f : 127.f;
-  const float sc = amax > 0.f ? __fdiv_rn(amax, top) : 1.f;
-  const float inv = __fdiv_rn(1.f, sc);
-  const int idx[4] = {lane, lane + 64, lane + 32, lane + 96};
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float t = __fmul_rn(x[j], inv);
-    uint8_t c;
-    if (dtype == kKvFp8) {
-      c = f32_to_e4m3(t);
-    } else {
-      float r = rintf(t);
-      r = fminf(fmaxf(r, -127.f), 127.f);
-      c = (uint8_t)(int8_t)(int)r;
-    }
-    if (value)
-      vc[v_offset(h, idx[j], slot, slots)] = c;
-    else
-      kc[k_offset(h, slot, idx[j], slots)] = c;
-  }
-  if (lane == 0) scales[(int64_t)h * slots + slot] = sc;
-}
 
 __device__ __forceinline__ void codes_to_f16(uint32_t word, int dtype, uint32_t& lo, uint32_t& hi) {
   if (dtype == kKvFp8) {
@@ -80,21 +52,15 @@ struct Stage {                    // one 64-slot chunk of one KV head, as it lie
 };
 
 struct Smem {
-  Stage stage[2][2];              // [warp pair][ring slot]
-  uint64_t bar[2][2];
+  Stage stage[kPairs];            // one chunk per warp pair; after the pair's last chunk, its softmax state
+  uint64_t bar[kPairs];
   uint4 qf[2][2][8][32];          // Q A fragments [m-tile][hi, lo][k16 step][lane]: q = hi + lo, both fp16
-  float q[kQRows][kD + 4];        // prepared queries (query row = group * activation row + head in group)
-  float k[kMaxRows][kD + 4];      // this call's keys / values (prepared)
-  float v[kMaxRows][kD + 4];
-  float rc[kMaxRows][64];          // this step's RoPE cos / sin rows
-  float rs[kMaxRows][64];
-  float qsc[4][kD];               // the q scales of this KV head's q heads
-  float mrg_m[2][16];             // half-1 warps' softmax state for the merge
-  float mrg_l[2][16];
-  float mrg_acc[2][16][kD + 4];
+  float q[kQRows][kD + 4];        // queries (query row = group * activation row + head in group)
 };
+// a pair's state in its stage after its last chunk: per query row m, l, acc[128]
+static_assert(sizeof(Stage) >= kQRows * kPartStride * sizeof(float), "stage too small for a pair's state");
 
-__global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -113,107 +79,40 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
   const uint8_t* vc = a.vc + (int64_t)kvh * kD * slots;
   const float* ks = a.ks + (int64_t)kvh * slots;
   const float* vs = a.vs + (int64_t)kvh * slots;
-  const int pair = warp >> 1;
+  const int pair = warp >> 1;   // pair p takes chunks cb + p, cb + p + 4, ...
   const uint32_t stage_bytes = 2 * 64 * kD + 2 * 64 * 4 + (a.ring ? 64 * 4 : 0);
-  // chunk c of this head into ring slot j of `pair` (its first warp's lane 0)
-  auto issue = [&](int pr, int j, int64_t c) {
-    Stage& st = sm.stage[pr][j];
-    uint64_t* bar = &sm.bar[pr][j];
-    mbar_expect_tx(bar, stage_bytes);
-    bulk_g2s(st.k, kc + c * 64 * kD, 64 * kD, bar);
-    bulk_g2s(st.v, vc + c * 64 * kD, 64 * kD, bar);
-    bulk_g2s(st.ks, ks + c * 64, 64 * 4, bar);
-    bulk_g2s(st.vs, vs + c * 64, 64 * 4, bar);
-    if (a.ring) bulk_g2s(st.pos, a.ring_pos + c * 64, 64 * 4, bar);
+  // chunk c of this head into ring slot j of `pair`, by lanes 0-4 of the pair's first warp: one bulk copy per lane
+  // (the copies of one thread complete one after another)
+  auto issue = [&](int pr, int64_t c) {
+    Stage& st = sm.stage[pr];
+    uint64_t* bar = &sm.bar[pr];
+    if (lane == 0) mbar_expect_tx(bar, stage_bytes);
+    __syncwarp();
+    if (lane == 0) bulk_g2s(st.k, kc + c * 64 * kD, 64 * kD, bar);
+    if (lane == 1) bulk_g2s(st.v, vc + c * 64 * kD, 64 * kD, bar);
+    if (lane == 2) bulk_g2s(st.ks, ks + c * 64, 64 * 4, bar);
+    if (lane == 3) bulk_g2s(st.vs, vs + c * 64, 64 * 4, bar);
+    if (lane == 4 && a.ring) bulk_g2s(st.pos, a.ring_pos + c * 64, 64 * 4, bar);
   };
-  // the cached keys and values do not depend on the previous kernel: start both pairs' first two chunks now
+  // the cached keys and values do not depend on the previous kernel: start every pair's first chunk now
   if (threadIdx.x == 0) {
-    for (int pr = 0; pr < 2; ++pr)
-      for (int j = 0; j < 2; ++j) mbar_init(&sm.bar[pr][j], 1);
+    for (int pr = 0; pr < kPairs; ++pr) mbar_init(&sm.bar[pr], 1);
     mbar_init_fence();
   }
   __syncthreads();
-  if (lane == 0 && (warp & 1) == 0) {
-    for (int j = 0; j < 2; ++j) {
-      const int64_t c = cb + pair + 2 * j;
-      if (c < ce) issue(pair, j, c);
-    }
-  }
+  if ((warp & 1) == 0 && cb + pair < ce) issue(pair, cb + pair);
   if (a.pdl) {
     pdl_launch_next();
     pdl_wait();
   }
 
-  // ---- prepare Q and this call's K / V (RoPE + justnorm + q scale in the fused step) ----
-  // (1) every vector this CTA needs lands in shared memory in one coalesced wave of 16-byte loads
-  {
-    const int nvec = kMaxRows * (group + 2);
-#pragma unroll 4
-    for (int idx = threadIdx.x; idx < nvec * 32; idx += kThreads) {
-      const int vec = idx >> 5, f4 = idx & 31;
-      const int i = vec / (group + 2), which = vec % (group + 2);
-      float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (i < m) {
-        const float* src;
-        if (a.proj) {
-          const float* row = a.proj + (int64_t)i * a.proj_ld;
-          src = which < group ? row + (int64_t)(kvh * group + which) * kD
-                              : row + (int64_t)a.heads * kD + (int64_t)(which - group) * a.kv_heads * kD + kvh * kD;
-        } else {
-          src = which < group ? a.q + ((int64_t)i * a.heads + kvh * group + which) * kD
-                              : (which == group ? a.k : a.v) + ((int64_t)i * a.kv_heads + kvh) * kD;
-        }
-        val = reinterpret_cast<const float4*>(src)[f4];
-      }
-      float* dst = which < group ? sm.q[i * group + which] : (which == group ? sm.k[i] : sm.v[i]);
-      reinterpret_cast<float4*>(dst)[f4] = val;
-    }
-    if (a.proj) {
-      for (int idx = threadIdx.x; idx < kMaxRows * 16; idx += kThreads) {
-        reinterpret_cast<float4*>(&sm.rc[0][0])[idx] = reinterpret_cast<const float4*>(a.rope_cos)[idx];
-        reinterpret_cast<float4*>(&sm.rs[0][0])[idx] = reinterpret_cast<const float4*>(a.rope_sin)[idx];
-      }
-      for (int idx = threadIdx.x; idx < group * 32; idx += kThreads)
-        reinterpret_cast<float4*>(&sm.qsc[0][0])[idx] =
-            reinterpret_cast<const float4*>(a.qscale + (int64_t)kvh * group * kD)[idx];
-    }
-  }
-  __syncthreads();
-  // (2) per vector (a warp each): RoPE and justnorm for q and k, q times its scales; this call's K / V rows into the
-  // cache (the first split)
-  if (a.proj || a.store) {
-    const int nvec = kMaxRows * (group + 2);
-    for (int vec = warp; vec < nvec; vec += kThreads / 32) {
-      const int i = vec / (group + 2), which = vec % (group + 2);
-      if (i >= m) continue;
-      float* x = which < group ? sm.q[i * group + which] : (which == group ? sm.k[i] : sm.v[i]);
-      float v0 = x[lane], v1 = x[lane + 64], v2 = x[lane + 32], v3 = x[lane + 96];
-      if (a.proj && which <= group) {
-        const float c0 = sm.rc[i][lane], s0 = sm.rs[i][lane], c1 = sm.rc[i][lane + 32], s1 = sm.rs[i][lane + 32];
-        const float r0 = v0 * c0 - v1 * s0, r1 = v1 * c0 + v0 * s0;
-        const float r2 = v2 * c1 - v3 * s1, r3 = v3 * c1 + v2 * s1;
-        const float f = 1.f / sqrtf(warp_sum(r0 * r0 + r1 * r1 + r2 * r2 + r3 * r3) + 1e-6f);
-        v0 = r0 * f;
-        v1 = r1 * f;
-        v2 = r2 * f;
-        v3 = r3 * f;
-        if (which < group) {
-          v0 *= sm.qsc[which][lane];
-          v1 *= sm.qsc[which][lane + 64];
-          v2 *= sm.qsc[which][lane + 32];
-          v3 *= sm.qsc[which][lane + 96];
-        }
-        x[lane] = v0;
-        x[lane + 64] = v1;
-        x[lane + 32] = v2;
-        x[lane + 96] = v3;
-      }
-      if (a.store && split == 0 && which >= group) {
-        const int64_t p = pos0 + i, slot = a.ring ? p % slots : p;
-        const float xv[4] = {v0, v1, v2, v3};
-        encode_row(xv, a.dtype, lane, which != group, a.kc, a.vc, which == group ? a.ks : a.vs, kvh, slot, slots);
-      }
-    }
+  // ---- the queries of this KV head (prepared: RoPE, justnorm, q scale), one coalesced wave of 16-byte loads ----
+  for (int idx = threadIdx.x; idx < kQRows * 32; idx += kThreads) {
+    const int r = idx >> 5, f4 = idx & 31, i = r / group, hg = r % group;
+    float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < m && r < kMaxRows * group)
+      val = reinterpret_cast<const float4*>(a.q + ((int64_t)i * a.heads + kvh * group + hg) * kD)[f4];
+    reinterpret_cast<float4*>(sm.q[r])[f4] = val;
   }
   __syncthreads();
   // A fragments of Q, split q = hi + lo (both fp16) so that the scores keep ~22 bits: step st, lane tq reads head
@@ -235,7 +134,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     sm.qf[t2][1][st][l] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
   __syncthreads();
-  const int mt = warp & 1, half = pair;
+  const int mt = warp & 1;
   const bool active = (16 * mt) / group < m;   // this warp's query rows hold at least one activation row
   // the activation rows of this lane's two query rows and their positions
   const int arow0 = (16 * mt + g) / group, arow1 = (16 * mt + g + 8) / group;
@@ -365,78 +264,19 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     }
   };
 
-  // this call's own keys j < m: scores in FP32 from the prepared rows (the reference attends to them unquantized);
-  // lane (g, tq) scores keys 2 tq, 2 tq + 1 for query rows 16 mt + g and + 8, then P V on the tensor cores (keys
-  // 0..15 of one k16 step, the upper 8 empty)
-  auto own_rows = [&]() {
-    const float* q0 = sm.q[16 * mt + g];
-    const float* q1 = sm.q[16 * mt + g + 8];
-    float sc[2][2];
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      const int j = 2 * tq + c;
-      const float* kr = sm.k[j];
-      float d0 = 0.f, d1 = 0.f;
-#pragma unroll 4
-      for (int e = 0; e < kD; e += 4) {
-        const float4 kv = *reinterpret_cast<const float4*>(kr + e);
-        const float4 a4 = *reinterpret_cast<const float4*>(q0 + e);
-        const float4 b4 = *reinterpret_cast<const float4*>(q1 + e);
-        d0 += a4.x * kv.x + a4.y * kv.y + a4.z * kv.z + a4.w * kv.w;
-        d1 += b4.x * kv.x + b4.y * kv.y + b4.z * kv.z + b4.w * kv.w;
-      }
-      const bool vis0 = live0 && j < m && j <= arow0 && (a.window == 0 || arow0 - j < a.window);
-      const bool vis1 = live1 && j < m && j <= arow1 && (a.window == 0 || arow1 - j < a.window);
-      sc[0][c] = vis0 ? d0 * a.scale : -INFINITY;
-      sc[1][c] = vis1 ? d1 * a.scale : -INFINITY;
-    }
-    float mx0 = fmaxf(sc[0][0], sc[0][1]), mx1 = fmaxf(sc[1][0], sc[1][1]);
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float new_m0 = fmaxf(run_m0, mx0), new_m1 = fmaxf(run_m1, mx1);
-    const float corr0 = new_m0 == -INFINITY ? 1.f : expf(run_m0 - new_m0);
-    const float corr1 = new_m1 == -INFINITY ? 1.f : expf(run_m1 - new_m1);
-    run_m0 = new_m0;
-    run_m1 = new_m1;
-    float p[2][2];
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      p[0][c] = sc[0][c] == -INFINITY ? 0.f : expf(sc[0][c] - new_m0);
-      p[1][c] = sc[1][c] == -INFINITY ? 0.f : expf(sc[1][c] - new_m1);
-    }
-    run_l0 = run_l0 * corr0 + p[0][0] + p[0][1];
-    run_l1 = run_l1 * corr1 + p[1][0] + p[1][1];
-    const uint32_t pa0 = pack_f16x2(p[0][0], p[0][1]), pa1 = pack_f16x2(p[1][0], p[1][1]);
-#pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
-      const int d = 8 * dt + g;
-      acc[dt][0] *= corr0;
-      acc[dt][1] *= corr0;
-      acc[dt][2] *= corr1;
-      acc[dt][3] *= corr1;
-      const uint32_t b0 = pack_f16x2(sm.v[2 * tq][d], sm.v[2 * tq + 1][d]);
-      mma_f16(acc[dt], pa0, pa1, 0u, 0u, b0, 0u);
-    }
-  };
-
-  // the pair's chunks cb + pair, + 2, ... through its 2-slot ring; both warps of the pair finish a slot before its
-  // refill (a 64-thread named barrier per pair), the pair's first warp refills it
+  // the pair's chunks cb + pair, + 4, ...: after each, both warps of the pair are done with the stage (a 64-thread
+  // named barrier) and the first warp refills it
   {
-    const int count = ce > cb + pair ? (int)((ce - cb - pair + 1) / 2) : 0;
+    const int count = ce > cb + pair ? (int)((ce - cb - pair + kPairs - 1) / kPairs) : 0;
     for (int i = 0; i < count; ++i) {
-      const int j = i & 1;
-      mbar_wait_bounded(&sm.bar[pair][j], (uint32_t)((i >> 1) & 1), lane == 0 ? a.err : nullptr);
-      if (active) chunk(sm.stage[pair][j], (cb + pair + 2 * (int64_t)i) * 64);
+      mbar_wait_bounded(&sm.bar[pair], (uint32_t)(i & 1), lane == 0 ? a.err : nullptr);
+      if (active) chunk(sm.stage[pair], (cb + pair + kPairs * (int64_t)i) * 64);
       asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
-      if (lane == 0 && mt == 0 && i + 2 < count) {
+      if (mt == 0 && i + 1 < count) {
         fence_proxy_async_smem();
-        issue(pair, j, cb + pair + 2 * (int64_t)(i + 2));
+        issue(pair, cb + pair + kPairs * (int64_t)(i + 1));
       }
     }
-    // this call's own keys: the last split, the first pair
-    if (active && split == a.splits - 1 && pair == 0) own_rows();
   }
   // the row sums live spread over the 4 lanes of a row
   run_l0 += __shfl_xor_sync(0xffffffffu, run_l0, 1);
@@ -444,53 +284,54 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
   run_l1 += __shfl_xor_sync(0xffffffffu, run_l1, 1);
   run_l1 += __shfl_xor_sync(0xffffffffu, run_l1, 2);
 
-  // ---- merge the two halves (warps mt and mt + 2), then write the CTA's partial per query row ----
-  if (half == 1) {
+  // ---- merge the 4 pairs' states (each in its own stage), then write the CTA's partial per query row ----
+  {
+    float* st = reinterpret_cast<float*>(&sm.stage[pair]);
+    const int qr0 = 16 * mt + g, qr1 = qr0 + 8;
     if (tq == 0) {
-      sm.mrg_m[mt][g] = run_m0;
-      sm.mrg_m[mt][g + 8] = run_m1;
-      sm.mrg_l[mt][g] = run_l0;
-      sm.mrg_l[mt][g + 8] = run_l1;
+      st[qr0 * kPartStride] = run_m0;
+      st[qr0 * kPartStride + 1] = run_l0;
+      st[qr1 * kPartStride] = run_m1;
+      st[qr1 * kPartStride + 1] = run_l1;
     }
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) {
       const int d = 8 * dt + 2 * tq;
-      sm.mrg_acc[mt][g][d] = acc[dt][0];
-      sm.mrg_acc[mt][g][d + 1] = acc[dt][1];
-      sm.mrg_acc[mt][g + 8][d] = acc[dt][2];
-      sm.mrg_acc[mt][g + 8][d + 1] = acc[dt][3];
+      st[qr0 * kPartStride + 2 + d] = acc[dt][0];
+      st[qr0 * kPartStride + 3 + d] = acc[dt][1];
+      st[qr1 * kPartStride + 2 + d] = acc[dt][2];
+      st[qr1 * kPartStride + 3 + d] = acc[dt][3];
     }
   }
   __syncthreads();
-  if (half == 0) {
-    const float om0 = sm.mrg_m[mt][g], om1 = sm.mrg_m[mt][g + 8];
-    const float ol0 = sm.mrg_l[mt][g], ol1 = sm.mrg_l[mt][g + 8];
-    const float M0 = fmaxf(run_m0, om0), M1 = fmaxf(run_m1, om1);
-    const float w0a = run_m0 == -INFINITY ? 0.f : expf(run_m0 - M0), w0b = om0 == -INFINITY ? 0.f : expf(om0 - M0);
-    const float w1a = run_m1 == -INFINITY ? 0.f : expf(run_m1 - M1), w1b = om1 == -INFINITY ? 0.f : expf(om1 - M1);
-    const int qr0 = 16 * mt + g, qr1 = qr0 + 8;
-    float* p0 = a.part + (((int64_t)kvh * a.splits + split) * kQRows + qr0) * kPartStride;
-    float* p1 = a.part + (((int64_t)kvh * a.splits + split) * kQRows + qr1) * kPartStride;
-    if (tq == 0) {
-      if (live0) {
-        p0[0] = M0;
-        p0[1] = run_l0 * w0a + ol0 * w0b;
-      }
-      if (live1) {
-        p1[0] = M1;
-        p1[1] = run_l1 * w1a + ol1 * w1b;
-      }
-    }
+  {
+    const int r = threadIdx.x >> 3, d0 = (threadIdx.x & 7) * 16;   // query row, 16 head dims
+    if (r / group < m) {
+      const float* st0 = reinterpret_cast<const float*>(&sm.stage[0]);
+      const int ss = (int)(sizeof(Stage) / sizeof(float));
+      float mp[kPairs], M = -INFINITY;
 #pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
-      const int d = 8 * dt + 2 * tq;
-      if (live0) {
-        p0[2 + d] = acc[dt][0] * w0a + sm.mrg_acc[mt][g][d] * w0b;
-        p0[3 + d] = acc[dt][1] * w0a + sm.mrg_acc[mt][g][d + 1] * w0b;
+      for (int pr = 0; pr < kPairs; ++pr) {
+        mp[pr] = st0[pr * ss + r * kPartStride];
+        M = fmaxf(M, mp[pr]);
       }
-      if (live1) {
-        p1[2 + d] = acc[dt][2] * w1a + sm.mrg_acc[mt][g + 8][d] * w1b;
-        p1[3 + d] = acc[dt][3] * w1a + sm.mrg_acc[mt][g + 8][d + 1] * w1b;
+      float w[kPairs], L = 0.f;
+#pragma unroll
+      for (int pr = 0; pr < kPairs; ++pr) {
+        w[pr] = mp[pr] == -INFINITY ? 0.f : expf(mp[pr] - M);
+        L += w[pr] == 0.f ? 0.f : st0[pr * ss + r * kPartStride + 1] * w[pr];
+      }
+      float* out = a.part + (((int64_t)kvh * a.splits + split) * kQRows + r) * kPartStride;
+      if (d0 == 0) {
+        out[0] = M;
+        out[1] = L;
+      }
+      for (int d = d0; d < d0 + 16; ++d) {
+        float o = 0.f;
+#pragma unroll
+        for (int pr = 0; pr < kPairs; ++pr)
+          if (w[pr] != 0.f) o += st0[pr * ss + r * kPartStride + 2 + d] * w[pr];
+        out[2 + d] = o;
       }
     }
   }
@@ -516,6 +357,7 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   const float* base = a.part + ((int64_t)kvh * a.splits * kQRows + qr) * kPartStride;
   const int64_t sstride = (int64_t)kQRows * kPartStride;
   // split weights exp(m_s - M) and 1 / sum_s l_s exp(m_s - M), by the first warp in a fixed order
+  __shared__ float mx_s;
   if (threadIdx.x < 32) {
     float mx = -INFINITY;
     for (int s = threadIdx.x; s < a.splits; s += 32) mx = fmaxf(mx, base[s * sstride]);
@@ -528,9 +370,39 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
       l += w == 0.f ? 0.f : base[s * sstride + 1] * w;
     }
     l = warp_sum(l);
-    if (threadIdx.x == 0) inv_l = l > 0.f ? 1.f / l : 0.f;
+    if (threadIdx.x == 0) {
+      inv_l = l;   // the cached part's sum, relative to mx
+      mx_s = mx;
+    }
   }
   __syncthreads();
+  const float wgt_max = mx_s;
+  // this call's own keys j <= i (FP32 from the prepared rows: the reference attends to them unquantized)
+  __shared__ float own_s[kMaxRows];
+  {
+    const float qd = a.q[((int64_t)i * a.heads + h) * kD + d];
+    float prod[kMaxRows];
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) prod[j] = j < m ? qd * a.k[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) prod[j] = warp_sum(prod[j]);
+    __shared__ float part_s[kD / 32][kMaxRows];
+    if ((d & 31) == 0)
+#pragma unroll
+      for (int j = 0; j < kMaxRows; ++j) part_s[d >> 5][j] = prod[j];
+    __syncthreads();
+    if (d < kMaxRows) {
+      const int j = d;
+      const bool vis = j < m && j <= i && (a.window == 0 || i - j < a.window);
+      own_s[j] = vis ? ((part_s[0][j] + part_s[1][j]) + (part_s[2][j] + part_s[3][j])) * a.scale : -INFINITY;
+    }
+  }
+  __syncthreads();
+  float own_m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kMaxRows; ++j) own_m = fmaxf(own_m, own_s[j]);
+  const float mall = fmaxf(own_m, wgt_max);
+  const float cs = wgt_max == -INFINITY ? 0.f : expf(wgt_max - mall);   // the cached part's weight
   float o = 0.f;
   int s = 0;
   for (; s + 8 <= a.splits; s += 8) {
@@ -542,7 +414,17 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   }
   for (; s < a.splits; ++s)
     if (wgt[s] != 0.f) o += base[s * sstride + 2 + d] * wgt[s];
-  o *= inv_l;
+  // merge the cached part (relative to wgt_max) and the own keys (relative to mall)
+  float lsum = inv_l * cs;
+  o *= cs;
+#pragma unroll
+  for (int j = 0; j < kMaxRows; ++j) {
+    if (own_s[j] == -INFINITY) continue;
+    const float pj = expf(own_s[j] - mall);
+    lsum += pj;
+    o += pj * a.v[((int64_t)j * a.kv_heads + kvh) * kD + d];
+  }
+  o *= lsum > 0.f ? 1.f / lsum : 0.f;
   if (a.out) {
     a.out[((int64_t)i * a.heads + h) * kD + d] = o;
     return;

@@ -34,16 +34,11 @@ struct StepParams {
 };
 
 struct AttnArgs {
-  // this call's rows: the fused step reads the QKV(G) projection rows [m][proj_ld] (q, k, v, g) and applies RoPE,
-  // justnorm and the q scale; the API form reads prepared q [m][heads][128], k / v [m][kv_heads][128]
-  const float* proj;
-  int proj_ld;
+  // this call's rows, prepared (RoPE, justnorm, q scale): q [m][heads][128], k / v [m][kv_heads][128] (already in the
+  // cache at positions pos0 .. pos0 + m - 1; the scores against them use these unquantized rows)
   const float* q;
   const float* k;
   const float* v;
-  const float* qscale;      // [heads * 128]
-  const float* rope_cos;    // [8][64] for positions pos0 .. pos0 + 7
-  const float* rope_sin;
   // the cache (layout in attention.cu)
   uint8_t* kc;
   uint8_t* vc;
@@ -53,7 +48,6 @@ struct AttnArgs {
   int ring;
   const int32_t* ring_pos;  // [slots] for a ring
   int dtype;
-  int store;                // write this call's K / V rows (fused step)
   int window;
   float scale;
   const StepParams* params; // m and pos0 on the device, or null: m, pos0
@@ -68,6 +62,12 @@ struct AttnArgs {
 
 struct CombineArgs {
   const float* part;
+  // this call's rows (as in AttnArgs): the own-key scores are computed here in FP32
+  const float* q;
+  const float* k;
+  const float* v;
+  float scale;
+  int window;
   int splits, heads, kv_heads;
   const StepParams* params;
   int m;

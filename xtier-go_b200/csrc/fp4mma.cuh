@@ -114,6 +114,13 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// store a float into CTA `rank`'s copy of the shared array `local` points into
+__device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, float v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
 // store 8 floats into CTA `rank`'s copy of the shared array `local` points into (16-byte aligned)
 __device__ __forceinline__ void st_cluster_f32x8(float* local, uint32_t rank, const float (&v)[8]) {
   uint32_t remote;

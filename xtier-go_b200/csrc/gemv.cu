@@ -19,6 +19,7 @@
 // every launch.
 #include <algorithm>
 
+#include "attention.h"
 #include "common.cuh"
 #include "fp4mma.cuh"
 #include "kernels.h"
@@ -78,6 +79,75 @@ __device__ __forceinline__ void wait_bar(uint64_t* bar, uint32_t parity, int* er
 
 // first row (STORE) or 16-feature group (SwiGLU) a cluster rank finishes: ceil(n * rank / split)
 __device__ __forceinline__ int share_begin(int n, int rank, int split) { return (n * rank + split - 1) / split; }
+
+// Block-wide (two halves of 128 threads) sum / max of v over the threads of each half; scratch: 8 floats.
+__device__ __forceinline__ float half_reduce(float v, bool is_max, float* scratch, int tid) {
+  v = is_max ? warp_max(v) : warp_sum(v);
+  __syncthreads();
+  if ((tid & 31) == 0) scratch[tid >> 5] = v;
+  __syncthreads();
+  const float* w = scratch + 4 * (tid >> 7);
+  return is_max ? fmaxf(fmaxf(w[0], w[1]), fmaxf(w[2], w[3])) : ((w[0] + w[1]) + (w[2] + w[3]));
+}
+
+// kEpiQkv, after the cluster's partials met: this rank's activation rows of tile t (one head), two rows at a time
+// (threads 0-127 and 128-255, thread = head dim)
+__device__ __forceinline__ void qkv_finish(const GemvArgs& a, const float* red, float* scratch, int t, int srank,
+                                           int S, int m, int tid) {
+  const int i0 = share_begin(8, srank, S), i1 = share_begin(8, srank + 1, S), nil = (8 + S - 1) / S;
+  const int type = t < a.q_tiles ? 0 : t < a.q_tiles + a.kv_tiles ? 1 : t < a.q_tiles + 2 * a.kv_tiles ? 2 : 3;
+  const int d = tid & 127, hf = tid >> 7;
+  float* xs = scratch + 8;   // [2][128]
+  const int64_t pos0 = *a.pos0_dev;
+  for (int ib = i0; ib < i1; ib += 2) {
+    const int i = ib + hf;
+    const bool row = i < i1, live = row && i < m;
+    float x = 0.f;
+    if (row)
+      for (int c = 0; c < S; ++c) x += red[(c * nil + (i - i0)) * kTileRows + d];
+    if (type == 3) {   // the gate: stored as kEpiStore does
+      const TileOut o = a.outs[t];
+      if (live && d < o.rows) o.y[(int64_t)i * o.ld + d] = x;
+      continue;
+    }
+    float r = x;
+    if (type <= 1) {   // NeoX RoPE on (d, d + 64), then justnorm over the head
+      xs[hf * 128 + d] = x;
+      __syncthreads();
+      const int e = d & 63, ir = row ? i : 0;
+      const float c = a.rope_cos[ir * 64 + e], sn = a.rope_sin[ir * 64 + e];
+      const float other = xs[hf * 128 + (d ^ 64)];
+      r = d < 64 ? x * c - other * sn : x * c + other * sn;
+      const float f = 1.f / sqrtf(half_reduce(r * r, false, scratch, tid) + 1e-6f);
+      r *= f;
+    }
+    if (type == 0) {
+      if (live) a.q_out[((int64_t)i * a.q_tiles + t) * 128 + d] = r * a.qscale[t * 128 + d];
+      continue;
+    }
+    // k / v: the prepared row, and its codes and scale in the cache (the KvCache::store rule)
+    const int h = t - a.q_tiles - (type == 2 ? a.kv_tiles : 0);
+    const float amax = half_reduce(fabsf(r), true, scratch, tid);
+    if (!live) continue;
+    (type == 1 ? a.k_out : a.v_out)[((int64_t)i * a.kv_tiles + h) * 128 + d] = r;
+    const float top = a.dtype == kKvFp8 ? 448.f : 127.f;
+    const float sc = amax > 0.f ? __fdiv_rn(amax, top) : 1.f;
+    const float tq = __fmul_rn(r, __fdiv_rn(1.f, sc));
+    uint8_t code;
+    if (a.dtype == kKvFp8) {
+      code = f32_to_e4m3(tq);
+    } else {
+      const float q = fminf(fmaxf(rintf(tq), -127.f), 127.f);
+      code = (uint8_t)(int8_t)(int)q;
+    }
+    const int64_t p = pos0 + i, slot = a.ring ? p % a.slots : p;
+    if (type == 1)
+      a.kc[k_offset(h, slot, d, a.slots)] = code;
+    else
+      a.vc[v_offset(h, d, slot, a.slots)] = code;
+    if (d == 0) (type == 1 ? a.ks : a.vs)[(int64_t)h * a.slots + slot] = sc;
+  }
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ Params P) {
@@ -317,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
           g = r < 64 ? o.global_lo : o.global_hi;
 #pragma unroll
         for (int i = 0; i < 8; ++i) y[i] *= g;
-        if (EPI == kEpiStore && S == 1) {
+        if (EPI == kEpiStore && S == 1 && EPI != kEpiQkv) {
           if (r < o.rows)
 #pragma unroll
             for (int i = 0; i < 8; ++i)
@@ -325,7 +395,20 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         } else {
           // push this CTA's part of row r to the cluster rank that finishes it
           int owner, slot;
-          if constexpr (EPI == kEpiStore) {
+          if constexpr (EPI == kEpiQkv) {   // ranks finish activation rows (whole heads)
+            const int nil = (8 + S - 1) / S;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int ow = (i * S) / 8;
+              float* dst = red + ((srank * nil) + (i - share_begin(8, ow, S))) * kTileRows + r;
+              if (S == 1)
+                *dst = y[i];
+              else
+                st_cluster_f32(dst, (uint32_t)ow, y[i]);
+            }
+            owner = -1;
+            slot = 0;
+          } else if constexpr (EPI == kEpiStore) {
             owner = (r * S) / kTileRows;
             slot = r - share_begin(kTileRows, owner, S);
           } else {
@@ -335,7 +418,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
             slot = (r >= 64 ? 16 * (g1 - g0) : 0) + f - 16 * g0;
           }
           float* dst = red + (srank * P.rpr + slot) * 8;
-          if (S == 1) {
+          if (owner < 0) {
+          } else if (S == 1) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) dst[i] = y[i];
           } else {
@@ -347,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   }
   // ---- split tiles meet in the cluster; SwiGLU pairs gate and up rows ----
   __syncthreads();
-  if (EPI != kEpiHead && (S > 1 || EPI == kEpiSwiglu)) {
+  if (EPI != kEpiHead && (S > 1 || EPI == kEpiSwiglu || EPI == kEpiQkv)) {
     if (S > 1) cluster_sync();
     const int t = t0;
     auto total = [&](int slot, int i) {
@@ -355,7 +439,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
       for (int c = 0; c < S; ++c) v += red[(c * P.rpr + slot) * 8 + i];
       return v;
     };
-    if constexpr (EPI == kEpiStore) {
+    if constexpr (EPI == kEpiQkv) {
+      qkv_finish(a, red, vsq, t, srank, S, m, tid);
+    } else if constexpr (EPI == kEpiStore) {
       const TileOut o = a.outs[t];
       const int r0 = share_begin(kTileRows, srank, S), nr = share_begin(kTileRows, srank + 1, S) - r0;
       for (int p = tid; p < nr * 8; p += kThreads) {
@@ -457,7 +543,8 @@ GemvPlan plan_gemv(int tiles, int kblocks, int num_sms, int max_split, int max_t
 
 void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bool pdl) {
   XTG_REQUIRE(epi != kEpiHead || p.split == 1, "gemv: the head epilogue takes whole tiles");
-  XTG_REQUIRE(epi != kEpiSwiglu || p.tiles_per_cta == 1, "gemv: the SwiGLU epilogue takes one tile per CTA");
+  XTG_REQUIRE((epi != kEpiSwiglu && epi != kEpiQkv) || p.tiles_per_cta == 1,
+              "gemv: the SwiGLU and q|k|v epilogues take one tile per CTA");
   XTG_REQUIRE(p.split >= 1 && p.split <= 8 && p.ring >= 1 && p.ring <= kMaxRing, "gemv: bad plan");
   Params P = {};
   P.a = a;
@@ -478,8 +565,11 @@ void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, 
   const int cols = tmem_columns(p.tiles_per_cta, P.slice_max, p.ring);
   XTG_REQUIRE(cols <= 512, "gemv: the K slice's scales do not fit in TMEM");
   P.tmem_cols = cols <= 256 ? 256 : 512;
-  static bool attr_set[3] = {false, false, false};
-  auto* k = epi == kEpiStore ? gemv_kernel<kEpiStore> : epi == kEpiSwiglu ? gemv_kernel<kEpiSwiglu> : gemv_kernel<kEpiHead>;
+  static bool attr_set[4] = {false, false, false, false};
+  auto* k = epi == kEpiStore    ? gemv_kernel<kEpiStore>
+            : epi == kEpiSwiglu ? gemv_kernel<kEpiSwiglu>
+            : epi == kEpiQkv    ? gemv_kernel<kEpiQkv>
+                                : gemv_kernel<kEpiHead>;
   if (!attr_set[epi]) {
     XTG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
     attr_set[epi] = true;

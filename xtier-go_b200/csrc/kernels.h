@@ -39,7 +39,7 @@ struct TileOut {
   float global_lo, global_hi;
 };
 
-enum GemvEpi { kEpiStore = 0, kEpiSwiglu = 1, kEpiHead = 2 };
+enum GemvEpi { kEpiStore = 0, kEpiSwiglu = 1, kEpiHead = 2, kEpiQkv = 3 };
 
 struct ArgCand {   // the best logit of a tile for one activation row
   float v;
@@ -67,6 +67,25 @@ struct GemvArgs {
   uint8_t* vb;               // [tiles][2048]
   float* vb_pre;             // [tiles * 4][8]
   float* vsum;               // [tiles * split][8]: sums of v^2 over the features each CTA finishes
+  // kEpiQkv: the q | k | v | g projection of an attention sublayer, one 128-row tile per head (head_dim 128): tiles
+  // [0, q_tiles) are q heads, then kv_tiles k heads, kv_tiles v heads, and the gate tiles (stored through `outs` as
+  // kEpiStore does). q: RoPE, justnorm, times its q scale; k: RoPE, justnorm; k and v rows go into the KV cache and
+  // out prepared (the attention's own rows).
+  int q_tiles, kv_tiles;
+  const float* rope_cos;     // [8][64] of this layer's theta (positions pos0 ..)
+  const float* rope_sin;
+  const float* qscale;       // [q_tiles * 128]
+  float* q_out;              // [8][q_tiles][128]
+  float* k_out;              // [8][kv_tiles][128]
+  float* v_out;
+  uint8_t* kc;
+  uint8_t* vc;
+  float* ks;
+  float* vs;
+  int64_t slots;
+  int ring;
+  int dtype;
+  const int64_t* pos0_dev;
   // kEpiHead
   float g_head;
   const float* logit_scale;  // [vocab]

@@ -209,6 +209,7 @@ struct xtg_cuda {
   // (the O projection's input), v (the down projection's input)
   uint8_t *xb = nullptr, *ab = nullptr, *vb = nullptr;
   float *xb_pre = nullptr, *ab_pre = nullptr, *vb_pre = nullptr;
+  float *q_prep = nullptr, *k_new = nullptr, *v_new = nullptr;   // this step's prepared q / k / v rows
   float *asum = nullptr, *vsum = nullptr, *logits = nullptr, *logits_host = nullptr, *argmax_val = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   int32_t* argmax = nullptr;
@@ -450,7 +451,6 @@ struct xtg_cuda {
 
   void alloc_activations() {
     const int H = c.hidden, F = c.ffn, Q = c.heads * c.head_dim, KV = c.kv_heads * c.head_dim;
-    (void)KV;
     params_dev = dalloc<StepParams>(1);
     XTG_CUDA(cudaMallocHost(&params_host, sizeof(StepParams)));
     std::memset(params_host, 0, sizeof(StepParams));
@@ -469,6 +469,9 @@ struct xtg_cuda {
     xb_pre = empty_pre(H);
     ab_pre = empty_pre(Q);
     vb_pre = empty_pre(F);
+    q_prep = dalloc<float>((size_t)kMaxRows * Q);
+    k_new = dalloc<float>((size_t)kMaxRows * KV);
+    v_new = dalloc<float>((size_t)kMaxRows * KV);
     asum = dalloc<float>((size_t)c.heads * kMaxRows);
     vsum = dalloc<float>((size_t)packed_tiles(F, true) * 8 * kMaxRows);
     logits = dalloc<float>((size_t)kMaxRows * c.vocab);
@@ -481,9 +484,10 @@ struct xtg_cuda {
     dev_err = dalloc<int>(1);
     XTG_CUDA(cudaMallocHost(&err_host, sizeof(int)));
     *err_host = 0;
-    // one CTA per SM: a global layer's splits fill the SMs once
-    splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, num_sms / c.kv_heads);
-    splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, std::min<int>(c.ring / 64, 8));
+    // one attention CTA per SM, 4 chunks of 64 slots at a time (a warp pair each): a global layer's splits fill the
+    // SMs once, a ring's take one chunk per warp pair
+    splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, std::min(256, num_sms / c.kv_heads));
+    splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, (int)((c.ring / 64 + 3) / 4));
     part = dalloc<float>((size_t)attention_part_floats(c.kv_heads, std::max(splits_g, splits_r)));
     ring_pos_dev = dalloc<int32_t>(c.ring);
     ring_pos.assign(c.ring, -1);
@@ -591,14 +595,31 @@ struct xtg_cuda {
         resid(kResidSlerp, E.lr);
         return;
       }
-      gemv(E.qkvg, kEpiStore, gemv_args(E.qkvg), xb, xb_pre, pdl);
       const KvInst& K = kv[E.cache];
+      {
+        GemvArgs g = gemv_args(E.qkvg);
+        g.q_tiles = c.heads;
+        g.kv_tiles = c.kv_heads;
+        g.rope_cos = rope_cos + E.theta * kMaxRows * 64;
+        g.rope_sin = rope_sin + E.theta * kMaxRows * 64;
+        g.qscale = E.qscale;
+        g.q_out = q_prep;
+        g.k_out = k_new;
+        g.v_out = v_new;
+        g.kc = K.kc;
+        g.vc = K.vc;
+        g.ks = K.ks;
+        g.vs = K.vs;
+        g.slots = K.slots;
+        g.ring = K.ring ? 1 : 0;
+        g.dtype = c.kv_dtype;
+        g.pos0_dev = &params_dev->pos0;
+        gemv(E.qkvg, kEpiQkv, g, xb, xb_pre, pdl);
+      }
       AttnArgs at = {};
-      at.proj = proj;
-      at.proj_ld = proj_ld;
-      at.qscale = E.qscale;
-      at.rope_cos = rope_cos + E.theta * kMaxRows * 64;
-      at.rope_sin = rope_sin + E.theta * kMaxRows * 64;
+      at.q = q_prep;
+      at.k = k_new;
+      at.v = v_new;
       at.kc = K.kc;
       at.vc = K.vc;
       at.ks = K.ks;
@@ -607,7 +628,6 @@ struct xtg_cuda {
       at.ring = K.ring ? 1 : 0;
       at.ring_pos = ring_pos_dev;
       at.dtype = c.kv_dtype;
-      at.store = 1;
       at.window = K.ring ? c.window : 0;
       at.scale = 1.f / std::sqrt((float)c.head_dim);
       at.params = params_dev;
@@ -621,6 +641,11 @@ struct xtg_cuda {
       mark(kClsAttn, false);
       CombineArgs cb = {};
       cb.part = part;
+      cb.q = q_prep;
+      cb.k = k_new;
+      cb.v = v_new;
+      cb.scale = at.scale;
+      cb.window = at.window;
       cb.splits = at.splits;
       cb.heads = c.heads;
       cb.kv_heads = c.kv_heads;
