@@ -343,9 +343,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
 constexpr int kMaxSplits = 256;
 
 __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
-  __shared__ float red[32];
+  constexpr int kRegSplits = 32;   // partials held in registers (the rest are read in a second pass)
   __shared__ float wgt[kMaxSplits];
-  __shared__ float inv_l;
+  __shared__ float cached[2];      // the splits' max m and their sum of l relative to it
+  __shared__ float part_s[kD / 32][kMaxRows];
   const int i = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
   if (a.pdl) {
     pdl_launch_next();
@@ -356,8 +357,19 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   const int group = a.heads / a.kv_heads, kvh = h / group, qr = i * group + h % group;
   const float* base = a.part + ((int64_t)kvh * a.splits * kQRows + qr) * kPartStride;
   const int64_t sstride = (int64_t)kQRows * kPartStride;
-  // split weights exp(m_s - M) and 1 / sum_s l_s exp(m_s - M), by the first warp in a fixed order
-  __shared__ float mx_s;
+  // every independent load first: this thread's dim of every split's partial, of q, of this call's keys / values
+  const int ns = a.splits < kRegSplits ? a.splits : kRegSplits;
+  float acc_s[kRegSplits];
+#pragma unroll
+  for (int s = 0; s < kRegSplits; ++s) acc_s[s] = s < ns ? base[s * sstride + 2 + d] : 0.f;
+  const float qd = a.q[((int64_t)i * a.heads + h) * kD + d];
+  float kj[kMaxRows], vj[kMaxRows];
+#pragma unroll
+  for (int j = 0; j < kMaxRows; ++j) {
+    kj[j] = j < m ? a.k[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
+    vj[j] = j < m ? a.v[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
+  }
+  // split weights exp(m_s - M) and sum_s l_s exp(m_s - M), by the first warp in a fixed order
   if (threadIdx.x < 32) {
     float mx = -INFINITY;
     for (int s = threadIdx.x; s < a.splits; s += 32) mx = fmaxf(mx, base[s * sstride]);
@@ -371,58 +383,44 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
     }
     l = warp_sum(l);
     if (threadIdx.x == 0) {
-      inv_l = l;   // the cached part's sum, relative to mx
-      mx_s = mx;
+      cached[0] = mx;
+      cached[1] = l;
     }
   }
-  __syncthreads();
-  const float wgt_max = mx_s;
-  // this call's own keys j <= i (FP32 from the prepared rows: the reference attends to them unquantized)
-  __shared__ float own_s[kMaxRows];
+  // this call's own keys j <= i, scored in FP32 from the prepared rows (the reference attends to them unquantized)
   {
-    const float qd = a.q[((int64_t)i * a.heads + h) * kD + d];
     float prod[kMaxRows];
 #pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) prod[j] = j < m ? qd * a.k[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
-#pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) prod[j] = warp_sum(prod[j]);
-    __shared__ float part_s[kD / 32][kMaxRows];
+    for (int j = 0; j < kMaxRows; ++j) prod[j] = warp_sum(qd * kj[j]);
     if ((d & 31) == 0)
 #pragma unroll
       for (int j = 0; j < kMaxRows; ++j) part_s[d >> 5][j] = prod[j];
-    __syncthreads();
-    if (d < kMaxRows) {
-      const int j = d;
-      const bool vis = j < m && j <= i && (a.window == 0 || i - j < a.window);
-      own_s[j] = vis ? ((part_s[0][j] + part_s[1][j]) + (part_s[2][j] + part_s[3][j])) * a.scale : -INFINITY;
-    }
   }
   __syncthreads();
-  float own_m = -INFINITY;
+  float own_s[kMaxRows], own_m = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kMaxRows; ++j) own_m = fmaxf(own_m, own_s[j]);
+  for (int j = 0; j < kMaxRows; ++j) {
+    const bool vis = j < m && j <= i && (a.window == 0 || i - j < a.window);
+    own_s[j] = vis ? ((part_s[0][j] + part_s[1][j]) + (part_s[2][j] + part_s[3][j])) * a.scale : -INFINITY;
+    own_m = fmaxf(own_m, own_s[j]);
+  }
+  const float wgt_max = cached[0];
   const float mall = fmaxf(own_m, wgt_max);
   const float cs = wgt_max == -INFINITY ? 0.f : expf(wgt_max - mall);   // the cached part's weight
   float o = 0.f;
-  int s = 0;
-  for (; s + 8 <= a.splits; s += 8) {
-    float v[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = wgt[s + j] != 0.f ? base[(s + j) * sstride + 2 + d] : 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o += v[j] * wgt[s + j];
-  }
-  for (; s < a.splits; ++s)
+  for (int s = 0; s < kRegSplits; ++s)
+    if (s < ns) o += acc_s[s] * wgt[s];
+  for (int s = kRegSplits; s < a.splits; ++s)
     if (wgt[s] != 0.f) o += base[s * sstride + 2 + d] * wgt[s];
   // merge the cached part (relative to wgt_max) and the own keys (relative to mall)
-  float lsum = inv_l * cs;
+  float lsum = cached[1] * cs;
   o *= cs;
 #pragma unroll
   for (int j = 0; j < kMaxRows; ++j) {
-    if (own_s[j] == -INFINITY) continue;
-    const float pj = expf(own_s[j] - mall);
+    const float pj = own_s[j] == -INFINITY ? 0.f : expf(own_s[j] - mall);
     lsum += pj;
-    o += pj * a.v[((int64_t)j * a.kv_heads + kvh) * kD + d];
+    o += pj * vj[j];
   }
   o *= lsum > 0.f ? 1.f / lsum : 0.f;
   if (a.out) {
@@ -432,6 +430,7 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   const int col = h * kD + d;
   const float gt = a.gate[(int64_t)i * a.gate_ld + col];
   o *= 1.f / (1.f + expf(-gt * a.gscale[col]));
+  __shared__ float red[32];
   const float ss = block_sum(o * o, red);
   if (d == 0) a.asum[h * kMaxRows + i] = ss;
   // the O projection's input: this head's 8 groups of 16 as B digits (warp 0, a quad per group)
