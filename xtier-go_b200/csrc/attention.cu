@@ -192,20 +192,45 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
       }
     }
     float mx0 = -INFINITY, mx1 = -INFINITY;
+    // a chunk whose every slot is visible to every row of the warp needs no per-score mask (the common case)
+    int pmin = kpos[0], pmax = kpos[0];
 #pragma unroll
-    for (int T = 0; T < 8; ++T) {
+    for (int kk = 1; kk < 16; ++kk) {
+      pmin = min(pmin, kpos[kk]);
+      pmax = max(pmax, kpos[kk]);
+    }
+    const bool all_vis =
+        __all_sync(0xffffffffu, live0 && live1 && pmin >= 0 && pmax < pos0 &&
+                                    (a.window == 0 || max(t0, t1) - pmin < a.window));
+    if (all_vis) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
-        const int p = kpos[kk];
-        const bool ok = p >= 0 && p < pos0;
-        const bool vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
-        const bool vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
-        const float f = ksc[kk] * a.scale;
-        s[T][c] = vis0 ? s[T][c] * f : -INFINITY;
-        s[T][2 + c] = vis1 ? s[T][2 + c] * f : -INFINITY;
-        mx0 = fmaxf(mx0, s[T][c]);
-        mx1 = fmaxf(mx1, s[T][2 + c]);
+      for (int T = 0; T < 8; ++T) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
+          const float f = ksc[kk] * a.scale;
+          s[T][c] *= f;
+          s[T][2 + c] *= f;
+          mx0 = fmaxf(mx0, s[T][c]);
+          mx1 = fmaxf(mx1, s[T][2 + c]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int T = 0; T < 8; ++T) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
+          const int p = kpos[kk];
+          const bool ok = p >= 0 && p < pos0;
+          const bool vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
+          const bool vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
+          const float f = ksc[kk] * a.scale;
+          s[T][c] = vis0 ? s[T][c] * f : -INFINITY;
+          s[T][2 + c] = vis1 ? s[T][2 + c] * f : -INFINITY;
+          mx0 = fmaxf(mx0, s[T][c]);
+          mx1 = fmaxf(mx1, s[T][2 + c]);
+        }
       }
     }
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -213,8 +238,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
     const float new_m0 = fmaxf(run_m0, mx0), new_m1 = fmaxf(run_m1, mx1);
-    const float corr0 = new_m0 == -INFINITY ? 1.f : expf(run_m0 - new_m0);
-    const float corr1 = new_m1 == -INFINITY ? 1.f : expf(run_m1 - new_m1);
+    const float corr0 = new_m0 == -INFINITY ? 1.f : __expf(run_m0 - new_m0);
+    const float corr1 = new_m1 == -INFINITY ? 1.f : __expf(run_m1 - new_m1);
     run_m0 = new_m0;
     run_m1 = new_m1;
     run_l0 *= corr0;
@@ -233,8 +258,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
-        p[c] = s[T][c] == -INFINITY ? 0.f : expf(s[T][c] - new_m0);
-        p[2 + c] = s[T][2 + c] == -INFINITY ? 0.f : expf(s[T][2 + c] - new_m1);
+        p[c] = s[T][c] == -INFINITY ? 0.f : __expf(s[T][c] - new_m0);
+        p[2 + c] = s[T][2 + c] == -INFINITY ? 0.f : __expf(s[T][2 + c] - new_m1);
         run_l0 += p[c];
         run_l1 += p[2 + c];
         p[c] *= vsc[kk];

@@ -249,15 +249,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) pmin = fminf(pmin, __shfl_xor_sync(0xffffffffu, pmin, o));
     if (lane == 0) pslice[i] = pmin;
-  }
-  if (EPI == kEpiStore && tid < 8) {
-    float t = 1.f;
-    if (a.sumsq) {
-      t = 0.f;
-      for (int q = 0; q < a.nparts; ++q) t += a.sumsq[q * 8 + tid];
-      t = 1.f / sqrtf(t + 1e-6f);
+    if (EPI == kEpiStore) {
+      // the row's sum of squares over the producer's parts: lane l takes parts l, l + 32, ... (independent loads),
+      // then a butterfly over the warp (a fixed order)
+      float t = 1.f;
+      if (a.sumsq) {
+        t = 0.f;
+        for (int q = lane; q < a.nparts; q += 32) t += a.sumsq[q * 8 + i];
+        t = warp_sum(t);
+        t = 1.f / sqrtf(t + 1e-6f);
+      }
+      if (lane == 0) rowscale[i] = t;
     }
-    rowscale[tid] = t;
   }
   wait_bar(bfull, 0, a.err);
   __syncthreads();
@@ -292,7 +295,42 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     // ---- MMA issuer: the slice's activation scales go to TMEM once; per unit the weight scales, then the MMA.
     // One thread issues everything, so the per-unit work is kept to a few instructions: indices advance
     // incrementally and the descriptors by their start-address field (16-byte units, no carry out of 14 bits). ----
-    if (lane == 0) {
+    if (lane == 0 && nt == 1) {
+      // One tile (every split CTA): unit u is K block u, each B block's scales are used once and go to TMEM just
+      // before its MMA, and a full stage is straight-line code (no per-unit branch: the issue loop stays short).
+      tc_fence_after();
+      const uint32_t ring_addr = smem_u32(ringbuf), b_addr = smem_u32(bbuf);
+      const uint32_t sfb0 = tbase + kAccCols, sfa0 = sfb0 + 4 * (uint32_t)nkb;
+      const uint64_t da0 = a_desc(ring_addr), dsfa0 = sf_desc(ring_addr + kUnitCodeBytes), db0 = a_desc(b_addr);
+      const uint64_t dsfb0 = sf_desc(b_addr + kBCodeBytes);
+      auto unit = [&](uint32_t ui, uint32_t kbi) {
+        tc_cp_sf(sfb0 + 4 * kbi, dsfb0 + kbi * (kBBlockBytes >> 4));
+        tc_cp_sf(sfa0 + 4 * ui, dsfa0 + ui * (kUnitBytes >> 4));
+        tc_mma_fp4(tbase, da0 + ui * (kUnitBytes >> 4), db0 + kbi * (kBBlockBytes >> 4), sfa0 + 4 * ui,
+                   sfb0 + 4 * kbi, kbi > 0 ? 1u : 0u);
+      };
+      int slot = 0;
+      uint32_t phase = 0;
+      for (int st = 0; st < nstages; ++st) {
+        wait_bar(&full[slot], phase, a.err);
+        tc_fence_after();
+        const uint32_t u0 = (uint32_t)(slot * kStageUnits), kb0 = (uint32_t)(st * kStageUnits);
+        const int cnt = nunits - st * kStageUnits;
+        if (cnt >= kStageUnits) {
+#pragma unroll
+          for (int idx = 0; idx < kStageUnits; ++idx) unit(u0 + idx, kb0 + idx);
+        } else {
+          for (int idx = 0; idx < cnt; ++idx) unit(u0 + idx, kb0 + idx);
+        }
+        tc_commit(&empty[slot]);
+        if (++slot == ring) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      }
+      tc_commit(&accfull[0]);
+      tc_commit(done);
+    } else if (lane == 0) {
       tc_fence_after();
       const uint32_t ring_addr = smem_u32(ringbuf), b_addr = smem_u32(bbuf);
       const uint32_t acc_cols = nt > 1 ? 2 * kAccCols : kAccCols;
