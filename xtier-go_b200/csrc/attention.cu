@@ -372,21 +372,33 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   __shared__ float wgt[kMaxSplits];
   __shared__ float cached[2];      // the splits' max m and their sum of l relative to it
   __shared__ float part_s[kD / 32][kMaxRows];
+  __shared__ float ml[2][kMaxSplits];   // every split's m and l
   const int i = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int col = h * kD + d;
+  // the gate's scale is a parameter: loaded before the dependency wait
+  const float gsc = a.out ? 0.f : a.gscale[col];
+  const int m = a.params ? a.params->m : a.m;
   if (a.pdl) {
     pdl_launch_next();
     pdl_wait();
   }
-  const int m = a.params ? a.params->m : a.m;
   if (i >= m) return;
   const int group = a.heads / a.kv_heads, kvh = h / group, qr = i * group + h % group;
   const float* base = a.part + ((int64_t)kvh * a.splits * kQRows + qr) * kPartStride;
   const int64_t sstride = (int64_t)kQRows * kPartStride;
-  // every independent load first: this thread's dim of every split's partial, of q, of this call's keys / values
+  // every independent load in one wave: this thread's dim of every split's partial, the m and l of splits d and
+  // d + 128, q, this call's keys / values, the gate
   const int ns = a.splits < kRegSplits ? a.splits : kRegSplits;
   float acc_s[kRegSplits];
 #pragma unroll
   for (int s = 0; s < kRegSplits; ++s) acc_s[s] = s < ns ? base[s * sstride + 2 + d] : 0.f;
+  float mls[2][2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int sp = d + u * kD;
+    mls[u][0] = sp < a.splits ? base[sp * sstride] : -INFINITY;
+    mls[u][1] = sp < a.splits ? base[sp * sstride + 1] : 0.f;
+  }
   const float qd = a.q[((int64_t)i * a.heads + h) * kD + d];
   float kj[kMaxRows], vj[kMaxRows];
 #pragma unroll
@@ -394,17 +406,27 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
     kj[j] = j < m ? a.k[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
     vj[j] = j < m ? a.v[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
   }
+  const float gt = a.out ? 0.f : a.gate[(int64_t)i * a.gate_ld + col];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int sp = d + u * kD;
+    if (sp < a.splits) {
+      ml[0][sp] = mls[u][0];
+      ml[1][sp] = mls[u][1];
+    }
+  }
+  __syncthreads();
   // split weights exp(m_s - M) and sum_s l_s exp(m_s - M), by the first warp in a fixed order
   if (threadIdx.x < 32) {
     float mx = -INFINITY;
-    for (int s = threadIdx.x; s < a.splits; s += 32) mx = fmaxf(mx, base[s * sstride]);
+    for (int s = threadIdx.x; s < a.splits; s += 32) mx = fmaxf(mx, ml[0][s]);
     mx = warp_max(mx);
     float l = 0.f;
     for (int s = threadIdx.x; s < a.splits; s += 32) {
-      const float ms = base[s * sstride];
+      const float ms = ml[0][s];
       const float w = ms == -INFINITY ? 0.f : expf(ms - mx);
       wgt[s] = w;
-      l += w == 0.f ? 0.f : base[s * sstride + 1] * w;
+      l += w == 0.f ? 0.f : ml[1][s] * w;
     }
     l = warp_sum(l);
     if (threadIdx.x == 0) {
@@ -452,9 +474,7 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
     a.out[((int64_t)i * a.heads + h) * kD + d] = o;
     return;
   }
-  const int col = h * kD + d;
-  const float gt = a.gate[(int64_t)i * a.gate_ld + col];
-  o *= 1.f / (1.f + expf(-gt * a.gscale[col]));
+  o *= 1.f / (1.f + expf(-gt * gsc));
   __shared__ float red[32];
   const float ss = block_sum(o * o, red);
   if (d == 0) a.asum[h * kMaxRows + i] = ss;

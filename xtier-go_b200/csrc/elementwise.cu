@@ -101,111 +101,148 @@ __device__ __forceinline__ float2 block_sum2(float x, float y, float2* red) {
   return t;
 }
 
-// One CTA per activation row: the residual updates. All norms are justnorm: x / sqrt(sum x^2 + 1e-6). Each thread
-// holds kPer elements (k = thread + j * blockDim) in registers.
+// One CTA per activation row: the residual updates. All norms are justnorm: x / sqrt(sum x^2 + 1e-6). Thread t holds
+// the 4 consecutive elements 4 c .. 4 c + 3 of each of its chunks c = t + j * blockDim (j < kChunks) in registers, so
+// that the 4 threads of a quad hold one 16-input group and digitize it straight from registers.
 constexpr int kResidThreads = 1024;
-constexpr int kPer = 8;   // hidden <= 8192
+constexpr int kChunks = 2;   // hidden <= 8192
+
+__device__ __forceinline__ float4 ld4(const float* p, int c, bool ok) {
+  return ok ? reinterpret_cast<const float4*>(p)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+__device__ __forceinline__ void st4(float* p, int c, const float (&v)[4]) {
+  reinterpret_cast<float4*>(p)[c] = make_float4(v[0], v[1], v[2], v[3]);
+}
 
 __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a) {
   __shared__ float2 red[32];
-  extern __shared__ float rowbuf[];   // [hidden]
   const int r = blockIdx.x, H = a.hidden;
+  bool ok[kChunks];
+  int ch[kChunks];
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    ch[j] = (int)threadIdx.x + j * kResidThreads;
+    ok[j] = 4 * ch[j] < H;
+  }
+  // the slerp's per-dimension rate is a parameter: loaded before the dependency wait
+  float lr[kChunks][4];
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    const float4 l4 = ld4(a.lr, ch[j], a.mode == kResidSlerp && ok[j]);
+    lr[j][0] = l4.x; lr[j][1] = l4.y; lr[j][2] = l4.z; lr[j][3] = l4.w;
+  }
+  const int m = a.params ? a.params->m : a.m;
   if (a.pdl) {
     pdl_launch_next();
     pdl_wait();
   }
-  const int m = a.params ? a.params->m : a.m;
   float* h = a.h + (int64_t)r * H;
+  float v[kChunks][4];
   if (r >= m) {
-    digitize_row(rowbuf, H, r, true, a.xb, a.xb_pre, kUnitNorm);
-    return;
-  }
-  float v[kPer];
-  if (a.mode == kResidSlerp) {
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
+  } else if (a.mode == kResidSlerp) {
     const float* o = a.o + (int64_t)r * H;
-    float hv[kPer], ov[kPer];
+    float hv[kChunks][4], ov[kChunks][4];
     float sa = 0.f, sb = 0.f;
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int k = threadIdx.x + j * kResidThreads;
-      hv[j] = k < H ? h[k] : 0.f;
-      ov[j] = k < H ? o[k] : 0.f;
+    for (int j = 0; j < kChunks; ++j) {
+      const float4 h4 = ld4(h, ch[j], ok[j]), o4 = ld4(o, ch[j], ok[j]);
+      hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
+      ov[j][0] = o4.x; ov[j][1] = o4.y; ov[j][2] = o4.z; ov[j][3] = o4.w;
     }
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      sa += hv[j] * hv[j];
-      sb += ov[j] * ov[j];
-    }
+    for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        sa += hv[j][c] * hv[j][c];
+        sb += ov[j][c] * ov[j][c];
+      }
     const float2 n2 = block_sum2(sa, sb, red);
     const float fa = 1.f / sqrtf(n2.x + 1e-6f), fb = 1.f / sqrtf(n2.y + 1e-6f);
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int k = threadIdx.x + j * kResidThreads;
-      const float ya = hv[j] * fa, yb = ov[j] * fb;
-      v[j] = k < H ? ya + a.lr[k] * (yb - ya) : 0.f;
-      ss += v[j] * v[j];
-    }
+    for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float ya = hv[j][c] * fa, yb = ov[j][c] * fb;
+        v[j][c] = ya + lr[j][c] * (yb - ya);
+        ss += v[j][c] * v[j][c];
+      }
     const float f = 1.f / sqrtf(block_sum2(ss, 0.f, red).x + 1e-6f);
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) v[j] *= f;
+    for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) v[j][c] *= f;
   } else {
     float* st = a.state + (int64_t)r * H;
     float* in = a.input + (int64_t)r * H;
-    float hv[kPer], iv[kPer];
+    float hv[kChunks][4], iv[kChunks][4];
 #pragma unroll
-    for (int j = 0; j < kPer; ++j) {
-      const int k = threadIdx.x + j * kResidThreads;
-      hv[j] = k < H ? h[k] : 0.f;
-      iv[j] = (k < H && a.mode != kResidLoopBegin) ? in[k] : 0.f;
+    for (int j = 0; j < kChunks; ++j) {
+      const float4 h4 = ld4(h, ch[j], ok[j]), i4 = ld4(in, ch[j], ok[j] && a.mode != kResidLoopBegin);
+      hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
+      iv[j][0] = i4.x; iv[j][1] = i4.y; iv[j][2] = i4.z; iv[j][3] = i4.w;
     }
     if (a.mode == kResidLoopBegin) {   // input = state = h
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int k = threadIdx.x + j * kResidThreads;
-        if (k < H) {
-          st[k] = hv[j];
-          in[k] = hv[j];
+      for (int j = 0; j < kChunks; ++j) {
+        if (ok[j]) {
+          st4(st, ch[j], hv[j]);
+          st4(in, ch[j], hv[j]);
         }
-        iv[j] = hv[j];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) iv[j][c] = hv[j][c];
       }
     } else {   // the loop that ends: state = justnorm(h)
       float s = 0.f;
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) s += hv[j] * hv[j];
+      for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s += hv[j][c] * hv[j][c];
       const float f = 1.f / sqrtf(block_sum2(s, 0.f, red).x + 1e-6f);
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int k = threadIdx.x + j * kResidThreads;
-        hv[j] *= f;
-        if (k < H) st[k] = hv[j];
+      for (int j = 0; j < kChunks; ++j) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) hv[j][c] *= f;
+        if (ok[j]) st4(st, ch[j], hv[j]);
       }
     }
     if (a.mode == kResidLoopEnd) {   // h = state
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) v[j] = hv[j];
+      for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) v[j][c] = hv[j][c];
     } else {   // a loop begins: h = justnorm(state + input)
       float s = 0.f;
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        v[j] = hv[j] + iv[j];
-        s += v[j] * v[j];
-      }
+      for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          v[j][c] = hv[j][c] + iv[j][c];
+          s += v[j][c] * v[j][c];
+        }
       const float f = 1.f / sqrtf(block_sum2(s, 0.f, red).x + 1e-6f);
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) v[j] *= f;
-    }
-  }
+      for (int j = 0; j < kChunks; ++j)
 #pragma unroll
-  for (int j = 0; j < kPer; ++j) {
-    const int k = threadIdx.x + j * kResidThreads;
-    if (k < H) {
-      h[k] = v[j];
-      rowbuf[k] = v[j];
+        for (int c = 0; c < 4; ++c) v[j][c] *= f;
     }
   }
-  __syncthreads();
-  digitize_row(rowbuf, H, r, false, a.xb, a.xb_pre, kUnitNorm);
+  // the new h, and its digits: the quad of threads 4 g .. 4 g + 3 of chunk j holds group g + 256 j
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    if (r < m && ok[j]) st4(h, ch[j], v[j]);
+    if (j * kResidThreads < H / 4) {   // whole warps take part in the quad's shuffles
+      uint32_t code[kDigits], sf[kDigits];
+      const float p = digitize16_quad(v[j], code, sf, kUnitNorm);
+      if (ok[j]) {
+        const int g = ch[j] >> 2, t = ch[j] & 3;
+        store_digits_quad(a.xb + (int64_t)(g >> 2) * kBBlockBytes, r, g & 3, t, code, sf);
+        if (t == 0) a.xb_pre[(int64_t)g * 8 + r] = p;
+      }
+    }
+  }
 }
 
 __global__ void argmax_kernel(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out,
@@ -347,8 +384,8 @@ void launch_embed(const EmbedArgs& a_in, cudaStream_t s, bool pdl) {
 void launch_resid(const ResidArgs& a_in, cudaStream_t s, bool pdl) {
   ResidArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
-  XTG_REQUIRE(a.hidden <= kPer * kResidThreads, "resid: hidden above 8192");
-  launch_pdl(resid_kernel, dim3(kMaxRows), dim3(kResidThreads), a, s, pdl, (size_t)a.hidden * sizeof(float));
+  XTG_REQUIRE(a.hidden <= 4 * kChunks * kResidThreads && a.hidden % 64 == 0, "resid: hidden a multiple of 64, at most 8192");
+  launch_pdl(resid_kernel, dim3(kMaxRows), dim3(kResidThreads), a, s, pdl, 0);
 }
 
 void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out, float* out_val,

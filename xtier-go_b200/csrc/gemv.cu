@@ -90,23 +90,36 @@ __device__ __forceinline__ float half_reduce(float v, bool is_max, float* scratc
   return is_max ? fmaxf(fmaxf(w[0], w[1]), fmaxf(w[2], w[3])) : ((w[0] + w[1]) + (w[2] + w[3]));
 }
 
+// What the q|k|v finish of one thread reads from memory other than the cluster's partials, loaded long before the
+// partials meet: the position, the q scale of its head dim, the gate tile's output, and the RoPE factors of its rows
+// (at most 4: rows i0 + hf, i0 + hf + 2, ...).
+struct QkvPre {
+  int64_t pos0;
+  float qscale;
+  TileOut out;
+  float cs[4], sn[4];
+};
+
 // kEpiQkv, after the cluster's partials met: this rank's activation rows of tile t (one head), two rows at a time
 // (threads 0-127 and 128-255, thread = head dim)
-__device__ __forceinline__ void qkv_finish(const GemvArgs& a, const float* red, float* scratch, int t, int srank,
-                                           int S, int m, int tid) {
+__device__ __forceinline__ void qkv_finish(const GemvArgs& a, const QkvPre& pre, const float* red, float* scratch,
+                                           int t, int srank, int S, int m, int tid) {
   const int i0 = share_begin(8, srank, S), i1 = share_begin(8, srank + 1, S), nil = (8 + S - 1) / S;
   const int type = t < a.q_tiles ? 0 : t < a.q_tiles + a.kv_tiles ? 1 : t < a.q_tiles + 2 * a.kv_tiles ? 2 : 3;
   const int d = tid & 127, hf = tid >> 7;
   float* xs = scratch + 8;   // [2][128]
-  const int64_t pos0 = *a.pos0_dev;
-  for (int ib = i0; ib < i1; ib += 2) {
+  const int64_t pos0 = pre.pos0;
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int ib = i0 + 2 * it;
+    if (ib >= i1) break;
     const int i = ib + hf;
     const bool row = i < i1, live = row && i < m;
     float x = 0.f;
     if (row)
       for (int c = 0; c < S; ++c) x += red[(c * nil + (i - i0)) * kTileRows + d];
     if (type == 3) {   // the gate: stored as kEpiStore does
-      const TileOut o = a.outs[t];
+      const TileOut& o = pre.out;
       if (live && d < o.rows) o.y[(int64_t)i * o.ld + d] = x;
       continue;
     }
@@ -114,15 +127,14 @@ __device__ __forceinline__ void qkv_finish(const GemvArgs& a, const float* red, 
     if (type <= 1) {   // NeoX RoPE on (d, d + 64), then justnorm over the head
       xs[hf * 128 + d] = x;
       __syncthreads();
-      const int e = d & 63, ir = row ? i : 0;
-      const float c = a.rope_cos[ir * 64 + e], sn = a.rope_sin[ir * 64 + e];
+      const float c = pre.cs[it], sn = pre.sn[it];
       const float other = xs[hf * 128 + (d ^ 64)];
       r = d < 64 ? x * c - other * sn : x * c + other * sn;
       const float f = 1.f / sqrtf(half_reduce(r * r, false, scratch, tid) + 1e-6f);
       r *= f;
     }
     if (type == 0) {
-      if (live) a.q_out[((int64_t)i * a.q_tiles + t) * 128 + d] = r * a.qscale[t * 128 + d];
+      if (live) a.q_out[((int64_t)i * a.q_tiles + t) * 128 + d] = r * pre.qscale;
       continue;
     }
     // k / v: the prepared row, and its codes and scale in the cache (the KvCache::store rule)
@@ -225,11 +237,50 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     for (int st = 0; st < ring && st < nstages; ++st) issue_stage(st);
   __syncwarp();
 
+  // Loads that do not depend on the previous kernel (parameters no kernel of the step writes) go out before the
+  // dependency wait, so that the finish after the MMAs does not wait for memory.
+  const int m = a.m_dev ? *a.m_dev : a.m;
+  float sgv[4] = {0.f, 0.f, 0.f, 0.f}, suv[4] = {0.f, 0.f, 0.f, 0.f};   // kEpiSwiglu: this thread's features
+  TileOut ofin = {};                                                    // kEpiStore: the tile's output
+  QkvPre qpre = {};
+  if constexpr (EPI == kEpiSwiglu) {
+    const int g0 = share_begin(4, srank, S), g1 = share_begin(4, srank + 1, S);
+    const int quad = tid >> 2, qt = tid & 3, gl = quad >> 3;
+    if (quad < (g1 - g0) * 8) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int f = t0 * 64 + 16 * (g0 + gl) + 4 * qt + c;
+        if (f < a.features) {
+          sgv[c] = a.sg[f];
+          suv[c] = a.su[f];
+        }
+      }
+    }
+  } else if constexpr (EPI == kEpiStore) {
+    if (a.outs) ofin = a.outs[t0];
+  } else if constexpr (EPI == kEpiQkv) {
+    qpre.pos0 = *a.pos0_dev;
+    if (t0 < a.q_tiles) qpre.qscale = a.qscale[t0 * 128 + (tid & 127)];
+    if (t0 >= a.q_tiles + 2 * a.kv_tiles && a.outs) qpre.out = a.outs[t0];
+  }
   if (a.pdl) {
     pdl_launch_next();
     pdl_wait();
   }
-  const int m = a.m_dev ? *a.m_dev : a.m;
+  if constexpr (EPI == kEpiQkv) {
+    // RoPE factors (written by the step's first kernel): q and k heads, this thread's rows
+    if (t0 < a.q_tiles + a.kv_tiles) {
+      const int i0 = share_begin(8, srank, S), i1 = share_begin(8, srank + 1, S), e = tid & 63;
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int i = i0 + 2 * it + (tid >> 7);
+        if (i < i1) {
+          qpre.cs[it] = a.rope_cos[i * 64 + e];
+          qpre.sn[it] = a.rope_sin[i * 64 + e];
+        }
+      }
+    }
+  }
 
   // ---- the B operand of this CTA's K slice: the producer's digits, brought to one prescale per row ----
   // (a thread other than the weight producer issues the copy, so that it does not queue behind the weight stages)
@@ -372,6 +423,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     for (int i = 0; i < 8; ++i) inv[i] = 1.f / pslice[i];
     for (int j = 0; j < nt; ++j) {
       const int acc = j & 1, t = t0 + j;
+      // the tile's output description (or logit scale) is loaded before the wait, off the MMAs' critical path
+      TileOut o = {};
+      float ls = 0.f;
+      if constexpr (EPI == kEpiHead) {
+        const int row = t * kTileRows + r;
+        ls = row < a.vocab ? a.logit_scale[row] * a.g_head : 0.f;
+      } else if constexpr (EPI != kEpiSwiglu) {
+        if (a.outs) o = a.outs[t];
+      }
       wait_bar(&accfull[acc], (uint32_t)(j >> 1) & 1u, a.err);
       tc_fence_after();
       float d[kDigitRows];
@@ -389,7 +449,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
       if constexpr (EPI == kEpiHead) {
         const int row = t * kTileRows + r;
         const bool ok = row < a.vocab;
-        const float ls = ok ? a.logit_scale[row] * a.g_head : 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           float l = ok ? y[i] * ls : -INFINITY;
@@ -417,7 +476,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
       } else {
-        const TileOut o = a.outs ? a.outs[t] : TileOut{};
         float g;
         if constexpr (EPI == kEpiSwiglu)
           g = r < 64 ? a.g_gate : a.g_up;
@@ -478,9 +536,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
       return v;
     };
     if constexpr (EPI == kEpiQkv) {
-      qkv_finish(a, red, vsq, t, srank, S, m, tid);
+      qkv_finish(a, qpre, red, vsq, t, srank, S, m, tid);
     } else if constexpr (EPI == kEpiStore) {
-      const TileOut o = a.outs[t];
+      const TileOut& o = ofin;
       const int r0 = share_begin(kTileRows, srank, S), nr = share_begin(kTileRows, srank + 1, S) - r0;
       for (int p = tid; p < nr * 8; p += kThreads) {
         const int i = p / nr, rl = p % nr, r = r0 + rl;
@@ -498,8 +556,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         for (int c = 0; c < 4; ++c) {
           const int fl = 16 * gl + 4 * qt + c, f = t * 64 + 16 * g + 4 * qt + c;
           if (f < a.features && i < m) {
-            const float z = total(fl, i) * a.sg[f];
-            const float u = total(nf + fl, i) * a.su[f];
+            const float z = total(fl, i) * sgv[c];
+            const float u = total(nf + fl, i) * suv[c];
             v[c] = z / (1.f + expf(-z)) * u;
           }
           sq += v[c] * v[c];
