@@ -10,14 +10,16 @@
 // position p is visible to the row at t when 0 <= p < pos0 (and t - p < window for a sliding layer); this call's
 // own key j is visible to own row i when j <= i (and i - j < window).
 //
-// One CTA per (split of the slots, KV head), 4 warps: warp w takes query rows 16 (w & 1) .. +15 -- a query row is
-// (activation row, q head of this KV head), 8 x 4 = 32 rows, so the 4 q heads sharing a KV head read it once -- and
-// the warp pair w >> 1 takes 64-slot chunks pair, pair + 2, ... of the split through its own 2-stage ring. Both products run on mma.m16n8k16: int8 codes become f16 exactly
-// (1152 + b as a half, less 1152), FP8 codes by cvt.rn.f16x2.e4m3x2; Q (after RoPE, justnorm, q scale) is rounded
-// once to fp16; scores are scaled per key by its K scale in FP32, probabilities times the key's V scale are the
-// fp16 A operand of PV. Two permutations make every load contiguous: the head dimension inside a k16 step (lane tq
-// reads 32 contiguous bytes of a K row, Q's fragments use the same order) and the slots inside a 64-slot chunk
-// (lane tq owns slots 16 tq .. 16 tq + 15 in both products).
+// One CTA per (split of the slots, KV head), 8 warps, two CTAs per SM. Every warp takes part in every 64-slot chunk:
+// warp w takes query rows 16 (w & 1) .. +15 -- a query row is (activation row, q head of this KV head), 8 x 4 = 32
+// rows, so the 4 q heads sharing a KV head read it once -- and the chunk's keys 16 (w >> 1) .. +15, so that a chunk
+// costs each warp a quarter of its products and the chunks stream through a 4-stage ring. Each warp keeps its own
+// online-softmax state over its keys; the 4 key quarters merge at the end. Both products run on mma.m16n8k16: int8
+// codes become f16 exactly (1152 + b as a half, less 1152), FP8 codes by cvt.rn.f16x2.e4m3x2; Q (after RoPE,
+// justnorm, q scale) is split once into fp16 hi + lo; scores are scaled per key by its K scale in FP32, probabilities
+// times the key's V scale are the fp16 A operand of PV. Two permutations make every load contiguous: the head
+// dimension inside a k16 step (lane tq reads 32 contiguous bytes of a K row, Q's fragments use the same order) and
+// the keys inside a warp's quarter (lane tq owns keys 4 tq .. 4 tq + 3 in both products).
 #include "attention.h"
 #include "common.cuh"
 #include "fp4mma.cuh"
@@ -27,8 +29,9 @@ namespace xtg {
 namespace {
 
 constexpr int kD = 128;
-constexpr int kThreads = 256;   // 4 warp pairs
-constexpr int kPairs = 4;
+constexpr int kThreads = 256;   // 8 warps: (row half) x (key quarter)
+constexpr int kQuarters = 4;    // key quarters of a chunk
+constexpr int kStages = 4;      // chunks in flight
 constexpr int kQRows = 32;
 constexpr int kPartStride = kD + 2;   // m, l, acc[128]
 
@@ -52,15 +55,16 @@ struct Stage {                    // one 64-slot chunk of one KV head, as it lie
 };
 
 struct Smem {
-  Stage stage[kPairs];            // one chunk per warp pair; after the pair's last chunk, its softmax state
-  uint64_t bar[kPairs];
+  Stage stage[kStages];           // the chunk ring; after the last chunk, key quarter j's softmax state in stage[j]
+  uint64_t full[kStages], empty[kStages];
   uint4 qf[2][2][8][32];          // Q A fragments [m-tile][hi, lo][k16 step][lane]: q = hi + lo, both fp16
   float q[kQRows][kD + 4];        // queries (query row = group * activation row + head in group)
 };
-// a pair's state in its stage after its last chunk: per query row m, l, acc[128]
-static_assert(sizeof(Stage) >= kQRows * kPartStride * sizeof(float), "stage too small for a pair's state");
+// a key quarter's state after the last chunk: per query row m, l, acc[128]
+static_assert(sizeof(Stage) >= kQRows * kPartStride * sizeof(float), "stage too small for a quarter's state");
+static_assert(kStages >= kQuarters, "the quarters' states live in the stages");
 
-__global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -75,17 +79,18 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
   const int64_t span = a.ring ? slots : pos0;
   const int64_t nchunks = (span + 63) / 64;
   const int64_t cb = nchunks * split / a.splits, ce = nchunks * (split + 1) / a.splits;
+  const int nc = (int)(ce - cb);
   const uint8_t* kc = a.kc + (int64_t)kvh * slots * kD;
   const uint8_t* vc = a.vc + (int64_t)kvh * kD * slots;
   const float* ks = a.ks + (int64_t)kvh * slots;
   const float* vs = a.vs + (int64_t)kvh * slots;
-  const int pair = warp >> 1;   // pair p takes chunks cb + p, cb + p + 4, ...
   const uint32_t stage_bytes = 2 * 64 * kD + 2 * 64 * 4 + (a.ring ? 64 * 4 : 0);
-  // chunk c of this head into ring slot j of `pair`, by lanes 0-4 of the pair's first warp: one bulk copy per lane
-  // (the copies of one thread complete one after another)
-  auto issue = [&](int pr, int64_t c) {
-    Stage& st = sm.stage[pr];
-    uint64_t* bar = &sm.bar[pr];
+  // chunk i of this CTA into stage i % kStages, by lanes 0-4 of warp 0: one bulk copy per lane (the copies of one
+  // thread complete one after another)
+  auto issue = [&](int i) {
+    Stage& st = sm.stage[i % kStages];
+    uint64_t* bar = &sm.full[i % kStages];
+    const int64_t c = cb + i;
     if (lane == 0) mbar_expect_tx(bar, stage_bytes);
     __syncwarp();
     if (lane == 0) bulk_g2s(st.k, kc + c * 64 * kD, 64 * kD, bar);
@@ -94,13 +99,17 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
     if (lane == 3) bulk_g2s(st.vs, vs + c * 64, 64 * 4, bar);
     if (lane == 4 && a.ring) bulk_g2s(st.pos, a.ring_pos + c * 64, 64 * 4, bar);
   };
-  // the cached keys and values do not depend on the previous kernel: start every pair's first chunk now
+  // the cached keys and values do not depend on the previous kernel: the first chunks go out now
   if (threadIdx.x == 0) {
-    for (int pr = 0; pr < kPairs; ++pr) mbar_init(&sm.bar[pr], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], kThreads / 32);
+    }
     mbar_init_fence();
   }
   __syncthreads();
-  if ((warp & 1) == 0 && cb + pair < ce) issue(pair, cb + pair);
+  if (warp == 0)
+    for (int i = 0; i < kStages && i < nc; ++i) issue(i);
   if (a.pdl) {
     pdl_launch_next();
     pdl_wait();
@@ -134,8 +143,8 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
     sm.qf[t2][1][st][l] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
   }
   __syncthreads();
-  const int mt = warp & 1;
-  const bool active = (16 * mt) / group < m;   // this warp's query rows hold at least one activation row
+  const int mt = warp & 1, kq = warp >> 1;   // this warp's query rows 16 mt .. + 15 and chunk keys 16 kq .. + 15
+  const bool active = (16 * mt) / group < m;   // its query rows hold at least one activation row
   // the activation rows of this lane's two query rows and their positions
   const int arow0 = (16 * mt + g) / group, arow1 = (16 * mt + g + 8) / group;
   const int t0 = pos0 + arow0, t1 = pos0 + arow1;
@@ -146,18 +155,21 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
   for (int dt = 0; dt < 16; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.f;
   float run_m0 = -INFINITY, run_m1 = -INFINITY, run_l0 = 0.f, run_l1 = 0.f;
 
-  // one 64-key chunk of the cache (slot base c0) from its shared-memory stage
+  // This warp's 16 keys of a chunk (slot base c0) from its stage. The MMA k index of the PV product and the keys
+  // are permuted so that lane tq owns the 4 consecutive keys 16 kq + 4 tq .. + 3: k = 2 tq + {0, 1} are keys
+  // 4 tq + {0, 1}, k = 2 tq + 8 + {0, 1} keys 4 tq + {2, 3}. The score tile T (n8) column 2 tq + c is then key
+  // 4 tq + 2 T + c, and the K row that lane g supplies to tile T is key 4 ((g >> 1) & 3) + 2 T + (g & 1).
   auto chunk = [&](const Stage& stg, int64_t c0) {
-    // ---- S = Q K^T: 8 n8-tiles, tile T = 2 j + ab holds chunk slots 16 (n >> 1) + 4 j + (n & 1) + 2 ab ----
-    float s[8][4];
+    // ---- S = Q K^T over 2 n8 tiles x 8 k16 steps, q = hi + lo ----
+    float s[2][4];
 #pragma unroll
-    for (int T = 0; T < 8; ++T) s[T][0] = s[T][1] = s[T][2] = s[T][3] = 0.f;
+    for (int T = 0; T < 2; ++T) s[T][0] = s[T][1] = s[T][2] = s[T][3] = 0.f;
 #pragma unroll
     for (int hs = 0; hs < 2; ++hs) {   // head dims 32 tq + 16 hs .. + 15: k16 steps 4 hs .. 4 hs + 3
-      uint4 kw[8];
+      uint4 kw[2];
 #pragma unroll
-      for (int T = 0; T < 8; ++T) {
-        const int key = 16 * (g >> 1) + 4 * (T >> 1) + (g & 1) + 2 * (T & 1);
+      for (int T = 0; T < 2; ++T) {
+        const int key = 16 * kq + 4 * ((g >> 1) & 3) + 2 * T + (g & 1);
         kw[T] = *reinterpret_cast<const uint4*>(stg.k + key * kD + 16 * ((2 * tq + hs) ^ swz_k(key)));
       }
 #pragma unroll
@@ -165,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
         const int st = 4 * hs + sub;
         const uint4 qh = sm.qf[mt][0][st][lane], ql = sm.qf[mt][1][st][lane];
 #pragma unroll
-        for (int T = 0; T < 8; ++T) {
+        for (int T = 0; T < 2; ++T) {
           const uint32_t word = sub == 0 ? kw[T].x : sub == 1 ? kw[T].y : sub == 2 ? kw[T].z : kw[T].w;
           uint32_t b0, b1;
           codes_to_f16(word, a.dtype, b0, b1);
@@ -174,63 +186,33 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
         }
       }
     }
-    // ---- scale, mask, online softmax: this lane's keys are chunk slots 16 tq + kk, kk = 4 j + 2 ab + {0, 1} ----
-    float ksc[16], vsc[16];
-    int kpos[16];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float4 kq = *reinterpret_cast<const float4*>(stg.ks + 16 * tq + 4 * q);
-      const float4 vq = *reinterpret_cast<const float4*>(stg.vs + 16 * tq + 4 * q);
-      ksc[4 * q] = kq.x; ksc[4 * q + 1] = kq.y; ksc[4 * q + 2] = kq.z; ksc[4 * q + 3] = kq.w;
-      vsc[4 * q] = vq.x; vsc[4 * q + 1] = vq.y; vsc[4 * q + 2] = vq.z; vsc[4 * q + 3] = vq.w;
-      if (a.ring) {
-        const int4 pq = *reinterpret_cast<const int4*>(stg.pos + 16 * tq + 4 * q);
-        kpos[4 * q] = pq.x; kpos[4 * q + 1] = pq.y; kpos[4 * q + 2] = pq.z; kpos[4 * q + 3] = pq.w;
-      } else {
-#pragma unroll
-        for (int r = 0; r < 4; ++r) kpos[4 * q + r] = (int)c0 + 16 * tq + 4 * q + r;
-      }
-    }
-    float mx0 = -INFINITY, mx1 = -INFINITY;
-    // a chunk whose every slot is visible to every row of the warp needs no per-score mask (the common case)
-    int pmin = kpos[0], pmax = kpos[0];
-#pragma unroll
-    for (int kk = 1; kk < 16; ++kk) {
-      pmin = min(pmin, kpos[kk]);
-      pmax = max(pmax, kpos[kk]);
-    }
-    const bool all_vis =
-        __all_sync(0xffffffffu, live0 && live1 && pmin >= 0 && pmax < pos0 &&
-                                    (a.window == 0 || max(t0, t1) - pmin < a.window));
-    if (all_vis) {
-#pragma unroll
-      for (int T = 0; T < 8; ++T) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
-          const float f = ksc[kk] * a.scale;
-          s[T][c] *= f;
-          s[T][2 + c] *= f;
-          mx0 = fmaxf(mx0, s[T][c]);
-          mx1 = fmaxf(mx1, s[T][2 + c]);
-        }
-      }
+    // ---- scale, mask, online softmax: s[T][c] (row g) and s[T][2 + c] (row g + 8) are key 16 kq + 4 tq + 2 T + c ----
+    const float4 kq4 = *reinterpret_cast<const float4*>(stg.ks + 16 * kq + 4 * tq);
+    const float4 vq4 = *reinterpret_cast<const float4*>(stg.vs + 16 * kq + 4 * tq);
+    const float ksc[4] = {kq4.x, kq4.y, kq4.z, kq4.w}, vsc[4] = {vq4.x, vq4.y, vq4.z, vq4.w};
+    int kpos[4];
+    if (a.ring) {
+      const int4 pq = *reinterpret_cast<const int4*>(stg.pos + 16 * kq + 4 * tq);
+      kpos[0] = pq.x; kpos[1] = pq.y; kpos[2] = pq.z; kpos[3] = pq.w;
     } else {
 #pragma unroll
-      for (int T = 0; T < 8; ++T) {
+      for (int r = 0; r < 4; ++r) kpos[r] = (int)c0 + 16 * kq + 4 * tq + r;
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
-          const int p = kpos[kk];
-          const bool ok = p >= 0 && p < pos0;
-          const bool vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
-          const bool vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
-          const float f = ksc[kk] * a.scale;
-          s[T][c] = vis0 ? s[T][c] * f : -INFINITY;
-          s[T][2 + c] = vis1 ? s[T][2 + c] * f : -INFINITY;
-          mx0 = fmaxf(mx0, s[T][c]);
-          mx1 = fmaxf(mx1, s[T][2 + c]);
-        }
+    for (int T = 0; T < 2; ++T) {
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int kk = 2 * T + c;
+        const int p = kpos[kk];
+        const bool ok = p >= 0 && p < pos0;
+        const bool vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
+        const bool vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
+        const float f = ksc[kk] * a.scale;
+        s[T][c] = vis0 ? s[T][c] * f : -INFINITY;
+        s[T][2 + c] = vis1 ? s[T][2 + c] * f : -INFINITY;
+        mx0 = fmaxf(mx0, s[T][c]);
+        mx1 = fmaxf(mx1, s[T][2 + c]);
       }
     }
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
@@ -244,20 +226,23 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
     run_m1 = new_m1;
     run_l0 *= corr0;
     run_l1 *= corr1;
+    if (corr0 != 1.f || corr1 != 1.f) {
 #pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
-      acc[dt][0] *= corr0;
-      acc[dt][1] *= corr0;
-      acc[dt][2] *= corr1;
-      acc[dt][3] *= corr1;
+      for (int dt = 0; dt < 16; ++dt) {
+        acc[dt][0] *= corr0;
+        acc[dt][1] *= corr0;
+        acc[dt][2] *= corr1;
+        acc[dt][3] *= corr1;
+      }
     }
-    uint32_t pa[4][4];   // A fragments of P' (probability times V scale), per key step j
+    // A fragment of P' (probability times V scale): a0 a1 row g k 2 tq .., a2 a3 row g + 8, a4 .. a7 the same at k + 8
+    uint32_t pa[4];
 #pragma unroll
-    for (int T = 0; T < 8; ++T) {
+    for (int T = 0; T < 2; ++T) {
       float p[4];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        const int kk = 4 * (T >> 1) + 2 * (T & 1) + c;
+        const int kk = 2 * T + c;
         p[c] = s[T][c] == -INFINITY ? 0.f : __expf(s[T][c] - new_m0);
         p[2 + c] = s[T][2 + c] == -INFINITY ? 0.f : __expf(s[T][2 + c] - new_m1);
         run_l0 += p[c];
@@ -265,42 +250,31 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
         p[c] *= vsc[kk];
         p[2 + c] *= vsc[kk];
       }
-      const int j = T >> 1;
-      if ((T & 1) == 0) {
-        pa[j][0] = pack_f16x2(p[0], p[1]);
-        pa[j][1] = pack_f16x2(p[2], p[3]);
-      } else {
-        pa[j][2] = pack_f16x2(p[0], p[1]);
-        pa[j][3] = pack_f16x2(p[2], p[3]);
-      }
+      pa[2 * T] = pack_f16x2(p[0], p[1]);
+      pa[2 * T + 1] = pack_f16x2(p[2], p[3]);
     }
-    // ---- O += P' V: V row d = 8 dt + g of the chunk, lane tq reads its slots 16 tq .. + 15 ----
+    // ---- O += P' V: head dim d = 8 dt + g; lane tq supplies keys 16 kq + 4 tq .. + 3 (one 32-bit word) ----
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) {
       const int d = 8 * dt + g;
-      const uint4 vv = *reinterpret_cast<const uint4*>(stg.v + d * 64 + 16 * (tq ^ ((d >> 1) & 3)));
-      const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t b0, b1;
-        codes_to_f16(vw[j], a.dtype, b0, b1);
-        mma_f16(acc[dt], pa[j][0], pa[j][1], pa[j][2], pa[j][3], b0, b1);
-      }
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(stg.v + d * 64 + 16 * (kq ^ ((d >> 1) & 3)) + 4 * tq);
+      uint32_t b0, b1;
+      codes_to_f16(w, a.dtype, b0, b1);
+      mma_f16(acc[dt], pa[0], pa[1], pa[2], pa[3], b0, b1);
     }
   };
 
-  // the pair's chunks cb + pair, + 4, ...: after each, both warps of the pair are done with the stage (a 64-thread
-  // named barrier) and the first warp refills it
-  {
-    const int count = ce > cb + pair ? (int)((ce - cb - pair + kPairs - 1) / kPairs) : 0;
-    for (int i = 0; i < count; ++i) {
-      mbar_wait_bounded(&sm.bar[pair], (uint32_t)(i & 1), lane == 0 ? a.err : nullptr);
-      if (active) chunk(sm.stage[pair], (cb + pair + kPairs * (int64_t)i) * 64);
-      asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
-      if (mt == 0 && i + 1 < count) {
-        fence_proxy_async_smem();
-        issue(pair, cb + pair + kPairs * (int64_t)(i + 1));
-      }
+  // every warp takes its part of every chunk; warp 0 refills a stage once all 8 warps are done with it
+  for (int i = 0; i < nc; ++i) {
+    const int s = i % kStages;
+    mbar_wait_bounded(&sm.full[s], (uint32_t)(i / kStages) & 1u, lane == 0 ? a.err : nullptr);
+    if (active) chunk(sm.stage[s], (cb + i) * 64);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty[s]);
+    if (warp == 0 && i + kStages < nc) {
+      mbar_wait_bounded(&sm.empty[s], (uint32_t)(i / kStages) & 1u, lane == 0 ? a.err : nullptr);
+      fence_proxy_async_smem();
+      issue(i + kStages);
     }
   }
   // the row sums live spread over the 4 lanes of a row
@@ -309,9 +283,10 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
   run_l1 += __shfl_xor_sync(0xffffffffu, run_l1, 1);
   run_l1 += __shfl_xor_sync(0xffffffffu, run_l1, 2);
 
-  // ---- merge the 4 pairs' states (each in its own stage), then write the CTA's partial per query row ----
+  // ---- merge the 4 key quarters' states (each in its own stage, every chunk consumed), then the CTA's partial ----
+  __syncthreads();
   {
-    float* st = reinterpret_cast<float*>(&sm.stage[pair]);
+    float* st = reinterpret_cast<float*>(&sm.stage[kq]);
     const int qr0 = 16 * mt + g, qr1 = qr0 + 8;
     if (tq == 0) {
       st[qr0 * kPartStride] = run_m0;
@@ -334,28 +309,29 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
     if (r / group < m) {
       const float* st0 = reinterpret_cast<const float*>(&sm.stage[0]);
       const int ss = (int)(sizeof(Stage) / sizeof(float));
-      float mp[kPairs], M = -INFINITY;
+      float mp[kQuarters], M = -INFINITY;
 #pragma unroll
-      for (int pr = 0; pr < kPairs; ++pr) {
-        mp[pr] = st0[pr * ss + r * kPartStride];
-        M = fmaxf(M, mp[pr]);
+      for (int j = 0; j < kQuarters; ++j) {
+        mp[j] = st0[j * ss + r * kPartStride];
+        M = fmaxf(M, mp[j]);
       }
-      float w[kPairs], L = 0.f;
+      float w[kQuarters], L = 0.f;
 #pragma unroll
-      for (int pr = 0; pr < kPairs; ++pr) {
-        w[pr] = mp[pr] == -INFINITY ? 0.f : expf(mp[pr] - M);
-        L += w[pr] == 0.f ? 0.f : st0[pr * ss + r * kPartStride + 1] * w[pr];
+      for (int j = 0; j < kQuarters; ++j) {
+        w[j] = mp[j] == -INFINITY ? 0.f : expf(mp[j] - M);
+        L += w[j] == 0.f ? 0.f : st0[j * ss + r * kPartStride + 1] * w[j];
       }
       float* out = a.part + (((int64_t)kvh * a.splits + split) * kQRows + r) * kPartStride;
       if (d0 == 0) {
         out[0] = M;
         out[1] = L;
       }
+#pragma unroll
       for (int d = d0; d < d0 + 16; ++d) {
         float o = 0.f;
 #pragma unroll
-        for (int pr = 0; pr < kPairs; ++pr)
-          if (w[pr] != 0.f) o += st0[pr * ss + r * kPartStride + 2 + d] * w[pr];
+        for (int j = 0; j < kQuarters; ++j)
+          if (w[j] != 0.f) o += st0[j * ss + r * kPartStride + 2 + d] * w[j];
         out[2 + d] = o;
       }
     }
@@ -368,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1) attention_kernel(const AttnArgs a
 constexpr int kMaxSplits = 256;
 
 __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
-  constexpr int kRegSplits = 32;   // partials held in registers (the rest are read in a second pass)
+  constexpr int kRegSplits = 64;   // partials held in registers (the rest are read in a second pass)
   __shared__ float wgt[kMaxSplits];
   __shared__ float cached[2];      // the splits' max m and their sum of l relative to it
   __shared__ float part_s[kD / 32][kMaxRows];

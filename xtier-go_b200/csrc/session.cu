@@ -486,8 +486,9 @@ struct xtg_cuda {
     *err_host = 0;
     // one attention CTA per SM, 4 chunks of 64 slots at a time (a warp pair each): a global layer's splits fill the
     // SMs once, a ring's take one chunk per warp pair
-    splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, std::min(256, num_sms / c.kv_heads));
-    splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, (int)((c.ring / 64 + 3) / 4));
+    // the attention runs 2 CTAs per SM: a global cache over every CTA slot, a ring one 64-slot chunk per CTA
+    splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, std::min(256, 2 * num_sms / c.kv_heads));
+    splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, std::min(256, (int)(c.ring / 64)));
     part = dalloc<float>((size_t)attention_part_floats(c.kv_heads, std::max(splits_g, splits_r)));
     ring_pos_dev = dalloc<int32_t>(c.ring);
     ring_pos.assign(c.ring, -1);
