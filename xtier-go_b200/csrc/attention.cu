@@ -58,10 +58,9 @@ struct Smem {
   Stage stage[kStages];           // the chunk ring; after the last chunk, key quarter j's softmax state in stage[j]
   uint64_t full[kStages], empty[kStages];
   uint4 qf[2][2][8][32];          // Q A fragments [m-tile][hi, lo][k16 step][lane]: q = hi + lo, both fp16
-  float q[kQRows][kD + 4];        // queries (query row = group * activation row + head in group)
 };
-// a key quarter's state after the last chunk: per query row m, l, acc[128]
-static_assert(sizeof(Stage) >= kQRows * kPartStride * sizeof(float), "stage too small for a quarter's state");
+// a key quarter's state after the last chunk: per query row m, l, acc[128] (rows kD + 4 floats apart)
+static_assert(sizeof(Stage) >= kQRows * (kD + 4) * sizeof(float), "stage too small for a quarter's state");
 static_assert(kStages >= kQuarters, "the quarters' states live in the stages");
 
 __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a) {
@@ -115,23 +114,28 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     pdl_wait();
   }
 
-  // ---- the queries of this KV head (prepared: RoPE, justnorm, q scale), one coalesced wave of 16-byte loads ----
-  for (int idx = threadIdx.x; idx < kQRows * 32; idx += kThreads) {
-    const int r = idx >> 5, f4 = idx & 31, i = r / group, hg = r % group;
-    float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (i < m && r < kMaxRows * group)
-      val = reinterpret_cast<const float4*>(a.q + ((int64_t)i * a.heads + kvh * group + hg) * kD)[f4];
-    reinterpret_cast<float4*>(sm.q[r])[f4] = val;
+  // ---- A fragments of the queries of this KV head (prepared: RoPE, justnorm, q scale), straight from memory, split
+  // q = hi + lo (both fp16) so that the scores keep ~22 bits: step st, lane tq reads head dims 32 tq + 4 st + {0, 1}
+  // (a0, a1) and + {2, 3} (a2, a3) of its rows gg and gg + 8 ----
+  auto qrow = [&](int r, int d0) {   // 4 head dims of query row r (zeros for rows past m)
+    const int i = r / group, hg = r % group;
+    return i < m ? *reinterpret_cast<const float4*>(a.q + ((int64_t)i * a.heads + kvh * group + hg) * kD + d0)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
+  float4 qv[2][2];
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {   // every load first
+    const int idx = (int)threadIdx.x + u * kThreads;
+    const int l = idx & 31, st = (idx >> 5) & 7, t2 = idx >> 8, gg = l >> 2, d0 = 32 * (l & 3) + 4 * st;
+    qv[u][0] = qrow(16 * t2 + gg, d0);
+    qv[u][1] = qrow(16 * t2 + gg + 8, d0);
   }
-  __syncthreads();
-  // A fragments of Q, split q = hi + lo (both fp16) so that the scores keep ~22 bits: step st, lane tq reads head
-  // dims 32 tq + 4 st + {0, 1} (a0, a1) and + {2, 3} (a2, a3)
-  for (int idx = threadIdx.x; idx < 2 * 8 * 32; idx += kThreads) {
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int idx = (int)threadIdx.x + u * kThreads;
     const int l = idx & 31, st = (idx >> 5) & 7, t2 = idx >> 8;
-    const int gg = l >> 2, tt = l & 3, d0 = 32 * tt + 4 * st;
-    const float* r0 = sm.q[16 * t2 + gg];
-    const float* r1 = sm.q[16 * t2 + gg + 8];
-    const float v[8] = {r0[d0], r0[d0 + 1], r1[d0], r1[d0 + 1], r0[d0 + 2], r0[d0 + 3], r1[d0 + 2], r1[d0 + 3]};
+    const float4 r0 = qv[u][0], r1 = qv[u][1];
+    const float v[8] = {r0.x, r0.y, r1.x, r1.y, r0.z, r0.w, r1.z, r1.w};
     uint32_t hi[4], lo[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -161,9 +165,9 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   // 4 tq + 2 T + c, and the K row that lane g supplies to tile T is key 4 ((g >> 1) & 3) + 2 T + (g & 1).
   auto chunk = [&](const Stage& stg, int64_t c0) {
     // ---- S = Q K^T over 2 n8 tiles x 8 k16 steps, q = hi + lo ----
-    float s[2][4];
+    float s[2][4], sl[2][4];   // the hi and lo products accumulate apart (shorter dependency chains)
 #pragma unroll
-    for (int T = 0; T < 2; ++T) s[T][0] = s[T][1] = s[T][2] = s[T][3] = 0.f;
+    for (int T = 0; T < 2; ++T) s[T][0] = s[T][1] = s[T][2] = s[T][3] = sl[T][0] = sl[T][1] = sl[T][2] = sl[T][3] = 0.f;
 #pragma unroll
     for (int hs = 0; hs < 2; ++hs) {   // head dims 32 tq + 16 hs .. + 15: k16 steps 4 hs .. 4 hs + 3
       uint4 kw[2];
@@ -182,10 +186,14 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
           uint32_t b0, b1;
           codes_to_f16(word, a.dtype, b0, b1);
           mma_f16(s[T], qh.x, qh.y, qh.z, qh.w, b0, b1);
-          mma_f16(s[T], ql.x, ql.y, ql.z, ql.w, b0, b1);
+          mma_f16(sl[T], ql.x, ql.y, ql.z, ql.w, b0, b1);
         }
       }
     }
+#pragma unroll
+    for (int T = 0; T < 2; ++T)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) s[T][c] += sl[T][c];
     // ---- scale, mask, online softmax: s[T][c] (row g) and s[T][2 + c] (row g + 8) are key 16 kq + 4 tq + 2 T + c ----
     const float4 kq4 = *reinterpret_cast<const float4*>(stg.ks + 16 * kq + 4 * tq);
     const float4 vq4 = *reinterpret_cast<const float4*>(stg.vs + 16 * kq + 4 * tq);
@@ -284,54 +292,56 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   run_l1 += __shfl_xor_sync(0xffffffffu, run_l1, 2);
 
   // ---- merge the 4 key quarters' states (each in its own stage, every chunk consumed), then the CTA's partial ----
+  // (state rows kStateStride floats apart, so that a warp's stores spread over the banks)
+  constexpr int kStateStride = kD + 4;   // m, l, acc[128], pad
   __syncthreads();
   {
     float* st = reinterpret_cast<float*>(&sm.stage[kq]);
     const int qr0 = 16 * mt + g, qr1 = qr0 + 8;
     if (tq == 0) {
-      st[qr0 * kPartStride] = run_m0;
-      st[qr0 * kPartStride + 1] = run_l0;
-      st[qr1 * kPartStride] = run_m1;
-      st[qr1 * kPartStride + 1] = run_l1;
+      st[qr0 * kStateStride] = run_m0;
+      st[qr0 * kStateStride + 1] = run_l0;
+      st[qr1 * kStateStride] = run_m1;
+      st[qr1 * kStateStride + 1] = run_l1;
     }
 #pragma unroll
     for (int dt = 0; dt < 16; ++dt) {
       const int d = 8 * dt + 2 * tq;
-      st[qr0 * kPartStride + 2 + d] = acc[dt][0];
-      st[qr0 * kPartStride + 3 + d] = acc[dt][1];
-      st[qr1 * kPartStride + 2 + d] = acc[dt][2];
-      st[qr1 * kPartStride + 3 + d] = acc[dt][3];
+      *reinterpret_cast<float2*>(&st[qr0 * kStateStride + 2 + d]) = make_float2(acc[dt][0], acc[dt][1]);
+      *reinterpret_cast<float2*>(&st[qr1 * kStateStride + 2 + d]) = make_float2(acc[dt][2], acc[dt][3]);
     }
   }
   __syncthreads();
   {
-    const int r = threadIdx.x >> 3, d0 = (threadIdx.x & 7) * 16;   // query row, 16 head dims
+    // thread: query row r, head dims j, j + 8, ...: a warp's stores cover 4 rows x 8 consecutive dims
+    const int r = threadIdx.x >> 3, j = threadIdx.x & 7;
     if (r / group < m) {
       const float* st0 = reinterpret_cast<const float*>(&sm.stage[0]);
       const int ss = (int)(sizeof(Stage) / sizeof(float));
       float mp[kQuarters], M = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < kQuarters; ++j) {
-        mp[j] = st0[j * ss + r * kPartStride];
-        M = fmaxf(M, mp[j]);
+      for (int q = 0; q < kQuarters; ++q) {
+        mp[q] = st0[q * ss + r * kStateStride];
+        M = fmaxf(M, mp[q]);
       }
       float w[kQuarters], L = 0.f;
 #pragma unroll
-      for (int j = 0; j < kQuarters; ++j) {
-        w[j] = mp[j] == -INFINITY ? 0.f : expf(mp[j] - M);
-        L += w[j] == 0.f ? 0.f : st0[j * ss + r * kPartStride + 1] * w[j];
+      for (int q = 0; q < kQuarters; ++q) {
+        w[q] = mp[q] == -INFINITY ? 0.f : expf(mp[q] - M);
+        L += w[q] == 0.f ? 0.f : st0[q * ss + r * kStateStride + 1] * w[q];
       }
       float* out = a.part + (((int64_t)kvh * a.splits + split) * kQRows + r) * kPartStride;
-      if (d0 == 0) {
+      if (j == 0) {
         out[0] = M;
         out[1] = L;
       }
 #pragma unroll
-      for (int d = d0; d < d0 + 16; ++d) {
+      for (int k = 0; k < kD / 8; ++k) {
+        const int d = j + 8 * k;
         float o = 0.f;
 #pragma unroll
-        for (int j = 0; j < kQuarters; ++j)
-          if (w[j] != 0.f) o += st0[j * ss + r * kPartStride + 2 + d] * w[j];
+        for (int q = 0; q < kQuarters; ++q)
+          if (w[q] != 0.f) o += st0[q * ss + r * kStateStride + 2 + d] * w[q];
         out[2 + d] = o;
       }
     }
