@@ -245,6 +245,67 @@ __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a)
   }
 }
 
+// The slerp update from the producer's row sums (GemvArgs::rsum): |h|^2, |o|^2 and the three sums that give
+// |(1 - lr) fa h + lr fb o|^2 = fa^2 A + 2 fa fb B + fb^2 C, so a CTA needs only its own dims. Grid (slices of 256
+// dims, 8 activation rows), 64 threads; thread t holds dims 256 s + 4 t .. + 3, a quad of threads one 16-input group.
+constexpr int kSlerpDims = 256, kSlerpThreads = kSlerpDims / 4;
+constexpr int kSlerpPartLoads = 5;   // partials per thread: at most 320 producer CTAs
+
+__global__ void __launch_bounds__(kSlerpThreads) resid_slerp_kernel(const ResidArgs a) {
+  __shared__ float red[kSlerpThreads / 32][5];
+  const int r = blockIdx.y, t = threadIdx.x, H = a.hidden, lane = t & 31, warp = t >> 5;
+  const int c = blockIdx.x * kSlerpThreads + t;   // this thread's float4 of the row
+  const bool ok = 4 * c < H;
+  const float4 l4 = ld4(a.lr, c, ok);   // a parameter: before the dependency wait
+  const int m = a.params ? a.params->m : a.m;
+  if (a.pdl) {
+    pdl_launch_next();
+    pdl_wait();
+  }
+  const bool live = r < m;
+  // one wave of loads: this thread's share of the partials (parts t, t + 64, ..., summed in order), h and o
+  float pv[kSlerpPartLoads][5];
+#pragma unroll
+  for (int it = 0; it < kSlerpPartLoads; ++it) {
+    const int q = t + it * kSlerpThreads;
+    const bool lq = live && q < a.nparts;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) pv[it][k] = lq ? a.rsum[((int64_t)q * 8 + r) * 5 + k] : 0.f;
+  }
+  float* h = a.h + (int64_t)r * H;
+  const float4 h4 = ld4(h, c, ok && live), o4 = ld4(a.o + (int64_t)r * H, c, ok && live);
+  float s5[5];
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    s5[k] = pv[0][k];
+#pragma unroll
+    for (int it = 1; it < kSlerpPartLoads; ++it) s5[k] += pv[it][k];
+  }
+#pragma unroll
+  for (int k = 0; k < 5; ++k) s5[k] = warp_sum(s5[k]);
+  if (lane == 0)
+#pragma unroll
+    for (int k = 0; k < 5; ++k) red[warp][k] = s5[k];
+  __syncthreads();
+  float tot[5];
+#pragma unroll
+  for (int k = 0; k < 5; ++k) tot[k] = red[0][k] + red[1][k];
+  const float fa = 1.f / sqrtf(tot[0] + 1e-6f), fb = 1.f / sqrtf(tot[1] + 1e-6f);
+  const float f = 1.f / sqrtf(fa * fa * tot[2] + 2.f * fa * fb * tot[3] + fb * fb * tot[4] + 1e-6f);
+  const float hv[4] = {h4.x, h4.y, h4.z, h4.w}, ov[4] = {o4.x, o4.y, o4.z, o4.w}, lv[4] = {l4.x, l4.y, l4.z, l4.w};
+  float v[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) v[k] = live ? ((1.f - lv[k]) * fa * hv[k] + lv[k] * fb * ov[k]) * f : 0.f;
+  if (live && ok) st4(h, c, v);
+  uint32_t code[kDigits], sf[kDigits];
+  const float p = digitize16_quad(v, code, sf, kUnitNorm);   // whole warps take part
+  if (ok) {
+    const int g = c >> 2, q = c & 3;
+    store_digits_quad(a.xb + (int64_t)(g >> 2) * kBBlockBytes, r, g & 3, q, code, sf);
+    if (q == 0) a.xb_pre[(int64_t)g * 8 + r] = p;
+  }
+}
+
 __global__ void argmax_kernel(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out,
                               float* out_val, int pdl) {
   __shared__ float bv[32];
@@ -385,6 +446,12 @@ void launch_resid(const ResidArgs& a_in, cudaStream_t s, bool pdl) {
   ResidArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
   XTG_REQUIRE(a.hidden <= 4 * kChunks * kResidThreads && a.hidden % 64 == 0, "resid: hidden a multiple of 64, at most 8192");
+  if (a.mode == kResidSlerp && a.rsum) {
+    XTG_REQUIRE(a.nparts <= kSlerpPartLoads * kSlerpThreads, "resid: at most 320 row-sum partials");
+    launch_pdl(resid_slerp_kernel, dim3((a.hidden + kSlerpDims - 1) / kSlerpDims, kMaxRows), dim3(kSlerpThreads), a,
+               s, pdl, 0);
+    return;
+  }
   launch_pdl(resid_kernel, dim3(kMaxRows), dim3(kResidThreads), a, s, pdl, 0);
 }
 

@@ -41,6 +41,10 @@ struct ResidArgs {
   float* input;
   uint8_t* xb;              // B digits of the new h
   float* xb_pre;            // [hidden / 16][8] their prescales
+  // slerp, optional: the producer's per-CTA row sums (kernels.h GemvArgs::rsum) -- the update then runs over many
+  // CTAs with no whole-row reduction
+  const float* rsum;
+  int nparts;
   int pdl;
 };
 

@@ -242,6 +242,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   const int m = a.m_dev ? *a.m_dev : a.m;
   float sgv[4] = {0.f, 0.f, 0.f, 0.f}, suv[4] = {0.f, 0.f, 0.f, 0.f};   // kEpiSwiglu: this thread's features
   TileOut ofin = {};                                                    // kEpiStore: the tile's output
+  float rs_lr = 0.f, rs_h = 0.f;   // kEpiStore with row sums: the rate and h of this thread's finished element
   QkvPre qpre = {};
   if constexpr (EPI == kEpiSwiglu) {
     const int g0 = share_begin(4, srank, S), g1 = share_begin(4, srank + 1, S);
@@ -258,6 +259,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     }
   } else if constexpr (EPI == kEpiStore) {
     if (a.outs) ofin = a.outs[t0];
+    if (a.rsum && S > 1) {
+      const int r0 = share_begin(kTileRows, srank, S), nr = share_begin(kTileRows, srank + 1, S) - r0;
+      if (tid < nr * 8) rs_lr = a.rs_lr[t0 * kTileRows + r0 + tid % nr];
+    }
   } else if constexpr (EPI == kEpiQkv) {
     qpre.pos0 = *a.pos0_dev;
     if (t0 < a.q_tiles) qpre.qscale = a.qscale[t0 * 128 + (tid & 127)];
@@ -266,6 +271,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   if (a.pdl) {
     pdl_launch_next();
     pdl_wait();
+  }
+  if constexpr (EPI == kEpiStore) {   // h (the previous residual update's output): loaded long before the finish
+    if (a.rsum && S > 1) {
+      const int r0 = share_begin(kTileRows, srank, S), nr = share_begin(kTileRows, srank + 1, S) - r0;
+      if (tid < nr * 8 && tid / nr < m) rs_h = a.rs_h[(int64_t)(tid / nr) * a.rs_ld + t0 * kTileRows + r0 + tid % nr];
+    }
   }
   if constexpr (EPI == kEpiQkv) {
     // RoPE factors (written by the step's first kernel): q and k heads, this thread's rows
@@ -540,9 +551,30 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     } else if constexpr (EPI == kEpiStore) {
       const TileOut& o = ofin;
       const int r0 = share_begin(kTileRows, srank, S), nr = share_begin(kTileRows, srank + 1, S) - r0;
-      for (int p = tid; p < nr * 8; p += kThreads) {
-        const int i = p / nr, rl = p % nr, r = r0 + rl;
-        if (i < m && r < o.rows) o.y[(int64_t)i * o.ld + r] = total(rl, i) * rowscale[i];
+      if (a.rsum) {
+        // one element per thread (nr * 8 <= 256); the row sums over the nr lanes of a row (nr divides 32: aligned
+        // groups of lanes), in a fixed butterfly order
+        const int i = tid / nr, rl = tid % nr, r = r0 + rl;
+        float y = 0.f;
+        if (tid < nr * 8 && i < m && r < o.rows) {
+          y = total(rl, i) * rowscale[i];
+          o.y[(int64_t)i * o.ld + r] = y;
+        }
+        const float h = rs_h, lr = rs_lr, w = 1.f - lr;
+        float v[5] = {h * h, y * y, w * w * h * h, lr * w * h * y, lr * lr * y * y};
+        for (int off = nr >> 1; off > 0; off >>= 1)
+#pragma unroll
+          for (int k = 0; k < 5; ++k) v[k] += __shfl_xor_sync(0xffffffffu, v[k], off);
+        if (tid < nr * 8 && rl == 0) {
+          float* dst = a.rsum + ((int64_t)blockIdx.x * 8 + i) * 5;
+#pragma unroll
+          for (int k = 0; k < 5; ++k) dst[k] = v[k];
+        }
+      } else {
+        for (int p = tid; p < nr * 8; p += kThreads) {
+          const int i = p / nr, rl = p % nr, r = r0 + rl;
+          if (i < m && r < o.rows) o.y[(int64_t)i * o.ld + r] = total(rl, i) * rowscale[i];
+        }
       }
     } else {
       // quad (group g, row i): lane t holds features 16 g + 4 t .. + 3 of the tile; v -> digits of the next GEMV
@@ -639,6 +671,8 @@ GemvPlan plan_gemv(int tiles, int kblocks, int num_sms, int max_split, int max_t
 
 void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bool pdl) {
   XTG_REQUIRE(epi != kEpiHead || p.split == 1, "gemv: the head epilogue takes whole tiles");
+  XTG_REQUIRE(!a.rsum || (epi == kEpiStore && p.split >= 4 && p.split <= 8 && (p.split & (p.split - 1)) == 0),
+              "gemv: row sums need a STORE GEMV split 4 or 8 ways");
   XTG_REQUIRE((epi != kEpiSwiglu && epi != kEpiQkv) || p.tiles_per_cta == 1,
               "gemv: the SwiGLU and q|k|v epilogues take one tile per CTA");
   XTG_REQUIRE(p.split >= 1 && p.split <= 8 && p.ring >= 1 && p.ring <= kMaxRing, "gemv: bad plan");

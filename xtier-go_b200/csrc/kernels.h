@@ -92,6 +92,14 @@ struct GemvArgs {
   float* logits;             // [n][vocab]
   int vocab;
   ArgCand* cand;             // [tiles][8]
+  // kEpiStore, split tiles (split >= 4), optional: the row sums the nGPT residual update that follows needs, per CTA,
+  // so that it reduces a few partials instead of whole rows. For the output dims y this CTA finishes (global index
+  // tile * 128 + r) and activation row i: sums of h^2, y^2, (1 - lr)^2 h^2, lr (1 - lr) h y, lr^2 y^2 ->
+  // rsum[(cta * 8 + i) * 5 + k]; h [8][rs_ld] is the residual stream the update starts from
+  float* rsum;
+  const float* rs_h;
+  const float* rs_lr;
+  int rs_ld;
   int* err;                  // set to 1 if a bounded wait gave up (never expected); may be null
   int pdl;                   // launched as a programmatic dependent
 };

@@ -210,7 +210,7 @@ struct xtg_cuda {
   uint8_t *xb = nullptr, *ab = nullptr, *vb = nullptr;
   float *xb_pre = nullptr, *ab_pre = nullptr, *vb_pre = nullptr;
   float *q_prep = nullptr, *k_new = nullptr, *v_new = nullptr;   // this step's prepared q / k / v rows
-  float *asum = nullptr, *vsum = nullptr, *logits = nullptr, *logits_host = nullptr, *argmax_val = nullptr;
+  float *asum = nullptr, *vsum = nullptr, *rsum = nullptr, *logits = nullptr, *logits_host = nullptr, *argmax_val = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   int32_t* argmax = nullptr;
   ArgCand* cand = nullptr;
@@ -474,6 +474,7 @@ struct xtg_cuda {
     v_new = dalloc<float>((size_t)kMaxRows * KV);
     asum = dalloc<float>((size_t)c.heads * kMaxRows);
     vsum = dalloc<float>((size_t)packed_tiles(F, true) * 8 * kMaxRows);
+    rsum = dalloc<float>((size_t)2 * num_sms * kMaxRows * 5);   // a split GEMV has at most 2 CTAs per SM
     logits = dalloc<float>((size_t)kMaxRows * c.vocab);
     XTG_CUDA(cudaMallocHost(&logits_host, (size_t)kMaxRows * c.vocab * sizeof(float)));
     cand = dalloc<ArgCand>((size_t)packed_tiles(c.vocab, false) * kMaxRows);
@@ -484,8 +485,6 @@ struct xtg_cuda {
     dev_err = dalloc<int>(1);
     XTG_CUDA(cudaMallocHost(&err_host, sizeof(int)));
     *err_host = 0;
-    // one attention CTA per SM, 4 chunks of 64 slots at a time (a warp pair each): a global layer's splits fill the
-    // SMs once, a ring's take one chunk per warp pair
     // the attention runs 2 CTAs per SM: a global cache over every CTA slot, a ring one 64-slot chunk per CTA
     splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, std::min(256, 2 * num_sms / c.kv_heads));
     splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, std::min(256, (int)(c.ring / 64)));
@@ -563,7 +562,18 @@ struct xtg_cuda {
     ea.ring = c.ring;
     launch_embed(ea, stream, false);
     mark(kClsSmall, false);
-    auto resid = [&](int mode, const float* lr) {
+    // the O / down projection feeds the slerp update with per-CTA row sums when split 4 or 8 ways
+    auto with_rsum = [&](const Linear& L, const float* lr) {
+      GemvArgs a = gemv_args(L);
+      if (L.plan.split == 4 || L.plan.split == 8) {
+        a.rsum = rsum;
+        a.rs_h = h;
+        a.rs_lr = lr;
+        a.rs_ld = H;
+      }
+      return a;
+    };
+    auto resid = [&](int mode, const float* lr, const Linear* producer = nullptr) {
       ResidArgs r = {};
       r.mode = mode;
       r.params = params_dev;
@@ -575,6 +585,10 @@ struct xtg_cuda {
       r.input = input;
       r.xb = xb;
       r.xb_pre = xb_pre;
+      if (producer && (producer->plan.split == 4 || producer->plan.split == 8)) {
+        r.rsum = rsum;
+        r.nparts = producer->plan.grid;
+      }
       mark(kClsSmall, true);
       launch_resid(r, stream, pdl);
       mark(kClsSmall, false);
@@ -592,8 +606,8 @@ struct xtg_cuda {
         a.vb_pre = vb_pre;
         a.vsum = vsum;
         gemv(E.gu, kEpiSwiglu, a, xb, xb_pre, pdl);
-        gemv(E.down, kEpiStore, gemv_args(E.down), vb, vb_pre, pdl, vsum, E.gu.tiles * E.gu.plan.split);
-        resid(kResidSlerp, E.lr);
+        gemv(E.down, kEpiStore, with_rsum(E.down, E.lr), vb, vb_pre, pdl, vsum, E.gu.tiles * E.gu.plan.split);
+        resid(kResidSlerp, E.lr, &E.down);
         return;
       }
       const KvInst& K = kv[E.cache];
@@ -660,8 +674,8 @@ struct xtg_cuda {
       mark(kClsCombine, true);
       launch_attn_combine(cb, stream, pdl);
       mark(kClsCombine, false);
-      gemv(E.o, kEpiStore, gemv_args(E.o), ab, ab_pre, pdl, asum, c.heads);
-      resid(kResidSlerp, E.lr);
+      gemv(E.o, kEpiStore, with_rsum(E.o, E.lr), ab, ab_pre, pdl, asum, c.heads);
+      resid(kResidSlerp, E.lr, &E.o);
     };
     int e = 0;
     for (int l = 0; l < c.n_in; ++l) sublayer(e++);
