@@ -85,7 +85,7 @@ __global__ void embed_kernel(const EmbedArgs a) {
 }
 
 // the residual stream is unit-norm after every update (|h| <= 1): one prescale for all its groups (2^11)
-constexpr float kUnitNorm = 2048.f;
+constexpr float kUnitNorm = kUnitPrescale;
 
 // Block-wide sums of two values at once (fixed order, deterministic).
 __device__ __forceinline__ float2 block_sum2(float x, float y, float2* red) {

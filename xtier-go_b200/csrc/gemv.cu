@@ -32,6 +32,7 @@ constexpr int kThreads = 256;
 constexpr int kStageUnits = 4;
 constexpr int kMaxRing = 6;
 constexpr int kAccCols = 64;   // TMEM columns per accumulator (48 used)
+constexpr int kSumsqLoads = 10;   // the producer's row-sum parts a lane loads: at most 320 parts
 
 struct Params {
   GemvArgs a;
@@ -302,22 +303,32 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   __syncwarp();
   {
     const int i = warp;   // warp i: activation row i
-    float pmin = 3.0e38f;
-    for (int b = lane; b < nkb * 4; b += 32) {
-      const float pb = a.xb_pre[((int64_t)k0 * 4 + b) * 8 + i];
-      pre_s[b * 8 + i] = pb;
-      pmin = fminf(pmin, pb);
-    }
+    float pmin = a.xb_fixed;
+    if (!(a.xb_fixed > 0.f)) {
+      pmin = 3.0e38f;
+      for (int b = lane; b < nkb * 4; b += 32) {
+        const float pb = a.xb_pre[((int64_t)k0 * 4 + b) * 8 + i];
+        pre_s[b * 8 + i] = pb;
+        pmin = fminf(pmin, pb);
+      }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) pmin = fminf(pmin, __shfl_xor_sync(0xffffffffu, pmin, o));
+      for (int o = 16; o > 0; o >>= 1) pmin = fminf(pmin, __shfl_xor_sync(0xffffffffu, pmin, o));
+    }
     if (lane == 0) pslice[i] = pmin;
     if (EPI == kEpiStore) {
-      // the row's sum of squares over the producer's parts: lane l takes parts l, l + 32, ... (independent loads),
+      // the row's sum of squares over the producer's parts: lane l takes parts l, l + 32, ... (one wave of loads),
       // then a butterfly over the warp (a fixed order)
       float t = 1.f;
       if (a.sumsq) {
-        t = 0.f;
-        for (int q = lane; q < a.nparts; q += 32) t += a.sumsq[q * 8 + i];
+        float pv[kSumsqLoads];
+#pragma unroll
+        for (int u = 0; u < kSumsqLoads; ++u) {
+          const int q = lane + 32 * u;
+          pv[u] = q < a.nparts ? a.sumsq[q * 8 + i] : 0.f;
+        }
+        t = pv[0];
+#pragma unroll
+        for (int u = 1; u < kSumsqLoads; ++u) t += pv[u];
         t = warp_sum(t);
         t = 1.f / sqrtf(t + 1e-6f);
       }
@@ -326,16 +337,24 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   }
   wait_bar(bfull, 0, a.err);
   __syncthreads();
-  for (int e = tid; e < nkb * 4 * 8; e += kThreads) {   // (group, row): its 6 digit scales
-    const int b = e >> 3, i = e & 7;
-    const int k = (__float_as_int(pre_s[b * 8 + i]) - __float_as_int(pslice[i])) >> 23;
-    if (k > 0) {
-      uint8_t* sfb = bbuf + (b >> 2) * kBBlockBytes + kBCodeBytes;
+  if (!(a.xb_fixed > 0.f)) {
+    // the scale words of the slice: word (K block kb, digit row r = 8 d + i) holds the scales of groups 4 kb .. 4 kb + 3,
+    // each brought from its group's prescale to the row's smallest
+    for (int e = tid; e < nkb * kDigitRows; e += kThreads) {
+      const int kb = e / kDigitRows, r = e - kb * kDigitRows, i = r & 7;
+      uint32_t* w = reinterpret_cast<uint32_t*>(bbuf + kb * kBBlockBytes + kBCodeBytes + sf_offset(r, 0));
+      const uint32_t v = *w;
+      const int ps = __float_as_int(pslice[i]);
+      uint32_t o = 0u;
 #pragma unroll
-      for (int d = 0; d < kDigits; ++d) sfb[sf_offset(8 * d + i, b & 3)] = (uint8_t)ue4m3_scale_down(sfb[sf_offset(8 * d + i, b & 3)], k);
+      for (int j = 0; j < 4; ++j) {
+        const int k = (__float_as_int(pre_s[(4 * kb + j) * 8 + i]) - ps) >> 23;
+        o |= ue4m3_scale_down((v >> (8 * j)) & 0xffu, k) << (8 * j);
+      }
+      if (o != v) *w = o;
     }
+    fence_proxy_async_smem();
   }
-  fence_proxy_async_smem();
   __syncthreads();
 
   if (warp == 0) {
@@ -671,6 +690,7 @@ GemvPlan plan_gemv(int tiles, int kblocks, int num_sms, int max_split, int max_t
 
 void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bool pdl) {
   XTG_REQUIRE(epi != kEpiHead || p.split == 1, "gemv: the head epilogue takes whole tiles");
+  XTG_REQUIRE(!a.sumsq || a.nparts <= 32 * kSumsqLoads, "gemv: at most 320 row-sum parts");
   XTG_REQUIRE(!a.rsum || (epi == kEpiStore && p.split >= 4 && p.split <= 8 && (p.split & (p.split - 1)) == 0),
               "gemv: row sums need a STORE GEMV split 4 or 8 ways");
   XTG_REQUIRE((epi != kEpiSwiglu && epi != kEpiQkv) || p.tiles_per_cta == 1,

@@ -20,6 +20,8 @@ inline int64_t packed_bytes(int n_out, int k, bool interleave) {
 }
 // activations as B digits (fp4mma.cuh): 2048 bytes per 64 inputs
 inline int64_t digit_bytes(int k) { return (int64_t)packed_kblocks(k) * 2048; }
+// the prescale of digits of a unit-norm vector (|x| <= 1): every group of the residual stream takes it
+constexpr float kUnitPrescale = 2048.f;
 
 void gen_normal_bf16(uint64_t seed, uint64_t stream, float stddev, uint16_t* out, int64_t n, cudaStream_t s);
 void gen_uniform(uint64_t seed, uint64_t stream, float lo, float hi, float* out, int64_t n, cudaStream_t s);
@@ -53,6 +55,7 @@ struct GemvArgs {
   // 16-input group and row ([kblocks * 4][8])
   const uint8_t* xb;
   const float* xb_pre;
+  float xb_fixed;            // > 0: every group's prescale is this (xb_pre is not read)
   const int* m_dev;          // activation rows (1..8) read on the device (a replayable graph), or null: m
   int m;
   // kEpiStore

@@ -531,10 +531,15 @@ struct xtg_cuda {
   }
 
   // a GEMV of activation digits (xb, xb_pre), with an optional justnorm row scale from sumsq (STORE)
+  // whether xb holds the digits of the residual stream (written by a residual update: one prescale for every group)
+  // rather than the embedding's
+  bool xb_unit = false;
+
   void gemv(const Linear& L, int epi, GemvArgs a, const uint8_t* in, const float* in_pre, bool pdl,
             const float* sumsq = nullptr, int nparts = 0) {
     a.xb = in;
     a.xb_pre = in_pre;
+    a.xb_fixed = (in == xb && xb_unit) ? kUnitPrescale : 0.f;
     a.sumsq = sumsq;
     a.nparts = nparts;
     mark(kClsGemv, true);
@@ -561,6 +566,7 @@ struct xtg_cuda {
     ea.ring_pos = ring_pos_dev;
     ea.ring = c.ring;
     launch_embed(ea, stream, false);
+    xb_unit = false;
     mark(kClsSmall, false);
     // the O / down projection feeds the slerp update with per-CTA row sums when split 4 or 8 ways
     auto with_rsum = [&](const Linear& L, const float* lr) {
@@ -592,6 +598,7 @@ struct xtg_cuda {
       mark(kClsSmall, true);
       launch_resid(r, stream, pdl);
       mark(kClsSmall, false);
+      xb_unit = true;
     };
     auto sublayer = [&](int e) {
       const Eval& E = evals[e];
