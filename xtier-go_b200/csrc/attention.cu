@@ -110,8 +110,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   if (warp == 0)
     for (int i = 0; i < kStages && i < nc; ++i) issue(i);
   if (a.pdl) {
-    pdl_launch_next();
     pdl_wait();
+    pdl_launch_next();
   }
 
   // ---- A fragments of the queries of this KV head (prepared: RoPE, justnorm, q scale), straight from memory, split
@@ -365,8 +365,8 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   const float gsc = a.out ? 0.f : a.gscale[col];
   const int m = a.params ? a.params->m : a.m;
   if (a.pdl) {
-    pdl_launch_next();
     pdl_wait();
+    pdl_launch_next();
   }
   if (i >= m) return;
   const int group = a.heads / a.kv_heads, kvh = h / group, qr = i * group + h % group;

@@ -50,8 +50,8 @@ __global__ void embed_kernel(const EmbedArgs a) {
   extern __shared__ float rowbuf[];   // [hidden]
   const int r = blockIdx.x;
   if (a.pdl) {
-    pdl_launch_next();
     pdl_wait();
+    pdl_launch_next();
   }
   const StepParams* p = a.params;
   const int m = p->m;
@@ -133,8 +133,8 @@ __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a)
   }
   const int m = a.params ? a.params->m : a.m;
   if (a.pdl) {
-    pdl_launch_next();
     pdl_wait();
+    pdl_launch_next();
   }
   float* h = a.h + (int64_t)r * H;
   float v[kChunks][4];
@@ -259,8 +259,8 @@ __global__ void __launch_bounds__(kSlerpThreads) resid_slerp_kernel(const ResidA
   const float4 l4 = ld4(a.lr, c, ok);   // a parameter: before the dependency wait
   const int m = a.params ? a.params->m : a.m;
   if (a.pdl) {
-    pdl_launch_next();
     pdl_wait();
+    pdl_launch_next();
   }
   const bool live = r < m;
   // one wave of loads: this thread's share of the partials (parts t, t + 64, ..., summed in order), h and o
@@ -312,8 +312,8 @@ __global__ void argmax_kernel(const ArgCand* cand, int tiles, const StepParams* 
   __shared__ int bi[32];
   const int n = blockIdx.x;
   if (pdl) {
-    pdl_launch_next();
     pdl_wait();
+    pdl_launch_next();
   }
   if (n >= params->m) return;
   float v = -INFINITY;

@@ -270,8 +270,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     if (t0 >= a.q_tiles + 2 * a.kv_tiles && a.outs) qpre.out = a.outs[t0];
   }
   if (a.pdl) {
-    pdl_launch_next();
     pdl_wait();
+    pdl_launch_next();
   }
   if constexpr (EPI == kEpiStore) {   // h (the previous residual update's output): loaded long before the finish
     if (a.rsum && S > 1) {
