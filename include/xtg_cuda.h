@@ -104,7 +104,8 @@ typedef struct xtg_cuda_linear xtg_cuda_linear;
 // global scales as host floats), all reading the same x. Packed once into the GEMV's streaming layout.
 XTG_CUDA_API xtg_cuda_linear* xtg_cuda_linear_new(int nw, const uint8_t* const* codes, const uint8_t* const* scales,
                                      const float* globals, const int* n_out, int k, char* err, int err_len);
-// y_i[m][n_out_i] = x[m][k] W_i^T for m <= 8 rows (x, ys: device f32). One handle runs on one stream at a time.
+// y_i[m][n_out_i] = x[m][k] W_i^T (x, ys: device f32): m <= 8 rows on the GEMV, more (a prefill chunk, a batch; up to
+// 65536) on the tensor-core GEMM. One handle runs on one stream at a time.
 XTG_CUDA_API int xtg_cuda_linear_forward(xtg_cuda_linear* w, const float* x, int m, float* const* ys, void* stream, char* err,
                             int err_len);
 XTG_CUDA_API int64_t xtg_cuda_linear_bytes(xtg_cuda_linear* w);   // packed weight bytes streamed per call

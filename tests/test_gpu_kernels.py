@@ -143,6 +143,54 @@ def test_gemv_deterministic(cuda, xtg, torch_mod):
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
+# ---- the tensor-core GEMM (matmul_nvfp4's m > 2 path: prefill chunks, batches) ----
+
+@pytest.mark.parametrize("m", [9, 33, 70])
+def test_gemm_ragged_shapes(cuda, xtg, torch_mod, m):
+    """Rows past a tile of 32, inputs not a multiple of 64 (padding), fused uneven weights; against the oracle."""
+    k = 336
+    ws = [O.synth_weight(2, 7700 + i, n, k)[1:] for i, n in enumerate((1, 17, 100, 130))]
+    x = O.gen_uniform(2, 7800 + m, -1.0, 1.0, m * k).reshape(m, k)
+    got = run_linear(xtg, torch_mod, ws, x)
+    ref = O.matmul_nvfp4(ws, x)
+    ok, worst = close_rel(np.concatenate([g_.ravel() for g_ in got]), np.concatenate([r.ravel() for r in ref]))
+    assert ok, worst
+
+
+def test_gemm_config1_m512(cuda, xtg, torch_mod):
+    """BASELINE config 1 at M = 512 (a prefill chunk on tcgen05): the full projection set runs on the GPU; the oracle
+    checks the first and last 128 output rows of every weight (the scalar oracle at full size takes minutes)."""
+    H, F, Q, KV, M = 3072, 9216, 3072, 768, 512
+    x = O.bf16_to_f32(O.gen_normal_bf16(1, 7900, 1.0, M * F)).reshape(M, F)
+    sets = {
+        "qkvg": ([(Q, H), (KV, H), (KV, H), (Q, H)], H),
+        "o": ([(H, Q)], Q),
+        "gate_up": ([(F, H), (F, H)], H),
+        "down": ([(H, F)], F),
+    }
+    for name, (shapes, k) in sets.items():
+        ws = [O.synth_weight(1, 8000 + 16 * i + len(name), n, kk)[1:] for i, (n, kk) in enumerate(shapes)]
+        got = run_linear(xtg, torch_mod, ws, x[:, :k])
+        for (codes, scales, g), y in zip(ws, got):
+            n = codes.shape[0]
+            for lo in (0, n - 128):
+                sub = [(codes[lo:lo + 128], scales[lo:lo + 128], g)]
+                ref = O.matmul_nvfp4(sub, x[:, :k])[0]
+                ok, worst = close_rel(y[:, lo:lo + 128], ref)
+                assert ok, (name, lo, worst)
+
+
+def test_gemm_deterministic(cuda, xtg, torch_mod):
+    torch = torch_mod
+    raw, codes, scales, g = O.synth_weight(4, 8100, 1024, 3072)
+    x = dev(torch, O.gen_uniform(4, 8101, -1.0, 1.0, 200 * 3072).reshape(200, 3072))
+    L = xtg.Linear([(dev(torch, codes), dev(torch, scales), g)], 3072)
+    a = L(x)[0].cpu().numpy()
+    b = L(x)[0].cpu().numpy()
+    L.close()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
 # ---- attention ----
 
 def swz_k(s64):

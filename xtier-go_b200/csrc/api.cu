@@ -28,12 +28,19 @@ struct xtg_cuda_linear {
   float* xb_pre = nullptr;
   GemvPlan plan;
   int64_t bytes = 0;
+  int sms = 0;
+  // GEMM path (m > 8): the activation units and row prescales, grown to the largest m seen
+  uint8_t* act = nullptr;
+  float* act_pre = nullptr;
+  int act_rows = 0;
 
   ~xtg_cuda_linear() {
     cudaFree(w);
     cudaFree(outs);
     cudaFree(xb);
     cudaFree(xb_pre);
+    cudaFree(act);
+    cudaFree(act_pre);
   }
 };
 
@@ -69,6 +76,7 @@ xtg_cuda_linear* xtg_cuda_linear_new(int nw, const uint8_t* const* codes, const 
     XTG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, L->device));
     L->k = k;
     L->nw = nw;
+    L->sms = sms;
     L->kblocks = packed_kblocks(k);
     for (int i = 0; i < nw; ++i) {
       XTG_REQUIRE(n_out[i] > 0, "linear: n_out must be positive");
@@ -103,7 +111,7 @@ xtg_cuda_linear* xtg_cuda_linear_new(int nw, const uint8_t* const* codes, const 
 int xtg_cuda_linear_forward(xtg_cuda_linear* L, const float* x, int m, float* const* ys, void* stream, char* err,
                             int err_len) {
   return guarded(err, err_len, [&] {
-    XTG_REQUIRE(m >= 1 && m <= kMaxRows, "linear: 1..8 rows");
+    XTG_REQUIRE(m >= 1 && m <= kMaxGemmRows, "linear: 1..65536 rows");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     for (int i = 0; i < L->nw; ++i) {
       const int t0 = L->tile0[i], nt = packed_tiles(L->n_out[i], false);
@@ -112,6 +120,26 @@ int xtg_cuda_linear_forward(xtg_cuda_linear* L, const float* x, int m, float* co
                                        L->globals[i], L->globals[i]};
     }
     XTG_CUDA(cudaMemcpyAsync(L->outs, L->outs_host.data(), sizeof(TileOut) * L->tiles, cudaMemcpyHostToDevice, s));
+    if (m > kMaxRows) {
+      // prefill chunk / batch: the tensor-core GEMM (matmul_nvfp4's m > 2 path)
+      if (m > L->act_rows) {
+        XTG_CUDA(cudaStreamSynchronize(s));
+        cudaFree(L->act);
+        cudaFree(L->act_pre);
+        L->act = nullptr;
+        L->act_pre = nullptr;
+        L->act_rows = 0;
+        const int rows = ((m + 31) / 32) * 32;
+        XTG_CUDA(cudaMalloc(&L->act, (size_t)gemm_act_bytes(rows, L->k)));
+        XTG_CUDA(cudaMemset(L->act, 0, (size_t)gemm_act_bytes(rows, L->k)));   // K padding stays zero
+        XTG_CUDA(cudaMalloc(&L->act_pre, (size_t)rows * sizeof(float)));
+        L->act_rows = rows;
+      }
+      gemm_digitize(x, m, L->k, L->act, L->act_pre, s);
+      launch_gemm(L->w, L->tiles, L->kblocks, L->act, L->act_pre, m, L->outs, L->sms, nullptr, s);
+      XTG_CUDA(cudaStreamSynchronize(s));
+      return;
+    }
     digitize_rows(x, m, L->k, L->xb, L->xb_pre, s);
     GemvArgs a = {};
     a.w = L->w;

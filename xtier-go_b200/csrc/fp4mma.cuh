@@ -168,8 +168,9 @@ __device__ __forceinline__ float block_prescale(float amax) {
 // shuffles of a per-digit maximum, for a reconstruction error within ~1.5x of it (~1.2e-5 of the group maximum at
 // most). A digit's value r / s only picks the code (the residual keeps the exact r - s q), so 1 / s may be the fast
 // reciprocal.
-__device__ __forceinline__ float digitize16_quad(const float (&x)[4], uint32_t (&code)[kDigits],
-                                                 uint32_t (&sf)[kDigits], float fixed = 0.f) {
+template <int D>
+__device__ __forceinline__ float digitize16_quad_n(const float (&x)[4], uint32_t (&code)[D], uint32_t (&sf)[D],
+                                                   float fixed = 0.f) {
   float m = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
   m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
   m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
@@ -178,7 +179,7 @@ __device__ __forceinline__ float digitize16_quad(const float (&x)[4], uint32_t (
   m *= p;
   float s = 0.f;
 #pragma unroll
-  for (int d = 0; d < kDigits; ++d) {
+  for (int d = 0; d < D; ++d) {
     float t;
     if (d & 1) {
       t = s * 0.16666668f;   // 1 / 6 rounded up
@@ -204,6 +205,10 @@ __device__ __forceinline__ float digitize16_quad(const float (&x)[4], uint32_t (
     r[3] = fmaf(-s, v1.y, r[3]);
   }
   return p;
+}
+__device__ __forceinline__ float digitize16_quad(const float (&x)[4], uint32_t (&code)[kDigits],
+                                                 uint32_t (&sf)[kDigits], float fixed = 0.f) {
+  return digitize16_quad_n<kDigits>(x, code, sf, fixed);
 }
 
 // the prescale of groups nobody wrote (all-zero digits): never the smallest of a slice

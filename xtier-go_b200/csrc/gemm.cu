@@ -1,0 +1,273 @@
+// K2: the NVFP4 x activation GEMM for prefill chunks and batched rows (matmul_nvfp4's m > 2 path,
+// engine/src/kernels.cpp:84-138, at M = 9 .. 4096) on the block-scaled FP4 tensor cores of sm_100a.
+//
+// The weights are the GEMV's packed units (kernels.h): tile t, K block b = 128 rows x 64 inputs, the codes in the MMA's
+// K-major A layout and the E4M3 block scales in the scale-factor atom, so they stream to the tensor core untouched.
+// tcgen05.mma kind::mxf4nvf4 needs both operands as E2M1 with UE4M3 block scales, so the activations become the B
+// operand as kGDigits scaled E2M1 digits (the GEMV's representation with fewer digits): per activation row one
+// power-of-two prescale p (from the row's max |x|, so that every K block of the row shares it and the products add
+// up in TMEM), per 16-input group and digit a UE4M3 scale. An activation unit is the same 4608-byte format as a weight
+// unit: 128 digit rows (digit d of activation row i of the tile is row 32 d + i) x 64 inputs.
+//
+// One MMA is 128 weight rows x 128 digit rows (32 activation rows) x 64 inputs. A persistent CTA per SM walks the
+// (weight tile, activation tile) pairs, activation tiles fastest, so that the CTAs working at one time share their
+// weight tiles in L2; one thread streams (weight unit, activation unit) stages through a ring (bulk copies), one issues
+// two scale copies and the MMA per stage, four warps drain the double-buffered TMEM accumulator: y = sum of the
+// digit columns / p * global.
+#include <algorithm>
+
+#include "common.cuh"
+#include "fp4mma.cuh"
+#include "kernels.h"
+
+namespace xtg {
+
+namespace {
+
+constexpr int kGDigits = 4;                       // activation digits of the B operand
+constexpr int kActRows = kTileRows / kGDigits;    // activation rows per unit (32)
+constexpr int kGStages = 13;   // ring stages of (weight unit, activation unit); > 114 KB: one CTA per SM
+constexpr int kGThreads = 256;
+constexpr int kGAccCols = 128;                    // TMEM columns per accumulator
+constexpr uint32_t kGTmemCols = 512;              // 2 accumulators + the ring's scale factors
+constexpr uint32_t kIdescGemm = (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+
+struct GemmParams {
+  const uint8_t* w;          // weight units [wtiles][kblocks]
+  int wtiles, kblocks;
+  const uint8_t* act;        // activation units [atiles][kblocks]
+  const float* act_pre;      // [atiles * 32] the rows' prescales
+  int atiles, m;
+  const TileOut* outs;       // [wtiles]
+  int* err;
+};
+
+__device__ __forceinline__ void tc_mma_gemm(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t tsfa, uint32_t tsfb,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(
+          tmem_d),
+      "l"(da), "l"(db), "r"(kIdescGemm), "r"(accumulate), "r"(tsfa), "r"(tsfb)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ GemmParams P) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int KB = P.kblocks, ntiles = P.wtiles * P.atiles;
+  const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
+  uint8_t* ring = smem;   // stage s: weight unit at s * 2 * kUnitBytes, activation unit right after it
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGStages * 2 * kUnitBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kGStages;
+  uint64_t* accfull = bars + 2 * kGStages;    // [2]
+  uint64_t* accempty = bars + 2 * kGStages + 2;   // [2]
+  uint64_t* done = bars + 2 * kGStages + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kGStages + 6);
+
+  if (warp == 2) tmem_alloc(tmem_slot, kGTmemCols);
+  if (tid == 0) {
+    for (int i = 0; i < kGStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accfull[i], 1);
+      mbar_init(&accempty[i], kTileRows);
+    }
+    mbar_init(done, 1);
+    mbar_init_fence();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  auto tile_of = [&](int i, int& wt, int& at) {
+    const int q = (int)blockIdx.x + i * (int)gridDim.x;
+    wt = q / P.atiles;
+    at = q - wt * P.atiles;
+  };
+
+  if (warp == 0) {
+    // ---- producer: stage u of this CTA is unit kb = u % KB of its tile u / KB ----
+    if (lane == 0) {
+      int u = 0;
+      for (int i = 0; i < my_tiles; ++i) {
+        int wt, at;
+        tile_of(i, wt, at);
+        const uint8_t* wsrc = P.w + (int64_t)wt * KB * kUnitBytes;
+        const uint8_t* asrc = P.act + (int64_t)at * KB * kUnitBytes;
+        for (int kb = 0; kb < KB; ++kb, ++u) {
+          const int slot = u % kGStages;
+          if (u >= kGStages) mbar_wait_bounded(&empty[slot], (uint32_t)((u / kGStages) - 1) & 1u, P.err);
+          uint8_t* dst = ring + slot * 2 * kUnitBytes;
+          mbar_expect_tx(&full[slot], 2 * kUnitBytes);
+          bulk_g2s(dst, wsrc + (int64_t)kb * kUnitBytes, kUnitBytes, &full[slot]);
+          bulk_g2s(dst + kUnitBytes, asrc + (int64_t)kb * kUnitBytes, kUnitBytes, &full[slot]);
+        }
+      }
+      // every copy has landed before the CTA may exit (normally long since)
+      for (int v = std::max(0, u - kGStages); v < u; ++v)
+        mbar_wait_bounded(&full[v % kGStages], (uint32_t)(v / kGStages) & 1u, P.err);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA issuer: per stage the two scale atoms to TMEM, then one MMA ----
+    if (lane == 0) {
+      tc_fence_after();
+      const uint32_t ring_addr = smem_u32(ring);
+      const uint32_t sf0 = tbase + 2 * kGAccCols;   // stage s: SFA at sf0 + 8 s, SFB at + 4
+      int u = 0;
+      for (int i = 0; i < my_tiles; ++i) {
+        const int acc = i & 1;
+        if (i >= 2) {
+          mbar_wait_bounded(&accempty[acc], (uint32_t)((i >> 1) - 1) & 1u, P.err);
+          tc_fence_after();
+        }
+        for (int kb = 0; kb < KB; ++kb, ++u) {
+          const int slot = u % kGStages;
+          mbar_wait_bounded(&full[slot], (uint32_t)(u / kGStages) & 1u, P.err);
+          tc_fence_after();
+          const uint32_t a_addr = ring_addr + (uint32_t)(slot * 2 * kUnitBytes), b_addr = a_addr + kUnitBytes;
+          const uint32_t sfa = sf0 + 8 * (uint32_t)slot, sfb = sfa + 4;
+          tc_cp_sf(sfa, sf_desc(a_addr + kUnitCodeBytes));
+          tc_cp_sf(sfb, sf_desc(b_addr + kUnitCodeBytes));
+          tc_mma_gemm(tbase + (uint32_t)(acc * kGAccCols), a_desc(a_addr), a_desc(b_addr), sfa, sfb,
+                      kb > 0 ? 1u : 0u);
+          tc_commit(&empty[slot]);
+        }
+        tc_commit(&accfull[acc]);
+      }
+      tc_commit(done);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ---- epilogue: TMEM lane quarter q = warp - 4 holds weight rows 32 q .. 32 q + 31 ----
+    const int q = warp - 4, r = 32 * q + lane;
+    for (int i = 0; i < my_tiles; ++i) {
+      int wt, at;
+      tile_of(i, wt, at);
+      const int acc = i & 1;
+      // the tile's output and its rows' prescales are loaded before the wait
+      const TileOut o = P.outs[wt];
+      float inv[kActRows];
+#pragma unroll
+      for (int ii = 0; ii < kActRows; ++ii) inv[ii] = 1.f / P.act_pre[at * kActRows + ii];
+      mbar_wait_bounded(&accfull[acc], (uint32_t)(i >> 1) & 1u, lane == 0 ? P.err : nullptr);
+      tc_fence_after();
+      float y[kActRows];
+      const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * kGAccCols);
+#pragma unroll
+      for (int d = 0; d < kGDigits; ++d) {
+        float v[kActRows];
+        tmem_ld16(taddr + 32 * d, *reinterpret_cast<float(*)[16]>(&v[0]));
+        tmem_ld16(taddr + 32 * d + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
+        tmem_ld_wait();
+#pragma unroll
+        for (int ii = 0; ii < kActRows; ++ii) y[ii] = d == 0 ? v[ii] : y[ii] + v[ii];
+      }
+      tc_fence_before();
+      mbar_arrive(&accempty[acc]);
+      const float g = r < 64 ? o.global_lo : o.global_hi;
+      if (r < o.rows)
+#pragma unroll
+        for (int ii = 0; ii < kActRows; ++ii) {
+          const int row = at * kActRows + ii;
+          if (row < P.m) o.y[(int64_t)row * o.ld + r] = y[ii] * inv[ii] * g;
+        }
+    }
+  }
+  // ---- teardown: every tcgen05 operation has completed before the columns go back ----
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) {
+    if (lane == 0) mbar_wait_bounded(done, 0, P.err);
+    __syncwarp();
+    tmem_dealloc(tbase, kGTmemCols);
+  }
+}
+
+// One CTA per activation row (grid: every row of the activation tiles; rows past m get zero digits): the row's max
+// |x| gives its prescale, then the quads of threads digitize its 16-input groups.
+__global__ void __launch_bounds__(256) act_digitize_kernel(const float* x, int m, int k, int kblocks, uint8_t* act,
+                                                          float* act_pre) {
+  __shared__ float red[8];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const bool live = row < m;
+  const float* xr = x + (int64_t)row * k;
+  float mx = 0.f;
+  if (live)
+    for (int c = tid * 4; c < k; c += 256 * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(xr + c);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+  mx = warp_max(mx);
+  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+  const float p = block_prescale(mx);
+  if (tid == 0) act_pre[row] = p;
+  const int groups = k / 16, i = row % kActRows;
+  uint8_t* units = act + (int64_t)(row / kActRows) * kblocks * kUnitBytes;
+  for (int g0 = 0; g0 < groups; g0 += 64) {   // 64 groups per pass, a quad each; every lane takes part
+    const int g = g0 + (tid >> 2), t = tid & 3;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (live && g < groups) {
+      const float4 x4 = *reinterpret_cast<const float4*>(xr + 16 * g + 4 * t);
+      v[0] = x4.x; v[1] = x4.y; v[2] = x4.z; v[3] = x4.w;
+    }
+    uint32_t code[kGDigits], sf[kGDigits];
+    digitize16_quad_n<kGDigits>(v, code, sf, p);
+    if (g < groups) {
+      uint8_t* unit = units + (int64_t)(g >> 2) * kUnitBytes;
+      const int j = g & 3;
+#pragma unroll
+      for (int d = 0; d < kGDigits; ++d) {
+        const int n = kActRows * d + i;
+        *reinterpret_cast<uint16_t*>(unit + a_code_offset(n, 16 * j + 4 * t)) = (uint16_t)code[d];
+        if (t == 0) unit[kUnitCodeBytes + sf_offset(n, j)] = (uint8_t)sf[d];
+      }
+    }
+  }
+}
+
+}  // namespace
+
+int64_t gemm_act_bytes(int m, int k) { return (int64_t)((m + kActRows - 1) / kActRows) * packed_kblocks(k) * kUnitBytes; }
+
+void gemm_digitize(const float* x, int m, int k, uint8_t* act, float* act_pre, cudaStream_t s) {
+  XTG_REQUIRE(m >= 1 && k % 16 == 0, "gemm: m >= 1 rows, k a multiple of 16");
+  const int atiles = (m + kActRows - 1) / kActRows;
+  act_digitize_kernel<<<atiles * kActRows, 256, 0, s>>>(x, m, k, packed_kblocks(k), act, act_pre);
+  XTG_CUDA(cudaGetLastError());
+}
+
+void launch_gemm(const uint8_t* w, int wtiles, int kblocks, const uint8_t* act, const float* act_pre, int m,
+                 const TileOut* outs, int num_sms, int* err, cudaStream_t s) {
+  XTG_REQUIRE(m >= 1 && wtiles >= 1 && kblocks >= 1, "gemm: empty problem");
+  GemmParams P = {};
+  P.w = w;
+  P.wtiles = wtiles;
+  P.kblocks = kblocks;
+  P.act = act;
+  P.act_pre = act_pre;
+  P.atiles = (m + kActRows - 1) / kActRows;
+  P.m = m;
+  P.outs = outs;
+  P.err = err;
+  const size_t smem = (size_t)kGStages * 2 * kUnitBytes + (2 * kGStages + 8) * 8;
+  static bool attr_set = false;
+  if (!attr_set) {
+    XTG_CUDA(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set = true;
+  }
+  const int ntiles = wtiles * P.atiles;
+  gemm_kernel<<<std::min(ntiles, num_sms), kGThreads, smem, s>>>(P);
+  XTG_CUDA(cudaGetLastError());
+}
+
+}  // namespace xtg

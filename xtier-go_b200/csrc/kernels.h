@@ -118,4 +118,13 @@ void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, 
 // x f32 [m][k] (k a multiple of 16; rows m..7 zero) -> B digits xb [kblocks][2048] and prescales xb_pre [k / 16][8]
 void digitize_rows(const float* x, int m, int k, uint8_t* xb, float* xb_pre, cudaStream_t s);
 
+// ---- the GEMM (gemm.cu): y[m][n] = x[m][k] W^T for prefill chunks and batches ----
+constexpr int kMaxGemmRows = 65536;
+// Activation units: [ceil(m / 32)][kblocks] of 4608 bytes (4 digits x 32 rows per unit) and a prescale per row.
+int64_t gemm_act_bytes(int m, int k);
+void gemm_digitize(const float* x, int m, int k, uint8_t* act, float* act_pre, cudaStream_t s);
+// weights: the packed units of wtiles tiles; outs[t] as for the GEMV's STORE epilogue (y[row * ld + r])
+void launch_gemm(const uint8_t* w, int wtiles, int kblocks, const uint8_t* act, const float* act_pre, int m,
+                 const TileOut* outs, int num_sms, int* err, cudaStream_t s);
+
 }  // namespace xtg
