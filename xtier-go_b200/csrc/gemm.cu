@@ -26,7 +26,9 @@ namespace {
 
 constexpr int kGDigits = 4;                       // activation digits of the B operand
 constexpr int kActRows = kTileRows / kGDigits;    // activation rows per unit (32)
-constexpr int kGStages = 13;   // ring stages of (weight unit, activation unit); > 114 KB: one CTA per SM
+constexpr int kGUnits = 4;      // K blocks per ring stage: one bulk copy of weight units, one of activation units
+constexpr int kGStageBytes = 2 * kGUnits * kUnitBytes;
+constexpr int kGStages = 4;     // ring stages (147 KB: one CTA per SM, which owns all 512 TMEM columns)
 constexpr int kGThreads = 256;
 constexpr int kGAccCols = 128;                    // TMEM columns per accumulator
 constexpr uint32_t kGTmemCols = 512;              // 2 accumulators + the ring's scale factors
@@ -57,8 +59,8 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int KB = P.kblocks, ntiles = P.wtiles * P.atiles;
   const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
-  uint8_t* ring = smem;   // stage s: weight unit at s * 2 * kUnitBytes, activation unit right after it
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGStages * 2 * kUnitBytes);
+  uint8_t* ring = smem;   // stage s: kGUnits weight units at s * kGStageBytes, then kGUnits activation units
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGStages * kGStageBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kGStages;
   uint64_t* accfull = bars + 2 * kGStages;    // [2]
@@ -89,8 +91,10 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     at = q - wt * P.atiles;
   };
 
+  // a tile's K blocks go in stages of kGUnits (the last one may be short); stages never span tiles
+  const int spt = (KB + kGUnits - 1) / kGUnits;
   if (warp == 0) {
-    // ---- producer: stage u of this CTA is unit kb = u % KB of its tile u / KB ----
+    // ---- producer: stage u of this CTA is stage u % spt of its tile u / spt ----
     if (lane == 0) {
       int u = 0;
       for (int i = 0; i < my_tiles; ++i) {
@@ -98,13 +102,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         tile_of(i, wt, at);
         const uint8_t* wsrc = P.w + (int64_t)wt * KB * kUnitBytes;
         const uint8_t* asrc = P.act + (int64_t)at * KB * kUnitBytes;
-        for (int kb = 0; kb < KB; ++kb, ++u) {
-          const int slot = u % kGStages;
+        for (int st = 0; st < spt; ++st, ++u) {
+          const int slot = u % kGStages, kb0 = st * kGUnits, cnt = min(kGUnits, KB - kb0);
           if (u >= kGStages) mbar_wait_bounded(&empty[slot], (uint32_t)((u / kGStages) - 1) & 1u, P.err);
-          uint8_t* dst = ring + slot * 2 * kUnitBytes;
-          mbar_expect_tx(&full[slot], 2 * kUnitBytes);
-          bulk_g2s(dst, wsrc + (int64_t)kb * kUnitBytes, kUnitBytes, &full[slot]);
-          bulk_g2s(dst + kUnitBytes, asrc + (int64_t)kb * kUnitBytes, kUnitBytes, &full[slot]);
+          uint8_t* dst = ring + slot * kGStageBytes;
+          mbar_expect_tx(&full[slot], (uint32_t)(2 * cnt * kUnitBytes));
+          bulk_g2s(dst, wsrc + (int64_t)kb0 * kUnitBytes, (uint32_t)(cnt * kUnitBytes), &full[slot]);
+          bulk_g2s(dst + kGUnits * kUnitBytes, asrc + (int64_t)kb0 * kUnitBytes, (uint32_t)(cnt * kUnitBytes),
+                   &full[slot]);
         }
       }
       // every copy has landed before the CTA may exit (normally long since)
@@ -113,28 +118,38 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---- MMA issuer: per stage the two scale atoms to TMEM, then one MMA ----
+    // ---- MMA issuer: per K block the two scale atoms to TMEM, then one MMA; a full stage is straight-line code ----
     if (lane == 0) {
       tc_fence_after();
       const uint32_t ring_addr = smem_u32(ring);
-      const uint32_t sf0 = tbase + 2 * kGAccCols;   // stage s: SFA at sf0 + 8 s, SFB at + 4
+      const uint32_t sf0 = tbase + 2 * kGAccCols;   // stage s, unit j: SFA at sf0 + 8 (kGUnits s + j), SFB at + 4
       int u = 0;
       for (int i = 0; i < my_tiles; ++i) {
         const int acc = i & 1;
+        const uint32_t tacc = tbase + (uint32_t)(acc * kGAccCols);
         if (i >= 2) {
           mbar_wait_bounded(&accempty[acc], (uint32_t)((i >> 1) - 1) & 1u, P.err);
           tc_fence_after();
         }
-        for (int kb = 0; kb < KB; ++kb, ++u) {
-          const int slot = u % kGStages;
+        for (int st = 0; st < spt; ++st, ++u) {
+          const int slot = u % kGStages, kb0 = st * kGUnits, cnt = min(kGUnits, KB - kb0);
           mbar_wait_bounded(&full[slot], (uint32_t)(u / kGStages) & 1u, P.err);
           tc_fence_after();
-          const uint32_t a_addr = ring_addr + (uint32_t)(slot * 2 * kUnitBytes), b_addr = a_addr + kUnitBytes;
-          const uint32_t sfa = sf0 + 8 * (uint32_t)slot, sfb = sfa + 4;
-          tc_cp_sf(sfa, sf_desc(a_addr + kUnitCodeBytes));
-          tc_cp_sf(sfb, sf_desc(b_addr + kUnitCodeBytes));
-          tc_mma_gemm(tbase + (uint32_t)(acc * kGAccCols), a_desc(a_addr), a_desc(b_addr), sfa, sfb,
-                      kb > 0 ? 1u : 0u);
+          const uint32_t a0 = ring_addr + (uint32_t)(slot * kGStageBytes), b0 = a0 + kGUnits * kUnitBytes;
+          const uint32_t sfs = sf0 + 8 * kGUnits * (uint32_t)slot;
+          auto unit = [&](int j) {
+            const uint32_t au = a0 + (uint32_t)(j * kUnitBytes), bu = b0 + (uint32_t)(j * kUnitBytes);
+            const uint32_t sfa = sfs + 8 * (uint32_t)j;
+            tc_cp_sf(sfa, sf_desc(au + kUnitCodeBytes));
+            tc_cp_sf(sfa + 4, sf_desc(bu + kUnitCodeBytes));
+            tc_mma_gemm(tacc, a_desc(au), a_desc(bu), sfa, sfa + 4, (kb0 + j) > 0 ? 1u : 0u);
+          };
+          if (cnt == kGUnits) {
+#pragma unroll
+            for (int j = 0; j < kGUnits; ++j) unit(j);
+          } else {
+            for (int j = 0; j < cnt; ++j) unit(j);
+          }
           tc_commit(&empty[slot]);
         }
         tc_commit(&accfull[acc]);
@@ -259,7 +274,7 @@ void launch_gemm(const uint8_t* w, int wtiles, int kblocks, const uint8_t* act, 
   P.m = m;
   P.outs = outs;
   P.err = err;
-  const size_t smem = (size_t)kGStages * 2 * kUnitBytes + (2 * kGStages + 8) * 8;
+  const size_t smem = (size_t)kGStages * kGStageBytes + (2 * kGStages + 8) * 8;
   static bool attr_set = false;
   if (!attr_set) {
     XTG_CUDA(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
