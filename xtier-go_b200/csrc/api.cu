@@ -129,7 +129,7 @@ int xtg_cuda_linear_forward(xtg_cuda_linear* L, const float* x, int m, float* co
         L->act = nullptr;
         L->act_pre = nullptr;
         L->act_rows = 0;
-        const int rows = ((m + 31) / 32) * 32;
+        const int rows = gemm_padded_rows(m);
         XTG_CUDA(cudaMalloc(&L->act, (size_t)gemm_act_bytes(rows, L->k)));
         XTG_CUDA(cudaMemset(L->act, 0, (size_t)gemm_act_bytes(rows, L->k)));   // K padding stays zero
         XTG_CUDA(cudaMalloc(&L->act_pre, (size_t)rows * sizeof(float)));

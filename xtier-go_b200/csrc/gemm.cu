@@ -6,14 +6,16 @@
 // tcgen05.mma kind::mxf4nvf4 needs both operands as E2M1 with UE4M3 block scales, so the activations become the B
 // operand as kGDigits scaled E2M1 digits (the GEMV's representation with fewer digits): per activation row one
 // power-of-two prescale p (from the row's max |x|, so that every K block of the row shares it and the products add
-// up in TMEM), per 16-input group and digit a UE4M3 scale. An activation unit is the same 4608-byte format as a weight
-// unit: 128 digit rows (digit d of activation row i of the tile is row 32 d + i) x 64 inputs.
+// up in TMEM), per 16-input group and digit a UE4M3 scale. An activation unit (9216 bytes) holds 256 digit rows
+// (digit d of activation row i of the tile is row 64 d + i) x 64 inputs in the weight unit's K-major layout, then
+// the scale atoms of digit rows 0-127 and 128-255.
 //
-// One MMA is 128 weight rows x 128 digit rows (32 activation rows) x 64 inputs. A persistent CTA per SM walks the
-// (weight tile, activation tile) pairs, activation tiles fastest, so that the CTAs working at one time share their
-// weight tiles in L2; one thread streams (weight unit, activation unit) stages through a ring (bulk copies), one issues
-// two scale copies and the MMA per stage, four warps drain the double-buffered TMEM accumulator: y = sum of the
-// digit columns / p * global.
+// One MMA is 128 weight rows x 256 digit rows (64 activation rows) x 64 inputs: N = 256 takes one MMA and three scale
+// copies per 4 MB of FP4 products, which is what the single issuing thread can keep up with. A persistent CTA per SM
+// walks the (weight tile, activation tile) pairs, activation tiles fastest, so that the CTAs working at one time
+// share their weight tiles in L2; one thread streams stages of 4 K blocks (weight units, activation units) through a
+// ring (bulk copies), one issues the scale copies and the MMAs, four warps drain the TMEM accumulator (read out digit
+// by digit, released before the arithmetic and the stores): y = sum of the digit columns / p * global.
 #include <algorithm>
 
 #include "common.cuh"
@@ -25,20 +27,25 @@ namespace xtg {
 namespace {
 
 constexpr int kGDigits = 4;                       // activation digits of the B operand
-constexpr int kActRows = kTileRows / kGDigits;    // activation rows per unit (32)
+constexpr int kGN = 256;                          // the MMA's N: digit rows
+constexpr int kActRows = kGN / kGDigits;          // activation rows per unit (64)
+constexpr int kActCodeBytes = kGN * 32;           // 8192
+constexpr int kActUnitBytes = kActCodeBytes + 2 * 512;
 constexpr int kGUnits = 4;      // K blocks per ring stage: one bulk copy of weight units, one of activation units
-constexpr int kGStageBytes = 2 * kGUnits * kUnitBytes;
-constexpr int kGStages = 4;     // ring stages (147 KB: one CTA per SM, which owns all 512 TMEM columns)
+constexpr int kGStageBytes = kGUnits * (kUnitBytes + kActUnitBytes);
+constexpr int kGStages = 3;     // ring stages (166 KB: one CTA per SM, which owns the TMEM it allocates)
 constexpr int kGThreads = 256;
-constexpr int kGAccCols = 128;                    // TMEM columns per accumulator
-constexpr uint32_t kGTmemCols = 512;              // 2 accumulators + the ring's scale factors
-constexpr uint32_t kIdescGemm = (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+constexpr int kGAccCols = kGN;                    // TMEM columns of the accumulator
+constexpr int kGSfCols = 12;                      // per K block: the weight scales (4 columns), the activations' (8)
+constexpr uint32_t kGTmemCols = 512;              // the accumulator + the ring's scale factors
+constexpr uint32_t kIdescGemm = (1u << 7) | (1u << 10) | ((uint32_t)(kGN >> 3) << 17) | ((128u >> 4) << 24);
+static_assert(kGAccCols + kGStages * kGUnits * kGSfCols <= (int)kGTmemCols, "TMEM columns");
 
 struct GemmParams {
   const uint8_t* w;          // weight units [wtiles][kblocks]
   int wtiles, kblocks;
   const uint8_t* act;        // activation units [atiles][kblocks]
-  const float* act_pre;      // [atiles * 32] the rows' prescales
+  const float* act_pre;      // [atiles * 64] the rows' prescales
   int atiles, m;
   const TileOut* outs;       // [wtiles]
   int* err;
@@ -63,7 +70,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGStages * kGStageBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + kGStages;
-  uint64_t* accfull = bars + 2 * kGStages;    // [2]
+  uint64_t* accfull = bars + 2 * kGStages;        // [2] (phases alternate per tile)
   uint64_t* accempty = bars + 2 * kGStages + 2;   // [2]
   uint64_t* done = bars + 2 * kGStages + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kGStages + 6);
@@ -101,14 +108,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
         int wt, at;
         tile_of(i, wt, at);
         const uint8_t* wsrc = P.w + (int64_t)wt * KB * kUnitBytes;
-        const uint8_t* asrc = P.act + (int64_t)at * KB * kUnitBytes;
+        const uint8_t* asrc = P.act + (int64_t)at * KB * kActUnitBytes;
         for (int st = 0; st < spt; ++st, ++u) {
           const int slot = u % kGStages, kb0 = st * kGUnits, cnt = min(kGUnits, KB - kb0);
           if (u >= kGStages) mbar_wait_bounded(&empty[slot], (uint32_t)((u / kGStages) - 1) & 1u, P.err);
           uint8_t* dst = ring + slot * kGStageBytes;
-          mbar_expect_tx(&full[slot], (uint32_t)(2 * cnt * kUnitBytes));
+          mbar_expect_tx(&full[slot], (uint32_t)(cnt * (kUnitBytes + kActUnitBytes)));
           bulk_g2s(dst, wsrc + (int64_t)kb0 * kUnitBytes, (uint32_t)(cnt * kUnitBytes), &full[slot]);
-          bulk_g2s(dst + kGUnits * kUnitBytes, asrc + (int64_t)kb0 * kUnitBytes, (uint32_t)(cnt * kUnitBytes),
+          bulk_g2s(dst + kGUnits * kUnitBytes, asrc + (int64_t)kb0 * kActUnitBytes, (uint32_t)(cnt * kActUnitBytes),
                    &full[slot]);
         }
       }
@@ -122,13 +129,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
     if (lane == 0) {
       tc_fence_after();
       const uint32_t ring_addr = smem_u32(ring);
-      const uint32_t sf0 = tbase + 2 * kGAccCols;   // stage s, unit j: SFA at sf0 + 8 (kGUnits s + j), SFB at + 4
+      const uint32_t sf0 = tbase + kGAccCols;   // stage s, unit j: SFA at sf0 + 12 (kGUnits s + j), SFB at + 4, + 8
       int u = 0;
       for (int i = 0; i < my_tiles; ++i) {
         const int acc = i & 1;
-        const uint32_t tacc = tbase + (uint32_t)(acc * kGAccCols);
-        if (i >= 2) {
-          mbar_wait_bounded(&accempty[acc], (uint32_t)((i >> 1) - 1) & 1u, P.err);
+        const uint32_t tacc = tbase;
+        if (i >= 1) {   // the epilogue has read the previous tile's accumulator out
+          mbar_wait_bounded(&accempty[acc ^ 1], (uint32_t)((i - 1) >> 1) & 1u, P.err);
           tc_fence_after();
         }
         for (int st = 0; st < spt; ++st, ++u) {
@@ -136,12 +143,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
           mbar_wait_bounded(&full[slot], (uint32_t)(u / kGStages) & 1u, P.err);
           tc_fence_after();
           const uint32_t a0 = ring_addr + (uint32_t)(slot * kGStageBytes), b0 = a0 + kGUnits * kUnitBytes;
-          const uint32_t sfs = sf0 + 8 * kGUnits * (uint32_t)slot;
+          const uint32_t sfs = sf0 + kGSfCols * kGUnits * (uint32_t)slot;
           auto unit = [&](int j) {
-            const uint32_t au = a0 + (uint32_t)(j * kUnitBytes), bu = b0 + (uint32_t)(j * kUnitBytes);
-            const uint32_t sfa = sfs + 8 * (uint32_t)j;
+            const uint32_t au = a0 + (uint32_t)(j * kUnitBytes), bu = b0 + (uint32_t)(j * kActUnitBytes);
+            const uint32_t sfa = sfs + kGSfCols * (uint32_t)j;
             tc_cp_sf(sfa, sf_desc(au + kUnitCodeBytes));
-            tc_cp_sf(sfa + 4, sf_desc(bu + kUnitCodeBytes));
+            tc_cp_sf(sfa + 4, sf_desc(bu + kActCodeBytes));
+            tc_cp_sf(sfa + 8, sf_desc(bu + kActCodeBytes + 512));
             tc_mma_gemm(tacc, a_desc(au), a_desc(bu), sfa, sfa + 4, (kb0 + j) > 0 ? 1u : 0u);
           };
           if (cnt == kGUnits) {
@@ -164,32 +172,30 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       int wt, at;
       tile_of(i, wt, at);
       const int acc = i & 1;
-      // the tile's output and its rows' prescales are loaded before the wait
-      const TileOut o = P.outs[wt];
-      float inv[kActRows];
-#pragma unroll
-      for (int ii = 0; ii < kActRows; ++ii) inv[ii] = 1.f / P.act_pre[at * kActRows + ii];
+      const TileOut o = P.outs[wt];   // loaded before the wait
       mbar_wait_bounded(&accfull[acc], (uint32_t)(i >> 1) & 1u, lane == 0 ? P.err : nullptr);
       tc_fence_after();
       float y[kActRows];
-      const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * kGAccCols);
+      const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16);
 #pragma unroll
       for (int d = 0; d < kGDigits; ++d) {
-        float v[kActRows];
-        tmem_ld16(taddr + 32 * d, *reinterpret_cast<float(*)[16]>(&v[0]));
-        tmem_ld16(taddr + 32 * d + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
-        tmem_ld_wait();
 #pragma unroll
-        for (int ii = 0; ii < kActRows; ++ii) y[ii] = d == 0 ? v[ii] : y[ii] + v[ii];
+        for (int c = 0; c < kActRows; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + (uint32_t)(kActRows * d + c), v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int ii = 0; ii < 16; ++ii) y[c + ii] = d == 0 ? v[ii] : y[c + ii] + v[ii];
+        }
       }
       tc_fence_before();
-      mbar_arrive(&accempty[acc]);
+      mbar_arrive(&accempty[acc]);   // the next tile's products may start
       const float g = r < 64 ? o.global_lo : o.global_hi;
       if (r < o.rows)
 #pragma unroll
         for (int ii = 0; ii < kActRows; ++ii) {
           const int row = at * kActRows + ii;
-          if (row < P.m) o.y[(int64_t)row * o.ld + r] = y[ii] * inv[ii] * g;
+          if (row < P.m) o.y[(int64_t)row * o.ld + r] = y[ii] * (1.f / P.act_pre[row]) * g;   // p: a power of two
         }
     }
   }
@@ -227,7 +233,7 @@ __global__ void __launch_bounds__(256) act_digitize_kernel(const float* x, int m
   const float p = block_prescale(mx);
   if (tid == 0) act_pre[row] = p;
   const int groups = k / 16, i = row % kActRows;
-  uint8_t* units = act + (int64_t)(row / kActRows) * kblocks * kUnitBytes;
+  uint8_t* units = act + (int64_t)(row / kActRows) * kblocks * kActUnitBytes;
   for (int g0 = 0; g0 < groups; g0 += 64) {   // 64 groups per pass, a quad each; every lane takes part
     const int g = g0 + (tid >> 2), t = tid & 3;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -238,13 +244,13 @@ __global__ void __launch_bounds__(256) act_digitize_kernel(const float* x, int m
     uint32_t code[kGDigits], sf[kGDigits];
     digitize16_quad_n<kGDigits>(v, code, sf, p);
     if (g < groups) {
-      uint8_t* unit = units + (int64_t)(g >> 2) * kUnitBytes;
+      uint8_t* unit = units + (int64_t)(g >> 2) * kActUnitBytes;
       const int j = g & 3;
 #pragma unroll
       for (int d = 0; d < kGDigits; ++d) {
         const int n = kActRows * d + i;
         *reinterpret_cast<uint16_t*>(unit + a_code_offset(n, 16 * j + 4 * t)) = (uint16_t)code[d];
-        if (t == 0) unit[kUnitCodeBytes + sf_offset(n, j)] = (uint8_t)sf[d];
+        if (t == 0) unit[kActCodeBytes + (n >> 7) * 512 + sf_offset(n & 127, j)] = (uint8_t)sf[d];
       }
     }
   }
@@ -252,7 +258,11 @@ __global__ void __launch_bounds__(256) act_digitize_kernel(const float* x, int m
 
 }  // namespace
 
-int64_t gemm_act_bytes(int m, int k) { return (int64_t)((m + kActRows - 1) / kActRows) * packed_kblocks(k) * kUnitBytes; }
+int gemm_padded_rows(int m) { return ((m + kActRows - 1) / kActRows) * kActRows; }
+
+int64_t gemm_act_bytes(int m, int k) {
+  return (int64_t)((m + kActRows - 1) / kActRows) * packed_kblocks(k) * kActUnitBytes;
+}
 
 void gemm_digitize(const float* x, int m, int k, uint8_t* act, float* act_pre, cudaStream_t s) {
   XTG_REQUIRE(m >= 1 && k % 16 == 0, "gemm: m >= 1 rows, k a multiple of 16");

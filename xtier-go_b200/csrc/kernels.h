@@ -120,7 +120,8 @@ void digitize_rows(const float* x, int m, int k, uint8_t* xb, float* xb_pre, cud
 
 // ---- the GEMM (gemm.cu): y[m][n] = x[m][k] W^T for prefill chunks and batches ----
 constexpr int kMaxGemmRows = 65536;
-// Activation units: [ceil(m / 32)][kblocks] of 4608 bytes (4 digits x 32 rows per unit) and a prescale per row.
+// Activation units: [ceil(m / 64)][kblocks] of 9216 bytes (4 digits x 64 rows per unit) and a prescale per row.
+int gemm_padded_rows(int m);   // rows of the activation tiles (a multiple of 64)
 int64_t gemm_act_bytes(int m, int k);
 void gemm_digitize(const float* x, int m, int k, uint8_t* act, float* act_pre, cudaStream_t s);
 // weights: the packed units of wtiles tiles; outs[t] as for the GEMV's STORE epilogue (y[row * ld + r])
