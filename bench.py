@@ -54,6 +54,13 @@ def peaks():
     return FALLBACK_HBM, "fallback"
 
 
+def peaks_bf16():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops"])
+    return 1590.0
+
+
 def ncu_traffic():
     """dram bytes per GEMV launch from the committed ncu summary (profiles/), or None."""
     p = os.path.join(ROOT, "profiles", "gemv_nvfp4_dory3072.txt")
@@ -284,6 +291,55 @@ def max_over_ranks(v, dist, device="cuda"):
     return float(t.item())
 
 
+GEMM_SETS = [("qkvg", [3072, 768, 768, 3072], 3072), ("o", [3072], 3072), ("gate_up", [9216, 9216], 3072),
+             ("down", [3072], 9216)]
+
+
+def gemm_block(x, device, m=512, reps=6):
+    """BASELINE config 1 at M = 512 (a prefill chunk) through the library's linear API on the tcgen05 GEMM: each
+    projection set of the sublayer with seeded random NVFP4 weights (3 copies rotated), x ~ N(0, 1). Device time of
+    the GEMM kernel and of the activation digitizer from the CUDA activity timeline; FLOPs = 2 M N K. The FP4 MMA work
+    is 4x that (4 activation digits); its peak is taken as 4x the measured dense bf16 GEMM peak."""
+    import re
+    import torch
+    from torch.profiler import profile, ProfilerActivity
+    g = torch.Generator(device=device)
+    g.manual_seed(1)
+    out = {}
+    for name, outs, k in GEMM_SETS:
+        lins = []
+        for _ in range(3):
+            ws = [(torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=device, generator=g),
+                   torch.randint(0x30, 0x40, (n, k // 16), dtype=torch.uint8, device=device, generator=g), 1.0)
+                  for n in outs]
+            lins.append(x.Linear(ws, k))
+        xin = torch.randn(m, k, device=device, generator=g)
+        ys = [torch.empty(m, n, device=device) for n in outs]
+        for it in range(6):
+            lins[it % 3](xin, ys)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for it in range(reps):
+                lins[it % 3](xin, ys)
+            torch.cuda.synchronize()
+        tot = {}
+        for ev in prof.events():
+            if ev.device_type == torch.autograd.DeviceType.CUDA:
+                mm = re.search(r"(\w+_kernel)", ev.name)
+                if mm:
+                    d = tot.setdefault(mm.group(1), [0, 0.0])
+                    d[0] += 1
+                    d[1] += ev.device_time_total
+        gemm_us = tot["gemm_kernel"][1] / tot["gemm_kernel"][0]
+        dig_us = tot["act_digitize_kernel"][1] / tot["act_digitize_kernel"][0]
+        flops = 2.0 * m * sum(outs) * k
+        out[name] = {"n": sum(outs), "k": k, "gemm_us": gemm_us, "digitize_us": dig_us,
+                     "tflops": flops / gemm_us / 1e6, "tflops_with_digitize": flops / (gemm_us + dig_us) / 1e6}
+        for l_ in lins:
+            l_.close()
+    return out
+
+
 def job_rows_per_s(world, ms_per_step):
     """Whole-job throughput: every rank verifies 8 rows of its own sequence per step (weak scaling)."""
     return world * 8.0 / (ms_per_step / 1e3)
@@ -330,6 +386,7 @@ def run_ours(args, rank, world, local_rank, dist):
     traffic = ncu_traffic()
     info = s.info()
     s.close()
+    gemm = gemm_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     if rank != 0:
         return
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -351,6 +408,17 @@ def run_ours(args, rank, world, local_rank, dist):
             "clocks": clk.summary(),
             "library": {"splits_global": info.get("splits_global"), "splits_ring": info.get("splits_ring"),
                         "graph": info.get("graph"), "pdl": info.get("pdl")}}
+    if gemm:
+        tot_flops = sum(2.0 * 512 * v["n"] * v["k"] for v in gemm.values())
+        tot_us = sum(v["gemm_us"] for v in gemm.values())
+        bf16 = peaks_bf16()
+        line["prefill_gemm"] = {
+            "config": "config1 projection set at M=512 (QKVG 7680, O 3072, gate+up 18432, down 3072x9216), tcgen05 "
+                      "mxf4nvf4, activations as 4 E2M1 digits", "per_projection": gemm,
+            "total_gemm_us": tot_us, "tflops": tot_flops / tot_us / 1e6,
+            "roofline": {"bound": "tensor", "achieved_fp4_mma_tflops": 4 * tot_flops / tot_us / 1e6,
+                         "peak": 4 * bf16, "unit": "TFLOP/s", "frac": 4 * tot_flops / tot_us / 1e6 / (4 * bf16),
+                         "peak_kind": "4x measured bf16 dense (burst)"}}
     if world == 1 and not args.no_cpu_baseline:
         try:
             step_s, detail, counts = reference_sample(model, os.cpu_count() or 1, 1, 0)
@@ -371,11 +439,30 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the config-1 M=512 prefill GEMM measurement")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling driver: run this many eager steps (no graph, no JSON) for ncu, then exit")
     ap.add_argument("--ncu-model", default="full", choices=["full", "small"],
                     help="small: the same shapes with 2 + 2 + 2 sublayers (about 0.5 GB on the device)")
+    ap.add_argument("--ncu-gemm", type=int, default=0,
+                    help="profiling driver: run the config-1 gate+up GEMM at M=512 this many times, then exit")
     args = ap.parse_args()
+    if args.ncu_gemm:
+        import torch
+        x = package()
+        g = torch.Generator(device="cuda")
+        g.manual_seed(1)
+        k = 3072
+        ws = [(torch.randint(0, 256, (9216, k // 2), dtype=torch.uint8, device="cuda", generator=g),
+               torch.randint(0x30, 0x40, (9216, k // 16), dtype=torch.uint8, device="cuda", generator=g), 1.0)
+              for _ in range(2)]
+        lin = x.Linear(ws, k)
+        xin = torch.randn(512, k, device="cuda", generator=g)
+        for _ in range(args.ncu_gemm):
+            lin(xin)
+        torch.cuda.synchronize()
+        lin.close()
+        return
     if args.ncu_steps:
         x = package()
         model = dict(x.DORY_3072)
