@@ -340,6 +340,100 @@ def gemm_block(x, device, m=512, reps=6):
     return out
 
 
+def kernel_times(prof):
+    """Mean device time (us) per kernel name (the `*_kernel` symbol) from a torch.profiler CUDA timeline."""
+    import re
+    import torch
+    tot = {}
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            mm = re.search(r"(\w+_kernel)", ev.name)
+            if mm:
+                d = tot.setdefault(mm.group(1), [0, 0.0])
+                d[0] += 1
+                d[1] += ev.device_time_total
+    return {k: v[1] / v[0] for k, v in tot.items()}
+
+
+def config0_block(x, device, copies=16, reps=32):
+    """one NVFP4 GEMV at M = 1 through the linear API, 9216 x 3072 and 3072 x 9216, 16 weight
+    copies rotated (> L2). Device time of the GEMV kernel (the activation digitizer listed apart); algorithmic bytes
+    as SURVEY 8(d) counts them (codes + scales + global + x bf16 + y f32)."""
+    import torch
+    from torch.profiler import profile, ProfilerActivity
+    g = torch.Generator(device=device)
+    g.manual_seed(0)
+    peak, peak_kind = peaks()
+    out = {}
+    for n, k, alg in ((9216, 3072, 15968260), (3072, 9216, 15955972)):
+        lins = [x.Linear([(torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=device, generator=g),
+                           torch.randint(0x30, 0x40, (n, k // 16), dtype=torch.uint8, device=device, generator=g),
+                           1.0)], k) for _ in range(copies)]
+        xin = torch.randn(1, k, device=device, generator=g)
+        ys = [torch.empty(1, n, device=device)]
+        for it in range(copies):
+            lins[it](xin, ys)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for it in range(reps):
+                lins[it % copies](xin, ys)
+            torch.cuda.synchronize()
+        t = kernel_times(prof)
+        us = t["gemv_kernel"]
+        out[f"{n}x{k}"] = {"gemv_us": us, "digitize_us": t.get("digitize_rows_kernel"), "algorithmic_bytes": alg,
+                           "gbs": alg / us / 1e3, "frac": alg / us / 1e3 / peak, "peak": peak, "peak_kind": peak_kind}
+        for l_ in lins:
+            l_.close()
+    return out
+
+
+def config2_block(x, device, reps=6):
+    """decode attention for 8 rows x 24 q heads over an int8 KV cache (6 KV heads, head_dim 128),
+    codes U[-127, 127], scales U(0.005, 0.02), q ~ N(0, 1) unit-normed per head: global layers at L = 4096, 8192,
+    32768 (p = L - 8) with the step's 49 splits, and a sliding layer (1088-slot ring in rotated order, window 1024,
+    17 splits). Device time of the attention kernel plus the split combine; bytes = L * 1584 + 147,456 (q and out)."""
+    import torch
+    from torch.profiler import profile, ProfilerActivity
+    g = torch.Generator(device=device)
+    g.manual_seed(2)
+    peak, peak_kind = peaks()
+    kvh, heads = 6, 24
+
+    def rows(n, h):
+        t = torch.randn(8, h, 128, device=device, generator=g)
+        return t / t.norm(dim=-1, keepdim=True)
+
+    out = {}
+    for name, slots, pos0, window, ring, splits in (("global_4096", 4096, 4088, 0, False, 49),
+                                                  ("global_8192", 8192, 8184, 0, False, 49),
+                                                  ("global_32768", 32768, 32760, 0, False, 49),
+                                                  ("sliding_1088", 1088, 40000, 1024, True, 17)):
+        q, k, v = rows(8, heads), rows(8, kvh), rows(8, kvh)
+        kc = torch.randint(-127, 128, (kvh * slots * 128,), dtype=torch.int8, device=device, generator=g)
+        vc = torch.randint(-127, 128, (kvh * slots * 128,), dtype=torch.int8, device=device, generator=g)
+        ks = torch.rand(kvh, slots, device=device, generator=g) * 0.015 + 0.005
+        vs = torch.rand(kvh, slots, device=device, generator=g) * 0.015 + 0.005
+        rp = None
+        if ring:   # the most recent 1088 positions, slot = position % 1088 (rotated order)
+            p = torch.arange(pos0 - slots, pos0, device=device, dtype=torch.int32)
+            rp = torch.empty(slots, dtype=torch.int32, device=device)
+            rp[p % slots] = p
+        args = (q, k, v, kc.view(torch.uint8), vc.view(torch.uint8), ks, vs, pos0, window, 1.0 / 128 ** 0.5 * 8)
+        for _ in range(3):
+            x.attention(*args, ring_pos=rp, splits=splits)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for _ in range(reps):
+                x.attention(*args, ring_pos=rp, splits=splits)
+            torch.cuda.synchronize()
+        t = kernel_times(prof)
+        us = t["attention_kernel"] + t["attn_combine_kernel"]
+        alg = slots * 1584 + 147456
+        out[name] = {"attention_us": t["attention_kernel"], "combine_us": t["attn_combine_kernel"],
+                     "algorithmic_bytes": alg, "gbs": alg / us / 1e3, "frac": alg / us / 1e3 / peak}
+    return out
+
+
 def job_rows_per_s(world, ms_per_step):
     """Whole-job throughput: every rank verifies 8 rows of its own sequence per step (weak scaling)."""
     return world * 8.0 / (ms_per_step / 1e3)
@@ -387,6 +481,8 @@ def run_ours(args, rank, world, local_rank, dist):
     info = s.info()
     s.close()
     gemm = gemm_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
+    cfg0 = config0_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
+    cfg2 = config2_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     if rank != 0:
         return
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -408,6 +504,11 @@ def run_ours(args, rank, world, local_rank, dist):
             "clocks": clk.summary(),
             "library": {"splits_global": info.get("splits_global"), "splits_ring": info.get("splits_ring"),
                         "graph": info.get("graph"), "pdl": info.get("pdl")}}
+    if cfg0:
+        line["config0_gemv"] = {"config": "config0: one NVFP4 GEMV, M = 1, 16 weight copies rotated", **cfg0}
+    if cfg2:
+        line["config2_attention"] = {"config": "config2: 8-row decode attention, int8 KV, attention + split combine",
+                                     **cfg2}
     if gemm:
         tot_flops = sum(2.0 * 512 * v["n"] * v["k"] for v in gemm.values())
         tot_us = sum(v["gemm_us"] for v in gemm.values())
