@@ -411,6 +411,45 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
       }
       tc_commit(&accfull[0]);
       tc_commit(done);
+    } else if (lane == 0 && nkb % kStageUnits == 0) {
+      // Several whole tiles whose K blocks fill whole stages (the head): the slice's activation scales go to TMEM
+      // once; a stage is straight-line code; the accumulator switches (and waits for the epilogue) only at the
+      // first stage of a tile and completes at its last.
+      tc_fence_after();
+      const uint32_t ring_addr = smem_u32(ringbuf), b_addr = smem_u32(bbuf);
+      const uint32_t sfb0 = tbase + 2 * kAccCols, sfa0 = sfb0 + 4 * (uint32_t)nkb;
+      for (int kb = 0; kb < nkb; ++kb) tc_cp_sf(sfb0 + 4 * kb, sf_desc(b_addr + (uint32_t)(kb * kBBlockBytes + kBCodeBytes)));
+      const uint64_t da0 = a_desc(ring_addr), dsfa0 = sf_desc(ring_addr + kUnitCodeBytes), db0 = a_desc(b_addr);
+      const int spt = nkb / kStageUnits;   // stages per tile
+      int slot = 0, j = 0, sj = 0;
+      uint32_t phase = 0;
+      for (int st = 0; st < nstages; ++st) {
+        if (sj == 0 && j >= 2) {
+          wait_bar(&accempty[j & 1], (uint32_t)((j >> 1) - 1) & 1u, a.err);
+        }
+        wait_bar(&full[slot], phase, a.err);
+        tc_fence_after();
+        const uint32_t u0 = (uint32_t)(slot * kStageUnits), kb0 = (uint32_t)(sj * kStageUnits);
+        const uint32_t tacc = tbase + (uint32_t)((j & 1) * kAccCols);
+#pragma unroll
+        for (int idx = 0; idx < kStageUnits; ++idx) {
+          const uint32_t ui = u0 + idx, kbi = kb0 + idx;
+          tc_cp_sf(sfa0 + 4 * ui, dsfa0 + ui * (kUnitBytes >> 4));
+          tc_mma_fp4(tacc, da0 + ui * (kUnitBytes >> 4), db0 + kbi * (kBBlockBytes >> 4), sfa0 + 4 * ui,
+                     sfb0 + 4 * kbi, kbi > 0 ? 1u : 0u);
+        }
+        tc_commit(&empty[slot]);
+        if (++sj == spt) {
+          tc_commit(&accfull[j & 1]);
+          sj = 0;
+          ++j;
+        }
+        if (++slot == ring) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      }
+      tc_commit(done);
     } else if (lane == 0) {
       tc_fence_after();
       const uint32_t ring_addr = smem_u32(ringbuf), b_addr = smem_u32(bbuf);
