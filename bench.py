@@ -434,6 +434,42 @@ def config2_block(x, device, reps=6):
     return out
 
 
+def split_kv_block(x, rank, world, local_rank, dist, steps, warmup, context=32768):
+    """The batch-1 long-context step split across the N processes: one sequence at 32K context, every process holding
+    the whole model and every cache, each attending 1/N of the global caches' chunks, the attention partials joined
+    by the attention kernels themselves (stores into every process's buffer over NVLink, flags that the combine
+    waits on) or, for comparison, by an NCCL all-gather between the kernels. Against the same step on one GPU (every
+    rank runs that alone too). Times are the max over ranks."""
+    import torch
+    model = dict(x.DORY_3072)
+    out = {"context": context, "n_past": context - 8}
+    for name, exch in (("one_gpu", None), ("split_kv", "peer"), ("split_kv_nccl", "nccl")):
+        opts = {}
+        if exch:
+            ids = [bytes(torch.cuda.nccl.unique_id()).hex() if rank == 0 else None]
+            dist.broadcast_object_list(ids, src=0)
+            opts = dict(kv_world=world, kv_rank=rank, nccl_id=ids[0], kv_exchange=exch)
+        s = x.Session(model, context=context, device=local_rank, **opts)
+        try:
+            s.prefill_synthetic(context - 8)
+            s.bench(TOKENS, max(1, warmup))
+            dist_barrier(dist)
+            ms, _, _ = s.bench(TOKENS, steps)
+            dist_barrier(dist)
+            out[name + "_ms_per_step"] = max_over_ranks(ms, dist)
+            if exch:
+                out[name + "_argmax_matches_one_gpu"] = s.argmax(8) == out["_argmax"]
+                out["splits_global_per_gpu"] = s.info()["splits_global"]
+            else:
+                out["_argmax"] = s.argmax(8)
+        finally:
+            s.close()
+    out.pop("_argmax")
+    out["speedup"] = out["one_gpu_ms_per_step"] / out["split_kv_ms_per_step"]
+    out["tok_s"] = 8.0 / (out["split_kv_ms_per_step"] / 1e3)
+    return out
+
+
 def job_rows_per_s(world, ms_per_step):
     """Whole-job throughput: every rank verifies 8 rows of its own sequence per step (weak scaling)."""
     return world * 8.0 / (ms_per_step / 1e3)
@@ -483,6 +519,7 @@ def run_ours(args, rank, world, local_rank, dist):
     gemm = gemm_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg0 = config0_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg2 = config2_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
+    skv = split_kv_block(x, rank, world, local_rank, dist, args.steps, args.warmup) if world > 1 else None
     if rank != 0:
         return
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -509,6 +546,10 @@ def run_ours(args, rank, world, local_rank, dist):
     if cfg2:
         line["config2_attention"] = {"config": "config2: 8-row decode attention, int8 KV, attention + split combine",
                                      **cfg2}
+    if skv:
+        line["batch1_split_kv"] = {"config": "batch-1 verify step (8 rows) at 32K context, the global caches' chunks "
+                                             "split over the GPUs, partials exchanged over NVLink by the attention "
+                                             "kernel (split_kv) or by ncclAllGather (split_kv_nccl)", **skv}
     if gemm:
         tot_flops = sum(2.0 * 512 * v["n"] * v["k"] for v in gemm.values())
         tot_us = sum(v["gemm_us"] for v in gemm.values())
@@ -585,6 +626,8 @@ def main():
         import datetime
         import torch
         import torch.distributed as tdist
+        # the collectives here are a barrier, a max and the split-KV step's small all-gather: plain peer copies
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local_rank)
         tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         dist = tdist

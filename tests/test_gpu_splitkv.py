@@ -1,0 +1,108 @@
+"""GPU (2 or more): the batch-1 long-context step with the global caches' chunks split across processes, one GPU
+each, and the attention partials of the global layers joined by an NCCL all-gather before the log-sum-exp combine.
+
+Every process holds the whole model and every cache and runs the whole step; only the chunk range each global-layer
+attention reads differs. With the same total number of splits the chunk ranges, the partials and therefore the
+logits are those of one process bit for bit; with the default split counts (more splits in total) the logits move
+only by rounding. The single-process step itself is pinned to the oracle by the session tests."""
+import importlib.util
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+N_PAST = 20000
+CONTEXT = 32768
+TOKENS = [7, 4001, 123]
+
+
+def _product():
+    if "xtier_go_b200" in sys.modules:
+        return sys.modules["xtier_go_b200"]
+    pkg = os.path.join(ROOT, "xtier-go_b200")
+    spec = importlib.util.spec_from_file_location("xtier_go_b200", os.path.join(pkg, "__init__.py"),
+                                                  submodule_search_locations=[pkg])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["xtier_go_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def _run(xtg, device, **opts):
+    with xtg.Session(model=xtg.SMALL, context=CONTEXT, device=device, **opts) as s:
+        info = s.info()
+        s.prefill_synthetic(N_PAST)
+        logits = s.forward(TOKENS, want=2)
+        return info, logits, s.argmax(len(TOKENS))
+
+
+def _alone(xtg, rank, world, nccl_id, barrier):
+    """Both processes step once together, then rank 1 steps alone: its combine waits for partials that never come
+    and must give up after kv_wait_ms with an error (the context stays usable), not hang."""
+    with xtg.Session(model=xtg.SMALL, context=4096, device=rank, kv_world=world, kv_rank=rank, nccl_id=nccl_id,
+                     kv_wait_ms=300) as s:
+        s.prefill_synthetic(2000)
+        s.forward(TOKENS[:1], want=0)
+        msg = None
+        if rank == 1:
+            try:
+                s.forward(TOKENS[:1], want=0)
+            except xtg.XtgError as e:
+                msg = str(e)
+        barrier.wait()   # rank 0 keeps its buffers mapped until rank 1 is done
+        return msg
+
+
+def _rank(rank, world, ids, barrier, out):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"   # plain peer copies: no NVLink multicast objects bound to a process
+    import torch   # loads the NCCL the parent's unique ids came from, which the library then binds
+    torch.cuda.set_device(rank)
+    xtg = _product()
+    split = dict(kv_world=world, kv_rank=rank)
+    same = _run(xtg, rank, nccl_id=ids[0], splits_global=128 // world, **split)
+    dflt = _run(xtg, rank, nccl_id=ids[1], **split)
+    nccl = _run(xtg, rank, nccl_id=ids[2], splits_global=128 // world, kv_exchange="nccl", **split)
+    alone = _alone(xtg, rank, world, ids[3], barrier)
+    out[rank] = (same, dflt, nccl, alone)
+
+
+@pytest.mark.gpu
+@pytest.mark.timeout(600)
+def test_split_kv_across_two_gpus(cuda, xtg):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("split-KV across processes needs 2 GPUs")
+    world = 2
+    ids = [bytes(torch.cuda.nccl.unique_id()).hex() for _ in range(4)]
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        out = mgr.dict()
+        mp.start_processes(_rank, args=(world, ids, mgr.Barrier(world), out), nprocs=world, join=True,
+                           start_method="spawn")
+        res = dict(out)
+    one_same = _run(xtg, 0, splits_global=128)
+    one_dflt = _run(xtg, 0)
+
+    for rank in range(world):
+        (info, logits, am), (dinfo, dlogits, dam), (ninfo, nlogits, nam), alone = res[rank]
+        assert info["kv_world"] == world and info["kv_rank"] == rank and info["splits_global"] == 128 // world
+        assert info["kv_exchange"] == "peer" and ninfo["kv_exchange"] == "nccl" and info["global_layers"] > 0
+        assert dinfo["splits_global"] * world <= 256
+        # the same 128 chunk ranges as one process: identical partials, identical logits, by either exchange
+        assert sorted(logits) == sorted(one_same[1]) == sorted(nlogits)
+        for r in logits:
+            np.testing.assert_array_equal(logits[r], one_same[1][r])
+            np.testing.assert_array_equal(nlogits[r], one_same[1][r])
+        assert am == one_same[2] == nam
+        assert (alone is None) if rank == 0 else ("timed out" in alone), alone
+        # default split counts: rounding only
+        for r in dlogits:
+            d = np.abs(dlogits[r] - one_dflt[1][r]).max()
+            assert d <= 5e-2, (rank, r, d)
+        assert dam == one_dflt[2]
+    # every process ends with the same result
+    for r in res[0][1][1]:
+        np.testing.assert_array_equal(res[0][1][1][r], res[1][1][1][r])

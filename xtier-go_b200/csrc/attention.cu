@@ -34,6 +34,7 @@ constexpr int kQuarters = 4;    // key quarters of a chunk
 constexpr int kStages = 4;      // chunks in flight
 constexpr int kQRows = 32;
 constexpr int kPartStride = kD + 2;   // m, l, acc[128]
+constexpr int kMaxSplits = 256;       // parts of a cache's chunks (the combine holds one weight per part)
 
 __device__ __forceinline__ void codes_to_f16(uint32_t word, int dtype, uint32_t& lo, uint32_t& hi) {
   if (dtype == kKvFp8) {
@@ -77,7 +78,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   // this CTA's 64-slot chunks: a global cache holds [0, pos0), a ring every slot
   const int64_t span = a.ring ? slots : pos0;
   const int64_t nchunks = (span + 63) / 64;
-  const int64_t cb = nchunks * split / a.splits, ce = nchunks * (split + 1) / a.splits;
+  const int stot = a.splits_total > 0 ? a.splits_total : a.splits, sidx = a.split0 + split;
+  const int64_t cb = nchunks * sidx / stot, ce = nchunks * (sidx + 1) / stot;
   const int nc = (int)(ce - cb);
   const uint8_t* kc = a.kc + (int64_t)kvh * slots * kD;
   const uint8_t* vc = a.vc + (int64_t)kvh * kD * slots;
@@ -312,6 +314,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     }
   }
   __syncthreads();
+  const int xw = a.x.world;   // > 1: the split-KV exchange across GPUs
+  const uint32_t xrun = xw > 1 ? *a.x.epoch * (uint32_t)a.x.n_g + (uint32_t)a.x.g : 0u;
   {
     // thread: query row r, head dims j, j + 8, ...: a warp's stores cover 4 rows x 8 consecutive dims
     const int r = threadIdx.x >> 3, j = threadIdx.x & 7;
@@ -330,29 +334,43 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
         w[q] = mp[q] == -INFINITY ? 0.f : expf(mp[q] - M);
         L += w[q] == 0.f ? 0.f : st0[q * ss + r * kStateStride + 1] * w[q];
       }
-      float* out = a.part + (((int64_t)kvh * a.splits + split) * kQRows + r) * kPartStride;
-      if (j == 0) {
-        out[0] = M;
-        out[1] = L;
-      }
+      float o[kD / 8];
 #pragma unroll
       for (int k = 0; k < kD / 8; ++k) {
         const int d = j + 8 * k;
-        float o = 0.f;
+        o[k] = 0.f;
 #pragma unroll
         for (int q = 0; q < kQuarters; ++q)
-          if (w[q] != 0.f) o += st0[q * ss + r * kStateStride + 2 + d] * w[q];
-        out[2 + d] = o;
+          if (w[q] != 0.f) o[k] += st0[q * ss + r * kStateStride + 2 + d] * w[q];
+      }
+      const int64_t off = (((int64_t)sidx * a.kv_heads + kvh) * kQRows + r) * kPartStride;
+      // the partial into this process's buffer, or with the exchange on into every process's (peers over NVLink)
+#pragma unroll
+      for (int t = 0; t < kMaxKvWorld; ++t) {
+        if (t > 0 && t >= xw) break;
+        float* out = (xw > 1 ? a.x.part[t] + (xrun & 1) * a.x.part_floats : a.part) + off;
+        if (j == 0) {
+          out[0] = M;
+          out[1] = L;
+        }
+#pragma unroll
+        for (int k = 0; k < kD / 8; ++k) out[2 + j + 8 * k] = o[k];
       }
     }
+  }
+  if (xw > 1) {   // every thread's stores are out before the flags go up (fence, then the block's barrier)
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0)
+#pragma unroll
+      for (int t = 0; t < kMaxKvWorld; ++t)
+        if (t < xw) st_release_sys(a.x.flag[t] + ((xrun & 1) * a.kv_heads + kvh) * kMaxSplits + sidx, xrun + 1);
   }
 }
 
 // Combine the splits of (activation row, q head) by log-sum-exp; then either the plain output (API) or the Dory
 // output gate, fp16 fragments for the O projection and the per-head sum of squares (the step). One CTA per (row,
 // head), one thread per head dimension; the split weights are computed once, every partial is loaded in one wave.
-constexpr int kMaxSplits = 256;
-
 __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   constexpr int kRegSplits = 64;   // partials held in registers (the rest are read in a second pass)
   __shared__ float wgt[kMaxSplits];
@@ -370,10 +388,29 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   }
   if (i >= m) return;
   const int group = a.heads / a.kv_heads, kvh = h / group, qr = i * group + h % group;
-  const float* base = a.part + ((int64_t)kvh * a.splits * kQRows + qr) * kPartStride;
-  const int64_t sstride = (int64_t)kQRows * kPartStride;
+  const float* base = a.part + ((int64_t)kvh * kQRows + qr) * kPartStride;   // split s at s * sstride
+  const int64_t sstride = (int64_t)a.kv_heads * kQRows * kPartStride;
+  const float qd = a.q[((int64_t)i * a.heads + h) * kD + d];
+  float kj[kMaxRows], vj[kMaxRows];
+#pragma unroll
+  for (int j = 0; j < kMaxRows; ++j) {
+    kj[j] = j < m ? a.k[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
+    vj[j] = j < m ? a.v[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
+  }
+  const float gt = a.out ? 0.f : a.gate[(int64_t)i * a.gate_ld + col];
+  if (a.x.world > 1) {   // the split-KV exchange: every part's flag in this process's memory, then its buffer
+    const uint32_t run = *a.x.epoch * (uint32_t)a.x.n_g + (uint32_t)a.x.g;
+    const uint32_t* fl = a.x.flag[0];
+#pragma unroll
+    for (int t = 1; t < kMaxKvWorld; ++t)
+      if (t == a.x.rank) fl = a.x.flag[t];
+    fl += ((run & 1) * a.kv_heads + kvh) * kMaxSplits;
+    for (int s = d; s < a.splits; s += kD) peer_wait_bounded(fl + s, run + 1, a.x.wait_ns, a.err);
+    base += (run & 1) * a.x.part_floats;
+    __syncthreads();
+  }
   // every independent load in one wave: this thread's dim of every split's partial, the m and l of splits d and
-  // d + 128, q, this call's keys / values, the gate
+  // d + 128
   const int ns = a.splits < kRegSplits ? a.splits : kRegSplits;
   float acc_s[kRegSplits];
 #pragma unroll
@@ -385,14 +422,6 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
     mls[u][0] = sp < a.splits ? base[sp * sstride] : -INFINITY;
     mls[u][1] = sp < a.splits ? base[sp * sstride + 1] : 0.f;
   }
-  const float qd = a.q[((int64_t)i * a.heads + h) * kD + d];
-  float kj[kMaxRows], vj[kMaxRows];
-#pragma unroll
-  for (int j = 0; j < kMaxRows; ++j) {
-    kj[j] = j < m ? a.k[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
-    vj[j] = j < m ? a.v[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
-  }
-  const float gt = a.out ? 0.f : a.gate[(int64_t)i * a.gate_ld + col];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
     const int sp = d + u * kD;
@@ -490,6 +519,13 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
   XTG_REQUIRE(a.heads % a.kv_heads == 0 && a.heads / a.kv_heads <= 4, "attention: at most 4 q heads per KV head");
   XTG_REQUIRE(a.slots % 64 == 0, "attention: cache slots must be a multiple of 64");
   XTG_REQUIRE(a.splits >= 1 && a.splits <= kMaxSplits, "attention: 1..256 splits");
+  XTG_REQUIRE(a.splits_total == 0 || (a.split0 >= 0 && a.split0 + a.splits <= a.splits_total &&
+                                       a.splits_total <= kMaxSplits),
+              "attention: split range outside 0..splits_total (at most 256)");
+  XTG_REQUIRE(a.x.world <= 1 || (a.x.world <= kMaxKvWorld && a.x.rank >= 0 && a.x.rank < a.x.world && a.x.epoch &&
+                                 a.splits_total > 0 && a.x.part_floats >= attention_part_floats(a.kv_heads,
+                                                                                                a.splits_total)),
+              "attention: split-KV exchange needs 2..8 processes, the epoch and a part buffer for every split");
   static bool attr_set = false;
   if (!attr_set) {
     XTG_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -512,6 +548,10 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
 void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
   CombineArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
+  XTG_REQUIRE(a.splits >= 1 && a.splits <= kMaxSplits, "combine: 1..256 splits");
+  XTG_REQUIRE(a.x.world <= 1 || (a.x.world <= kMaxKvWorld && a.x.rank >= 0 && a.x.rank < a.x.world && a.x.epoch &&
+                                 a.err && a.x.flag[a.x.rank]),
+              "combine: split-KV exchange needs 2..8 processes, the epoch, its flags and an error word");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kMaxRows, a.heads);
   cfg.blockDim = dim3(kD);

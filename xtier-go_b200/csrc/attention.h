@@ -33,6 +33,22 @@ struct StepParams {
   int64_t pos0;
 };
 
+// Batch-1 split-KV across GPUs with the partials exchanged by the attention kernel itself (world > 1): every CTA
+// stores its partial into the part buffer of every process (this one's and the peers', mapped by CUDA IPC over
+// NVLink) and then raises its flag there; each process's combine waits for the flags of all parts, then reads its
+// own buffer. Two buffers alternate by the running global-layer count, so a process one layer ahead never writes a
+// buffer that a slower one is still reading: its next write to the same buffer needs the slower one's next layer.
+constexpr int kMaxKvWorld = 8;
+struct PeerXchg {
+  float* part[kMaxKvWorld];      // by rank: that process's 2 part buffers, part_floats apart
+  uint32_t* flag[kMaxKvWorld];   // by rank: that process's flags [2][kv_heads][256]
+  int64_t part_floats;           // one buffer: splits_total x kv_heads x 32 x 130
+  const uint32_t* epoch;         // steps completed here (the step's last kernel advances it)
+  uint64_t wait_ns;              // the combine's bound on waiting for a peer
+  int world, rank;               // world 0 or 1: off
+  int g, n_g;                    // this layer's index among the step's n_g global layers
+};
+
 struct AttnArgs {
   // this call's rows, prepared (RoPE, justnorm, q scale): q [m][heads][128], k / v [m][kv_heads][128] (already in the
   // cache at positions pos0 .. pos0 + m - 1; the scores against them use these unquantized rows)
@@ -54,10 +70,14 @@ struct AttnArgs {
   int m;
   int64_t pos0;
   int heads, kv_heads;
-  int splits;
-  float* part;              // [kv_heads][splits][32][130]
+  int splits;               // CTAs per KV head in this launch
+  // The chunks of the cache are cut into splits_total parts; this launch computes parts split0 .. split0 + splits - 1
+  // (another process may compute the rest: the batch-1 split-KV over GPUs). 0 / 0: split0 0, splits_total = splits.
+  int split0, splits_total;
+  float* part;              // [splits_total][kv_heads][32][130], split-major (a process's splits are contiguous)
   int* err;                 // set if a bounded wait gave up (never expected); may be null
   int pdl;
+  PeerXchg x;               // global layers of a split-KV step across GPUs (part unused then)
 };
 
 struct CombineArgs {
@@ -68,7 +88,7 @@ struct CombineArgs {
   const float* v;
   float scale;
   int window;
-  int splits, heads, kv_heads;
+  int splits, heads, kv_heads;   // splits: every part of the cache's chunks (AttnArgs::splits_total)
   const StepParams* params;
   int m;
   float* out;               // API: [m][heads][128]; null in the step
@@ -79,6 +99,8 @@ struct CombineArgs {
   float* ab_pre;            // [heads * 8][8] their prescales
   float* asum;              // step: [heads][8] sum of squares per head and activation row
   int pdl;
+  PeerXchg x;               // as in AttnArgs: part is then this process's buffer pair, x.flag[x.rank] its flags
+  int* err;                 // set if the wait for a peer gave up
 };
 
 size_t attention_smem_bytes();

@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(kSlerpThreads) resid_slerp_kernel(const ResidA
 }
 
 __global__ void argmax_kernel(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out,
-                              float* out_val, int pdl) {
+                              float* out_val, uint32_t* epoch, int pdl) {
   __shared__ float bv[32];
   __shared__ int bi[32];
   const int n = blockIdx.x;
@@ -315,6 +315,8 @@ __global__ void argmax_kernel(const ArgCand* cand, int tiles, const StepParams* 
     pdl_wait();
     pdl_launch_next();
   }
+  // the step's last kernel: every earlier one has finished, so the step count moves on here
+  if (epoch && n == 0 && threadIdx.x == 0) *epoch += 1u;
   if (n >= params->m) return;
   float v = -INFINITY;
   int idx = 0x7fffffff;
@@ -456,7 +458,7 @@ void launch_resid(const ResidArgs& a_in, cudaStream_t s, bool pdl) {
 }
 
 void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out, float* out_val,
-                   cudaStream_t s, bool pdl) {
+                   uint32_t* epoch, cudaStream_t s, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kMaxRows);
   cfg.blockDim = dim3(1024);
@@ -466,7 +468,7 @@ void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  XTG_CUDA(cudaLaunchKernelEx(&cfg, argmax_kernel, cand, tiles, params, out, out_val, pdl ? 1 : 0));
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, argmax_kernel, cand, tiles, params, out, out_val, epoch, pdl ? 1 : 0));
 }
 
 void launch_kv_store(const KvStoreArgs& a, cudaStream_t s) {

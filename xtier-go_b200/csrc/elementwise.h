@@ -65,8 +65,9 @@ struct KvStoreArgs {
 
 void launch_embed(const EmbedArgs& a, cudaStream_t s, bool pdl);
 void launch_resid(const ResidArgs& a, cudaStream_t s, bool pdl);
+// epoch (or null): the step counter of the split-KV exchange, advanced once by this, the step's last kernel
 void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out, float* out_val,
-                   cudaStream_t s, bool pdl);
+                   uint32_t* epoch, cudaStream_t s, bool pdl);
 void launch_kv_store(const KvStoreArgs& a, cudaStream_t s);
 void kv_prefill(uint64_t seed, uint64_t stream_base, float lo, float hi, int64_t filled, int kv_heads, int64_t slots,
                 uint8_t* kc, uint8_t* vc, float* ks, float* vs, cudaStream_t s);

@@ -23,6 +23,7 @@
 #include "elementwise.h"
 #include "fp4mma.cuh"
 #include "json.h"
+#include "nccl_rt.h"
 #include "kernels.h"
 
 namespace xtg {
@@ -45,6 +46,15 @@ struct Config {
   int device = 0;
   bool graph = true, pdl = true;
   int splits_global = 0, splits_ring = 0;   // 0: chosen from the SM count
+  // batch-1 split-KV across processes (one GPU each): every process holds the whole model and every cache and runs
+  // the whole step, but attends only its share of each global cache's chunks; the attention partials of the global
+  // layers meet by an NCCL all-gather (kv_world processes, this one kv_rank, nccl_id the 128-byte unique id in hex)
+  int kv_world = 1, kv_rank = 0;
+  std::string nccl_id;
+  // "peer": the attention kernels store their partials into every process's buffer over NVLink (CUDA IPC) and the
+  // combine waits on flags, at most kv_wait_ms; "nccl": an ncclAllGather of the partials between the two kernels
+  std::string kv_exchange = "peer";
+  int kv_wait_ms = 10000;
 
   int n_evals() const { return n_in + n_rec * loops + n_out; }
   int phys(int e) const {
@@ -128,6 +138,17 @@ Config parse_config(const std::string& options) {
   c.pdl = o.number("pdl", 1) != 0;
   c.splits_global = (int)o.number("splits_global", 0);
   c.splits_ring = (int)o.number("splits_ring", 0);
+  c.kv_world = (int)o.number("kv_world", 1);
+  c.kv_rank = (int)o.number("kv_rank", 0);
+  c.nccl_id = o.string("nccl_id", "");
+  c.kv_exchange = o.string("kv_exchange", "peer");
+  c.kv_wait_ms = (int)o.number("kv_wait_ms", 10000);
+  if (c.kv_exchange != "peer" && c.kv_exchange != "nccl") throw CudaError("kv_exchange: \"peer\" or \"nccl\"");
+  if (c.kv_wait_ms < 1) throw CudaError("kv_wait_ms: at least 1");
+  if (c.kv_world < 1 || c.kv_world > 8 || c.kv_rank < 0 || c.kv_rank >= c.kv_world)
+    throw CudaError("kv_world: 1..8 processes, kv_rank below it");
+  if (c.kv_world > 1 && c.nccl_id.size() != 2 * sizeof(ncclUniqueId))
+    throw CudaError("nccl_id: the NCCL unique id as " + std::to_string(2 * sizeof(ncclUniqueId)) + " hex digits");
   if (c.head_dim != 128) throw CudaError("model: head_dim must be 128");
   if (c.heads % c.kv_heads || c.heads / c.kv_heads > 4) throw CudaError("model: at most 4 q heads per KV head");
   if (c.hidden % 64 || c.ffn % 64 || c.hidden > 8192) throw CudaError("model: hidden, ffn multiples of 64, hidden <= 8192");
@@ -218,6 +239,14 @@ struct xtg_cuda {
   int* err_host = nullptr;  // pinned copy of dev_err
   int splits_g = 1, splits_r = 1;
   int proj_ld = 0;
+  ncclComm_t comm = nullptr;   // split-KV only
+  // the peer exchange: this process's 2 part buffers + flags in one allocation (exported by CUDA IPC), the peers'
+  // (imported), the step counter, the global layers per step
+  void* xbuf = nullptr;
+  void* peer_base[kMaxKvWorld] = {};
+  PeerXchg xchg = {};
+  uint32_t* epoch = nullptr;
+  int n_glob = 0;
   // graph
   cudaGraphExec_t exec = nullptr;
   // profiling
@@ -236,6 +265,10 @@ struct xtg_cuda {
   ~xtg_cuda() {
     if (stream) cudaStreamSynchronize(stream);
     if (exec) cudaGraphExecDestroy(exec);
+    for (void* p : peer_base)
+      if (p) cudaIpcCloseMemHandle(p);
+    if (xbuf) cudaFree(xbuf);
+    if (comm) nccl_api().comm_destroy(comm);
     free_kv(kv);
     for (auto& s : snaps) free_kv(s.rings);
     for (void* p : allocs) cudaFree(p);
@@ -487,8 +520,9 @@ struct xtg_cuda {
     *err_host = 0;
     // the attention runs 2 CTAs per SM: a global cache over every CTA slot, a ring one 64-slot chunk per CTA
     splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, std::min(256, 2 * num_sms / c.kv_heads));
+    splits_g = std::min(splits_g, 256 / c.kv_world);   // the combine takes at most 256 parts
     splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, std::min(256, (int)(c.ring / 64)));
-    part = dalloc<float>((size_t)attention_part_floats(c.kv_heads, std::max(splits_g, splits_r)));
+    part = dalloc<float>((size_t)attention_part_floats(c.kv_heads, std::max(splits_g * c.kv_world, splits_r)));
     ring_pos_dev = dalloc<int32_t>(c.ring);
     ring_pos.assign(c.ring, -1);
     std::vector<int32_t> neg(c.ring, -1);
@@ -500,6 +534,8 @@ struct xtg_cuda {
     for (int e = 0; e < c.n_evals(); ++e)
       if (evals[e].kind != 0)
         kv.push_back(alloc_kv(c.kv_heads, evals[e].kind == 1 ? c.ring : c.context, evals[e].kind == 1, stream));
+    n_glob = 0;
+    for (int e = 0; e < c.n_evals(); ++e) n_glob += evals[e].kind == 2;
     snaps.resize(c.snapshots);
   }
 
@@ -549,6 +585,7 @@ struct xtg_cuda {
 
   void enqueue_step(bool pdl) {
     const int H = c.hidden, F = c.ffn, Q = c.heads * c.head_dim;
+    int glob = 0;   // global layers enqueued so far
     mark(kClsSmall, true);
     EmbedArgs ea = {};
     ea.params = params_dev;
@@ -656,19 +693,33 @@ struct xtg_cuda {
       at.heads = c.heads;
       at.kv_heads = c.kv_heads;
       at.splits = K.ring ? splits_r : splits_g;
-      at.part = part;
+      const bool shard = !K.ring && comm;   // this process attends its share of the global cache's chunks
+      const bool peer = shard && xbuf;      // ... and sends its partials to the peers itself
+      at.split0 = shard ? c.kv_rank * splits_g : 0;
+      at.splits_total = shard ? splits_g * c.kv_world : at.splits;
+      at.part = peer ? xchg.part[c.kv_rank] : part;
       at.err = dev_err;
+      if (peer) {
+        at.x = xchg;
+        at.x.g = glob++;
+      }
       mark(kClsAttn, true);
       launch_attention(at, stream, pdl);
       mark(kClsAttn, false);
+      if (shard && !peer) {   // in place: this process's partials are the block at its split offset
+        const size_t n = (size_t)attention_part_floats(c.kv_heads, splits_g);
+        nccl_check(nccl_api().all_gather(part + c.kv_rank * n, part, n, ncclFloat32, comm, stream), "ncclAllGather");
+      }
       CombineArgs cb = {};
-      cb.part = part;
+      cb.part = at.part;
+      cb.x = at.x;
+      cb.err = dev_err;
       cb.q = q_prep;
       cb.k = k_new;
       cb.v = v_new;
       cb.scale = at.scale;
       cb.window = at.window;
-      cb.splits = at.splits;
+      cb.splits = at.splits_total;
       cb.heads = c.heads;
       cb.kv_heads = c.kv_heads;
       cb.params = params_dev;
@@ -703,8 +754,55 @@ struct xtg_cuda {
     a.cand = cand;
     gemv(head, kEpiHead, a, xb, xb_pre, pdl);
     mark(kClsSmall, true);
-    launch_argmax(cand, head.tiles, params_dev, argmax, argmax_val, stream, pdl);
+    launch_argmax(cand, head.tiles, params_dev, argmax, argmax_val, epoch, stream, pdl);
     mark(kClsSmall, false);
+  }
+
+  // The split-KV peer exchange: allocate this process's part buffers and flags, export them by CUDA IPC, and map the
+  // peers' (the handles travel by an NCCL all-gather, which also checks that every process sized them alike).
+  void open_peer_exchange() {
+    struct Record {
+      cudaIpcMemHandle_t handle;
+      uint64_t bytes;
+      int32_t n_glob, splits;
+    };
+    const int w = c.kv_world, r = c.kv_rank;
+    if (w > kMaxKvWorld) throw CudaError("split-KV: at most 8 processes");
+    const int64_t pf = attention_part_floats(c.kv_heads, splits_g * w);
+    const size_t flag_bytes = (size_t)2 * c.kv_heads * 256 * sizeof(uint32_t);
+    const size_t bytes = (size_t)2 * pf * sizeof(float) + flag_bytes;
+    XTG_CUDA(cudaMalloc(&xbuf, bytes));
+    XTG_CUDA(cudaMemset(xbuf, 0, bytes));
+    epoch = dalloc<uint32_t>(1);
+    XTG_CUDA(cudaDeviceSynchronize());   // zeroed before any peer can map it
+    Record mine = {};
+    XTG_CUDA(cudaIpcGetMemHandle(&mine.handle, xbuf));
+    mine.bytes = bytes;
+    mine.n_glob = n_glob;
+    mine.splits = splits_g;
+    std::vector<Record> all(w);
+    Record* stage = dalloc<Record>((size_t)w, false);
+    XTG_CUDA(cudaMemcpy(stage + r, &mine, sizeof(Record), cudaMemcpyHostToDevice));
+    nccl_check(nccl_api().all_gather(stage + r, stage, sizeof(Record), ncclUint8, comm, stream), "ncclAllGather");
+    XTG_CUDA(cudaStreamSynchronize(stream));
+    XTG_CUDA(cudaMemcpy(all.data(), stage, sizeof(Record) * w, cudaMemcpyDeviceToHost));
+    for (int t = 0; t < w; ++t) {
+      if (all[t].bytes != bytes || all[t].n_glob != n_glob || all[t].splits != splits_g)
+        throw CudaError("split-KV: process " + std::to_string(t) + " has another model, context or split count");
+      char* base = static_cast<char*>(xbuf);
+      if (t != r) {
+        XTG_CUDA(cudaIpcOpenMemHandle(&peer_base[t], all[t].handle, cudaIpcMemLazyEnablePeerAccess));
+        base = static_cast<char*>(peer_base[t]);
+      }
+      xchg.part[t] = reinterpret_cast<float*>(base);
+      xchg.flag[t] = reinterpret_cast<uint32_t*>(base + (size_t)2 * pf * sizeof(float));
+    }
+    xchg.part_floats = pf;
+    xchg.epoch = epoch;
+    xchg.wait_ns = (uint64_t)c.kv_wait_ms * 1000000ull;
+    xchg.world = w;
+    xchg.rank = r;
+    xchg.n_g = n_glob;
   }
 
   void capture() {
@@ -943,6 +1041,14 @@ xtg_cuda* xtg_cuda_open(const char* model_path, const char* options, char* err, 
     h->build_model();
     h->alloc_caches();
     XTG_CUDA(cudaStreamSynchronize(h->stream));
+    if (h->c.kv_world > 1) {   // every process opens its handle at the same time (a collective)
+      ncclUniqueId id;
+      auto hex = [](char ch) { return ch <= '9' ? ch - '0' : (ch | 0x20) - 'a' + 10; };
+      for (size_t i = 0; i < sizeof(id); ++i)
+        id.internal[i] = (char)(hex(h->c.nccl_id[2 * i]) * 16 + hex(h->c.nccl_id[2 * i + 1]));
+      nccl_check(nccl_api().comm_init_rank(&h->comm, h->c.kv_world, id, h->c.kv_rank), "ncclCommInitRank");
+      if (h->c.kv_exchange == "peer") h->open_peer_exchange();
+    }
   } catch (const std::exception& e) {
     set_err(err, err_len, e.what());
     return nullptr;
@@ -958,11 +1064,13 @@ int xtg_cuda_info(xtg_cuda* h, char* out, int out_len) {
       "{\"vocab\":%d,\"context\":%lld,\"max_position\":%lld,\"prefill_ar\":%d,\"decode_ar\":%d,"
       "\"kv_instances\":%d,\"ring_instances\":%d,\"ring_slots\":%d,\"sliding_window\":%d,\"kv_bytes\":%lld,"
       "\"snapshots\":%d,\"kvmap\":false,\"kv_dtype\":\"%s\",\"weight_bytes\":%lld,\"hidden\":%d,\"evaluations\":%d,"
-      "\"sm_count\":%d,\"graph\":%s,\"pdl\":%s,\"splits_global\":%d,\"splits_ring\":%d}",
+      "\"sm_count\":%d,\"graph\":%s,\"pdl\":%s,\"splits_global\":%d,\"splits_ring\":%d,"
+      "\"kv_world\":%d,\"kv_rank\":%d,\"kv_exchange\":\"%s\",\"global_layers\":%d}",
       h->c.vocab, (long long)h->c.context, (long long)h->c.context - 1, h->c.decode_rows, h->c.decode_rows,
       (int)h->kv.size(), rings, h->c.ring, h->c.window, (long long)h->kv_bytes(), (int)h->snaps.size(),
       h->c.kv_dtype == kKvFp8 ? "fp8" : "int8", (long long)h->arena_bytes, h->c.hidden, h->c.n_evals(), h->num_sms,
-      h->c.graph ? "true" : "false", h->c.pdl ? "true" : "false", h->splits_g, h->splits_r);
+      h->c.graph ? "true" : "false", h->c.pdl ? "true" : "false", h->splits_g, h->splits_r,
+      h->c.kv_world, h->c.kv_rank, h->c.kv_world > 1 ? h->c.kv_exchange.c_str() : "none", h->n_glob);
   return len < out_len ? len : -1;
 }
 
