@@ -78,6 +78,37 @@ XTG_CUDA_API void xtg_cuda_close(xtg_cuda* h);   // xtg_npu.h:47
 // of that step. Returns the number of rows written or -1.
 XTG_CUDA_API int xtg_cuda_argmax(xtg_cuda* h, int32_t* out, int n);
 
+// The candidates of the reference's sampler for the rows of the last step, computed on the device from the logits
+// still there (engine/src/sampler.cpp: more_likely 26-28, top_logprobs 30-40, the candidate phase of Sampler::sample
+// 41-75): idx / logit [rows][k] the k most likely entries of each row, most likely first (ties: lowest index first),
+// row_max [rows], total [rows] = sum over the whole row of exp((l - row_max) / temperature) in double (temperature
+// <= 0: 1; at 1, log-sum-exp = row_max + log(total), so top_logprobs = logit - that). k in 1..min(1024, vocab).
+// A caller reads rows x k candidates back instead of rows x vocab logits. Returns the number of rows or -1.
+XTG_CUDA_API int xtg_cuda_topk(xtg_cuda* h, int k, float temperature, int32_t* idx, float* logit, float* row_max,
+                               double* total, char* err, int err_len);
+
+// xtg_cuda_topk on caller-owned device memory: logits [rows][vocab] f32 (vocab <= 131072); idx / logit [rows][k],
+// row_max [rows], total [rows] on the device; enqueued on stream, not waited for. Returns 0 or -1.
+XTG_CUDA_API int xtg_cuda_topk_rows(const float* logits, int rows, int vocab, int k, float temperature, int32_t* idx,
+                                    float* logit, float* row_max, double* total, void* stream, char* err,
+                                    int err_len);
+
+// Sampler::sample's parameters (engine/include/xtg/sampler.h SamplingParams).
+typedef struct {
+  float temperature;   // <= 0: greedy
+  int top_k;           // 0: off
+  float top_p;         // 1: off
+  float min_p;         // 0: off
+} xtg_cuda_sampling;
+
+// Host only (no device work): Sampler::sample (sampler.cpp:41-94) over one row's candidates from xtg_cuda_topk (k of
+// them, fetched at p->temperature) with u, a uniform draw in [0, 1) from the caller's generator standing for the
+// reference's uniform_real_distribution(0, total). Returns the token; -2 when the k candidates cannot decide (top_k
+// above k, or top_p / min_p with k below min(vocab, 1024), or a top_p mass beyond the sorted 1024-entry head, where
+// the reference sorts the whole row): the caller then samples from the full logits row; -1 on bad arguments.
+XTG_CUDA_API int xtg_cuda_sample_candidates(const int32_t* idx, const float* logit, int k, float row_max, double total,
+                                            int vocab, const xtg_cuda_sampling* p, double u);
+
 // Seeded KV prefill: positions 0 .. n_past - 1 of every instance get the synthetic model's seeded codes and scales
 // (the stream map of oracle/xtg_oracle.h); pos() becomes n_past, the ring table and snapshots are reset. -1 when
 // n_past does not fit the tier.

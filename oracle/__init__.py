@@ -171,6 +171,13 @@ def ref():
                                    f32p, f32p, f32p, C.c_void_p, f32p]
         R.xr_sublayer.restype = C.c_int
         R.xr_head.restype = C.c_int
+        R.xr_argmax.restype = C.c_int
+        R.xr_argmax.argtypes = [f32p, C.c_int]
+        R.xr_top_logprobs.restype = C.c_int
+        R.xr_top_logprobs.argtypes = [f32p, C.c_int, C.c_int, f32p, i32p]
+        R.xr_sample.restype = C.c_int
+        R.xr_sample.argtypes = [f32p, C.c_int, C.c_float, C.c_int, C.c_float, C.c_float, C.c_uint64,
+                                C.POINTER(C.c_double)]
         _ref = R
     return _ref
 
@@ -424,3 +431,65 @@ def kinds(cfg: dict):
     c = synth_cfg(**cfg)
     L = lib()
     return [L.xo_synth_kind(C.byref(c), e) for e in range(L.xo_synth_n_evals(C.byref(c)))]
+
+
+def topk(logits, k):
+    """The k most likely entries of a row, most likely first: more_likely (engine/src/sampler.cpp:26-28), value
+    descending, ties to the lowest index; as top_logprobs' partial_sort (sampler.cpp:30-40) orders them."""
+    logits = np.asarray(logits, np.float32)
+    order = np.lexsort((np.arange(len(logits)), -logits.astype(np.float64)))
+    return order[:k].astype(np.int32), logits[order[:k]]
+
+
+def sample(logits, temperature, top_k, top_p, min_p, u):
+    """Sampler::sample (engine/src/sampler.cpp:41-94) restated with the draw given: u in [0, 1) stands for
+    uniform_real_distribution<double>(0, total) (value = u * total). Where the reference's partial_sort leaves the
+    tail past its sorted head in an unspecified order, this sorts the whole row; callers compare only where the
+    sorted head decides."""
+    logits = np.asarray(logits, np.float32)
+    n = len(logits)
+    if temperature <= 0.0:
+        return int(np.argmax(logits))                       # argmax: the first index of the maximum
+    mx = logits.max()
+    inv_t = np.float32(1.0) / np.float32(temperature)
+    w = np.exp((logits - mx) * inv_t).astype(np.float32)   # float weights, as std::exp(float)
+    total = float(np.sum(w.astype(np.float64)))
+    idx = np.arange(n)
+    keep = n
+    if 0 < top_k < n:
+        order = np.lexsort((idx, -w.astype(np.float64)))
+        keep = top_k
+        total = float(np.sum(w[order[:keep]].astype(np.float64)))
+    elif top_p < 1.0 or min_p > 0.0:
+        order = np.lexsort((idx, -w.astype(np.float64)))
+    else:
+        order = idx                                         # no filter: the row in index order
+    cw = w[order]
+    if min_p > 0.0:
+        floor = np.float32(min_p) * cw[0]
+        k = 0
+        t = 0.0
+        while k < keep and cw[k] >= floor:
+            t += float(cw[k])
+            k += 1
+        keep = max(1, k)
+        total = t if k else float(cw[0])
+    if top_p < 1.0:
+        target = total * float(np.float32(top_p))
+        cum = 0.0
+        k = 0
+        while k < keep:
+            cum += float(cw[k])
+            k += 1
+            if cum >= target:
+                break
+        keep = max(1, k)
+        total = cum
+    r = u * total
+    cum = 0.0
+    for i in range(keep):
+        cum += float(cw[i])
+        if r < cum:
+            return int(order[i])
+    return int(order[keep - 1])
+

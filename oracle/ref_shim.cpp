@@ -11,12 +11,15 @@
 #include <cstdio>
 #include <cstring>
 #include <exception>
+#include <limits>
+#include <random>
 #include <memory>
 #include <vector>
 
 #include "xtg/fp.h"
 #include "xtg/kernels.h"
 #include "xtg/kv.h"
+#include "xtg/sampler.h"
 #include "xtg/threadpool.h"
 
 using namespace xtg;
@@ -236,6 +239,36 @@ int xr_head(void* pool, const uint8_t* codes, const uint8_t* scales, float globa
     for (int r = 0; r < m; ++r)
       for (int j = 0; j < vocab; ++j) logits[size_t(r) * vocab + j] *= logit_scale[j];
   });
+}
+
+// Sampler (engine/include/xtg/sampler.h, engine/src/sampler.cpp)
+int xr_argmax(const float* logits, int n) { return argmax(logits, n); }
+
+// top_logprobs (sampler.cpp:30-40): the k most likely (log probability, token) pairs, most likely first.
+int xr_top_logprobs(const float* logits, int n, int k, float* lp, int32_t* idx) {
+  return guarded([&] {
+    std::vector<std::pair<float, int>> out;
+    top_logprobs(logits, n, k, out);
+    for (size_t i = 0; i < out.size(); ++i) {
+      lp[i] = out[i].first;
+      idx[i] = out[i].second;
+    }
+  });
+}
+
+// A fresh Sampler(seed)'s sample (sampler.cpp:41-94); *u = the first draw of an identically seeded engine in
+// [0, 1), the value its uniform_real_distribution(0, total) scales by total.
+int xr_sample(const float* logits, int n, float temperature, int top_k, float top_p, float min_p, uint64_t seed,
+              double* u) {
+  SamplingParams p;
+  p.temperature = temperature;
+  p.top_k = top_k;
+  p.top_p = top_p;
+  p.min_p = min_p;
+  Sampler s(seed);
+  std::mt19937_64 eng(seed);
+  *u = std::generate_canonical<double, std::numeric_limits<double>::digits>(eng);
+  return s.sample(logits, n, p);
 }
 
 }  // extern "C"

@@ -13,6 +13,11 @@ parameters and the reference's outputs. Cases follow the reference's own tests/k
   elementwise.npz  justnorm, slerp_residual, rope, swiglu_scaled (kernels.cpp:169-234)
   step_fp8.npz     three steps (8, 8, 3 rows) of a tiny synthetic Dory from an empty state, run with the reference's
                    kernels in DorySession::sublayer / run_chunk order with FP8 KvCaches (ring = window + 16 slots)
+  sampling.npz     argmax, top_logprobs and Sampler(seed).sample (sampler.cpp:8-94) on seeded logits rows with ties
+                   (vocab 4096 and 131072) under the filter settings of SAMPLING_PARAMS, with the first uniform draw
+                   of each seed's engine
+
+    python tests/golden/make_golden.py sampling   # only sampling.npz
 """
 import ctypes as C
 import os
@@ -188,9 +193,59 @@ def reference_steps(cfg, steps, threads=4):
     return out
 
 
+SAMPLING_VOCABS = (4096, 131072)
+SAMPLING_ROWS = 4
+SAMPLING_DRAWS = 12
+SAMPLING_TOPK = 64
+# (temperature, top_k, top_p, min_p)
+SAMPLING_PARAMS = [(0.0, 0, 1.0, 0.0), (0.7, 40, 1.0, 0.0), (1.0, 0, 0.9, 0.0), (0.8, 0, 1.0, 0.05),
+                   (1.2, 50, 0.95, 0.02), (1.0, 0, 1.0, 0.0), (0.6, 0, 0.5, 0.1), (0.05, 0, 0.99, 0.0)]
+
+
+def sampling_inputs(vocab):
+    """Logits rows N(0, 3^2) with ties: row 1 repeats its max ten times, row 2 rounds every 7th entry to 0.1, row 3
+    is rounded to 0.5 throughout (many equal values)."""
+    rng = np.random.default_rng(9 + vocab)
+    x = (rng.standard_normal((SAMPLING_ROWS, vocab)) * 3.0).astype(np.float32)
+    x[1, 100:110] = x[1].max()
+    x[2, ::7] = np.round(x[2, ::7], 1)
+    x[3] = np.round(x[3] * 2.0) / 2.0
+    return x
+
+
+def sampling_fixture(R):
+    res = {}
+    for vocab in SAMPLING_VOCABS:
+        x = sampling_inputs(vocab)
+        am = np.array([R.xr_argmax(O.ptr(np.ascontiguousarray(r), f32p), vocab) for r in x], np.int32)
+        lp = np.zeros((SAMPLING_ROWS, SAMPLING_TOPK), np.float32)
+        ix = np.zeros((SAMPLING_ROWS, SAMPLING_TOPK), np.int32)
+        tok = np.zeros((SAMPLING_ROWS, len(SAMPLING_PARAMS), SAMPLING_DRAWS), np.int32)
+        us = np.zeros((SAMPLING_ROWS, len(SAMPLING_PARAMS), SAMPLING_DRAWS), np.float64)
+        for r in range(SAMPLING_ROWS):
+            row = np.ascontiguousarray(x[r])
+            assert R.xr_top_logprobs(O.ptr(row, f32p), vocab, SAMPLING_TOPK, O.ptr(lp[r], f32p),
+                                     ix[r].ctypes.data_as(O.i32p)) == 0
+            for pi, (t, k, tp, mp) in enumerate(SAMPLING_PARAMS):
+                for d in range(SAMPLING_DRAWS):
+                    u = C.c_double()
+                    tok[r, pi, d] = R.xr_sample(O.ptr(row, f32p), vocab, t, k, tp, mp, 1000 + 17 * d, C.byref(u))
+                    us[r, pi, d] = u.value
+        res[f"v{vocab}_argmax"] = am
+        res[f"v{vocab}_top_lp"] = lp
+        res[f"v{vocab}_top_idx"] = ix
+        res[f"v{vocab}_tokens"] = tok
+        res[f"v{vocab}_u"] = us
+    np.savez_compressed(os.path.join(HERE, "sampling.npz"), **res)
+
+
 def main():
     R = O.ref()
     assert R is not None, "oracle/_ref/libxtgref.so missing: run `make -C oracle ref` with the reference present"
+    if sys.argv[1:] == ["sampling"]:
+        sampling_fixture(R)
+        print("sampling.npz written to", HERE)
+        return
     pool = R.xr_pool_new(4)
     # e4m3
     grid = e4m3_grid()
@@ -243,6 +298,7 @@ def main():
     # step
     logits = reference_steps(TINY, STEP_TOKENS)
     np.savez_compressed(os.path.join(HERE, "step_fp8.npz"), **{f"step{i}": l for i, l in enumerate(logits)})
+    sampling_fixture(R)
     R.xr_pool_free(pool)
     print("golden fixtures written to", HERE)
 

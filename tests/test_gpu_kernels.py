@@ -339,3 +339,51 @@ def test_kv_store_bit_exact(cuda, xtg, torch_mod, dtype, ring):
             assert np.array_equal(kc[h, s], c[0]) and kss[h, s] == sc[0]
             c, sc = O.kv_encode(dtype, v[p - pos, h][None])
             assert np.array_equal(vc[h, :, s], c[0]) and vss[h, s] == sc[0]
+
+
+# ---- top-k candidates of the sampler (engine/src/sampler.cpp): bit-exact indices and values ----
+
+def _total_f32_exp(row, temperature):
+    inv_t = np.float32(1.0) / np.float32(temperature)
+    return float(np.sum(np.exp((row - row.max()) * inv_t).astype(np.float32).astype(np.float64)))
+
+
+@pytest.mark.parametrize("vocab", G.SAMPLING_VOCABS)
+def test_topk_rows_match_oracle(cuda, xtg, torch_mod, vocab):
+    """The fixture's rows (ties: a repeated max, rounded entries, a row of half-integers) at k from 1 to 1024."""
+    torch = torch_mod
+    x = G.sampling_inputs(vocab)
+    t = torch.from_numpy(x).cuda()
+    for k in (1, 5, 64, 1024):
+        for temp in (1.0, 0.7):
+            idx, val, mx, tot = xtg.topk(t, k, temp)
+            torch.cuda.synchronize()
+            idx, val, mx, tot = idx.cpu().numpy(), val.cpu().numpy(), mx.cpu().numpy(), tot.cpu().numpy()
+            for r in range(G.SAMPLING_ROWS):
+                ri, rv = O.topk(x[r], k)
+                np.testing.assert_array_equal(idx[r], ri, err_msg=f"k={k} row {r}")
+                np.testing.assert_array_equal(val[r], rv)
+                assert mx[r] == x[r].max()
+                assert abs(tot[r] - _total_f32_exp(x[r], temp)) <= 1e-6 * tot[r]
+
+
+@pytest.mark.parametrize("vocab,k", [(7, 7), (1000, 1000), (1001, 3), (4099, 1024), (131071, 100)])
+def test_topk_rows_ragged(cuda, xtg, torch_mod, vocab, k):
+    """Rows that do not fill the cluster's entries (scalar loads, entries past the row), k up to the whole row."""
+    torch = torch_mod
+    rng = np.random.default_rng(vocab)
+    x = np.round(rng.standard_normal((3, vocab)) * 4).astype(np.float32)   # many ties
+    idx, val, mx, tot = xtg.topk(torch.from_numpy(x).cuda(), k, 1.0)
+    torch.cuda.synchronize()
+    for r in range(3):
+        ri, rv = O.topk(x[r], k)
+        np.testing.assert_array_equal(idx[r].cpu().numpy(), ri)
+        np.testing.assert_array_equal(val[r].cpu().numpy(), rv)
+        assert abs(tot[r].item() - _total_f32_exp(x[r], 1.0)) <= 1e-6 * tot[r].item()
+
+
+def test_topk_rejects_bad_k(cuda, xtg, torch_mod):
+    t = torch_mod.zeros(2, 100, device="cuda")
+    for k in (0, 101, 1025):
+        with pytest.raises(xtg.XtgError):
+            xtg.topk(t, k)

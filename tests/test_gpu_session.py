@@ -160,3 +160,33 @@ def test_error_paths_leave_state_unchanged(cuda, xtg, cfg):
         xtg.Session(cfg, context=100)            # not a multiple of 64
     with pytest.raises(xtg.XtgError):
         xtg.Session(dict(cfg, head_dim=64))      # the kernels are written for head_dim 128
+
+
+def test_topk_and_sampling_from_the_step(cuda, xtg, cfg):
+    """xtg_cuda_topk on the last step's logits equals the oracle's top-k of the logits the callback returned, and a
+    draw from the candidates equals Sampler::sample's (restated) on the whole row wherever the candidates decide."""
+    toks = [5, 17, 900, 3, 44, 1023, 0, 256]
+    with xtg.Session(cfg, context=256) as s:
+        s.prefill_synthetic(70)
+        out = logits_of(s.forward(toks, want=2), 8)
+        assert s.argmax(8) == [int(np.argmax(r)) for r in out]
+        for k, temp in ((1, 1.0), (64, 0.8), (1024, 1.0)):
+            idx, val, mx, tot = s.topk(k, temp)
+            assert idx.shape == (8, k)
+            for r in range(8):
+                ri, rv = O.topk(out[r], k)
+                np.testing.assert_array_equal(idx[r], ri)
+                np.testing.assert_array_equal(val[r], rv)
+                assert mx[r] == out[r].max()
+        idx, val, mx, tot = s.topk(1024, 0.8)
+        decided = 0
+        for r in range(8):
+            for (tk, tp, mp) in ((40, 1.0, 0.0), (0, 0.9, 0.0), (0, 1.0, 0.05), (20, 0.8, 0.01)):
+                for u in (0.0, 0.13, 0.5, 0.77, 0.999):
+                    got = xtg.sample_candidates(idx[r], val[r], mx[r], tot[r], cfg["vocab"], 0.8, tk, tp, mp, u)
+                    if got != -2:
+                        decided += 1
+                        assert got == O.sample(out[r], 0.8, tk, tp, mp, u)
+        assert decided > 0
+        with pytest.raises(xtg.XtgError):
+            s.topk(0)

@@ -2,9 +2,12 @@
 each, and the attention partials of the global layers joined by an NCCL all-gather before the log-sum-exp combine.
 
 Every process holds the whole model and every cache and runs the whole step; only the chunk range each global-layer
-attention reads differs. With the same total number of splits the chunk ranges, the partials and therefore the
-logits are those of one process bit for bit; with the default split counts (more splits in total) the logits move
-only by rounding. The single-process step itself is pinned to the oracle by the session tests."""
+attention reads differs. Two exchanges: the default one inside the combine kernel (each process merges its own
+splits, then the processes' partials meet over NVLink as sequence-numbered words) and an ncclAllGather of every
+split's partial. With the same total number of splits as one process, the all-gather gives that process's logits bit
+for bit and the peer exchange moves them by rounding only; every process computes the same bits either way. The
+single-process step itself is pinned to the oracle by the session tests. A process that steps alone makes its
+peers' words never arrive: the bounded wait gives up with an error instead of hanging."""
 import importlib.util
 import os
 import sys
@@ -91,11 +94,14 @@ def test_split_kv_across_two_gpus(cuda, xtg):
         assert info["kv_world"] == world and info["kv_rank"] == rank and info["splits_global"] == 128 // world
         assert info["kv_exchange"] == "peer" and ninfo["kv_exchange"] == "nccl" and info["global_layers"] > 0
         assert dinfo["splits_global"] * world <= 256
-        # the same 128 chunk ranges as one process: identical partials, identical logits, by either exchange
+        # the same 128 chunk ranges as one process: through the all-gather every split's partial meets in the same
+        # combine, so the logits are identical; the peer exchange merges each process's splits first, then the
+        # processes' partials (rounding only)
         assert sorted(logits) == sorted(one_same[1]) == sorted(nlogits)
         for r in logits:
-            np.testing.assert_array_equal(logits[r], one_same[1][r])
             np.testing.assert_array_equal(nlogits[r], one_same[1][r])
+            d = np.abs(logits[r] - one_same[1][r]).max()
+            assert d <= 5e-2, (rank, r, d)
         assert am == one_same[2] == nam
         assert (alone is None) if rank == 0 else ("timed out" in alone), alone
         # default split counts: rounding only
@@ -103,6 +109,7 @@ def test_split_kv_across_two_gpus(cuda, xtg):
             d = np.abs(dlogits[r] - one_dflt[1][r]).max()
             assert d <= 5e-2, (rank, r, d)
         assert dam == one_dflt[2]
-    # every process ends with the same result
-    for r in res[0][1][1]:
-        np.testing.assert_array_equal(res[0][1][1][r], res[1][1][1][r])
+    # every process computes the same bits (the partials are merged in rank order everywhere)
+    for k in range(3):
+        for r in res[0][k][1]:
+            np.testing.assert_array_equal(res[0][k][1][r], res[1][k][1][r])

@@ -38,6 +38,11 @@ class AttnArgs(C.Structure):
                 ("ring_pos", C.c_void_p), ("dtype", C.c_int), ("out", C.c_void_p)]
 
 
+class Sampling(C.Structure):
+    """xtg_cuda_sampling: Sampler::sample's parameters."""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_int), ("top_p", C.c_float), ("min_p", C.c_float)]
+
+
 def lib():
     """The loaded library; raises if it was not built (no silent fallback)."""
     global _lib
@@ -73,6 +78,15 @@ def lib():
         L.xtg_cuda_close.argtypes = [C.c_void_p]
         L.xtg_cuda_argmax.restype = C.c_int
         L.xtg_cuda_argmax.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int]
+        L.xtg_cuda_topk.restype = C.c_int
+        L.xtg_cuda_topk.argtypes = [C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                    E, C.c_int]
+        L.xtg_cuda_topk_rows.restype = C.c_int
+        L.xtg_cuda_topk_rows.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_void_p, C.c_void_p, E, C.c_int]
+        L.xtg_cuda_sample_candidates.restype = C.c_int
+        L.xtg_cuda_sample_candidates.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_double, C.c_int,
+                                                 C.POINTER(Sampling), C.c_double]
         L.xtg_cuda_prefill_synthetic.restype = C.c_int
         L.xtg_cuda_prefill_synthetic.argtypes = [C.c_void_p, C.c_int64, E, C.c_int]
         L.xtg_cuda_bench.restype = C.c_int
@@ -246,6 +260,21 @@ class Session:
             raise XtgError("argmax: no step yet")
         return list(out[:k])
 
+    def topk(self, k, temperature=1.0):
+        """xtg_cuda_topk: the last step's rows' k most likely entries (idx, logit [rows][k]), row max, total."""
+        import numpy as np
+        idx = np.empty((8, k), np.int32)
+        val = np.empty((8, k), np.float32)
+        mx = np.empty(8, np.float32)
+        tot = np.empty(8, np.float64)
+        err = _err()
+        rows = lib().xtg_cuda_topk(self.h, k, temperature, idx.ctypes.data, val.ctypes.data, mx.ctypes.data,
+                                   tot.ctypes.data, err, len(err))
+        if rows < 0:
+            raise XtgError(err.value.decode(errors="replace"))
+        return idx.reshape(-1)[:rows * k].reshape(rows, k), val.reshape(-1)[:rows * k].reshape(rows, k), \
+            mx[:rows], tot[:rows]
+
     def prefill_synthetic(self, n_past):
         err = _err()
         _check(lib().xtg_cuda_prefill_synthetic(self.h, n_past, err, len(err)), err)
@@ -364,6 +393,32 @@ def attention_noalloc(q, k, v, k_codes, v_codes, k_scales, v_scales, pos0, windo
     err = _err()
     _check(lib().xtg_cuda_attention_noalloc(C.byref(a), splits, _stream(), err, len(err)), err)
     return out
+
+
+def topk(logits, k, temperature=1.0):
+    """xtg_cuda_topk_rows on a torch CUDA tensor [rows][vocab] f32: (idx, logit [rows][k], row_max, total)."""
+    import torch
+    rows, vocab = logits.shape
+    dev = logits.device
+    idx = torch.empty(rows, k, dtype=torch.int32, device=dev)
+    val = torch.empty(rows, k, dtype=torch.float32, device=dev)
+    mx = torch.empty(rows, dtype=torch.float32, device=dev)
+    tot = torch.empty(rows, dtype=torch.float64, device=dev)
+    err = _err()
+    _check(lib().xtg_cuda_topk_rows(logits.data_ptr(), rows, vocab, k, temperature, idx.data_ptr(), val.data_ptr(),
+                                    mx.data_ptr(), tot.data_ptr(), _stream(), err, len(err)), err)
+    return idx, val, mx, tot
+
+
+def sample_candidates(idx, logit, row_max, total, vocab, temperature=1.0, top_k=0, top_p=1.0, min_p=0.0, u=0.5):
+    """xtg_cuda_sample_candidates (host only): Sampler::sample over one row's candidates; -2 when they cannot
+    decide (the caller samples from the full row)."""
+    import numpy as np
+    idx = np.ascontiguousarray(idx, np.int32)
+    logit = np.ascontiguousarray(logit, np.float32)
+    p = Sampling(temperature, top_k, top_p, min_p)
+    return lib().xtg_cuda_sample_candidates(idx.ctypes.data, logit.ctypes.data, len(idx), float(row_max),
+                                            float(total), vocab, C.byref(p), u)
 
 
 def kv_store(k, v, pos, slots, ring, dtype, k_codes, v_codes, k_scales, v_scales):

@@ -11,6 +11,7 @@
 #include "attention.h"
 #include "common.cuh"
 #include "elementwise.h"
+#include "sampling.h"
 #include "fp4mma.cuh"
 #include "kernels.h"
 
@@ -361,6 +362,14 @@ int xtg_cuda_gen(int what, uint64_t seed, uint64_t stream_id, float a, float b, 
     else
       throw CudaError("gen: what must be 0, 1 or 2");
     XTG_CUDA(cudaStreamSynchronize(s));
+  });
+}
+
+int xtg_cuda_topk_rows(const float* logits, int rows, int vocab, int k, float temperature, int32_t* idx, float* logit,
+                       float* row_max, double* total, void* stream, char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_REQUIRE(logits && idx && logit && row_max && total, "topk: null pointer");
+    launch_topk(logits, rows, vocab, k, temperature, idx, logit, row_max, total, static_cast<cudaStream_t>(stream));
   });
 }
 

@@ -314,8 +314,6 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     }
   }
   __syncthreads();
-  const int xw = a.x.world;   // > 1: the split-KV exchange across GPUs
-  const uint32_t xrun = xw > 1 ? *a.x.epoch * (uint32_t)a.x.n_g + (uint32_t)a.x.g : 0u;
   {
     // thread: query row r, head dims j, j + 8, ...: a warp's stores cover 4 rows x 8 consecutive dims
     const int r = threadIdx.x >> 3, j = threadIdx.x & 7;
@@ -334,37 +332,22 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
         w[q] = mp[q] == -INFINITY ? 0.f : expf(mp[q] - M);
         L += w[q] == 0.f ? 0.f : st0[q * ss + r * kStateStride + 1] * w[q];
       }
-      float o[kD / 8];
+      const int pidx = a.part_local ? split : sidx;
+      float* out = a.part + (((int64_t)pidx * a.kv_heads + kvh) * kQRows + r) * kPartStride;
+      if (j == 0) {
+        out[0] = M;
+        out[1] = L;
+      }
 #pragma unroll
       for (int k = 0; k < kD / 8; ++k) {
         const int d = j + 8 * k;
-        o[k] = 0.f;
+        float o = 0.f;
 #pragma unroll
         for (int q = 0; q < kQuarters; ++q)
-          if (w[q] != 0.f) o[k] += st0[q * ss + r * kStateStride + 2 + d] * w[q];
-      }
-      const int64_t off = (((int64_t)sidx * a.kv_heads + kvh) * kQRows + r) * kPartStride;
-      // the partial into this process's buffer, or with the exchange on into every process's (peers over NVLink)
-#pragma unroll
-      for (int t = 0; t < kMaxKvWorld; ++t) {
-        if (t > 0 && t >= xw) break;
-        float* out = (xw > 1 ? a.x.part[t] + (xrun & 1) * a.x.part_floats : a.part) + off;
-        if (j == 0) {
-          out[0] = M;
-          out[1] = L;
-        }
-#pragma unroll
-        for (int k = 0; k < kD / 8; ++k) out[2 + j + 8 * k] = o[k];
+          if (w[q] != 0.f) o += st0[q * ss + r * kStateStride + 2 + d] * w[q];
+        out[2 + d] = o;
       }
     }
-  }
-  if (xw > 1) {   // every thread's stores are out before the flags go up (fence, then the block's barrier)
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x == 0)
-#pragma unroll
-      for (int t = 0; t < kMaxKvWorld; ++t)
-        if (t < xw) st_release_sys(a.x.flag[t] + ((xrun & 1) * a.kv_heads + kvh) * kMaxSplits + sidx, xrun + 1);
   }
 }
 
@@ -398,17 +381,6 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
     vj[j] = j < m ? a.v[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
   }
   const float gt = a.out ? 0.f : a.gate[(int64_t)i * a.gate_ld + col];
-  if (a.x.world > 1) {   // the split-KV exchange: every part's flag in this process's memory, then its buffer
-    const uint32_t run = *a.x.epoch * (uint32_t)a.x.n_g + (uint32_t)a.x.g;
-    const uint32_t* fl = a.x.flag[0];
-#pragma unroll
-    for (int t = 1; t < kMaxKvWorld; ++t)
-      if (t == a.x.rank) fl = a.x.flag[t];
-    fl += ((run & 1) * a.kv_heads + kvh) * kMaxSplits;
-    for (int s = d; s < a.splits; s += kD) peer_wait_bounded(fl + s, run + 1, a.x.wait_ns, a.err);
-    base += (run & 1) * a.x.part_floats;
-    __syncthreads();
-  }
   // every independent load in one wave: this thread's dim of every split's partial, the m and l of splits d and
   // d + 128
   const int ns = a.splits < kRegSplits ? a.splits : kRegSplits;
@@ -466,17 +438,67 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
     own_s[j] = vis ? ((part_s[0][j] + part_s[1][j]) + (part_s[2][j] + part_s[3][j])) * a.scale : -INFINITY;
     own_m = fmaxf(own_m, own_s[j]);
   }
-  const float wgt_max = cached[0];
-  const float mall = fmaxf(own_m, wgt_max);
-  const float cs = wgt_max == -INFINITY ? 0.f : expf(wgt_max - mall);   // the cached part's weight
+  float wgt_max = cached[0], lcached = cached[1];
   float o = 0.f;
 #pragma unroll
   for (int s = 0; s < kRegSplits; ++s)
     if (s < ns) o += acc_s[s] * wgt[s];
   for (int s = kRegSplits; s < a.splits; ++s)
     if (wgt[s] != 0.f) o += base[s * sstride + 2 + d] * wgt[s];
+  if (a.x.world > 1) {
+    // split-KV across GPUs: this process's cached part (m, l, o relative to m) to every peer, theirs from this
+    // process's slots, all merged in rank order (the same bits on every process)
+    const uint32_t run = *a.x.epoch * (uint32_t)a.x.n_g + (uint32_t)a.x.g, seq = run + 1;
+    const int64_t set = (int64_t)(run & 1) * a.x.world;
+    auto slot_of = [&](uint64_t* sl, int src) { return sl + (((set + src) * kMaxRows + i) * a.heads + h) * kPartStride; };
+    uint64_t* mine = a.x.slot[0];
+#pragma unroll
+    for (int t = 0; t < kMaxKvWorld; ++t) {
+      if (t < a.x.world && t == a.x.rank) mine = a.x.slot[t];
+      if (t < a.x.world && t != a.x.rank) {
+        uint64_t* w = slot_of(a.x.slot[t], a.x.rank);
+        put_seq_word(w + 2 + d, o, seq);
+        if (d == 0) {
+          put_seq_word(w, wgt_max, seq);
+          put_seq_word(w + 1, lcached, seq);
+        }
+      }
+    }
+    float mt[kMaxKvWorld], lt[kMaxKvWorld], ot[kMaxKvWorld];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int t = 0; t < kMaxKvWorld; ++t) {
+      mt[t] = -INFINITY;
+      lt[t] = ot[t] = 0.f;
+      if (t < a.x.world) {
+        if (t == a.x.rank) {
+          mt[t] = wgt_max;
+          lt[t] = lcached;
+          ot[t] = o;
+        } else {
+          const uint64_t* w = slot_of(mine, t);
+          mt[t] = take_seq_word(w, seq, a.x.wait_ns, a.err);
+          lt[t] = take_seq_word(w + 1, seq, a.x.wait_ns, a.err);
+          ot[t] = take_seq_word(w + 2 + d, seq, a.x.wait_ns, a.err);
+        }
+      }
+      mx = fmaxf(mx, mt[t]);
+    }
+    float l = 0.f, oo = 0.f;
+#pragma unroll
+    for (int t = 0; t < kMaxKvWorld; ++t) {
+      const float wt = mt[t] == -INFINITY ? 0.f : expf(mt[t] - mx);
+      l += wt == 0.f ? 0.f : lt[t] * wt;
+      oo += wt == 0.f ? 0.f : ot[t] * wt;
+    }
+    wgt_max = mx;
+    lcached = l;
+    o = oo;
+  }
+  const float mall = fmaxf(own_m, wgt_max);
+  const float cs = wgt_max == -INFINITY ? 0.f : expf(wgt_max - mall);   // the cached part's weight
   // merge the cached part (relative to wgt_max) and the own keys (relative to mall)
-  float lsum = cached[1] * cs;
+  float lsum = lcached * cs;
   o *= cs;
 #pragma unroll
   for (int j = 0; j < kMaxRows; ++j) {
@@ -522,10 +544,6 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
   XTG_REQUIRE(a.splits_total == 0 || (a.split0 >= 0 && a.split0 + a.splits <= a.splits_total &&
                                        a.splits_total <= kMaxSplits),
               "attention: split range outside 0..splits_total (at most 256)");
-  XTG_REQUIRE(a.x.world <= 1 || (a.x.world <= kMaxKvWorld && a.x.rank >= 0 && a.x.rank < a.x.world && a.x.epoch &&
-                                 a.splits_total > 0 && a.x.part_floats >= attention_part_floats(a.kv_heads,
-                                                                                                a.splits_total)),
-              "attention: split-KV exchange needs 2..8 processes, the epoch and a part buffer for every split");
   static bool attr_set = false;
   if (!attr_set) {
     XTG_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -550,8 +568,10 @@ void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
   a.pdl = pdl ? 1 : 0;
   XTG_REQUIRE(a.splits >= 1 && a.splits <= kMaxSplits, "combine: 1..256 splits");
   XTG_REQUIRE(a.x.world <= 1 || (a.x.world <= kMaxKvWorld && a.x.rank >= 0 && a.x.rank < a.x.world && a.x.epoch &&
-                                 a.err && a.x.flag[a.x.rank]),
-              "combine: split-KV exchange needs 2..8 processes, the epoch, its flags and an error word");
+                                 a.err && a.out == nullptr),
+              "combine: split-KV exchange needs 2..8 processes, the epoch and an error word (the step only)");
+  for (int t = 0; t < a.x.world && a.x.world > 1; ++t)
+    XTG_REQUIRE(a.x.slot[t], "combine: split-KV exchange without the slots of every process");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kMaxRows, a.heads);
   cfg.blockDim = dim3(kD);

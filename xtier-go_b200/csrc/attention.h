@@ -33,18 +33,19 @@ struct StepParams {
   int64_t pos0;
 };
 
-// Batch-1 split-KV across GPUs with the partials exchanged by the attention kernel itself (world > 1): every CTA
-// stores its partial into the part buffer of every process (this one's and the peers', mapped by CUDA IPC over
-// NVLink) and then raises its flag there; each process's combine waits for the flags of all parts, then reads its
-// own buffer. Two buffers alternate by the running global-layer count, so a process one layer ahead never writes a
-// buffer that a slower one is still reading: its next write to the same buffer needs the slower one's next layer.
+// Batch-1 split-KV across GPUs with the exchange inside the combine kernel (world > 1): each process attends its
+// share of the global cache's chunks and merges its own splits; each combine CTA then stores its (row, head)'s merged
+// partial (max m, sum l, o[128]) into every peer's exchange slots as 64-bit words that carry the step's sequence
+// number beside each value -- a word is complete once its number is right, so no fence or flag is needed -- reads
+// the peers' words from its own slots and merges all processes' partials in rank order, so that every process
+// computes the same bits. Two slot sets alternate by the running global-layer count: a process one layer ahead never
+// writes a slot that a slower one has still to read, since its next write to the same set needs the slower one's
+// next layer.
 constexpr int kMaxKvWorld = 8;
 struct PeerXchg {
-  float* part[kMaxKvWorld];      // by rank: that process's 2 part buffers, part_floats apart
-  uint32_t* flag[kMaxKvWorld];   // by rank: that process's flags [2][kv_heads][256]
-  int64_t part_floats;           // one buffer: splits_total x kv_heads x 32 x 130
+  uint64_t* slot[kMaxKvWorld];   // by rank: that process's slots [2][world][8 rows][heads][130]
   const uint32_t* epoch;         // steps completed here (the step's last kernel advances it)
-  uint64_t wait_ns;              // the combine's bound on waiting for a peer
+  uint64_t wait_ns;              // bound on waiting for a peer's words
   int world, rank;               // world 0 or 1: off
   int g, n_g;                    // this layer's index among the step's n_g global layers
 };
@@ -75,9 +76,9 @@ struct AttnArgs {
   // (another process may compute the rest: the batch-1 split-KV over GPUs). 0 / 0: split0 0, splits_total = splits.
   int split0, splits_total;
   float* part;              // [splits_total][kv_heads][32][130], split-major (a process's splits are contiguous)
+  int part_local;           // partials at index split (this launch's own) instead of split0 + split
   int* err;                 // set if a bounded wait gave up (never expected); may be null
   int pdl;
-  PeerXchg x;               // global layers of a split-KV step across GPUs (part unused then)
 };
 
 struct CombineArgs {
@@ -99,7 +100,7 @@ struct CombineArgs {
   float* ab_pre;            // [heads * 8][8] their prescales
   float* asum;              // step: [heads][8] sum of squares per head and activation row
   int pdl;
-  PeerXchg x;               // as in AttnArgs: part is then this process's buffer pair, x.flag[x.rank] its flags
+  PeerXchg x;               // split-KV across GPUs: splits are this process's, merged with the peers' here
   int* err;                 // set if the wait for a peer gave up
 };
 

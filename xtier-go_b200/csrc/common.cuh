@@ -91,36 +91,38 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   return true;
 }
 
-// ---- flags between GPUs (another process's memory, mapped over NVLink) ----
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
+// ---- words between GPUs (another process's memory, mapped over NVLink) ----
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
 
-// Wait until *f == want, a value another GPU stores. After wait_ns, or once *err is set (another wait of this step
-// gave up), set *err and return false: a process that stopped stepping costs one timeout per step, not one per wait.
-__device__ __forceinline__ bool peer_wait_bounded(const uint32_t* f, uint32_t want, uint64_t wait_ns, int* err) {
-  if (ld_acquire_sys(f) == want) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    __nanosleep(64);
-    if (ld_acquire_sys(f) == want) return true;
-    if ((it & 63) == 0 && (*reinterpret_cast<volatile int*>(err) != 0 || globaltimer_ns() - t0 > wait_ns)) {
-      atomicExch(err, 2);
-      return false;
+// A value and a sequence number in one 64-bit word: an aligned 64-bit store is seen whole or not at all, so the
+// reader knows the value is this round's once the number matches.
+__device__ __forceinline__ void put_seq_word(uint64_t* p, float v, uint32_t seq) {
+  const uint64_t w = ((uint64_t)seq << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+// The value of *p once its number is seq. After wait_ns, or at once when *err is set (another wait of this step
+// gave up), set *err and return 0: a process that stopped stepping costs one timeout per step, not one per wait.
+__device__ __forceinline__ float take_seq_word(const uint64_t* p, uint32_t seq, uint64_t wait_ns, int* err) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  if ((uint32_t)(w >> 32) != seq) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+      __nanosleep(32);
+      asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+      if ((uint32_t)(w >> 32) == seq) break;
+      if ((it & 63) == 0 && (*reinterpret_cast<volatile int*>(err) != 0 || globaltimer_ns() - t0 > wait_ns)) {
+        atomicExch(err, 2);
+        return 0.f;
+      }
     }
   }
+  return __uint_as_float((uint32_t)w);
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() {

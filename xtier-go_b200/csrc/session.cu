@@ -24,6 +24,7 @@
 #include "fp4mma.cuh"
 #include "json.h"
 #include "nccl_rt.h"
+#include "sampling.h"
 #include "kernels.h"
 
 namespace xtg {
@@ -51,8 +52,8 @@ struct Config {
   // layers meet by an NCCL all-gather (kv_world processes, this one kv_rank, nccl_id the 128-byte unique id in hex)
   int kv_world = 1, kv_rank = 0;
   std::string nccl_id;
-  // "peer": the attention kernels store their partials into every process's buffer over NVLink (CUDA IPC) and the
-  // combine waits on flags, at most kv_wait_ms; "nccl": an ncclAllGather of the partials between the two kernels
+  // "peer": each combine kernel sends its merged partials to the peers' exchange slots over NVLink (CUDA IPC) and
+  // waits for theirs, at most kv_wait_ms; "nccl": an ncclAllGather of every split's partial between the kernels
   std::string kv_exchange = "peer";
   int kv_wait_ms = 10000;
 
@@ -234,14 +235,19 @@ struct xtg_cuda {
   float *asum = nullptr, *vsum = nullptr, *rsum = nullptr, *logits = nullptr, *logits_host = nullptr, *argmax_val = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   int32_t* argmax = nullptr;
+  // xtg_cuda_topk's results on the device (allocated at its first call)
+  int32_t* tk_idx = nullptr;
+  float* tk_val = nullptr;
+  float* tk_max = nullptr;
+  double* tk_total = nullptr;
   ArgCand* cand = nullptr;
   int* dev_err = nullptr;   // bounded device waits that gave up (never expected)
   int* err_host = nullptr;  // pinned copy of dev_err
   int splits_g = 1, splits_r = 1;
   int proj_ld = 0;
   ncclComm_t comm = nullptr;   // split-KV only
-  // the peer exchange: this process's 2 part buffers + flags in one allocation (exported by CUDA IPC), the peers'
-  // (imported), the step counter, the global layers per step
+  // the peer exchange: this process's exchange slots (exported by CUDA IPC), the peers' (imported), the step
+  // counter, the global layers per step
   void* xbuf = nullptr;
   void* peer_base[kMaxKvWorld] = {};
   PeerXchg xchg = {};
@@ -694,15 +700,12 @@ struct xtg_cuda {
       at.kv_heads = c.kv_heads;
       at.splits = K.ring ? splits_r : splits_g;
       const bool shard = !K.ring && comm;   // this process attends its share of the global cache's chunks
-      const bool peer = shard && xbuf;      // ... and sends its partials to the peers itself
+      const bool peer = shard && xbuf;      // ... and merges its splits before the peers' partials come in
       at.split0 = shard ? c.kv_rank * splits_g : 0;
       at.splits_total = shard ? splits_g * c.kv_world : at.splits;
-      at.part = peer ? xchg.part[c.kv_rank] : part;
+      at.part_local = peer ? 1 : 0;
+      at.part = part;
       at.err = dev_err;
-      if (peer) {
-        at.x = xchg;
-        at.x.g = glob++;
-      }
       mark(kClsAttn, true);
       launch_attention(at, stream, pdl);
       mark(kClsAttn, false);
@@ -711,15 +714,18 @@ struct xtg_cuda {
         nccl_check(nccl_api().all_gather(part + c.kv_rank * n, part, n, ncclFloat32, comm, stream), "ncclAllGather");
       }
       CombineArgs cb = {};
-      cb.part = at.part;
-      cb.x = at.x;
+      cb.part = part;
       cb.err = dev_err;
+      if (peer) {
+        cb.x = xchg;
+        cb.x.g = glob++;
+      }
       cb.q = q_prep;
       cb.k = k_new;
       cb.v = v_new;
       cb.scale = at.scale;
       cb.window = at.window;
-      cb.splits = at.splits_total;
+      cb.splits = peer ? at.splits : at.splits_total;
       cb.heads = c.heads;
       cb.kv_heads = c.kv_heads;
       cb.params = params_dev;
@@ -758,8 +764,8 @@ struct xtg_cuda {
     mark(kClsSmall, false);
   }
 
-  // The split-KV peer exchange: allocate this process's part buffers and flags, export them by CUDA IPC, and map the
-  // peers' (the handles travel by an NCCL all-gather, which also checks that every process sized them alike).
+  // The split-KV peer exchange: allocate this process's exchange slots, export them by CUDA IPC, and map the peers'
+  // (the handles travel by an NCCL all-gather, which also checks that every process sized them alike).
   void open_peer_exchange() {
     struct Record {
       cudaIpcMemHandle_t handle;
@@ -768,9 +774,7 @@ struct xtg_cuda {
     };
     const int w = c.kv_world, r = c.kv_rank;
     if (w > kMaxKvWorld) throw CudaError("split-KV: at most 8 processes");
-    const int64_t pf = attention_part_floats(c.kv_heads, splits_g * w);
-    const size_t flag_bytes = (size_t)2 * c.kv_heads * 256 * sizeof(uint32_t);
-    const size_t bytes = (size_t)2 * pf * sizeof(float) + flag_bytes;
+    const size_t bytes = (size_t)2 * w * kMaxRows * c.heads * 130 * sizeof(uint64_t);
     XTG_CUDA(cudaMalloc(&xbuf, bytes));
     XTG_CUDA(cudaMemset(xbuf, 0, bytes));
     epoch = dalloc<uint32_t>(1);
@@ -789,15 +793,13 @@ struct xtg_cuda {
     for (int t = 0; t < w; ++t) {
       if (all[t].bytes != bytes || all[t].n_glob != n_glob || all[t].splits != splits_g)
         throw CudaError("split-KV: process " + std::to_string(t) + " has another model, context or split count");
-      char* base = static_cast<char*>(xbuf);
+      void* base = xbuf;
       if (t != r) {
         XTG_CUDA(cudaIpcOpenMemHandle(&peer_base[t], all[t].handle, cudaIpcMemLazyEnablePeerAccess));
-        base = static_cast<char*>(peer_base[t]);
+        base = peer_base[t];
       }
-      xchg.part[t] = reinterpret_cast<float*>(base);
-      xchg.flag[t] = reinterpret_cast<uint32_t*>(base + (size_t)2 * pf * sizeof(float));
+      xchg.slot[t] = static_cast<uint64_t*>(base);
     }
-    xchg.part_floats = pf;
     xchg.epoch = epoch;
     xchg.wait_ns = (uint64_t)c.kv_wait_ms * 1000000ull;
     xchg.world = w;
@@ -1163,6 +1165,31 @@ int xtg_cuda_argmax(xtg_cuda* h, int32_t* out, int n) {
   } catch (const std::exception&) {
     return -1;
   }
+}
+
+int xtg_cuda_topk(xtg_cuda* h, int k, float temperature, int32_t* idx, float* logit, float* row_max, double* total,
+                  char* err, int err_len) {
+  int rows = 0;
+  const int rc = guarded(err, err_len, [&] {
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    rows = h->last_rows;
+    XTG_REQUIRE(rows > 0, "topk: no step yet");
+    XTG_REQUIRE(k >= 1 && k <= kMaxTopK && k <= h->c.vocab, "topk: k in 1..min(1024, vocab)");
+    XTG_REQUIRE(idx && logit && row_max && total, "topk: null output");
+    if (!h->tk_idx) {
+      h->tk_idx = h->dalloc<int32_t>((size_t)kMaxRows * kMaxTopK, false);
+      h->tk_val = h->dalloc<float>((size_t)kMaxRows * kMaxTopK, false);
+      h->tk_max = h->dalloc<float>(kMaxRows, false);
+      h->tk_total = h->dalloc<double>(kMaxRows, false);
+    }
+    launch_topk(h->logits, rows, h->c.vocab, k, temperature, h->tk_idx, h->tk_val, h->tk_max, h->tk_total, h->stream);
+    XTG_CUDA(cudaMemcpyAsync(idx, h->tk_idx, sizeof(int32_t) * rows * k, cudaMemcpyDeviceToHost, h->stream));
+    XTG_CUDA(cudaMemcpyAsync(logit, h->tk_val, sizeof(float) * rows * k, cudaMemcpyDeviceToHost, h->stream));
+    XTG_CUDA(cudaMemcpyAsync(row_max, h->tk_max, sizeof(float) * rows, cudaMemcpyDeviceToHost, h->stream));
+    XTG_CUDA(cudaMemcpyAsync(total, h->tk_total, sizeof(double) * rows, cudaMemcpyDeviceToHost, h->stream));
+    XTG_CUDA(cudaStreamSynchronize(h->stream));
+  });
+  return rc == 0 ? rows : -1;
 }
 
 int xtg_cuda_prefill_synthetic(xtg_cuda* h, int64_t n_past, char* err, int err_len) {
