@@ -33,6 +33,7 @@ METRIC = "decode tok/s per B200 (NVFP4 Dory-shape, 8K ctx) and % of HBM roofline
 UNIT = "tok/s"
 TOKENS = [17, 4242, 99, 131071, 5, 70000, 123, 2048]
 PREFILL = 8184
+TOPK = 64
 FALLBACK_HBM = 6650.0
 
 
@@ -470,6 +471,32 @@ def split_kv_block(x, rank, world, local_rank, dist, steps, warmup, context=3276
     return out
 
 
+def topk_block(x, device, vocab, reps=20):
+    """Device time of the sampler-candidate kernel (xtg_cuda_topk_rows) on 8 rows of logits at k = 64 and 1024:
+    one read of the rows (8 x vocab x 4 bytes) against the HBM roofline."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(5)
+    logits = torch.randn(8, vocab, device=device, generator=g) * 3
+    peak, _ = peaks()
+    out = {}
+    for k in (TOPK, 1024):
+        for _ in range(3):
+            x.topk(logits, k)
+        torch.cuda.synchronize()
+        st = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            x.topk(logits, k)
+        e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        alg = 8 * vocab * 4
+        out[f"k{k}"] = {"us": us, "algorithmic_bytes": alg, "gbs": alg / us / 1e3, "frac": alg / us / 1e3 / peak}
+    return out
+
+
 def job_rows_per_s(world, ms_per_step):
     """Whole-job throughput: every rank verifies 8 rows of its own sequence per step (weak scaling)."""
     return world * 8.0 / (ms_per_step / 1e3)
@@ -506,6 +533,20 @@ def run_ours(args, rank, world, local_rank, dist):
     e2e_s = (time.perf_counter() - t0) / args.steps
     barrier()
     e2e_s = max_over_ranks(e2e_s, dist)
+    # the same, reading back the sampler's 64 most likely candidates per row (xtg_cuda_topk) instead of whole rows
+    for _ in range(2):
+        s.forward(TOKENS, want=0)
+        s.topk(TOPK)
+        s.rewind(PREFILL)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        s.forward(TOKENS, want=0)
+        s.topk(TOPK)
+        s.rewind(PREFILL)
+    e2e_topk_s = (time.perf_counter() - t0) / args.steps
+    barrier()
+    e2e_topk_s = max_over_ranks(e2e_topk_s, dist)
     # per-kernel-class device time (eager launches with events), for the roofline of the dominant kernel
     pms, cms, cl = s.bench(TOKENS, 3, profile=True)
     gemv_bytes = s.step_bytes(1, 8)
@@ -516,6 +557,7 @@ def run_ours(args, rank, world, local_rank, dist):
     traffic = ncu_traffic()
     info = s.info()
     s.close()
+    topk_t = topk_block(x, f"cuda:{local_rank}", model["vocab"]) if world == 1 else None
     gemm = gemm_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg0 = config0_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg2 = config2_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
@@ -528,6 +570,9 @@ def run_ours(args, rank, world, local_rank, dist):
             "data": "synthetic (seeded random-init weights, random prefilled KV)", "config": config_block(world),
             "e2e": {"value": world * 8.0 / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 48,
                     "d2h_bytes_per_step": 8 * model["vocab"] * 4, "ms_per_step": e2e_s * 1e3},
+            "e2e_topk": {"value": world * 8.0 / e2e_topk_s, "unit": UNIT, "h2d_bytes_per_step": 48,
+                         "d2h_bytes_per_step": 8 * TOPK * 8 + 8 * 12, "ms_per_step": e2e_topk_s * 1e3,
+                         "note": f"forward without logits, then xtg_cuda_topk(k={TOPK}): the sampler's candidates"},
             "roofline": {"bound": "hbm", "kernel": "gemv_nvfp4 (all NVFP4 GEMVs of the step)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": traffic,
@@ -541,6 +586,8 @@ def run_ours(args, rank, world, local_rank, dist):
             "clocks": clk.summary(),
             "library": {"splits_global": info.get("splits_global"), "splits_ring": info.get("splits_ring"),
                         "graph": info.get("graph"), "pdl": info.get("pdl")}}
+    if topk_t:
+        line["topk"] = topk_t
     if cfg0:
         line["config0_gemv"] = {"config": "config0: one NVFP4 GEMV, M = 1, 16 weight copies rotated", **cfg0}
     if cfg2:
