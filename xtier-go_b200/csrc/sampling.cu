@@ -239,8 +239,9 @@ __global__ void __cluster_dims__(kTkCtas, 1, 1) __launch_bounds__(kTkThreads, 1)
   }
   if ((int)threadIdx.x < k) {
     const unsigned long long c = cand[threadIdx.x];
-    out_idx[(int64_t)row * k + threadIdx.x] = (int32_t)(0xffffffffu - (uint32_t)(c & 0xffffffffull));
-    out_val[(int64_t)row * k + threadIdx.x] = key_value((uint32_t)(c >> 32));
+    const int32_t i = (int32_t)(0xffffffffu - (uint32_t)(c & 0xffffffffull));
+    out_idx[(int64_t)row * k + threadIdx.x] = i;
+    out_val[(int64_t)row * k + threadIdx.x] = src[i];   // the logit as given (a -0 keeps its sign)
   }
 }
 
