@@ -28,9 +28,11 @@ constexpr int kTkCtas = 8;
 constexpr int kTkThreads = 1024;
 constexpr int kTkPer = 16;   // entries per thread: 8 x 1024 x 16 = 131,072 per row at most
 
-// float -> key with the same order (larger value, larger key); NaN is not expected in logits
+// float -> key with the same order (larger value, larger key); -0 and +0 compare equal as floats do (more_likely
+// breaks their tie by index), so both get +0's key. NaN is not expected in logits.
 __device__ __forceinline__ uint32_t order_key(float f) {
-  const uint32_t u = __float_as_uint(f);
+  uint32_t u = __float_as_uint(f);
+  if (u == 0x80000000u) u = 0u;
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
