@@ -204,9 +204,13 @@ class Session:
         toks = (C.c_int32 * len(tokens))(*[int(t) for t in tokens])
         out = {}
         vocab = self.model["vocab"]
+        rows = np.empty((len(tokens) if want == 2 else min(1, want), vocab), np.float32) if want else None
+        nbytes = vocab * 4
 
-        def cb(row, ptr, user):
-            out[row] = np.ctypeslib.as_array(ptr, shape=(vocab,)).copy()
+        def cb(row, ptr, user):   # the row is valid only during the call: one copy into the result array
+            dst = rows[row if want == 2 else 0]
+            C.memmove(dst.ctypes.data, ptr, nbytes)
+            out[row] = dst
 
         fn = LOGITS_FN(cb)
         err = _err()

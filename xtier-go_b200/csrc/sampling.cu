@@ -224,11 +224,13 @@ __global__ void __cluster_dims__(kTkCtas, 1, 1) __launch_bounds__(kTkThreads, 1)
   }
   cl.sync();   // the leader holds all k candidates; every CTA is done with the others' shared memory
   if (crank != 0) return;
-  // ---- bitonic sort of 1024 composite keys, descending ----
-  for (int size = 2; size <= 1024; size <<= 1) {
+  // ---- bitonic sort of the first P composite keys (P: the power of two at or above k), descending ----
+  int P = 2;
+  while (P < k) P <<= 1;
+  for (int size = 2; size <= P; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       const int i = (int)threadIdx.x, j = i ^ stride;
-      if (j > i) {
+      if (j > i && j < P) {
         const unsigned long long a = cand[i], b = cand[j];
         const bool desc = (i & size) == 0;
         if (desc ? a < b : a > b) {
