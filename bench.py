@@ -561,7 +561,9 @@ def run_ours(args, rank, world, local_rank, dist):
     gemm = gemm_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg0 = config0_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg2 = config2_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
-    skv = split_kv_block(x, rank, world, local_rank, dist, args.steps, args.warmup) if world > 1 else None
+    # the batch-1 split over GPUs: measured where its 2-GPU tests run (--split-kv-max raises the bound)
+    skv = (split_kv_block(x, rank, world, local_rank, dist, args.steps, args.warmup)
+           if 1 < world <= args.split_kv_max else None)
     if rank != 0:
         return
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -629,6 +631,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-1 M=512 prefill GEMM measurement")
+    ap.add_argument("--split-kv-max", type=int, default=2,
+                    help="largest world size at which the batch-1 split-KV step is measured (N > 1)")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling driver: run this many eager steps (no graph, no JSON) for ncu, then exit")
     ap.add_argument("--ncu-model", default="full", choices=["full", "small"],
