@@ -631,7 +631,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-1 M=512 prefill GEMM measurement")
-    ap.add_argument("--split-kv-max", type=int, default=2,
+    ap.add_argument("--split-kv-max", type=int, default=4,
                     help="largest world size at which the batch-1 split-KV step is measured (N > 1)")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling driver: run this many eager steps (no graph, no JSON) for ncu, then exit")
