@@ -387,3 +387,20 @@ def test_topk_rejects_bad_k(cuda, xtg, torch_mod):
     for k in (0, 101, 1025):
         with pytest.raises(xtg.XtgError):
             xtg.topk(t, k)
+
+
+def test_topk_rows_unaligned_pointer(cuda, xtg, torch_mod):
+    """Rows starting one float past a 16-byte boundary (a caller's sub-view) take the scalar loads."""
+    torch = torch_mod
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((2, 4096)).astype(np.float32)
+    buf = torch.zeros(2 * 4096 + 1, device="cuda")
+    buf[1:] = torch.from_numpy(x.reshape(-1)).cuda()
+    view = buf[1:].view(2, 4096)
+    assert view.data_ptr() % 16 == 4
+    idx, val, mx, tot = xtg.topk(view, 64, 1.0)
+    torch.cuda.synchronize()
+    for r in range(2):
+        ri, rv = O.topk(x[r], 64)
+        np.testing.assert_array_equal(idx[r].cpu().numpy(), ri)
+        np.testing.assert_array_equal(val[r].cpu().numpy(), rv)

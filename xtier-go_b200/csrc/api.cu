@@ -62,6 +62,16 @@ int guarded(char* err, int err_len, F&& f) {
   }
 }
 
+// The kernels read these operands 16 bytes at a time (vector loads, bulk copies): a caller's pointer must start on a
+// 16-byte boundary, checked here so that a bad pointer is an error, not a GPU fault.
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+void require_attn_alignment(const xtg_cuda_attn_args* p) {
+  XTG_REQUIRE(aligned16(p->q) && aligned16(p->k_codes) && aligned16(p->v_codes) && aligned16(p->k_scales) &&
+                  aligned16(p->v_scales) && (p->ring == 0 || aligned16(p->ring_pos)),
+              "attention: q, the cache codes and scales and the ring table must start on 16-byte boundaries");
+}
+
 }  // namespace
 
 extern "C" {
@@ -113,6 +123,7 @@ int xtg_cuda_linear_forward(xtg_cuda_linear* L, const float* x, int m, float* co
                             int err_len) {
   return guarded(err, err_len, [&] {
     XTG_REQUIRE(m >= 1 && m <= kMaxGemmRows, "linear: 1..65536 rows");
+    XTG_REQUIRE(aligned16(x), "linear: x must start on a 16-byte boundary");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     for (int i = 0; i < L->nw; ++i) {
       const int t0 = L->tile0[i], nt = packed_tiles(L->n_out[i], false);
@@ -181,6 +192,7 @@ int xtg_cuda_quantize_nvfp4(const uint16_t* w_bf16, int n_out, int k, uint8_t* c
 int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, char* err, int err_len) {
   return guarded(err, err_len, [&] {
     XTG_REQUIRE(p->head_dim == 128, "attention: head_dim 128");
+    require_attn_alignment(p);
     XTG_REQUIRE(p->n_q >= 1 && p->n_q <= kMaxRows, "attention: 1..8 query rows");
     XTG_REQUIRE(splits >= 1, "attention: at least one split");
     XTG_REQUIRE(p->ring == 0 || p->ring_pos != nullptr, "attention: a ring needs its slot -> position table");
@@ -278,6 +290,7 @@ extern "C" {
 int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* p, int splits, void* stream, char* err, int err_len) {
   return guarded(err, err_len, [&] {
     XTG_REQUIRE(p->head_dim == 128, "attention: head_dim 128");
+    require_attn_alignment(p);
     XTG_REQUIRE(p->n_q >= 1 && p->n_q <= kMaxRows, "attention: 1..8 query rows");
     XTG_REQUIRE(splits >= 1, "attention: at least one split");
     XTG_REQUIRE(p->ring == 0 || p->ring_pos != nullptr, "attention: a ring needs its slot -> position table");

@@ -69,8 +69,8 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t* w
 }
 
 __global__ void __cluster_dims__(kTkCtas, 1, 1) __launch_bounds__(kTkThreads, 1)
-    topk_kernel(const float* __restrict__ logits, int vocab, int k, float inv_t, int32_t* out_idx, float* out_val,
-                float* out_max, double* out_total) {
+    topk_kernel(const float* __restrict__ logits, int vocab, int k, float inv_t, int vec4, int32_t* out_idx,
+                float* out_val, float* out_max, double* out_total) {
   cg::cluster_group cl = cg::this_cluster();
   const int crank = (int)cl.block_rank();
   const int row = blockIdx.y;
@@ -89,7 +89,7 @@ __global__ void __cluster_dims__(kTkCtas, 1, 1) __launch_bounds__(kTkThreads, 1)
   const float* src = logits + (int64_t)row * vocab;
   uint32_t key[kTkPer];
   float mx = -INFINITY;
-  if (e0 + kTkPer <= vocab && (vocab & 3) == 0) {
+  if (vec4 && e0 + kTkPer <= vocab) {   // vec4: 16-byte aligned rows
 #pragma unroll
     for (int q = 0; q < kTkPer / 4; ++q) {
       const float4 v = *reinterpret_cast<const float4*>(src + e0 + 4 * q);
@@ -257,7 +257,9 @@ void launch_topk(const float* logits, int rows, int vocab, int k, float temperat
   XTG_REQUIRE(vocab >= 1 && vocab <= kTkCtas * kTkThreads * kTkPer, "topk: 1..131072 entries per row");
   XTG_REQUIRE(k >= 1 && k <= kMaxTopK && k <= vocab, "topk: k in 1..min(1024, vocab)");
   const float inv_t = temperature > 0.f ? 1.f / temperature : 1.f;
-  topk_kernel<<<dim3(kTkCtas, rows), kTkThreads, 0, s>>>(logits, vocab, k, inv_t, idx, val, row_max, total);
+  // 16-byte loads only where every row starts on a 16-byte boundary (a caller's pointer may sit anywhere)
+  const int vec4 = (reinterpret_cast<uintptr_t>(logits) & 15) == 0 && (vocab & 3) == 0;
+  topk_kernel<<<dim3(kTkCtas, rows), kTkThreads, 0, s>>>(logits, vocab, k, inv_t, vec4, idx, val, row_max, total);
   XTG_CUDA(cudaGetLastError());
 }
 
