@@ -497,6 +497,35 @@ def topk_block(x, device, vocab, reps=20):
     return out
 
 
+def shared_sessions_block(x, s, dist, steps, sessions=4):
+    """Config 4's layout on each GPU: `sessions` independent sequences over one weight set (the first is the bench's
+    session, the others opened with xtg_cuda_open_shared, each at 8184 positions), each stepping in its own thread on
+    its own stream and graph. Rows per second by wall clock around all of them (max over ranks)."""
+    import threading
+    others = [x.Session.shared(s, context=8192) for _ in range(sessions - 1)]
+    try:
+        every = [s] + others
+        for o in others:
+            o.prefill_synthetic(PREFILL)
+        for o in every:
+            o.bench(TOKENS, 3)
+        dist_barrier(dist)
+        th = [threading.Thread(target=o.bench, args=(TOKENS, steps)) for o in every]
+        t0 = time.perf_counter()
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        wall = time.perf_counter() - t0
+        dist_barrier(dist)
+        wall = max_over_ranks(wall, dist)
+    finally:
+        for o in others:
+            o.close()
+    return {"sessions_per_gpu": sessions, "steps_each": steps, "wall_s": wall,
+            "rows_per_s_per_gpu": sessions * 8 * steps / wall}
+
+
 def job_rows_per_s(world, ms_per_step):
     """Whole-job throughput: every rank verifies 8 rows of its own sequence per step (weak scaling)."""
     return world * 8.0 / (ms_per_step / 1e3)
@@ -556,6 +585,7 @@ def run_ours(args, rank, world, local_rank, dist):
     achieved = gemv_bytes / (cms[0] / 1e3) / 1e9
     traffic = ncu_traffic()
     info = s.info()
+    shared = shared_sessions_block(x, s, dist, args.steps)
     s.close()
     topk_t = topk_block(x, f"cuda:{local_rank}", model["vocab"]) if world == 1 else None
     gemm = gemm_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
@@ -590,6 +620,10 @@ def run_ours(args, rank, world, local_rank, dist):
                         "graph": info.get("graph"), "pdl": info.get("pdl")}}
     if topk_t:
         line["topk"] = topk_t
+    line["config4_shared_sessions"] = {
+        "config": "4 independent sequences per GPU over one weight set (xtg_cuda_open_shared), 8K tier, each "
+                  "stepping concurrently on its own stream; wall clock", **shared,
+        "job_rows_per_s": world * shared["rows_per_s_per_gpu"], "vs_one_session": shared["rows_per_s_per_gpu"] / (value / world)}
     if cfg0:
         line["config0_gemv"] = {"config": "config0: one NVFP4 GEMV, M = 1, 16 weight copies rotated", **cfg0}
     if cfg2:

@@ -37,6 +37,15 @@ typedef void (*xtg_cuda_logits_fn)(int row, const float* logits, void* user);
 // launches, default 1). NULL on failure, the reason in err.
 XTG_CUDA_API xtg_cuda* xtg_cuda_open(const char* model_path, const char* options, char* err, int err_len);
 
+// No counterpart in xtg_npu.h, whose ABI is one session per handle: many sequences per device over one weight set.
+// Open another session over `owner`'s weights on owner's device: its own KV instances, ring table,
+// snapshots, activations, stream and step graph; the packed weights are shared, not copied (3.4 GB for the
+// Dory-3072 shape). options as for xtg_cuda_open, except that "model" and "device" are the owner's and kv_world
+// must be 1. The weights live until the last session over them is closed, whichever is closed first. Sessions are
+// independent: each is used by one thread at a time, and several stepping at once from different threads run
+// concurrently on the GPU. NULL on failure, the reason in err.
+XTG_CUDA_API xtg_cuda* xtg_cuda_open_shared(xtg_cuda* owner, const char* options, char* err, int err_len);
+
 // {"vocab", "context", "max_position", "prefill_ar", "decode_ar", "kv_instances", "ring_instances", "ring_slots",
 //  "sliding_window", "kv_bytes", "snapshots", "kvmap", ...} as JSON; the length or -1 (xtg_npu.h:24-26).
 XTG_CUDA_API int xtg_cuda_info(xtg_cuda* h, char* out, int out_len);

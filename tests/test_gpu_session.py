@@ -190,3 +190,43 @@ def test_topk_and_sampling_from_the_step(cuda, xtg, cfg):
         assert decided > 0
         with pytest.raises(xtg.XtgError):
             s.topk(0)
+
+
+def test_sessions_over_shared_weights(cuda, xtg, cfg):
+    """xtg_cuda_open_shared: sessions over one weight set (one shared from another, with its own tier) stepping at
+    the same time from their own threads give the logits of an independent session bit for bit, and keep the
+    weights after the owner is closed."""
+    import threading
+    steps = [[5, 17, 900, 3, 44, 1023, 0, 256], [9, 10]]
+    with xtg.Session(cfg, context=256) as ref:
+        ref.prefill_synthetic(70)
+        want = [logits_of(ref.forward(t, want=2), len(t)) for t in steps]
+    a = xtg.Session(cfg, context=256)
+    b = xtg.Session.shared(a, context=256)
+    c = xtg.Session.shared(b, context=512)
+    try:
+        assert b.info()["weight_bytes"] == c.info()["weight_bytes"] == a.info()["weight_bytes"]
+        assert c.info()["context"] == 512
+        for s in (a, b, c):
+            s.prefill_synthetic(70)
+        got = {}
+
+        def run(name, s):
+            got[name] = logits_of(s.forward(steps[0], want=2), 8)
+
+        th = [threading.Thread(target=run, args=(n, s)) for n, s in (("a", a), ("b", b), ("c", c))]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        for n in "abc":
+            np.testing.assert_array_equal(got[n], want[0], err_msg=n)
+        a.close()   # the owner goes first: b and c still hold the weights
+        for s in (b, c):
+            np.testing.assert_array_equal(logits_of(s.forward(steps[1], want=2), 2), want[1])
+    finally:
+        for s in (a, b, c):
+            s.close()
+    with pytest.raises(xtg.XtgError):
+        with xtg.Session(cfg, context=256) as o:
+            xtg.Session.shared(o, context=256, kv_world=2, kv_rank=0, nccl_id="00" * 128)

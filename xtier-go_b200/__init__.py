@@ -53,6 +53,8 @@ def lib():
         E = C.c_char_p
         L.xtg_cuda_open.restype = C.c_void_p
         L.xtg_cuda_open.argtypes = [C.c_char_p, C.c_char_p, E, C.c_int]
+        L.xtg_cuda_open_shared.restype = C.c_void_p
+        L.xtg_cuda_open_shared.argtypes = [C.c_void_p, C.c_char_p, E, C.c_int]
         L.xtg_cuda_info.restype = C.c_int
         L.xtg_cuda_info.argtypes = [C.c_void_p, C.c_char_p, C.c_int]
         L.xtg_cuda_forward.restype = C.c_int
@@ -173,6 +175,21 @@ class Session:
         self.h = lib().xtg_cuda_open(b"synthetic", json.dumps(opts).encode(), err, len(err))
         if not self.h:
             raise XtgError(err.value.decode(errors="replace"))
+
+    @classmethod
+    def shared(cls, owner, context=8192, kv_dtype="int8", snapshots=2, decode_rows=8, graph=True, pdl=True, **extra):
+        """xtg_cuda_open_shared: another session over owner's weights (its own caches, stream and graph)."""
+        self = cls.__new__(cls)
+        opts = dict(context=context, kv_dtype=kv_dtype, snapshots=snapshots, decode_rows=decode_rows,
+                    graph=int(graph), pdl=int(pdl))
+        opts.update(extra)
+        self.options = dict(owner.options, **opts)
+        self.model = owner.model
+        err = _err()
+        self.h = lib().xtg_cuda_open_shared(owner.h, json.dumps(opts).encode(), err, len(err))
+        if not self.h:
+            raise XtgError(err.value.decode(errors="replace"))
+        return self
 
     def close(self):
         if getattr(self, "h", None):

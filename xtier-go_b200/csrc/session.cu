@@ -177,7 +177,8 @@ struct Linear {
 
 struct Eval {
   int kind = 0;
-  Linear qkvg, o, gu, down;
+  Linear qkvg, o, gu, down;   // o.g0 / down.g0: their global scales; gq: those of q, k, v, g
+  float gq[4] = {1.f, 1.f, 1.f, 1.f};
   float *lr = nullptr, *qscale = nullptr, *gscale = nullptr, *sg = nullptr, *su = nullptr;
   int theta = 0;   // 0 sliding, 1 global
   int cache = -1;
@@ -209,6 +210,15 @@ struct xtg_cuda {
   cudaStream_t stream = nullptr;
   int num_sms = 148;
   std::vector<void*> allocs;   // freed at close
+  // the model's weights (packed arena, per-layer vectors, RoPE frequencies): shared by the sessions opened from this
+  // one with xtg_cuda_open_shared, freed with the last of them
+  struct DeviceBlocks {
+    std::vector<void*> p;
+    ~DeviceBlocks() {
+      for (void* q : p) cudaFree(q);
+    }
+  };
+  std::shared_ptr<DeviceBlocks> wmem = std::make_shared<DeviceBlocks>();
   // model
   uint8_t* arena = nullptr;
   int64_t arena_bytes = 0;
@@ -258,6 +268,14 @@ struct xtg_cuda {
   // profiling
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>>* prof = nullptr;
   std::vector<int>* prof_cls = nullptr;
+
+  template <class T>
+  T* walloc(size_t n) {
+    void* p = nullptr;
+    XTG_CUDA(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    wmem->p.push_back(p);
+    return static_cast<T*>(p);
+  }
 
   template <class T>
   T* dalloc(size_t n, bool zero = true) {
@@ -356,7 +374,7 @@ struct xtg_cuda {
                  kPackUnitBytes;
       }
     arena_bytes = total;
-    arena = dalloc<uint8_t>((size_t)total, false);
+    arena = walloc<uint8_t>((size_t)total);
     // temporaries: the largest weight (the head) in bf16, ModelOpt codes / scales for two weights
     const int64_t max_elems = std::max<int64_t>((int64_t)c.vocab * H, (int64_t)F * H);
     uint16_t* raw = nullptr;
@@ -379,7 +397,7 @@ struct xtg_cuda {
       return g;
     };
     auto vec = [&](uint64_t stream_id, float lo, float hi, int n) {
-      float* v = dalloc<float>(n, false);
+      float* v = walloc<float>(n);
       gen_uniform(c.seed, stream_id, lo, hi, v, n, stream);
       return v;
     };
@@ -392,11 +410,6 @@ struct xtg_cuda {
       L.bytes = (int64_t)tiles * kblocks * kPackUnitBytes;
       L.plan = plan_gemv(tiles, kblocks, num_sms, max_split, max_tpc);
       cursor += L.bytes;
-    };
-    auto tile_outs = [&](float* y, int ld, int n, float g) {
-      std::vector<TileOut> v(packed_tiles(n, false));
-      for (int t = 0; t < (int)v.size(); ++t) v[t] = TileOut{y + 128 * t, ld, std::min(128, n - 128 * t), g, g};
-      return v;
     };
     auto alg = [](int n, int k) { return (int64_t)n * k / 2 + (int64_t)n * k / 16 + 4; };
     proj_ld = 2 * Q + 2 * KV;
@@ -423,7 +436,7 @@ struct xtg_cuda {
         E.down.alg_bytes = alg(H, F);
         E.down.n_total = H;
         E.down.k = F;
-        E.down.outs = upload(tile_outs(o, H, H, gd));
+        E.down.g0 = gd;
       } else {
         E.qscale = vec(base + 9, c.qs_lo, c.qs_hi, Q);
         E.gscale = vec(base + 10, c.gs_lo, c.gs_hi, Q);
@@ -431,20 +444,15 @@ struct xtg_cuda {
         E.cache = n_attn++;
         const int tq = packed_tiles(Q, false), tk = packed_tiles(KV, false), kblocks = packed_kblocks(H);
         place(E.qkvg, 2 * tq + 2 * tk, kblocks);
-        std::vector<TileOut> outs;
         const int n_out[4] = {Q, KV, KV, Q};
-        const int col[4] = {0, Q, Q + KV, Q + 2 * KV};
         int tile0 = 0;
         for (int j = 0; j < 4; ++j) {
-          const float gj = make(base + j, n_out[j], H, codes_a, scales_a);
+          E.gq[j] = make(base + j, n_out[j], H, codes_a, scales_a);
           pack_nvfp4(codes_a, scales_a, nullptr, nullptr, n_out[j], H, false,
                      E.qkvg.w + (int64_t)tile0 * kblocks * kPackUnitBytes, stream);
-          const int tj = packed_tiles(n_out[j], false);
-          for (const TileOut& t : tile_outs(proj + col[j], proj_ld, n_out[j], gj)) outs.push_back(t);
-          tile0 += tj;
+          tile0 += packed_tiles(n_out[j], false);
           E.qkvg.alg_bytes += alg(n_out[j], H);
         }
-        E.qkvg.outs = upload(outs);
         E.qkvg.n_total = 2 * Q + 2 * KV;
         E.qkvg.k = H;
         place(E.o, packed_tiles(H, false), packed_kblocks(Q));
@@ -453,7 +461,7 @@ struct xtg_cuda {
         E.o.alg_bytes = alg(H, Q);
         E.o.n_total = H;
         E.o.k = Q;
-        E.o.outs = upload(tile_outs(o, H, H, go));
+        E.o.g0 = go;
       }
     }
     place(head, packed_tiles(c.vocab, false), packed_kblocks(H), 1);
@@ -469,8 +477,10 @@ struct xtg_cuda {
     const float th[2] = {c.theta_sliding, c.theta_global};
     for (int t = 0; t < 2; ++t)
       for (int i = 0; i < 64; ++i) inv[t * 64 + i] = 1.f / std::pow(th[t], float(2 * i) / float(c.head_dim));
-    inv_freq = upload(inv);
+    inv_freq = walloc<float>(inv.size());
+    XTG_CUDA(cudaMemcpyAsync(inv_freq, inv.data(), inv.size() * sizeof(float), cudaMemcpyHostToDevice, stream));
     XTG_CUDA(cudaStreamSynchronize(stream));
+    make_outs();
     cudaFree(raw);
     cudaFree(codes_a);
     cudaFree(scales_a);
@@ -478,6 +488,44 @@ struct xtg_cuda {
     cudaFree(scales_b);
     cudaFree(gdev);
     cudaFree(amax);
+  }
+
+  // this session's output descriptors of the STORE / q|k|v GEMVs (they point into its own activation buffers)
+  static std::vector<TileOut> tile_outs(float* y, int ld, int n, float g) {
+    std::vector<TileOut> v(packed_tiles(n, false));
+    for (int t = 0; t < (int)v.size(); ++t) v[t] = TileOut{y + 128 * t, ld, std::min(128, n - 128 * t), g, g};
+    return v;
+  }
+
+  void make_outs() {
+    const int H = c.hidden, Q = c.heads * c.head_dim, KV = c.kv_heads * c.head_dim;
+    for (Eval& E : evals) {
+      if (E.kind == 0) {
+        E.down.outs = upload(tile_outs(o, H, H, E.down.g0));
+        continue;
+      }
+      std::vector<TileOut> outs;
+      const int n_out[4] = {Q, KV, KV, Q};
+      const int col[4] = {0, Q, Q + KV, Q + 2 * KV};
+      for (int j = 0; j < 4; ++j)
+        for (const TileOut& t : tile_outs(proj + col[j], proj_ld, n_out[j], E.gq[j])) outs.push_back(t);
+      E.qkvg.outs = upload(outs);
+      E.o.outs = upload(tile_outs(o, H, H, E.o.g0));
+    }
+  }
+
+  // A session over another's weights (xtg_cuda_open_shared): the model's device blocks are shared, the output
+  // descriptors are this session's own.
+  void share_model(const xtg_cuda& m) {
+    wmem = m.wmem;
+    arena = m.arena;
+    arena_bytes = m.arena_bytes;
+    evals = m.evals;
+    head = m.head;
+    logit_scale = m.logit_scale;
+    inv_freq = m.inv_freq;
+    proj_ld = m.proj_ld;
+    make_outs();
   }
 
   template <class T>
@@ -1051,6 +1099,40 @@ xtg_cuda* xtg_cuda_open(const char* model_path, const char* options, char* err, 
       nccl_check(nccl_api().comm_init_rank(&h->comm, h->c.kv_world, id, h->c.kv_rank), "ncclCommInitRank");
       if (h->c.kv_exchange == "peer") h->open_peer_exchange();
     }
+  } catch (const std::exception& e) {
+    set_err(err, err_len, e.what());
+    return nullptr;
+  }
+  return h.release();
+}
+
+xtg_cuda* xtg_cuda_open_shared(xtg_cuda* owner, const char* options, char* err, int err_len) {
+  std::unique_ptr<xtg_cuda> h;
+  try {
+    XTG_REQUIRE(owner, "open_shared: no session to share weights with");
+    const Config o = parse_config(options ? options : "");
+    XTG_REQUIRE(o.kv_world == 1, "open_shared: a shared session runs in one process (kv_world 1)");
+    h = std::make_unique<xtg_cuda>();
+    // the owner's model and device; this session's own tier, KV format, snapshots, rows, graph and splits
+    h->c = owner->c;
+    h->c.context = o.context;
+    h->c.kv_dtype = o.kv_dtype;
+    h->c.snapshots = o.snapshots;
+    h->c.decode_rows = o.decode_rows;
+    h->c.graph = o.graph;
+    h->c.pdl = o.pdl;
+    h->c.splits_global = o.splits_global;
+    h->c.splits_ring = o.splits_ring;
+    h->c.kv_world = 1;
+    h->c.kv_rank = 0;
+    h->c.nccl_id.clear();
+    XTG_CUDA(cudaSetDevice(h->c.device));
+    h->num_sms = owner->num_sms;
+    XTG_CUDA(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+    h->alloc_activations();
+    h->share_model(*owner);
+    h->alloc_caches();
+    XTG_CUDA(cudaStreamSynchronize(h->stream));
   } catch (const std::exception& e) {
     set_err(err, err_len, e.what());
     return nullptr;
