@@ -631,7 +631,7 @@ def run_ours(args, rank, world, local_rank, dist):
                                      **cfg2}
     if skv:
         line["batch1_split_kv"] = {"config": "batch-1 verify step (8 rows) at 32K context, the global caches' chunks "
-                                             "split over the GPUs, partials exchanged over NVLink by the attention "
+                                             "split over the GPUs, partials exchanged over NVLink inside the combine "
                                              "kernel (split_kv) or by ncclAllGather (split_kv_nccl)", **skv}
     if gemm:
         tot_flops = sum(2.0 * 512 * v["n"] * v["k"] for v in gemm.values())
