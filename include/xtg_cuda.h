@@ -56,6 +56,17 @@ XTG_CUDA_API int xtg_cuda_info(xtg_cuda* h, char* out, int out_len);
 XTG_CUDA_API int xtg_cuda_forward(xtg_cuda* h, const int32_t* tokens, int n, int want, xtg_cuda_logits_fn fn, void* user,
                      char* err, int err_len);
 
+// No counterpart in xtg_npu.h: xtg_cuda_forward for nh sessions at once from one thread (a server's single engine
+// thread). Session i runs n[i] tokens from tokens[i]. Each round enqueues every session's next step (up to its
+// decode_rows tokens) on that session's own stream before waiting for any of them, so the steps run concurrently on
+// the GPU; then each session commits its step and the callback gets its rows, session by session, numbered across
+// the call: session i's row j is base_i + j, base_i = n[0] + ... + n[i-1]. want as for xtg_cuda_forward. Every
+// token and context check is made before the first step (a refused call changes nothing); a session may appear
+// once. If a device wait times out in a session's step, that step is discarded, the round's other steps are
+// committed and the call returns -1 after the round. 0 on success.
+XTG_CUDA_API int xtg_cuda_forward_batch(xtg_cuda* const* hs, int nh, const int32_t* const* tokens, const int* n,
+                                       int want, xtg_cuda_logits_fn fn, void* user, char* err, int err_len);
+
 XTG_CUDA_API int64_t xtg_cuda_pos(xtg_cuda* h);   // xtg_npu.h:30
 
 // Back to n positions (n <= pos()). Global caches keep every position; the rings must still hold the window before

@@ -230,3 +230,35 @@ def test_sessions_over_shared_weights(cuda, xtg, cfg):
     with pytest.raises(xtg.XtgError):
         with xtg.Session(cfg, context=256) as o:
             xtg.Session.shared(o, context=256, kv_world=2, kv_rank=0, nccl_id="00" * 128)
+
+
+def test_forward_batch_matches_one_by_one(cuda, xtg, cfg):
+    """xtg_cuda_forward_batch over sessions with different token counts (one of them two steps, one none) gives
+    each session's logits of a forward of its own, bit for bit, and advances each position; a refused call (a
+    session twice, a token out of range) changes nothing."""
+    lists = [[5, 17, 900, 3, 44, 1023, 0, 256], [8, 9, 10], list(range(100, 111)), []]
+    with xtg.Session(cfg, context=256) as owner:
+        owner.prefill_synthetic(70)
+        singles = [xtg.Session.shared(owner, context=256) for _ in lists]
+        batch = [xtg.Session.shared(owner, context=256) for _ in lists]
+        try:
+            want = []
+            for s, t in zip(singles, lists):
+                s.prefill_synthetic(70)
+                want.append(s.forward(t, want=2) if t else {})
+            for s in batch:
+                s.prefill_synthetic(70)
+            with pytest.raises(xtg.XtgError):
+                xtg.forward_batch([batch[0], batch[0]], [lists[0], lists[1]])
+            with pytest.raises(xtg.XtgError):
+                xtg.forward_batch(batch[:2], [lists[0], [cfg["vocab"]]])
+            assert [s.pos() for s in batch] == [70] * len(batch)
+            got = xtg.forward_batch(batch, lists, want=2)
+            for i, t in enumerate(lists):
+                assert sorted(got[i]) == sorted(want[i]) == list(range(len(t)))
+                for r in want[i]:
+                    np.testing.assert_array_equal(got[i][r], want[i][r], err_msg=f"session {i} row {r}")
+                assert batch[i].pos() == 70 + len(t)
+        finally:
+            for s in singles + batch:
+                s.close()

@@ -60,6 +60,9 @@ def lib():
         L.xtg_cuda_forward.restype = C.c_int
         L.xtg_cuda_forward.argtypes = [C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_int, LOGITS_FN, C.c_void_p,
                                        E, C.c_int]
+        L.xtg_cuda_forward_batch.restype = C.c_int
+        L.xtg_cuda_forward_batch.argtypes = [C.POINTER(C.c_void_p), C.c_int, C.POINTER(C.POINTER(C.c_int32)),
+                                             C.POINTER(C.c_int), C.c_int, LOGITS_FN, C.c_void_p, E, C.c_int]
         L.xtg_cuda_pos.restype = C.c_int64
         L.xtg_cuda_pos.argtypes = [C.c_void_p]
         L.xtg_cuda_rewind.restype = C.c_int
@@ -317,6 +320,31 @@ class Session:
 # ----------------------------------------------------------------------------------------------------------------
 # Kernel level (torch CUDA tensors as device memory)
 # ----------------------------------------------------------------------------------------------------------------
+
+def forward_batch(sessions, token_lists, want=2):
+    """xtg_cuda_forward_batch: every session's steps in flight together from this thread; returns one
+    {row: logits} dict per session (rows numbered within each session)."""
+    import numpy as np
+    nh = len(sessions)
+    hs = (C.c_void_p * nh)(*[s.h for s in sessions])
+    arrs = [(C.c_int32 * max(1, len(t)))(*[int(v) for v in t]) for t in token_lists]
+    toks = (C.POINTER(C.c_int32) * nh)(*[C.cast(a, C.POINTER(C.c_int32)) for a in arrs])
+    ns = (C.c_int * nh)(*[len(t) for t in token_lists])
+    base = np.cumsum([0] + [len(t) for t in token_lists])
+    vocab = sessions[0].model["vocab"] if nh else 0
+    out = [dict() for _ in range(nh)]
+
+    def cb(row, ptr, user):
+        i = int(np.searchsorted(base, row, side="right")) - 1
+        dst = np.empty(vocab, np.float32)
+        C.memmove(dst.ctypes.data, ptr, vocab * 4)
+        out[i][row - int(base[i])] = dst
+
+    fn = LOGITS_FN(cb)
+    err = _err()
+    _check(lib().xtg_cuda_forward_batch(hs, nh, toks, ns, want, fn, None, err, len(err)), err)
+    return out
+
 
 def _ptr(t):
     return C.c_void_p(t.data_ptr())

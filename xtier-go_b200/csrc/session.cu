@@ -896,35 +896,61 @@ struct xtg_cuda {
     n_past += m;
   }
 
-  void forward(const int32_t* tokens, int n, int want, xtg_cuda_logits_fn fn, void* user) {
-    if (n <= 0) return;
+  // forward() in three parts, so that several sessions' steps can be in flight at once (xtg_cuda_forward_batch):
+  // check the call (nothing changes on failure), enqueue one step of up to decode_rows tokens without waiting, then
+  // wait for it, commit it and hand its logits out.
+  void check_tokens(const int32_t* tokens, int n) const {
     for (int i = 0; i < n; ++i)
       if (tokens[i] < 0 || tokens[i] >= c.vocab)
         throw CudaError("token " + std::to_string(tokens[i]) + " out of range");
     if (n_past + n > c.context)
       throw CudaError("context full: " + std::to_string(n_past) + " + " + std::to_string(n) + " tokens (" +
                       std::to_string(c.context) + ")");
+  }
+
+  void drop_snapshots_past() {
     for (Snap& s : snaps)   // a snapshot past this point no longer matches what the caches will hold
       if (s.pos > n_past) s.pos = -1;
+  }
+
+  struct Chunk {
+    int off, m, r0;
+  };
+
+  Chunk enqueue_chunk(const int32_t* tokens, int n, int off, int want, bool copy) {
+    const int m = std::min(c.decode_rows, n - off);
+    set_params(tokens + off, m);
+    launch_step();
+    const int r0 = want == 2 ? 0 : (want == 1 && off + m == n ? m - 1 : m);
+    if (r0 < m && copy)
+      XTG_CUDA(cudaMemcpyAsync(logits_host + (size_t)r0 * c.vocab, logits + (size_t)r0 * c.vocab,
+                               (size_t)(m - r0) * c.vocab * sizeof(float), cudaMemcpyDeviceToHost, stream));
+    XTG_CUDA(cudaMemcpyAsync(err_host, dev_err, sizeof(int), cudaMemcpyDeviceToHost, stream));
+    return Chunk{off, m, r0};
+  }
+
+  // false: a bounded device wait gave up, the step's results are not to be trusted (not committed)
+  bool finish_chunk(const Chunk& k, xtg_cuda_logits_fn fn, void* user, int row_base) {
+    XTG_CUDA(cudaStreamSynchronize(stream));
+    if (*err_host) {
+      *err_host = 0;
+      XTG_CUDA(cudaMemsetAsync(dev_err, 0, sizeof(int), stream));
+      return false;
+    }
+    commit(k.m);
+    last_rows = k.m;
+    if (fn)
+      for (int i = k.r0; i < k.m; ++i) fn(row_base + k.off + i, logits_host + (size_t)i * c.vocab, user);
+    return true;
+  }
+
+  void forward(const int32_t* tokens, int n, int want, xtg_cuda_logits_fn fn, void* user) {
+    if (n <= 0) return;
+    check_tokens(tokens, n);
+    drop_snapshots_past();
     for (int off = 0; off < n; off += c.decode_rows) {
-      const int m = std::min(c.decode_rows, n - off);
-      set_params(tokens + off, m);
-      launch_step();
-      const int r0 = want == 2 ? 0 : (want == 1 && off + m == n ? m - 1 : m);
-      if (r0 < m && fn)
-        XTG_CUDA(cudaMemcpyAsync(logits_host + (size_t)r0 * c.vocab, logits + (size_t)r0 * c.vocab,
-                                 (size_t)(m - r0) * c.vocab * sizeof(float), cudaMemcpyDeviceToHost, stream));
-      XTG_CUDA(cudaMemcpyAsync(err_host, dev_err, sizeof(int), cudaMemcpyDeviceToHost, stream));
-      XTG_CUDA(cudaStreamSynchronize(stream));
-      if (*err_host) {   // a bounded device wait gave up: the step's results are not to be trusted
-        *err_host = 0;
-        XTG_CUDA(cudaMemsetAsync(dev_err, 0, sizeof(int), stream));
-        throw CudaError("a device wait timed out during the step (results discarded)");
-      }
-      commit(m);
-      last_rows = m;
-      if (fn)
-        for (int i = r0; i < m; ++i) fn(off + i, logits_host + (size_t)i * c.vocab, user);
+      const Chunk k = enqueue_chunk(tokens, n, off, want, fn != nullptr);
+      if (!finish_chunk(k, fn, user, 0)) throw CudaError("a device wait timed out during the step (results discarded)");
     }
   }
 
@@ -1163,6 +1189,44 @@ int xtg_cuda_forward(xtg_cuda* h, const int32_t* tokens, int n, int want, xtg_cu
   return guarded(err, err_len, [&] {
     XTG_CUDA(cudaSetDevice(h->c.device));
     h->forward(tokens, n, want, fn, user);
+  });
+}
+
+int xtg_cuda_forward_batch(xtg_cuda* const* hs, int nh, const int32_t* const* tokens, const int* n, int want,
+                           xtg_cuda_logits_fn fn, void* user, char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_REQUIRE(nh >= 0 && (nh == 0 || (hs && tokens && n)), "forward_batch: null arrays");
+    std::vector<int> base((size_t)nh + 1, 0);
+    for (int i = 0; i < nh; ++i) {   // every check before any step: a refused call changes nothing
+      XTG_REQUIRE(hs[i], "forward_batch: null session");
+      XTG_REQUIRE(n[i] >= 0, "forward_batch: negative token count");
+      for (int j = 0; j < i; ++j) XTG_REQUIRE(hs[j] != hs[i], "forward_batch: a session appears twice");
+      hs[i]->check_tokens(tokens[i], n[i]);
+      base[(size_t)i + 1] = base[(size_t)i] + n[i];
+    }
+    for (int i = 0; i < nh; ++i) hs[i]->drop_snapshots_past();
+    std::string failed;
+    std::vector<xtg_cuda::Chunk> ks((size_t)nh);
+    for (int step = 0;; ++step) {
+      bool any = false;
+      for (int i = 0; i < nh; ++i) {   // every session's next step goes out before the first wait
+        xtg_cuda* h = hs[i];
+        const int off = step * h->c.decode_rows;
+        ks[(size_t)i].m = 0;
+        if (off >= n[i]) continue;
+        XTG_CUDA(cudaSetDevice(h->c.device));
+        ks[(size_t)i] = h->enqueue_chunk(tokens[i], n[i], off, want, fn != nullptr);
+        any = true;
+      }
+      if (!any) break;
+      for (int i = 0; i < nh; ++i) {
+        if (ks[(size_t)i].m == 0) continue;
+        XTG_CUDA(cudaSetDevice(hs[i]->c.device));
+        if (!hs[i]->finish_chunk(ks[(size_t)i], fn, user, base[(size_t)i]) && failed.empty())
+          failed = "session " + std::to_string(i) + ": a device wait timed out during the step (results discarded)";
+      }
+      if (!failed.empty()) throw CudaError(failed);
+    }
   });
 }
 
