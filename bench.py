@@ -359,7 +359,7 @@ def kernel_times(prof):
 def config0_block(x, device, copies=16, reps=32):
     """one NVFP4 GEMV at M = 1 through the linear API, 9216 x 3072 and 3072 x 9216, 16 weight
     copies rotated (> L2). Device time of the GEMV kernel (the activation digitizer listed apart); algorithmic bytes
-    as SURVEY 8(d) counts them (codes + scales + global + x bf16 + y f32)."""
+    = NVFP4 codes + scales + global + x in bf16 + y in f32."""
     import torch
     from torch.profiler import profile, ProfilerActivity
     g = torch.Generator(device=device)
