@@ -519,45 +519,41 @@ def shared_sessions_block(x, s, dist, steps, sessions=4):
         wall = time.perf_counter() - t0
         dist_barrier(dist)
         wall = max_over_ranks(wall, dist)
-        # end to end from one thread (a server's engine thread): xtg_cuda_forward_batch with host tokens in and every
-        # row's logits out, then each session's rewind
-        lists = [TOKENS] * sessions
-        for _ in range(2):
-            x.forward_batch(every, lists, want=2)
-            for o in every:
-                o.rewind(PREFILL)
-        dist_barrier(dist)
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            x.forward_batch(every, lists, want=2)
-            for o in every:
-                o.rewind(PREFILL)
-        e2e = time.perf_counter() - t0
-        dist_barrier(dist)
-        e2e = max_over_ranks(e2e, dist)
-        # the same with the sampler's 64 candidates per row instead of whole rows (xtg_cuda_topk per session)
-        for _ in range(2):
-            x.forward_batch(every, lists, want=0)
-            for o in every:
-                o.topk(TOPK)
-                o.rewind(PREFILL)
-        dist_barrier(dist)
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            x.forward_batch(every, lists, want=0)
-            for o in every:
-                o.topk(TOPK)
-                o.rewind(PREFILL)
-        e2e_tk = time.perf_counter() - t0
-        dist_barrier(dist)
-        e2e_tk = max_over_ranks(e2e_tk, dist)
+        e2e = e2e_tk = None
+        if dist is None:   # one process: the end-to-end legs (measured on 1 GPU only)
+            # end to end from one thread (a server's engine thread): xtg_cuda_forward_batch with host tokens in and every
+            # row's logits out, then each session's rewind
+            lists = [TOKENS] * sessions
+            for _ in range(2):
+                x.forward_batch(every, lists, want=2)
+                for o in every:
+                    o.rewind(PREFILL)
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                x.forward_batch(every, lists, want=2)
+                for o in every:
+                    o.rewind(PREFILL)
+            e2e = time.perf_counter() - t0
+            # the same with the sampler's 64 candidates per row instead of whole rows (xtg_cuda_topk per session)
+            for _ in range(2):
+                x.forward_batch(every, lists, want=0)
+                for o in every:
+                    o.topk(TOPK)
+                    o.rewind(PREFILL)
+            t0 = time.perf_counter()
+            for _ in range(steps):
+                x.forward_batch(every, lists, want=0)
+                for o in every:
+                    o.topk(TOPK)
+                    o.rewind(PREFILL)
+            e2e_tk = time.perf_counter() - t0
     finally:
         for o in others:
             o.close()
     return {"sessions_per_gpu": sessions, "steps_each": steps, "wall_s": wall,
             "rows_per_s_per_gpu": sessions * 8 * steps / wall,
-            "e2e_forward_batch_rows_per_s_per_gpu": sessions * 8 * steps / e2e,
-            "e2e_forward_batch_topk_rows_per_s_per_gpu": sessions * 8 * steps / e2e_tk,
+            "e2e_forward_batch_rows_per_s_per_gpu": sessions * 8 * steps / e2e if e2e else None,
+            "e2e_forward_batch_topk_rows_per_s_per_gpu": sessions * 8 * steps / e2e_tk if e2e_tk else None,
             "e2e_d2h_bytes_per_round": sessions * 8 * 131072 * 4}
 
 
