@@ -63,7 +63,8 @@ XTG_CUDA_API int xtg_cuda_forward(xtg_cuda* h, const int32_t* tokens, int n, int
 // the call: session i's row j is base_i + j, base_i = n[0] + ... + n[i-1]. want as for xtg_cuda_forward. Every
 // token and context check is made before the first step (a refused call changes nothing); a session may appear
 // once. If a device wait times out in a session's step, that step is discarded, the round's other steps are
-// committed and the call returns -1 after the round. 0 on success.
+// committed and the call returns -1 after the round. A session given no tokens keeps its snapshots. The caller's
+// current CUDA device is the same after the call. 0 on success.
 XTG_CUDA_API int xtg_cuda_forward_batch(xtg_cuda* const* hs, int nh, const int32_t* const* tokens, const int* n,
                                        int want, xtg_cuda_logits_fn fn, void* user, char* err, int err_len);
 

@@ -61,3 +61,16 @@ def test_attention_rejects_unaligned_pointers_before_any_device_work(xtg, entry)
         err = C.create_string_buffer(512)
         rc = getattr(xtg.lib(), entry)(C.byref(a), 4, None, err, len(err))
         assert rc == -1 and b"16-byte" in err.value, (field, err.value)
+
+
+@pytest.mark.parametrize("entry", ["xtg_cuda_attention", "xtg_cuda_attention_noalloc"])
+@pytest.mark.parametrize("kv_heads", [0, -2])
+def test_attention_rejects_no_kv_heads_before_any_device_work(xtg, entry, kv_heads):
+    """q heads are grouped over the KV heads (heads % kv_heads): kv_heads < 1 is an error at the call, checked on the
+    host before any division or allocation (this runs without a GPU)."""
+    good = 4096
+    a = xtg.AttnArgs(8, 100, 24, kv_heads, 128, 0, 0.1, good, good, good, good, good, good, good, 128, 0, None, 0,
+                     good)
+    err = C.create_string_buffer(512)
+    rc = getattr(xtg.lib(), entry)(C.byref(a), 4, None, err, len(err))
+    assert rc == -1 and b"KV head" in err.value, err.value

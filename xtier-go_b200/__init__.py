@@ -331,11 +331,12 @@ def forward_batch(sessions, token_lists, want=2):
     toks = (C.POINTER(C.c_int32) * nh)(*[C.cast(a, C.POINTER(C.c_int32)) for a in arrs])
     ns = (C.c_int * nh)(*[len(t) for t in token_lists])
     base = np.cumsum([0] + [len(t) for t in token_lists])
-    vocab = sessions[0].model["vocab"] if nh else 0
+    vocabs = [s.model["vocab"] for s in sessions]   # the sessions may serve different models
     out = [dict() for _ in range(nh)]
 
     def cb(row, ptr, user):
         i = int(np.searchsorted(base, row, side="right")) - 1
+        vocab = vocabs[i]
         dst = np.empty(vocab, np.float32)
         C.memmove(dst.ctypes.data, ptr, vocab * 4)
         out[i][row - int(base[i])] = dst

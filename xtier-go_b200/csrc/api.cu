@@ -195,6 +195,7 @@ int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, ch
     require_attn_alignment(p);
     XTG_REQUIRE(p->n_q >= 1 && p->n_q <= kMaxRows, "attention: 1..8 query rows");
     XTG_REQUIRE(splits >= 1, "attention: at least one split");
+    XTG_REQUIRE(p->kv_heads >= 1 && p->heads >= 1, "attention: at least one q head and one KV head");
     XTG_REQUIRE(p->ring == 0 || p->ring_pos != nullptr, "attention: a ring needs its slot -> position table");
     XTG_REQUIRE(p->ring != 0 || p->pos0 <= p->slots, "attention: pos0 beyond the cache");
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -538,18 +538,15 @@ int64_t attention_part_floats(int kv_heads, int splits) { return (int64_t)kv_hea
 void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
   AttnArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
+  XTG_REQUIRE(a.kv_heads >= 1 && a.heads >= 1, "attention: at least one q head and one KV head");
   XTG_REQUIRE(a.heads % a.kv_heads == 0 && a.heads / a.kv_heads <= 4, "attention: at most 4 q heads per KV head");
   XTG_REQUIRE(a.slots % 64 == 0, "attention: cache slots must be a multiple of 64");
   XTG_REQUIRE(a.splits >= 1 && a.splits <= kMaxSplits, "attention: 1..256 splits");
   XTG_REQUIRE(a.splits_total == 0 || (a.split0 >= 0 && a.split0 + a.splits <= a.splits_total &&
                                        a.splits_total <= kMaxSplits),
               "attention: split range outside 0..splits_total (at most 256)");
-  static bool attr_set = false;
-  if (!attr_set) {
-    XTG_CUDA(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)sizeof(Smem)));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> optin{0};
+  ensure_smem_optin((const void*)attention_kernel, (int)sizeof(Smem), optin);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.splits, a.kv_heads);
   cfg.blockDim = dim3(kThreads);
@@ -567,6 +564,7 @@ void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
   CombineArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
   XTG_REQUIRE(a.splits >= 1 && a.splits <= kMaxSplits, "combine: 1..256 splits");
+  XTG_REQUIRE(a.kv_heads >= 1 && a.heads >= 1 && a.heads % a.kv_heads == 0, "combine: q heads a multiple of KV heads");
   XTG_REQUIRE(a.x.world <= 1 || (a.x.world <= kMaxKvWorld && a.x.rank >= 0 && a.x.rank < a.x.world && a.x.epoch &&
                                  a.err && a.out == nullptr),
               "combine: split-KV exchange needs 2..8 processes, the epoch and an error word (the step only)");

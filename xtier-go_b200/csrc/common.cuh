@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <cstdio>
 #include <stdexcept>
 #include <string>
@@ -29,6 +30,18 @@ struct CudaError : std::runtime_error {
   do {                                               \
     if (!(cond)) throw ::xtg::CudaError(std::string(msg)); \
   } while (0)
+
+// The opt-in to more than 48 KB of dynamic shared memory: cudaFuncSetAttribute applies to the current device only,
+// so each kernel keeps the set of devices (ordinals below 64) that already have it. Thread-safe: threads that race
+// both set the attribute, which is harmless; a device at 64 or above sets it on every launch.
+inline void ensure_smem_optin(const void* func, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  XTG_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return;
+  XTG_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  if (bit) done.fetch_or(bit, std::memory_order_acq_rel);
+}
 
 // ---- programmatic dependent launch: a kernel waits for its predecessor's results only where it reads them ----
 // Every kernel of the step lets its dependent launch only once its own wait is over: the next kernel's CTAs then

@@ -285,11 +285,8 @@ void launch_gemm(const uint8_t* w, int wtiles, int kblocks, const uint8_t* act, 
   P.outs = outs;
   P.err = err;
   const size_t smem = (size_t)kGStages * kGStageBytes + (2 * kGStages + 8) * 8;
-  static bool attr_set = false;
-  if (!attr_set) {
-    XTG_CUDA(cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> optin{0};
+  ensure_smem_optin((const void*)gemm_kernel, (int)smem, optin);
   const int ntiles = wtiles * P.atiles;
   gemm_kernel<<<std::min(ntiles, num_sms), kGThreads, smem, s>>>(P);
   XTG_CUDA(cudaGetLastError());

@@ -754,15 +754,12 @@ void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, 
   const int cols = tmem_columns(p.tiles_per_cta, P.slice_max, p.ring);
   XTG_REQUIRE(cols <= 512, "gemv: the K slice's scales do not fit in TMEM");
   P.tmem_cols = cols <= 256 ? 256 : 512;
-  static bool attr_set[4] = {false, false, false, false};
+  static std::atomic<uint64_t> optin[4];
   auto* k = epi == kEpiStore    ? gemv_kernel<kEpiStore>
             : epi == kEpiSwiglu ? gemv_kernel<kEpiSwiglu>
             : epi == kEpiQkv    ? gemv_kernel<kEpiQkv>
                                 : gemv_kernel<kEpiHead>;
-  if (!attr_set[epi]) {
-    XTG_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448));
-    attr_set[epi] = true;
-  }
+  ensure_smem_optin((const void*)k, 232448, optin[epi]);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
   cfg.blockDim = dim3(kThreads);

@@ -1194,17 +1194,29 @@ int xtg_cuda_forward(xtg_cuda* h, const int32_t* tokens, int n, int want, xtg_cu
 
 int xtg_cuda_forward_batch(xtg_cuda* const* hs, int nh, const int32_t* const* tokens, const int* n, int want,
                            xtg_cuda_logits_fn fn, void* user, char* err, int err_len) {
+  // the caller's current device is restored on every exit (the steps switch to each session's device)
+  int caller_device = -1;
+  cudaGetDevice(&caller_device);
+  struct RestoreDevice {
+    int d;
+    ~RestoreDevice() {
+      if (d >= 0) cudaSetDevice(d);
+    }
+  } restore_device{caller_device};
   return guarded(err, err_len, [&] {
     XTG_REQUIRE(nh >= 0 && (nh == 0 || (hs && tokens && n)), "forward_batch: null arrays");
     std::vector<int> base((size_t)nh + 1, 0);
     for (int i = 0; i < nh; ++i) {   // every check before any step: a refused call changes nothing
       XTG_REQUIRE(hs[i], "forward_batch: null session");
       XTG_REQUIRE(n[i] >= 0, "forward_batch: negative token count");
+      XTG_REQUIRE(n[i] == 0 || tokens[i], "forward_batch: null token list");
       for (int j = 0; j < i; ++j) XTG_REQUIRE(hs[j] != hs[i], "forward_batch: a session appears twice");
       hs[i]->check_tokens(tokens[i], n[i]);
       base[(size_t)i + 1] = base[(size_t)i] + n[i];
     }
-    for (int i = 0; i < nh; ++i) hs[i]->drop_snapshots_past();
+    // as forward() does: a session given no tokens keeps its snapshots
+    for (int i = 0; i < nh; ++i)
+      if (n[i] > 0) hs[i]->drop_snapshots_past();
     std::string failed;
     std::vector<xtg_cuda::Chunk> ks((size_t)nh);
     for (int step = 0;; ++step) {
