@@ -296,7 +296,8 @@ int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* p, int splits, void* st
     XTG_REQUIRE(splits >= 1, "attention: at least one split");
     XTG_REQUIRE(p->ring == 0 || p->ring_pos != nullptr, "attention: a ring needs its slot -> position table");
     XTG_REQUIRE(p->ring != 0 || p->pos0 <= p->slots, "attention: pos0 beyond the cache");
-    XTG_REQUIRE(p->kv_heads >= 1 && attention_part_floats(p->kv_heads, splits) <= kNoAllocFloats,
+    XTG_REQUIRE(p->kv_heads >= 1 && p->heads >= 1, "attention: at least one q head and one KV head");
+    XTG_REQUIRE(attention_part_floats(p->kv_heads, splits) <= kNoAllocFloats,
                 "attention_noalloc: kv_heads x splits above 256, the fixed scratch's limit (4,259,840 bytes)");
     float* part = noalloc_scratch();
     // every split writes the partial of every live query row that the combine reads: nothing needs clearing
