@@ -11,9 +11,8 @@ resident (CUDA events on the session's stream, max over ranks); `e2e` is the sam
 with host token buffers and every row's logits copied back (wall clock around the call).
 
 --impl reference times XTier Go's own CPU kernels (oracle/_ref/libxtgref.so, compiled from the reference sources)
-on the same config: a bounded sample per step (one global attention, one sliding attention and one MLP sublayer in
-DorySession::sublayer order with FP8 KvCaches, plus 1/16 of the head) scaled to the full step's 11 + 33 + 44
-sublayers and the whole head; all host cores.
+on the same config: whole steps (88 sublayers in DorySession order and the whole head) on all host cores, with the
+reference's FP8 KvCache and its 1040-slot rings (it has no int8 cache).
 """
 import argparse
 import ctypes as C
@@ -131,112 +130,134 @@ class Clocks:
 
 
 # ------------------------------------------------------------------------------------------------------------------
-# the reference's CPU implementation (oracle/_ref), a bounded sample of the step
+# the reference's CPU implementation (oracle/_ref): whole steps
 # ------------------------------------------------------------------------------------------------------------------
 
-def reference_sample(model, threads, reps, warmup):
-    """Seconds per full step estimated from the reference's kernels; returns (step_s, detail)."""
-    import numpy as np
-    import oracle as O
-    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
-    from make_golden import XrShape, XrSublayer  # the ctypes mirrors of ref_shim.cpp's structs
-    R = O.ref()
-    if R is None:
-        raise RuntimeError("oracle/_ref/libxtgref.so is not built")
-    f32p, u8p = O.f32p, O.u8p
-    R.xr_sublayer.argtypes = [C.c_void_p, C.POINTER(XrShape), C.POINTER(XrSublayer), f32p, C.c_int, C.c_int64,
-                              C.c_int, f32p]
-    R.xr_head.argtypes = [C.c_void_p, u8p, u8p, C.c_float, C.c_int, C.c_int, f32p, C.c_int, f32p, f32p]
-    H, F, heads, kvh, d = model["hidden"], model["ffn"], model["heads"], model["kv_heads"], model["head_dim"]
-    Q, KV = heads * d, kvh * d
-    seed = model["seed"]
-    keep = []
+class ReferenceStep:
+    """The config-3 verify step on XTier Go's own CPU kernels (oracle/_ref/libxtgref.so, compiled from the reference
+    sources), in DorySession::forward / run_chunk / sublayer order (packs/dory/dory.cpp:467-578): the tied head's
+    rows (nvfp4_row), 4 + 40 x 2 + 4 sublayers (matmul_nvfp4, rope, justnorm, attention, KvCache::store, swiglu_scaled,
+    slerp_residual) with the loop norms between them, then the NVFP4 head. Weights: the seeded synthetic Dory (the
+    oracle builds them; the reference kernels read the same NVFP4 bytes). Caches: the reference's FP8 KvCache (it has
+    no int8 one), a global cache per global sublayer holding 8184 positions and a ring of window + 16 = 1040 slots
+    (the reference's own ring size) per sliding sublayer holding its last 1040. Every step runs at the same position
+    (a verify step after a rewind)."""
 
-    def w(stream, n, k):
-        _, codes, scales, g = O.synth_weight(seed, stream, n, k, model["weight_std"])
-        keep.extend([codes, scales])
-        return codes, scales, g
+    def __init__(self, model, threads, prefill=PREFILL):
+        import numpy as np
+        import oracle as O
+        sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+        from make_golden import XrShape, XrSublayer  # the ctypes mirrors of ref_shim.cpp's structs
+        R = O.ref()
+        if R is None:
+            raise RuntimeError("oracle/_ref/libxtgref.so is not built")
+        self.O, self.R, self.np = O, R, np
+        R.xr_sublayer.argtypes = [C.c_void_p, C.POINTER(XrShape), C.POINTER(XrSublayer), O.f32p, C.c_int, C.c_int64,
+                                  C.c_int, O.f32p]
+        R.xr_head.argtypes = [C.c_void_p, O.u8p, O.u8p, C.c_float, C.c_int, C.c_int, O.f32p, C.c_int, O.f32p,
+                              O.f32p]
+        self.cfg = cfg = dict(model)
+        self.pos = prefill
+        self.ring = cfg["window"] + 16
+        self.synth = O.SynthDory(cfg, ctx=64, n_prefill=0, kv_dtype=O.KV_FP8)
+        M = self.synth.model.contents
+        self.pool = R.xr_pool_new(threads)
+        H, F, Q, kvh, d = cfg["hidden"], cfg["ffn"], cfg["heads"] * cfg["head_dim"], cfg["kv_heads"], cfg["head_dim"]
+        self.shape = XrShape(H, F, cfg["heads"], kvh, d)
+        self.kinds = O.kinds(cfg)
+        self.caches, self.subs = [], []
+        for e, kind in enumerate(self.kinds):
+            L = M.layers[e]
+            sub = XrSublayer()
+            sub.kind = kind
+            for j in range(5):
+                sub.codes[j] = L.w[j].codes
+                sub.scales[j] = L.w[j].scales
+                sub.globals[j] = L.w[j].global_
+            sub.lr, sub.qscale, sub.gscale, sub.sg, sub.su = L.lr, L.qscale, L.gscale, L.sg, L.su
+            sub.theta = L.theta
+            sub.window = cfg["window"] if kind == 1 else 0
+            if kind:
+                c = R.xr_kv_new(kvh, d, 8192, self.ring if kind == 1 else 0, 1)
+                first = 0 if kind == 2 else prefill - self.ring
+                for p in range(first, prefill, 512):
+                    n = min(512, prefill - p)
+                    kk = O.gen_uniform(cfg["seed"], 600000 + 2 * e, -0.1, 0.1, n * kvh * d)
+                    vv = O.gen_uniform(cfg["seed"], 600001 + 2 * e, -0.1, 0.1, n * kvh * d)
+                    assert R.xr_kv_store(c, p, n, O.ptr(kk, O.f32p), O.ptr(vv, O.f32p)) == 0, R.xr_last_error()
+                self.caches.append(c)
+                sub.cache = c
+            self.subs.append(sub)
+        codes, scales, self.g_head = self.synth.weight(-1, 0)
+        self.c_head, self.s_head = np.ascontiguousarray(codes), np.ascontiguousarray(scales)
+        self.ls = np.ctypeslib.as_array(M.logit_scale, shape=(cfg["vocab"],)).copy()
+        self.work = np.zeros(8 * (4 * H + 3 * Q + 2 * F) + 64, np.float32)
+        self.logits = np.zeros((8, cfg["vocab"]), np.float32)
 
-    def vec(stream, lo, hi, n):
-        v = O.gen_uniform(seed, stream, lo, hi, n)
-        keep.append(v)
-        return v
+    def step(self, tokens):
+        O, R, np, cfg = self.O, self.R, self.np, self.cfg
+        H, m, f32p, u8p = cfg["hidden"], len(tokens), O.f32p, O.u8p
+        x = np.zeros((m, H), np.float32)
+        for r, t in enumerate(tokens):
+            R.xr_nvfp4_row(O.ptr(self.c_head, u8p), O.ptr(self.s_head, u8p), self.g_head, cfg["vocab"], H, t,
+                           O.ptr(x[r], f32p))
+        e = 0
 
-    pool = R.xr_pool_new(threads)
-    shape = XrShape(H, F, heads, kvh, d)
+        def sub(x):
+            nonlocal e
+            assert R.xr_sublayer(self.pool, C.byref(self.shape), C.byref(self.subs[e]), O.ptr(x, f32p), m,
+                                 self.pos, 1, O.ptr(self.work, f32p)) == 0, R.xr_last_error()
+            e += 1
 
-    def attn_sub(kind, base):
-        s = XrSublayer()
-        s.kind = kind
-        for j, (n, k) in enumerate([(Q, H), (KV, H), (KV, H), (Q, H), (H, Q)]):
-            c, sc, g = w(base + j, n, k)
-            s.codes[j] = O.ptr(c, u8p)
-            s.scales[j] = O.ptr(sc, u8p)
-            s.globals[j] = g
-        s.lr = O.ptr(vec(base + 8, model["lr_lo"], model["lr_hi"], H), f32p)
-        s.qscale = O.ptr(vec(base + 9, model["qs_lo"], model["qs_hi"], Q), f32p)
-        s.gscale = O.ptr(vec(base + 10, model["gs_lo"], model["gs_hi"], Q), f32p)
-        s.theta = model["theta_global"] if kind == 2 else model["theta_sliding"]
-        s.window = model["window"] if kind == 1 else 0
-        # an FP8 KvCache (the reference has no int8 one) with the prefill stored; a sliding layer's ring is the
-        # reference's own window + 16 slots
-        cache = R.xr_kv_new(kvh, d, 8192, model["window"] + 16 if kind == 1 else 0, 1)
-        first = 0 if kind == 2 else PREFILL - (model["window"] + 16)
-        for p in range(first, PREFILL, 512):
-            n = min(512, PREFILL - p)
-            kk = O.gen_uniform(seed, base + 14, -0.1, 0.1, n * kvh * d)
-            vv = O.gen_uniform(seed, base + 15, -0.1, 0.1, n * kvh * d)
-            assert R.xr_kv_store(cache, p, n, O.ptr(kk, f32p), O.ptr(vv, f32p)) == 0
-        s.cache = cache
-        return s
+        for _ in range(cfg["n_in"]):
+            sub(x)
+        inp, state = x.copy(), x.copy()
+        for _ in range(cfg["loops"]):
+            x = np.ascontiguousarray(state + inp, np.float32)
+            R.xr_justnorm(O.ptr(x, f32p), m, H)
+            for _ in range(cfg["n_rec"]):
+                sub(x)
+            state = x.copy()
+            R.xr_justnorm(O.ptr(state, f32p), m, H)
+        x = state.copy()
+        for _ in range(cfg["n_out"]):
+            sub(x)
+        assert R.xr_head(self.pool, O.ptr(self.c_head, u8p), O.ptr(self.s_head, u8p), self.g_head, cfg["vocab"], H,
+                         O.ptr(x, f32p), m, O.ptr(self.ls, f32p), O.ptr(self.logits, f32p)) == 0
+        return self.logits[:m]
 
-    def mlp_sub(base):
-        s = XrSublayer()
-        s.kind = 0
-        for j, (n, k) in enumerate([(F, H), (F, H), (H, F)]):
-            c, sc, g = w(base + j, n, k)
-            s.codes[j] = O.ptr(c, u8p)
-            s.scales[j] = O.ptr(sc, u8p)
-            s.globals[j] = g
-        s.lr = O.ptr(vec(base + 8, model["lr_lo"], model["lr_hi"], H), f32p)
-        s.sg = O.ptr(vec(base + 11, model["suv_lo"], model["suv_hi"], F), f32p)
-        s.su = O.ptr(vec(base + 12, model["suv_lo"], model["suv_hi"], F), f32p)
-        return s
+    def close(self):
+        for c in self.caches:
+            self.R.xr_kv_free(c)
+        self.caches = []
+        if self.pool:
+            self.R.xr_pool_free(self.pool)
+            self.pool = None
+        self.synth.close()
 
-    subs = {"global": attn_sub(2, 1000 + 16 * 6), "sliding": attn_sub(1, 1000), "mlp": mlp_sub(1000 + 16)}
-    head_rows = model["vocab"] // 16
-    hc, hs, hg = w(1, head_rows, H)
-    ls = vec(2, model["ls_lo"], model["ls_hi"], head_rows)
-    x0 = O.gen_uniform(seed, 9, -0.03, 0.03, 8 * H).reshape(8, H)
-    work = np.zeros(8 * (4 * H + 3 * Q + 2 * F) + 64, np.float32)
-    logits = np.zeros((8, head_rows), np.float32)
-    times = {k: [] for k in ("global", "sliding", "mlp", "head")}
-    for rep in range(warmup + reps):
-        for name, s in subs.items():
-            x = np.ascontiguousarray(x0)
-            t0 = time.perf_counter()
-            assert R.xr_sublayer(pool, C.byref(shape), C.byref(s), O.ptr(x, f32p), 8, PREFILL, 1,
-                                 O.ptr(work, f32p)) == 0, R.xr_last_error()
-            if rep >= warmup:
-                times[name].append(time.perf_counter() - t0)
-        x = np.ascontiguousarray(x0)
+
+def reference_steps(model, threads, steps, warmup):
+    """Seconds per whole reference step (the mean over `steps` timed steps after `warmup`), and the setup time."""
+    t0 = time.perf_counter()
+    ref = ReferenceStep(model, threads)
+    setup = time.perf_counter() - t0
+    try:
+        for _ in range(warmup):
+            ref.step(TOKENS)
         t0 = time.perf_counter()
-        assert R.xr_head(pool, O.ptr(hc, u8p), O.ptr(hs, u8p), hg, head_rows, H, O.ptr(x, f32p), 8, O.ptr(ls, f32p),
-                         O.ptr(logits, f32p)) == 0
-        if rep >= warmup:
-            times["head"].append(time.perf_counter() - t0)
-    for s in subs.values():
-        if s.kind:
-            R.xr_kv_free(s.cache)
-    R.xr_pool_free(pool)
-    ev = [e for e in range(model["n_in"] + model["n_rec"] * model["loops"] + model["n_out"])]
-    kinds = O.kinds(model)
-    n_g, n_s, n_m = kinds.count(2), kinds.count(1), kinds.count(0)
-    del ev
-    med = {k: statistics.median(v) for k, v in times.items()}
-    step = n_g * med["global"] + n_s * med["sliding"] + n_m * med["mlp"] + 16 * med["head"]
-    detail = {k: round(v * 1e3, 3) for k, v in med.items()}
-    return step, detail, (n_g, n_s, n_m)
+        for _ in range(steps):
+            ref.step(TOKENS)
+        step_s = (time.perf_counter() - t0) / steps
+    finally:
+        ref.close()
+    return step_s, setup
+
+
+def reference_config(n):
+    c = config_block(n)
+    c.update(kv_dtype="fp8 (the reference's KvCache has no int8 form)", ring_slots=1040,
+             ring_note="the reference's own ring: window 1024 + 16 slots")
+    return c
 
 
 def run_reference(args, rank):
@@ -245,15 +266,17 @@ def run_reference(args, rank):
     x = package()
     model = dict(x.DORY_3072)
     threads = os.cpu_count() or 1
-    step_s, detail, counts = reference_sample(model, threads, max(1, args.steps), max(0, args.warmup))
+    steps, warmup = max(1, args.steps), max(0, args.warmup)
+    step_s, setup = reference_steps(model, threads, steps, warmup)
     value = 8.0 / step_s
-    sample = (f"per step: 1 global + 1 sliding attention + 1 MLP sublayer (8 rows, 8184 cached, FP8 KvCache: "
-              f"the reference has no int8 cache) and 1/16 of the NVFP4 head, scaled by {counts[0]} / {counts[1]} / "
-              f"{counts[2]} sublayers and 16; medians ms {detail}")
+    sample = (f"whole config-3 steps: {steps} timed after {warmup} warm-up, each the 88 sublayers and the whole "
+              f"NVFP4 head on the reference's kernels (8 rows at position 8184, FP8 KvCaches, 1040-slot rings); "
+              f"setup {setup:.1f} s untimed")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations, NVFP4 weights", "data": "synthetic",
-            "config": config_block(args.gpus),
+            "steps": steps, "warmup": warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 activations, NVFP4 weights, fp8 KV",
+            "data": "synthetic", "config": reference_config(args.gpus),
+            "steps_per_s": 1.0 / step_s, "rows_per_s": value,
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -557,6 +580,21 @@ def shared_sessions_block(x, s, dist, steps, sessions=4):
             "e2e_d2h_bytes_per_round": sessions * 8 * 131072 * 4}
 
 
+def acceptance_draws(n, seed=4):
+    """BASELINE config 4's seeded acceptance: tokens accepted per verify step, uniform in 1..4 (numpy PCG64, seed 4)."""
+    import numpy as np
+    return np.random.default_rng(seed).integers(1, 5, n)
+
+
+def rates(world, ms_per_step):
+    """Steps, verify rows and accepted tokens per second for the whole job (accepted: the mean of 256 seeded draws
+    of 1..4 tokens per step, as config 4 drives its rewinds)."""
+    steps = world / (ms_per_step / 1e3)
+    acc = float(acceptance_draws(256).mean())
+    return {"steps_per_s": steps, "rows_per_s": 8.0 * steps, "accepted_tok_per_s": acc * steps,
+            "accepted_per_step": acc}
+
+
 def job_rows_per_s(world, ms_per_step):
     """Whole-job throughput: every rank verifies 8 rows of its own sequence per step (weak scaling)."""
     return world * 8.0 / (ms_per_step / 1e3)
@@ -631,6 +669,8 @@ def run_ours(args, rank, world, local_rank, dist):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "nvfp4 weights x e2m1-digit activations (6 block-scaled digits) on tcgen05, f32 accumulate; int8 KV",
             "data": "synthetic (seeded random-init weights, random prefilled KV)", "config": config_block(world),
+            "value_counts": "verify rows per second (8 per step); accepted tokens per second are in `rates`",
+            "rates": rates(world, ms),
             "e2e": {"value": world * 8.0 / e2e_s, "unit": UNIT, "h2d_bytes_per_step": 48,
                     "d2h_bytes_per_step": 8 * model["vocab"] * 4, "ms_per_step": e2e_s * 1e3},
             "e2e_topk": {"value": world * 8.0 / e2e_topk_s, "unit": UNIT, "h2d_bytes_per_step": 48,
@@ -677,11 +717,11 @@ def run_ours(args, rank, world, local_rank, dist):
                          "peak_kind": "4x measured bf16 dense (burst)"}}
     if world == 1 and not args.no_cpu_baseline:
         try:
-            step_s, detail, counts = reference_sample(model, os.cpu_count() or 1, 1, 0)
+            step_s, setup = reference_steps(model, os.cpu_count() or 1, 2, 1)
             line["cpu_baseline"] = {"value": 8.0 / step_s, "unit": UNIT, "cores": os.cpu_count() or 1,
                                     "kind": "reference",
-                                    "sample": f"1 global + 1 sliding + 1 MLP sublayer + 1/16 head, scaled to the "
-                                              f"step; medians ms {detail}"}
+                                    "sample": "2 whole config-3 steps after 1 warm-up on the reference's kernels "
+                                              "(FP8 KvCaches, 1040-slot rings: the reference has no int8 cache)"}
         except Exception as e:  # the baseline is reported, never the target
             line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": os.cpu_count() or 1, "kind": "reference",
                                     "sample": f"unavailable: {e}"}
