@@ -11,11 +11,12 @@
 // Operand B (activations): each 16-input group of an activation row x is brought into (1344, 2688] by a power of
 // two p (kept beside the digits) and written as kDigits rows of E2M1 digits q_d with a UE4M3 scale s_d each,
 // x p ~= sum_d s_d q_d: s_1 = the smallest UE4M3 >= max |x p| / 6, q_1 = the nearest E2M1 of x p / s_1, and each next
-// digit encodes what is left. Every digit shrinks the residual by about 5x, so 6 digits leave |x - sum / p| <=
-// ~5e-5 of the group's largest |x|, finer than an fp16 rounding of x. A GEMV CTA brings the groups of its K slice
+// digit encodes what is left. After a digit of scale s every residual is at most s (E2M1 rounding errs by at most one
+// unit), so 4 digits leave |x - sum / p| <= ~8e-4 of the group's largest |x| in the worst case, and ~1e-4 typically:
+// finer than a bf16 rounding of the group's largest element (2^-9 of it). A GEMV CTA brings the groups of its K slice
 // to one prescale per row (the slice's smallest p) by scaling their s_d down, exactly unless they turn subnormal.
-// Digit row n = 8 d + i (digit d of activation row i), N = 48, so one MMA multiplies 128 weight rows by every digit
-// of all 8 rows; the epilogue adds the 6 digit columns of each row.
+// Digit row n = 8 d + i (digit d of activation row i), N = 32, so one MMA multiplies 128 weight rows by every digit
+// of all 8 rows; the epilogue adds the 4 digit columns of each row.
 #pragma once
 
 #include "common.cuh"
@@ -26,10 +27,10 @@ constexpr int kTileRows = 128;               // weight rows per tile (the MMA's 
 constexpr int kKBlock = 64;                  // inputs per MMA
 constexpr int kUnitBytes = 4608;             // one (tile, K block) of A: 4096 code bytes + 512 scale bytes
 constexpr int kUnitCodeBytes = 4096;
-constexpr int kDigits = 6;
+constexpr int kDigits = 4;
 constexpr int kDigitRows = 8 * kDigits;      // the MMA's N
-constexpr int kBBlockBytes = 2048;           // one K block of B: 1536 digit bytes + 512 scale bytes
-constexpr int kBCodeBytes = 1536;
+constexpr int kBCodeBytes = kDigits * 256;   // 8 rows x 64 inputs x 4 bits per digit
+constexpr int kBBlockBytes = kBCodeBytes + 512;   // one K block of B: 1024 digit bytes + 512 scale bytes
 
 // ---- operand layouts ----
 
@@ -52,7 +53,7 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
 __device__ __forceinline__ uint64_t a_desc(uint32_t saddr) { return smem_desc(saddr, 128, 256); }
 __device__ __forceinline__ uint64_t sf_desc(uint32_t saddr) { return smem_desc(saddr, 0, 128); }
 
-// kind::mxf4nvf4 instruction descriptor: E2M1 A and B, K-major, UE4M3 scales, M = 128, N = 48, K = 64
+// kind::mxf4nvf4 instruction descriptor: E2M1 A and B, K-major, UE4M3 scales, M = 128, N = 32, K = 64
 constexpr uint32_t kIdescFp4 = (1u << 7) | (1u << 10) | ((uint32_t)(kDigitRows >> 3) << 17) | ((128u >> 4) << 24);
 
 // ---- tcgen05 ----
@@ -163,11 +164,10 @@ __device__ __forceinline__ float block_prescale(float amax) {
 // prescale p (returned) is `fixed` if given (> 0; the caller guarantees max |x| fixed <= 2688), else its own. Per
 // digit, lane t gets the 2 code bytes of its inputs (code[d]: bits 0-15) and every lane the scale byte sf[d].
 // Digit scales: E2M1 rounding of |y| <= 6 errs by at most 1 (the step from 4 to 6), so after a digit of scale s every
-// residual is at most s and ceil(s / 6) is a safe next scale without looking at the residuals. Digits 0, 2, 4 take
-// their scale from the group's residual maximum (a max over the quad), digits 1, 3, 5 from that bound: half the
-// shuffles of a per-digit maximum, for a reconstruction error within ~1.5x of it (~1.2e-5 of the group maximum at
-// most). A digit's value r / s only picks the code (the residual keeps the exact r - s q), so 1 / s may be the fast
-// reciprocal.
+// residual is at most s and ceil(s / 6) is a safe next scale without looking at the residuals. Even digits take
+// their scale from the group's residual maximum (a max over the quad), odd digits from that bound: half the shuffles
+// of a per-digit maximum, for a reconstruction error within ~1.5x of it. A digit's value r / s only picks the code
+// (the residual keeps the exact r - s q), so 1 / s may be the fast reciprocal.
 template <int D>
 __device__ __forceinline__ float digitize16_quad_n(const float (&x)[4], uint32_t (&code)[D], uint32_t (&sf)[D],
                                                    float fixed = 0.f) {

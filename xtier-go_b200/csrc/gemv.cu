@@ -6,7 +6,7 @@
 // CUDA cores costs ~95 instructions per 576 weight bytes, which alone fills the SM's issue slots at HBM rate.
 // tcgen05.mma kind::mxf4nvf4 takes the codes and the per-16 E4M3 scales as they are stored, so the weights go from
 // HBM to shared memory (bulk copies) to the tensor core untouched. The activations become the FP4 B operand as
-// 6 scaled E2M1 digits per value (fp4mma.cuh): N = 48 digit rows, the epilogue adds each row's 6 digit columns.
+// 4 scaled E2M1 digits per value (fp4mma.cuh): N = 32 digit rows, the epilogue adds each row's 4 digit columns.
 // One MMA is 128 weight rows x 64 inputs; its accumulator lives in TMEM.
 //
 // Work split: tiles of 128 rows. A GEMV with fewer tiles than CTA slots splits each tile's K blocks over a cluster
@@ -31,7 +31,8 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kStageUnits = 4;
 constexpr int kMaxRing = 6;
-constexpr int kAccCols = 64;   // TMEM columns per accumulator (48 used)
+constexpr int kAccCols = 64;   // TMEM columns per accumulator (32 used)
+static_assert(kBBlockBytes == kDigitBlockBytes, "the host's digit buffer size");
 constexpr int kSumsqLoads = 10;   // the producer's row-sum parts a lane loads: at most 320 parts
 
 struct Params {
@@ -507,14 +508,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
       const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)(acc * kAccCols);
       tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(&d[0]));
       tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(&d[16]));
-      tmem_ld16(taddr + 32, *reinterpret_cast<float(*)[16]>(&d[32]));
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&accempty[acc]);
       float y[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        y[i] = ((((d[i] + d[8 + i]) + d[16 + i]) + d[24 + i]) + (d[32 + i] + d[40 + i])) * inv[i];
+        y[i] = ((d[i] + d[8 + i]) + (d[16 + i] + d[24 + i])) * inv[i];
       if constexpr (EPI == kEpiHead) {
         const int row = t * kTileRows + r;
         const bool ok = row < a.vocab;

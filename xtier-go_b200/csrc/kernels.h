@@ -18,8 +18,10 @@ inline int packed_tiles(int n_out, bool interleave) { return interleave ? (n_out
 inline int64_t packed_bytes(int n_out, int k, bool interleave) {
   return (int64_t)packed_tiles(n_out, interleave) * packed_kblocks(k) * kPackUnitBytes;
 }
-// activations as B digits (fp4mma.cuh): 2048 bytes per 64 inputs
-inline int64_t digit_bytes(int k) { return (int64_t)packed_kblocks(k) * 2048; }
+// activations as B digits (fp4mma.cuh): 1536 bytes per 64 inputs (4 digits of 8 rows, 1024 bytes, and a 512-byte
+// scale atom)
+constexpr int kDigitBlockBytes = 1536;
+inline int64_t digit_bytes(int k) { return (int64_t)packed_kblocks(k) * kDigitBlockBytes; }
 // the prescale of digits of a unit-norm vector (|x| <= 1): every group of the residual stream takes it
 constexpr float kUnitPrescale = 2048.f;
 
@@ -51,7 +53,7 @@ struct ArgCand {   // the best logit of a tile for one activation row
 struct GemvArgs {
   const uint8_t* w;          // units [tiles][kblocks]
   int tiles, kblocks;
-  // input: the B digits of the activations ([kblocks][2048], fp4mma.cuh) and the power-of-two prescale of every
+  // input: the B digits of the activations ([kblocks][1536], fp4mma.cuh) and the power-of-two prescale of every
   // 16-input group and row ([kblocks * 4][8])
   const uint8_t* xb;
   const float* xb_pre;
@@ -67,7 +69,7 @@ struct GemvArgs {
   const float* sg;
   const float* su;
   int features;              // F
-  uint8_t* vb;               // [tiles][2048]
+  uint8_t* vb;               // [tiles][1536]
   float* vb_pre;             // [tiles * 4][8]
   float* vsum;               // [tiles * split][8]: sums of v^2 over the features each CTA finishes
   // kEpiQkv: the q | k | v | g projection of an attention sublayer, one 128-row tile per head (head_dim 128): tiles
@@ -115,7 +117,7 @@ struct GemvPlan {
 };
 GemvPlan plan_gemv(int tiles, int kblocks, int num_sms, int max_split, int max_tiles_per_cta);
 void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, bool pdl);
-// x f32 [m][k] (k a multiple of 16; rows m..7 zero) -> B digits xb [kblocks][2048] and prescales xb_pre [k / 16][8]
+// x f32 [m][k] (k a multiple of 16; rows m..7 zero) -> B digits xb [kblocks][1536] and prescales xb_pre [k / 16][8]
 void digitize_rows(const float* x, int m, int k, uint8_t* xb, float* xb_pre, cudaStream_t s);
 
 // ---- the GEMM (gemm.cu): y[m][n] = x[m][k] W^T for prefill chunks and batches ----
