@@ -240,7 +240,8 @@ def test_forward_batch_matches_one_by_one(cuda, xtg, cfg):
     with xtg.Session(cfg, context=256) as owner:
         owner.prefill_synthetic(70)
         singles = [xtg.Session.shared(owner, context=256) for _ in lists]
-        batch = [xtg.Session.shared(owner, context=256) for _ in lists]
+        # batch=0: each session's own step graph, all in flight at once (the batched step is tested below)
+        batch = [xtg.Session.shared(owner, context=256, batch=0) for _ in lists]
         try:
             want = []
             for s, t in zip(singles, lists):
@@ -248,6 +249,10 @@ def test_forward_batch_matches_one_by_one(cuda, xtg, cfg):
                 want.append(s.forward(t, want=2) if t else {})
             for s in batch:
                 s.prefill_synthetic(70)
+            # the session given no tokens keeps a snapshot past its position (as a forward of nothing does)
+            batch[3].forward([1] * 8, want=0)
+            batch[3].snapshot(0)
+            assert batch[3].rewind(70) and batch[3].snapshot_pos(0) == 78
             with pytest.raises(xtg.XtgError):
                 xtg.forward_batch([batch[0], batch[0]], [lists[0], lists[1]])
             with pytest.raises(xtg.XtgError):
@@ -259,6 +264,50 @@ def test_forward_batch_matches_one_by_one(cuda, xtg, cfg):
                 for r in want[i]:
                     np.testing.assert_array_equal(got[i][r], want[i][r], err_msg=f"session {i} row {r}")
                 assert batch[i].pos() == 70 + len(t)
+            assert batch[3].snapshot_pos(0) == 78
         finally:
             for s in singles + batch:
+                s.close()
+
+
+def test_forward_batch_batched_step(cuda, xtg, cfg):
+    """xtg_cuda_forward_batch over sessions that share one weight set runs them as one batched step (every projection
+    one tcgen05 GEMM over all their rows): nine sessions (a group of 8 and a group of 1) at different positions, with
+    different token counts (one of two rounds, one of none), each within the step tolerance of a forward of its own
+    (identical argmax), the first also against the oracle; positions advance, and a second call after rewinds gives
+    the same logits again."""
+    lists = [[5, 17, 900, 3, 44, 1023, 0, 256], [8, 9, 10], list(range(100, 111)), [], [4095], [1, 2, 3, 4],
+             [700] * 8, [9, 8, 7, 6, 5], [11, 12]]
+    pre = [70, 90, 64, 100, 75, 128, 81, 99, 70]
+    with xtg.Session(cfg, context=512) as owner:
+        sess = [xtg.Session.shared(owner, context=512) for _ in lists]
+        singles = [xtg.Session.shared(owner, context=512) for _ in lists]
+        try:
+            for s, p in zip(sess + singles, pre + pre):
+                s.prefill_synthetic(p)
+            want = [s.forward(t, want=2) if t else {} for s, t in zip(singles, lists)]
+            got = xtg.forward_batch(sess, lists, want=2)
+            for i, t in enumerate(lists):
+                assert sorted(got[i]) == list(range(len(t)))
+                assert sess[i].pos() == pre[i] + len(t)
+                if not t:
+                    continue
+                g, w = logits_of(got[i], len(t)), logits_of(want[i], len(t))
+                assert np.array_equal(g.argmax(1), w.argmax(1)), i
+                assert np.abs(g - w).max() <= LOGIT_TOL, (i, np.abs(g - w).max())
+            ref = O.SynthDory(cfg, ctx=512, n_prefill=pre[0])
+            oracle = ref.step(lists[0])
+            ref.close()
+            g0 = logits_of(got[0], 8)
+            assert np.array_equal(g0.argmax(1), oracle.argmax(1))
+            assert np.abs(g0 - oracle).max() <= LOGIT_TOL
+            assert sess[0].argmax(8) == list(oracle.argmax(1))
+            for s, p in zip(sess, pre):
+                assert s.rewind(p)
+            again = xtg.forward_batch(sess, lists, want=2)
+            for i, t in enumerate(lists):
+                for r in range(len(t)):
+                    np.testing.assert_array_equal(again[i][r], got[i][r], err_msg=f"session {i} row {r}")
+        finally:
+            for s in sess + singles:
                 s.close()

@@ -21,6 +21,7 @@
 // dimension inside a k16 step (lane tq reads 32 contiguous bytes of a K row, Q's fragments use the same order) and
 // the keys inside a warp's quarter (lane tq owns keys 4 tq .. 4 tq + 3 in both products).
 #include "attention.h"
+#include "batch.h"
 #include "common.cuh"
 #include "fp4mma.cuh"
 
@@ -69,11 +70,15 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, tq = lane & 3;
-  const int split = blockIdx.x, kvh = blockIdx.y;
-  const int m = a.params ? a.params->m : a.m;
-  const int pos0 = (int)(a.params ? a.params->pos0 : a.pos0);   // positions stay below 2^31
-  const int64_t slots = a.slots;
+  const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+  const StepParams* prm = a.params ? a.params + seq : nullptr;
+  const KvSeq* sq = a.seqs ? a.seqs + seq : nullptr;
+  const int m = prm ? prm->m : a.m;
+  const int pos0 = (int)(prm ? prm->pos0 : a.pos0);   // positions stay below 2^31
+  const int64_t slots = sq ? sq->slots : a.slots;
   const int group = a.heads / a.kv_heads;
+  const int32_t* ring_pos = sq ? sq->ring_pos : a.ring_pos;
+  const float* aq = a.q + (int64_t)seq * kMaxRows * a.heads * kD;
 
   // this CTA's 64-slot chunks: a global cache holds [0, pos0), a ring every slot
   const int64_t span = a.ring ? slots : pos0;
@@ -81,10 +86,10 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   const int stot = a.splits_total > 0 ? a.splits_total : a.splits, sidx = a.split0 + split;
   const int64_t cb = nchunks * sidx / stot, ce = nchunks * (sidx + 1) / stot;
   const int nc = (int)(ce - cb);
-  const uint8_t* kc = a.kc + (int64_t)kvh * slots * kD;
-  const uint8_t* vc = a.vc + (int64_t)kvh * kD * slots;
-  const float* ks = a.ks + (int64_t)kvh * slots;
-  const float* vs = a.vs + (int64_t)kvh * slots;
+  const uint8_t* kc = (sq ? sq->kc : a.kc) + (int64_t)kvh * slots * kD;
+  const uint8_t* vc = (sq ? sq->vc : a.vc) + (int64_t)kvh * kD * slots;
+  const float* ks = (sq ? sq->ks : a.ks) + (int64_t)kvh * slots;
+  const float* vs = (sq ? sq->vs : a.vs) + (int64_t)kvh * slots;
   const uint32_t stage_bytes = 2 * 64 * kD + 2 * 64 * 4 + (a.ring ? 64 * 4 : 0);
   // chunk i of this CTA into stage i % kStages, by lanes 0-4 of warp 0: one bulk copy per lane (the copies of one
   // thread complete one after another)
@@ -98,7 +103,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     if (lane == 1) bulk_g2s(st.v, vc + c * 64 * kD, 64 * kD, bar);
     if (lane == 2) bulk_g2s(st.ks, ks + c * 64, 64 * 4, bar);
     if (lane == 3) bulk_g2s(st.vs, vs + c * 64, 64 * 4, bar);
-    if (lane == 4 && a.ring) bulk_g2s(st.pos, a.ring_pos + c * 64, 64 * 4, bar);
+    if (lane == 4 && a.ring) bulk_g2s(st.pos, ring_pos + c * 64, 64 * 4, bar);
   };
   // the cached keys and values do not depend on the previous kernel: the first chunks go out now
   if (threadIdx.x == 0) {
@@ -121,7 +126,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   // (a0, a1) and + {2, 3} (a2, a3) of its rows gg and gg + 8 ----
   auto qrow = [&](int r, int d0) {   // 4 head dims of query row r (zeros for rows past m)
     const int i = r / group, hg = r % group;
-    return i < m ? *reinterpret_cast<const float4*>(a.q + ((int64_t)i * a.heads + kvh * group + hg) * kD + d0)
+    return i < m ? *reinterpret_cast<const float4*>(aq + ((int64_t)i * a.heads + kvh * group + hg) * kD + d0)
                  : make_float4(0.f, 0.f, 0.f, 0.f);
   };
   float4 qv[2][2];
@@ -333,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
         L += w[q] == 0.f ? 0.f : st0[q * ss + r * kStateStride + 1] * w[q];
       }
       const int pidx = a.part_local ? split : sidx;
-      float* out = a.part + (((int64_t)pidx * a.kv_heads + kvh) * kQRows + r) * kPartStride;
+      float* out = a.part + (int64_t)seq * a.part_seq_stride + (((int64_t)pidx * a.kv_heads + kvh) * kQRows + r) * kPartStride;
       if (j == 0) {
         out[0] = M;
         out[1] = L;
@@ -360,27 +365,28 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   __shared__ float cached[2];      // the splits' max m and their sum of l relative to it
   __shared__ float part_s[kD / 32][kMaxRows];
   __shared__ float ml[2][kMaxSplits];   // every split's m and l
-  const int i = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int i = blockIdx.x, h = blockIdx.y, seq = blockIdx.z, d = threadIdx.x;
   const int col = h * kD + d;
   // the gate's scale is a parameter: loaded before the dependency wait
   const float gsc = a.out ? 0.f : a.gscale[col];
-  const int m = a.params ? a.params->m : a.m;
+  const int m = a.params ? a.params[seq].m : a.m;
+  const int64_t rows0 = (int64_t)seq * kMaxRows;   // this sequence's first activation row
   if (a.pdl) {
     pdl_wait();
     pdl_launch_next();
   }
   if (i >= m) return;
   const int group = a.heads / a.kv_heads, kvh = h / group, qr = i * group + h % group;
-  const float* base = a.part + ((int64_t)kvh * kQRows + qr) * kPartStride;   // split s at s * sstride
-  const int64_t sstride = (int64_t)a.kv_heads * kQRows * kPartStride;
-  const float qd = a.q[((int64_t)i * a.heads + h) * kD + d];
+  const float* base = a.part + (int64_t)seq * a.part_seq_stride + ((int64_t)kvh * kQRows + qr) * kPartStride;
+  const int64_t sstride = (int64_t)a.kv_heads * kQRows * kPartStride;   // split s at s * sstride
+  const float qd = a.q[((rows0 + i) * a.heads + h) * kD + d];
   float kj[kMaxRows], vj[kMaxRows];
 #pragma unroll
   for (int j = 0; j < kMaxRows; ++j) {
-    kj[j] = j < m ? a.k[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
-    vj[j] = j < m ? a.v[((int64_t)j * a.kv_heads + kvh) * kD + d] : 0.f;
+    kj[j] = j < m ? a.k[((rows0 + j) * a.kv_heads + kvh) * kD + d] : 0.f;
+    vj[j] = j < m ? a.v[((rows0 + j) * a.kv_heads + kvh) * kD + d] : 0.f;
   }
-  const float gt = a.out ? 0.f : a.gate[(int64_t)i * a.gate_ld + col];
+  const float gt = a.out ? 0.f : a.gate[(rows0 + i) * a.gate_ld + col];
   // every independent load in one wave: this thread's dim of every split's partial, the m and l of splits d and
   // d + 128
   const int ns = a.splits < kRegSplits ? a.splits : kRegSplits;
@@ -514,6 +520,11 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   o *= 1.f / (1.f + expf(-gt * gsc));
   __shared__ float red[32];
   const float ss = block_sum(o * o, red);
+  if (a.gated_out) {   // the batched step: f32 rows for the GEMM's digitizer
+    a.gated_out[(rows0 + i) * a.heads * kD + col] = o;
+    if (d == 0) a.asum[h * a.asum_ld + rows0 + i] = ss;
+    return;
+  }
   if (d == 0) a.asum[h * kMaxRows + i] = ss;
   // the O projection's input: this head's 8 groups of 16 as B digits (warp 0, a quad per group)
   __shared__ float ov[kD];
@@ -548,7 +559,8 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
   static std::atomic<uint64_t> optin{0};
   ensure_smem_optin((const void*)attention_kernel, (int)sizeof(Smem), optin);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.splits, a.kv_heads);
+  XTG_REQUIRE(!a.seqs || (a.nseq >= 1 && a.nseq <= kMaxBatch && a.params), "attention: 1..8 sequences with params");
+  cfg.gridDim = dim3(a.splits, a.kv_heads, a.seqs ? a.nseq : 1);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = sizeof(Smem);
   cfg.stream = s;
@@ -570,8 +582,10 @@ void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
               "combine: split-KV exchange needs 2..8 processes, the epoch and an error word (the step only)");
   for (int t = 0; t < a.x.world && a.x.world > 1; ++t)
     XTG_REQUIRE(a.x.slot[t], "combine: split-KV exchange without the slots of every process");
+  XTG_REQUIRE(!a.gated_out || (a.nseq >= 1 && a.nseq <= kMaxBatch && a.params && a.asum && a.gate && a.gscale),
+              "combine: the batched step needs 1..8 sequences, params, the gate and the sums");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kMaxRows, a.heads);
+  cfg.gridDim = dim3(kMaxRows, a.heads, a.gated_out ? a.nseq : 1);
   cfg.blockDim = dim3(kD);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];

@@ -50,6 +50,8 @@ struct PeerXchg {
   int g, n_g;                    // this layer's index among the step's n_g global layers
 };
 
+struct KvSeq;   // batch.h
+
 struct AttnArgs {
   // this call's rows, prepared (RoPE, justnorm, q scale): q [m][heads][128], k / v [m][kv_heads][128] (already in the
   // cache at positions pos0 .. pos0 + m - 1; the scores against them use these unquantized rows)
@@ -79,6 +81,12 @@ struct AttnArgs {
   int part_local;           // partials at index split (this launch's own) instead of split0 + split
   int* err;                 // set if a bounded wait gave up (never expected); may be null
   int pdl;
+  // Several sequences in one launch (the batched step, grid z = sequence s): s's caches and ring table from seqs[s]
+  // (kc ... ring_pos, slots above unused), its m and pos0 from params[s], its rows of q / k / v 8 s .. 8 s + 7, its
+  // partials part_seq_stride floats after sequence s - 1's. null: one sequence.
+  const KvSeq* seqs;
+  int nseq;
+  int64_t part_seq_stride;
 };
 
 struct CombineArgs {
@@ -102,6 +110,12 @@ struct CombineArgs {
   int pdl;
   PeerXchg x;               // split-KV across GPUs: splits are this process's, merged with the peers' here
   int* err;                 // set if the wait for a peer gave up
+  // the batched step (grid z = sequence s, params[s], rows 8 s ..): the gated output in f32 (gated_out [8 S][heads *
+  // 128]) and the per-head sums of squares (asum[h * asum_ld + 8 s + i]) instead of digits
+  float* gated_out;
+  int asum_ld;
+  int nseq;
+  int64_t part_seq_stride;
 };
 
 size_t attention_smem_bytes();

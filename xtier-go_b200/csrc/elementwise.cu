@@ -131,14 +131,15 @@ __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a)
     const float4 l4 = ld4(a.lr, ch[j], a.mode == kResidSlerp && ok[j]);
     lr[j][0] = l4.x; lr[j][1] = l4.y; lr[j][2] = l4.z; lr[j][3] = l4.w;
   }
-  const int m = a.params ? a.params->m : a.m;
+  // live rows: one sequence's rows below m, or (batched) row r % 8 of sequence r / 8 below that sequence's m
   if (a.pdl) {
     pdl_wait();
     pdl_launch_next();
   }
+  const bool live = a.nseq > 0 ? (r % kMaxRows) < a.params[r / kMaxRows].m : r < (a.params ? a.params->m : a.m);
   float* h = a.h + (int64_t)r * H;
   float v[kChunks][4];
-  if (r >= m) {
+  if (!live) {
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) v[j][0] = v[j][1] = v[j][2] = v[j][3] = 0.f;
   } else if (a.mode == kResidSlerp) {
@@ -147,7 +148,15 @@ __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a)
     float sa = 0.f, sb = 0.f;
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
-      const float4 h4 = ld4(h, ch[j], ok[j]), o4 = ld4(o, ch[j], ok[j]);
+      const float4 h4 = ld4(h, ch[j], ok[j]);
+      float4 o4 = ld4(o, ch[j], ok[j]);
+      for (int q = 1; q < a.o_parts; ++q) {   // a K-split GEMM's partial outputs, in order
+        const float4 p4 = ld4(o + q * a.o_stride, ch[j], ok[j]);
+        o4.x += p4.x;
+        o4.y += p4.y;
+        o4.z += p4.z;
+        o4.w += p4.w;
+      }
       hv[j][0] = h4.x; hv[j][1] = h4.y; hv[j][2] = h4.z; hv[j][3] = h4.w;
       ov[j][0] = o4.x; ov[j][1] = o4.y; ov[j][2] = o4.z; ov[j][3] = o4.w;
     }
@@ -232,8 +241,8 @@ __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a)
   // the new h, and its digits: the quad of threads 4 g .. 4 g + 3 of chunk j holds group g + 256 j
 #pragma unroll
   for (int j = 0; j < kChunks; ++j) {
-    if (r < m && ok[j]) st4(h, ch[j], v[j]);
-    if (j * kResidThreads < H / 4) {   // whole warps take part in the quad's shuffles
+    if (live && ok[j]) st4(h, ch[j], v[j]);
+    if (a.xb && j * kResidThreads < H / 4) {   // whole warps take part in the quad's shuffles
       uint32_t code[kDigits], sf[kDigits];
       const float p = digitize16_quad(v[j], code, sf, kUnitNorm);
       if (ok[j]) {
@@ -454,7 +463,9 @@ void launch_resid(const ResidArgs& a_in, cudaStream_t s, bool pdl) {
                s, pdl, 0);
     return;
   }
-  launch_pdl(resid_kernel, dim3(kMaxRows), dim3(kResidThreads), a, s, pdl, 0);
+  XTG_REQUIRE(a.nseq >= 0 && a.nseq <= 64, "resid: at most 64 sequences");
+  if (a.o_parts < 1) a.o_parts = 1;
+  launch_pdl(resid_kernel, dim3(kMaxRows * (a.nseq > 0 ? a.nseq : 1)), dim3(kResidThreads), a, s, pdl, 0);
 }
 
 void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out, float* out_val,

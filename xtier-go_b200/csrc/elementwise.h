@@ -46,6 +46,11 @@ struct ResidArgs {
   const float* rsum;
   int nparts;
   int pdl;
+  // the batched step (nseq > 0): row r is row r % 8 of sequence r / 8 (its m from params[r / 8]); o is the sum of
+  // o_parts partial outputs o_stride floats apart (a K-split GEMM); xb null: no digits
+  int nseq;
+  int o_parts;
+  int64_t o_stride;
 };
 
 struct KvStoreArgs {

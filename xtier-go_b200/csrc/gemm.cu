@@ -45,9 +45,15 @@ struct GemmParams {
   const uint8_t* w;          // weight units [wtiles][kblocks]
   int wtiles, kblocks;
   const uint8_t* act;        // activation units [atiles][kblocks]
-  const float* act_pre;      // [atiles * 64] the rows' prescales
+  const float* act_post;     // [atiles * 64] per row: 1 / its prescale, times an optional row scale
   int atiles, m;
   const TileOut* outs;       // [wtiles]
+  // K split ksplit ways (few activation rows: more CTAs than weight tiles): part ks of a tile sums K blocks
+  // [kblocks ks / ksplit, kblocks (ks + 1) / ksplit) and writes its own partial output, split_stride floats after
+  // part ks - 1's (the reader sums the parts in order)
+  int ksplit;
+  int64_t split_stride;
+  int pdl;                   // launched as a programmatic dependent (the weights of the first stages go out first)
   int* err;
 };
 
@@ -64,7 +70,7 @@ __device__ __forceinline__ void tc_mma_gemm(uint32_t tmem_d, uint64_t da, uint64
 __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constant__ GemmParams P) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int KB = P.kblocks, ntiles = P.wtiles * P.atiles;
+  const int KB = P.kblocks, ntiles = P.wtiles * P.ksplit * P.atiles;
   const int my_tiles = (int)blockIdx.x < ntiles ? (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x : 0;
   uint8_t* ring = smem;   // stage s: kGUnits weight units at s * kGStageBytes, then kGUnits activation units
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kGStages * kGStageBytes);
@@ -92,29 +98,54 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  auto tile_of = [&](int i, int& wt, int& at) {
+  // tile i of this CTA: weight tile wt, K part ks (K blocks [k0, k0 + nk)), activation tile at
+  auto tile_of = [&](int i, int& wt, int& ks, int& at, int& k0, int& nk) {
     const int q = (int)blockIdx.x + i * (int)gridDim.x;
-    wt = q / P.atiles;
-    at = q - wt * P.atiles;
+    const int vt = q / P.atiles;
+    at = q - vt * P.atiles;
+    wt = vt / P.ksplit;
+    ks = vt - wt * P.ksplit;
+    k0 = KB * ks / P.ksplit;
+    nk = KB * (ks + 1) / P.ksplit - k0;
   };
 
   // a tile's K blocks go in stages of kGUnits (the last one may be short); stages never span tiles
-  const int spt = (KB + kGUnits - 1) / kGUnits;
   if (warp == 0) {
-    // ---- producer: stage u of this CTA is stage u % spt of its tile u / spt ----
+    // ---- producer ----
     if (lane == 0) {
+      // As a dependent launch the first stages' weight units (which no kernel writes) go out before the wait, their
+      // activation units after it.
+      const int early = P.pdl ? kGStages : 0;
+      if (P.pdl) {
+        int v = 0;
+        for (int i = 0; i < my_tiles && v < early; ++i) {
+          int wt, ks, at, k0, nk;
+          tile_of(i, wt, ks, at, k0, nk);
+          const uint8_t* wsrc = P.w + ((int64_t)wt * KB + k0) * kUnitBytes;
+          for (int kb0 = 0; kb0 < nk && v < early; kb0 += kGUnits, ++v) {
+            const int cnt = min(kGUnits, nk - kb0);
+            mbar_expect_tx(&full[v], (uint32_t)(cnt * (kUnitBytes + kActUnitBytes)));
+            bulk_g2s(ring + v * kGStageBytes, wsrc + (int64_t)kb0 * kUnitBytes, (uint32_t)(cnt * kUnitBytes), &full[v]);
+          }
+        }
+        pdl_wait();
+        pdl_launch_next();
+      }
       int u = 0;
       for (int i = 0; i < my_tiles; ++i) {
-        int wt, at;
-        tile_of(i, wt, at);
-        const uint8_t* wsrc = P.w + (int64_t)wt * KB * kUnitBytes;
-        const uint8_t* asrc = P.act + (int64_t)at * KB * kActUnitBytes;
+        int wt, ks, at, k0, nk;
+        tile_of(i, wt, ks, at, k0, nk);
+        const uint8_t* wsrc = P.w + ((int64_t)wt * KB + k0) * kUnitBytes;
+        const uint8_t* asrc = P.act + ((int64_t)at * KB + k0) * kActUnitBytes;
+        const int spt = (nk + kGUnits - 1) / kGUnits;
         for (int st = 0; st < spt; ++st, ++u) {
-          const int slot = u % kGStages, kb0 = st * kGUnits, cnt = min(kGUnits, KB - kb0);
+          const int slot = u % kGStages, kb0 = st * kGUnits, cnt = min(kGUnits, nk - kb0);
           if (u >= kGStages) mbar_wait_bounded(&empty[slot], (uint32_t)((u / kGStages) - 1) & 1u, P.err);
           uint8_t* dst = ring + slot * kGStageBytes;
-          mbar_expect_tx(&full[slot], (uint32_t)(cnt * (kUnitBytes + kActUnitBytes)));
-          bulk_g2s(dst, wsrc + (int64_t)kb0 * kUnitBytes, (uint32_t)(cnt * kUnitBytes), &full[slot]);
+          if (u >= early) {
+            mbar_expect_tx(&full[slot], (uint32_t)(cnt * (kUnitBytes + kActUnitBytes)));
+            bulk_g2s(dst, wsrc + (int64_t)kb0 * kUnitBytes, (uint32_t)(cnt * kUnitBytes), &full[slot]);
+          }
           bulk_g2s(dst + kGUnits * kUnitBytes, asrc + (int64_t)kb0 * kActUnitBytes, (uint32_t)(cnt * kActUnitBytes),
                    &full[slot]);
         }
@@ -138,8 +169,11 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
           mbar_wait_bounded(&accempty[acc ^ 1], (uint32_t)((i - 1) >> 1) & 1u, P.err);
           tc_fence_after();
         }
+        int wt, ks, at, k0, nk;
+        tile_of(i, wt, ks, at, k0, nk);
+        const int spt = (nk + kGUnits - 1) / kGUnits;
         for (int st = 0; st < spt; ++st, ++u) {
-          const int slot = u % kGStages, kb0 = st * kGUnits, cnt = min(kGUnits, KB - kb0);
+          const int slot = u % kGStages, kb0 = st * kGUnits, cnt = min(kGUnits, nk - kb0);
           mbar_wait_bounded(&full[slot], (uint32_t)(u / kGStages) & 1u, P.err);
           tc_fence_after();
           const uint32_t a0 = ring_addr + (uint32_t)(slot * kGStageBytes), b0 = a0 + kGUnits * kUnitBytes;
@@ -168,11 +202,13 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
   } else if (warp >= 4) {
     // ---- epilogue: TMEM lane quarter q = warp - 4 holds weight rows 32 q .. 32 q + 31 ----
     const int q = warp - 4, r = 32 * q + lane;
+    if (P.pdl) pdl_wait();   // the rows' factors come from the kernel before
     for (int i = 0; i < my_tiles; ++i) {
-      int wt, at;
-      tile_of(i, wt, at);
+      int wt, ks, at, k0, nk;
+      tile_of(i, wt, ks, at, k0, nk);
       const int acc = i & 1;
-      const TileOut o = P.outs[wt];   // loaded before the wait
+      TileOut o = P.outs[wt];
+      o.y += (int64_t)ks * P.split_stride;
       mbar_wait_bounded(&accfull[acc], (uint32_t)(i >> 1) & 1u, lane == 0 ? P.err : nullptr);
       tc_fence_after();
       float y[kActRows];
@@ -195,7 +231,7 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
 #pragma unroll
         for (int ii = 0; ii < kActRows; ++ii) {
           const int row = at * kActRows + ii;
-          if (row < P.m) o.y[(int64_t)row * o.ld + r] = y[ii] * (1.f / P.act_pre[row]) * g;   // p: a power of two
+          if (row < P.m) o.y[(int64_t)row * o.ld + r] = y[ii] * P.act_post[row] * g;
         }
     }
   }
@@ -212,10 +248,17 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
 
 // One CTA per activation row (grid: every row of the activation tiles; rows past m get zero digits): the row's max
 // |x| gives its prescale, then the quads of threads digitize its 16-input groups.
+// Optional row scale (a justnorm of x applied to the product): 1 / sqrt(sum_p sumsq[p * ld + row] + 1e-6), the parts
+// summed in order. act_post[row] = row scale / the prescale (a power of two: exact).
 __global__ void __launch_bounds__(256) act_digitize_kernel(const float* x, int m, int k, int kblocks, uint8_t* act,
-                                                          float* act_pre) {
+                                                          float* act_post, const float* sumsq, int nparts, int ld,
+                                                          int pdl) {
   __shared__ float red[8];
   const int row = blockIdx.x, tid = threadIdx.x;
+  if (pdl) {
+    pdl_wait();
+    pdl_launch_next();
+  }
   const bool live = row < m;
   const float* xr = x + (int64_t)row * k;
   float mx = 0.f;
@@ -231,7 +274,15 @@ __global__ void __launch_bounds__(256) act_digitize_kernel(const float* x, int m
 #pragma unroll
   for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
   const float p = block_prescale(mx);
-  if (tid == 0) act_pre[row] = p;
+  if (tid == 0) {
+    float rs = 1.f;
+    if (sumsq && live) {
+      float t = 0.f;
+      for (int q = 0; q < nparts; ++q) t += sumsq[(int64_t)q * ld + row];
+      rs = 1.f / sqrtf(t + 1e-6f);
+    }
+    act_post[row] = rs * (1.f / p);
+  }
   const int groups = k / 16, i = row % kActRows;
   uint8_t* units = act + (int64_t)(row / kActRows) * kblocks * kActUnitBytes;
   for (int g0 = 0; g0 < groups; g0 += 64) {   // 64 groups per pass, a quad each; every lane takes part
@@ -264,32 +315,56 @@ int64_t gemm_act_bytes(int m, int k) {
   return (int64_t)((m + kActRows - 1) / kActRows) * packed_kblocks(k) * kActUnitBytes;
 }
 
-void gemm_digitize(const float* x, int m, int k, uint8_t* act, float* act_pre, cudaStream_t s) {
+void gemm_digitize(const float* x, int m, int k, uint8_t* act, float* act_post, cudaStream_t s, const float* sumsq,
+                   int nparts, int ld, bool pdl) {
   XTG_REQUIRE(m >= 1 && k % 16 == 0, "gemm: m >= 1 rows, k a multiple of 16");
   const int atiles = (m + kActRows - 1) / kActRows;
-  act_digitize_kernel<<<atiles * kActRows, 256, 0, s>>>(x, m, k, packed_kblocks(k), act, act_pre);
-  XTG_CUDA(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(atiles * kActRows);
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, act_digitize_kernel, x, m, k, packed_kblocks(k), act, act_post, sumsq, nparts, ld,
+                              pdl ? 1 : 0));
 }
 
-void launch_gemm(const uint8_t* w, int wtiles, int kblocks, const uint8_t* act, const float* act_pre, int m,
-                 const TileOut* outs, int num_sms, int* err, cudaStream_t s) {
+void launch_gemm(const uint8_t* w, int wtiles, int kblocks, const uint8_t* act, const float* act_post, int m,
+                 const TileOut* outs, int num_sms, int* err, cudaStream_t s, int ksplit, int64_t split_stride,
+                 bool pdl) {
   XTG_REQUIRE(m >= 1 && wtiles >= 1 && kblocks >= 1, "gemm: empty problem");
+  XTG_REQUIRE(ksplit >= 1 && ksplit <= kblocks, "gemm: 1..kblocks K parts");
   GemmParams P = {};
   P.w = w;
   P.wtiles = wtiles;
   P.kblocks = kblocks;
   P.act = act;
-  P.act_pre = act_pre;
+  P.act_post = act_post;
   P.atiles = (m + kActRows - 1) / kActRows;
   P.m = m;
   P.outs = outs;
+  P.ksplit = ksplit;
+  P.split_stride = split_stride;
+  P.pdl = pdl ? 1 : 0;
   P.err = err;
   const size_t smem = (size_t)kGStages * kGStageBytes + (2 * kGStages + 8) * 8;
   static std::atomic<uint64_t> optin{0};
   ensure_smem_optin((const void*)gemm_kernel, (int)smem, optin);
-  const int ntiles = wtiles * P.atiles;
-  gemm_kernel<<<std::min(ntiles, num_sms), kGThreads, smem, s>>>(P);
-  XTG_CUDA(cudaGetLastError());
+  const int ntiles = wtiles * ksplit * P.atiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(std::min(ntiles, num_sms));
+  cfg.blockDim = dim3(kGThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, gemm_kernel, P));
 }
 
 }  // namespace xtg

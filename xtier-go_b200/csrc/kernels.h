@@ -122,12 +122,17 @@ void digitize_rows(const float* x, int m, int k, uint8_t* xb, float* xb_pre, cud
 
 // ---- the GEMM (gemm.cu): y[m][n] = x[m][k] W^T for prefill chunks and batches ----
 constexpr int kMaxGemmRows = 65536;
-// Activation units: [ceil(m / 64)][kblocks] of 9216 bytes (4 digits x 64 rows per unit) and a prescale per row.
+// Activation units: [ceil(m / 64)][kblocks] of 9216 bytes (4 digits x 64 rows per unit) and a factor per row
+// (1 / its power-of-two prescale, times an optional row scale).
 int gemm_padded_rows(int m);   // rows of the activation tiles (a multiple of 64)
 int64_t gemm_act_bytes(int m, int k);
-void gemm_digitize(const float* x, int m, int k, uint8_t* act, float* act_pre, cudaStream_t s);
-// weights: the packed units of wtiles tiles; outs[t] as for the GEMV's STORE epilogue (y[row * ld + r])
-void launch_gemm(const uint8_t* w, int wtiles, int kblocks, const uint8_t* act, const float* act_pre, int m,
-                 const TileOut* outs, int num_sms, int* err, cudaStream_t s);
+// sumsq (optional): the row scale 1 / sqrt(sum_p sumsq[p * ld + row] + 1e-6) (a justnorm of x) goes into act_post
+void gemm_digitize(const float* x, int m, int k, uint8_t* act, float* act_post, cudaStream_t s,
+                   const float* sumsq = nullptr, int nparts = 0, int ld = 0, bool pdl = false);
+// weights: the packed units of wtiles tiles; outs[t] as for the GEMV's STORE epilogue (y[row * ld + r]); ksplit > 1:
+// each tile's K blocks in ksplit parts, part ks written split_stride floats further (partial sums)
+void launch_gemm(const uint8_t* w, int wtiles, int kblocks, const uint8_t* act, const float* act_post, int m,
+                 const TileOut* outs, int num_sms, int* err, cudaStream_t s, int ksplit = 1, int64_t split_stride = 0,
+                 bool pdl = false);
 
 }  // namespace xtg

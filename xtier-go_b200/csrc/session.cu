@@ -13,7 +13,9 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -22,6 +24,7 @@
 #include "common.cuh"
 #include "elementwise.h"
 #include "fp4mma.cuh"
+#include "batch.h"
 #include "json.h"
 #include "nccl_rt.h"
 #include "sampling.h"
@@ -46,6 +49,7 @@ struct Config {
   int decode_rows = 8;
   int device = 0;
   bool graph = true, pdl = true;
+  bool batch = true;   // xtg_cuda_forward_batch steps sessions over one weight set together (batch.h)
   int splits_global = 0, splits_ring = 0;   // 0: chosen from the SM count
   // batch-1 split-KV across processes (one GPU each): every process holds the whole model and every cache and runs
   // the whole step, but attends only its share of each global cache's chunks; the attention partials of the global
@@ -137,6 +141,7 @@ Config parse_config(const std::string& options) {
   c.device = (int)o.number("device", c.device);
   c.graph = o.number("graph", 1) != 0;
   c.pdl = o.number("pdl", 1) != 0;
+  c.batch = o.number("batch", 1) != 0;
   c.splits_global = (int)o.number("splits_global", 0);
   c.splits_ring = (int)o.number("splits_ring", 0);
   c.kv_world = (int)o.number("kv_world", 1);
@@ -231,6 +236,7 @@ struct xtg_cuda {
   int32_t* ring_pos_dev = nullptr;
   std::vector<int64_t> ring_pos;
   int64_t n_past = 0;
+  uint64_t generation = 0;   // advanced when the caches move (a tier change): a batched step built over them is stale
   std::vector<Snap> snaps;
   int last_rows = 0;
   // activations and scratch
@@ -1021,6 +1027,7 @@ struct xtg_cuda {
       k = next[i++];
     }
     c.context = ctx;
+    ++generation;
     for (Snap& s : snaps)   // a smaller tier drops what it cannot hold
       if (s.pos > ctx) s.pos = -1;
     if (exec) {   // the graph holds the old caches' addresses
@@ -1075,6 +1082,383 @@ struct xtg_cuda {
   }
 };
 
+// ---- the batched verify step (batch.h): S sessions over one weight set, one step for all of them ----
+// Every projection is one tcgen05 GEMM over the S sessions' 8 S activation rows (the weights stream once per step for
+// all of them; K split so that a GEMM of few weight tiles still spreads over the SMs); embedding, q / k / v
+// preparation with the KV store, SwiGLU and the logit scale run as the batch kernels, the attention and its combine
+// per sequence over that session's own caches (grid z = sequence), the nGPT residual updates per row. Each session
+// keeps its caches, ring table, snapshots and position; its step is the same arithmetic as its own forward (the
+// activations as the GEMM's 4 digits per value, one prescale per row). Captured once into a CUDA graph per set of
+// sessions.
+struct BatchStep {
+  xtg_cuda* model = nullptr;   // the first session: the weights every session shares
+  std::vector<xtg_cuda*> seqs;
+  std::vector<uint64_t> gens;
+  int S = 0, H = 0, F = 0, Q = 0, KV = 0, proj_ld = 0, splits_g = 1, splits_r = 1;
+  cudaStream_t stream = nullptr;
+  std::vector<void*> allocs;
+  StepParams* params_dev = nullptr;
+  StepParams* params_host = nullptr;
+  float *h = nullptr, *state = nullptr, *input = nullptr, *o = nullptr, *proj = nullptr, *q_prep = nullptr;
+  float *k_new = nullptr, *v_new = nullptr, *att = nullptr, *asum = nullptr, *gu = nullptr, *logits = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr, *act_post = nullptr, *part = nullptr;
+  uint8_t* act = nullptr;
+  int32_t* argmax = nullptr;
+  int32_t** ring_tab = nullptr;
+  KvSeq* kvseq = nullptr;                    // [attention evaluations][S]
+  std::vector<TileOut*> outs_a, outs_b;      // per evaluation: qkvg | gate/up, o | down
+  TileOut* outs_head = nullptr;
+  int* dev_err = nullptr;
+  int* err_host = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  static constexpr int kRows = 64;           // one GEMM activation tile
+  int ks_qkv = 2, ks_o = 6, ks_gu = 1, ks_down = 6;
+
+  template <class T>
+  T* alloc(size_t n) {
+    void* p = nullptr;
+    XTG_CUDA(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)));
+    allocs.push_back(p);
+    XTG_CUDA(cudaMemsetAsync(p, 0, std::max<size_t>(n, 1) * sizeof(T), stream));
+    return static_cast<T*>(p);
+  }
+  template <class T>
+  T* upload(const std::vector<T>& v) {
+    T* p = alloc<T>(v.size());
+    XTG_CUDA(cudaMemcpyAsync(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, stream));
+    XTG_CUDA(cudaStreamSynchronize(stream));
+    return p;
+  }
+
+  ~BatchStep() {
+    if (stream) cudaStreamSynchronize(stream);
+    if (exec) cudaGraphExecDestroy(exec);
+    for (void* p : allocs) cudaFree(p);
+    if (params_host) cudaFreeHost(params_host);
+    if (err_host) cudaFreeHost(err_host);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  // K parts of a GEMM over wtiles weight tiles: enough (weight tile, K part) pairs to cover the SMs
+  static int ksplit_for(int wtiles, int kblocks, int sms) {
+    return std::max(1, std::min(kblocks / 4, sms / std::max(1, wtiles)));
+  }
+
+  void build(const std::vector<xtg_cuda*>& sessions) {
+    seqs = sessions;
+    S = (int)seqs.size();
+    model = seqs[0];
+    const Config& c = model->c;
+    H = c.hidden;
+    F = c.ffn;
+    Q = c.heads * c.head_dim;
+    KV = c.kv_heads * c.head_dim;
+    proj_ld = model->proj_ld;
+    for (xtg_cuda* q : seqs) gens.push_back(q->generation);
+    XTG_CUDA(cudaSetDevice(c.device));
+    XTG_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+    const int sms = model->num_sms;
+    const Eval* e_att = nullptr;
+    const Eval* e_mlp = nullptr;
+    for (const Eval& E : model->evals) (E.kind ? e_att : e_mlp) = &E;
+    if (e_att) {
+      ks_qkv = ksplit_for(e_att->qkvg.tiles, e_att->qkvg.kblocks, sms);
+      ks_o = ksplit_for(e_att->o.tiles, e_att->o.kblocks, sms);
+    }
+    if (e_mlp) {
+      ks_gu = ksplit_for(e_mlp->gu.tiles, e_mlp->gu.kblocks, sms);
+      ks_down = ksplit_for(e_mlp->down.tiles, e_mlp->down.kblocks, sms);
+    }
+    XTG_CUDA(cudaMallocHost(&params_host, sizeof(StepParams) * S));
+    std::memset(params_host, 0, sizeof(StepParams) * S);
+    params_dev = alloc<StepParams>(S);
+    const int R = kRows;
+    h = alloc<float>((size_t)R * H);
+    state = alloc<float>((size_t)R * H);
+    input = alloc<float>((size_t)R * H);
+    o = alloc<float>((size_t)std::max(ks_o, ks_down) * R * H);
+    proj = alloc<float>((size_t)ks_qkv * R * proj_ld);
+    q_prep = alloc<float>((size_t)R * Q);
+    k_new = alloc<float>((size_t)R * KV);
+    v_new = alloc<float>((size_t)R * KV);
+    att = alloc<float>((size_t)R * Q);
+    asum = alloc<float>((size_t)c.heads * R);
+    gu = alloc<float>((size_t)ks_gu * R * 2 * F);
+    logits = alloc<float>((size_t)R * c.vocab);
+    rope_cos = alloc<float>((size_t)S * 2 * kMaxRows * 64);
+    rope_sin = alloc<float>((size_t)S * 2 * kMaxRows * 64);
+    act = alloc<uint8_t>((size_t)gemm_act_bytes(R, std::max(std::max(H, F), Q)));
+    act_post = alloc<float>(R);
+    argmax = alloc<int32_t>(R);
+    dev_err = alloc<int>(1);
+    XTG_CUDA(cudaMallocHost(&err_host, sizeof(int)));
+    *err_host = 0;
+    splits_g = std::max(1, std::min(256, 2 * sms / c.kv_heads));
+    splits_r = std::max(1, std::min(256, (int)(c.ring / 64)));
+    part = alloc<float>((size_t)S * attention_part_floats(c.kv_heads, std::max(splits_g, splits_r)));
+    std::vector<int32_t*> rt;
+    for (xtg_cuda* q : seqs) rt.push_back(q->ring_pos_dev);
+    ring_tab = upload(rt);
+    std::vector<KvSeq> kt;
+    for (size_t i = 0; i < model->kv.size(); ++i)
+      for (xtg_cuda* q : seqs) {
+        const KvInst& k = q->kv[i];
+        kt.push_back(KvSeq{k.kc, k.vc, k.ks, k.vs, k.ring ? q->ring_pos_dev : nullptr, k.slots});
+      }
+    kvseq = upload(kt);
+    // the GEMMs' output tiles (this batch's buffers, the model's global scales)
+    auto tiles = [](float* y, int ld, int n, float g) {
+      std::vector<TileOut> v(packed_tiles(n, false));
+      for (int t = 0; t < (int)v.size(); ++t) v[t] = TileOut{y + 128 * t, ld, std::min(128, n - 128 * t), g, g};
+      return v;
+    };
+    for (const Eval& E : model->evals) {
+      if (E.kind == 0) {
+        std::vector<TileOut> g(E.gu.tiles);
+        for (int t = 0; t < E.gu.tiles; ++t) g[t] = TileOut{gu + 128 * t, 2 * F, 128, E.gu.g0, E.gu.g1};
+        outs_a.push_back(upload(g));
+        outs_b.push_back(upload(tiles(o, H, H, E.down.g0)));
+      } else {
+        std::vector<TileOut> v;
+        const int n_out[4] = {Q, KV, KV, Q}, col[4] = {0, Q, Q + KV, Q + 2 * KV};
+        for (int j = 0; j < 4; ++j)
+          for (const TileOut& t : tiles(proj + col[j], proj_ld, n_out[j], E.gq[j])) v.push_back(t);
+        outs_a.push_back(upload(v));
+        outs_b.push_back(upload(tiles(o, H, H, E.o.g0)));
+      }
+    }
+    outs_head = upload(tiles(logits, c.vocab, c.vocab, model->head.g0));
+    XTG_CUDA(cudaStreamSynchronize(stream));
+  }
+
+  void gemm(const Linear& L, const TileOut* outs, int ksplit, int64_t stride, bool pdl) {
+    launch_gemm(L.w, L.tiles, L.kblocks, act, act_post, kMaxRows * S, outs, model->num_sms, dev_err, stream, ksplit,
+                stride, pdl);
+  }
+
+  void enqueue() {
+    const Config& c = model->c;
+    const int M = kMaxRows * S;
+    const bool pdl = c.pdl;
+    EmbedBatchArgs ea = {};
+    ea.params = params_dev;
+    ea.nseq = S;
+    ea.head = model->head.w;
+    ea.kblocks = model->head.kblocks;
+    ea.global = model->head.g0;
+    ea.hidden = H;
+    ea.h = h;
+    ea.inv_freq = model->inv_freq;
+    ea.rope_cos = rope_cos;
+    ea.rope_sin = rope_sin;
+    ea.ring_pos = ring_tab;
+    ea.ring = c.ring;
+    launch_embed_batch(ea, stream);
+    auto resid = [&](int mode, const float* lr, int oparts) {
+      ResidArgs r = {};
+      r.mode = mode;
+      r.params = params_dev;
+      r.hidden = H;
+      r.h = h;
+      r.o = o;
+      r.lr = lr;
+      r.state = state;
+      r.input = input;
+      r.nseq = S;
+      r.o_parts = oparts;
+      r.o_stride = (int64_t)kRows * H;
+      launch_resid(r, stream, pdl);
+    };
+    int e = 0, a_i = 0;
+    auto sublayer = [&](int ei) {
+      const Eval& E = model->evals[ei];
+      gemm_digitize(h, M, H, act, act_post, stream, nullptr, 0, 0, pdl);
+      if (E.kind == 0) {
+        gemm(E.gu, outs_a[ei], ks_gu, (int64_t)kRows * 2 * F, pdl);
+        SwigluBatchArgs sa = {};
+        sa.params = params_dev;
+        sa.nseq = S;
+        sa.gu = gu;
+        sa.ksplit = ks_gu;
+        sa.split_stride = (int64_t)kRows * 2 * F;
+        sa.features = F;
+        sa.sg = E.sg;
+        sa.su = E.su;
+        sa.act = act;
+        sa.act_post = act_post;
+        sa.pdl = pdl;
+        launch_swiglu_batch(sa, stream);
+        gemm(E.down, outs_b[ei], ks_down, (int64_t)kRows * H, pdl);
+        resid(kResidSlerp, E.lr, ks_down);
+        return;
+      }
+      gemm(E.qkvg, outs_a[ei], ks_qkv, (int64_t)kRows * proj_ld, pdl);
+      QkvPrepArgs qa = {};
+      qa.params = params_dev;
+      qa.nseq = S;
+      qa.proj = proj;
+      qa.proj_ld = proj_ld;
+      qa.ksplit = ks_qkv;
+      qa.split_stride = (int64_t)kRows * proj_ld;
+      qa.heads = c.heads;
+      qa.kv_heads = c.kv_heads;
+      qa.rope_cos = rope_cos;
+      qa.rope_sin = rope_sin;
+      qa.theta = E.theta;
+      qa.qscale = E.qscale;
+      qa.q_out = q_prep;
+      qa.k_out = k_new;
+      qa.v_out = v_new;
+      qa.seqs = kvseq + (size_t)E.cache * S;
+      qa.ring = E.kind == 1;
+      qa.dtype = c.kv_dtype;
+      qa.pdl = pdl;
+      launch_qkv_prep(qa, stream);
+      const bool ring = E.kind == 1;
+      AttnArgs at = {};
+      at.q = q_prep;
+      at.k = k_new;
+      at.v = v_new;
+      at.ring = ring ? 1 : 0;
+      at.dtype = c.kv_dtype;
+      at.window = ring ? c.window : 0;
+      at.scale = 1.f / std::sqrt((float)c.head_dim);
+      at.params = params_dev;
+      at.heads = c.heads;
+      at.kv_heads = c.kv_heads;
+      at.splits = ring ? splits_r : splits_g;
+      at.slots = 64;   // per sequence from seqs
+      at.part = part;
+      at.err = dev_err;
+      at.seqs = kvseq + (size_t)E.cache * S;
+      at.nseq = S;
+      at.part_seq_stride = attention_part_floats(c.kv_heads, std::max(splits_g, splits_r));
+      launch_attention(at, stream, pdl);
+      CombineArgs cb = {};
+      cb.part = part;
+      cb.q = q_prep;
+      cb.k = k_new;
+      cb.v = v_new;
+      cb.scale = at.scale;
+      cb.window = at.window;
+      cb.splits = at.splits;
+      cb.heads = c.heads;
+      cb.kv_heads = c.kv_heads;
+      cb.params = params_dev;
+      cb.gate = proj + Q + 2 * KV;   // the gate columns (K part 0; the parts are summed below)
+      cb.gate_ld = proj_ld;
+      cb.gscale = E.gscale;
+      cb.asum = asum;
+      cb.asum_ld = kRows;
+      cb.gated_out = att;
+      cb.nseq = S;
+      cb.part_seq_stride = at.part_seq_stride;
+      cb.err = dev_err;
+      launch_attn_combine(cb, stream, pdl);
+      gemm_digitize(att, M, Q, act, act_post, stream, asum, c.heads, kRows, pdl);
+      gemm(E.o, outs_b[ei], ks_o, (int64_t)kRows * H, pdl);
+      resid(kResidSlerp, E.lr, ks_o);
+      ++a_i;
+    };
+    for (int l = 0; l < c.n_in; ++l) sublayer(e++);
+    if (c.loops > 0) {
+      resid(kResidLoopBegin, nullptr, 1);
+      for (int i = 0; i < c.loops; ++i) {
+        for (int r = 0; r < c.n_rec; ++r) sublayer(e++);
+        resid(i + 1 < c.loops ? kResidLoopNext : kResidLoopEnd, nullptr, 1);
+      }
+    }
+    for (int l = 0; l < c.n_out; ++l) sublayer(e++);
+    gemm_digitize(h, M, H, act, act_post, stream, nullptr, 0, 0, pdl);
+    gemm(model->head, outs_head, 1, 0, pdl);
+    ScaleArgmaxArgs sa = {};
+    sa.params = params_dev;
+    sa.nseq = S;
+    sa.logits = logits;
+    sa.vocab = c.vocab;
+    sa.logit_scale = model->logit_scale;
+    sa.argmax = argmax;
+    sa.pdl = pdl;
+    launch_scale_argmax(sa, stream);
+    // each session's rows and argmax into its own buffers (xtg_cuda_argmax / xtg_cuda_topk read the last step there)
+    for (int i = 0; i < S; ++i) {
+      XTG_CUDA(cudaMemcpyAsync(seqs[i]->logits, logits + (size_t)kMaxRows * i * c.vocab,
+                               (size_t)kMaxRows * c.vocab * sizeof(float), cudaMemcpyDeviceToDevice, stream));
+      XTG_CUDA(cudaMemcpyAsync(seqs[i]->argmax, argmax + kMaxRows * i, kMaxRows * sizeof(int32_t),
+                               cudaMemcpyDeviceToDevice, stream));
+    }
+  }
+
+  void capture() {
+    if (exec) return;
+    cudaGraph_t g = nullptr;
+    XTG_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      XTG_CUDA(cudaMemcpyAsync(params_dev, params_host, sizeof(StepParams) * S, cudaMemcpyHostToDevice, stream));
+      enqueue();
+    } catch (...) {
+      cudaStreamEndCapture(stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    XTG_CUDA(cudaStreamEndCapture(stream, &g));
+    cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    XTG_CUDA(e);
+  }
+
+  bool stale() const {
+    for (size_t i = 0; i < seqs.size(); ++i)
+      if (seqs[i]->generation != gens[i]) return true;
+    return false;
+  }
+};
+
+namespace {
+
+// The batched steps built so far, by their sessions (in call order). A session's close or tier change drops those it
+// is in; one engine thread uses them at a time (the plugin's threading rule).
+std::mutex g_batches_mu;
+std::map<std::vector<xtg_cuda*>, std::unique_ptr<BatchStep>> g_batches;
+
+void drop_batches_of(xtg_cuda* h) {
+  std::lock_guard<std::mutex> lock(g_batches_mu);
+  for (auto it = g_batches.begin(); it != g_batches.end();)
+    if (std::find(it->first.begin(), it->first.end(), h) != it->first.end())
+      it = g_batches.erase(it);
+    else
+      ++it;
+}
+
+BatchStep* batch_for(const std::vector<xtg_cuda*>& key) {
+  std::lock_guard<std::mutex> lock(g_batches_mu);
+  auto it = g_batches.find(key);
+  if (it != g_batches.end() && it->second->stale()) {
+    g_batches.erase(it);
+    it = g_batches.end();
+  }
+  if (it == g_batches.end()) {
+    auto b = std::make_unique<BatchStep>();
+    b->build(key);
+    it = g_batches.emplace(key, std::move(b)).first;
+  }
+  return it->second.get();
+}
+
+// sessions that can step as one: one weight set, one device, one KV format, graphs on, one process each
+bool batchable(xtg_cuda* const* hs, int nh) {
+  if (nh < 2) return false;
+  for (int i = 0; i < nh; ++i) {
+    const Config& c = hs[i]->c;
+    if (!c.batch || !c.graph || c.kv_world != 1 || hs[i]->wmem != hs[0]->wmem || c.device != hs[0]->c.device ||
+        c.kv_dtype != hs[0]->c.kv_dtype || c.decode_rows != hs[0]->c.decode_rows)
+      return false;
+  }
+  return true;
+}
+
+}  // namespace
+
 namespace {
 
 void set_err(char* err, int len, const char* what) {
@@ -1089,6 +1473,74 @@ int guarded(char* err, int err_len, F&& f) {
   } catch (const std::exception& e) {
     set_err(err, err_len, e.what());
     return -1;
+  }
+}
+
+// xtg_cuda_forward_batch over sessions that step as one (batchable): groups of up to kMaxBatch sessions, in call
+// order, each group one batched step per round on its own stream; every group's round is in flight before the first
+// wait. A round's rows: session i's next min(decode_rows, what is left) tokens, none once it is done.
+void run_batched(xtg_cuda* const* hs, int nh, const int32_t* const* tokens, const int* n, int want,
+                 xtg_cuda_logits_fn fn, void* user, const std::vector<int>& base) {
+  std::vector<BatchStep*> groups;
+  for (int g0 = 0; g0 < nh; g0 += kMaxBatch) {
+    const std::vector<xtg_cuda*> key(hs + g0, hs + std::min(nh, g0 + kMaxBatch));
+    groups.push_back(batch_for(key));
+  }
+  XTG_CUDA(cudaSetDevice(hs[0]->c.device));
+  const int rows = hs[0]->c.decode_rows;
+  for (int off = 0;; off += rows) {
+    bool any = false;
+    for (size_t gi = 0; gi < groups.size(); ++gi) {
+      BatchStep* b = groups[gi];
+      bool live = false;
+      for (int k = 0; k < b->S; ++k) {
+        const int i = (int)gi * kMaxBatch + k;
+        xtg_cuda* h = hs[i];
+        StepParams& p = b->params_host[k];
+        std::memset(&p, 0, sizeof(p));
+        const int m = off < n[i] ? std::min(rows, n[i] - off) : 0;
+        for (int r = 0; r < m; ++r) p.tokens[r] = tokens[i][off + r];
+        p.m = m;
+        p.pos0 = h->n_past;
+        live |= m > 0;
+      }
+      if (!live) continue;
+      any = true;
+      b->capture();
+      XTG_CUDA(cudaGraphLaunch(b->exec, b->stream));
+      for (int k = 0; k < b->S; ++k) {
+        const int i = (int)gi * kMaxBatch + k, m = b->params_host[k].m;
+        const int r0 = want == 2 ? 0 : (want == 1 && off + m == n[i] ? m - 1 : m);
+        xtg_cuda* h = hs[i];
+        if (m > 0 && r0 < m && fn)
+          XTG_CUDA(cudaMemcpyAsync(h->logits_host + (size_t)r0 * h->c.vocab, h->logits + (size_t)r0 * h->c.vocab,
+                                   (size_t)(m - r0) * h->c.vocab * sizeof(float), cudaMemcpyDeviceToHost, b->stream));
+      }
+      XTG_CUDA(cudaMemcpyAsync(b->err_host, b->dev_err, sizeof(int), cudaMemcpyDeviceToHost, b->stream));
+    }
+    if (!any) break;
+    std::string failed;
+    for (size_t gi = 0; gi < groups.size(); ++gi) {
+      BatchStep* b = groups[gi];
+      XTG_CUDA(cudaStreamSynchronize(b->stream));
+      if (*b->err_host) {
+        *b->err_host = 0;
+        XTG_CUDA(cudaMemsetAsync(b->dev_err, 0, sizeof(int), b->stream));
+        if (failed.empty()) failed = "a device wait timed out during a batched step (results discarded)";
+        continue;
+      }
+      for (int k = 0; k < b->S; ++k) {
+        const int i = (int)gi * kMaxBatch + k, m = b->params_host[k].m;
+        if (m == 0) continue;
+        xtg_cuda* h = hs[i];
+        h->commit(m);
+        h->last_rows = m;
+        const int r0 = want == 2 ? 0 : (want == 1 && off + m == n[i] ? m - 1 : m);
+        if (fn)
+          for (int r = r0; r < m; ++r) fn(base[(size_t)i] + off + r, h->logits_host + (size_t)r * h->c.vocab, user);
+      }
+    }
+    if (!failed.empty()) throw CudaError(failed);
   }
 }
 
@@ -1147,6 +1599,7 @@ xtg_cuda* xtg_cuda_open_shared(xtg_cuda* owner, const char* options, char* err, 
     h->c.decode_rows = o.decode_rows;
     h->c.graph = o.graph;
     h->c.pdl = o.pdl;
+    h->c.batch = o.batch;
     h->c.splits_global = o.splits_global;
     h->c.splits_ring = o.splits_ring;
     h->c.kv_world = 1;
@@ -1217,6 +1670,10 @@ int xtg_cuda_forward_batch(xtg_cuda* const* hs, int nh, const int32_t* const* to
     // as forward() does: a session given no tokens keeps its snapshots
     for (int i = 0; i < nh; ++i)
       if (n[i] > 0) hs[i]->drop_snapshots_past();
+    if (batchable(hs, nh)) {
+      run_batched(hs, nh, tokens, n, want, fn, user, base);
+      return;
+    }
     std::string failed;
     std::vector<xtg_cuda::Chunk> ks((size_t)nh);
     for (int step = 0;; ++step) {
@@ -1311,6 +1768,7 @@ int64_t xtg_cuda_debug_cache(xtg_cuda* h, int instance, int value, void* out, in
 void xtg_cuda_close(xtg_cuda* h) {
   if (!h) return;
   cudaSetDevice(h->c.device);
+  drop_batches_of(h);
   delete h;
 }
 
