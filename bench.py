@@ -315,6 +315,16 @@ def max_over_ranks(v, dist, device="cuda"):
     return float(t.item())
 
 
+def sum_over_ranks(v, dist, device="cuda"):
+    """The sum over every rank (an all-reduce; NCCL on GPUs, gloo in the CPU tests)."""
+    import torch
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 GEMM_SETS = [("qkvg", [3072, 768, 768, 3072], 3072), ("o", [3072], 3072), ("gate_up", [9216, 9216], 3072),
              ("down", [3072], 9216)]
 
@@ -595,6 +605,69 @@ def rates(world, ms_per_step):
             "accepted_per_step": acc}
 
 
+def config4_draws(rank, world, steps, seqs_total):
+    """This rank's share of config 4's seeded acceptances: sequences rank * per_gpu .. (rank + 1) * per_gpu - 1 of the
+    [steps][seqs_total] draws (the same draws whatever the partition)."""
+    per_gpu = seqs_total // world
+    return acceptance_draws(steps * seqs_total).reshape(steps, seqs_total)[:, rank * per_gpu:(rank + 1) * per_gpu]
+
+
+def config4_block(x, rank, world, local_rank, dist, steps=256, seqs_total=64, context=32768, prefill=30000):
+    """64 independent sequences of the config-3 model at the 32K tier, each prefilled to 30000
+    positions, partitioned over the N GPUs (64 / N per GPU, no collective on the data path). 256 verify rounds: every
+    sequence verifies 8 rows (xtg_cuda_forward_batch: the sessions step as batched steps of up to 8 sequences, each
+    projection one tcgen05 GEMM over their rows), its 8 argmax tokens are read back, and a seeded acceptance of 1..4
+    tokens (numpy PCG64, seed 4, one draw per sequence and round) drives its rewind to base + accepted. Wall clock around
+    the rounds, max over ranks."""
+    per_gpu = seqs_total // world
+    model = dict(x.DORY_3072)
+    acc = config4_draws(rank, world, steps, seqs_total)
+    owner = x.Session(model, context=context, device=local_rank)
+    sessions = [owner] + [x.Session.shared(owner, context=context) for _ in range(per_gpu - 1)]
+    try:
+        for s in sessions:
+            s.prefill_synthetic(prefill)
+        lists = [TOKENS] * per_gpu
+        for _ in range(2):   # warm-up (the batched graphs are captured here)
+            x.forward_batch(sessions, lists, want=0)
+            for s in sessions:
+                s.argmax(8)
+                s.rewind(prefill)
+        dist_barrier(dist)
+        base = [prefill] * per_gpu
+        t0 = time.perf_counter()
+        for st in range(steps):
+            x.forward_batch(sessions, lists, want=0)
+            for j, s in enumerate(sessions):
+                s.argmax(8)
+                base[j] += int(acc[st, j])
+                assert s.rewind(base[j])
+        wall = time.perf_counter() - t0
+        dist_barrier(dist)
+        wall = max_over_ranks(wall, dist)
+        accepted = sum_over_ranks(float(acc.sum()), dist)   # every rank's own draws
+        kv = sessions[0].step_bytes(2, 8)   # one sequence's KV read per round at its last position
+        weights = sessions[0].step_bytes(1, 8)
+        groups = (per_gpu + 7) // 8
+    finally:
+        for s in sessions:
+            s.close()
+    rows = 8.0 * per_gpu * steps / wall
+    peak, peak_kind = peaks()
+    bytes_round = groups * weights + per_gpu * kv
+    return {"sequences": seqs_total, "per_gpu": per_gpu, "context": context, "prefill": prefill, "steps": steps,
+            "wall_s": wall, "rows_per_s_per_gpu": rows, "job_rows_per_s": rows * world,
+            "accepted_tok_per_s_per_gpu": accepted / world / wall, "job_accepted_tok_per_s": accepted / wall,
+            "mean_accepted_per_round": float(acc.mean()), "ms_per_round": wall / steps * 1e3,
+            "batched_groups_per_gpu": groups,
+            "roofline": {"bound": "hbm", "bytes_per_round_per_gpu": bytes_round,
+                         "note": "weights once per batched group of 8 + every sequence's KV (at its final position)",
+                         "achieved": bytes_round / (wall / steps) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": bytes_round / (wall / steps) / 1e9 / peak, "peak_kind": peak_kind},
+            "e2e": {"h2d_bytes_per_round": per_gpu * 48, "d2h_bytes_per_round": per_gpu * 8 * 4,
+                    "note": "the rounds above are end to end: host tokens in, each session's argmax read back"}}
+
+
 def job_rows_per_s(world, ms_per_step):
     """Whole-job throughput: every rank verifies 8 rows of its own sequence per step (weak scaling)."""
     return world * 8.0 / (ms_per_step / 1e3)
@@ -656,6 +729,7 @@ def run_ours(args, rank, world, local_rank, dist):
     info = s.info()
     shared = shared_sessions_block(x, s, dist, args.steps)
     s.close()
+    cfg4 = None if args.no_config4 else config4_block(x, rank, world, local_rank, dist, steps=args.config4_steps)
     topk_t = topk_block(x, f"cuda:{local_rank}", model["vocab"]) if world == 1 else None
     gemm = gemm_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg0 = config0_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
@@ -695,6 +769,11 @@ def run_ours(args, rank, world, local_rank, dist):
         "config": "4 independent sequences per GPU over one weight set (xtg_cuda_open_shared), 8K tier, each "
                   "stepping concurrently on its own stream; wall clock", **shared,
         "job_rows_per_s": world * shared["rows_per_s_per_gpu"], "vs_one_session": shared["rows_per_s_per_gpu"] / (value / world)}
+    if cfg4:
+        line["config4"] = {"config": "config4: 64 sequences of the config-3 model at the 32K tier (30000 prefilled), "
+                                     "partitioned over the GPUs, 8-row verify rounds through xtg_cuda_forward_batch "
+                                     "(batched steps of up to 8 sequences), argmax read back, seeded 1..4 acceptance "
+                                     "driving rewinds; wall clock, max over ranks", **cfg4}
     if cfg0:
         line["config0_gemv"] = {"config": "config0: one NVFP4 GEMV, M = 1, 16 weight copies rotated", **cfg0}
     if cfg2:
@@ -736,6 +815,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-1 M=512 prefill GEMM measurement")
+    ap.add_argument("--no-config4", action="store_true", help="skip the config-4 batched serving measurement")
+    ap.add_argument("--config4-steps", type=int, default=256, help="verify rounds of the config-4 measurement")
     ap.add_argument("--split-kv-max", type=int, default=4,
                     help="largest world size at which the batch-1 split-KV step is measured (N > 1)")
     ap.add_argument("--ncu-steps", type=int, default=0,

@@ -26,7 +26,9 @@ def _rank(rank, world, port, times, out):
     try:
         bench.dist_barrier(dist, device="cpu")
         ms = bench.max_over_ranks(times[rank], dist, device="cpu")
-        out[rank] = (ms, bench.job_rows_per_s(world, ms))
+        acc = bench.config4_draws(rank, world, 16, 64)
+        total = bench.sum_over_ranks(float(acc.sum()), dist, device="cpu")
+        out[rank] = (ms, bench.job_rows_per_s(world, ms), acc.shape, total)
         bench.dist_barrier(dist, device="cpu")
     finally:
         dist.destroy_process_group()
@@ -38,7 +40,16 @@ def test_two_ranks_agree_on_the_slowest_step():
         out = mgr.dict()
         mp.spawn(_rank, args=(world, _free_port(), times, out), nprocs=world, join=True)
         res = dict(out)
-    assert res[0] == res[1] == (5.5, pytest.approx(2 * 8 / 5.5e-3))
+    everyone = float(bench_module().acceptance_draws(16 * 64).sum())
+    for r in (0, 1):   # config 4: each rank its 32 sequences' draws, the job's sum the same as one GPU's
+        assert res[r][:2] == (5.5, pytest.approx(2 * 8 / 5.5e-3))
+        assert res[r][2] == (16, 32) and res[r][3] == everyone
+
+
+def bench_module():
+    sys.path.insert(0, ROOT)
+    import bench
+    return bench
 
 
 def test_one_rank_needs_no_process_group():
