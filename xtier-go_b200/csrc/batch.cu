@@ -14,6 +14,8 @@ namespace xtg {
 
 namespace {
 
+constexpr int kMaxClusterRanks = 8;
+
 template <class Args>
 void launch_with_pdl(void (*kernel)(Args), dim3 grid, dim3 block, size_t smem, const Args& args, cudaStream_t s,
                      bool pdl) {
@@ -39,9 +41,11 @@ __device__ __forceinline__ float head_weight(const uint8_t* w, int kblocks, floa
   return __fmul_rn(e2m1_to_f32((kk & 1) ? byte >> 4 : byte & 15), s);
 }
 
-// grid (8, nseq): row i of sequence s
+// grid (8, nseq): row i of sequence s; the row is digitized for the first GEMM too (its max sets its prescale)
 __global__ void embed_batch_kernel(const EmbedBatchArgs a) {
-  const int i = blockIdx.x, s = blockIdx.y;
+  extern __shared__ float hrow[];   // [hidden]
+  __shared__ float red[8];
+  const int i = blockIdx.x, s = blockIdx.y, r = kMaxRows * s + i;
   if (a.pdl) {
     pdl_wait();
     pdl_launch_next();
@@ -49,10 +53,33 @@ __global__ void embed_batch_kernel(const EmbedBatchArgs a) {
   const StepParams& p = a.params[s];
   const int m = p.m;
   const int64_t pos0 = p.pos0;
-  float* h = a.h + (int64_t)(8 * s + i) * a.hidden;
+  float* h = a.h + (int64_t)r * a.hidden;
   const int tok = i < m ? p.tokens[i] : 0;
-  for (int k = threadIdx.x; k < a.hidden; k += blockDim.x)
-    h[k] = i < m ? head_weight(a.head, a.kblocks, a.global, tok, k) : 0.f;
+  float mx = 0.f;
+  for (int k = threadIdx.x; k < a.hidden; k += blockDim.x) {
+    const float v = i < m ? head_weight(a.head, a.kblocks, a.global, tok, k) : 0.f;
+    h[k] = v;
+    hrow[k] = v;
+    mx = fmaxf(mx, fabsf(v));
+  }
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+  const float pre = block_prescale(mx);
+  if (threadIdx.x == 0) a.act_post[r] = 1.f / pre;
+  const int groups = a.hidden / 16;
+  for (int g0 = 0; g0 < groups; g0 += (int)blockDim.x / 4) {   // a quad per group; every lane takes part
+    const int g = g0 + (int)(threadIdx.x >> 2), t = threadIdx.x & 3;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (g < groups)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) v[c] = hrow[16 * g + 4 * t + c];
+    uint32_t code[kGemmDigits], sf[kGemmDigits];
+    digitize16_quad_n<kGemmDigits>(v, code, sf, pre);
+    if (g < groups) store_gemm_digits_quad(a.act, r, g, t, code, sf);
+  }
   // this row's RoPE factors for both thetas (FP32(pos) * inv_freq, then cos / sin)
   for (int e = threadIdx.x; e < 2 * 64; e += blockDim.x) {
     const int th = e >> 6, f = e & 63;
@@ -146,75 +173,143 @@ __global__ void __launch_bounds__(128) qkv_prep_kernel(const QkvPrepArgs a) {
   if (d == 0) (type == 1 ? kv.ks : kv.vs)[(int64_t)h * kv.slots + slot] = sc;
 }
 
-constexpr int kSwThreads = 1024;
-
-// one CTA per activation row (the 64 rows of the GEMM's activation tile; rows past a sequence's m, and past 8 nseq,
-// get zero digits)
-__global__ void __launch_bounds__(kSwThreads) swiglu_batch_kernel(const SwigluBatchArgs a) {
-  extern __shared__ float vrow[];   // [features]
-  __shared__ float red[32], redm[32];
-  const int r = blockIdx.x, s = r / kMaxRows, i = r % kMaxRows, F = a.features, tid = threadIdx.x;
+// One cluster of `C` CTAs per activation row (the 64 rows of the GEMM's activation tile; rows past a sequence's m,
+// and past 8 nseq, get zero digits), CTA c the features F c / C .., a thread 4 consecutive features (a quad one
+// 16-feature group). The row's sum of squares and max |v| meet over distributed shared memory (added in rank order).
+__global__ void swiglu_batch_kernel(const SwigluBatchArgs a) {
+  __shared__ float part[2][kMaxClusterRanks];
+  __shared__ float red[2][32];
+  const int tid = threadIdx.x, r = blockIdx.y, s = r / kMaxRows, i = r % kMaxRows, F = a.features;
+  const int C = (int)gridDim.x, rank = (int)cluster_rank();
+  const int f0 = rank * (F / C) + 4 * tid;
+  float sgv[4], suv[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {   // parameters: before the wait
+    sgv[c] = a.sg[f0 + c];
+    suv[c] = a.su[f0 + c];
+  }
   if (a.pdl) {
     pdl_wait();
     pdl_launch_next();
   }
   const bool live = s < a.nseq && i < a.params[s].m;
   const float* gu = a.gu + (int64_t)r * 2 * F;
-  float ss = 0.f, mx = 0.f;
-  for (int f = tid; f < F; f += kSwThreads) {
-    float v = 0.f;
-    if (live) {
-      const int base = 128 * (f >> 6) + (f & 63);
-      float gz = gu[base], gv = gu[base + 64];
-      for (int k = 1; k < a.ksplit; ++k) {   // the K parts, in order
-        gz += gu[k * a.split_stride + base];
-        gv += gu[k * a.split_stride + base + 64];
-      }
-      const float z = gz * a.sg[f];
-      const float u = gv * a.su[f];
-      v = z / (1.f + expf(-z)) * u;
+  float v[4] = {0.f, 0.f, 0.f, 0.f}, ss = 0.f, mx = 0.f;
+  if (live) {
+    const int base = 128 * (f0 >> 6) + (f0 & 63);   // 4 consecutive features share their 64-feature tile
+    float4 g4 = *reinterpret_cast<const float4*>(gu + base), u4 = *reinterpret_cast<const float4*>(gu + base + 64);
+    for (int k = 1; k < a.ksplit; ++k) {   // the K parts, in order
+      const float4 gk = *reinterpret_cast<const float4*>(gu + k * a.split_stride + base);
+      const float4 uk = *reinterpret_cast<const float4*>(gu + k * a.split_stride + base + 64);
+      g4.x += gk.x; g4.y += gk.y; g4.z += gk.z; g4.w += gk.w;
+      u4.x += uk.x; u4.y += uk.y; u4.z += uk.z; u4.w += uk.w;
     }
-    vrow[f] = v;
-    ss += v * v;
-    mx = fmaxf(mx, fabsf(v));
+    const float gz[4] = {g4.x, g4.y, g4.z, g4.w}, gv[4] = {u4.x, u4.y, u4.z, u4.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const float z = gz[c] * sgv[c];
+      const float u = gv[c] * suv[c];
+      v[c] = z / (1.f + expf(-z)) * u;
+      ss += v[c] * v[c];
+      mx = fmaxf(mx, fabsf(v[c]));
+    }
   }
   ss = warp_sum(ss);
   mx = warp_max(mx);
   if ((tid & 31) == 0) {
-    red[tid >> 5] = ss;
-    redm[tid >> 5] = mx;
+    red[0][tid >> 5] = ss;
+    red[1][tid >> 5] = mx;
   }
   __syncthreads();
-  float tot = 0.f, amax = 0.f;
-  for (int w = 0; w < kSwThreads / 32; ++w) {
-    tot += red[w];
-    amax = fmaxf(amax, redm[w]);
-  }
-  const float p = block_prescale(amax);
-  if (tid == 0) a.act_post[r] = (1.f / sqrtf(tot + 1e-6f)) * (1.f / p);
-  // the row's digits (4 per value, one prescale for the row: the GEMM's activation units)
-  constexpr int kRows = 64, kDig = 4, kCode = 256 * 32, kUnit = kCode + 2 * 512;
-  const int groups = F / 16, kblocks = (F + 63) / 64, ir = r % kRows;
-  for (int g0 = 0; g0 < groups; g0 += kSwThreads / 4) {   // a quad per group; every lane takes part
-    const int g = g0 + (tid >> 2), t = tid & 3;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (g < groups)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) v[c] = vrow[16 * g + 4 * t + c];
-    uint32_t code[kDig], sf[kDig];
-    digitize16_quad_n<kDig>(v, code, sf, p);
-    if (g < groups) {
-      uint8_t* unit = a.act + (int64_t)(g >> 2) * kUnit;
-      const int j = g & 3;
-#pragma unroll
-      for (int dd = 0; dd < kDig; ++dd) {
-        const int n = kRows * dd + ir;
-        *reinterpret_cast<uint16_t*>(unit + a_code_offset(n, 16 * j + 4 * t)) = (uint16_t)code[dd];
-        if (t == 0) unit[kCode + (n >> 7) * 512 + sf_offset(n & 127, j)] = (uint8_t)sf[dd];
-      }
+  if (tid == 0) {
+    float t = 0.f, m = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      t += red[0][w];
+      m = fmaxf(m, red[1][w]);
+    }
+    for (int q = 0; q < C; ++q) {   // this CTA's part into every rank's table
+      st_cluster_f32(&part[0][rank], (uint32_t)q, t);
+      st_cluster_f32(&part[1][rank], (uint32_t)q, m);
     }
   }
-  (void)kblocks;
+  cluster_sync();
+  float tot = 0.f, amax = 0.f;
+  for (int q = 0; q < C; ++q) {
+    tot += part[0][q];
+    amax = fmaxf(amax, part[1][q]);
+  }
+  const float p = block_prescale(amax);
+  if (rank == 0 && tid == 0) a.act_post[r] = (1.f / sqrtf(tot + 1e-6f)) * (1.f / p);
+  uint32_t code[kGemmDigits], sf[kGemmDigits];
+  digitize16_quad_n<kGemmDigits>(v, code, sf, p);   // whole warps: blockDim a multiple of 32
+  store_gemm_digits_quad(a.act, r, f0 >> 4, tid & 3, code, sf);
+}
+
+// One cluster of C CTAs per activation row, a thread 4 consecutive dims (a quad one 16-dim group): the five sums that
+// give |h|, |o| and |(1 - l) fa h + l fb o| (fa = 1 / |h|, fb = 1 / |o|) meet over distributed shared memory (added
+// in rank order), then every CTA updates and digitizes its own dims.
+__global__ void slerp_batch_kernel(const SlerpBatchArgs a) {
+  __shared__ float part[5][kMaxClusterRanks];
+  __shared__ float red[5][32];
+  const int tid = threadIdx.x, r = blockIdx.y, s = r / kMaxRows, i = r % kMaxRows, H = a.hidden;
+  const int C = (int)gridDim.x, rank = (int)cluster_rank();
+  const int d0 = rank * (H / C) + 4 * tid;
+  const float4 l4 = *reinterpret_cast<const float4*>(a.lr + d0);   // a parameter: before the wait
+  if (a.pdl) {
+    pdl_wait();
+    pdl_launch_next();
+  }
+  const bool live = i < a.params[s].m;
+  float* hr = a.h + (int64_t)r * H;
+  float4 h4 = make_float4(0.f, 0.f, 0.f, 0.f), o4 = h4;
+  if (live) {
+    h4 = *reinterpret_cast<const float4*>(hr + d0);
+    const float* orow = a.o + (int64_t)r * H;
+    o4 = *reinterpret_cast<const float4*>(orow + d0);
+    for (int q = 1; q < a.o_parts; ++q) {   // the K parts, in order
+      const float4 p4 = *reinterpret_cast<const float4*>(orow + q * a.o_stride + d0);
+      o4.x += p4.x; o4.y += p4.y; o4.z += p4.z; o4.w += p4.w;
+    }
+  }
+  const float hv[4] = {h4.x, h4.y, h4.z, h4.w}, ov[4] = {o4.x, o4.y, o4.z, o4.w}, lv[4] = {l4.x, l4.y, l4.z, l4.w};
+  float v5[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const float w = 1.f - lv[c];
+    v5[0] += hv[c] * hv[c];
+    v5[1] += ov[c] * ov[c];
+    v5[2] += w * w * hv[c] * hv[c];
+    v5[3] += lv[c] * w * hv[c] * ov[c];
+    v5[4] += lv[c] * lv[c] * ov[c] * ov[c];
+  }
+#pragma unroll
+  for (int k = 0; k < 5; ++k) v5[k] = warp_sum(v5[k]);
+  if ((tid & 31) == 0)
+#pragma unroll
+    for (int k = 0; k < 5; ++k) red[k][tid >> 5] = v5[k];
+  __syncthreads();
+  if (tid < 5) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[tid][w];
+    for (int q = 0; q < C; ++q) st_cluster_f32(&part[tid][rank], (uint32_t)q, t);
+  }
+  cluster_sync();
+  float tot[5];
+#pragma unroll
+  for (int k = 0; k < 5; ++k) {
+    tot[k] = 0.f;
+    for (int q = 0; q < C; ++q) tot[k] += part[k][q];
+  }
+  const float fa = 1.f / sqrtf(tot[0] + 1e-6f), fb = 1.f / sqrtf(tot[1] + 1e-6f);
+  const float f = 1.f / sqrtf(fa * fa * tot[2] + 2.f * fa * fb * tot[3] + fb * fb * tot[4] + 1e-6f);
+  float v[4];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) v[c] = live ? ((1.f - lv[c]) * fa * hv[c] + lv[c] * fb * ov[c]) * f : 0.f;
+  if (live) *reinterpret_cast<float4*>(hr + d0) = make_float4(v[0], v[1], v[2], v[3]);
+  uint32_t code[kGemmDigits], sf[kGemmDigits];
+  digitize16_quad_n<kGemmDigits>(v, code, sf, kUnitPrescale);   // whole warps: blockDim a multiple of 32
+  store_gemm_digits_quad(a.act, r, d0 >> 4, tid & 3, code, sf);
+  if (rank == 0 && tid == 0) a.act_post[r] = 1.f / kUnitPrescale;
 }
 
 // one CTA per activation row
@@ -275,7 +370,8 @@ __global__ void __launch_bounds__(1024) scale_argmax_kernel(const ScaleArgmaxArg
 
 void launch_embed_batch(const EmbedBatchArgs& a, cudaStream_t s) {
   XTG_REQUIRE(a.nseq >= 1 && a.nseq <= kMaxBatch, "embed_batch: 1..8 sequences");
-  launch_with_pdl(embed_batch_kernel, dim3(kMaxRows, a.nseq), dim3(256), 0, a, s, a.pdl != 0);
+  XTG_REQUIRE(a.hidden % 64 == 0 && a.hidden <= 12288, "embed_batch: hidden a multiple of 64, at most 12288");
+  launch_with_pdl(embed_batch_kernel, dim3(kMaxRows, a.nseq), dim3(256), (size_t)a.hidden * 4, a, s, a.pdl != 0);
 }
 
 void launch_qkv_prep(const QkvPrepArgs& a, cudaStream_t s) {
@@ -285,11 +381,46 @@ void launch_qkv_prep(const QkvPrepArgs& a, cudaStream_t s) {
 }
 
 void launch_swiglu_batch(const SwigluBatchArgs& a, cudaStream_t s) {
-  XTG_REQUIRE(a.features % 64 == 0 && a.features * 4 <= 200 * 1024, "swiglu_batch: features a multiple of 64");
-  static std::atomic<uint64_t> optin{0};
-  const int smem = a.features * 4;
-  if (smem > 48 * 1024) ensure_smem_optin((const void*)swiglu_batch_kernel, smem, optin);
-  launch_with_pdl(swiglu_batch_kernel, dim3(64), dim3(kSwThreads), (size_t)smem, a, s, a.pdl != 0);
+  // the cluster size: the most CTAs per row (up to 8) whose threads (4 features each) fill whole warps
+  int C = 0;
+  for (int c = kMaxClusterRanks; c >= 1 && !C; c >>= 1)
+    if (a.features % (128 * c) == 0 && a.features / c / 4 <= 1024) C = c;
+  XTG_REQUIRE(C >= 1, "swiglu_batch: features a multiple of 128, at most 4096 per CTA");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, kGemmRows);
+  cfg.blockDim = dim3(a.features / C / 4);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 2 : 1;
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, swiglu_batch_kernel, a));
+}
+
+void launch_slerp_batch(const SlerpBatchArgs& a, cudaStream_t s) {
+  int C = 0;   // the most CTAs per row (up to 8) whose threads (4 dims each) fill whole warps
+  for (int c = kMaxClusterRanks; c >= 1 && !C; c >>= 1)
+    if (a.hidden % (128 * c) == 0 && a.hidden / c / 4 <= 1024) C = c;
+  XTG_REQUIRE(C >= 1 && a.nseq >= 1 && a.nseq <= kMaxBatch && a.o_parts >= 1, "slerp_batch: hidden a multiple of 128");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(C, kMaxRows * a.nseq);
+  cfg.blockDim = dim3(a.hidden / C / 4);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 2 : 1;
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, slerp_batch_kernel, a));
 }
 
 void launch_scale_argmax(const ScaleArgmaxArgs& a, cudaStream_t s) {

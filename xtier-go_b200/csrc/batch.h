@@ -36,6 +36,8 @@ struct EmbedBatchArgs {
   float* rope_sin;
   int32_t* const* ring_pos;   // [nseq] each sequence's table (null entries: no sliding layers)
   int64_t ring;
+  uint8_t* act;               // h's digits as GEMM activation units (a prescale per row from its max)
+  float* act_post;            // [64]
   int pdl;
 };
 
@@ -90,7 +92,25 @@ struct ScaleArgmaxArgs {
   int pdl;
 };
 
+// The nGPT residual update of every live row (slerp_residual, engine/src/kernels.cpp:177-189): h <- justnorm((1 - l)
+// justnorm(h) + l justnorm(o)), o the sum of o_parts K-split partial outputs; the new h also as GEMM activation units
+// (the unit prescale).
+struct SlerpBatchArgs {
+  const StepParams* params;
+  int nseq;
+  int hidden;
+  float* h;                   // [8 nseq][hidden], updated in place
+  const float* o;
+  int o_parts;
+  int64_t o_stride;
+  const float* lr;            // [hidden]
+  uint8_t* act;
+  float* act_post;
+  int pdl;
+};
+
 void launch_embed_batch(const EmbedBatchArgs& a, cudaStream_t s);
+void launch_slerp_batch(const SlerpBatchArgs& a, cudaStream_t s);
 void launch_qkv_prep(const QkvPrepArgs& a, cudaStream_t s);
 void launch_swiglu_batch(const SwigluBatchArgs& a, cudaStream_t s);
 void launch_scale_argmax(const ScaleArgmaxArgs& a, cudaStream_t s);

@@ -239,6 +239,17 @@ __global__ void __launch_bounds__(kResidThreads) resid_kernel(const ResidArgs a)
     }
   }
   // the new h, and its digits: the quad of threads 4 g .. 4 g + 3 of chunk j holds group g + 256 j
+  if (a.gemm_act) {   // the batched step's GEMM digits of the new h (4 per value, the unit prescale)
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+      if (j * kResidThreads < H / 4) {   // whole warps take part in the quad's shuffles
+        uint32_t code[kGemmDigits], sf[kGemmDigits];
+        digitize16_quad_n<kGemmDigits>(v[j], code, sf, kUnitNorm);
+        if (ok[j]) store_gemm_digits_quad(a.gemm_act, r, ch[j] >> 2, ch[j] & 3, code, sf);
+      }
+    }
+    if (threadIdx.x == 0) a.gemm_post[r] = 1.f / kUnitNorm;
+  }
 #pragma unroll
   for (int j = 0; j < kChunks; ++j) {
     if (live && ok[j]) st4(h, ch[j], v[j]);
@@ -464,6 +475,7 @@ void launch_resid(const ResidArgs& a_in, cudaStream_t s, bool pdl) {
     return;
   }
   XTG_REQUIRE(a.nseq >= 0 && a.nseq <= 64, "resid: at most 64 sequences");
+  XTG_REQUIRE(!a.gemm_act || (a.nseq >= 1 && a.nseq <= 8 && a.gemm_post), "resid: GEMM digits for 1..8 sequences");
   if (a.o_parts < 1) a.o_parts = 1;
   launch_pdl(resid_kernel, dim3(kMaxRows * (a.nseq > 0 ? a.nseq : 1)), dim3(kResidThreads), a, s, pdl, 0);
 }

@@ -51,6 +51,10 @@ struct ResidArgs {
   int nseq;
   int o_parts;
   int64_t o_stride;
+  // the batched step: the new h's digits as GEMM activation units (fp4mma.cuh; the unit prescale for every row) and
+  // each row's factor (1 / the prescale), or null
+  uint8_t* gemm_act;
+  float* gemm_post;
 };
 
 struct KvStoreArgs {

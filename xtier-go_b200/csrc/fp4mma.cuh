@@ -211,6 +211,27 @@ __device__ __forceinline__ float digitize16_quad(const float (&x)[4], uint32_t (
   return digitize16_quad_n<kDigits>(x, code, sf, fixed);
 }
 
+// ---- the GEMM's activation units (gemm.cu): 64 activation rows x 64 inputs, 4 digits each (N = 256 digit rows,
+// digit d of row i at row 64 d + i) in the weight unit's K-major layout, then the scale atoms of digit rows 0-127 and
+// 128-255; one power-of-two prescale per activation row ----
+constexpr int kGemmDigits = 4;
+constexpr int kGemmRows = 64;
+constexpr int kGemmCodeBytes = kGemmRows * kGemmDigits * 32;   // 8192
+constexpr int kGemmUnitBytes = kGemmCodeBytes + 2 * 512;
+// Lane t of the quad stores its part of 16-input group g of activation row `row` (of the 64-row tile at act)
+__device__ __forceinline__ void store_gemm_digits_quad(uint8_t* act, int row, int g, int t,
+                                                       const uint32_t (&code)[kGemmDigits],
+                                                       const uint32_t (&sf)[kGemmDigits]) {
+  uint8_t* unit = act + (int64_t)(g >> 2) * kGemmUnitBytes;
+  const int j = g & 3, i = row % kGemmRows;
+#pragma unroll
+  for (int d = 0; d < kGemmDigits; ++d) {
+    const int n = kGemmRows * d + i;
+    *reinterpret_cast<uint16_t*>(unit + a_code_offset(n, 16 * j + 4 * t)) = (uint16_t)code[d];
+    if (t == 0) unit[kGemmCodeBytes + (n >> 7) * 512 + sf_offset(n & 127, j)] = (uint8_t)sf[d];
+  }
+}
+
 // the prescale of groups nobody wrote (all-zero digits): never the smallest of a slice
 constexpr float kEmptyPrescale = 8.507059e37f;   // 2^126
 

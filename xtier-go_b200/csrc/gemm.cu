@@ -26,11 +26,12 @@ namespace xtg {
 
 namespace {
 
-constexpr int kGDigits = 4;                       // activation digits of the B operand
+constexpr int kGDigits = kGemmDigits;             // activation digits of the B operand (fp4mma.cuh)
 constexpr int kGN = 256;                          // the MMA's N: digit rows
-constexpr int kActRows = kGN / kGDigits;          // activation rows per unit (64)
-constexpr int kActCodeBytes = kGN * 32;           // 8192
-constexpr int kActUnitBytes = kActCodeBytes + 2 * 512;
+constexpr int kActRows = kGemmRows;               // activation rows per unit (64)
+constexpr int kActCodeBytes = kGemmCodeBytes;     // 8192
+constexpr int kActUnitBytes = kGemmUnitBytes;
+static_assert(kGN == kActRows * kGDigits, "the activation unit's digit rows");
 constexpr int kGUnits = 4;      // K blocks per ring stage: one bulk copy of weight units, one of activation units
 constexpr int kGStageBytes = kGUnits * (kUnitBytes + kActUnitBytes);
 constexpr int kGStages = 3;     // ring stages (166 KB: one CTA per SM, which owns the TMEM it allocates)
@@ -294,16 +295,7 @@ __global__ void __launch_bounds__(256) act_digitize_kernel(const float* x, int m
     }
     uint32_t code[kGDigits], sf[kGDigits];
     digitize16_quad_n<kGDigits>(v, code, sf, p);
-    if (g < groups) {
-      uint8_t* unit = units + (int64_t)(g >> 2) * kActUnitBytes;
-      const int j = g & 3;
-#pragma unroll
-      for (int d = 0; d < kGDigits; ++d) {
-        const int n = kActRows * d + i;
-        *reinterpret_cast<uint16_t*>(unit + a_code_offset(n, 16 * j + 4 * t)) = (uint16_t)code[d];
-        if (t == 0) unit[kActCodeBytes + (n >> 7) * 512 + sf_offset(n & 127, j)] = (uint8_t)sf[d];
-      }
-    }
+    if (g < groups) store_gemm_digits_quad(units, i, g, t, code, sf);
   }
 }
 

@@ -1193,8 +1193,9 @@ struct BatchStep {
     dev_err = alloc<int>(1);
     XTG_CUDA(cudaMallocHost(&err_host, sizeof(int)));
     *err_host = 0;
-    splits_g = std::max(1, std::min(256, 2 * sms / c.kv_heads));
-    splits_r = std::max(1, std::min(256, (int)(c.ring / 64)));
+    // one wave of attention CTAs (2 per SM) over every sequence's KV heads
+    splits_g = std::max(1, std::min(256, 2 * sms / (c.kv_heads * S)));
+    splits_r = std::max(1, std::min(splits_g, (int)(c.ring / 64)));
     part = alloc<float>((size_t)S * attention_part_floats(c.kv_heads, std::max(splits_g, splits_r)));
     std::vector<int32_t*> rt;
     for (xtg_cuda* q : seqs) rt.push_back(q->ring_pos_dev);
@@ -1253,6 +1254,8 @@ struct BatchStep {
     ea.rope_sin = rope_sin;
     ea.ring_pos = ring_tab;
     ea.ring = c.ring;
+    ea.act = act;
+    ea.act_post = act_post;
     launch_embed_batch(ea, stream);
     auto resid = [&](int mode, const float* lr, int oparts) {
       ResidArgs r = {};
@@ -1267,12 +1270,28 @@ struct BatchStep {
       r.nseq = S;
       r.o_parts = oparts;
       r.o_stride = (int64_t)kRows * H;
+      r.gemm_act = act;   // the next GEMM's input: the new h
+      r.gemm_post = act_post;
       launch_resid(r, stream, pdl);
+    };
+    auto slerp = [&](const float* lr, int oparts) {
+      SlerpBatchArgs sb = {};
+      sb.params = params_dev;
+      sb.nseq = S;
+      sb.hidden = H;
+      sb.h = h;
+      sb.o = o;
+      sb.o_parts = oparts;
+      sb.o_stride = (int64_t)kRows * H;
+      sb.lr = lr;
+      sb.act = act;
+      sb.act_post = act_post;
+      sb.pdl = pdl;
+      launch_slerp_batch(sb, stream);
     };
     int e = 0, a_i = 0;
     auto sublayer = [&](int ei) {
       const Eval& E = model->evals[ei];
-      gemm_digitize(h, M, H, act, act_post, stream, nullptr, 0, 0, pdl);
       if (E.kind == 0) {
         gemm(E.gu, outs_a[ei], ks_gu, (int64_t)kRows * 2 * F, pdl);
         SwigluBatchArgs sa = {};
@@ -1289,7 +1308,7 @@ struct BatchStep {
         sa.pdl = pdl;
         launch_swiglu_batch(sa, stream);
         gemm(E.down, outs_b[ei], ks_down, (int64_t)kRows * H, pdl);
-        resid(kResidSlerp, E.lr, ks_down);
+        slerp(E.lr, ks_down);
         return;
       }
       gemm(E.qkvg, outs_a[ei], ks_qkv, (int64_t)kRows * proj_ld, pdl);
@@ -1357,7 +1376,7 @@ struct BatchStep {
       launch_attn_combine(cb, stream, pdl);
       gemm_digitize(att, M, Q, act, act_post, stream, asum, c.heads, kRows, pdl);
       gemm(E.o, outs_b[ei], ks_o, (int64_t)kRows * H, pdl);
-      resid(kResidSlerp, E.lr, ks_o);
+      slerp(E.lr, ks_o);
       ++a_i;
     };
     for (int l = 0; l < c.n_in; ++l) sublayer(e++);
@@ -1369,7 +1388,6 @@ struct BatchStep {
       }
     }
     for (int l = 0; l < c.n_out; ++l) sublayer(e++);
-    gemm_digitize(h, M, H, act, act_post, stream, nullptr, 0, 0, pdl);
     gemm(model->head, outs_head, 1, 0, pdl);
     ScaleArgmaxArgs sa = {};
     sa.params = params_dev;
