@@ -97,6 +97,10 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     Stage& st = sm.stage[i % kStages];
     uint64_t* bar = &sm.full[i % kStages];
     const int64_t c = cb + i;
+    if (c < 0 || (c + 1) * 64 > slots) {   // never: a chunk outside the cache is recorded, not read
+      if (lane == 0 && a.err) atomicExch(a.err, 5);
+      return;
+    }
     if (lane == 0) mbar_expect_tx(bar, stage_bytes);
     __syncwarp();
     if (lane == 0) bulk_g2s(st.k, kc + c * 64 * kD, 64 * kD, bar);

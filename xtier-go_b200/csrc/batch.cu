@@ -166,6 +166,10 @@ __global__ void __launch_bounds__(128) qkv_prep_kernel(const QkvPrepArgs a) {
   }
   const KvSeq& kv = a.seqs[s];
   const int64_t pos = p.pos0 + i, slot = a.ring ? pos % kv.slots : pos;
+  if (slot < 0 || slot >= kv.slots) {   // a position outside the cache: recorded, nothing written
+    if (d == 0 && a.err) atomicExch(a.err, 4);
+    return;
+  }
   if (type == 1)
     kv.kc[k_offset(h, slot, d, kv.slots)] = code;
   else
@@ -182,6 +186,7 @@ __global__ void swiglu_batch_kernel(const SwigluBatchArgs a) {
   const int tid = threadIdx.x, r = blockIdx.y, s = r / kMaxRows, i = r % kMaxRows, F = a.features;
   const int C = (int)gridDim.x, rank = (int)cluster_rank();
   const int f0 = rank * (F / C) + 4 * tid;
+  cluster_arrive_relaxed();   // every CTA of the cluster is running before the first remote store (below)
   float sgv[4], suv[4];
 #pragma unroll
   for (int c = 0; c < 4; ++c) {   // parameters: before the wait
@@ -221,6 +226,7 @@ __global__ void swiglu_batch_kernel(const SwigluBatchArgs a) {
     red[1][tid >> 5] = mx;
   }
   __syncthreads();
+  cluster_wait();
   if (tid == 0) {
     float t = 0.f, m = 0.f;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
@@ -254,6 +260,7 @@ __global__ void slerp_batch_kernel(const SlerpBatchArgs a) {
   const int tid = threadIdx.x, r = blockIdx.y, s = r / kMaxRows, i = r % kMaxRows, H = a.hidden;
   const int C = (int)gridDim.x, rank = (int)cluster_rank();
   const int d0 = rank * (H / C) + 4 * tid;
+  cluster_arrive_relaxed();   // every CTA of the cluster is running before the first remote store (below)
   const float4 l4 = *reinterpret_cast<const float4*>(a.lr + d0);   // a parameter: before the wait
   if (a.pdl) {
     pdl_wait();
@@ -288,6 +295,7 @@ __global__ void slerp_batch_kernel(const SlerpBatchArgs a) {
 #pragma unroll
     for (int k = 0; k < 5; ++k) red[k][tid >> 5] = v5[k];
   __syncthreads();
+  cluster_wait();
   if (tid < 5) {
     float t = 0.f;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[tid][w];

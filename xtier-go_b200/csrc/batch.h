@@ -60,6 +60,7 @@ struct QkvPrepArgs {
   float* v_out;
   const KvSeq* seqs;          // [nseq]
   int ring, dtype;
+  int* err;                   // set (4) for a position outside its cache (nothing is written there)
   int pdl;
 };
 

@@ -115,6 +115,12 @@ __device__ __forceinline__ uint32_t cluster_rank() {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// A cluster phase in two halves: every CTA arrives at its start, and waits before its first store into another CTA's
+// shared memory, so that every CTA of the cluster has started by then.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 // store a float into CTA `rank`'s copy of the shared array `local` points into
 __device__ __forceinline__ void st_cluster_f32(float* local, uint32_t rank, float v) {
   uint32_t remote;

@@ -203,6 +203,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   float* rowscale = reinterpret_cast<float*>(smem + P.off_misc + 48);   // [8]
 
   // ---- set-up: TMEM before the dependent launch (a dependent CTA on this SM may wait for our columns) ----
+  if (S > 1) cluster_arrive_relaxed();   // every CTA of the cluster is running before the first remote store
   if (warp == 2) tmem_alloc(tmem_slot, P.tmem_cols);
   if (tid == 0) {
     for (int i = 0; i < ring; ++i) {
@@ -357,6 +358,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     fence_proxy_async_smem();
   }
   __syncthreads();
+  if (S > 1) cluster_wait();   // every thread: the cluster phase opened at the start
 
   if (warp == 0) {
     // ---- producer ----

@@ -1331,6 +1331,7 @@ struct BatchStep {
       qa.seqs = kvseq + (size_t)E.cache * S;
       qa.ring = E.kind == 1;
       qa.dtype = c.kv_dtype;
+      qa.err = dev_err;
       qa.pdl = pdl;
       launch_qkv_prep(qa, stream);
       const bool ring = E.kind == 1;
