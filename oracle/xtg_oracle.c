@@ -381,6 +381,10 @@ void xo_attention(const xo_attn* a) {
       for (int e = 0; e < d; ++e) dot += q[e] * kr[e];
       memcpy(vt + (int64_t)n * d, vr, sizeof(float) * (size_t)d);
       sc[n++] = dot * a->scale;
+      if (n == TILE) {   // a prompt chunk of more than a tile of own keys: folded tile by tile as well
+        fold_tile(&st, acc, d, sc, vt, n);
+        n = 0;
+      }
     }
     fold_tile(&st, acc, d, sc, vt, n);
     float* o = a->out + ((int64_t)i * a->heads + h) * d;

@@ -239,8 +239,9 @@ def test_forward_batch_matches_one_by_one(cuda, xtg, cfg):
     lists = [[5, 17, 900, 3, 44, 1023, 0, 256], [8, 9, 10], list(range(100, 111)), []]
     with xtg.Session(cfg, context=256) as owner:
         owner.prefill_synthetic(70)
-        singles = [xtg.Session.shared(owner, context=256) for _ in lists]
-        # batch=0: each session's own step graph, all in flight at once (the batched step is tested below)
+        # batch=0: verify steps of each session's own graph (8 rows at a time), all in flight at once in the batch
+        # call (the batched step and the prompt chunks are tested below)
+        singles = [xtg.Session.shared(owner, context=256, batch=0) for _ in lists]
         batch = [xtg.Session.shared(owner, context=256, batch=0) for _ in lists]
         try:
             want = []
@@ -311,3 +312,36 @@ def test_forward_batch_batched_step(cuda, xtg, cfg):
         finally:
             for s in sess + singles:
                 s.close()
+
+
+def test_prompt_chunks_match_oracle_and_verify_steps(cuda, xtg, cfg):
+    """A forward of more than decode_rows tokens runs prompt chunks of up to 64 rows through the batched step: 8-row
+    groups of the session, group g attending the cache up to its own first row (the earlier groups' keys among them,
+    stored by the same step) and its own rows as this call's keys -- the arithmetic of 8-row verify steps. 100 tokens (a
+    chunk of 64, one of 36) within the step tolerance of the oracle stepped 8 rows at a time (identical argmax), and of
+    the same tokens in the session's 8-row verify steps (batch=0); the position and the next verify step agree too."""
+    toks = [(37 * i + 11) % cfg["vocab"] for i in range(100)]
+    ref = O.SynthDory(cfg, ctx=512, n_prefill=70)
+    want = np.concatenate([ref.step(toks[o:o + 8]) for o in range(0, 100, 8)])
+    nxt_want = ref.step([5, 6, 7, 8])
+    ref.close()
+    with xtg.Session(cfg, context=512) as a, xtg.Session(cfg, context=512, batch=0) as b:
+        assert a.info()["prefill_ar"] == 64
+        a.prefill_synthetic(70)
+        b.prefill_synthetic(70)
+        ga = logits_of(a.forward(toks, want=2), 100)
+        gb = logits_of(b.forward(toks, want=2), 100)
+        assert a.pos() == b.pos() == 170
+        for got in (ga, gb):
+            assert np.array_equal(got.argmax(1), want.argmax(1))
+            assert np.abs(got - want).max() <= LOGIT_TOL, np.abs(got - want).max()
+        assert a.argmax(8)[:4] == list(want[96:].argmax(1))
+        last = a.forward(toks[:1], want=1)   # one more row: a single verify step after the chunks
+        assert sorted(last) == [0]
+        assert a.rewind(170) and b.rewind(170)   # the oracle's state: 170 positions
+        na = logits_of(a.forward([5, 6, 7, 8], want=2), 4)
+        nb = logits_of(b.forward([5, 6, 7, 8], want=2), 4)
+        for got in (na, nb):
+            assert np.array_equal(got.argmax(1), nxt_want.argmax(1))
+            assert np.abs(got - nxt_want).max() <= LOGIT_TOL
+        assert a.pos() == 174

@@ -79,6 +79,9 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   const int group = a.heads / a.kv_heads;
   const int32_t* ring_pos = sq ? sq->ring_pos : a.ring_pos;
   const float* aq = a.q + (int64_t)seq * kMaxRows * a.heads * kD;
+  // a sequence with no rows in this step (a batched step's idle group) reads nothing: its position may lie past its
+  // cache
+  if (m <= 0) return;
 
   // this CTA's 64-slot chunks: a global cache holds [0, pos0), a ring every slot
   const int64_t span = a.ring ? slots : pos0;
@@ -109,7 +112,8 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     if (lane == 3) bulk_g2s(st.vs, vs + c * 64, 64 * 4, bar);
     if (lane == 4 && a.ring) bulk_g2s(st.pos, ring_pos + c * 64, 64 * 4, bar);
   };
-  // the cached keys and values do not depend on the previous kernel: the first chunks go out now
+  // the cached keys and values below pos0 do not depend on the previous kernel (this step writes positions pos0 ..
+  // only): the first chunks go out now -- unless that kernel wrote some of them (late_copies)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], 1);
@@ -118,12 +122,14 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     mbar_init_fence();
   }
   __syncthreads();
-  if (warp == 0)
+  if (warp == 0 && !a.late_copies)
     for (int i = 0; i < kStages && i < nc; ++i) issue(i);
   if (a.pdl) {
     pdl_wait();
     pdl_launch_next();
   }
+  if (warp == 0 && a.late_copies)
+    for (int i = 0; i < kStages && i < nc; ++i) issue(i);
 
   // ---- A fragments of the queries of this KV head (prepared: RoPE, justnorm, q scale), straight from memory, split
   // q = hi + lo (both fp16) so that the scores keep ~22 bits: step st, lane tq reads head dims 32 tq + 4 st + {0, 1}

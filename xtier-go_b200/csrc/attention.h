@@ -87,6 +87,9 @@ struct AttnArgs {
   const KvSeq* seqs;
   int nseq;
   int64_t part_seq_stride;
+  // the cache below pos0 is written by the kernel just before (a prompt chunk's row groups over one cache): its
+  // chunks are copied only after the wait for that kernel, not before
+  int late_copies;
 };
 
 struct CombineArgs {

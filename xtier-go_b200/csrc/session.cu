@@ -210,6 +210,13 @@ enum KernelClass { kClsGemv = 0, kClsAttn = 1, kClsCombine = 2, kClsSmall = 3, k
 
 using namespace xtg;
 
+namespace {
+// prompt chunks of more than decode_rows rows as one batched step (defined with BatchStep below)
+int prefill_rows(const xtg_cuda* h);
+void prefill_chunk(xtg_cuda* h, const int32_t* tokens, int m, int want, int off, int n, xtg_cuda_logits_fn fn,
+                   void* user);
+}  // namespace
+
 struct xtg_cuda {
   Config c;
   cudaStream_t stream = nullptr;
@@ -950,13 +957,24 @@ struct xtg_cuda {
     return true;
   }
 
+  // Rows n <= decode_rows run the verify step; longer inputs go in prompt chunks of up to prefill_rows (64: the
+  // ring's slack past the window) through the batched step, the rest in verify steps (xtg_npu.cpp:346-360).
   void forward(const int32_t* tokens, int n, int want, xtg_cuda_logits_fn fn, void* user) {
     if (n <= 0) return;
     check_tokens(tokens, n);
     drop_snapshots_past();
-    for (int off = 0; off < n; off += c.decode_rows) {
+    const int pr = prefill_rows(this);
+    for (int off = 0; off < n;) {
+      const int left = n - off;
+      if (pr > c.decode_rows && left > c.decode_rows) {
+        const int m = std::min(pr, left);
+        prefill_chunk(this, tokens + off, m, want, off, n, fn, user);
+        off += m;
+        continue;
+      }
       const Chunk k = enqueue_chunk(tokens, n, off, want, fn != nullptr);
       if (!finish_chunk(k, fn, user, 0)) throw CudaError("a device wait timed out during the step (results discarded)");
+      off += c.decode_rows;
     }
   }
 
@@ -1112,6 +1130,7 @@ struct BatchStep {
   int* err_host = nullptr;
   cudaGraphExec_t exec = nullptr;
   static constexpr int kRows = 64;           // one GEMM activation tile
+  bool distinct = true;                      // false: the row groups of one session's prompt chunk
   int ks_qkv = 2, ks_o = 6, ks_gu = 1, ks_down = 6;
 
   template <class T>
@@ -1155,6 +1174,7 @@ struct BatchStep {
     KV = c.kv_heads * c.head_dim;
     proj_ld = model->proj_ld;
     for (xtg_cuda* q : seqs) gens.push_back(q->generation);
+    distinct = std::count(seqs.begin(), seqs.end(), seqs[0]) == 1;   // forward_batch never repeats a session
     XTG_CUDA(cudaSetDevice(c.device));
     XTG_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
     const int sms = model->num_sms;
@@ -1352,6 +1372,7 @@ struct BatchStep {
       at.err = dev_err;
       at.seqs = kvseq + (size_t)E.cache * S;
       at.nseq = S;
+      at.late_copies = distinct ? 0 : 1;   // a prompt chunk: the earlier groups' keys come from qkv_prep just before
       at.part_seq_stride = attention_part_floats(c.kv_heads, std::max(splits_g, splits_r));
       launch_attention(at, stream, pdl);
       CombineArgs cb = {};
@@ -1399,8 +1420,9 @@ struct BatchStep {
     sa.argmax = argmax;
     sa.pdl = pdl;
     launch_scale_argmax(sa, stream);
-    // each session's rows and argmax into its own buffers (xtg_cuda_argmax / xtg_cuda_topk read the last step there)
-    for (int i = 0; i < S; ++i) {
+    // each session's rows and argmax into its own buffers (xtg_cuda_argmax / xtg_cuda_topk read the last step there);
+    // a prompt chunk (one session's row groups) copies its last group's after the step
+    for (int i = 0; i < S && distinct; ++i) {
       XTG_CUDA(cudaMemcpyAsync(seqs[i]->logits, logits + (size_t)kMaxRows * i * c.vocab,
                                (size_t)kMaxRows * c.vocab * sizeof(float), cudaMemcpyDeviceToDevice, stream));
       XTG_CUDA(cudaMemcpyAsync(seqs[i]->argmax, argmax + kMaxRows * i, kMaxRows * sizeof(int32_t),
@@ -1462,6 +1484,59 @@ BatchStep* batch_for(const std::vector<xtg_cuda*>& key) {
     it = g_batches.emplace(key, std::move(b)).first;
   }
   return it->second.get();
+}
+
+// Prompt chunks through the batched step: the chunk's rows as kMaxBatch groups of 8 of one session, group g at
+// position n_past + 8 g, every group over the session's own caches. The projections of all the chunk's rows are one
+// GEMM each; the keys and values of all of them are stored before any attention of the step runs, so group g attends
+// the cache up to its own first row (the earlier groups' rows included) and its own rows as this call's keys. A ring
+// holds the window plus its slack: the chunk's new rows overwrite only slots of positions the window has left, so a
+// chunk is at most the slack (64 for the 1088-slot ring over a window of 1024).
+int prefill_rows(const xtg_cuda* h) {
+  const Config& c = h->c;
+  if (!c.batch || !c.graph || c.kv_world != 1) return 0;
+  const int slack = c.ring - c.window;
+  return std::min(kMaxBatch * kMaxRows, slack / kMaxRows * kMaxRows);
+}
+
+void prefill_chunk(xtg_cuda* h, const int32_t* tokens, int m, int want, int off, int n, xtg_cuda_logits_fn fn,
+                   void* user) {
+  BatchStep* b = batch_for(std::vector<xtg_cuda*>(kMaxBatch, h));
+  const int vocab = h->c.vocab;
+  for (int g = 0; g < kMaxBatch; ++g) {
+    StepParams& p = b->params_host[g];
+    std::memset(&p, 0, sizeof(p));
+    const int mg = std::max(0, std::min(kMaxRows, m - kMaxRows * g));
+    for (int r = 0; r < mg; ++r) p.tokens[r] = tokens[kMaxRows * g + r];
+    p.m = mg;
+    p.pos0 = h->n_past + kMaxRows * g;
+  }
+  b->capture();
+  XTG_CUDA(cudaGraphLaunch(b->exec, b->stream));
+  // the session's last-step buffers get the chunk's last group (xtg_cuda_argmax / xtg_cuda_topk read them)
+  const int G = (m - 1) / kMaxRows, mlast = m - kMaxRows * G;
+  XTG_CUDA(cudaMemcpyAsync(h->logits, b->logits + (size_t)kMaxRows * G * vocab, (size_t)kMaxRows * vocab * sizeof(float),
+                           cudaMemcpyDeviceToDevice, b->stream));
+  XTG_CUDA(cudaMemcpyAsync(h->argmax, b->argmax + kMaxRows * G, kMaxRows * sizeof(int32_t), cudaMemcpyDeviceToDevice,
+                           b->stream));
+  XTG_CUDA(cudaMemcpyAsync(b->err_host, b->dev_err, sizeof(int), cudaMemcpyDeviceToHost, b->stream));
+  XTG_CUDA(cudaStreamSynchronize(b->stream));
+  if (*b->err_host) {
+    *b->err_host = 0;
+    XTG_CUDA(cudaMemsetAsync(b->dev_err, 0, sizeof(int), b->stream));
+    throw CudaError("a device wait timed out during a prompt chunk (results discarded)");
+  }
+  h->commit(m);
+  h->last_rows = mlast;
+  const int r0 = want == 2 ? 0 : (want == 1 && off + m == n ? m - 1 : m);
+  if (!fn) return;
+  for (int g0 = r0; g0 < m; g0 += kMaxRows) {   // the rows through the session's 8-row host buffer
+    const int cnt = std::min(kMaxRows, m - g0);
+    XTG_CUDA(cudaMemcpyAsync(h->logits_host, b->logits + (size_t)g0 * vocab, (size_t)cnt * vocab * sizeof(float),
+                             cudaMemcpyDeviceToHost, b->stream));
+    XTG_CUDA(cudaStreamSynchronize(b->stream));
+    for (int r = 0; r < cnt; ++r) fn(off + g0 + r, h->logits_host + (size_t)r * vocab, user);
+  }
 }
 
 // sessions that can step as one: one weight set, one device, one KV format, graphs on, one process each
@@ -1648,7 +1723,8 @@ int xtg_cuda_info(xtg_cuda* h, char* out, int out_len) {
       "\"snapshots\":%d,\"kvmap\":false,\"kv_dtype\":\"%s\",\"weight_bytes\":%lld,\"hidden\":%d,\"evaluations\":%d,"
       "\"sm_count\":%d,\"graph\":%s,\"pdl\":%s,\"splits_global\":%d,\"splits_ring\":%d,"
       "\"kv_world\":%d,\"kv_rank\":%d,\"kv_exchange\":\"%s\",\"global_layers\":%d}",
-      h->c.vocab, (long long)h->c.context, (long long)h->c.context - 1, h->c.decode_rows, h->c.decode_rows,
+      h->c.vocab, (long long)h->c.context, (long long)h->c.context - 1, std::max(h->c.decode_rows, prefill_rows(h)),
+      h->c.decode_rows,
       (int)h->kv.size(), rings, h->c.ring, h->c.window, (long long)h->kv_bytes(), (int)h->snaps.size(),
       h->c.kv_dtype == kKvFp8 ? "fp8" : "int8", (long long)h->arena_bytes, h->c.hidden, h->c.n_evals(), h->num_sms,
       h->c.graph ? "true" : "false", h->c.pdl ? "true" : "false", h->splits_g, h->splits_r,
