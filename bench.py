@@ -668,6 +668,31 @@ def config4_block(x, rank, world, local_rank, dist, steps=256, seqs_total=64, co
                     "note": "the rounds above are end to end: host tokens in, each session's argmax read back"}}
 
 
+def prefill_block(x, local_rank, n_tokens=4096, reps=3):
+    """Prompt processing on the config-3 model (8K tier, from position 0): xtg_cuda_forward of n_tokens tokens without
+    logits, in prompt chunks of 64 rows through the batched step (every projection one tcgen05 GEMM over the chunk),
+    against the same tokens in 8-row verify steps (batch=0). Wall clock per call (best of reps)."""
+    model = dict(x.DORY_3072)
+    toks = [(37 * i + 11) % model["vocab"] for i in range(n_tokens)]
+    out = {"tokens": n_tokens}
+    for name, batch in (("chunks64", 1), ("verify8", 0)):
+        s = x.Session(model, context=8192, device=local_rank, batch=batch)
+        try:
+            best = None
+            for _ in range(reps + 1):
+                s.rewind(0)
+                t0 = time.perf_counter()
+                s.forward(toks, want=0)
+                dt = time.perf_counter() - t0
+                best = dt if best is None else min(best, dt)
+            out[name + "_s"] = best
+            out[name + "_tok_per_s"] = n_tokens / best
+        finally:
+            s.close()
+    out["speedup"] = out["verify8_s"] / out["chunks64_s"]
+    return out
+
+
 def job_rows_per_s(world, ms_per_step):
     """Whole-job throughput: every rank verifies 8 rows of its own sequence per step (weak scaling)."""
     return world * 8.0 / (ms_per_step / 1e3)
@@ -730,6 +755,7 @@ def run_ours(args, rank, world, local_rank, dist):
     shared = shared_sessions_block(x, s, dist, args.steps)
     s.close()
     cfg4 = None if args.no_config4 else config4_block(x, rank, world, local_rank, dist, steps=args.config4_steps)
+    pre = prefill_block(x, local_rank) if world == 1 else None
     topk_t = topk_block(x, f"cuda:{local_rank}", model["vocab"]) if world == 1 else None
     gemm = gemm_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg0 = config0_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
@@ -774,6 +800,10 @@ def run_ours(args, rank, world, local_rank, dist):
                                      "partitioned over the GPUs, 8-row verify rounds through xtg_cuda_forward_batch "
                                      "(batched steps of up to 8 sequences), argmax read back, seeded 1..4 acceptance "
                                      "driving rewinds; wall clock, max over ranks", **cfg4}
+    if pre:
+        line["prefill"] = {"config": "prompt of 4096 tokens on the config-3 model (8K tier) from position 0, no logits: "
+                                     "64-row prompt chunks (tcgen05 GEMM, batched step) vs 8-row verify steps; wall "
+                                     "clock, best of 3", **pre}
     if cfg0:
         line["config0_gemv"] = {"config": "config0: one NVFP4 GEMV, M = 1, 16 weight copies rotated", **cfg0}
     if cfg2:
