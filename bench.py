@@ -855,6 +855,8 @@ def main():
                     help="small: the same shapes with 2 + 2 + 2 sublayers (about 0.5 GB on the device)")
     ap.add_argument("--ncu-gemm", type=int, default=0,
                     help="profiling driver: run the config-1 gate+up GEMM at M=512 this many times, then exit")
+    ap.add_argument("--ncu-batch", type=int, default=0,
+                    help="profiling driver: this many batched rounds of 8 sequences (8K tier), then exit")
     args = ap.parse_args()
     if args.ncu_gemm:
         import torch
@@ -871,6 +873,22 @@ def main():
             lin(xin)
         torch.cuda.synchronize()
         lin.close()
+        return
+    if args.ncu_batch:
+        x = package()
+        model = dict(x.DORY_3072)
+        if args.ncu_model == "small":
+            model.update(n_in=2, n_rec=2, n_out=2, loops=1)
+        owner = x.Session(model, context=8192)
+        sess = [owner] + [x.Session.shared(owner, context=8192) for _ in range(7)]
+        for s_ in sess:
+            s_.prefill_synthetic(PREFILL)
+        for _ in range(args.ncu_batch):
+            x.forward_batch(sess, [TOKENS] * 8, want=0)
+            for s_ in sess:
+                s_.rewind(PREFILL)
+        for s_ in sess:
+            s_.close()
         return
     if args.ncu_steps:
         x = package()
