@@ -767,7 +767,7 @@ def run_ours(args, rank, world, local_rank, dist):
         return
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "nvfp4 weights x e2m1-digit activations (6 block-scaled digits) on tcgen05, f32 accumulate; int8 KV",
+            "vs_baseline": None, "dtype": "nvfp4 weights x e2m1-digit activations (4 block-scaled digits) on tcgen05, f32 accumulate; int8 KV",
             "data": "synthetic (seeded random-init weights, random prefilled KV)", "config": config_block(world),
             "value_counts": "verify rows per second (8 per step); accepted tokens per second are in `rates`",
             "rates": rates(world, ms),

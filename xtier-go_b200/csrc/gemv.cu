@@ -31,6 +31,8 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kStageUnits = 4;
 constexpr int kMaxRing = 6;
+// shared memory of an SM, the part the system keeps per CTA, the most one CTA may have
+constexpr int64_t kSmPerSm = 233472, kPerCtaReserve = 1024, kMaxSmem = 232448;
 constexpr int kAccCols = 64;   // TMEM columns per accumulator (32 used)
 static_assert(kBBlockBytes == kDigitBlockBytes, "the host's digit buffer size");
 constexpr int kSumsqLoads = 10;   // the producer's row-sum parts a lane loads: at most 320 parts
@@ -705,7 +707,6 @@ __global__ void digitize_rows_kernel(const float* x, int m, int k, uint8_t* xb, 
 }  // namespace
 
 GemvPlan plan_gemv(int tiles, int kblocks, int num_sms, int max_split, int max_tiles_per_cta) {
-  constexpr int64_t kSmPerSm = 233472, kPerCtaReserve = 1024, kMaxSmem = 232448;
   GemvPlan p;
   for (int cps = 2; cps >= 1; --cps) {
     const int slots = num_sms * cps;
@@ -756,16 +757,22 @@ void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, 
   const int cols = tmem_columns(p.tiles_per_cta, P.slice_max, p.ring);
   XTG_REQUIRE(cols <= 512, "gemv: the K slice's scales do not fit in TMEM");
   P.tmem_cols = cols <= 256 ? 256 : 512;
+  // No more CTAs on an SM than its 512 TMEM columns hold: a CTA beyond that would wait in tcgen05.alloc until a
+  // neighbour exits (measured: a third 76 KB O-projection CTA on an SM started ~7 us late). The dynamic shared memory
+  // is raised, where needed, until one more CTA no longer fits.
+  const int per_sm = 512 / (int)P.tmem_cols;
+  const uint32_t smem_floor = (uint32_t)(kSmPerSm / (per_sm + 1) - kPerCtaReserve + 128);
+  const uint32_t smem_bytes = std::max(sp.total, smem_floor);
   static std::atomic<uint64_t> optin[4];
   auto* k = epi == kEpiStore    ? gemv_kernel<kEpiStore>
             : epi == kEpiSwiglu ? gemv_kernel<kEpiSwiglu>
             : epi == kEpiQkv    ? gemv_kernel<kEpiQkv>
                                 : gemv_kernel<kEpiHead>;
-  ensure_smem_optin((const void*)k, 232448, optin[epi]);
+  ensure_smem_optin((const void*)k, (int)kMaxSmem, optin[epi]);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = sp.total;
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   int n = 0;
