@@ -374,6 +374,45 @@ def gemm_block(x, device, m=512, reps=6):
     return out
 
 
+def head_block(x, device, m=8, reps=20):
+    """The lm_head at the Dory-3072 shape (vocab 131072 x 3072, 8 rows): the NVFP4 head on the GEMV (226 MB, the
+    synthetic model's) beside a checkpoint's BF16 head (805 MB, the reference's matmul_bf16, head.cu). Seeded random
+    weights, one copy each (both larger than L2); device time per launch from the CUDA activity timeline; algorithmic
+    bytes = the weight bytes + x in f32 + logits in f32."""
+    import torch
+    from torch.profiler import profile, ProfilerActivity
+    V, H = 131072, 3072
+    g = torch.Generator(device=device)
+    g.manual_seed(5)
+    peak, peak_kind = peaks()
+    xin = torch.randn(m, H, device=device, generator=g)
+    xin = xin / xin.norm(dim=1, keepdim=True)
+    codes = torch.randint(0, 256, (V, H // 2), dtype=torch.uint8, device=device, generator=g)
+    scales = torch.randint(0x30, 0x40, (V, H // 16), dtype=torch.uint8, device=device, generator=g)
+    lin = x.Linear([(codes, scales, 1.0)], H)
+    ys = [torch.empty(m, V, device=device)]
+    w = (torch.randn(V, H, device=device, generator=g) * 0.02).to(torch.bfloat16)
+    ls = torch.rand(V, device=device, generator=g) * 100 + 100
+    for _ in range(3):
+        lin(xin, ys)
+        x.head_bf16(xin, w, ls)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            lin(xin, ys)
+            x.head_bf16(xin, w, ls)
+        torch.cuda.synchronize()
+    kt = kernel_times(prof)
+    io = m * H * 4 + m * V * 4
+    out = {}
+    for name, kern, wb in (("nvfp4", "gemv_kernel", V * H // 2 + V * H // 16 + 4), ("bf16", "head_bf16_kernel", V * H * 2)):
+        us = kt[kern]
+        out[name] = {"us": us, "algorithmic_bytes": wb + io, "gbs": (wb + io) / us / 1e3,
+                     "frac": (wb + io) / us / 1e3 / peak, "peak": peak, "peak_kind": peak_kind}
+    lin.close()
+    return out
+
+
 def kernel_times(prof):
     """Mean device time (us) per kernel name (the `*_kernel` symbol) from a torch.profiler CUDA timeline."""
     import re
@@ -760,6 +799,7 @@ def run_ours(args, rank, world, local_rank, dist):
     gemm = gemm_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg0 = config0_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg2 = config2_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
+    heads = head_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     # the batch-1 split over GPUs: measured where its 2-GPU tests run (--split-kv-max raises the bound)
     skv = (split_kv_block(x, rank, world, local_rank, dist, args.steps, args.warmup)
            if 1 < world <= args.split_kv_max else None)
@@ -809,6 +849,10 @@ def run_ours(args, rank, world, local_rank, dist):
     if cfg2:
         line["config2_attention"] = {"config": "config2: 8-row decode attention, int8 KV, attention + split combine",
                                      **cfg2}
+    if heads:
+        line["lm_head"] = {"config": "lm_head at vocab 131072 x 3072, 8 rows: NVFP4 on the GEMV (the synthetic model's "
+                                     "head) and a checkpoint's BF16 head (head.cu, mma.sync over bf16 hi + lo rows)",
+                           **heads}
     if skv:
         line["batch1_split_kv"] = {"config": "batch-1 verify step (8 rows) at 32K context, the global caches' chunks "
                                              "split over the GPUs, partials exchanged over NVLink inside the combine "
@@ -847,7 +891,7 @@ def main():
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-1 M=512 prefill GEMM measurement")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 batched serving measurement")
     ap.add_argument("--config4-steps", type=int, default=256, help="verify rounds of the config-4 measurement")
-    ap.add_argument("--split-kv-max", type=int, default=4,
+    ap.add_argument("--split-kv-max", type=int, default=8,
                     help="largest world size at which the batch-1 split-KV step is measured (N > 1)")
     ap.add_argument("--ncu-steps", type=int, default=0,
                     help="profiling driver: run this many eager steps (no graph, no JSON) for ncu, then exit")

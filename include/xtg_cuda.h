@@ -163,6 +163,14 @@ XTG_CUDA_API int xtg_cuda_linear_forward(xtg_cuda_linear* w, const float* x, int
 XTG_CUDA_API int64_t xtg_cuda_linear_bytes(xtg_cuda_linear* w);   // packed weight bytes streamed per call
 XTG_CUDA_API void xtg_cuda_linear_free(xtg_cuda_linear* w);
 
+// A checkpoint's BF16 lm_head: matmul_bf16 (engine/src/kernels.cpp:140-155) times the folded logit scale
+// (packs/dory/dory.cpp:566-576) for m <= 8 rows, and each row's argmax (ties to the lowest index, sampler.cpp:8-13).
+// Device pointers: x [m][hidden] f32, w [vocab][hidden] bf16 (both 16-byte aligned; hidden a multiple of 32, at most
+// 6144), logit_scale [vocab], logits [m][vocab] (or NULL), argmax [m] int32 (or NULL). Waits for the result.
+XTG_CUDA_API int xtg_cuda_head_bf16(const float* x, int m, const uint16_t* w, int vocab, int hidden,
+                                    const float* logit_scale, float* logits, int32_t* argmax, void* stream, char* err,
+                                    int err_len);
+
 // The NVFP4 quantizer (device): bf16 [n_out][k] -> codes [n_out][k / 2], scales [n_out][k / 16], global (a device
 // float). global = amax / (6 * 448); block scale = E4M3(amax_block / (6 * global)); nearest E2M1, ties to even.
 XTG_CUDA_API int xtg_cuda_quantize_nvfp4(const uint16_t* w_bf16, int n_out, int k, uint8_t* codes, uint8_t* scales,

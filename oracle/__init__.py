@@ -8,6 +8,7 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline and
 package, and only as the checker or the timed CPU baseline; the product (``libxtg_cuda.so``) never calls it.
 """
 import ctypes as C
+import json
 import os
 import subprocess
 
@@ -56,7 +57,7 @@ class Model(C.Structure):
     _fields_ = [("hidden", C.c_int), ("ffn", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
                 ("head_dim", C.c_int), ("vocab", C.c_int), ("window", C.c_int), ("n_in", C.c_int),
                 ("n_rec", C.c_int), ("n_out", C.c_int), ("loops", C.c_int), ("layers", C.POINTER(Layer)),
-                ("head", Nvfp4), ("logit_scale", f32p)]
+                ("head", Nvfp4), ("logit_scale", f32p), ("embed_bf16", u16p), ("head_bf16", u16p)]
 
 
 class State(C.Structure):
@@ -178,8 +179,75 @@ def ref():
         R.xr_sample.restype = C.c_int
         R.xr_sample.argtypes = [f32p, C.c_int, C.c_float, C.c_int, C.c_float, C.c_float, C.c_uint64,
                                 C.POINTER(C.c_double)]
+        R.xr_dory_load.restype = C.c_void_p
+        R.xr_dory_load.argtypes = [C.c_char_p, C.c_char_p, C.c_void_p]
+        R.xr_dory_free.argtypes = [C.c_void_p]
+        R.xr_dory_vocab.restype = C.c_int
+        R.xr_dory_vocab.argtypes = [C.c_void_p]
+        R.xr_dory_session.restype = C.c_void_p
+        R.xr_dory_session.argtypes = [C.c_void_p]
+        R.xr_dory_session_free.argtypes = [C.c_void_p]
+        R.xr_dory_n_past.restype = C.c_int64
+        R.xr_dory_n_past.argtypes = [C.c_void_p]
+        R.xr_dory_rewind.restype = C.c_int
+        R.xr_dory_rewind.argtypes = [C.c_void_p, C.c_int64]
+        R.xr_dory_forward.restype = C.c_int
+        R.xr_dory_forward.argtypes = [C.c_void_p, i32p, C.c_int, C.c_int, f32p]
         _ref = R
     return _ref
+
+
+class RefDory:
+    """The reference's own Dory pack (packs/dory/dory.cpp, CPU backend) on a checkpoint directory: DoryModel's
+    loader and a DorySession, forward with every row's logits."""
+
+    def __init__(self, directory, threads=0, **options):
+        R = ref()
+        if R is None:
+            raise RuntimeError("oracle/_ref is not built")
+        self.R = R
+        self.pool = R.xr_pool_new(threads or (os.cpu_count() or 1))
+        opts = dict(backend="cpu")
+        opts.update(options)
+        self.model = R.xr_dory_load(os.fsencode(directory), json.dumps(opts).encode(), self.pool)
+        if not self.model:
+            R.xr_pool_free(self.pool)
+            raise RuntimeError(R.xr_last_error().decode())
+        self.vocab = R.xr_dory_vocab(self.model)
+        self.s = R.xr_dory_session(self.model)
+        if not self.s:
+            raise RuntimeError(R.xr_last_error().decode())
+
+    @property
+    def n_past(self):
+        return self.R.xr_dory_n_past(self.s)
+
+    def forward(self, tokens):
+        toks = np.ascontiguousarray(tokens, np.int32)
+        out = np.zeros((len(toks), self.vocab), np.float32)
+        if self.R.xr_dory_forward(self.s, ptr(toks, i32p), len(toks), self.vocab, ptr(out, f32p)) != 0:
+            raise RuntimeError(self.R.xr_last_error().decode())
+        return out
+
+    def rewind(self, n):
+        return self.R.xr_dory_rewind(self.s, n) == 0
+
+    def close(self):
+        if getattr(self, "s", None):
+            self.R.xr_dory_session_free(self.s)
+            self.s = None
+        if getattr(self, "model", None):
+            self.R.xr_dory_free(self.model)
+            self.model = None
+        if getattr(self, "pool", None):
+            self.R.xr_pool_free(self.pool)
+            self.pool = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ----------------------------------------------------------------------------------------------------------------
@@ -425,6 +493,119 @@ class SynthDory:
         ks = np.ctypeslib.as_array(c.ks, shape=(n * kvh,)).reshape(n, kvh).copy()
         vs = np.ctypeslib.as_array(c.vs, shape=(n * kvh,)).reshape(n, kvh).copy()
         return k, v, ks, vs, bool(c.ring)
+
+
+class CheckpointDory(SynthDory):
+    """A Dory checkpoint's tensors stepped by the restatement: the model packs/dory/dory.cpp:316-439 builds from
+    config.json and model.safetensors (recurrent sublayers' weights shared by every loop, the stored scales folded as
+    dory.cpp:326-364 folds them), with the BF16 embedding table and either the BF16 lm_head (head "bf16") or its
+    NVFP4 quantization (head "nvfp4", the device loader's option). The KV state is seeded as the synthetic model's.
+
+    config: config.json as a dict; tensors: name -> array (U8 codes, F8_E4M3 scales as uint8, F32 globals, BF16 as
+    uint16 bits), as the checkpoint stores them."""
+
+    def __init__(self, config: dict, tensors: dict, ctx: int, n_prefill: int, loops=None, head="bf16",
+                 kv_dtype=KV_I8, ring=None, seed=3, kvs_lo=0.0008, kvs_hi=0.0016):
+        c = config
+        H, F = c["hidden_size"], c["intermediate_size"]
+        heads, kvh, d = c["num_attention_heads"], c["num_key_value_heads"], c["head_dim"]
+        V = c["vocab_size"]
+        n_in, n_rec, n_out = c["n_input_layers"], c["n_recurrent_layers"], c["n_output_layers"]
+        loops = c.get("n_recurrent_loops", 1) if loops is None else loops
+        kinds_ = [{"mlp": 0, "sliding_attention": 1, "full_attention": 2}[t] for t in c["layer_types"]]
+        window = c.get("sliding_window", 0) if 1 in kinds_ else 64
+        ring = window + 64 if ring is None else ring
+        f32 = np.float32
+        init_range = f32(c["initializer_range"])
+        alpha_scale = f32(c["ngpt_alpha_init"]) / init_range
+        sqk_factor = np.sqrt(f32(d)) / init_range
+        gate_init = c.get("attention_output_gate_logit_scale_init")
+        gate_init = np.sqrt(f32(H)) if gate_init is None else f32(gate_init)
+        gate_factor = np.sqrt(f32(gate_init)) / init_range
+        suv_factor = np.sqrt(f32(H))
+        rope = c["rope_parameters"]
+        theta = {1: f32(rope.get("sliding_attention", {}).get("rope_theta", 0)),
+                 2: f32(rope.get("full_attention", {}).get("rope_theta", 0))}
+        keep = []
+
+        def arr(a, dt):
+            a = np.ascontiguousarray(a, dt)
+            keep.append(a)
+            return a
+
+        def bf16(name):
+            return bf16_to_f32(tensors[name]).astype(f32)
+
+        def nvfp4(name):
+            w = Nvfp4()
+            codes = arr(tensors[name + ".weight"], np.uint8)
+            scales = arr(tensors[name + ".weight_scale"], np.uint8)
+            w.codes, w.scales = ptr(codes, u8p), ptr(scales, u8p)
+            w.global_ = float(np.asarray(tensors[name + ".weight_scale_2"], f32).reshape(()))
+            w.n_out, w.k = codes.shape[0], codes.shape[1] * 2
+            return w
+
+        phys = list(range(n_in)) + [n_in + r for _ in range(loops) for r in range(n_rec)] + \
+            [n_in + n_rec + r for r in range(n_out)]
+        layers = (Layer * len(phys))()
+        built = {}
+        n_attn = 0
+        for e, l in enumerate(phys):
+            L = layers[e]
+            k = kinds_[l]
+            L.kind = k
+            p = f"backbone.layers.{l}."
+            if l not in built:
+                lr = arr(np.abs(bf16(p + ("mlp_alpha" if k == 0 else "attn_alpha")) * alpha_scale), f32)
+                if k == 0:
+                    ws = [nvfp4(p + "mixer." + n) for n in ("gate_proj", "up_proj", "down_proj")]
+                    vec = dict(sg=arr(bf16(p + "mixer.suv_gate") * suv_factor, f32),
+                               su=arr(bf16(p + "mixer.suv_up") * suv_factor, f32))
+                else:
+                    ws = [nvfp4(p + "mixer." + n) for n in ("q_proj", "k_proj", "v_proj", "g_proj", "o_proj")]
+                    qs, gs = bf16(p + "mixer.sqk"), bf16(p + "mixer.s_gate")
+                    vec = dict(qscale=arr((qs * sqk_factor) * (qs * sqk_factor), f32),
+                               gscale=arr((gs * gate_factor) * (gs * gate_factor), f32))
+                built[l] = (ws, lr, vec)
+            ws, lr, vec = built[l]
+            for j, w in enumerate(ws):
+                L.w[j] = w
+            L.lr = ptr(lr, f32p)
+            for name, a in vec.items():
+                setattr(L, name, ptr(a, f32p))
+            if k != 0:
+                L.theta = float(theta[k])
+                L.cache = n_attn
+                n_attn += 1
+        M = Model()
+        M.hidden, M.ffn, M.heads, M.kv_heads, M.head_dim, M.vocab = H, F, heads, kvh, d, V
+        M.window, M.n_in, M.n_rec, M.n_out, M.loops = window, n_in, n_rec, n_out, loops
+        M.layers = C.cast(layers, C.POINTER(Layer))
+        M.logit_scale = ptr(arr(bf16("lm_head.logit_scale") / init_range, f32), f32p)
+        M.embed_bf16 = ptr(arr(tensors["backbone.embeddings.weight"], np.uint16), u16p)
+        lm = arr(tensors["lm_head.weight"], np.uint16)
+        if head == "bf16":
+            M.head_bf16 = ptr(lm, u16p)
+        else:   # the loader's quantizer (bit-exact with this one)
+            codes, scales, g = quantize_nvfp4(lm)
+            hw = Nvfp4()
+            hw.codes, hw.scales = ptr(arr(codes, np.uint8), u8p), ptr(arr(scales, np.uint8), u8p)
+            hw.global_, hw.n_out, hw.k = g, V, H
+            M.head = hw
+        self._keep = (keep, layers, M)
+        self.cfg = dict(hidden=H, ffn=F, heads=heads, kv_heads=kvh, head_dim=d, vocab=V, n_in=n_in, n_rec=n_rec,
+                        n_out=n_out, loops=loops, window=window, ring=ring, global_every=0, theta_sliding=1e4,
+                        theta_global=1e4, weight_std=0.02, lr_lo=0, lr_hi=1, qs_lo=0, qs_hi=1, gs_lo=0, gs_hi=1,
+                        suv_lo=0, suv_hi=1, ls_lo=0, ls_hi=1, kvs_lo=kvs_lo, kvs_hi=kvs_hi, seed=seed)
+        self.c = synth_cfg(**self.cfg)
+        self.model = C.pointer(M)
+        self.state = lib().xo_synth_state_new(self.model, C.byref(self.c), ctx, kv_dtype, n_prefill)
+
+    def close(self):
+        if self.state:
+            lib().xo_synth_state_free(self.state)
+            self.state = None
+        self.model = None
 
 
 def kinds(cfg: dict):

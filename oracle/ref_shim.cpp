@@ -1,7 +1,8 @@
 // TEST INFRASTRUCTURE ONLY (the checker, never the product): C entry points over XTier Go's own CPU kernels.
 //
 // oracle/Makefile compiles this file together with the reference's engine sources, unmodified and in place
-// (engine/src/{kernels,fp,kv,threadpool,common}.cpp), into oracle/_ref/libxtgref.so. Tests call it through ctypes to
+// (engine/src/{kernels,fp,kv,threadpool,common,sampler}.cpp, and for whole checkpoints model.cpp, safetensors.cpp,
+// opencl.cpp and packs/dory/{dory,npu}.cpp), into oracle/_ref/libxtgref.so. Tests call it through ctypes to
 // pin the C restatement (xtg_oracle.c) against the reference's own arithmetic, and bench.py's reference arm times
 // it as the reference's CPU implementation of the Dory verify step. Every function below forwards to the named
 // reference function; the step harness at the end calls them in the order of DorySession::sublayer
@@ -14,11 +15,14 @@
 #include <limits>
 #include <random>
 #include <memory>
+#include <mutex>
 #include <vector>
 
+#include "dory/dory.h"
 #include "xtg/fp.h"
 #include "xtg/kernels.h"
 #include "xtg/kv.h"
+#include "xtg/model.h"
 #include "xtg/sampler.h"
 #include "xtg/threadpool.h"
 
@@ -269,6 +273,36 @@ int xr_sample(const float* logits, int n, float temperature, int top_k, float to
   std::mt19937_64 eng(seed);
   *u = std::generate_canonical<double, std::numeric_limits<double>::digits>(eng);
   return s.sample(logits, n, p);
+}
+
+// A Dory checkpoint through the reference's own pack (packs/dory/dory.cpp: DoryModel, DorySession) on its CPU
+// backend: load_model (engine/src/model.cpp) with JSON launch options, sessions, forward with every row's logits.
+void* xr_dory_load(const char* dir, const char* options, void* pool) {
+  static std::once_flag once;
+  std::unique_ptr<Model> m;
+  const int rc = guarded([&] {
+    std::call_once(once, [] { dory::register_pack(); });
+    m = load_model(dir, json::parse(options ? options : "{}"), *static_cast<ThreadPool*>(pool));
+  });
+  return rc == 0 ? m.release() : nullptr;
+}
+void xr_dory_free(void* model) { delete static_cast<Model*>(model); }
+int xr_dory_vocab(void* model) { return static_cast<Model*>(model)->info().vocab; }
+void* xr_dory_session(void* model) {
+  std::unique_ptr<Session> s;
+  const int rc = guarded([&] { s = static_cast<Model*>(model)->new_session(); });
+  return rc == 0 ? s.release() : nullptr;
+}
+void xr_dory_session_free(void* s) { delete static_cast<Session*>(s); }
+int64_t xr_dory_n_past(void* s) { return static_cast<Session*>(s)->n_past(); }
+int xr_dory_rewind(void* s, int64_t n) { return static_cast<Session*>(s)->rewind(n) ? 0 : -1; }
+// logits [n][vocab]: every row of this call
+int xr_dory_forward(void* s, const int32_t* tokens, int n, int vocab, float* logits) {
+  return guarded([&] {
+    static_cast<Session*>(s)->forward(tokens, n, Logits::All, [&](int row, const float* lg) {
+      std::memcpy(logits + size_t(row) * size_t(vocab), lg, sizeof(float) * size_t(vocab));
+    });
+  });
 }
 
 }  // extern "C"

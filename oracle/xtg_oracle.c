@@ -518,7 +518,14 @@ void xo_step(const xo_model* M, xo_state* S, const int32_t* tokens, int m, float
   b.mg = p;     p += (int64_t)m * F;
   b.mu = p;
   const int64_t n = (int64_t)m * H;
-  for (int r = 0; r < m; ++r) xo_nvfp4_row(&M->head, tokens[r], b.x + (int64_t)r * H);
+  for (int r = 0; r < m; ++r) {
+    float* xr = b.x + (int64_t)r * H;
+    if (M->embed_bf16) {   // bf16_row (engine/src/kernels.cpp:157-160)
+      for (int j = 0; j < H; ++j) xr[j] = xo_bf16_to_f32(M->embed_bf16[(int64_t)tokens[r] * H + j]);
+    } else {
+      xo_nvfp4_row(&M->head, tokens[r], xr);
+    }
+  }
   int e = 0;
   for (int l = 0; l < M->n_in; ++l) sublayer(M, S, &M->layers[e++], &b, m);
   memcpy(b.input, b.x, sizeof(float) * (size_t)n);
@@ -532,8 +539,20 @@ void xo_step(const xo_model* M, xo_state* S, const int32_t* tokens, int m, float
   }
   memcpy(b.x, b.state, sizeof(float) * (size_t)n);
   for (int l = 0; l < M->n_out; ++l) sublayer(M, S, &M->layers[e++], &b, m);
-  float* yl[1] = {logits};
-  xo_matmul_nvfp4(&M->head, 1, b.x, m, yl);
+  if (M->head_bf16) {   // matmul_bf16 (engine/src/kernels.cpp:140-155): row n's f32 weights dotted with each row
+    for (int n = 0; n < M->vocab; ++n) {
+      const uint16_t* w = M->head_bf16 + (int64_t)n * H;
+      for (int r = 0; r < m; ++r) {
+        const float* xr = b.x + (int64_t)r * H;
+        float acc = 0.f;
+        for (int j = 0; j < H; ++j) acc += xo_bf16_to_f32(w[j]) * xr[j];
+        logits[(int64_t)r * M->vocab + n] = acc;
+      }
+    }
+  } else {
+    float* yl[1] = {logits};
+    xo_matmul_nvfp4(&M->head, 1, b.x, m, yl);
+  }
   for (int r = 0; r < m; ++r)
     for (int j = 0; j < M->vocab; ++j) logits[(int64_t)r * M->vocab + j] *= M->logit_scale[j];
   for (int r = 0; r < m; ++r) S->ring_pos[(S->n_past + r) % S->ring] = S->n_past + r;

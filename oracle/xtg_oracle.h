@@ -114,6 +114,10 @@ typedef struct {
   const xo_layer* layers;
   xo_nvfp4 head;                   // tied: row t is also token t's embedding
   const float* logit_scale;        // [vocab], folded (dory.cpp:326-327)
+  // a checkpoint's (packs/dory/dory.cpp:322-325), or null: the BF16 embedding table [vocab][hidden] (bf16_row,
+  // engine/src/kernels.cpp:157-160) and the untied BF16 lm_head [vocab][hidden] (matmul_bf16, kernels.cpp:140-155)
+  const uint16_t* embed_bf16;
+  const uint16_t* head_bf16;
 } xo_model;
 
 typedef struct {

@@ -42,7 +42,9 @@ def test_open_without_gpu_reports_an_error(xtg):
 def test_open_rejects_unknown_models_and_bad_options(xtg):
     L = xtg.lib()
     err = C.create_string_buffer(512)
-    assert not L.xtg_cuda_open(b"/no/such/model", b"{}", err, len(err))
+    assert not L.xtg_cuda_open(b"/no/such/model", b"{}", err, len(err))   # a checkpoint directory without files
+    assert b"no config.json" in err.value
+    assert not L.xtg_cuda_open(b"", b"{}", err, len(err))
     assert b"synthetic" in err.value
     assert not L.xtg_cuda_open(b"synthetic", b"{\"kv_dtype\": \"bf16\"", err, len(err))
     assert err.value

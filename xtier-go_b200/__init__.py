@@ -89,6 +89,9 @@ def lib():
         L.xtg_cuda_topk_rows.restype = C.c_int
         L.xtg_cuda_topk_rows.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_void_p, C.c_void_p, E, C.c_int]
+        L.xtg_cuda_head_bf16.restype = C.c_int
+        L.xtg_cuda_head_bf16.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                         C.c_void_p, C.c_void_p, E, C.c_int]
         L.xtg_cuda_sample_candidates.restype = C.c_int
         L.xtg_cuda_sample_candidates.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_double, C.c_int,
                                                  C.POINTER(Sampling), C.c_double]
@@ -168,14 +171,28 @@ class Session:
     """One xtg_cuda handle (npu/xtg_npu.h's session): weights, KV instances, ring table, snapshots."""
 
     def __init__(self, model=None, context=8192, kv_dtype="int8", snapshots=2, decode_rows=8, device=0, graph=True,
-                 pdl=True, **extra):
-        opts = dict(model=dict(model or DORY_3072), context=context, kv_dtype=kv_dtype, snapshots=snapshots,
-                    decode_rows=decode_rows, device=device, graph=int(graph), pdl=int(pdl))
+                 pdl=True, path=None, **extra):
+        """The synthetic model of shape `model` (default DORY_3072), or (path) the Dory checkpoint in that directory
+        (config.json + model.safetensors, ModelOpt W4A16_NVFP4); extra options as xtg_cuda_open takes them (for a
+        checkpoint: loops, kv_mode, ring, head "bf16" | "nvfp4")."""
+        opts = dict(context=context, kv_dtype=kv_dtype, snapshots=snapshots, decode_rows=decode_rows, device=device,
+                    graph=int(graph), pdl=int(pdl))
+        if path is None:
+            opts["model"] = dict(model or DORY_3072)
         opts.update(extra)
         self.options = opts
-        self.model = opts["model"]
+        self.path = path
+        if path is None:
+            self.model = opts["model"]
+        else:
+            with open(os.path.join(path, "config.json")) as f:
+                cfg = json.load(f)
+            self.model = dict(hidden=cfg["hidden_size"], ffn=cfg["intermediate_size"],
+                              heads=cfg["num_attention_heads"], kv_heads=cfg["num_key_value_heads"],
+                              head_dim=cfg["head_dim"], vocab=cfg["vocab_size"])
         err = _err()
-        self.h = lib().xtg_cuda_open(b"synthetic", json.dumps(opts).encode(), err, len(err))
+        src = b"synthetic" if path is None else os.fsencode(path)
+        self.h = lib().xtg_cuda_open(src, json.dumps(opts).encode(), err, len(err))
         if not self.h:
             raise XtgError(err.value.decode(errors="replace"))
 
@@ -443,6 +460,20 @@ def attention_noalloc(q, k, v, k_codes, v_codes, k_scales, v_scales, pos0, windo
     err = _err()
     _check(lib().xtg_cuda_attention_noalloc(C.byref(a), splits, _stream(), err, len(err)), err)
     return out
+
+
+def head_bf16(x, w, logit_scale, logits=True):
+    """xtg_cuda_head_bf16 on torch CUDA tensors: x [m][hidden] f32, w [vocab][hidden] bf16 (or int16 bits),
+    logit_scale [vocab] f32 -> (logits [m][vocab] or None, argmax [m] int32)."""
+    import torch
+    m, hidden = x.shape
+    vocab = w.shape[0]
+    out = torch.empty((m, vocab), dtype=torch.float32, device=x.device) if logits else None
+    am = torch.empty(m, dtype=torch.int32, device=x.device)
+    err = _err()
+    _check(lib().xtg_cuda_head_bf16(x.data_ptr(), m, w.data_ptr(), vocab, hidden, logit_scale.data_ptr(),
+                                    out.data_ptr() if logits else None, am.data_ptr(), _stream(), err, len(err)), err)
+    return out, am
 
 
 def topk(logits, k, temperature=1.0):

@@ -380,6 +380,45 @@ int xtg_cuda_gen(int what, uint64_t seed, uint64_t stream_id, float a, float b, 
   });
 }
 
+int xtg_cuda_head_bf16(const float* x, int m, const uint16_t* w, int vocab, int hidden, const float* logit_scale,
+                       float* logits, int32_t* argmax, void* stream, char* err, int err_len) {
+  return guarded(err, err_len, [&] {
+    XTG_REQUIRE(x && w && logit_scale && (logits || argmax), "head_bf16: null pointer");
+    XTG_REQUIRE(m >= 1 && m <= kMaxRows && vocab >= 1, "head_bf16: 1..8 rows, a vocabulary");
+    XTG_REQUIRE(aligned16(x) && aligned16(w), "head_bf16: x and w must start on a 16-byte boundary");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int dev = 0, sms = 0;
+    XTG_CUDA(cudaGetDevice(&dev));
+    XTG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int tiles = (vocab + 127) / 128;
+    // the per-tile candidates and the rows for the argmax kernel (it reads m from a StepParams)
+    void* scratch = nullptr;
+    const size_t cand_bytes = (size_t)tiles * kMaxRows * sizeof(ArgCand);
+    XTG_CUDA(cudaMalloc(&scratch, cand_bytes + sizeof(StepParams)));
+    struct Free {
+      void* p;
+      ~Free() { cudaFree(p); }
+    } f{scratch};
+    ArgCand* cand = static_cast<ArgCand*>(scratch);
+    StepParams* params = reinterpret_cast<StepParams*>(static_cast<uint8_t*>(scratch) + cand_bytes);
+    StepParams hp = {};
+    hp.m = m;
+    XTG_CUDA(cudaMemcpyAsync(params, &hp, sizeof(hp), cudaMemcpyHostToDevice, s));
+    HeadBf16Args h = {};
+    h.x = x;
+    h.m = m;
+    h.w = w;
+    h.vocab = vocab;
+    h.hidden = hidden;
+    h.logit_scale = logit_scale;
+    h.logits = logits;
+    h.cand = cand;
+    launch_head_bf16(h, sms, s, false);
+    if (argmax) launch_argmax(cand, tiles, params, argmax, nullptr, nullptr, s, false);
+    XTG_CUDA(cudaStreamSynchronize(s));   // the scratch is freed on return
+  });
+}
+
 int xtg_cuda_topk_rows(const float* logits, int rows, int vocab, int k, float temperature, int32_t* idx, float* logit,
                        float* row_max, double* total, void* stream, char* err, int err_len) {
   return guarded(err, err_len, [&] {

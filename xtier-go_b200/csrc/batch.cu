@@ -57,7 +57,9 @@ __global__ void embed_batch_kernel(const EmbedBatchArgs a) {
   const int tok = i < m ? p.tokens[i] : 0;
   float mx = 0.f;
   for (int k = threadIdx.x; k < a.hidden; k += blockDim.x) {
-    const float v = i < m ? head_weight(a.head, a.kblocks, a.global, tok, k) : 0.f;
+    const float v = i >= m    ? 0.f
+                    : a.table ? bf16_bits_to_f32(a.table[(int64_t)tok * a.hidden + k])
+                              : head_weight(a.head, a.kblocks, a.global, tok, k);
     h[k] = v;
     hrow[k] = v;
     mx = fmaxf(mx, fabsf(v));

@@ -29,6 +29,7 @@ struct EmbedBatchArgs {
   const uint8_t* head;        // the tied NVFP4 head in tensor-core units
   int kblocks;
   float global;
+  const uint16_t* table;      // or a BF16 embedding table [vocab][hidden] (a checkpoint's)
   int hidden;
   float* h;                   // [8 nseq][hidden]
   const float* inv_freq;      // [2][64]

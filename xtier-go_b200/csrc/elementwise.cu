@@ -1,4 +1,5 @@
-// K4 / K5 helpers of the step: the embedding of a tied NVFP4 head (nvfp4_row, engine/src/kernels.cpp:34-45) with the
+// K4 / K5 helpers of the step: the embedding of a tied NVFP4 head (nvfp4_row, engine/src/kernels.cpp:34-45) or of a
+// checkpoint's BF16 table (bf16_row, kernels.cpp:157-160) with the
 // step's RoPE tables and ring bookkeeping, the nGPT residual updates (slerp_residual and the loop norms,
 // kernels.cpp:177-189 and packs/dory/dory.cpp:530-542), the argmax over the head's tile candidates
 // (engine/src/sampler.cpp:8-13), and the KV writes outside the attention kernel (KvCache::store, kv.cpp:75-112, in
@@ -59,7 +60,8 @@ __global__ void embed_kernel(const EmbedArgs a) {
   if (r < m) {
     const int tok = p->tokens[r];
     for (int k = threadIdx.x; k < a.hidden; k += blockDim.x) {
-      const float v = packed_weight(a.head, a.kblocks, a.global, tok, k);
+      const float v = a.table ? bf16_bits_to_f32(a.table[(int64_t)tok * a.hidden + k])
+                              : packed_weight(a.head, a.kblocks, a.global, tok, k);
       a.h[(int64_t)r * a.hidden + k] = v;
       rowbuf[k] = v;
     }

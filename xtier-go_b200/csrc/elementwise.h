@@ -14,6 +14,7 @@ struct EmbedArgs {
   const uint8_t* head;      // the tied NVFP4 head in tensor-core units
   int kblocks;              // 64-input blocks per row tile
   float global;
+  const uint16_t* table;    // or a BF16 embedding table [vocab][hidden] (a checkpoint's): row t is token t's
   int hidden;
   float* h;                 // [8][hidden]
   uint8_t* xb;              // B digits of h

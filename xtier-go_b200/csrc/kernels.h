@@ -120,6 +120,20 @@ void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, 
 // x f32 [m][k] (k a multiple of 16; rows m..7 zero) -> B digits xb [kblocks][1536] and prescales xb_pre [k / 16][8]
 void digitize_rows(const float* x, int m, int k, uint8_t* xb, float* xb_pre, cudaStream_t s);
 
+// ---- the BF16 lm_head of a checkpoint (head.cu) ----
+constexpr int kMaxHeadBf16Hidden = 6144;   // x's two bf16 planes stay in shared memory
+struct HeadBf16Args {
+  const float* x;             // [8][hidden] the step's rows (rows >= m unused)
+  const int* m_dev;           // rows read on the device (a replayable graph), or null: m
+  int m;
+  const uint16_t* w;          // [vocab][hidden] bf16
+  int vocab, hidden;
+  const float* logit_scale;   // [vocab], folded
+  float* logits;              // [8][vocab] or null
+  ArgCand* cand;              // [ceil(vocab / 128)][8] per-tile argmax candidates
+};
+void launch_head_bf16(const HeadBf16Args& h, int num_sms, cudaStream_t s, bool pdl);
+
 // ---- the GEMM (gemm.cu): y[m][n] = x[m][k] W^T for prefill chunks and batches ----
 constexpr int kMaxGemmRows = 65536;
 // Activation units: [ceil(m / 64)][kblocks] of 9216 bytes (4 digits x 64 rows per unit) and a factor per row

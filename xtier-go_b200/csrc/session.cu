@@ -25,6 +25,7 @@
 #include "elementwise.h"
 #include "fp4mma.cuh"
 #include "batch.h"
+#include "checkpoint.h"
 #include "json.h"
 #include "nccl_rt.h"
 #include "sampling.h"
@@ -60,6 +61,11 @@ struct Config {
   // waits for theirs, at most kv_wait_ms; "nccl": an ncclAllGather of every split's partial between the kernels
   std::string kv_exchange = "peer";
   int kv_wait_ms = 10000;
+  // a checkpoint (path to a ModelOpt W4A16_NVFP4 Dory directory; "synthetic": the seeded synthetic model): the kind
+  // of every physical sublayer, and the lm_head kept in BF16 (the reference's matmul_bf16) or quantized to NVFP4
+  std::string path = "synthetic";
+  std::vector<int> kinds;
+  bool head_bf16 = false;
 
   int n_evals() const { return n_in + n_rec * loops + n_out; }
   int phys(int e) const {
@@ -71,6 +77,7 @@ struct Config {
   // 0 MLP, 1 sliding attention, 2 global attention (the oracle's xo_synth_kind)
   int kind(int e) const {
     const int l = phys(e);
+    if (!kinds.empty()) return kinds[l];
     if (l % 2) return 0;
     const int a = l / 2;
     return (global_every > 0 && a % global_every == global_every - 1) ? 2 : 1;
@@ -91,43 +98,73 @@ int64_t parse_tier(const std::string& s) {
   return n;
 }
 
-Config parse_config(const std::string& options) {
+// Session options (JSON) over the synthetic model's shape (options "model": {...}) or a checkpoint's (ck, its
+// config.json; the options may then pick loops, kv_mode, ring and how the head is kept).
+Config parse_config(const std::string& options, const DoryConfig* ck = nullptr) {
   Config c;
   Json o = options.empty() ? Json() : Json::parse(options);
   if (o.kind != Json::Null && o.kind != Json::Object) throw CudaError("options: not a JSON object");
   const Json& m = o.at("model");
-  auto I = [&](const char* k, int& v) { v = (int)m.number(k, v); };
-  auto F = [&](const char* k, float& v) { v = (float)m.number(k, v); };
-  I("hidden", c.hidden);
-  I("ffn", c.ffn);
-  I("heads", c.heads);
-  I("kv_heads", c.kv_heads);
-  I("head_dim", c.head_dim);
-  I("vocab", c.vocab);
-  I("n_in", c.n_in);
-  I("n_rec", c.n_rec);
-  I("n_out", c.n_out);
-  I("loops", c.loops);
-  I("window", c.window);
-  c.ring = c.window + 64;
-  I("ring", c.ring);
-  I("global_every", c.global_every);
-  F("theta_sliding", c.theta_sliding);
-  F("theta_global", c.theta_global);
-  F("weight_std", c.weight_std);
-  F("lr_lo", c.lr_lo);
-  F("lr_hi", c.lr_hi);
-  F("qs_lo", c.qs_lo);
-  F("qs_hi", c.qs_hi);
-  F("gs_lo", c.gs_lo);
-  F("gs_hi", c.gs_hi);
-  F("suv_lo", c.suv_lo);
-  F("suv_hi", c.suv_hi);
-  F("ls_lo", c.ls_lo);
-  F("ls_hi", c.ls_hi);
-  F("kvs_lo", c.kvs_lo);
-  F("kvs_hi", c.kvs_hi);
-  c.seed = (uint64_t)m.number("seed", (double)c.seed);
+  if (ck) {
+    if (m.kind != Json::Null) throw CudaError("model: a checkpoint brings its own shape (no \"model\" option)");
+    c.hidden = ck->hidden;
+    c.ffn = ck->ffn;
+    c.heads = ck->heads;
+    c.kv_heads = ck->kv_heads;
+    c.head_dim = ck->head_dim;
+    c.vocab = ck->vocab;
+    c.n_in = ck->n_in;
+    c.n_rec = ck->n_rec;
+    c.n_out = ck->n_out;
+    c.kinds = ck->kind;
+    c.global_every = 0;
+    c.theta_sliding = ck->theta_sliding;
+    c.theta_global = ck->theta_global;
+    const bool sliding = std::count(c.kinds.begin(), c.kinds.end(), 1) > 0;
+    c.window = sliding ? ck->window : 64;   // no sliding layer: a ring nothing reads
+    c.ring = (int)o.number("ring", c.window + 64);
+    c.loops = (int)o.number("loops", ck->default_loops);
+    if (c.loops < 1 || c.loops > 4) throw CudaError("loops: 1..4");
+    const std::string mode = o.string("kv_mode", ck->kv_mode);
+    if (mode != "per_loop") throw CudaError("kv_mode: " + mode + " (only per_loop: a KV instance per loop)");
+    const std::string head = o.string("head", "bf16");
+    if (head != "bf16" && head != "nvfp4") throw CudaError("head: " + head + " (bf16 | nvfp4)");
+    c.head_bf16 = head == "bf16";
+  }
+  if (!ck) {   // the synthetic model's shape and seeds
+    auto I = [&](const char* k, int& v) { v = (int)m.number(k, v); };
+    auto F = [&](const char* k, float& v) { v = (float)m.number(k, v); };
+    I("hidden", c.hidden);
+    I("ffn", c.ffn);
+    I("heads", c.heads);
+    I("kv_heads", c.kv_heads);
+    I("head_dim", c.head_dim);
+    I("vocab", c.vocab);
+    I("n_in", c.n_in);
+    I("n_rec", c.n_rec);
+    I("n_out", c.n_out);
+    I("loops", c.loops);
+    I("window", c.window);
+    c.ring = c.window + 64;
+    I("ring", c.ring);
+    I("global_every", c.global_every);
+    F("theta_sliding", c.theta_sliding);
+    F("theta_global", c.theta_global);
+    F("weight_std", c.weight_std);
+    F("lr_lo", c.lr_lo);
+    F("lr_hi", c.lr_hi);
+    F("qs_lo", c.qs_lo);
+    F("qs_hi", c.qs_hi);
+    F("gs_lo", c.gs_lo);
+    F("gs_hi", c.gs_hi);
+    F("suv_lo", c.suv_lo);
+    F("suv_hi", c.suv_hi);
+    F("ls_lo", c.ls_lo);
+    F("ls_hi", c.ls_hi);
+    F("kvs_lo", c.kvs_lo);
+    F("kvs_hi", c.kvs_hi);
+    c.seed = (uint64_t)m.number("seed", (double)c.seed);
+  }
   const Json& ctx = o.at("context");
   if (ctx.kind == Json::String)
     c.context = parse_tier(ctx.str);
@@ -165,6 +202,9 @@ Config parse_config(const std::string& options) {
   if (c.context < 64 || c.context % 64) throw CudaError("context: a multiple of 64");
   if (c.decode_rows < 1 || c.decode_rows > kMaxRows) throw CudaError("decode_rows: 1..8");
   if (c.snapshots < 0 || c.snapshots > 8) throw CudaError("snapshots: 0..8");
+  if (ck && c.context > ck->max_pos) throw CudaError("context: above the model's max_position_embeddings");
+  if (c.head_bf16 && (c.hidden > kMaxHeadBf16Hidden || c.hidden % 32))
+    throw CudaError("head: bf16 takes hidden <= 6144 (a multiple of 32); use \"nvfp4\"");
   return c;
 }
 
@@ -238,6 +278,10 @@ struct xtg_cuda {
   Linear head;
   float* logit_scale = nullptr;
   float* inv_freq = nullptr;   // [2][64]
+  // a checkpoint's BF16 embedding table and (head "bf16") BF16 lm_head, [vocab][hidden]; null for the synthetic
+  // model, whose tied NVFP4 head is also its embedding
+  uint16_t* embed_bf16 = nullptr;
+  uint16_t* head_w_bf16 = nullptr;
   // session
   std::vector<KvInst> kv;
   int32_t* ring_pos_dev = nullptr;
@@ -368,6 +412,10 @@ struct xtg_cuda {
   // ---- model construction (the seeded synthetic Dory; the oracle's stream map) ----
 
   void build_model() {
+    if (c.path != "synthetic") {
+      load_checkpoint();
+      return;
+    }
     const int H = c.hidden, F = c.ffn, Q = c.heads * c.head_dim, KV = c.kv_heads * c.head_dim;
     const int ne = c.n_evals();
     // arena size
@@ -503,6 +551,190 @@ struct xtg_cuda {
     cudaFree(amax);
   }
 
+  // ---- a Dory checkpoint (packs/dory/dory.cpp:316-439): ModelOpt NVFP4 rows repacked into tensor-core units ----
+  // Weights of a recurrent sublayer are packed once and read by every loop's evaluation; each attention evaluation
+  // keeps its own KV instance (per_loop). The stored scales are folded as the reference folds them: logit scale /
+  // init_range, |alpha| * alpha_init / init_range, (sqk sqrt(head_dim) / init_range)^2, (s_gate sqrt(gate_init) /
+  // init_range)^2, suv * sqrt(hidden).
+  void load_checkpoint() {
+    const DoryConfig dc = read_dory_config(c.path);
+    SafeTensors st(c.path + "/model.safetensors");
+    const int H = c.hidden, F = c.ffn, Q = c.heads * c.head_dim, KV = c.kv_heads * c.head_dim, V = c.vocab;
+    const int ne = c.n_evals(), layers = (int)c.kinds.size();
+    const int tq = packed_tiles(Q, false), tk = packed_tiles(KV, false);
+    int64_t total = 0;
+    for (int l = 0; l < layers; ++l)
+      total += c.kinds[l] == 0 ? packed_bytes(F, H, true) + packed_bytes(H, F, false)
+                               : (int64_t)(2 * tq + 2 * tk) * packed_kblocks(H) * kPackUnitBytes + packed_bytes(H, Q, false);
+    if (!c.head_bf16) total += packed_bytes(V, H, false);
+    arena_bytes = total;
+    arena = walloc<uint8_t>((size_t)total);
+    const int64_t max_elems = std::max<int64_t>({(int64_t)F * H, (int64_t)Q * H, c.head_bf16 ? 0 : (int64_t)V * H});
+    uint8_t *codes_a = nullptr, *scales_a = nullptr, *codes_b = nullptr, *scales_b = nullptr;
+    XTG_CUDA(cudaMalloc(&codes_a, max_elems / 2));
+    XTG_CUDA(cudaMalloc(&scales_a, max_elems / 16));
+    XTG_CUDA(cudaMalloc(&codes_b, (int64_t)F * H / 2));
+    XTG_CUDA(cudaMalloc(&scales_b, (int64_t)F * H / 16));
+    struct Temps {
+      std::vector<void*> p;
+      ~Temps() {
+        for (void* q : p) cudaFree(q);
+      }
+    } temps;
+    temps.p = {codes_a, scales_a, codes_b, scales_b};
+    auto h2d = [&](void* dst, const TensorView& t) {
+      XTG_CUDA(cudaMemcpyAsync(dst, t.data, t.bytes, cudaMemcpyHostToDevice, stream));
+    };
+    // an NVFP4 weight's codes and scales into (codes, scales); its global scale
+    auto nvfp4 = [&](const std::string& name, int n_out, int k, uint8_t* codes, uint8_t* scales) {
+      h2d(codes, st.get(name + ".weight", "U8", {n_out, k / 2}));
+      h2d(scales, st.get(name + ".weight_scale", "F8_E4M3", {n_out, k / 16}));
+      const TensorView& g = st.get(name + ".weight_scale_2", "F32", {});
+      float v;
+      std::memcpy(&v, g.data, 4);
+      XTG_CUDA(cudaStreamSynchronize(stream));   // the temporaries are reused by the next weight
+      return v;
+    };
+    auto bf16_vec = [&](const std::string& name, int n) {
+      const TensorView& t = st.get(name, "BF16", {n});
+      std::vector<float> v(n);
+      for (int i = 0; i < n; ++i) {
+        uint16_t hb;
+        std::memcpy(&hb, t.data + 2 * i, 2);
+        v[i] = bf16_bits_f32(hb);
+      }
+      return v;
+    };
+    auto wupload = [&](const std::vector<float>& v) {
+      float* d = walloc<float>(v.size());
+      XTG_CUDA(cudaMemcpyAsync(d, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice, stream));
+      XTG_CUDA(cudaStreamSynchronize(stream));
+      return d;
+    };
+    uint8_t* cursor = arena;
+    auto place = [&](Linear& L, int tiles, int kblocks, int max_split = 8, int max_tpc = 1 << 20) {
+      L.w = cursor;
+      L.tiles = tiles;
+      L.kblocks = kblocks;
+      L.bytes = (int64_t)tiles * kblocks * kPackUnitBytes;
+      L.plan = plan_gemv(tiles, kblocks, num_sms, max_split, max_tpc);
+      cursor += L.bytes;
+    };
+    auto alg = [](int n, int k) { return (int64_t)n * k / 2 + (int64_t)n * k / 16 + 4; };
+    const float alpha_scale = dc.alpha_init / dc.init_range;
+    const float sqk_factor = std::sqrt(float(c.head_dim)) / dc.init_range;
+    const float gate_factor = std::sqrt(dc.gate_init) / dc.init_range;
+    const float suv_factor = std::sqrt(float(H));
+    proj_ld = 2 * Q + 2 * KV;
+    evals.resize(ne);
+    std::vector<int> first(layers, -1);
+    int n_attn = 0;
+    for (int e = 0; e < ne; ++e) {
+      Eval& E = evals[e];
+      const int l = c.phys(e);
+      if (first[l] >= 0) {   // a later loop of a recurrent sublayer: the same weights
+        E = evals[first[l]];
+        if (E.kind != 0) E.cache = n_attn++;
+        continue;
+      }
+      first[l] = e;
+      E.kind = c.kinds[l];
+      const std::string p = "backbone.layers." + std::to_string(l) + ".";
+      std::vector<float> lr = bf16_vec(p + (E.kind == 0 ? "mlp_alpha" : "attn_alpha"), H);
+      for (float& x : lr) x = std::fabs(x * alpha_scale);
+      E.lr = wupload(lr);
+      if (E.kind == 0) {
+        std::vector<float> sg = bf16_vec(p + "mixer.suv_gate", F), su = bf16_vec(p + "mixer.suv_up", F);
+        for (float& x : sg) x *= suv_factor;
+        for (float& x : su) x *= suv_factor;
+        E.sg = wupload(sg);
+        E.su = wupload(su);
+        place(E.gu, packed_tiles(F, true), packed_kblocks(H), 8, 1);
+        E.gu.g0 = nvfp4(p + "mixer.gate_proj", F, H, codes_a, scales_a);
+        E.gu.g1 = nvfp4(p + "mixer.up_proj", F, H, codes_b, scales_b);
+        pack_nvfp4(codes_a, scales_a, codes_b, scales_b, F, H, true, E.gu.w, stream);
+        E.gu.alg_bytes = 2 * alg(F, H);
+        E.gu.n_total = 2 * F;
+        E.gu.k = H;
+        place(E.down, packed_tiles(H, false), packed_kblocks(F));
+        E.down.g0 = nvfp4(p + "mixer.down_proj", H, F, codes_a, scales_a);
+        pack_nvfp4(codes_a, scales_a, nullptr, nullptr, H, F, false, E.down.w, stream);
+        E.down.alg_bytes = alg(H, F);
+        E.down.n_total = H;
+        E.down.k = F;
+      } else {
+        std::vector<float> qs = bf16_vec(p + "mixer.sqk", Q), gs = bf16_vec(p + "mixer.s_gate", Q);
+        for (float& x : qs) x = (x * sqk_factor) * (x * sqk_factor);
+        for (float& x : gs) x = (x * gate_factor) * (x * gate_factor);
+        E.qscale = wupload(qs);
+        E.gscale = wupload(gs);
+        E.theta = E.kind == 2 ? 1 : 0;
+        E.cache = n_attn++;
+        const int kblocks = packed_kblocks(H);
+        place(E.qkvg, 2 * tq + 2 * tk, kblocks);
+        const int n_out[4] = {Q, KV, KV, Q};
+        const char* names[4] = {"mixer.q_proj", "mixer.k_proj", "mixer.v_proj", "mixer.g_proj"};
+        int tile0 = 0;
+        for (int j = 0; j < 4; ++j) {
+          E.gq[j] = nvfp4(p + names[j], n_out[j], H, codes_a, scales_a);
+          pack_nvfp4(codes_a, scales_a, nullptr, nullptr, n_out[j], H, false,
+                     E.qkvg.w + (int64_t)tile0 * kblocks * kPackUnitBytes, stream);
+          tile0 += packed_tiles(n_out[j], false);
+          E.qkvg.alg_bytes += alg(n_out[j], H);
+        }
+        E.qkvg.n_total = 2 * Q + 2 * KV;
+        E.qkvg.k = H;
+        place(E.o, packed_tiles(H, false), packed_kblocks(Q));
+        E.o.g0 = nvfp4(p + "mixer.o_proj", H, Q, codes_a, scales_a);
+        pack_nvfp4(codes_a, scales_a, nullptr, nullptr, H, Q, false, E.o.w, stream);
+        E.o.alg_bytes = alg(H, Q);
+        E.o.n_total = H;
+        E.o.k = Q;
+      }
+    }
+    // the embedding table and the head (untied, packs/dory/dory.cpp:322-327)
+    embed_bf16 = walloc<uint16_t>((size_t)V * H);
+    h2d(embed_bf16, st.get("backbone.embeddings.weight", "BF16", {V, H}));
+    const TensorView& lm = st.get("lm_head.weight", "BF16", {V, H});
+    head.tiles = packed_tiles(V, false);
+    head.kblocks = packed_kblocks(H);
+    head.n_total = V;
+    head.k = H;
+    if (c.head_bf16) {
+      head_w_bf16 = walloc<uint16_t>((size_t)V * H);
+      h2d(head_w_bf16, lm);
+      head.alg_bytes = (int64_t)V * H * 2;
+      head.g0 = 1.f;
+    } else {   // quantized here, as the synthetic model's head is
+      uint16_t* raw = nullptr;
+      float* gdev = nullptr;
+      unsigned int* amax = nullptr;
+      XTG_CUDA(cudaMalloc(&raw, (size_t)V * H * 2));
+      temps.p.push_back(raw);
+      XTG_CUDA(cudaMalloc(&gdev, sizeof(float)));
+      temps.p.push_back(gdev);
+      XTG_CUDA(cudaMalloc(&amax, sizeof(unsigned int)));
+      temps.p.push_back(amax);
+      h2d(raw, lm);
+      quantize_nvfp4(raw, V, H, codes_a, scales_a, gdev, amax, stream);
+      place(head, head.tiles, head.kblocks, 1);
+      pack_nvfp4(codes_a, scales_a, nullptr, nullptr, V, H, false, head.w, stream);
+      XTG_CUDA(cudaMemcpyAsync(&head.g0, gdev, sizeof(float), cudaMemcpyDeviceToHost, stream));
+      head.alg_bytes = alg(V, H);
+    }
+    std::vector<float> ls = bf16_vec("lm_head.logit_scale", V);
+    for (float& x : ls) x /= dc.init_range;
+    logit_scale = wupload(ls);
+    XTG_REQUIRE(cursor == arena + arena_bytes, "weight arena size mismatch");
+    std::vector<float> inv(128);
+    const float th[2] = {c.theta_sliding > 0 ? c.theta_sliding : 1e4f, c.theta_global > 0 ? c.theta_global : 1e4f};
+    for (int t = 0; t < 2; ++t)
+      for (int i = 0; i < 64; ++i) inv[t * 64 + i] = 1.f / std::pow(th[t], float(2 * i) / float(c.head_dim));
+    inv_freq = wupload(inv);
+    XTG_CUDA(cudaStreamSynchronize(stream));
+    make_outs();
+  }
+
   // this session's output descriptors of the STORE / q|k|v GEMVs (they point into its own activation buffers)
   static std::vector<TileOut> tile_outs(float* y, int ld, int n, float g) {
     std::vector<TileOut> v(packed_tiles(n, false));
@@ -536,6 +768,8 @@ struct xtg_cuda {
     evals = m.evals;
     head = m.head;
     logit_scale = m.logit_scale;
+    embed_bf16 = m.embed_bf16;
+    head_w_bf16 = m.head_w_bf16;
     inv_freq = m.inv_freq;
     proj_ld = m.proj_ld;
     make_outs();
@@ -659,6 +893,7 @@ struct xtg_cuda {
     ea.head = head.w;
     ea.kblocks = head.kblocks;
     ea.global = head.g0;
+    ea.table = embed_bf16;
     ea.hidden = H;
     ea.h = h;
     ea.xb = xb;
@@ -812,14 +1047,29 @@ struct xtg_cuda {
       }
     }
     for (int l = 0; l < c.n_out; ++l) sublayer(e++);
-    GemvArgs a = gemv_args(head);
-    a.outs = nullptr;
-    a.g_head = head.g0;
-    a.logit_scale = logit_scale;
-    a.logits = logits;
-    a.vocab = c.vocab;
-    a.cand = cand;
-    gemv(head, kEpiHead, a, xb, xb_pre, pdl);
+    if (head_w_bf16) {   // a checkpoint's BF16 head over the f32 rows
+      HeadBf16Args hb = {};
+      hb.x = h;
+      hb.m_dev = &params_dev->m;
+      hb.w = head_w_bf16;
+      hb.vocab = c.vocab;
+      hb.hidden = H;
+      hb.logit_scale = logit_scale;
+      hb.logits = logits;
+      hb.cand = cand;
+      mark(kClsGemv, true);
+      launch_head_bf16(hb, num_sms, stream, pdl);
+      mark(kClsGemv, false);
+    } else {
+      GemvArgs a = gemv_args(head);
+      a.outs = nullptr;
+      a.g_head = head.g0;
+      a.logit_scale = logit_scale;
+      a.logits = logits;
+      a.vocab = c.vocab;
+      a.cand = cand;
+      gemv(head, kEpiHead, a, xb, xb_pre, pdl);
+    }
     mark(kClsSmall, true);
     launch_argmax(cand, head.tiles, params_dev, argmax, argmax_val, epoch, stream, pdl);
     mark(kClsSmall, false);
@@ -1267,6 +1517,7 @@ struct BatchStep {
     ea.head = model->head.w;
     ea.kblocks = model->head.kblocks;
     ea.global = model->head.g0;
+    ea.table = model->embed_bf16;
     ea.hidden = H;
     ea.h = h;
     ea.inv_freq = model->inv_freq;
@@ -1494,7 +1745,7 @@ BatchStep* batch_for(const std::vector<xtg_cuda*>& key) {
 // chunk is at most the slack (64 for the 1088-slot ring over a window of 1024).
 int prefill_rows(const xtg_cuda* h) {
   const Config& c = h->c;
-  if (!c.batch || !c.graph || c.kv_world != 1) return 0;
+  if (!c.batch || !c.graph || c.kv_world != 1 || h->head_w_bf16) return 0;   // the batched step's head is NVFP4
   const int slack = c.ring - c.window;
   return std::min(kMaxBatch * kMaxRows, slack / kMaxRows * kMaxRows);
 }
@@ -1544,7 +1795,8 @@ bool batchable(xtg_cuda* const* hs, int nh) {
   if (nh < 2) return false;
   for (int i = 0; i < nh; ++i) {
     const Config& c = hs[i]->c;
-    if (!c.batch || !c.graph || c.kv_world != 1 || hs[i]->wmem != hs[0]->wmem || c.device != hs[0]->c.device ||
+    if (!c.batch || !c.graph || c.kv_world != 1 || hs[i]->head_w_bf16 || hs[i]->wmem != hs[0]->wmem ||
+        c.device != hs[0]->c.device ||
         c.kv_dtype != hs[0]->c.kv_dtype || c.decode_rows != hs[0]->c.decode_rows)
       return false;
   }
@@ -1646,10 +1898,16 @@ xtg_cuda* xtg_cuda_open(const char* model_path, const char* options, char* err, 
   std::unique_ptr<xtg_cuda> h;
   try {
     const std::string path = model_path ? model_path : "";
-    if (path != "synthetic")
-      throw CudaError("model " + path + ": only \"synthetic\" (the seeded synthetic Dory) is supported");
+    if (path.empty()) throw CudaError("model: no path (a Dory checkpoint directory, or \"synthetic\")");
     h = std::make_unique<xtg_cuda>();
-    h->c = parse_config(options ? options : "");
+    if (path == "synthetic") {
+      h->c = parse_config(options ? options : "");
+    } else {   // read and checked before any device work
+      const DoryConfig dc = read_dory_config(path);
+      h->c = parse_config(options ? options : "", &dc);
+      h->c.path = path;
+      SafeTensors probe(path + "/model.safetensors");
+    }
     int ndev = 0;
     XTG_CUDA(cudaGetDeviceCount(&ndev));
     XTG_REQUIRE(h->c.device >= 0 && h->c.device < ndev, "device: no CUDA device " + std::to_string(h->c.device));
@@ -1722,13 +1980,15 @@ int xtg_cuda_info(xtg_cuda* h, char* out, int out_len) {
       "\"kv_instances\":%d,\"ring_instances\":%d,\"ring_slots\":%d,\"sliding_window\":%d,\"kv_bytes\":%lld,"
       "\"snapshots\":%d,\"kvmap\":false,\"kv_dtype\":\"%s\",\"weight_bytes\":%lld,\"hidden\":%d,\"evaluations\":%d,"
       "\"sm_count\":%d,\"graph\":%s,\"pdl\":%s,\"splits_global\":%d,\"splits_ring\":%d,"
-      "\"kv_world\":%d,\"kv_rank\":%d,\"kv_exchange\":\"%s\",\"global_layers\":%d}",
+      "\"kv_world\":%d,\"kv_rank\":%d,\"kv_exchange\":\"%s\",\"global_layers\":%d,\"source\":\"%s\","
+      "\"head\":\"%s\",\"loops\":%d}",
       h->c.vocab, (long long)h->c.context, (long long)h->c.context - 1, std::max(h->c.decode_rows, prefill_rows(h)),
       h->c.decode_rows,
       (int)h->kv.size(), rings, h->c.ring, h->c.window, (long long)h->kv_bytes(), (int)h->snaps.size(),
       h->c.kv_dtype == kKvFp8 ? "fp8" : "int8", (long long)h->arena_bytes, h->c.hidden, h->c.n_evals(), h->num_sms,
       h->c.graph ? "true" : "false", h->c.pdl ? "true" : "false", h->splits_g, h->splits_r,
-      h->c.kv_world, h->c.kv_rank, h->c.kv_world > 1 ? h->c.kv_exchange.c_str() : "none", h->n_glob);
+      h->c.kv_world, h->c.kv_rank, h->c.kv_world > 1 ? h->c.kv_exchange.c_str() : "none", h->n_glob,
+      h->c.path == "synthetic" ? "synthetic" : "checkpoint", h->head_w_bf16 ? "bf16" : "nvfp4", h->c.loops);
   return len < out_len ? len : -1;
 }
 
