@@ -535,7 +535,7 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
     if (d == 0) a.asum[h * a.asum_ld + rows0 + i] = ss;
     return;
   }
-  if (d == 0) a.asum[h * kMaxRows + i] = ss;
+  if (d == 0) a.asum[(int64_t)i * a.heads + h] = ss;   // [row][head]: the O projection's parts of row i together
   // the O projection's input: this head's 8 groups of 16 as B digits (warp 0, a quad per group)
   __shared__ float ov[kD];
   ov[d] = o;

@@ -109,7 +109,7 @@ struct CombineArgs {
   const float* gscale;      // [heads * 128]
   uint8_t* ab;              // step: the gated output as B digits (the O projection's input, K = heads * 128)
   float* ab_pre;            // [heads * 8][8] their prescales
-  float* asum;              // step: [heads][8] sum of squares per head and activation row
+  float* asum;              // step: [8][heads] sum of squares per activation row and head
   int pdl;
   PeerXchg x;               // split-KV across GPUs: splits are this process's, merged with the peers' here
   int* err;                 // set if the wait for a peer gave up

@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kSlerpThreads) resid_slerp_kernel(const ResidA
     const int q = t + it * kSlerpThreads;
     const bool lq = live && q < a.nparts;
 #pragma unroll
-    for (int k = 0; k < 5; ++k) pv[it][k] = lq ? a.rsum[((int64_t)q * 8 + r) * 5 + k] : 0.f;
+    for (int k = 0; k < 5; ++k) pv[it][k] = lq ? a.rsum[((int64_t)k * 8 + r) * a.nparts + q] : 0.f;
   }
   float* h = a.h + (int64_t)r * H;
   const float4 h4 = ld4(h, c, ok && live), o4 = ld4(a.o + (int64_t)r * H, c, ok && live);

@@ -309,26 +309,27 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     const int i = warp;   // warp i: activation row i
     float pmin = a.xb_fixed;
     if (!(a.xb_fixed > 0.f)) {
+      // the slice's prescales ([group][row]) are one contiguous range: every thread loads a share (whole cache
+      // lines per warp), then warp i takes row i's smallest from shared memory
+      const float* src = a.xb_pre + (int64_t)k0 * 4 * 8;
+      for (int e = tid; e < nkb * 4 * 8; e += kThreads) pre_s[e] = src[e];
+      __syncthreads();
       pmin = 3.0e38f;
-      for (int b = lane; b < nkb * 4; b += 32) {
-        const float pb = a.xb_pre[((int64_t)k0 * 4 + b) * 8 + i];
-        pre_s[b * 8 + i] = pb;
-        pmin = fminf(pmin, pb);
-      }
+      for (int b = lane; b < nkb * 4; b += 32) pmin = fminf(pmin, pre_s[b * 8 + i]);
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) pmin = fminf(pmin, __shfl_xor_sync(0xffffffffu, pmin, o));
     }
     if (lane == 0) pslice[i] = pmin;
     if (EPI == kEpiStore) {
-      // the row's sum of squares over the producer's parts: lane l takes parts l, l + 32, ... (one wave of loads),
-      // then a butterfly over the warp (a fixed order)
+      // the row's sum of squares over the producer's parts ([row][part]): lane l takes parts l, l + 32, ... (one
+      // wave of coalesced loads), then a butterfly over the warp (a fixed order)
       float t = 1.f;
       if (a.sumsq) {
         float pv[kSumsqLoads];
 #pragma unroll
         for (int u = 0; u < kSumsqLoads; ++u) {
           const int q = lane + 32 * u;
-          pv[u] = q < a.nparts ? a.sumsq[q * 8 + i] : 0.f;
+          pv[u] = q < a.nparts ? a.sumsq[(int64_t)i * a.nparts + q] : 0.f;
         }
         t = pv[0];
 #pragma unroll
@@ -628,9 +629,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
 #pragma unroll
           for (int k = 0; k < 5; ++k) v[k] += __shfl_xor_sync(0xffffffffu, v[k], off);
         if (tid < nr * 8 && rl == 0) {
-          float* dst = a.rsum + ((int64_t)blockIdx.x * 8 + i) * 5;
 #pragma unroll
-          for (int k = 0; k < 5; ++k) dst[k] = v[k];
+          for (int k = 0; k < 5; ++k) a.rsum[((int64_t)k * 8 + i) * gridDim.x + blockIdx.x] = v[k];
         }
       } else {
         for (int p = tid; p < nr * 8; p += kThreads) {
@@ -668,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
       if (tid < 8) {
         float s2 = 0.f;
         for (int e = 0; e < 4 * (g1 - g0); ++e) s2 += vsq[tid * 16 + e];
-        a.vsum[((int64_t)t * S + srank) * 8 + tid] = s2;
+        a.vsum[(int64_t)tid * gridDim.x + blockIdx.x] = s2;   // [row][part], part = t * S + srank
       }
     }
   }

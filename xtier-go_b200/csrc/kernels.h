@@ -62,7 +62,7 @@ struct GemvArgs {
   int m;
   // kEpiStore
   const TileOut* outs;       // [tiles]
-  const float* sumsq;        // optional: y *= 1 / sqrt(sum_p sumsq[p][n] + 1e-6), p < nparts (a justnorm of x)
+  const float* sumsq;        // optional: y *= 1 / sqrt(sum_p sumsq[n][p] + 1e-6), p < nparts (a justnorm of x)
   int nparts;
   // kEpiSwiglu (interleaved gate / up tiles): v = silu(g * sg) * (u * su) as the next GEMV's digits (K = F)
   float g_gate, g_up;
@@ -71,7 +71,7 @@ struct GemvArgs {
   int features;              // F
   uint8_t* vb;               // [tiles][1536]
   float* vb_pre;             // [tiles * 4][8]
-  float* vsum;               // [tiles * split][8]: sums of v^2 over the features each CTA finishes
+  float* vsum;               // [8][tiles * split]: sums of v^2 over the features each CTA (part) finishes
   // kEpiQkv: the q | k | v | g projection of an attention sublayer, one 128-row tile per head (head_dim 128): tiles
   // [0, q_tiles) are q heads, then kv_tiles k heads, kv_tiles v heads, and the gate tiles (stored through `outs` as
   // kEpiStore does). q: RoPE, justnorm, times its q scale; k: RoPE, justnorm; k and v rows go into the KV cache and
@@ -100,7 +100,8 @@ struct GemvArgs {
   // kEpiStore, split tiles (split >= 4), optional: the row sums the nGPT residual update that follows needs, per CTA,
   // so that it reduces a few partials instead of whole rows. For the output dims y this CTA finishes (global index
   // tile * 128 + r) and activation row i: sums of h^2, y^2, (1 - lr)^2 h^2, lr (1 - lr) h y, lr^2 y^2 ->
-  // rsum[(cta * 8 + i) * 5 + k]; h [8][rs_ld] is the residual stream the update starts from
+  // rsum[(k * 8 + i) * grid + cta] (each sum's parts contiguous); h [8][rs_ld] is the residual stream the update
+  // starts from
   float* rsum;
   const float* rs_h;
   const float* rs_lr;
