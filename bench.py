@@ -510,9 +510,9 @@ def config2_block(x, device, reps=6):
 def split_kv_block(x, rank, world, local_rank, dist, steps, warmup, context=32768):
     """The batch-1 long-context step split across the N processes: one sequence at 32K context, every process holding
     the whole model and every cache, each attending 1/N of the global caches' chunks, the attention partials joined
-    by the attention kernels themselves (stores into every process's buffer over NVLink, flags that the combine
-    waits on) or, for comparison, by an NCCL all-gather between the kernels. Against the same step on one GPU (every
-    rank runs that alone too). Times are the max over ranks."""
+    inside the combine kernel (each process's merged partial stored into every peer's slots over NVLink as words
+    carrying the step's sequence number) or, for comparison, by an NCCL all-gather between the kernels. Against the
+    same step on one GPU (every rank runs that alone too). Times are the max over ranks."""
     import torch
     model = dict(x.DORY_3072)
     out = {"context": context, "n_past": context - 8}

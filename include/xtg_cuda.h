@@ -165,8 +165,8 @@ XTG_CUDA_API void xtg_cuda_linear_free(xtg_cuda_linear* w);
 
 // A checkpoint's BF16 lm_head: matmul_bf16 (engine/src/kernels.cpp:140-155) times the folded logit scale
 // (packs/dory/dory.cpp:566-576) for m <= 8 rows, and each row's argmax (ties to the lowest index, sampler.cpp:8-13).
-// Device pointers: x [m][hidden] f32, w [vocab][hidden] bf16 (both 16-byte aligned; hidden a multiple of 32, at most
-// 6144), logit_scale [vocab], logits [m][vocab] (or NULL), argmax [m] int32 (or NULL). Waits for the result.
+// Device pointers: x [m][hidden] f32, w [vocab][hidden] bf16 (both 16-byte aligned; hidden a multiple of 64, at most
+// 5120), logit_scale [vocab], logits [m][vocab] (or NULL), argmax [m] int32 (or NULL). Waits for the result.
 XTG_CUDA_API int xtg_cuda_head_bf16(const float* x, int m, const uint16_t* w, int vocab, int hidden,
                                     const float* logit_scale, float* logits, int32_t* argmax, void* stream, char* err,
                                     int err_len);
@@ -206,7 +206,7 @@ XTG_CUDA_API int xtg_cuda_attention(const xtg_cuda_attn_args* a, int splits, voi
 
 // No counterpart in the reference. xtg_cuda_attention for callers that cannot call cudaMalloc: a host runtime that
 // reserved the GPU's memory for its own arena at start-up, or a path on which an allocation may not block or
-// synchronise the device. The same kernels and results; the split-KV partials live in a fixed 4,259,840-byte array
+// synchronise the device. The same kernels and results; the split-KV partials live in a fixed 4,325,376-byte array
 // of this library, so kv_heads x splits must be at most 256 (larger requests fail with an error). It allocates
 // nothing, enqueues both kernels on `stream` and returns without waiting. The array is held on every GPU that loads
 // the library until the process exits; the first call on a device looks up its address there (make that call

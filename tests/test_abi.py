@@ -52,14 +52,14 @@ def test_open_rejects_unknown_models_and_bad_options(xtg):
 
 @pytest.mark.parametrize("entry", ["xtg_cuda_attention", "xtg_cuda_attention_noalloc"])
 def test_attention_rejects_unaligned_pointers_before_any_device_work(xtg, entry):
-    """The cache is read by 16-byte bulk copies and q by 16-byte loads: a pointer off a 16-byte boundary is an
-    error at the call (checked on the host, so this runs without a GPU), never a GPU fault."""
+    """The cache is read by 16-byte bulk copies, q, k, v and out by 16-byte loads and stores: a pointer off a 16-byte
+    boundary is an error at the call (checked on the host, so this runs without a GPU), never a GPU fault."""
     good, bad = 4096, 4096 + 4
-    for field in ("q", "k_codes", "v_codes", "k_scales", "v_scales"):
-        ptrs = dict(q=good, k=good, v=good, k_codes=good, v_codes=good, k_scales=good, v_scales=good)
+    for field in ("q", "k", "v", "out", "k_codes", "v_codes", "k_scales", "v_scales"):
+        ptrs = dict(q=good, k=good, v=good, out=good, k_codes=good, v_codes=good, k_scales=good, v_scales=good)
         ptrs[field] = bad
         a = xtg.AttnArgs(8, 100, 24, 6, 128, 0, 0.1, ptrs["q"], ptrs["k"], ptrs["v"], ptrs["k_codes"],
-                         ptrs["v_codes"], ptrs["k_scales"], ptrs["v_scales"], 128, 0, None, 0, good)
+                         ptrs["v_codes"], ptrs["k_scales"], ptrs["v_scales"], 128, 0, None, 0, ptrs["out"])
         err = C.create_string_buffer(512)
         rc = getattr(xtg.lib(), entry)(C.byref(a), 4, None, err, len(err))
         assert rc == -1 and b"16-byte" in err.value, (field, err.value)

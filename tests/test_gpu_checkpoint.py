@@ -98,7 +98,7 @@ def test_checkpoint_bf16_head_keeps_verify_steps(cuda, xtg, ckpt):
     check(got, want)
 
 
-@pytest.mark.parametrize("vocab,hidden,m", [(131072, 3072, 8), (4099, 512, 3), (200, 6144, 1)])
+@pytest.mark.parametrize("vocab,hidden,m", [(131072, 3072, 8), (4099, 512, 3), (200, 5120, 1)])
 def test_head_bf16_kernel(cuda, xtg, vocab, hidden, m):
     """xtg_cuda_head_bf16 at the Dory-3072 head shape and ragged ones against a float64 torch reference of
     matmul_bf16 x logit scale: |d logit| <= 1e-3 (x is carried as bf16 hi + lo, ~16 bits), argmax a true maximum."""

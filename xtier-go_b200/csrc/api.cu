@@ -67,9 +67,10 @@ int guarded(char* err, int err_len, F&& f) {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 void require_attn_alignment(const xtg_cuda_attn_args* p) {
-  XTG_REQUIRE(aligned16(p->q) && aligned16(p->k_codes) && aligned16(p->v_codes) && aligned16(p->k_scales) &&
-                  aligned16(p->v_scales) && (p->ring == 0 || aligned16(p->ring_pos)),
-              "attention: q, the cache codes and scales and the ring table must start on 16-byte boundaries");
+  XTG_REQUIRE(aligned16(p->q) && aligned16(p->k) && aligned16(p->v) && aligned16(p->out) && aligned16(p->k_codes) &&
+                  aligned16(p->v_codes) && aligned16(p->k_scales) && aligned16(p->v_scales) &&
+                  (p->ring == 0 || aligned16(p->ring_pos)),
+              "attention: q, k, v, out, the cache codes and scales and the ring table must start on 16-byte boundaries");
 }
 
 }  // namespace
@@ -252,12 +253,12 @@ int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, ch
 // Some callers cannot call cudaMalloc: a host runtime that reserved the GPU's memory for its own arena at start-up
 // (a fresh allocation then fails, or fragments that arena), and code on a path where an allocation may not block
 // or synchronise the device. xtg_cuda_attention allocates its split-KV partials per call; for those callers
-// xtg_cuda_attention_noalloc keeps them in the fixed array below instead: 4,259,840 bytes, room for 256 KV-head x
-// split pairs (32 query rows x 130 floats each). Every GPU that loads this library holds the array until the process
+// xtg_cuda_attention_noalloc keeps them in the fixed array below instead: 4,325,376 bytes, room for 256 KV-head x
+// split pairs (32 query rows x 132 floats each). Every GPU that loads this library holds the array until the process
 // exits. All calls share it, and it keeps the last call's contents.
 namespace {
 constexpr int kNoAllocPairs = 256;
-constexpr int64_t kNoAllocFloats = (int64_t)kNoAllocPairs * 32 * 130;
+constexpr int64_t kNoAllocFloats = (int64_t)kNoAllocPairs * 32 * 132;
 }  // namespace
 
 // In host code this name is only a host-side stand-in for the array; its device address comes from
@@ -298,7 +299,7 @@ int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* p, int splits, void* st
     XTG_REQUIRE(p->ring != 0 || p->pos0 <= p->slots, "attention: pos0 beyond the cache");
     XTG_REQUIRE(p->kv_heads >= 1 && p->heads >= 1, "attention: at least one q head and one KV head");
     XTG_REQUIRE(attention_part_floats(p->kv_heads, splits) <= kNoAllocFloats,
-                "attention_noalloc: kv_heads x splits above 256, the fixed scratch's limit (4,259,840 bytes)");
+                "attention_noalloc: kv_heads x splits above 256, the fixed scratch's limit (4,325,376 bytes)");
     float* part = noalloc_scratch();
     // every split writes the partial of every live query row that the combine reads: nothing needs clearing
     AttnArgs a = {};
@@ -394,16 +395,18 @@ int xtg_cuda_head_bf16(const float* x, int m, const uint16_t* w, int vocab, int 
     // the per-tile candidates and the rows for the argmax kernel (it reads m from a StepParams)
     void* scratch = nullptr;
     const size_t cand_bytes = (size_t)tiles * kMaxRows * sizeof(ArgCand);
-    XTG_CUDA(cudaMalloc(&scratch, cand_bytes + sizeof(StepParams)));
+    XTG_CUDA(cudaMalloc(&scratch, cand_bytes + sizeof(StepParams) + 16));
     struct Free {
       void* p;
       ~Free() { cudaFree(p); }
     } f{scratch};
     ArgCand* cand = static_cast<ArgCand*>(scratch);
     StepParams* params = reinterpret_cast<StepParams*>(static_cast<uint8_t*>(scratch) + cand_bytes);
+    int* derr = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(params) + sizeof(StepParams));
     StepParams hp = {};
     hp.m = m;
     XTG_CUDA(cudaMemcpyAsync(params, &hp, sizeof(hp), cudaMemcpyHostToDevice, s));
+    XTG_CUDA(cudaMemsetAsync(derr, 0, sizeof(int), s));
     HeadBf16Args h = {};
     h.x = x;
     h.m = m;
@@ -413,9 +416,13 @@ int xtg_cuda_head_bf16(const float* x, int m, const uint16_t* w, int vocab, int 
     h.logit_scale = logit_scale;
     h.logits = logits;
     h.cand = cand;
+    h.err = derr;
     launch_head_bf16(h, sms, s, false);
     if (argmax) launch_argmax(cand, tiles, params, argmax, nullptr, nullptr, s, false);
+    int e = 0;
+    XTG_CUDA(cudaMemcpyAsync(&e, derr, sizeof(int), cudaMemcpyDeviceToHost, s));
     XTG_CUDA(cudaStreamSynchronize(s));   // the scratch is freed on return
+    XTG_REQUIRE(e == 0, "head_bf16: a device wait timed out");
   });
 }
 

@@ -20,6 +20,8 @@
 // times the key's V scale are the fp16 A operand of PV. Two permutations make every load contiguous: the head
 // dimension inside a k16 step (lane tq reads 32 contiguous bytes of a K row, Q's fragments use the same order) and
 // the keys inside a warp's quarter (lane tq owns keys 4 tq .. 4 tq + 3 in both products).
+#include <algorithm>
+
 #include "attention.h"
 #include "batch.h"
 #include "common.cuh"
@@ -34,7 +36,8 @@ constexpr int kThreads = 256;   // 8 warps: (row half) x (key quarter)
 constexpr int kQuarters = 4;    // key quarters of a chunk
 constexpr int kStages = 4;      // chunks in flight
 constexpr int kQRows = 32;
-constexpr int kPartStride = kD + 2;   // m, l, acc[128]
+constexpr int kPartStride = kD + 4;   // m, l, 2 pads, acc[128]: the dims 16-byte aligned
+constexpr int kXchgStride = kD + 2;   // a split-KV exchange slot: m, l, o[128] as 64-bit words
 constexpr int kMaxSplits = 256;       // parts of a cache's chunks (the combine holds one weight per part)
 
 __device__ __forceinline__ void codes_to_f16(uint32_t word, int dtype, uint32_t& lo, uint32_t& hi) {
@@ -360,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
 #pragma unroll
         for (int q = 0; q < kQuarters; ++q)
           if (w[q] != 0.f) o += st0[q * ss + r * kStateStride + 2 + d] * w[q];
-        out[2 + d] = o;
+        out[4 + d] = o;
       }
     }
   }
@@ -402,7 +405,7 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   const int ns = a.splits < kRegSplits ? a.splits : kRegSplits;
   float acc_s[kRegSplits];
 #pragma unroll
-  for (int s = 0; s < kRegSplits; ++s) acc_s[s] = s < ns ? base[s * sstride + 2 + d] : 0.f;
+  for (int s = 0; s < kRegSplits; ++s) acc_s[s] = s < ns ? base[s * sstride + 4 + d] : 0.f;
   float mls[2][2];
 #pragma unroll
   for (int u = 0; u < 2; ++u) {
@@ -460,13 +463,13 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   for (int s = 0; s < kRegSplits; ++s)
     if (s < ns) o += acc_s[s] * wgt[s];
   for (int s = kRegSplits; s < a.splits; ++s)
-    if (wgt[s] != 0.f) o += base[s * sstride + 2 + d] * wgt[s];
+    if (wgt[s] != 0.f) o += base[s * sstride + 4 + d] * wgt[s];
   if (a.x.world > 1) {
     // split-KV across GPUs: this process's cached part (m, l, o relative to m) to every peer, theirs from this
     // process's slots, all merged in rank order (the same bits on every process)
     const uint32_t run = *a.x.epoch * (uint32_t)a.x.n_g + (uint32_t)a.x.g, seq = run + 1;
     const int64_t set = (int64_t)(run & 1) * a.x.world;
-    auto slot_of = [&](uint64_t* sl, int src) { return sl + (((set + src) * kMaxRows + i) * a.heads + h) * kPartStride; };
+    auto slot_of = [&](uint64_t* sl, int src) { return sl + (((set + src) * kMaxRows + i) * a.heads + h) * kXchgStride; };
     uint64_t* mine = a.x.slot[0];
 #pragma unroll
     for (int t = 0; t < kMaxKvWorld; ++t) {
@@ -550,6 +553,101 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   }
 }
 
+// The batched step's combine (up to kWarpSplits splits): one warp per (sequence, activation row, q head), lane l
+// holding head dims 4 l .. 4 l + 3 and split l's m and l. The merge, the own keys' dot products and the norm need only
+// shuffles, no block barrier; every load goes out in one wave after the dependency wait. (For the 8-row step the
+// CTA per pair above measured faster: 2.538 against 2.614-2.647 ms per config-3 step, its loads spread over 4
+// warps.)
+constexpr int kWarpSplits = 24;
+constexpr int kCombineWarps = 8;
+
+__device__ __forceinline__ float4 ld4g(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float dot4(float4 a, float4 b) { return (a.x * b.x + a.y * b.y) + (a.z * b.z + a.w * b.w); }
+
+__global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(const CombineArgs a) {
+  const int lane = threadIdx.x & 31;
+  const int pair = (int)blockIdx.x * (int)(blockDim.x >> 5) + (int)(threadIdx.x >> 5);
+  const int per_seq = kMaxRows * a.heads;
+  const int seq = pair / per_seq, i = (pair % per_seq) / a.heads, h = pair % a.heads;
+  const bool exists = seq < a.nseq;
+  const int d0 = 4 * lane, col = h * kD + d0;
+  // the gate's scale is a parameter: loaded before the dependency wait
+  const float4 gsc = exists ? ld4g(a.gscale + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const int m = exists ? (a.params ? a.params[seq].m : a.m) : 0;
+  const int64_t rows0 = (int64_t)seq * kMaxRows;
+  if (a.pdl) {
+    pdl_wait();
+    pdl_launch_next();
+  }
+  if (i >= m) return;   // the whole warp
+  const int group = a.heads / a.kv_heads, kvh = h / group, qr = i * group + h % group;
+  const float* base = a.part + (int64_t)seq * a.part_seq_stride + ((int64_t)kvh * kQRows + qr) * kPartStride;
+  const int64_t sstride = (int64_t)a.kv_heads * kQRows * kPartStride;
+  const float ms = lane < a.splits ? base[lane * sstride] : -INFINITY;
+  const float ls = lane < a.splits ? base[lane * sstride + 1] : 0.f;
+  float4 acc[kWarpSplits];
+#pragma unroll
+  for (int s = 0; s < kWarpSplits; ++s)
+    acc[s] = s < a.splits ? ld4g(base + s * sstride + 4 + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 q4 = ld4g(a.q + ((rows0 + i) * a.heads + h) * kD + d0);
+  float4 kj[kMaxRows], vj[kMaxRows];
+#pragma unroll
+  for (int j = 0; j < kMaxRows; ++j) {
+    kj[j] = j < m ? ld4g(a.k + ((rows0 + j) * a.kv_heads + kvh) * kD + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
+    vj[j] = j < m ? ld4g(a.v + ((rows0 + j) * a.kv_heads + kvh) * kD + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float4 gt = ld4g(a.gate + (rows0 + i) * a.gate_ld + col);
+  // split weights exp(m_s - M) and sum_s l_s exp(m_s - M); the dims' sum in split order
+  const float M = warp_max(ms);
+  const float w = ms == -INFINITY ? 0.f : expf(ms - M);
+  const float lcached = warp_sum(w == 0.f ? 0.f : ls * w);
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int s = 0; s < kWarpSplits; ++s) {
+    const float ws = __shfl_sync(0xffffffffu, w, s);
+    if (s < a.splits) {
+      o.x += acc[s].x * ws;
+      o.y += acc[s].y * ws;
+      o.z += acc[s].z * ws;
+      o.w += acc[s].w * ws;
+    }
+  }
+  // this call's own keys j <= i, scored in FP32 from the prepared rows (the reference attends to them unquantized)
+  float own_s[kMaxRows], own_m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kMaxRows; ++j) {
+    const float pr = warp_sum(dot4(q4, kj[j]));
+    const bool vis = j < m && j <= i && (a.window == 0 || i - j < a.window);
+    own_s[j] = vis ? pr * a.scale : -INFINITY;
+    own_m = fmaxf(own_m, own_s[j]);
+  }
+  const float mall = fmaxf(own_m, M);
+  const float cs = M == -INFINITY ? 0.f : expf(M - mall);   // the cached part's weight
+  float lsum = lcached * cs;
+  o.x *= cs;
+  o.y *= cs;
+  o.z *= cs;
+  o.w *= cs;
+#pragma unroll
+  for (int j = 0; j < kMaxRows; ++j) {
+    const float pj = own_s[j] == -INFINITY ? 0.f : expf(own_s[j] - mall);
+    lsum += pj;
+    o.x += pj * vj[j].x;
+    o.y += pj * vj[j].y;
+    o.z += pj * vj[j].z;
+    o.w += pj * vj[j].w;
+  }
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  float v[4] = {o.x * inv, o.y * inv, o.z * inv, o.w * inv};
+  const float gtv[4] = {gt.x, gt.y, gt.z, gt.w}, gsv[4] = {gsc.x, gsc.y, gsc.z, gsc.w};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) v[c] *= 1.f / (1.f + expf(-gtv[c] * gsv[c]));
+  const float ss = warp_sum((v[0] * v[0] + v[1] * v[1]) + (v[2] * v[2] + v[3] * v[3]));
+  // f32 rows for the GEMM's digitizer and the per-head sums of squares
+  *reinterpret_cast<float4*>(a.gated_out + (rows0 + i) * a.heads * kD + col) = make_float4(v[0], v[1], v[2], v[3]);
+  if (lane == 0) a.asum[h * a.asum_ld + rows0 + i] = ss;
+}
+
 }  // namespace
 
 size_t attention_smem_bytes() { return sizeof(Smem); }
@@ -595,14 +693,26 @@ void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
   XTG_REQUIRE(!a.gated_out || (a.nseq >= 1 && a.nseq <= kMaxBatch && a.params && a.asum && a.gate && a.gscale),
               "combine: the batched step needs 1..8 sequences, params, the gate and the sums");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kMaxRows, a.heads, a.gated_out ? a.nseq : 1);
-  cfg.blockDim = dim3(kD);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
+  if (a.gated_out && a.splits <= kWarpSplits && a.x.world <= 1) {   // the batched step: a warp per pair
+    // as many warps per CTA as keep one CTA per SM or more
+    const int pairs = a.nseq * kMaxRows * a.heads;
+    int dev = 0, sms = 0;
+    XTG_CUDA(cudaGetDevice(&dev));
+    XTG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int wpc = std::max(1, std::min(kCombineWarps, pairs / std::max(1, sms)));
+    cfg.gridDim = dim3((unsigned)((pairs + wpc - 1) / wpc));
+    cfg.blockDim = dim3(wpc * 32);
+    XTG_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_warp_kernel, a));
+    return;
+  }
+  cfg.gridDim = dim3(kMaxRows, a.heads, a.gated_out ? a.nseq : 1);
+  cfg.blockDim = dim3(kD);
   XTG_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_kernel, a));
 }
 

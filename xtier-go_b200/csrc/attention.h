@@ -77,7 +77,8 @@ struct AttnArgs {
   // The chunks of the cache are cut into splits_total parts; this launch computes parts split0 .. split0 + splits - 1
   // (another process may compute the rest: the batch-1 split-KV over GPUs). 0 / 0: split0 0, splits_total = splits.
   int split0, splits_total;
-  float* part;              // [splits_total][kv_heads][32][130], split-major (a process's splits are contiguous)
+  float* part;              // [splits_total][kv_heads][32][132] (m, l, 2 pads, acc[128]), split-major (a process's
+                            // splits are contiguous)
   int part_local;           // partials at index split (this launch's own) instead of split0 + split
   int* err;                 // set if a bounded wait gave up (never expected); may be null
   int pdl;

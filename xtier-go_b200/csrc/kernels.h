@@ -122,7 +122,7 @@ void launch_gemv(int epi, const GemvArgs& a, const GemvPlan& p, cudaStream_t s, 
 void digitize_rows(const float* x, int m, int k, uint8_t* xb, float* xb_pre, cudaStream_t s);
 
 // ---- the BF16 lm_head of a checkpoint (head.cu) ----
-constexpr int kMaxHeadBf16Hidden = 6144;   // x's two bf16 planes stay in shared memory
+constexpr int kMaxHeadBf16Hidden = 5120;   // x's two bf16 planes and the weight stages stay in shared memory
 struct HeadBf16Args {
   const float* x;             // [8][hidden] the step's rows (rows >= m unused)
   const int* m_dev;           // rows read on the device (a replayable graph), or null: m
@@ -132,6 +132,7 @@ struct HeadBf16Args {
   const float* logit_scale;   // [vocab], folded
   float* logits;              // [8][vocab] or null
   ArgCand* cand;              // [ceil(vocab / 128)][8] per-tile argmax candidates
+  int* err;                   // set if a bounded wait gave up (never expected); may be null
 };
 void launch_head_bf16(const HeadBf16Args& h, int num_sms, cudaStream_t s, bool pdl);
 

@@ -203,8 +203,8 @@ Config parse_config(const std::string& options, const DoryConfig* ck = nullptr) 
   if (c.decode_rows < 1 || c.decode_rows > kMaxRows) throw CudaError("decode_rows: 1..8");
   if (c.snapshots < 0 || c.snapshots > 8) throw CudaError("snapshots: 0..8");
   if (ck && c.context > ck->max_pos) throw CudaError("context: above the model's max_position_embeddings");
-  if (c.head_bf16 && (c.hidden > kMaxHeadBf16Hidden || c.hidden % 32))
-    throw CudaError("head: bf16 takes hidden <= 6144 (a multiple of 32); use \"nvfp4\"");
+  if (c.head_bf16 && (c.hidden > kMaxHeadBf16Hidden || c.hidden % 64))
+    throw CudaError("head: bf16 takes hidden <= 5120 (a multiple of 64); use \"nvfp4\"");
   return c;
 }
 
@@ -1057,6 +1057,7 @@ struct xtg_cuda {
       hb.logit_scale = logit_scale;
       hb.logits = logits;
       hb.cand = cand;
+      hb.err = dev_err;
       mark(kClsGemv, true);
       launch_head_bf16(hb, num_sms, stream, pdl);
       mark(kClsGemv, false);
