@@ -901,6 +901,8 @@ def main():
                     help="profiling driver: run the config-1 gate+up GEMM at M=512 this many times, then exit")
     ap.add_argument("--ncu-batch", type=int, default=0,
                     help="profiling driver: this many batched rounds of 8 sequences (8K tier), then exit")
+    ap.add_argument("--ncu-head", type=int, default=0,
+                    help="profiling driver: the BF16 lm_head (vocab 131072 x 3072, 8 rows) this many times, then exit")
     args = ap.parse_args()
     if args.ncu_gemm:
         import torch
@@ -917,6 +919,17 @@ def main():
             lin(xin)
         torch.cuda.synchronize()
         lin.close()
+        return
+    if args.ncu_head:
+        import torch
+        x = package()
+        g = torch.Generator(device="cuda").manual_seed(5)
+        w = (torch.randn(131072, 3072, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+        xin = torch.randn(8, 3072, device="cuda", generator=g)
+        ls = torch.rand(131072, device="cuda", generator=g) * 100 + 100
+        for _ in range(args.ncu_head):
+            x.head_bf16(xin, w, ls)
+        torch.cuda.synchronize()
         return
     if args.ncu_batch:
         x = package()
