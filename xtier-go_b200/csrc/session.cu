@@ -19,6 +19,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../include/xtg_cuda.h"
 #include "attention.h"
 #include "common.cuh"
@@ -51,6 +53,7 @@ struct Config {
   int device = 0;
   bool graph = true, pdl = true;
   bool batch = true;   // xtg_cuda_forward_batch steps sessions over one weight set together (batch.h)
+  bool nvtx = false;   // NVTX ranges per sublayer while a step is enqueued (aligned with the kernels when graph = 0)
   int splits_global = 0, splits_ring = 0;   // 0: chosen from the SM count
   // batch-1 split-KV across processes (one GPU each): every process holds the whole model and every cache and runs
   // the whole step, but attends only its share of each global cache's chunks; the attention partials of the global
@@ -179,6 +182,7 @@ Config parse_config(const std::string& options, const DoryConfig* ck = nullptr) 
   c.graph = o.number("graph", 1) != 0;
   c.pdl = o.number("pdl", 1) != 0;
   c.batch = o.number("batch", 1) != 0;
+  c.nvtx = o.number("nvtx", 0) != 0;
   c.splits_global = (int)o.number("splits_global", 0);
   c.splits_ring = (int)o.number("splits_ring", 0);
   c.kv_world = (int)o.number("kv_world", 1);
@@ -243,6 +247,17 @@ struct Snap {
 };
 
 enum KernelClass { kClsGemv = 0, kClsAttn = 1, kClsCombine = 2, kClsSmall = 3, kClasses = 4 };
+
+// An NVTX range for as long as it lives (nothing when off; NVTX itself is inert without a tool attached).
+struct NvtxRange {
+  bool on;
+  NvtxRange(bool enabled, const char* name) : on(enabled) {
+    if (on) nvtxRangePushA(name);
+  }
+  ~NvtxRange() {
+    if (on) nvtxRangePop();
+  }
+};
 
 }  // namespace
 
@@ -939,8 +954,12 @@ struct xtg_cuda {
       mark(kClsSmall, false);
       xb_unit = true;
     };
+    static const char* const kKindName[3] = {"mlp", "sliding attention", "global attention"};
     auto sublayer = [&](int e) {
       const Eval& E = evals[e];
+      char label[64];
+      if (c.nvtx) std::snprintf(label, sizeof(label), "eval %d: %s", e, kKindName[E.kind]);
+      NvtxRange range(c.nvtx, label);
       if (E.kind == 0) {
         GemvArgs a = gemv_args(E.gu);
         a.g_gate = E.gu.g0;
@@ -1953,6 +1972,7 @@ xtg_cuda* xtg_cuda_open_shared(xtg_cuda* owner, const char* options, char* err, 
     h->c.graph = o.graph;
     h->c.pdl = o.pdl;
     h->c.batch = o.batch;
+    h->c.nvtx = o.nvtx;
     h->c.splits_global = o.splits_global;
     h->c.splits_ring = o.splits_ring;
     h->c.kv_world = 1;
