@@ -276,6 +276,10 @@ class Session:
         err = _err()
         _check(lib().xtg_cuda_grow(self.h, str(tier).encode(), err, len(err)), err)
 
+    def tiers(self, contexts):
+        """The session over a list of context tiers (Tiers below); the session's own context must be the first."""
+        return Tiers(self, contexts)
+
     def debug_cache(self, instance, value):
         """K codes [kv_heads][128][slots] (0), V codes [kv_heads][slots][128] (1), K / V scales [kv_heads][slots]
         (2 / 3) as numpy arrays; None for no such instance."""
@@ -332,6 +336,51 @@ class Session:
 
     def step_bytes(self, what=0, m=8):
         return lib().xtg_cuda_step_bytes(self.h, what, m)
+
+
+class Tiers:
+    """A session over context tiers, as packs/dory/npu.cpp's NpuModel keeps its .pte buckets (npu.cpp:142-160) and
+    NpuSession::forward fits each chunk (npu.cpp:266-270). fit(need) moves the session to the smallest tier with
+    room for `need` positions (npu.cpp:181-198): up when a request outgrows the current tier, down when a shorter
+    conversation follows, never below the positions already held. A tier here is a context length given to
+    xtg_cuda_grow in place of a .pte path; the caches are reallocated and the held positions copied on the device."""
+
+    def __init__(self, session, contexts):
+        ctx = [int(c) for c in contexts]
+        if not ctx:
+            raise XtgError("tiers: no context tiers")
+        for a, b in zip(ctx, ctx[1:]):
+            if b <= a:
+                raise XtgError(f"tiers: {b} after {a}: list the tiers by context")
+        have = session.info()["context"]
+        if have != ctx[0]:
+            raise XtgError(f"tiers: the session holds {have} positions, the first tier {ctx[0]}")
+        self.session = session
+        self.contexts = ctx
+        self.cur = 0
+        self.moves = []
+
+    @property
+    def context(self):
+        return self.contexts[-1]
+
+    def fit(self, need):
+        to = 0
+        while to < len(self.contexts) and self.contexts[to] < need:
+            to += 1
+        if to == len(self.contexts):
+            raise XtgError(f"context full: {need} positions (the largest tier holds {self.contexts[-1]})")
+        if to == self.cur or self.session.pos() > self.contexts[to]:
+            return
+        self.session.grow(self.contexts[to])
+        self.cur = to
+        self.moves.append(self.contexts[to])
+
+    def forward(self, tokens, want=2):
+        """The session's forward after fitting n_past + len(tokens); the rows as Session.forward returns them."""
+        if len(self.contexts) > 1:
+            self.fit(self.session.pos() + len(tokens))
+        return self.session.forward(tokens, want)
 
 
 # ----------------------------------------------------------------------------------------------------------------
