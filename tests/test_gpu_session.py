@@ -144,18 +144,23 @@ def test_grow_moves_tier_bit_exactly(cuda, xtg, cfg):
 
 def test_tiers_fit_up_and_down(cuda, xtg, cfg):
     """Tiers over a real session (NpuModel::fit, npu.cpp:181-198): a prompt past the first tier moves the session up
-    before the forward, logits bit-identical to a session opened at the large tier; after a rewind to a short
-    prefix the next forward moves it down again, still bit-identical."""
+    before the forward, logits bit-identical to a session opened at the large tier; after a restore to a short
+    prefix (a snapshot taken at 64 positions, kept across the move) the next forward moves it down again, still
+    bit-identical."""
     prompt = [(7 * i + 3) % cfg["vocab"] for i in range(300)]
     nxt = list(range(40, 48))
     with xtg.Session(cfg, context=256) as s, xtg.Session(cfg, context=1024) as big:
         t = s.tiers([256, 512, 1024])
-        a = logits_of(t.forward(prompt, want=2), 300)
-        b = logits_of(big.forward(prompt, want=2), 300)
+        a0 = logits_of(t.forward(prompt[:64], want=2), 64)
+        b0 = logits_of(big.forward(prompt[:64], want=2), 64)
+        s.snapshot(0)
+        big.snapshot(0)
+        a = np.concatenate([a0, logits_of(t.forward(prompt[64:], want=2), 236)])
+        b = np.concatenate([b0, logits_of(big.forward(prompt[64:], want=2), 236)])
         assert t.moves == [512] and s.info()["context"] == 512
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
-        s.rewind(64)
-        big.rewind(64)
+        assert s.snapshot_pos(0) == 64 and s.restore(0) and big.restore(0)
+        assert s.pos() == 64
         a = logits_of(t.forward(nxt, want=2), 8)
         b = logits_of(big.forward(nxt, want=2), 8)
         assert t.moves == [512, 256] and s.info()["context"] == 256

@@ -109,10 +109,18 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     }
     if (lane == 0) mbar_expect_tx(bar, stage_bytes);
     __syncwarp();
-    if (lane == 0) bulk_g2s(st.k, kc + c * 64 * kD, 64 * kD, bar);
-    if (lane == 1) bulk_g2s(st.v, vc + c * 64 * kD, 64 * kD, bar);
-    if (lane == 2) bulk_g2s(st.ks, ks + c * 64, 64 * 4, bar);
-    if (lane == 3) bulk_g2s(st.vs, vs + c * 64, 64 * 4, bar);
+    if (a.l2_first) {
+      const uint64_t pol = l2_evict_first();
+      if (lane == 0) bulk_g2s_hint(st.k, kc + c * 64 * kD, 64 * kD, bar, pol);
+      if (lane == 1) bulk_g2s_hint(st.v, vc + c * 64 * kD, 64 * kD, bar, pol);
+      if (lane == 2) bulk_g2s_hint(st.ks, ks + c * 64, 64 * 4, bar, pol);
+      if (lane == 3) bulk_g2s_hint(st.vs, vs + c * 64, 64 * 4, bar, pol);
+    } else {
+      if (lane == 0) bulk_g2s(st.k, kc + c * 64 * kD, 64 * kD, bar);
+      if (lane == 1) bulk_g2s(st.v, vc + c * 64 * kD, 64 * kD, bar);
+      if (lane == 2) bulk_g2s(st.ks, ks + c * 64, 64 * 4, bar);
+      if (lane == 3) bulk_g2s(st.vs, vs + c * 64, 64 * 4, bar);
+    }
     if (lane == 4 && a.ring) bulk_g2s(st.pos, ring_pos + c * 64, 64 * 4, bar);
   };
   // the cached keys and values below pos0 do not depend on the previous kernel (this step writes positions pos0 ..

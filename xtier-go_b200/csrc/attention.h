@@ -91,6 +91,8 @@ struct AttnArgs {
   // the cache below pos0 is written by the kernel just before (a prompt chunk's row groups over one cache): its
   // chunks are copied only after the wait for that kernel, not before
   int late_copies;
+  // the cache's chunks with the L2 evict_first policy (a global cache, read once per step; a ring stays in L2)
+  int l2_first;
 };
 
 struct CombineArgs {

@@ -90,6 +90,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                : "memory");
 }
 
+// An L2 policy for data read once per step (weights, the global KV caches): its lines are the first evicted, so the
+// stream does not push the kernels' code, the activations and the ring caches out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 constexpr uint32_t kMaxSpins = 1u << 24;   // bound on every mbarrier wait
 
 // Wait for phase `parity` of an mbarrier; after kMaxSpins polls give up, set *err (if given) and return false.

@@ -232,11 +232,16 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     const int t = t0 + u / nkb, kb = k0 + u % nkb;
     return a.w + ((int64_t)t * KB + kb) * kUnitBytes;
   };
+  const uint64_t wpol = l2_evict_first();
   auto issue_stage = [&](int st) {
     const int slot = st % ring, first = st * kStageUnits;
     const int cnt = min(kStageUnits, nunits - first);
     mbar_expect_tx(&full[slot], (uint32_t)cnt * kUnitBytes);
-    bulk_g2s(ringbuf + slot * kStageUnits * kUnitBytes, unit_src(first), (uint32_t)cnt * kUnitBytes, &full[slot]);
+    if (a.l2_first)
+      bulk_g2s_hint(ringbuf + slot * kStageUnits * kUnitBytes, unit_src(first), (uint32_t)cnt * kUnitBytes,
+                    &full[slot], wpol);
+    else
+      bulk_g2s(ringbuf + slot * kStageUnits * kUnitBytes, unit_src(first), (uint32_t)cnt * kUnitBytes, &full[slot]);
   };
   if (tid == 0)
     for (int st = 0; st < ring && st < nstages; ++st) issue_stage(st);
@@ -307,6 +312,16 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   __syncwarp();
   {
     const int i = warp;   // warp i: activation row i
+    // the row's sum of squares over the producer's parts ([row][part]): lane l takes parts l, l + 32, ... (one wave
+    // of coalesced loads, issued with the prescale loads below so that the two take one round trip)
+    float pv[kSumsqLoads];
+    if (EPI == kEpiStore && a.sumsq) {
+#pragma unroll
+      for (int u = 0; u < kSumsqLoads; ++u) {
+        const int q = lane + 32 * u;
+        pv[u] = q < a.nparts ? a.sumsq[(int64_t)i * a.nparts + q] : 0.f;
+      }
+    }
     float pmin = a.xb_fixed;
     if (!(a.xb_fixed > 0.f)) {
       // the slice's prescales ([group][row]) are one contiguous range: every thread loads a share (whole cache
@@ -321,16 +336,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     }
     if (lane == 0) pslice[i] = pmin;
     if (EPI == kEpiStore) {
-      // the row's sum of squares over the producer's parts ([row][part]): lane l takes parts l, l + 32, ... (one
-      // wave of coalesced loads), then a butterfly over the warp (a fixed order)
+      // the parts summed in lane order, then a butterfly over the warp (a fixed order)
       float t = 1.f;
       if (a.sumsq) {
-        float pv[kSumsqLoads];
-#pragma unroll
-        for (int u = 0; u < kSumsqLoads; ++u) {
-          const int q = lane + 32 * u;
-          pv[u] = q < a.nparts ? a.sumsq[(int64_t)i * a.nparts + q] : 0.f;
-        }
         t = pv[0];
 #pragma unroll
         for (int u = 1; u < kSumsqLoads; ++u) t += pv[u];

@@ -108,6 +108,7 @@ struct GemvArgs {
   int rs_ld;
   int* err;                  // set to 1 if a bounded wait gave up (never expected); may be null
   int pdl;                   // launched as a programmatic dependent
+  int l2_first;              // weight stages with the L2 evict_first policy (read once per step)
 };
 
 // How a GEMV is spread over the GPU: `split` CTAs (one cluster) share each tile's K blocks, or (split 1) each CTA

@@ -51,7 +51,7 @@ struct Config {
   int snapshots = 2;
   int decode_rows = 8;
   int device = 0;
-  bool graph = true, pdl = true;
+  bool graph = true, pdl = true, l2_first = true;
   bool batch = true;   // xtg_cuda_forward_batch steps sessions over one weight set together (batch.h)
   bool nvtx = false;   // NVTX ranges per sublayer while a step is enqueued (aligned with the kernels when graph = 0)
   int splits_global = 0, splits_ring = 0;   // 0: chosen from the SM count
@@ -181,6 +181,7 @@ Config parse_config(const std::string& options, const DoryConfig* ck = nullptr) 
   c.device = (int)o.number("device", c.device);
   c.graph = o.number("graph", 1) != 0;
   c.pdl = o.number("pdl", 1) != 0;
+  c.l2_first = o.number("l2_evict_first", 1) != 0;
   c.batch = o.number("batch", 1) != 0;
   c.nvtx = o.number("nvtx", 0) != 0;
   c.splits_global = (int)o.number("splits_global", 0);
@@ -894,6 +895,7 @@ struct xtg_cuda {
     a.xb_fixed = (in == xb && xb_unit) ? kUnitPrescale : 0.f;
     a.sumsq = sumsq;
     a.nparts = nparts;
+    a.l2_first = c.l2_first ? 1 : 0;
     mark(kClsGemv, true);
     launch_gemv(epi, a, L.plan, stream, pdl);
     mark(kClsGemv, false);
@@ -1021,6 +1023,7 @@ struct xtg_cuda {
       at.part_local = peer ? 1 : 0;
       at.part = part;
       at.err = dev_err;
+      at.l2_first = (!K.ring && c.l2_first) ? 1 : 0;
       mark(kClsAttn, true);
       launch_attention(at, stream, pdl);
       mark(kClsAttn, false);
@@ -1643,7 +1646,8 @@ struct BatchStep {
       at.err = dev_err;
       at.seqs = kvseq + (size_t)E.cache * S;
       at.nseq = S;
-      at.late_copies = distinct ? 0 : 1;   // a prompt chunk: the earlier groups' keys come from qkv_prep just before
+      at.late_copies = distinct ? 0 : 1;
+      at.l2_first = (!ring && c.l2_first) ? 1 : 0;   // a prompt chunk: the earlier groups' keys come from qkv_prep just before
       at.part_seq_stride = attention_part_floats(c.kv_heads, std::max(splits_g, splits_r));
       launch_attention(at, stream, pdl);
       CombineArgs cb = {};
@@ -1971,6 +1975,7 @@ xtg_cuda* xtg_cuda_open_shared(xtg_cuda* owner, const char* options, char* err, 
     h->c.decode_rows = o.decode_rows;
     h->c.graph = o.graph;
     h->c.pdl = o.pdl;
+    h->c.l2_first = o.l2_first;
     h->c.batch = o.batch;
     h->c.nvtx = o.nvtx;
     h->c.splits_global = o.splits_global;
