@@ -44,6 +44,25 @@ def test_oracle_checkpoint_matches_reference_pack(ckpt, loops):
         ora.close()
 
 
+def test_oracle_checkpoint_head_dim_256_matches_reference_pack(tmp_path):
+    """The real Dory 4B's head shape (head_dim 256, 4 q heads per KV head) on a small checkpoint: CheckpointDory
+    against the reference's DoryModel, 8 rows then 3, FP8 KV."""
+    if O.ref() is None:
+        pytest.skip("oracle/_ref (the reference's own kernels) is not built")
+    cfg, tensors = dory_ckpt.write_checkpoint(str(tmp_path), dory_ckpt.small_config(head_dim=256), seed=3)
+    ref = O.RefDory(str(tmp_path), kv_dtype="fp8", context=1024)
+    ora = O.CheckpointDory(cfg, tensors, ctx=1024, n_prefill=0, kv_dtype=O.KV_FP8)
+    try:
+        for toks in (TOKS, [1, 2, 3]):
+            want = ref.forward(toks)
+            got = ora.step(toks)
+            assert np.array_equal(got.argmax(1), want.argmax(1))
+            assert np.abs(got - want).max() <= 1e-4 * max(1.0, np.abs(want).max())
+    finally:
+        ref.close()
+        ora.close()
+
+
 def _open(xtg, path, options=b"{}"):
     err = C.create_string_buffer(1024)
     h = xtg.lib().xtg_cuda_open(os.fsencode(path), options, err, len(err))
@@ -76,7 +95,7 @@ def _variant(tmp_path, base, name, config=None, safetensors=None):
     ("no_theta", {"rope_parameters": {"sliding_attention": {"rope_theta": 1e4}}}, "no rope_theta"),
     ("partial_rope", {"rope_parameters": {"sliding_attention": {"rope_theta": 1e4, "partial_rotary_factor": 0.5},
                                           "full_attention": {"rope_theta": 1e7}}}, "full-width RoPE"),
-    ("head_dim", {"head_dim": 256}, "head_dim must be 128"),
+    ("head_dim", {"head_dim": 64}, "head_dim must be 128 or 256"),
 ])
 def test_open_rejects_bad_configs(xtg, ckpt, tmp_path, name, config, needle):
     h, msg = _open(xtg, _variant(tmp_path, ckpt, name, config=config))

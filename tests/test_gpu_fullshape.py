@@ -65,3 +65,41 @@ def test_config3_bench_replay_matches_oracle(session, oracle_logits):
     assert session.rewind(PREFILL)
     session.bench(TOKENS, 2)
     assert session.argmax(8) == list(oracle_logits.argmax(1))
+
+
+# ---- the real Dory 4B's shape: head_dim 256, 16 q / 4 KV heads, hidden 2560, FFN 7168 ----
+
+# every width and the 8K tier; 12 sublayers of the 112, a global and a sliding attention sublayer in the loop
+DORY_4B_CUT = dict(n_in=2, n_rec=4, n_out=2, loops=2, global_every=2)
+
+
+@pytest.fixture(scope="module")
+def dory4b(cuda, xtg):
+    """(session, oracle logits) for one 8-row step of the Dory 4B shape (synthetic weights, 1088-slot rings, vocab
+    131072) over 8184 prefilled positions."""
+    cfg = dict(xtg.DORY_4B, **DORY_4B_CUT)
+    ref = O.SynthDory(cfg, ctx=8192, n_prefill=PREFILL)
+    try:
+        want = ref.step(TOKENS)
+    finally:
+        ref.close()
+    s = xtg.Session(cfg, context=8192)
+    s.prefill_synthetic(PREFILL)
+    yield s, want
+    s.close()
+
+
+def test_dory4b_step_matches_oracle(dory4b):
+    s, want = dory4b
+    got = rows(s.forward(TOKENS, want=2), 8)
+    assert np.array_equal(got.argmax(1), want.argmax(1)), (got.argmax(1), want.argmax(1))
+    assert np.abs(got - want).max() <= LOGIT_TOL, np.abs(got - want).max()
+    assert s.info()["kv_bytes"] > 0 and s.pos() == PREFILL + 8
+
+
+def test_dory4b_verify_matches_sequential(dory4b):
+    s, want = dory4b
+    assert s.rewind(PREFILL)
+    seq = np.stack([s.forward([t], want=1)[0] for t in TOKENS])
+    assert np.array_equal(seq.argmax(1), want.argmax(1))
+    assert np.abs(seq - want).max() <= LOGIT_TOL

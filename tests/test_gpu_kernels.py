@@ -197,26 +197,27 @@ def swz_k(s64):
     return (s64 ^ (s64 >> 3)) & 7
 
 
-def k_index(kvh, slots):
-    """Flat position of element (h, s, d) of K in the library's layout (include/xtg_cuda.h), shape [h][s][d]."""
-    h, sl, d = np.meshgrid(np.arange(kvh), np.arange(slots), np.arange(128), indexing="ij")
-    return (h * slots + sl) * 128 + 16 * ((d >> 4) ^ swz_k(sl & 63)) + (d & 15)
+def k_index(kvh, slots, D=128):
+    """Flat position of element (h, s, d) of K in the library's layout (include/xtg_cuda.h), shape [h][s][d]: each
+    128-dim half of a row swizzled in 16-byte units."""
+    h, sl, d = np.meshgrid(np.arange(kvh), np.arange(slots), np.arange(D), indexing="ij")
+    return (h * slots + sl) * D + 128 * (d >> 7) + 16 * (((d >> 4) & 7) ^ swz_k(sl & 63)) + (d & 15)
 
 
-def v_index(kvh, slots):
+def v_index(kvh, slots, D=128):
     """Flat position of element (h, d, s) of V, shape [h][d][s]."""
-    h, d, sl = np.meshgrid(np.arange(kvh), np.arange(128), np.arange(slots), indexing="ij")
-    return ((h * (slots // 64) + sl // 64) * 128 + d) * 64 + 16 * (((sl & 63) >> 4) ^ ((d >> 1) & 3)) + (sl & 15)
+    h, d, sl = np.meshgrid(np.arange(kvh), np.arange(D), np.arange(slots), indexing="ij")
+    return ((h * (slots // 64) + sl // 64) * D + d) * 64 + 16 * (((sl & 63) >> 4) ^ ((d >> 1) & 3)) + (sl & 15)
 
 
 def cache_to_device(torch, codes_k, codes_v, ks, vs):
-    """Oracle layout [slots][kv_heads][128] / [slots][kv_heads] -> the library's K and V layouts and scales
+    """Oracle layout [slots][kv_heads][D] / [slots][kv_heads] -> the library's K and V layouts and scales
     [h][slots]."""
-    slots, kvh, _ = codes_k.shape
-    kc = np.zeros(kvh * slots * 128, np.uint8)
+    slots, kvh, D = codes_k.shape
+    kc = np.zeros(kvh * slots * D, np.uint8)
     vc = np.zeros_like(kc)
-    kc[k_index(kvh, slots)] = codes_k.transpose(1, 0, 2)
-    vc[v_index(kvh, slots)] = codes_v.transpose(1, 2, 0)
+    kc[k_index(kvh, slots, D)] = codes_k.transpose(1, 0, 2)
+    vc[v_index(kvh, slots, D)] = codes_v.transpose(1, 2, 0)
     return dev(torch, kc), dev(torch, vc), dev(torch, np.ascontiguousarray(ks.T)), dev(torch, np.ascontiguousarray(vs.T))
 
 
@@ -227,8 +228,7 @@ def rope_rows(x, pos0, theta):
     return x
 
 
-def config2_inputs(seed, slots, n_q, ring):
-    heads, kvh, d = 24, 6, 128
+def config2_inputs(seed, slots, n_q, ring, heads=24, kvh=6, d=128):
     ck = O.gen_int8(seed, 1, slots * kvh * d).view(np.uint8).reshape(slots, kvh, d)
     cv = O.gen_int8(seed, 2, slots * kvh * d).view(np.uint8).reshape(slots, kvh, d)
     ks = O.gen_uniform(seed, 3, 0.005, 0.02, slots * kvh).reshape(slots, kvh)
@@ -311,6 +311,29 @@ def test_attention_reference_cases(cuda, xtg, torch_mod, dtype, case):
                         splits=3).cpu().numpy()
     ok, worst = close_rel(got, ref)
     assert ok, worst
+
+
+@pytest.mark.parametrize("ring", [False, True])
+def test_attention_head_dim_256(cuda, xtg, torch_mod, ring):
+    """The real Dory 4B's attention shape: head_dim 256, 16 q / 4 KV heads; a global cache of 4096 positions and a
+    1088-slot rotated ring (window 1024), int8 codes, at several splits, against the oracle."""
+    torch = torch_mod
+    n_q = 8
+    slots = 1088 if ring else 4096
+    pos0 = 5000 if ring else 4088
+    ck, cv, ks, vs, q, k, v = config2_inputs(7 + ring, slots, n_q, ring, heads=16, kvh=4, d=256)
+    q = rope_rows(q, pos0, 1e4)
+    k = rope_rows(k, pos0, 1e4)
+    scale = 1.0 / math.sqrt(256)
+    rp = np.array([pos0 - 1 - ((pos0 - 1 - s) % slots) for s in range(slots)], np.int64) if ring else None
+    window = 1024 if ring else 0
+    ref = O.attention(q, k, v, ck, cv, ks, vs, pos0, window, scale, ring_pos=rp)
+    kc, vc, kss, vss = cache_to_device(torch, ck, cv, ks, vs)
+    for splits in ((1, 17) if ring else (1, 5, 37)):
+        got = xtg.attention(dev(torch, q), dev(torch, k), dev(torch, v), kc, vc, kss, vss, pos0, window, scale,
+                            ring_pos=dev(torch, rp.astype(np.int32)) if ring else None, splits=splits).cpu().numpy()
+        ok, worst = close_rel(got, ref)
+        assert ok, (splits, worst)
 
 
 # ---- KV store: bit-exact encode ----

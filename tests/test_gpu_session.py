@@ -167,6 +167,34 @@ def test_tiers_fit_up_and_down(cuda, xtg, cfg):
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
+def test_head_dim_256_matches_oracle(cuda, xtg, cfg):
+    """The real Dory 4B's head shape (head_dim 256, 4 q heads per KV head) at the small widths: verify steps against
+    the oracle (the q|k|v preparation kernel after the projection, the 256-dim attention and combine), then a tier
+    move and a snapshot restore bit-exact, and verify against sequential decoding."""
+    c = dict(cfg, head_dim=256, seed=21)
+    steps = [[5, 17, 900, 3, 44, 1023, 0, 256], [8, 9, 10], [4000, 1, 2, 3, 4, 5, 6, 7]]
+    ref = O.SynthDory(c, ctx=256, n_prefill=150)
+    with xtg.Session(c, context=256) as s, xtg.Session(c, context=512) as big:
+        s.prefill_synthetic(150)
+        big.prefill_synthetic(150)
+        for toks in steps:
+            got = logits_of(s.forward(toks, want=2), len(toks))
+            want = ref.step(toks)
+            assert np.array_equal(got.argmax(1), want.argmax(1))
+            assert np.abs(got - want).max() <= LOGIT_TOL, np.abs(got - want).max()
+            big.forward(toks, want=0)
+        s.snapshot(0)
+        s.grow("512")
+        a = logits_of(s.forward([7, 8, 9], want=2), 3)
+        b = logits_of(big.forward([7, 8, 9], want=2), 3)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        p = s.snapshot_pos(0)
+        assert s.restore(0) and s.pos() == p
+        seq = np.stack([s.forward([t], want=1)[0] for t in [7, 8, 9]])
+        assert np.array_equal(seq.argmax(1), a.argmax(1)) and np.abs(seq - a).max() <= LOGIT_TOL
+    ref.close()
+
+
 def test_error_paths_leave_state_unchanged(cuda, xtg, cfg):
     with xtg.Session(cfg, context=128) as s:
         s.prefill_synthetic(100)

@@ -158,6 +158,11 @@ DORY_3072 = dict(hidden=3072, ffn=9216, heads=24, kv_heads=6, head_dim=128, voca
                  weight_std=0.02, lr_lo=0.05, lr_hi=0.2, qs_lo=48.0, qs_hi=80.0, gs_lo=25.0, gs_hi=75.0,
                  suv_lo=25.0, suv_hi=75.0, ls_lo=100.0, ls_hi=200.0, kvs_lo=0.0008, kvs_hi=0.0016, seed=3)
 
+# The real Dory 4B's shape (head_dim 256, GQA 4, 16 + 40 x 2 + 16 sublayers) with the synthetic model's seeded weights
+# and sublayer alternation.
+DORY_4B = dict(DORY_3072, hidden=2560, ffn=7168, heads=16, kv_heads=4, head_dim=256, n_in=16, n_rec=40, n_out=16,
+               seed=5)
+
 # A small model with the same structure for parity tests that a CPU oracle finishes in seconds.
 SMALL = dict(DORY_3072, hidden=512, ffn=1024, heads=8, kv_heads=2, vocab=4096, n_in=2, n_rec=4, n_out=2, loops=2,
              window=64, ring=128, global_every=2, seed=11)

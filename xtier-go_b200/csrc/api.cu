@@ -192,7 +192,7 @@ int xtg_cuda_quantize_nvfp4(const uint16_t* w_bf16, int n_out, int k, uint8_t* c
 
 int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, char* err, int err_len) {
   return guarded(err, err_len, [&] {
-    XTG_REQUIRE(p->head_dim == 128, "attention: head_dim 128");
+    XTG_REQUIRE(p->head_dim == 128 || p->head_dim == 256, "attention: head_dim 128 or 256");
     require_attn_alignment(p);
     XTG_REQUIRE(p->n_q >= 1 && p->n_q <= kMaxRows, "attention: 1..8 query rows");
     XTG_REQUIRE(splits >= 1, "attention: at least one split");
@@ -201,7 +201,7 @@ int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, ch
     XTG_REQUIRE(p->ring != 0 || p->pos0 <= p->slots, "attention: pos0 beyond the cache");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     float* part = nullptr;
-    XTG_CUDA(cudaMalloc(&part, attention_part_floats(p->kv_heads, splits) * sizeof(float)));
+    XTG_CUDA(cudaMalloc(&part, attention_part_floats(p->kv_heads, splits, p->head_dim) * sizeof(float)));
     try {
       AttnArgs a = {};
       a.q = p->q;
@@ -224,6 +224,7 @@ int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, ch
       a.splits = splits;
       a.part = part;
       a.err = nullptr;
+      a.head_dim = p->head_dim;
       launch_attention(a, s, false);
       CombineArgs cb = {};
       cb.part = part;
@@ -237,6 +238,7 @@ int xtg_cuda_attention(const xtg_cuda_attn_args* p, int splits, void* stream, ch
       cb.kv_heads = p->kv_heads;
       cb.m = p->n_q;
       cb.out = p->out;
+      cb.head_dim = p->head_dim;
       launch_attn_combine(cb, s, false);
       XTG_CUDA(cudaStreamSynchronize(s));
     } catch (...) {
@@ -291,15 +293,16 @@ extern "C" {
 
 int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* p, int splits, void* stream, char* err, int err_len) {
   return guarded(err, err_len, [&] {
-    XTG_REQUIRE(p->head_dim == 128, "attention: head_dim 128");
+    XTG_REQUIRE(p->head_dim == 128 || p->head_dim == 256, "attention: head_dim 128 or 256");
     require_attn_alignment(p);
     XTG_REQUIRE(p->n_q >= 1 && p->n_q <= kMaxRows, "attention: 1..8 query rows");
     XTG_REQUIRE(splits >= 1, "attention: at least one split");
     XTG_REQUIRE(p->ring == 0 || p->ring_pos != nullptr, "attention: a ring needs its slot -> position table");
     XTG_REQUIRE(p->ring != 0 || p->pos0 <= p->slots, "attention: pos0 beyond the cache");
     XTG_REQUIRE(p->kv_heads >= 1 && p->heads >= 1, "attention: at least one q head and one KV head");
-    XTG_REQUIRE(attention_part_floats(p->kv_heads, splits) <= kNoAllocFloats,
-                "attention_noalloc: kv_heads x splits above 256, the fixed scratch's limit (4,325,376 bytes)");
+    XTG_REQUIRE(attention_part_floats(p->kv_heads, splits, p->head_dim) <= kNoAllocFloats,
+                "attention_noalloc: kv_heads x splits above 256 (128 at head_dim 256), the fixed scratch's limit "
+                "(4,325,376 bytes)");
     float* part = noalloc_scratch();
     // every split writes the partial of every live query row that the combine reads: nothing needs clearing
     AttnArgs a = {};
@@ -323,6 +326,7 @@ int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* p, int splits, void* st
     a.splits = splits;
     a.part = part;
     a.err = nullptr;
+    a.head_dim = p->head_dim;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     launch_attention(a, s, false);
     CombineArgs cb = {};
@@ -337,6 +341,7 @@ int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* p, int splits, void* st
     cb.kv_heads = p->kv_heads;
     cb.m = p->n_q;
     cb.out = p->out;
+    cb.head_dim = p->head_dim;
     launch_attn_combine(cb, s, false);
   });
 }

@@ -31,14 +31,14 @@ namespace xtg {
 
 namespace {
 
-constexpr int kD = 128;
 constexpr int kThreads = 256;   // 8 warps: (row half) x (key quarter)
 constexpr int kQuarters = 4;    // key quarters of a chunk
 constexpr int kStages = 4;      // chunks in flight
 constexpr int kQRows = 32;
-constexpr int kPartStride = kD + 4;   // m, l, 2 pads, acc[128]: the dims 16-byte aligned
-constexpr int kXchgStride = kD + 2;   // a split-KV exchange slot: m, l, o[128] as 64-bit words
-constexpr int kMaxSplits = 256;       // parts of a cache's chunks (the combine holds one weight per part)
+constexpr int kXchgStride = 128 + 2;   // a split-KV exchange slot: m, l, o[128] as 64-bit words (head dim 128)
+constexpr int kMaxSplits = 256;        // parts of a cache's chunks (the combine holds one weight per part)
+// a partial's floats at head dim D: m, l, 2 pads, acc[D] (the dims 16-byte aligned)
+__host__ __device__ constexpr int part_stride(int D) { return D + 4; }
 
 __device__ __forceinline__ void codes_to_f16(uint32_t word, int dtype, uint32_t& lo, uint32_t& hi) {
   if (dtype == kKvFp8) {
@@ -51,26 +51,36 @@ __device__ __forceinline__ void codes_to_f16(uint32_t word, int dtype, uint32_t&
   }
 }
 
+template <int D>
 struct Stage {                    // one 64-slot chunk of one KV head, as it lies in the cache
-  uint8_t k[64 * kD];
-  uint8_t v[kD * 64];
+  uint8_t k[64 * D];
+  uint8_t v[D * 64];
   float ks[64];
   float vs[64];
   int32_t pos[64];
 };
 
+template <int D>
 struct Smem {
-  Stage stage[kStages];           // the chunk ring; after the last chunk, key quarter j's softmax state in stage[j]
+  Stage<D> stage[kStages];        // the chunk ring; after the last chunk, key quarter j's softmax state in stage[j]
   uint64_t full[kStages], empty[kStages];
-  uint4 qf[2][2][8][32];          // Q A fragments [m-tile][hi, lo][k16 step][lane]: q = hi + lo, both fp16
+  uint4 qf[2][2][D / 16][32];     // Q A fragments [m-tile][hi, lo][k16 step][lane]: q = hi + lo, both fp16
 };
-// a key quarter's state after the last chunk: per query row m, l, acc[128] (rows kD + 4 floats apart)
-static_assert(sizeof(Stage) >= kQRows * (kD + 4) * sizeof(float), "stage too small for a quarter's state");
+// a key quarter's state after the last chunk: per query row m, l, acc[D] (rows D + 4 floats apart)
+static_assert(sizeof(Stage<128>) >= kQRows * (128 + 4) * sizeof(float), "stage too small for a quarter's state");
+static_assert(sizeof(Stage<256>) >= kQRows * (256 + 4) * sizeof(float), "stage too small for a quarter's state");
 static_assert(kStages >= kQuarters, "the quarters' states live in the stages");
 
-__global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a) {
+// Head dim 256: the same warp roles over twice the dims (16 k16 steps, 32 n8 tiles of the output); the accumulator
+// takes twice the registers and a stage twice the shared memory, so one CTA fits an SM.
+template <int D>
+__global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(const AttnArgs a) {
+  static_assert(D == 128 || D == 256, "head dim 128 or 256");
+  constexpr int kSteps = D / 16;                          // k16 steps of QK^T
+  constexpr int kTiles = D / 8;                           // n8 tiles of the output
+  constexpr int kPartStride = part_stride(D);
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+  Smem<D>& sm = *reinterpret_cast<Smem<D>*>(smem_raw);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, tq = lane & 3;
   const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
@@ -81,7 +91,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   const int64_t slots = sq ? sq->slots : a.slots;
   const int group = a.heads / a.kv_heads;
   const int32_t* ring_pos = sq ? sq->ring_pos : a.ring_pos;
-  const float* aq = a.q + (int64_t)seq * kMaxRows * a.heads * kD;
+  const float* aq = a.q + (int64_t)seq * kMaxRows * a.heads * D;
   // a sequence with no rows in this step (a batched step's idle group) reads nothing: its position may lie past its
   // cache
   if (m <= 0) return;
@@ -92,15 +102,15 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   const int stot = a.splits_total > 0 ? a.splits_total : a.splits, sidx = a.split0 + split;
   const int64_t cb = nchunks * sidx / stot, ce = nchunks * (sidx + 1) / stot;
   const int nc = (int)(ce - cb);
-  const uint8_t* kc = (sq ? sq->kc : a.kc) + (int64_t)kvh * slots * kD;
-  const uint8_t* vc = (sq ? sq->vc : a.vc) + (int64_t)kvh * kD * slots;
+  const uint8_t* kc = (sq ? sq->kc : a.kc) + (int64_t)kvh * slots * D;
+  const uint8_t* vc = (sq ? sq->vc : a.vc) + (int64_t)kvh * D * slots;
   const float* ks = (sq ? sq->ks : a.ks) + (int64_t)kvh * slots;
   const float* vs = (sq ? sq->vs : a.vs) + (int64_t)kvh * slots;
-  const uint32_t stage_bytes = 2 * 64 * kD + 2 * 64 * 4 + (a.ring ? 64 * 4 : 0);
+  const uint32_t stage_bytes = 2 * 64 * D + 2 * 64 * 4 + (a.ring ? 64 * 4 : 0);
   // chunk i of this CTA into stage i % kStages, by lanes 0-4 of warp 0: one bulk copy per lane (the copies of one
   // thread complete one after another)
   auto issue = [&](int i) {
-    Stage& st = sm.stage[i % kStages];
+    Stage<D>& st = sm.stage[i % kStages];
     uint64_t* bar = &sm.full[i % kStages];
     const int64_t c = cb + i;
     if (c < 0 || (c + 1) * 64 > slots) {   // never: a chunk outside the cache is recorded, not read
@@ -111,13 +121,13 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     __syncwarp();
     if (a.l2_first) {
       const uint64_t pol = l2_evict_first();
-      if (lane == 0) bulk_g2s_hint(st.k, kc + c * 64 * kD, 64 * kD, bar, pol);
-      if (lane == 1) bulk_g2s_hint(st.v, vc + c * 64 * kD, 64 * kD, bar, pol);
+      if (lane == 0) bulk_g2s_hint(st.k, kc + c * 64 * D, 64 * D, bar, pol);
+      if (lane == 1) bulk_g2s_hint(st.v, vc + c * 64 * D, 64 * D, bar, pol);
       if (lane == 2) bulk_g2s_hint(st.ks, ks + c * 64, 64 * 4, bar, pol);
       if (lane == 3) bulk_g2s_hint(st.vs, vs + c * 64, 64 * 4, bar, pol);
     } else {
-      if (lane == 0) bulk_g2s(st.k, kc + c * 64 * kD, 64 * kD, bar);
-      if (lane == 1) bulk_g2s(st.v, vc + c * 64 * kD, 64 * kD, bar);
+      if (lane == 0) bulk_g2s(st.k, kc + c * 64 * D, 64 * D, bar);
+      if (lane == 1) bulk_g2s(st.v, vc + c * 64 * D, 64 * D, bar);
       if (lane == 2) bulk_g2s(st.ks, ks + c * 64, 64 * 4, bar);
       if (lane == 3) bulk_g2s(st.vs, vs + c * 64, 64 * 4, bar);
     }
@@ -143,25 +153,27 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     for (int i = 0; i < kStages && i < nc; ++i) issue(i);
 
   // ---- A fragments of the queries of this KV head (prepared: RoPE, justnorm, q scale), straight from memory, split
-  // q = hi + lo (both fp16) so that the scores keep ~22 bits: step st, lane tq reads head dims 32 tq + 4 st + {0, 1}
-  // (a0, a1) and + {2, 3} (a2, a3) of its rows gg and gg + 8 ----
+  // q = hi + lo (both fp16) so that the scores keep ~22 bits: step st, lane tq reads head dims
+  // 128 (st >> 3) + 32 tq + 4 (st & 7) + {0, 1} (a0, a1) and + {2, 3} (a2, a3) of its rows gg and gg + 8 ----
   auto qrow = [&](int r, int d0) {   // 4 head dims of query row r (zeros for rows past m)
     const int i = r / group, hg = r % group;
-    return i < m ? *reinterpret_cast<const float4*>(aq + ((int64_t)i * a.heads + kvh * group + hg) * kD + d0)
+    return i < m ? *reinterpret_cast<const float4*>(aq + ((int64_t)i * a.heads + kvh * group + hg) * D + d0)
                  : make_float4(0.f, 0.f, 0.f, 0.f);
   };
-  float4 qv[2][2];
+  constexpr int kFragLoads = 2 * kSteps * 32 / kThreads;   // (m-tile, step, lane) fragments per thread
+  float4 qv[kFragLoads][2];
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {   // every load first
+  for (int u = 0; u < kFragLoads; ++u) {   // every load first
     const int idx = (int)threadIdx.x + u * kThreads;
-    const int l = idx & 31, st = (idx >> 5) & 7, t2 = idx >> 8, gg = l >> 2, d0 = 32 * (l & 3) + 4 * st;
+    const int l = idx & 31, st = (idx >> 5) % kSteps, t2 = idx / (32 * kSteps), gg = l >> 2;
+    const int d0 = 128 * (st >> 3) + 32 * (l & 3) + 4 * (st & 7);
     qv[u][0] = qrow(16 * t2 + gg, d0);
     qv[u][1] = qrow(16 * t2 + gg + 8, d0);
   }
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
+  for (int u = 0; u < kFragLoads; ++u) {
     const int idx = (int)threadIdx.x + u * kThreads;
-    const int l = idx & 31, st = (idx >> 5) & 7, t2 = idx >> 8;
+    const int l = idx & 31, st = (idx >> 5) % kSteps, t2 = idx / (32 * kSteps);
     const float4 r0 = qv[u][0], r1 = qv[u][1];
     const float v[8] = {r0.x, r0.y, r1.x, r1.y, r0.z, r0.w, r1.z, r1.w};
     uint32_t hi[4], lo[4];
@@ -182,27 +194,28 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
   const int t0 = pos0 + arow0, t1 = pos0 + arow1;
   const bool live0 = arow0 < m, live1 = arow1 < m;
 
-  float acc[16][4];
+  float acc[kTiles][4];
 #pragma unroll
-  for (int dt = 0; dt < 16; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.f;
+  for (int dt = 0; dt < kTiles; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.f;
   float run_m0 = -INFINITY, run_m1 = -INFINITY, run_l0 = 0.f, run_l1 = 0.f;
 
   // This warp's 16 keys of a chunk (slot base c0) from its stage. The MMA k index of the PV product and the keys
   // are permuted so that lane tq owns the 4 consecutive keys 16 kq + 4 tq .. + 3: k = 2 tq + {0, 1} are keys
   // 4 tq + {0, 1}, k = 2 tq + 8 + {0, 1} keys 4 tq + {2, 3}. The score tile T (n8) column 2 tq + c is then key
   // 4 tq + 2 T + c, and the K row that lane g supplies to tile T is key 4 ((g >> 1) & 3) + 2 T + (g & 1).
-  auto chunk = [&](const Stage& stg, int64_t c0) {
-    // ---- S = Q K^T over 2 n8 tiles x 8 k16 steps, q = hi + lo ----
+  auto chunk = [&](const Stage<D>& stg, int64_t c0) {
+    // ---- S = Q K^T over 2 n8 tiles x kSteps k16 steps, q = hi + lo ----
     float s[2][4], sl[2][4];   // the hi and lo products accumulate apart (shorter dependency chains)
 #pragma unroll
     for (int T = 0; T < 2; ++T) s[T][0] = s[T][1] = s[T][2] = s[T][3] = sl[T][0] = sl[T][1] = sl[T][2] = sl[T][3] = 0.f;
 #pragma unroll
-    for (int hs = 0; hs < 2; ++hs) {   // head dims 32 tq + 16 hs .. + 15: k16 steps 4 hs .. 4 hs + 3
+    for (int hs = 0; hs < D / 64; ++hs) {   // dims 128 (hs >> 1) + 32 tq + 16 (hs & 1) .. + 15: steps 4 hs .. + 3
       uint4 kw[2];
 #pragma unroll
       for (int T = 0; T < 2; ++T) {
         const int key = 16 * kq + 4 * ((g >> 1) & 3) + 2 * T + (g & 1);
-        kw[T] = *reinterpret_cast<const uint4*>(stg.k + key * kD + 16 * ((2 * tq + hs) ^ swz_k(key)));
+        kw[T] = *reinterpret_cast<const uint4*>(stg.k + key * D + 128 * (hs >> 1) +
+                                                16 * ((2 * tq + (hs & 1)) ^ swz_k(key)));
       }
 #pragma unroll
       for (int sub = 0; sub < 4; ++sub) {
@@ -264,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     run_l1 *= corr1;
     if (corr0 != 1.f || corr1 != 1.f) {
 #pragma unroll
-      for (int dt = 0; dt < 16; ++dt) {
+      for (int dt = 0; dt < kTiles; ++dt) {
         acc[dt][0] *= corr0;
         acc[dt][1] *= corr0;
         acc[dt][2] *= corr1;
@@ -291,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     }
     // ---- O += P' V: head dim d = 8 dt + g; lane tq supplies keys 16 kq + 4 tq .. + 3 (one 32-bit word) ----
 #pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
+    for (int dt = 0; dt < kTiles; ++dt) {
       const int d = 8 * dt + g;
       const uint32_t w = *reinterpret_cast<const uint32_t*>(stg.v + d * 64 + 16 * (kq ^ ((d >> 1) & 3)) + 4 * tq);
       uint32_t b0, b1;
@@ -321,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
 
   // ---- merge the 4 key quarters' states (each in its own stage, every chunk consumed), then the CTA's partial ----
   // (state rows kStateStride floats apart, so that a warp's stores spread over the banks)
-  constexpr int kStateStride = kD + 4;   // m, l, acc[128], pad
+  constexpr int kStateStride = D + 4;   // m, l, acc[D], pad
   __syncthreads();
   {
     float* st = reinterpret_cast<float*>(&sm.stage[kq]);
@@ -333,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
       st[qr1 * kStateStride + 1] = run_l1;
     }
 #pragma unroll
-    for (int dt = 0; dt < 16; ++dt) {
+    for (int dt = 0; dt < kTiles; ++dt) {
       const int d = 8 * dt + 2 * tq;
       *reinterpret_cast<float2*>(&st[qr0 * kStateStride + 2 + d]) = make_float2(acc[dt][0], acc[dt][1]);
       *reinterpret_cast<float2*>(&st[qr1 * kStateStride + 2 + d]) = make_float2(acc[dt][2], acc[dt][3]);
@@ -345,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
     const int r = threadIdx.x >> 3, j = threadIdx.x & 7;
     if (r / group < m) {
       const float* st0 = reinterpret_cast<const float*>(&sm.stage[0]);
-      const int ss = (int)(sizeof(Stage) / sizeof(float));
+      const int ss = (int)(sizeof(Stage<D>) / sizeof(float));
       float mp[kQuarters], M = -INFINITY;
 #pragma unroll
       for (int q = 0; q < kQuarters; ++q) {
@@ -365,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
         out[1] = L;
       }
 #pragma unroll
-      for (int k = 0; k < kD / 8; ++k) {
+      for (int k = 0; k < D / 8; ++k) {
         const int d = j + 8 * k;
         float o = 0.f;
 #pragma unroll
@@ -380,14 +393,16 @@ __global__ void __launch_bounds__(kThreads, 2) attention_kernel(const AttnArgs a
 // Combine the splits of (activation row, q head) by log-sum-exp; then either the plain output (API) or the Dory
 // output gate, fp16 fragments for the O projection and the per-head sum of squares (the step). One CTA per (row,
 // head), one thread per head dimension; the split weights are computed once, every partial is loaded in one wave.
-__global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
+template <int D>
+__global__ void __launch_bounds__(D) attn_combine_kernel(const CombineArgs a) {
   constexpr int kRegSplits = 64;   // partials held in registers (the rest are read in a second pass)
+  constexpr int kPartStride = part_stride(D);
   __shared__ float wgt[kMaxSplits];
   __shared__ float cached[2];      // the splits' max m and their sum of l relative to it
-  __shared__ float part_s[kD / 32][kMaxRows];
+  __shared__ float part_s[D / 32][kMaxRows];
   __shared__ float ml[2][kMaxSplits];   // every split's m and l
   const int i = blockIdx.x, h = blockIdx.y, seq = blockIdx.z, d = threadIdx.x;
-  const int col = h * kD + d;
+  const int col = h * D + d;
   // the gate's scale is a parameter: loaded before the dependency wait
   const float gsc = a.out ? 0.f : a.gscale[col];
   const int m = a.params ? a.params[seq].m : a.m;
@@ -400,30 +415,31 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   const int group = a.heads / a.kv_heads, kvh = h / group, qr = i * group + h % group;
   const float* base = a.part + (int64_t)seq * a.part_seq_stride + ((int64_t)kvh * kQRows + qr) * kPartStride;
   const int64_t sstride = (int64_t)a.kv_heads * kQRows * kPartStride;   // split s at s * sstride
-  const float qd = a.q[((rows0 + i) * a.heads + h) * kD + d];
+  const float qd = a.q[((rows0 + i) * a.heads + h) * D + d];
   float kj[kMaxRows], vj[kMaxRows];
 #pragma unroll
   for (int j = 0; j < kMaxRows; ++j) {
-    kj[j] = j < m ? a.k[((rows0 + j) * a.kv_heads + kvh) * kD + d] : 0.f;
-    vj[j] = j < m ? a.v[((rows0 + j) * a.kv_heads + kvh) * kD + d] : 0.f;
+    kj[j] = j < m ? a.k[((rows0 + j) * a.kv_heads + kvh) * D + d] : 0.f;
+    vj[j] = j < m ? a.v[((rows0 + j) * a.kv_heads + kvh) * D + d] : 0.f;
   }
   const float gt = a.out ? 0.f : a.gate[(rows0 + i) * a.gate_ld + col];
-  // every independent load in one wave: this thread's dim of every split's partial, the m and l of splits d and
-  // d + 128
+  // every independent load in one wave: this thread's dim of every split's partial, the m and l of splits d,
+  // d + D, ...
   const int ns = a.splits < kRegSplits ? a.splits : kRegSplits;
   float acc_s[kRegSplits];
 #pragma unroll
   for (int s = 0; s < kRegSplits; ++s) acc_s[s] = s < ns ? base[s * sstride + 4 + d] : 0.f;
-  float mls[2][2];
+  constexpr int kMlLoads = kMaxSplits / D;
+  float mls[kMlLoads][2];
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int sp = d + u * kD;
+  for (int u = 0; u < kMlLoads; ++u) {
+    const int sp = d + u * D;
     mls[u][0] = sp < a.splits ? base[sp * sstride] : -INFINITY;
     mls[u][1] = sp < a.splits ? base[sp * sstride + 1] : 0.f;
   }
 #pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int sp = d + u * kD;
+  for (int u = 0; u < kMlLoads; ++u) {
+    const int sp = d + u * D;
     if (sp < a.splits) {
       ml[0][sp] = mls[u][0];
       ml[1][sp] = mls[u][1];
@@ -462,7 +478,9 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
 #pragma unroll
   for (int j = 0; j < kMaxRows; ++j) {
     const bool vis = j < m && j <= i && (a.window == 0 || i - j < a.window);
-    own_s[j] = vis ? ((part_s[0][j] + part_s[1][j]) + (part_s[2][j] + part_s[3][j])) * a.scale : -INFINITY;
+    float pr = (part_s[0][j] + part_s[1][j]) + (part_s[2][j] + part_s[3][j]);
+    if constexpr (D == 256) pr += (part_s[4][j] + part_s[5][j]) + (part_s[6][j] + part_s[7][j]);
+    own_s[j] = vis ? pr * a.scale : -INFINITY;
     own_m = fmaxf(own_m, own_s[j]);
   }
   float wgt_max = cached[0], lcached = cached[1];
@@ -472,7 +490,7 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
     if (s < ns) o += acc_s[s] * wgt[s];
   for (int s = kRegSplits; s < a.splits; ++s)
     if (wgt[s] != 0.f) o += base[s * sstride + 4 + d] * wgt[s];
-  if (a.x.world > 1) {
+  if (D == 128 && a.x.world > 1) {   // head dim 128 only: the exchange slots hold 128 dims
     // split-KV across GPUs: this process's cached part (m, l, o relative to m) to every peer, theirs from this
     // process's slots, all merged in rank order (the same bits on every process)
     const uint32_t run = *a.x.epoch * (uint32_t)a.x.n_g + (uint32_t)a.x.g, seq = run + 1;
@@ -535,24 +553,24 @@ __global__ void __launch_bounds__(kD) attn_combine_kernel(const CombineArgs a) {
   }
   o *= lsum > 0.f ? 1.f / lsum : 0.f;
   if (a.out) {
-    a.out[((int64_t)i * a.heads + h) * kD + d] = o;
+    a.out[((int64_t)i * a.heads + h) * D + d] = o;
     return;
   }
   o *= 1.f / (1.f + expf(-gt * gsc));
   __shared__ float red[32];
   const float ss = block_sum(o * o, red);
   if (a.gated_out) {   // the batched step: f32 rows for the GEMM's digitizer
-    a.gated_out[(rows0 + i) * a.heads * kD + col] = o;
+    a.gated_out[(rows0 + i) * a.heads * D + col] = o;
     if (d == 0) a.asum[h * a.asum_ld + rows0 + i] = ss;
     return;
   }
   if (d == 0) a.asum[(int64_t)i * a.heads + h] = ss;   // [row][head]: the O projection's parts of row i together
-  // the O projection's input: this head's 8 groups of 16 as B digits (warp 0, a quad per group)
-  __shared__ float ov[kD];
+  // the O projection's input: this head's D / 16 groups of 16 as B digits (a quad per group)
+  __shared__ float ov[D];
   ov[d] = o;
   __syncthreads();
-  if (d < 32) {
-    const int gl = d >> 2, t = d & 3, G = h * (kD / 16) + gl;
+  if (d < D / 4) {
+    const int gl = d >> 2, t = d & 3, G = h * (D / 16) + gl;
     const float v[4] = {ov[16 * gl + 4 * t], ov[16 * gl + 4 * t + 1], ov[16 * gl + 4 * t + 2], ov[16 * gl + 4 * t + 3]};
     uint32_t code[kDigits], sf[kDigits];
     const float p = digitize16_quad(v, code, sf);
@@ -573,6 +591,7 @@ __device__ __forceinline__ float4 ld4g(const float* p) { return *reinterpret_cas
 __device__ __forceinline__ float dot4(float4 a, float4 b) { return (a.x * b.x + a.y * b.y) + (a.z * b.z + a.w * b.w); }
 
 __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(const CombineArgs a) {
+  constexpr int kD = 128, kPartStride = part_stride(kD);   // head dim 128
   const int lane = threadIdx.x & 31;
   const int pair = (int)blockIdx.x * (int)(blockDim.x >> 5) + (int)(threadIdx.x >> 5);
   const int per_seq = kMaxRows * a.heads;
@@ -658,9 +677,11 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(c
 
 }  // namespace
 
-size_t attention_smem_bytes() { return sizeof(Smem); }
+int attention_ctas_per_sm(int head_dim) { return head_dim == 256 ? 1 : 2; }
 
-int64_t attention_part_floats(int kv_heads, int splits) { return (int64_t)kv_heads * splits * kQRows * kPartStride; }
+int64_t attention_part_floats(int kv_heads, int splits, int head_dim) {
+  return (int64_t)kv_heads * splits * kQRows * part_stride(head_dim);
+}
 
 void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
   AttnArgs a = a_in;
@@ -672,25 +693,37 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
   XTG_REQUIRE(a.splits_total == 0 || (a.split0 >= 0 && a.split0 + a.splits <= a.splits_total &&
                                        a.splits_total <= kMaxSplits),
               "attention: split range outside 0..splits_total (at most 256)");
-  static std::atomic<uint64_t> optin{0};
-  ensure_smem_optin((const void*)attention_kernel, (int)sizeof(Smem), optin);
+  if (a.head_dim == 0) a.head_dim = 128;
+  XTG_REQUIRE(a.head_dim == 128 || a.head_dim == 256, "attention: head_dim 128 or 256");
+  const bool d256 = a.head_dim == 256;
+  const void* fn = d256 ? (const void*)attention_kernel<256> : (const void*)attention_kernel<128>;
+  const int smem = d256 ? (int)sizeof(Smem<256>) : (int)sizeof(Smem<128>);
+  static std::atomic<uint64_t> optin128{0}, optin256{0};
+  ensure_smem_optin(fn, smem, d256 ? optin256 : optin128);
   cudaLaunchConfig_t cfg = {};
   XTG_REQUIRE(!a.seqs || (a.nseq >= 1 && a.nseq <= kMaxBatch && a.params), "attention: 1..8 sequences with params");
   cfg.gridDim = dim3(a.splits, a.kv_heads, a.seqs ? a.nseq : 1);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = sizeof(Smem);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  XTG_CUDA(cudaLaunchKernelEx(&cfg, attention_kernel, a));
+  if (d256)
+    XTG_CUDA(cudaLaunchKernelEx(&cfg, attention_kernel<256>, a));
+  else
+    XTG_CUDA(cudaLaunchKernelEx(&cfg, attention_kernel<128>, a));
 }
 
 void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
   CombineArgs a = a_in;
   a.pdl = pdl ? 1 : 0;
+  if (a.head_dim == 0) a.head_dim = 128;
+  XTG_REQUIRE(a.head_dim == 128 || a.head_dim == 256, "combine: head_dim 128 or 256");
+  XTG_REQUIRE(a.head_dim == 128 || (a.x.world <= 1 && !a.gated_out),
+              "combine: head_dim 256 in one process and the 8-row step (no split-KV exchange, no batched step)");
   XTG_REQUIRE(a.splits >= 1 && a.splits <= kMaxSplits, "combine: 1..256 splits");
   XTG_REQUIRE(a.kv_heads >= 1 && a.heads >= 1 && a.heads % a.kv_heads == 0, "combine: q heads a multiple of KV heads");
   XTG_REQUIRE(a.x.world <= 1 || (a.x.world <= kMaxKvWorld && a.x.rank >= 0 && a.x.rank < a.x.world && a.x.epoch &&
@@ -720,8 +753,11 @@ void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
     return;
   }
   cfg.gridDim = dim3(kMaxRows, a.heads, a.gated_out ? a.nseq : 1);
-  cfg.blockDim = dim3(kD);
-  XTG_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_kernel, a));
+  cfg.blockDim = dim3(a.head_dim);
+  if (a.head_dim == 256)
+    XTG_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_kernel<256>, a));
+  else
+    XTG_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_kernel<128>, a));
 }
 
 }  // namespace xtg

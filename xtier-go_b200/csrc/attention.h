@@ -8,20 +8,23 @@ namespace xtg {
 
 enum KvDtype { kKvInt8 = 0, kKvFp8 = 1 };
 
-// ---- the cache layout of one instance (slots a multiple of 64; codes 8-bit, scales f32 [kv_heads][slots]) ----
-// K: [kv_heads][slots][128], the 16-byte unit u of slot s's row stored at unit u ^ swz_k(s % 64);
-// V: [kv_heads][slots / 64][128][64] (a 64-slot chunk of a head is one contiguous 8 KB block, head dim d its row),
+// ---- the cache layout of one instance (slots a multiple of 64; head dim D 128 or 256; codes 8-bit, scales f32
+// [kv_heads][slots]) ----
+// K: [kv_heads][slots][D], each 128-dim half of a row as 8 16-byte units, unit u of slot s's half stored at unit
+//    u ^ swz_k(s % 64);
+// V: [kv_heads][slots / 64][D][64] (a 64-slot chunk of a head is one contiguous D x 64 block, head dim d its row),
 //    the 16-byte unit u (slots 16 u .. 16 u + 15 of the chunk) of row d stored at unit u ^ ((d >> 1) & 3).
 // The XORs make the attention kernel's fragment reads from shared memory bank-conflict free; a chunk of K, V and
 // its scales are contiguous so that each arrives in one bulk copy.
 __host__ __device__ __forceinline__ int swz_k(int s64) { return (s64 ^ (s64 >> 3)) & 7; }
 
-__host__ __device__ __forceinline__ int64_t k_offset(int h, int64_t slot, int d, int64_t slots) {
-  return ((int64_t)h * slots + slot) * 128 + 16 * ((d >> 4) ^ swz_k((int)(slot & 63))) + (d & 15);
+__host__ __device__ __forceinline__ int64_t k_offset(int h, int64_t slot, int d, int64_t slots, int D = 128) {
+  return ((int64_t)h * slots + slot) * D + 128 * (d >> 7) + 16 * (((d >> 4) & 7) ^ swz_k((int)(slot & 63))) +
+         (d & 15);
 }
 
-__host__ __device__ __forceinline__ int64_t v_offset(int h, int d, int64_t slot, int64_t slots) {
-  return (((int64_t)h * (slots / 64) + slot / 64) * 128 + d) * 64 + 16 * ((int)((slot & 63) >> 4) ^ ((d >> 1) & 3)) +
+__host__ __device__ __forceinline__ int64_t v_offset(int h, int d, int64_t slot, int64_t slots, int D = 128) {
+  return (((int64_t)h * (slots / 64) + slot / 64) * D + d) * 64 + 16 * ((int)((slot & 63) >> 4) ^ ((d >> 1) & 3)) +
          (slot & 15);
 }
 
@@ -53,7 +56,7 @@ struct PeerXchg {
 struct KvSeq;   // batch.h
 
 struct AttnArgs {
-  // this call's rows, prepared (RoPE, justnorm, q scale): q [m][heads][128], k / v [m][kv_heads][128] (already in the
+  // this call's rows, prepared (RoPE, justnorm, q scale): q [m][heads][D], k / v [m][kv_heads][D] (already in the
   // cache at positions pos0 .. pos0 + m - 1; the scores against them use these unquantized rows)
   const float* q;
   const float* k;
@@ -77,7 +80,7 @@ struct AttnArgs {
   // The chunks of the cache are cut into splits_total parts; this launch computes parts split0 .. split0 + splits - 1
   // (another process may compute the rest: the batch-1 split-KV over GPUs). 0 / 0: split0 0, splits_total = splits.
   int split0, splits_total;
-  float* part;              // [splits_total][kv_heads][32][132] (m, l, 2 pads, acc[128]), split-major (a process's
+  float* part;              // [splits_total][kv_heads][32][D + 4] (m, l, 2 pads, acc[D]), split-major (a process's
                             // splits are contiguous)
   int part_local;           // partials at index split (this launch's own) instead of split0 + split
   int* err;                 // set if a bounded wait gave up (never expected); may be null
@@ -93,6 +96,7 @@ struct AttnArgs {
   int late_copies;
   // the cache's chunks with the L2 evict_first policy (a global cache, read once per step; a ring stays in L2)
   int l2_first;
+  int head_dim;             // D: 128 (0 reads as 128) or 256
 };
 
 struct CombineArgs {
@@ -106,12 +110,12 @@ struct CombineArgs {
   int splits, heads, kv_heads;   // splits: every part of the cache's chunks (AttnArgs::splits_total)
   const StepParams* params;
   int m;
-  float* out;               // API: [m][heads][128]; null in the step
+  float* out;               // API: [m][heads][D]; null in the step
   const float* gate;        // step: g rows [m][gate_ld] (the projection's g columns)
   int gate_ld;
-  const float* gscale;      // [heads * 128]
-  uint8_t* ab;              // step: the gated output as B digits (the O projection's input, K = heads * 128)
-  float* ab_pre;            // [heads * 8][8] their prescales
+  const float* gscale;      // [heads * D]
+  uint8_t* ab;              // step: the gated output as B digits (the O projection's input, K = heads * D)
+  float* ab_pre;            // [heads * D / 16][8] their prescales
   float* asum;              // step: [8][heads] sum of squares per activation row and head
   int pdl;
   PeerXchg x;               // split-KV across GPUs: splits are this process's, merged with the peers' here
@@ -122,10 +126,12 @@ struct CombineArgs {
   int asum_ld;
   int nseq;
   int64_t part_seq_stride;
+  int head_dim;             // D: 128 (0 reads as 128) or 256
 };
 
-size_t attention_smem_bytes();
-int64_t attention_part_floats(int kv_heads, int splits);
+// CTAs of the attention kernel that fit on one SM at head dim D (2 at 128, 1 at 256)
+int attention_ctas_per_sm(int head_dim);
+int64_t attention_part_floats(int kv_heads, int splits, int head_dim = 128);
 void launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 void launch_attn_combine(const CombineArgs& a, cudaStream_t s, bool pdl);
 

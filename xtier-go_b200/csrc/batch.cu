@@ -99,34 +99,43 @@ __global__ void embed_batch_kernel(const EmbedBatchArgs a) {
   }
 }
 
-// Sum of v over the 128 threads of the block (4 warps), every thread gets it; red: 4 floats, fixed order.
-__device__ __forceinline__ float sum128(float v, float* red) {
+// Sum (max) of v over the D threads of the block (D / 32 warps), every thread gets it; red: D / 32 floats, fixed
+// order.
+template <int D>
+__device__ __forceinline__ float sum_heads(float v, float* red) {
   v = warp_sum(v);
   __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  return (red[0] + red[1]) + (red[2] + red[3]);
+  float t = (red[0] + red[1]) + (red[2] + red[3]);
+  if constexpr (D == 256) t += (red[4] + red[5]) + (red[6] + red[7]);
+  return t;
 }
-__device__ __forceinline__ float max128(float v, float* red) {
+template <int D>
+__device__ __forceinline__ float max_heads(float v, float* red) {
   v = warp_max(v);
   __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
   __syncthreads();
-  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  float t = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  if constexpr (D == 256) t = fmaxf(t, fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
+  return t;
 }
 
-// grid (2 heads + 2 kv_heads, 8 nseq), 128 threads: thread d of head column block h, activation row r = 8 s + i.
-// The gate's blocks only sum the K parts (into part 0, which the combine reads).
-__global__ void __launch_bounds__(128) qkv_prep_kernel(const QkvPrepArgs a) {
-  __shared__ float red[4];
-  __shared__ float xs[128];
+// grid (2 heads + 2 kv_heads, 8 nseq), D threads: thread d of head column block h, activation row r = 8 s + i.
+// The gate's blocks only sum the K parts (into part 0, which the combine reads). Also the 8-row step's q|k|v
+// preparation at head dim 256 (nseq 1, one K part), where a head spans two of the GEMV's 128-row tiles.
+template <int D>
+__global__ void __launch_bounds__(D) qkv_prep_kernel(const QkvPrepArgs a) {
+  constexpr int kHalf = D / 2;
+  __shared__ float red[D / 32];
+  __shared__ float xs[D];
   const int hb = blockIdx.x, r = blockIdx.y, s = r / kMaxRows, i = r % kMaxRows, d = threadIdx.x;
   const int nq = a.heads, nk = a.kv_heads;
   const int type = hb < nq ? 0 : hb < nq + nk ? 1 : hb < nq + 2 * nk ? 2 : 3;   // q, k, v, gate
   const int h = type == 0 ? hb : type == 1 ? hb - nq : type == 2 ? hb - nq - nk : hb - nq - 2 * nk;
-  const int col = (type == 0 ? 0 : type == 1 ? nq * 128 : type == 2 ? (nq + nk) * 128 : (nq + 2 * nk) * 128) +
-                  h * 128 + d;
-  const float qs = type == 0 ? a.qscale[h * 128 + d] : 0.f;   // a parameter: before the wait
+  const int col = (type == 0 ? 0 : type == 1 ? nq * D : type == 2 ? (nq + nk) * D : (nq + 2 * nk) * D) + h * D + d;
+  const float qs = type == 0 ? a.qscale[h * D + d] : 0.f;   // a parameter: before the wait
   if (a.pdl) {
     pdl_wait();
     pdl_launch_next();
@@ -140,22 +149,22 @@ __global__ void __launch_bounds__(128) qkv_prep_kernel(const QkvPrepArgs a) {
     return;
   }
   float v = x;
-  if (type <= 1) {   // NeoX RoPE on (d, d + 64), then justnorm over the head
+  if (type <= 1) {   // NeoX RoPE on (d, d + D / 2), then justnorm over the head
     xs[d] = x;
     __syncthreads();
-    const int64_t at = (((int64_t)s * 2 + a.theta) * kMaxRows + i) * 64 + (d & 63);
+    const int64_t at = (((int64_t)s * 2 + a.theta) * kMaxRows + i) * kHalf + (d & (kHalf - 1));
     const float c = a.rope_cos[at], sn = a.rope_sin[at];
-    const float other = xs[d ^ 64];
-    v = d < 64 ? x * c - other * sn : x * c + other * sn;
-    v *= 1.f / sqrtf(sum128(v * v, red) + 1e-6f);
+    const float other = xs[d ^ kHalf];
+    v = d < kHalf ? x * c - other * sn : x * c + other * sn;
+    v *= 1.f / sqrtf(sum_heads<D>(v * v, red) + 1e-6f);
   }
   if (type == 0) {
-    a.q_out[((int64_t)r * a.heads + h) * 128 + d] = v * qs;
+    a.q_out[((int64_t)r * a.heads + h) * D + d] = v * qs;
     return;
   }
   // k / v: the prepared row, and its codes and scale in the sequence's cache (the KvCache::store rule)
-  (type == 1 ? a.k_out : a.v_out)[((int64_t)r * a.kv_heads + h) * 128 + d] = v;
-  const float amax = max128(fabsf(v), red);
+  (type == 1 ? a.k_out : a.v_out)[((int64_t)r * a.kv_heads + h) * D + d] = v;
+  const float amax = max_heads<D>(fabsf(v), red);
   const float top = a.dtype == kKvFp8 ? 448.f : 127.f;
   const float sc = amax > 0.f ? __fdiv_rn(amax, top) : 1.f;
   const float tq = __fmul_rn(v, __fdiv_rn(1.f, sc));
@@ -173,9 +182,9 @@ __global__ void __launch_bounds__(128) qkv_prep_kernel(const QkvPrepArgs a) {
     return;
   }
   if (type == 1)
-    kv.kc[k_offset(h, slot, d, kv.slots)] = code;
+    kv.kc[k_offset(h, slot, d, kv.slots, D)] = code;
   else
-    kv.vc[v_offset(h, d, slot, kv.slots)] = code;
+    kv.vc[v_offset(h, d, slot, kv.slots, D)] = code;
   if (d == 0) (type == 1 ? kv.ks : kv.vs)[(int64_t)h * kv.slots + slot] = sc;
 }
 
@@ -386,8 +395,14 @@ void launch_embed_batch(const EmbedBatchArgs& a, cudaStream_t s) {
 
 void launch_qkv_prep(const QkvPrepArgs& a, cudaStream_t s) {
   XTG_REQUIRE(a.nseq >= 1 && a.nseq <= kMaxBatch && a.ksplit >= 1, "qkv_prep: 1..8 sequences");
-  launch_with_pdl(qkv_prep_kernel, dim3(2 * a.heads + 2 * a.kv_heads, kMaxRows * a.nseq), dim3(128), 0, a, s,
-                  a.pdl != 0);
+  const int D = a.head_dim > 0 ? a.head_dim : 128;
+  XTG_REQUIRE(D == 128 || D == 256, "qkv_prep: head_dim 128 or 256");
+  if (D == 256)
+    launch_with_pdl(qkv_prep_kernel<256>, dim3(2 * a.heads + 2 * a.kv_heads, kMaxRows * a.nseq), dim3(256), 0, a, s,
+                    a.pdl != 0);
+  else
+    launch_with_pdl(qkv_prep_kernel<128>, dim3(2 * a.heads + 2 * a.kv_heads, kMaxRows * a.nseq), dim3(128), 0, a, s,
+                    a.pdl != 0);
 }
 
 void launch_swiglu_batch(const SwigluBatchArgs& a, cudaStream_t s) {

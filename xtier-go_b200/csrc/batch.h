@@ -52,17 +52,18 @@ struct QkvPrepArgs {
   int proj_ld, ksplit;
   int64_t split_stride;
   int heads, kv_heads;
-  const float* rope_cos;      // [nseq][2][8][64], this layer's theta at [s][theta]
+  const float* rope_cos;      // [nseq][2][8][D / 2], this layer's theta at [s][theta]
   const float* rope_sin;
   int theta;
-  const float* qscale;        // [heads * 128]
-  float* q_out;               // [8 nseq][heads][128]
-  float* k_out;               // [8 nseq][kv_heads][128]
+  const float* qscale;        // [heads * D]
+  float* q_out;               // [8 nseq][heads][D]
+  float* k_out;               // [8 nseq][kv_heads][D]
   float* v_out;
   const KvSeq* seqs;          // [nseq]
   int ring, dtype;
   int* err;                   // set (4) for a position outside its cache (nothing is written there)
   int pdl;
+  int head_dim;               // D: 128 (0 reads as 128) or 256
 };
 
 // gate / up rows (interleaved tiles: columns 128 t + r, r < 64 gate feature 64 t + r, else up feature 64 t + r - 64)

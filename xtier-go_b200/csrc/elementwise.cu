@@ -70,13 +70,14 @@ __global__ void embed_kernel(const EmbedArgs a) {
   digitize_row(rowbuf, a.hidden, r, r >= m, a.xb, a.xb_pre, 0.f);
   // RoPE tables of this step's positions (FP32(pos) * inv_freq, then cos / sin), one per theta
   if (r < a.n_thetas) {
-    for (int idx = threadIdx.x; idx < kMaxRows * 64; idx += blockDim.x) {
-      const int i = idx / 64, e = idx % 64;
-      const float ang = __fmul_rn((float)(pos0 + i), a.inv_freq[r * 64 + e]);
+    const int half = a.rope_half > 0 ? a.rope_half : 64;
+    for (int idx = threadIdx.x; idx < kMaxRows * half; idx += blockDim.x) {
+      const int i = idx / half, e = idx % half;
+      const float ang = __fmul_rn((float)(pos0 + i), a.inv_freq[r * half + e]);
       float s, c;
       sincosf(ang, &s, &c);
-      a.rope_cos[(r * kMaxRows + i) * 64 + e] = c;
-      a.rope_sin[(r * kMaxRows + i) * 64 + e] = s;
+      a.rope_cos[(r * kMaxRows + i) * half + e] = c;
+      a.rope_sin[(r * kMaxRows + i) * half + e] = s;
     }
   }
   // the ring's slot -> position table gains this step's rows (attention masks positions >= pos0 anyway)
@@ -424,16 +425,16 @@ __global__ void kv_store_kernel(const KvStoreArgs a) {
 // The seeded prefill of one instance (the oracle's xo_synth_state_new): element (slot, head, e) of K / V codes is
 // draw (slot * kv_heads + head) * 128 + e of its stream, scales draw slot * kv_heads + head; `filled` slots.
 __global__ void kv_prefill_kernel(uint64_t key_k, uint64_t key_v, uint64_t key_ks, uint64_t key_vs, float lo,
-                                  float span, int64_t filled, int kv_heads, int64_t slots, uint8_t* kc, uint8_t* vc,
-                                  float* ks, float* vs) {
-  const int64_t total = filled * kv_heads * 128;
+                                  float span, int64_t filled, int kv_heads, int hd, int64_t slots, uint8_t* kc,
+                                  uint8_t* vc, float* ks, float* vs) {
+  const int64_t total = filled * kv_heads * hd;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int e = (int)(i % 128);
-    const int64_t sh = i / 128;   // slot * kv_heads + head
+    const int e = (int)(i % hd);
+    const int64_t sh = i / hd;   // slot * kv_heads + head
     const int h = (int)(sh % kv_heads);
     const int64_t s = sh / kv_heads;
-    kc[k_offset(h, s, e, slots)] = (uint8_t)(int8_t)((int)(rand_bits(key_k, i) % 255u) - 127);
-    vc[v_offset(h, e, s, slots)] = (uint8_t)(int8_t)((int)(rand_bits(key_v, i) % 255u) - 127);
+    kc[k_offset(h, s, e, slots, hd)] = (uint8_t)(int8_t)((int)(rand_bits(key_k, i) % 255u) - 127);
+    vc[v_offset(h, e, s, slots, hd)] = (uint8_t)(int8_t)((int)(rand_bits(key_v, i) % 255u) - 127);
     if (e == 0) {
       ks[(int64_t)h * slots + s] = uniform_from_bits(rand_bits(key_ks, sh), lo, span);
       vs[(int64_t)h * slots + s] = uniform_from_bits(rand_bits(key_vs, sh), lo, span);
@@ -504,15 +505,15 @@ void launch_kv_store(const KvStoreArgs& a, cudaStream_t s) {
   XTG_CUDA(cudaGetLastError());
 }
 
-void kv_prefill(uint64_t seed, uint64_t stream_base, float lo, float hi, int64_t filled, int kv_heads, int64_t slots,
-                uint8_t* kc, uint8_t* vc, float* ks, float* vs, cudaStream_t s) {
+void kv_prefill(uint64_t seed, uint64_t stream_base, float lo, float hi, int64_t filled, int kv_heads, int hd,
+                int64_t slots, uint8_t* kc, uint8_t* vc, float* ks, float* vs, cudaStream_t s) {
   if (filled <= 0) return;
-  const int64_t total = filled * kv_heads * 128;
+  const int64_t total = filled * kv_heads * hd;
   const int64_t g = (total + 255) / 256;
   const int grid = (int)(g < 148 * 16 ? g : 148 * 16);
   kv_prefill_kernel<<<grid, 256, 0, s>>>(rand_key(seed, stream_base + 0), rand_key(seed, stream_base + 1),
                                          rand_key(seed, stream_base + 2), rand_key(seed, stream_base + 3), lo,
-                                         hi - lo, filled, kv_heads, slots, kc, vc, ks, vs);
+                                         hi - lo, filled, kv_heads, hd, slots, kc, vc, ks, vs);
   XTG_CUDA(cudaGetLastError());
 }
 

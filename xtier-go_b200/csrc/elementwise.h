@@ -19,9 +19,10 @@ struct EmbedArgs {
   float* h;                 // [8][hidden]
   uint8_t* xb;              // B digits of h
   float* xb_pre;            // [hidden / 16][8] their prescales
-  const float* inv_freq;    // [n_thetas][64]
+  const float* inv_freq;    // [n_thetas][half]
   int n_thetas;
-  float* rope_cos;          // [n_thetas][8][64]
+  int rope_half;            // half the head dim: 64 (0 reads as 64) or 128
+  float* rope_cos;          // [n_thetas][8][half]
   float* rope_sin;
   int32_t* ring_pos;        // null without sliding layers
   int64_t ring;
@@ -79,7 +80,7 @@ void launch_resid(const ResidArgs& a, cudaStream_t s, bool pdl);
 void launch_argmax(const ArgCand* cand, int tiles, const StepParams* params, int32_t* out, float* out_val,
                    uint32_t* epoch, cudaStream_t s, bool pdl);
 void launch_kv_store(const KvStoreArgs& a, cudaStream_t s);
-void kv_prefill(uint64_t seed, uint64_t stream_base, float lo, float hi, int64_t filled, int kv_heads, int64_t slots,
-                uint8_t* kc, uint8_t* vc, float* ks, float* vs, cudaStream_t s);
+void kv_prefill(uint64_t seed, uint64_t stream_base, float lo, float hi, int64_t filled, int kv_heads, int hd,
+                int64_t slots, uint8_t* kc, uint8_t* vc, float* ks, float* vs, cudaStream_t s);
 
 }  // namespace xtg

@@ -197,7 +197,9 @@ Config parse_config(const std::string& options, const DoryConfig* ck = nullptr) 
     throw CudaError("kv_world: 1..8 processes, kv_rank below it");
   if (c.kv_world > 1 && c.nccl_id.size() != 2 * sizeof(ncclUniqueId))
     throw CudaError("nccl_id: the NCCL unique id as " + std::to_string(2 * sizeof(ncclUniqueId)) + " hex digits");
-  if (c.head_dim != 128) throw CudaError("model: head_dim must be 128");
+  if (c.head_dim != 128 && c.head_dim != 256) throw CudaError("model: head_dim must be 128 or 256");
+  if (c.head_dim != 128 && c.kv_world > 1)
+    throw CudaError("kv_world: split-KV across GPUs takes head_dim 128 (the exchange slots hold 128 dims)");
   if (c.heads % c.kv_heads || c.heads / c.kv_heads > 4) throw CudaError("model: at most 4 q heads per KV head");
   if (c.hidden % 64 || c.ffn % 64 || c.hidden > 8192) throw CudaError("model: hidden, ffn multiples of 64, hidden <= 8192");
   if (c.vocab <= 0 || c.n_in < 0 || c.n_rec < 0 || c.n_out < 0 || c.loops < 0 || c.n_evals() <= 0)
@@ -293,13 +295,14 @@ struct xtg_cuda {
   std::vector<Eval> evals;
   Linear head;
   float* logit_scale = nullptr;
-  float* inv_freq = nullptr;   // [2][64]
+  float* inv_freq = nullptr;   // [2][head_dim / 2]
   // a checkpoint's BF16 embedding table and (head "bf16") BF16 lm_head, [vocab][hidden]; null for the synthetic
   // model, whose tied NVFP4 head is also its embedding
   uint16_t* embed_bf16 = nullptr;
   uint16_t* head_w_bf16 = nullptr;
   // session
   std::vector<KvInst> kv;
+  KvSeq* kv_seq_dev = nullptr;   // the instances as the q|k|v preparation kernel takes them (head dim 256)
   int32_t* ring_pos_dev = nullptr;
   std::vector<int64_t> ring_pos;
   int64_t n_past = 0;
@@ -385,11 +388,11 @@ struct xtg_cuda {
     v.clear();
   }
 
-  static KvInst alloc_kv(int kv_heads, int64_t slots, bool ring, cudaStream_t s) {
+  static KvInst alloc_kv(int kv_heads, int hd, int64_t slots, bool ring, cudaStream_t s) {
     KvInst k;
     k.slots = slots;
     k.ring = ring;
-    const size_t codes = (size_t)kv_heads * slots * 128, sc = (size_t)kv_heads * slots * sizeof(float);
+    const size_t codes = (size_t)kv_heads * slots * hd, sc = (size_t)kv_heads * slots * sizeof(float);
     cudaError_t e = cudaMalloc(&k.kc, codes);
     if (e == cudaSuccess) e = cudaMalloc(&k.vc, codes);
     if (e == cudaSuccess) e = cudaMalloc(&k.ks, sc);
@@ -410,14 +413,14 @@ struct xtg_cuda {
     return k;
   }
 
-  static void copy_kv(const KvInst& src, KvInst& dst, int kv_heads, int64_t used, cudaStream_t s) {
+  static void copy_kv(const KvInst& src, KvInst& dst, int kv_heads, int hd, int64_t used, cudaStream_t s) {
     if (used <= 0) return;
-    // K [kv_heads][slots][128]: rows of used * 128 bytes
-    XTG_CUDA(cudaMemcpy2DAsync(dst.kc, dst.slots * 128, src.kc, src.slots * 128, used * 128, kv_heads,
+    // K [kv_heads][slots][hd]: rows of used * hd bytes
+    XTG_CUDA(cudaMemcpy2DAsync(dst.kc, dst.slots * hd, src.kc, src.slots * hd, used * hd, kv_heads,
                                cudaMemcpyDeviceToDevice, s));
-    // V [kv_heads][slots / 64][128][64]: the whole 64-slot chunks that hold the first `used` slots
-    const int64_t vbytes = (used + 63) / 64 * 64 * 128;
-    XTG_CUDA(cudaMemcpy2DAsync(dst.vc, dst.slots * 128, src.vc, src.slots * 128, vbytes, kv_heads,
+    // V [kv_heads][slots / 64][hd][64]: the whole 64-slot chunks that hold the first `used` slots
+    const int64_t vbytes = (used + 63) / 64 * 64 * hd;
+    XTG_CUDA(cudaMemcpy2DAsync(dst.vc, dst.slots * hd, src.vc, src.slots * hd, vbytes, kv_heads,
                                cudaMemcpyDeviceToDevice, s));
     XTG_CUDA(cudaMemcpy2DAsync(dst.ks, dst.slots * 4, src.ks, src.slots * 4, used * 4, kv_heads,
                                cudaMemcpyDeviceToDevice, s));
@@ -550,10 +553,11 @@ struct xtg_cuda {
     logit_scale = vec(2, c.ls_lo, c.ls_hi, c.vocab);
     XTG_REQUIRE(cursor == arena + arena_bytes, "weight arena size mismatch");
     // RoPE inverse frequencies, computed as the reference does on the host: 1 / theta^(2i / d) in FP32
-    std::vector<float> inv(128);
+    const int half = c.head_dim / 2;
+    std::vector<float> inv(2 * half);
     const float th[2] = {c.theta_sliding, c.theta_global};
     for (int t = 0; t < 2; ++t)
-      for (int i = 0; i < 64; ++i) inv[t * 64 + i] = 1.f / std::pow(th[t], float(2 * i) / float(c.head_dim));
+      for (int i = 0; i < half; ++i) inv[t * half + i] = 1.f / std::pow(th[t], float(2 * i) / float(c.head_dim));
     inv_freq = walloc<float>(inv.size());
     XTG_CUDA(cudaMemcpyAsync(inv_freq, inv.data(), inv.size() * sizeof(float), cudaMemcpyHostToDevice, stream));
     XTG_CUDA(cudaStreamSynchronize(stream));
@@ -742,10 +746,11 @@ struct xtg_cuda {
     for (float& x : ls) x /= dc.init_range;
     logit_scale = wupload(ls);
     XTG_REQUIRE(cursor == arena + arena_bytes, "weight arena size mismatch");
-    std::vector<float> inv(128);
+    const int half = c.head_dim / 2;
+    std::vector<float> inv(2 * half);
     const float th[2] = {c.theta_sliding > 0 ? c.theta_sliding : 1e4f, c.theta_global > 0 ? c.theta_global : 1e4f};
     for (int t = 0; t < 2; ++t)
-      for (int i = 0; i < 64; ++i) inv[t * 64 + i] = 1.f / std::pow(th[t], float(2 * i) / float(c.head_dim));
+      for (int i = 0; i < half; ++i) inv[t * half + i] = 1.f / std::pow(th[t], float(2 * i) / float(c.head_dim));
     inv_freq = wupload(inv);
     XTG_CUDA(cudaStreamSynchronize(stream));
     make_outs();
@@ -830,16 +835,19 @@ struct xtg_cuda {
     cand = dalloc<ArgCand>((size_t)packed_tiles(c.vocab, false) * kMaxRows);
     argmax = dalloc<int32_t>(kMaxRows);
     argmax_val = dalloc<float>(kMaxRows);
-    rope_cos = dalloc<float>(2 * kMaxRows * 64);
-    rope_sin = dalloc<float>(2 * kMaxRows * 64);
+    rope_cos = dalloc<float>((size_t)2 * kMaxRows * (c.head_dim / 2));
+    rope_sin = dalloc<float>((size_t)2 * kMaxRows * (c.head_dim / 2));
     dev_err = dalloc<int>(1);
     XTG_CUDA(cudaMallocHost(&err_host, sizeof(int)));
     *err_host = 0;
-    // the attention runs 2 CTAs per SM: a global cache over every CTA slot, a ring one 64-slot chunk per CTA
-    splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, std::min(256, 2 * num_sms / c.kv_heads));
+    // the attention runs 2 CTAs per SM (1 at head dim 256): a global cache over every CTA slot, a ring one 64-slot
+    // chunk per CTA
+    const int per_sm = attention_ctas_per_sm(c.head_dim);
+    splits_g = c.splits_global > 0 ? c.splits_global : std::max(1, std::min(256, per_sm * num_sms / c.kv_heads));
     splits_g = std::min(splits_g, 256 / c.kv_world);   // the combine takes at most 256 parts
     splits_r = c.splits_ring > 0 ? c.splits_ring : std::max(1, std::min(256, (int)(c.ring / 64)));
-    part = dalloc<float>((size_t)attention_part_floats(c.kv_heads, std::max(splits_g * c.kv_world, splits_r)));
+    part = dalloc<float>(
+        (size_t)attention_part_floats(c.kv_heads, std::max(splits_g * c.kv_world, splits_r), c.head_dim));
     ring_pos_dev = dalloc<int32_t>(c.ring);
     ring_pos.assign(c.ring, -1);
     std::vector<int32_t> neg(c.ring, -1);
@@ -850,10 +858,22 @@ struct xtg_cuda {
   void alloc_caches() {
     for (int e = 0; e < c.n_evals(); ++e)
       if (evals[e].kind != 0)
-        kv.push_back(alloc_kv(c.kv_heads, evals[e].kind == 1 ? c.ring : c.context, evals[e].kind == 1, stream));
+        kv.push_back(alloc_kv(c.kv_heads, c.head_dim, evals[e].kind == 1 ? c.ring : c.context, evals[e].kind == 1,
+                              stream));
     n_glob = 0;
     for (int e = 0; e < c.n_evals(); ++e) n_glob += evals[e].kind == 2;
     snaps.resize(c.snapshots);
+    kv_seq_dev = dalloc<KvSeq>(kv.size());
+    upload_kv_seq();
+  }
+
+  void upload_kv_seq() {
+    std::vector<KvSeq> v(kv.size());
+    for (size_t i = 0; i < kv.size(); ++i)
+      v[i] = KvSeq{kv[i].kc, kv[i].vc, kv[i].ks, kv[i].vs, kv[i].ring ? ring_pos_dev : nullptr, kv[i].slots};
+    if (v.empty()) return;
+    XTG_CUDA(cudaMemcpyAsync(kv_seq_dev, v.data(), v.size() * sizeof(KvSeq), cudaMemcpyHostToDevice, stream));
+    XTG_CUDA(cudaStreamSynchronize(stream));
   }
 
   // ---- the step ----
@@ -917,6 +937,7 @@ struct xtg_cuda {
     ea.xb_pre = xb_pre;
     ea.inv_freq = inv_freq;
     ea.n_thetas = 2;
+    ea.rope_half = c.head_dim / 2;
     ea.rope_cos = rope_cos;
     ea.rope_sin = rope_sin;
     ea.ring_pos = ring_pos_dev;
@@ -978,7 +999,34 @@ struct xtg_cuda {
         return;
       }
       const KvInst& K = kv[E.cache];
-      {
+      if (c.head_dim != 128) {
+        // a head spans two 128-row tiles: the projection's outputs, then RoPE, the norms and the KV store per head
+        gemv(E.qkvg, kEpiStore, gemv_args(E.qkvg), xb, xb_pre, pdl);
+        QkvPrepArgs qa = {};
+        qa.params = params_dev;
+        qa.nseq = 1;
+        qa.proj = proj;
+        qa.proj_ld = proj_ld;
+        qa.ksplit = 1;
+        qa.heads = c.heads;
+        qa.kv_heads = c.kv_heads;
+        qa.rope_cos = rope_cos;
+        qa.rope_sin = rope_sin;
+        qa.theta = E.theta;
+        qa.qscale = E.qscale;
+        qa.q_out = q_prep;
+        qa.k_out = k_new;
+        qa.v_out = v_new;
+        qa.seqs = kv_seq_dev + E.cache;
+        qa.ring = K.ring ? 1 : 0;
+        qa.dtype = c.kv_dtype;
+        qa.err = dev_err;
+        qa.pdl = pdl ? 1 : 0;
+        qa.head_dim = c.head_dim;
+        mark(kClsSmall, true);
+        launch_qkv_prep(qa, stream);
+        mark(kClsSmall, false);
+      } else {
         GemvArgs g = gemv_args(E.qkvg);
         g.q_tiles = c.heads;
         g.kv_tiles = c.kv_heads;
@@ -999,6 +1047,7 @@ struct xtg_cuda {
         gemv(E.qkvg, kEpiQkv, g, xb, xb_pre, pdl);
       }
       AttnArgs at = {};
+      at.head_dim = c.head_dim;
       at.q = q_prep;
       at.k = k_new;
       at.v = v_new;
@@ -1034,6 +1083,7 @@ struct xtg_cuda {
       CombineArgs cb = {};
       cb.part = part;
       cb.err = dev_err;
+      cb.head_dim = c.head_dim;
       if (peer) {
         cb.x = xchg;
         cb.x.g = glob++;
@@ -1264,10 +1314,10 @@ struct xtg_cuda {
     Snap& s = snaps[slot];
     if (s.rings.empty())
       for (const KvInst& k : kv)
-        if (k.ring) s.rings.push_back(alloc_kv(c.kv_heads, k.slots, true, stream));
+        if (k.ring) s.rings.push_back(alloc_kv(c.kv_heads, c.head_dim, k.slots, true, stream));
     size_t i = 0;
     for (const KvInst& k : kv)
-      if (k.ring) copy_kv(k, s.rings[i++], c.kv_heads, k.slots, stream);
+      if (k.ring) copy_kv(k, s.rings[i++], c.kv_heads, c.head_dim, k.slots, stream);
     XTG_CUDA(cudaStreamSynchronize(stream));
     s.ring_pos = ring_pos;
     s.pos = n_past;
@@ -1278,7 +1328,7 @@ struct xtg_cuda {
     Snap& s = snaps[slot];
     size_t i = 0;
     for (KvInst& k : kv)
-      if (k.ring) copy_kv(s.rings[i++], k, c.kv_heads, k.slots, stream);
+      if (k.ring) copy_kv(s.rings[i++], k, c.kv_heads, c.head_dim, k.slots, stream);
     ring_pos = s.ring_pos;
     upload_ring_pos();
     n_past = s.pos;
@@ -1300,8 +1350,8 @@ struct xtg_cuda {
     try {
       for (const KvInst& k : kv) {
         if (k.ring) continue;
-        next.push_back(alloc_kv(c.kv_heads, ctx, false, stream));
-        copy_kv(k, next.back(), c.kv_heads, n_past, stream);
+        next.push_back(alloc_kv(c.kv_heads, c.head_dim, ctx, false, stream));
+        copy_kv(k, next.back(), c.kv_heads, c.head_dim, n_past, stream);
       }
       XTG_CUDA(cudaStreamSynchronize(stream));
     } catch (...) {
@@ -1318,6 +1368,7 @@ struct xtg_cuda {
       k = next[i++];
     }
     c.context = ctx;
+    upload_kv_seq();
     ++generation;
     for (Snap& s : snaps)   // a smaller tier drops what it cannot hold
       if (s.pos > ctx) s.pos = -1;
@@ -1332,8 +1383,8 @@ struct xtg_cuda {
     for (size_t i = 0; i < kv.size(); ++i) {
       KvInst& k = kv[i];
       const int64_t filled = k.ring ? std::min<int64_t>(n, k.slots) : n;
-      kv_prefill(c.seed, 500000 + 8 * (uint64_t)i, c.kvs_lo, c.kvs_hi, filled, c.kv_heads, k.slots, k.kc, k.vc, k.ks,
-                 k.vs, stream);
+      kv_prefill(c.seed, 500000 + 8 * (uint64_t)i, c.kvs_lo, c.kvs_hi, filled, c.kv_heads, c.head_dim, k.slots, k.kc,
+                 k.vc, k.ks, k.vs, stream);
     }
     for (int r = 0; r < c.ring; ++r) {
       int64_t p = -1;
@@ -1350,7 +1401,7 @@ struct xtg_cuda {
 
   int64_t kv_bytes() const {
     int64_t b = 0;
-    for (const KvInst& k : kv) b += (int64_t)c.kv_heads * k.slots * (2 * 128 + 8);
+    for (const KvInst& k : kv) b += (int64_t)c.kv_heads * k.slots * (2 * c.head_dim + 8);
     return b;
   }
 
@@ -1364,7 +1415,7 @@ struct xtg_cuda {
       } else {
         gemv += E.qkvg.alg_bytes + act(E.qkvg) + E.o.alg_bytes + act(E.o);
         const int64_t keys = E.kind == 1 ? c.ring : n_past;
-        attn += keys * c.kv_heads * (2 * 128 + 8) + (int64_t)m * Q * 4 * 2;
+        attn += keys * c.kv_heads * (2 * c.head_dim + 8) + (int64_t)m * Q * 4 * 2;
       }
     }
     gemv += head.alg_bytes + act(head);
@@ -1769,7 +1820,8 @@ BatchStep* batch_for(const std::vector<xtg_cuda*>& key) {
 // chunk is at most the slack (64 for the 1088-slot ring over a window of 1024).
 int prefill_rows(const xtg_cuda* h) {
   const Config& c = h->c;
-  if (!c.batch || !c.graph || c.kv_world != 1 || h->head_w_bf16) return 0;   // the batched step's head is NVFP4
+  // the batched step's head is NVFP4 and its attention path head dim 128
+  if (!c.batch || !c.graph || c.kv_world != 1 || h->head_w_bf16 || c.head_dim != 128) return 0;
   const int slack = c.ring - c.window;
   return std::min(kMaxBatch * kMaxRows, slack / kMaxRows * kMaxRows);
 }
@@ -1819,7 +1871,8 @@ bool batchable(xtg_cuda* const* hs, int nh) {
   if (nh < 2) return false;
   for (int i = 0; i < nh; ++i) {
     const Config& c = hs[i]->c;
-    if (!c.batch || !c.graph || c.kv_world != 1 || hs[i]->head_w_bf16 || hs[i]->wmem != hs[0]->wmem ||
+    if (!c.batch || !c.graph || c.kv_world != 1 || hs[i]->head_w_bf16 || c.head_dim != 128 ||
+        hs[i]->wmem != hs[0]->wmem ||
         c.device != hs[0]->c.device ||
         c.kv_dtype != hs[0]->c.kv_dtype || c.decode_rows != hs[0]->c.decode_rows)
       return false;
@@ -2119,7 +2172,8 @@ int64_t xtg_cuda_debug_cache(xtg_cuda* h, int instance, int value, void* out, in
   if (instance < 0 || instance >= (int)h->kv.size() || value < 0 || value > 3) return -1;
   const KvInst& k = h->kv[instance];
   const int kvh = h->c.kv_heads;
-  const int64_t codes = (int64_t)kvh * k.slots * 128, scales = (int64_t)kvh * k.slots * 4;
+  const int hd = h->c.head_dim;
+  const int64_t codes = (int64_t)kvh * k.slots * hd, scales = (int64_t)kvh * k.slots * 4;
   const int64_t bytes = value < 2 ? codes : scales;
   if (!out || len < bytes) return bytes;
   try {
@@ -2134,11 +2188,11 @@ int64_t xtg_cuda_debug_cache(xtg_cuda* h, int instance, int value, void* out, in
     // this library's layouts (attention.h) -> K [h][d][slot], V [h][slot][d]
     for (int hh = 0; hh < kvh; ++hh)
       for (int64_t s = 0; s < k.slots; ++s)
-        for (int d = 0; d < 128; ++d) {
+        for (int d = 0; d < hd; ++d) {
           if (value == 0)
-            o[((int64_t)hh * 128 + d) * k.slots + s] = tmp[k_offset(hh, s, d, k.slots)];
+            o[((int64_t)hh * hd + d) * k.slots + s] = tmp[k_offset(hh, s, d, k.slots, hd)];
           else
-            o[((int64_t)hh * k.slots + s) * 128 + d] = tmp[v_offset(hh, d, s, k.slots)];
+            o[((int64_t)hh * k.slots + s) * hd + d] = tmp[v_offset(hh, d, s, k.slots, hd)];
         }
   } catch (const std::exception&) {
     return -1;
