@@ -27,11 +27,12 @@ typedef struct xtg_cuda xtg_cuda;
 // row: index in this call's tokens; logits: vocab floats, valid during the callback (npu/xtg_npu.h:16-17)
 typedef void (*xtg_cuda_logits_fn)(int row, const float* logits, void* user);
 
-// Open a session (replaces xtg_npu_open, npu/xtg_npu.h:19-23). model_path: "synthetic" builds the seeded synthetic
-// Dory of options "model" on the device (no checkpoint); anything else is rejected for now. options: JSON, may be
-// empty: "model" {hidden, ffn, heads, kv_heads, head_dim (128), vocab, n_in, n_rec, n_out, loops, window, ring,
-// global_every, theta_sliding, theta_global, weight_std, lr_lo, lr_hi, qs_lo, qs_hi, gs_lo, gs_hi, suv_lo, suv_hi,
-// ls_lo, ls_hi, kvs_lo, kvs_hi, seed}; "context" (tier, default 8192); "kv_dtype" ("int8" | "fp8", default int8);
+// Open a session (replaces xtg_npu_open, npu/xtg_npu.h:19-23). model_path: a Dory checkpoint directory (config.json +
+// model.safetensors, ModelOpt W4A16_NVFP4), or "synthetic": the seeded synthetic Dory of options "model", built on
+// the device. options: JSON, may be empty: "model" {hidden, ffn, heads, kv_heads, head_dim (128 | 256), vocab, n_in,
+// n_rec, n_out, loops, window, ring, global_every, theta_sliding, theta_global, weight_std, lr_lo, lr_hi, qs_lo,
+// qs_hi, gs_lo, gs_hi, suv_lo, suv_hi, ls_lo, ls_hi, kvs_lo, kvs_hi, seed} (synthetic only); "context" (tier,
+// default 8192); "kv_dtype" ("int8" | "fp8", default int8);
 // "snapshots" (ring snapshots kept, default 2); "decode_rows" (rows per step, 1..8, default 8); "device" (CUDA
 // device, default 0); "graph" (1: replay the step as a CUDA graph, default 1); "pdl" (1: programmatic dependent
 // launches, default 1). NULL on failure, the reason in err.
@@ -178,19 +179,20 @@ XTG_CUDA_API int xtg_cuda_quantize_nvfp4(const uint16_t* w_bf16, int n_out, int 
 
 // attention(pool, AttnArgs) (engine/include/xtg/kv.h:64-79, engine/src/kv.cpp:166-286) over a device KV cache in this
 // library's layout (slots a multiple of 64; 16-byte aligned buffers):
-//   K codes [kv_heads][slots][128]: the 16-byte unit u of slot s's row lies at unit u ^ ((s % 64) ^ (s % 64 >> 3)) & 7;
-//   V codes [kv_heads][slots / 64][128][64]: per 64-slot chunk, head dim d's row of 64 slots, its 16-byte unit u at
+//   K codes [kv_heads][slots][D]: each 128-dim half of slot s's row as 8 16-byte units, unit u of the half at unit
+//     u ^ ((s % 64) ^ (s % 64 >> 3)) & 7;
+//   V codes [kv_heads][slots / 64][D][64]: per 64-slot chunk, head dim d's row of 64 slots, its 16-byte unit u at
 //     unit u ^ ((d >> 1) & 3);
 //   scales f32 [kv_heads][slots].
-// ring != 0: slot s holds position ring_pos[s] (int32, -1 empty), else slot = position. head_dim 128, at most 4 q
-// heads per KV head, n_q <= 8.
+// ring != 0: slot s holds position ring_pos[s] (int32, -1 empty), else slot = position. head_dim D 128 or 256, at
+// most 4 q heads per KV head, n_q <= 8.
 typedef struct {
   int n_q;
   int64_t pos0;
   int heads, kv_heads, head_dim, window;
   float scale;
-  const float* q;           // [n_q][heads][128]
-  const float* k;           // [n_q][kv_heads][128] this call's keys
+  const float* q;           // [n_q][heads][head_dim]
+  const float* k;           // [n_q][kv_heads][head_dim] this call's keys
   const float* v;
   const uint8_t* k_codes;
   const uint8_t* v_codes;
@@ -200,7 +202,7 @@ typedef struct {
   int ring;
   const int32_t* ring_pos;
   int dtype;                // 0 int8, 1 FP8 E4M3
-  float* out;               // [n_q][heads][128]
+  float* out;               // [n_q][heads][head_dim]
 } xtg_cuda_attn_args;
 XTG_CUDA_API int xtg_cuda_attention(const xtg_cuda_attn_args* a, int splits, void* stream, char* err, int err_len);
 
@@ -215,8 +217,9 @@ XTG_CUDA_API int xtg_cuda_attention(const xtg_cuda_attn_args* a, int splits, voi
 XTG_CUDA_API int xtg_cuda_attention_noalloc(const xtg_cuda_attn_args* a, int splits, void* stream, char* err,
                                             int err_len);
 
-// KvCache::store (engine/src/kv.cpp:75-112) into the layout above: rows k, v [n][kv_heads][128] (device f32) at positions
-// pos .. pos + n - 1; a ring keeps the last `slots`. int8: scale amax / 127; FP8: amax / 448 (the reference's rule).
+// KvCache::store (engine/src/kv.cpp:75-112) into the layout above at head_dim 128: rows k, v [n][kv_heads][128]
+// (device f32) at positions pos .. pos + n - 1; a ring keeps the last `slots`. int8: scale amax / 127; FP8: amax / 448
+// (the reference's rule).
 XTG_CUDA_API int xtg_cuda_kv_store(const float* k, const float* v, int64_t pos, int n, int kv_heads, int64_t slots, int ring,
                       int dtype, uint8_t* k_codes, uint8_t* v_codes, float* k_scales, float* v_scales, void* stream,
                       char* err, int err_len);
