@@ -732,6 +732,32 @@ def prefill_block(x, local_rank, n_tokens=4096, reps=3):
     return out
 
 
+def dory4b_block(x, local_rank, steps, warmup):
+    """The real Dory 4B's shape (hidden 2560, 16 q / 4 KV heads of 256, FFN 7168, vocab 131072, 16 + 40 x 2 + 16
+    sublayers; synthetic weights): the 8-row verify step at the 8K tier over 8184 prefilled positions, graph replays
+    timed with CUDA events as the headline step is, with its own step roofline."""
+    s = x.Session(dict(x.DORY_4B), context=8192, device=local_rank)
+    try:
+        s.prefill_synthetic(PREFILL)
+        s.bench(TOKENS, max(1, warmup))
+        ms, _, _ = s.bench(TOKENS, steps)
+        pms, cms, cl = s.bench(TOKENS, 3, profile=True)
+        step_bytes = s.step_bytes(0, 8)
+        gemv_bytes = s.step_bytes(1, 8)
+        peak, peak_kind = peaks()
+        return {"ms_per_step": ms, "rows_per_s": 8.0 / (ms / 1e3), "rates": rates(1, ms),
+                "launches_per_step": int(sum(cl)),
+                "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (ms / 1e3) / 1e9,
+                                  "frac": step_bytes / (ms / 1e3) / 1e9 / peak, "peak": peak, "peak_kind": peak_kind},
+                "gemv_roofline": {"achieved_gbs": gemv_bytes / (cms[0] / 1e3) / 1e9,
+                                  "frac": gemv_bytes / (cms[0] / 1e3) / 1e9 / peak},
+                "kernel_ms_per_step": {"gemv": cms[0], "attention": cms[1], "combine": cms[2], "small": cms[3],
+                                       "eager_total": pms},
+                "splits_global": s.info().get("splits_global")}
+    finally:
+        s.close()
+
+
 def job_rows_per_s(world, ms_per_step):
     """Whole-job throughput: every rank verifies 8 rows of its own sequence per step (weak scaling)."""
     return world * 8.0 / (ms_per_step / 1e3)
@@ -800,6 +826,7 @@ def run_ours(args, rank, world, local_rank, dist):
     cfg0 = config0_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     cfg2 = config2_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
     heads = head_block(x, f"cuda:{local_rank}") if (world == 1 and not args.no_gemm) else None
+    d4b = dory4b_block(x, local_rank, args.steps, args.warmup) if world == 1 else None
     # the batch-1 split over GPUs: measured where its 2-GPU tests run (--split-kv-max raises the bound)
     skv = (split_kv_block(x, rank, world, local_rank, dist, args.steps, args.warmup)
            if 1 < world <= args.split_kv_max else None)
@@ -853,6 +880,10 @@ def run_ours(args, rank, world, local_rank, dist):
         line["lm_head"] = {"config": "lm_head at vocab 131072 x 3072, 8 rows: NVFP4 on the GEMV (the synthetic model's "
                                      "head) and a checkpoint's BF16 head (head.cu, mma.sync over bf16 hi + lo rows)",
                            **heads}
+    if d4b:
+        line["dory4b"] = {"config": "the real Dory 4B shape (hidden 2560, 16 q / 4 KV heads of head_dim 256, FFN 7168, "
+                                    "vocab 131072, 16 + 40 x 2 + 16 sublayers) with synthetic weights, 8K tier, "
+                                    "8184 prefilled, 8-row verify step, graph replays", **d4b}
     if skv:
         line["batch1_split_kv"] = {"config": "batch-1 verify step (8 rows) at 32K context, the global caches' chunks "
                                              "split over the GPUs, partials exchanged over NVLink inside the combine "

@@ -101,12 +101,13 @@ def test_checkpoint_bf16_head_keeps_verify_steps(cuda, xtg, ckpt):
 @pytest.mark.parametrize("head", ["bf16", "nvfp4"])
 def test_checkpoint_head_dim_256(cuda, xtg, tmp_path, head):
     """A head_dim-256 checkpoint (the real Dory 4B's head shape, GQA 4): verify steps against the oracle's checkpoint
-    model and the reference's own Dory pack; prompts run as 8-row steps (the batched path takes head_dim 128)."""
+    model and the reference's own Dory pack; with the NVFP4 head the 20-token prompt runs as a 64-row chunk of the
+    batched step, with the BF16 head as 8-row steps."""
     cfg, tensors = dory_ckpt.write_checkpoint(str(tmp_path), dory_ckpt.small_config(head_dim=256), seed=4)
     ora = O.CheckpointDory(cfg, tensors, ctx=1024, n_prefill=0, head=head, kv_dtype=O.KV_FP8)
     ref = O.RefDory(str(tmp_path), kv_dtype="fp8", context=1024) if O.ref() is not None else None
     with xtg.Session(path=str(tmp_path), context=1024, kv_dtype="fp8", head=head) as s:
-        assert s.info()["prefill_ar"] == 8
+        assert s.info()["prefill_ar"] == (64 if head == "nvfp4" else 8)
         for toks in STEPS + [[(11 * i + 5) % 4096 for i in range(20)]]:
             got = rows(s.forward(toks, want=2), len(toks))
             want = np.concatenate([ora.step(toks[i:i + 8]) for i in range(0, len(toks), 8)])

@@ -324,12 +324,14 @@ def test_forward_batch_matches_one_by_one(cuda, xtg, cfg):
                 s.close()
 
 
-def test_forward_batch_batched_step(cuda, xtg, cfg):
+@pytest.mark.parametrize("hd", [128, 256])
+def test_forward_batch_batched_step(cuda, xtg, cfg, hd):
     """xtg_cuda_forward_batch over sessions that share one weight set runs them as one batched step (every projection
     one tcgen05 GEMM over all their rows): nine sessions (a group of 8 and a group of 1) at different positions, with
     different token counts (one of two rounds, one of none), each within the step tolerance of a forward of its own
     (identical argmax), the first also against the oracle; positions advance, and a second call after rewinds gives
-    the same logits again."""
+    the same logits again. At head_dim 128 and 256 (the real Dory 4B's)."""
+    cfg = dict(cfg, head_dim=hd)
     lists = [[5, 17, 900, 3, 44, 1023, 0, 256], [8, 9, 10], list(range(100, 111)), [], [4095], [1, 2, 3, 4],
              [700] * 8, [9, 8, 7, 6, 5], [11, 12]]
     pre = [70, 90, 64, 100, 75, 128, 81, 99, 70]
@@ -367,12 +369,15 @@ def test_forward_batch_batched_step(cuda, xtg, cfg):
                 s.close()
 
 
-def test_prompt_chunks_match_oracle_and_verify_steps(cuda, xtg, cfg):
+@pytest.mark.parametrize("hd", [128, 256])
+def test_prompt_chunks_match_oracle_and_verify_steps(cuda, xtg, cfg, hd):
     """A forward of more than decode_rows tokens runs prompt chunks of up to 64 rows through the batched step: 8-row
     groups of the session, group g attending the cache up to its own first row (the earlier groups' keys among them,
     stored by the same step) and its own rows as this call's keys -- the arithmetic of 8-row verify steps. 100 tokens (a
     chunk of 64, one of 36) within the step tolerance of the oracle stepped 8 rows at a time (identical argmax), and of
-    the same tokens in the session's 8-row verify steps (batch=0); the position and the next verify step agree too."""
+    the same tokens in the session's 8-row verify steps (batch=0); the position and the next verify step agree too.
+    At head_dim 128 and 256."""
+    cfg = dict(cfg, head_dim=hd)
     toks = [(37 * i + 11) % cfg["vocab"] for i in range(100)]
     ref = O.SynthDory(cfg, ctx=512, n_prefill=70)
     want = np.concatenate([ref.step(toks[o:o + 8]) for o in range(0, 100, 8)])

@@ -722,8 +722,7 @@ void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
   a.pdl = pdl ? 1 : 0;
   if (a.head_dim == 0) a.head_dim = 128;
   XTG_REQUIRE(a.head_dim == 128 || a.head_dim == 256, "combine: head_dim 128 or 256");
-  XTG_REQUIRE(a.head_dim == 128 || (a.x.world <= 1 && !a.gated_out),
-              "combine: head_dim 256 in one process and the 8-row step (no split-KV exchange, no batched step)");
+  XTG_REQUIRE(a.head_dim == 128 || a.x.world <= 1, "combine: head_dim 256 in one process (no split-KV exchange)");
   XTG_REQUIRE(a.splits >= 1 && a.splits <= kMaxSplits, "combine: 1..256 splits");
   XTG_REQUIRE(a.kv_heads >= 1 && a.heads >= 1 && a.heads % a.kv_heads == 0, "combine: q heads a multiple of KV heads");
   XTG_REQUIRE(a.x.world <= 1 || (a.x.world <= kMaxKvWorld && a.x.rank >= 0 && a.x.rank < a.x.world && a.x.epoch &&
@@ -740,7 +739,7 @@ void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (a.gated_out && a.splits <= kWarpSplits && a.x.world <= 1) {   // the batched step: a warp per pair
+  if (a.gated_out && a.splits <= kWarpSplits && a.x.world <= 1 && a.head_dim == 128) {   // batched: a warp per pair
     // as many warps per CTA as keep one CTA per SM or more
     const int pairs = a.nseq * kMaxRows * a.heads;
     int dev = 0, sms = 0;

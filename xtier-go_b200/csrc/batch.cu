@@ -83,12 +83,13 @@ __global__ void embed_batch_kernel(const EmbedBatchArgs a) {
     if (g < groups) store_gemm_digits_quad(a.act, r, g, t, code, sf);
   }
   // this row's RoPE factors for both thetas (FP32(pos) * inv_freq, then cos / sin)
-  for (int e = threadIdx.x; e < 2 * 64; e += blockDim.x) {
-    const int th = e >> 6, f = e & 63;
-    const float ang = __fmul_rn((float)(pos0 + i), a.inv_freq[th * 64 + f]);
+  const int half = a.rope_half > 0 ? a.rope_half : 64;
+  for (int e = threadIdx.x; e < 2 * half; e += blockDim.x) {
+    const int th = e / half, f = e % half;
+    const float ang = __fmul_rn((float)(pos0 + i), a.inv_freq[th * half + f]);
     float sn, c;
     sincosf(ang, &sn, &c);
-    const int64_t at = (((int64_t)s * 2 + th) * kMaxRows + i) * 64 + f;
+    const int64_t at = (((int64_t)s * 2 + th) * kMaxRows + i) * half + f;
     a.rope_cos[at] = c;
     a.rope_sin[at] = sn;
   }

@@ -32,8 +32,9 @@ struct EmbedBatchArgs {
   const uint16_t* table;      // or a BF16 embedding table [vocab][hidden] (a checkpoint's)
   int hidden;
   float* h;                   // [8 nseq][hidden]
-  const float* inv_freq;      // [2][64]
-  float* rope_cos;            // [nseq][2][8][64]
+  const float* inv_freq;      // [2][half]
+  int rope_half;              // half the head dim: 64 (0 reads as 64) or 128
+  float* rope_cos;            // [nseq][2][8][half]
   float* rope_sin;
   int32_t* const* ring_pos;   // [nseq] each sequence's table (null entries: no sliding layers)
   int64_t ring;

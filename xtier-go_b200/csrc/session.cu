@@ -1529,18 +1529,18 @@ struct BatchStep {
     asum = alloc<float>((size_t)c.heads * R);
     gu = alloc<float>((size_t)ks_gu * R * 2 * F);
     logits = alloc<float>((size_t)R * c.vocab);
-    rope_cos = alloc<float>((size_t)S * 2 * kMaxRows * 64);
-    rope_sin = alloc<float>((size_t)S * 2 * kMaxRows * 64);
+    rope_cos = alloc<float>((size_t)S * 2 * kMaxRows * (c.head_dim / 2));
+    rope_sin = alloc<float>((size_t)S * 2 * kMaxRows * (c.head_dim / 2));
     act = alloc<uint8_t>((size_t)gemm_act_bytes(R, std::max(std::max(H, F), Q)));
     act_post = alloc<float>(R);
     argmax = alloc<int32_t>(R);
     dev_err = alloc<int>(1);
     XTG_CUDA(cudaMallocHost(&err_host, sizeof(int)));
     *err_host = 0;
-    // one wave of attention CTAs (2 per SM) over every sequence's KV heads
-    splits_g = std::max(1, std::min(256, 2 * sms / (c.kv_heads * S)));
+    // one wave of attention CTAs (2 per SM, 1 at head dim 256) over every sequence's KV heads
+    splits_g = std::max(1, std::min(256, attention_ctas_per_sm(c.head_dim) * sms / (c.kv_heads * S)));
     splits_r = std::max(1, std::min(splits_g, (int)(c.ring / 64)));
-    part = alloc<float>((size_t)S * attention_part_floats(c.kv_heads, std::max(splits_g, splits_r)));
+    part = alloc<float>((size_t)S * attention_part_floats(c.kv_heads, std::max(splits_g, splits_r), c.head_dim));
     std::vector<int32_t*> rt;
     for (xtg_cuda* q : seqs) rt.push_back(q->ring_pos_dev);
     ring_tab = upload(rt);
@@ -1595,6 +1595,7 @@ struct BatchStep {
     ea.hidden = H;
     ea.h = h;
     ea.inv_freq = model->inv_freq;
+    ea.rope_half = c.head_dim / 2;
     ea.rope_cos = rope_cos;
     ea.rope_sin = rope_sin;
     ea.ring_pos = ring_tab;
@@ -1678,6 +1679,7 @@ struct BatchStep {
       qa.dtype = c.kv_dtype;
       qa.err = dev_err;
       qa.pdl = pdl;
+      qa.head_dim = c.head_dim;
       launch_qkv_prep(qa, stream);
       const bool ring = E.kind == 1;
       AttnArgs at = {};
@@ -1697,9 +1699,10 @@ struct BatchStep {
       at.err = dev_err;
       at.seqs = kvseq + (size_t)E.cache * S;
       at.nseq = S;
-      at.late_copies = distinct ? 0 : 1;
-      at.l2_first = (!ring && c.l2_first) ? 1 : 0;   // a prompt chunk: the earlier groups' keys come from qkv_prep just before
-      at.part_seq_stride = attention_part_floats(c.kv_heads, std::max(splits_g, splits_r));
+      at.late_copies = distinct ? 0 : 1;   // a prompt chunk: the earlier groups' keys come from qkv_prep just before
+      at.l2_first = (!ring && c.l2_first) ? 1 : 0;
+      at.part_seq_stride = attention_part_floats(c.kv_heads, std::max(splits_g, splits_r), c.head_dim);
+      at.head_dim = c.head_dim;
       launch_attention(at, stream, pdl);
       CombineArgs cb = {};
       cb.part = part;
@@ -1721,6 +1724,7 @@ struct BatchStep {
       cb.nseq = S;
       cb.part_seq_stride = at.part_seq_stride;
       cb.err = dev_err;
+      cb.head_dim = c.head_dim;
       launch_attn_combine(cb, stream, pdl);
       gemm_digitize(att, M, Q, act, act_post, stream, asum, c.heads, kRows, pdl);
       gemm(E.o, outs_b[ei], ks_o, (int64_t)kRows * H, pdl);
@@ -1820,8 +1824,7 @@ BatchStep* batch_for(const std::vector<xtg_cuda*>& key) {
 // chunk is at most the slack (64 for the 1088-slot ring over a window of 1024).
 int prefill_rows(const xtg_cuda* h) {
   const Config& c = h->c;
-  // the batched step's head is NVFP4 and its attention path head dim 128
-  if (!c.batch || !c.graph || c.kv_world != 1 || h->head_w_bf16 || c.head_dim != 128) return 0;
+  if (!c.batch || !c.graph || c.kv_world != 1 || h->head_w_bf16) return 0;   // the batched step's head is NVFP4
   const int slack = c.ring - c.window;
   return std::min(kMaxBatch * kMaxRows, slack / kMaxRows * kMaxRows);
 }
@@ -1871,8 +1874,7 @@ bool batchable(xtg_cuda* const* hs, int nh) {
   if (nh < 2) return false;
   for (int i = 0; i < nh; ++i) {
     const Config& c = hs[i]->c;
-    if (!c.batch || !c.graph || c.kv_world != 1 || hs[i]->head_w_bf16 || c.head_dim != 128 ||
-        hs[i]->wmem != hs[0]->wmem ||
+    if (!c.batch || !c.graph || c.kv_world != 1 || hs[i]->head_w_bf16 || hs[i]->wmem != hs[0]->wmem ||
         c.device != hs[0]->c.device ||
         c.kv_dtype != hs[0]->c.kv_dtype || c.decode_rows != hs[0]->c.decode_rows)
       return false;
