@@ -76,3 +76,24 @@ def test_attention_rejects_no_kv_heads_before_any_device_work(xtg, entry, kv_hea
     err = C.create_string_buffer(512)
     rc = getattr(xtg.lib(), entry)(C.byref(a), 4, None, err, len(err))
     assert rc == -1 and b"KV head" in err.value, err.value
+
+
+@pytest.mark.parametrize("options,needle", [
+    (b'{"model": {"head_dim": 64}}', b"head_dim must be 128 or 256"),
+    (b'{"model": {"head_dim": 256}, "kv_world": 2, "kv_rank": 0, "nccl_id": "' + b"0" * 256 + b'"}',
+     b"takes head_dim 128"),
+])
+def test_open_checks_head_dim_before_any_device_work(xtg, options, needle):
+    """head_dim 128 or 256 (the real Dory 4B's); split-KV across GPUs at 128 only: refused from the options alone."""
+    err = C.create_string_buffer(512)
+    assert not xtg.lib().xtg_cuda_open(b"synthetic", options, err, len(err))
+    assert needle in err.value, err.value
+
+
+@pytest.mark.parametrize("entry", ["xtg_cuda_attention", "xtg_cuda_attention_noalloc"])
+def test_attention_rejects_other_head_dims_before_any_device_work(xtg, entry):
+    good = 4096
+    a = xtg.AttnArgs(8, 100, 16, 4, 192, 0, 0.1, good, good, good, good, good, good, good, 128, 0, None, 0, good)
+    err = C.create_string_buffer(512)
+    rc = getattr(xtg.lib(), entry)(C.byref(a), 4, None, err, len(err))
+    assert rc == -1 and b"head_dim 128 or 256" in err.value, err.value
