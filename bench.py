@@ -939,7 +939,26 @@ def main():
                     help="profiling driver: this many batched rounds of 8 sequences (8K tier), then exit")
     ap.add_argument("--ncu-head", type=int, default=0,
                     help="profiling driver: the BF16 lm_head (vocab 131072 x 3072, 8 rows) this many times, then exit")
+    ap.add_argument("--ncu-attn", type=int, default=0,
+                    help="profiling driver: config-2 global attention (int8 KV, L = 32768, 49 splits) this many "
+                         "times, then exit")
     args = ap.parse_args()
+    if args.ncu_attn:
+        import torch
+        x = package()
+        g = torch.Generator(device="cuda").manual_seed(2)
+        kvh, heads, slots = 6, 24, 32768
+        q, k, v = (torch.nn.functional.normalize(torch.randn(8, h, 128, device="cuda", generator=g), dim=-1)
+                   for h in (heads, kvh, kvh))
+        kc = torch.randint(-127, 128, (kvh * slots * 128,), dtype=torch.int8, device="cuda", generator=g)
+        vc = torch.randint(-127, 128, (kvh * slots * 128,), dtype=torch.int8, device="cuda", generator=g)
+        ks = torch.rand(kvh, slots, device="cuda", generator=g) * 0.015 + 0.005
+        vs = torch.rand(kvh, slots, device="cuda", generator=g) * 0.015 + 0.005
+        for _ in range(args.ncu_attn):
+            x.attention(q, k, v, kc.view(torch.uint8), vc.view(torch.uint8), ks, vs, slots - 8, 0,
+                        1.0 / 128 ** 0.5 * 8, splits=49)
+        torch.cuda.synchronize()
+        return
     if args.ncu_gemm:
         import torch
         x = package()

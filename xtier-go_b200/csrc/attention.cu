@@ -14,12 +14,16 @@
 // warp w takes query rows 16 (w & 1) .. +15 -- a query row is (activation row, q head of this KV head), 8 x 4 = 32
 // rows, so the 4 q heads sharing a KV head read it once -- and the chunk's keys 16 (w >> 1) .. +15, so that a chunk
 // costs each warp a quarter of its products and the chunks stream through a 4-stage ring. Each warp keeps its own
-// online-softmax state over its keys; the 4 key quarters merge at the end. Both products run on mma.m16n8k16: int8
-// codes become f16 exactly (1152 + b as a half, less 1152), FP8 codes by cvt.rn.f16x2.e4m3x2; Q (after RoPE,
-// justnorm, q scale) is split once into fp16 hi + lo; scores are scaled per key by its K scale in FP32, probabilities
-// times the key's V scale are the fp16 A operand of PV. Two permutations make every load contiguous: the head
-// dimension inside a k16 step (lane tq reads 32 contiguous bytes of a K row, Q's fragments use the same order) and
-// the keys inside a warp's quarter (lane tq owns keys 4 tq .. 4 tq + 3 in both products).
+// online-softmax state over its keys; the 4 key quarters merge at the end.
+// QK^T over an int8 cache runs on mma.m16n8k32.s8 straight from the cached codes: Q (after RoPE, justnorm, q scale)
+// becomes two signed 8-bit digits per element against its row's max |q| (q = max / 127 * (hi + lo / 254), ~16
+// bits), the two integer products are exact and combine as 254 hi + lo before one conversion to FP32. Over an FP8
+// cache both digits are fp16 (q = hi + lo, ~22 bits) and the codes become f16 (cvt.rn.f16x2.e4m3x2) for
+// mma.m16n8k16. Scores are scaled per key by its K scale in FP32. PV runs on mma.m16n8k16: probabilities times the
+// key's V scale are the fp16 A operand, int8 codes become f16 exactly (1152 + b as a half, less 1152). Two
+// permutations make every load contiguous: the head dimension inside a k step (lane tq reads 32 contiguous bytes of
+// a K row, Q's fragments use the same order) and the keys inside a warp's quarter (lane tq owns keys 4 tq .. 4 tq + 3
+// in both products).
 #include <algorithm>
 
 #include "attention.h"
@@ -64,7 +68,11 @@ template <int D>
 struct Smem {
   Stage<D> stage[kStages];        // the chunk ring; after the last chunk, key quarter j's softmax state in stage[j]
   uint64_t full[kStages], empty[kStages];
-  uint4 qf[2][2][D / 16][32];     // Q A fragments [m-tile][hi, lo][k16 step][lane]: q = hi + lo, both fp16
+  // Q A fragments. FP8 cache: [m-tile][hi, lo][k16 step][lane], q = hi + lo, both fp16. Int8 cache: the first half
+  // as [m-tile][hi, lo][k32 step][lane] of signed 8-bit digits (qi below).
+  uint4 qf[2][2][D / 16][32];
+  float qmaxp[kQRows][D / 32];    // int8 cache: a query row's max |q| over the 8-dim pieces of one k32 step
+  float qfac[kQRows];             // int8 cache: a query row's digit unit, max |q| / (127 * 254)
 };
 // a key quarter's state after the last chunk: per query row m, l, acc[D] (rows D + 4 floats apart)
 static_assert(sizeof(Stage<128>) >= kQRows * (128 + 4) * sizeof(float), "stage too small for a quarter's state");
@@ -73,7 +81,7 @@ static_assert(kStages >= kQuarters, "the quarters' states live in the stages");
 
 // Head dim 256: the same warp roles over twice the dims (16 k16 steps, 32 n8 tiles of the output); the accumulator
 // takes twice the registers and a stage twice the shared memory, so one CTA fits an SM.
-template <int D>
+template <int D, bool I8>
 __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(const AttnArgs a) {
   static_assert(D == 128 || D == 256, "head dim 128 or 256");
   constexpr int kSteps = D / 16;                          // k16 steps of QK^T
@@ -160,34 +168,109 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
     return i < m ? *reinterpret_cast<const float4*>(aq + ((int64_t)i * a.heads + kvh * group + hg) * D + d0)
                  : make_float4(0.f, 0.f, 0.f, 0.f);
   };
-  constexpr int kFragLoads = 2 * kSteps * 32 / kThreads;   // (m-tile, step, lane) fragments per thread
-  float4 qv[kFragLoads][2];
+  // int8 cache: the digit fragments of k32 step st (4 per 128-dim half), m-tile t2, lane (gg, t): rows gg and gg + 8
+  // of the tile, head dims d0 .. d0 + 3 (registers x: row gg, y: row gg + 8) and d0 + 4 .. d0 + 7 (z, w), where
+  // d0 = 128 (st >> 2) + 32 t + 8 (st & 3) -- the MMA's k index 4 t + i is head dim d0 + i, 16 + 4 t + i is d0 + 4 + i
+  uint4 (*qi)[2][D / 32][32] = reinterpret_cast<uint4 (*)[2][D / 32][32]>(&sm.qf[0][0][0][0]);
+  if constexpr (I8) {
+    constexpr int kSt = D / 32;
+    constexpr int kFrag = 2 * kSt * 32 / kThreads;   // (m-tile, k32 step, lane) fragments per thread
+    float4 qv[kFrag][4];
 #pragma unroll
-  for (int u = 0; u < kFragLoads; ++u) {   // every load first
-    const int idx = (int)threadIdx.x + u * kThreads;
-    const int l = idx & 31, st = (idx >> 5) % kSteps, t2 = idx / (32 * kSteps), gg = l >> 2;
-    const int d0 = 128 * (st >> 3) + 32 * (l & 3) + 4 * (st & 7);
-    qv[u][0] = qrow(16 * t2 + gg, d0);
-    qv[u][1] = qrow(16 * t2 + gg + 8, d0);
-  }
-#pragma unroll
-  for (int u = 0; u < kFragLoads; ++u) {
-    const int idx = (int)threadIdx.x + u * kThreads;
-    const int l = idx & 31, st = (idx >> 5) % kSteps, t2 = idx / (32 * kSteps);
-    const float4 r0 = qv[u][0], r1 = qv[u][1];
-    const float v[8] = {r0.x, r0.y, r1.x, r1.y, r0.z, r0.w, r1.z, r1.w};
-    uint32_t hi[4], lo[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const __half h0 = __float2half_rn(v[2 * j]), h1 = __float2half_rn(v[2 * j + 1]);
-      hi[j] = pack_f16x2(__half2float(h0), __half2float(h1));
-      lo[j] = pack_f16x2(v[2 * j] - __half2float(h0), v[2 * j + 1] - __half2float(h1));
+    for (int u = 0; u < kFrag; ++u) {   // every load first
+      const int idx = (int)threadIdx.x + u * kThreads;
+      const int l = idx & 31, st = (idx >> 5) % kSt, t2 = idx / (32 * kSt), gg = l >> 2;
+      const int d0 = 128 * (st >> 2) + 32 * (l & 3) + 8 * (st & 3);
+      qv[u][0] = qrow(16 * t2 + gg, d0);
+      qv[u][1] = qrow(16 * t2 + gg + 8, d0);
+      qv[u][2] = qrow(16 * t2 + gg, d0 + 4);
+      qv[u][3] = qrow(16 * t2 + gg + 8, d0 + 4);
     }
-    sm.qf[t2][0][st][l] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    sm.qf[t2][1][st][l] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    // each row's max |q|: over the 4 lanes of a row within a fragment, then over the k32 steps through shared memory
+#pragma unroll
+    for (int u = 0; u < kFrag; ++u) {
+      const int idx = (int)threadIdx.x + u * kThreads;
+      const int l = idx & 31, st = (idx >> 5) % kSt, t2 = idx / (32 * kSt), gg = l >> 2;
+      float mx[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const float4 p = qv[u][h], r = qv[u][2 + h];
+        mx[h] = fmaxf(fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))),
+                      fmaxf(fmaxf(fabsf(r.x), fabsf(r.y)), fmaxf(fabsf(r.z), fabsf(r.w))));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+      }
+      if ((l & 3) == 0) {
+        sm.qmaxp[16 * t2 + gg][st] = mx[0];
+        sm.qmaxp[16 * t2 + gg + 8][st] = mx[1];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kFrag; ++u) {
+      const int idx = (int)threadIdx.x + u * kThreads;
+      const int l = idx & 31, st = (idx >> 5) % kSt, t2 = idx / (32 * kSt), gg = l >> 2;
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {   // h: row gg (registers x, z) or gg + 8 (y, w)
+        const int r = 16 * t2 + gg + 8 * h;
+        float M = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < kSt; ++s2) M = fmaxf(M, sm.qmaxp[r][s2]);
+        const float inv = M > 0.f ? 127.f / M : 0.f;
+        if (st == 0 && (l & 3) == 0) sm.qfac[r] = M * (1.f / (127.f * 254.f));
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {   // dims d0 .. + 3 (x / y) and d0 + 4 .. + 7 (z / w)
+          const float4 p = qv[u][h + 2 * half];
+          const float v[4] = {p.x, p.y, p.z, p.w};
+          uint32_t wh = 0, wl = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float x = v[e] * inv, xh = rintf(x);
+            const int dh = (int)xh, dl = (int)rintf((x - xh) * 254.f);   // |dh|, |dl| <= 127
+            wh |= (uint32_t)(dh & 0xff) << (8 * e);
+            wl |= (uint32_t)(dl & 0xff) << (8 * e);
+          }
+          hi[h + 2 * half] = wh;
+          lo[h + 2 * half] = wl;
+        }
+      }
+      qi[t2][0][st][l] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      qi[t2][1][st][l] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+  } else {
+    constexpr int kFragLoads = 2 * kSteps * 32 / kThreads;   // (m-tile, step, lane) fragments per thread
+    float4 qv[kFragLoads][2];
+#pragma unroll
+    for (int u = 0; u < kFragLoads; ++u) {   // every load first
+      const int idx = (int)threadIdx.x + u * kThreads;
+      const int l = idx & 31, st = (idx >> 5) % kSteps, t2 = idx / (32 * kSteps), gg = l >> 2;
+      const int d0 = 128 * (st >> 3) + 32 * (l & 3) + 4 * (st & 7);
+      qv[u][0] = qrow(16 * t2 + gg, d0);
+      qv[u][1] = qrow(16 * t2 + gg + 8, d0);
+    }
+#pragma unroll
+    for (int u = 0; u < kFragLoads; ++u) {
+      const int idx = (int)threadIdx.x + u * kThreads;
+      const int l = idx & 31, st = (idx >> 5) % kSteps, t2 = idx / (32 * kSteps);
+      const float4 r0 = qv[u][0], r1 = qv[u][1];
+      const float v[8] = {r0.x, r0.y, r1.x, r1.y, r0.z, r0.w, r1.z, r1.w};
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const __half h0 = __float2half_rn(v[2 * j]), h1 = __float2half_rn(v[2 * j + 1]);
+        hi[j] = pack_f16x2(__half2float(h0), __half2float(h1));
+        lo[j] = pack_f16x2(v[2 * j] - __half2float(h0), v[2 * j + 1] - __half2float(h1));
+      }
+      sm.qf[t2][0][st][l] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+      sm.qf[t2][1][st][l] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
   }
   __syncthreads();
   const int mt = warp & 1, kq = warp >> 1;   // this warp's query rows 16 mt .. + 15 and chunk keys 16 kq .. + 15
+  // per-row factor of a raw score: the int8 path's digit unit times the softmax scale, the FP8 path's scale alone
+  const float rf0 = I8 ? sm.qfac[16 * mt + (lane >> 2)] * a.scale : a.scale;
+  const float rf1 = I8 ? sm.qfac[16 * mt + (lane >> 2) + 8] * a.scale : a.scale;
   const bool active = (16 * mt) / group < m;   // its query rows hold at least one activation row
   // the activation rows of this lane's two query rows and their positions
   const int arow0 = (16 * mt + g) / group, arow1 = (16 * mt + g + 8) / group;
@@ -204,37 +287,71 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
   // 4 tq + {0, 1}, k = 2 tq + 8 + {0, 1} keys 4 tq + {2, 3}. The score tile T (n8) column 2 tq + c is then key
   // 4 tq + 2 T + c, and the K row that lane g supplies to tile T is key 4 ((g >> 1) & 3) + 2 T + (g & 1).
   auto chunk = [&](const Stage<D>& stg, int64_t c0) {
-    // ---- S = Q K^T over 2 n8 tiles x kSteps k16 steps, q = hi + lo ----
-    float s[2][4], sl[2][4];   // the hi and lo products accumulate apart (shorter dependency chains)
+    float s[2][4];   // raw scores of 2 n8 tiles: x rf (row) x the key's K scale below
+    if constexpr (I8) {
+      // ---- S = Q K^T on the int8 codes: 2 n8 tiles x D / 32 k32 steps x (hi, lo) digits, exact in int32 ----
+      int ch[2][4], cl[2][4];
 #pragma unroll
-    for (int T = 0; T < 2; ++T) s[T][0] = s[T][1] = s[T][2] = s[T][3] = sl[T][0] = sl[T][1] = sl[T][2] = sl[T][3] = 0.f;
+      for (int T = 0; T < 2; ++T) ch[T][0] = ch[T][1] = ch[T][2] = ch[T][3] = cl[T][0] = cl[T][1] = cl[T][2] = cl[T][3] = 0;
 #pragma unroll
-    for (int hs = 0; hs < D / 64; ++hs) {   // dims 128 (hs >> 1) + 32 tq + 16 (hs & 1) .. + 15: steps 4 hs .. + 3
-      uint4 kw[2];
-#pragma unroll
-      for (int T = 0; T < 2; ++T) {
-        const int key = 16 * kq + 4 * ((g >> 1) & 3) + 2 * T + (g & 1);
-        kw[T] = *reinterpret_cast<const uint4*>(stg.k + key * D + 128 * (hs >> 1) +
-                                                16 * ((2 * tq + (hs & 1)) ^ swz_k(key)));
-      }
-#pragma unroll
-      for (int sub = 0; sub < 4; ++sub) {
-        const int st = 4 * hs + sub;
-        const uint4 qh = sm.qf[mt][0][st][lane], ql = sm.qf[mt][1][st][lane];
+      for (int hs = 0; hs < D / 128; ++hs) {   // a 128-dim half: lane tq's 32 bytes of a K row, units 2 tq, 2 tq + 1
+        uint4 kw[2][2];
 #pragma unroll
         for (int T = 0; T < 2; ++T) {
-          const uint32_t word = sub == 0 ? kw[T].x : sub == 1 ? kw[T].y : sub == 2 ? kw[T].z : kw[T].w;
-          uint32_t b0, b1;
-          codes_to_f16(word, a.dtype, b0, b1);
-          mma_f16(s[T], qh.x, qh.y, qh.z, qh.w, b0, b1);
-          mma_f16(sl[T], ql.x, ql.y, ql.z, ql.w, b0, b1);
+          const int key = 16 * kq + 4 * ((g >> 1) & 3) + 2 * T + (g & 1);
+          const uint8_t* row = stg.k + key * D + 128 * hs;
+          kw[T][0] = *reinterpret_cast<const uint4*>(row + 16 * ((2 * tq) ^ swz_k(key)));
+          kw[T][1] = *reinterpret_cast<const uint4*>(row + 16 * ((2 * tq + 1) ^ swz_k(key)));
+        }
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) {   // k32 step 4 hs + sub: bytes 8 sub .. + 7 of the lane's 32
+          const uint4 qh = qi[mt][0][4 * hs + sub][lane], ql = qi[mt][1][4 * hs + sub][lane];
+#pragma unroll
+          for (int T = 0; T < 2; ++T) {
+            const uint4& w = kw[T][sub >> 1];
+            const uint32_t b0 = (sub & 1) ? w.z : w.x, b1 = (sub & 1) ? w.w : w.y;
+            mma_s8(ch[T], qh, b0, b1);
+            mma_s8(cl[T], ql, b0, b1);
+          }
         }
       }
+#pragma unroll
+      for (int T = 0; T < 2; ++T)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[T][c] = __int2float_rn(254 * ch[T][c] + cl[T][c]);   // |.| < 2^31
+    } else {
+      // ---- S = Q K^T over 2 n8 tiles x kSteps k16 steps, q = hi + lo ----
+      float sl[2][4];   // the hi and lo products accumulate apart (shorter dependency chains)
+#pragma unroll
+      for (int T = 0; T < 2; ++T) s[T][0] = s[T][1] = s[T][2] = s[T][3] = sl[T][0] = sl[T][1] = sl[T][2] = sl[T][3] = 0.f;
+#pragma unroll
+      for (int hs = 0; hs < D / 64; ++hs) {   // dims 128 (hs >> 1) + 32 tq + 16 (hs & 1) .. + 15: steps 4 hs .. + 3
+        uint4 kw[2];
+#pragma unroll
+        for (int T = 0; T < 2; ++T) {
+          const int key = 16 * kq + 4 * ((g >> 1) & 3) + 2 * T + (g & 1);
+          kw[T] = *reinterpret_cast<const uint4*>(stg.k + key * D + 128 * (hs >> 1) +
+                                                  16 * ((2 * tq + (hs & 1)) ^ swz_k(key)));
+        }
+#pragma unroll
+        for (int sub = 0; sub < 4; ++sub) {
+          const int st = 4 * hs + sub;
+          const uint4 qh = sm.qf[mt][0][st][lane], ql = sm.qf[mt][1][st][lane];
+#pragma unroll
+          for (int T = 0; T < 2; ++T) {
+            const uint32_t word = sub == 0 ? kw[T].x : sub == 1 ? kw[T].y : sub == 2 ? kw[T].z : kw[T].w;
+            uint32_t b0, b1;
+            codes_to_f16(word, (int)kKvFp8, b0, b1);
+            mma_f16(s[T], qh.x, qh.y, qh.z, qh.w, b0, b1);
+            mma_f16(sl[T], ql.x, ql.y, ql.z, ql.w, b0, b1);
+          }
+        }
+      }
+#pragma unroll
+      for (int T = 0; T < 2; ++T)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[T][c] += sl[T][c];
     }
-#pragma unroll
-    for (int T = 0; T < 2; ++T)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) s[T][c] += sl[T][c];
     // ---- scale, mask, online softmax: s[T][c] (row g) and s[T][2 + c] (row g + 8) are key 16 kq + 4 tq + 2 T + c ----
     const float4 kq4 = *reinterpret_cast<const float4*>(stg.ks + 16 * kq + 4 * tq);
     const float4 vq4 = *reinterpret_cast<const float4*>(stg.vs + 16 * kq + 4 * tq);
@@ -257,9 +374,8 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
         const bool ok = p >= 0 && p < pos0;
         const bool vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
         const bool vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
-        const float f = ksc[kk] * a.scale;
-        s[T][c] = vis0 ? s[T][c] * f : -INFINITY;
-        s[T][2 + c] = vis1 ? s[T][2 + c] * f : -INFINITY;
+        s[T][c] = vis0 ? s[T][c] * (ksc[kk] * rf0) : -INFINITY;
+        s[T][2 + c] = vis1 ? s[T][2 + c] * (ksc[kk] * rf1) : -INFINITY;
         mx0 = fmaxf(mx0, s[T][c]);
         mx1 = fmaxf(mx1, s[T][2 + c]);
       }
@@ -308,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
       const int d = 8 * dt + g;
       const uint32_t w = *reinterpret_cast<const uint32_t*>(stg.v + d * 64 + 16 * (kq ^ ((d >> 1) & 3)) + 4 * tq);
       uint32_t b0, b1;
-      codes_to_f16(w, a.dtype, b0, b1);
+      codes_to_f16(w, I8 ? (int)kKvInt8 : (int)kKvFp8, b0, b1);
       mma_f16(acc[dt], pa[0], pa[1], pa[2], pa[3], b0, b1);
     }
   };
@@ -695,11 +811,14 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
               "attention: split range outside 0..splits_total (at most 256)");
   if (a.head_dim == 0) a.head_dim = 128;
   XTG_REQUIRE(a.head_dim == 128 || a.head_dim == 256, "attention: head_dim 128 or 256");
-  const bool d256 = a.head_dim == 256;
-  const void* fn = d256 ? (const void*)attention_kernel<256> : (const void*)attention_kernel<128>;
+  XTG_REQUIRE(a.dtype == kKvInt8 || a.dtype == kKvFp8, "attention: KV dtype int8 (0) or fp8 (1)");
+  const bool d256 = a.head_dim == 256, i8 = a.dtype == kKvInt8;
+  // one kernel per (head dim, KV dtype): the int8 cache's QK^T runs on integer MMAs
+  void (*const fn)(const AttnArgs) = d256 ? (i8 ? attention_kernel<256, true> : attention_kernel<256, false>)
+                                          : (i8 ? attention_kernel<128, true> : attention_kernel<128, false>);
   const int smem = d256 ? (int)sizeof(Smem<256>) : (int)sizeof(Smem<128>);
-  static std::atomic<uint64_t> optin128{0}, optin256{0};
-  ensure_smem_optin(fn, smem, d256 ? optin256 : optin128);
+  static std::atomic<uint64_t> optin[4];
+  ensure_smem_optin((const void*)fn, smem, optin[(d256 ? 2 : 0) + (i8 ? 1 : 0)]);
   cudaLaunchConfig_t cfg = {};
   XTG_REQUIRE(!a.seqs || (a.nseq >= 1 && a.nseq <= kMaxBatch && a.params), "attention: 1..8 sequences with params");
   cfg.gridDim = dim3(a.splits, a.kv_heads, a.seqs ? a.nseq : 1);
@@ -711,10 +830,7 @@ void launch_attention(const AttnArgs& a_in, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  if (d256)
-    XTG_CUDA(cudaLaunchKernelEx(&cfg, attention_kernel<256>, a));
-  else
-    XTG_CUDA(cudaLaunchKernelEx(&cfg, attention_kernel<128>, a));
+  XTG_CUDA(cudaLaunchKernelEx(&cfg, fn, a));
 }
 
 void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
