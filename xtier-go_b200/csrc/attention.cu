@@ -268,9 +268,11 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
   }
   __syncthreads();
   const int mt = warp & 1, kq = warp >> 1;   // this warp's query rows 16 mt .. + 15 and chunk keys 16 kq .. + 15
-  // per-row factor of a raw score: the int8 path's digit unit times the softmax scale, the FP8 path's scale alone
-  const float rf0 = I8 ? sm.qfac[16 * mt + (lane >> 2)] * a.scale : a.scale;
-  const float rf1 = I8 ? sm.qfac[16 * mt + (lane >> 2) + 8] * a.scale : a.scale;
+  // per-row factor of a raw score: the int8 path's digit unit times the softmax scale (the FP8 path's scale alone),
+  // times log2(e): the running max and the probabilities are kept in base 2, p = 2^(s - max) = e^(s ln 2 - max ln 2)
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float rf0 = (I8 ? sm.qfac[16 * mt + g] * a.scale : a.scale) * kLog2e;
+  const float rf1 = (I8 ? sm.qfac[16 * mt + g + 8] * a.scale : a.scale) * kLog2e;
   const bool active = (16 * mt) / group < m;   // its query rows hold at least one activation row
   // the activation rows of this lane's two query rows and their positions
   const int arow0 = (16 * mt + g) / group, arow1 = (16 * mt + g + 8) / group;
@@ -356,37 +358,53 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
     const float4 kq4 = *reinterpret_cast<const float4*>(stg.ks + 16 * kq + 4 * tq);
     const float4 vq4 = *reinterpret_cast<const float4*>(stg.vs + 16 * kq + 4 * tq);
     const float ksc[4] = {kq4.x, kq4.y, kq4.z, kq4.w}, vsc[4] = {vq4.x, vq4.y, vq4.z, vq4.w};
-    int kpos[4];
-    if (a.ring) {
-      const int4 pq = *reinterpret_cast<const int4*>(stg.pos + 16 * kq + 4 * tq);
-      kpos[0] = pq.x; kpos[1] = pq.y; kpos[2] = pq.z; kpos[3] = pq.w;
-    } else {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) kpos[r] = (int)c0 + 16 * kq + 4 * tq + r;
-    }
     float mx0 = -INFINITY, mx1 = -INFINITY;
+    if (!a.ring && a.window == 0 && c0 + 64 <= pos0) {
+      // every key of the chunk lies below pos0 and no window applies: visible to every row (rows past m hold zero
+      // queries and are never written out)
 #pragma unroll
-    for (int T = 0; T < 2; ++T) {
+      for (int T = 0; T < 2; ++T)
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int kk = 2 * T + c;
-        const int p = kpos[kk];
-        const bool ok = p >= 0 && p < pos0;
-        const bool vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
-        const bool vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
-        s[T][c] = vis0 ? s[T][c] * (ksc[kk] * rf0) : -INFINITY;
-        s[T][2 + c] = vis1 ? s[T][2 + c] * (ksc[kk] * rf1) : -INFINITY;
-        mx0 = fmaxf(mx0, s[T][c]);
-        mx1 = fmaxf(mx1, s[T][2 + c]);
+        for (int c = 0; c < 2; ++c) {
+          s[T][c] *= ksc[2 * T + c] * rf0;
+          s[T][2 + c] *= ksc[2 * T + c] * rf1;
+          mx0 = fmaxf(mx0, s[T][c]);
+          mx1 = fmaxf(mx1, s[T][2 + c]);
+        }
+    } else {
+      int kpos[4];
+      if (a.ring) {
+        const int4 pq = *reinterpret_cast<const int4*>(stg.pos + 16 * kq + 4 * tq);
+        kpos[0] = pq.x; kpos[1] = pq.y; kpos[2] = pq.z; kpos[3] = pq.w;
+      } else {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) kpos[r] = (int)c0 + 16 * kq + 4 * tq + r;
+      }
+#pragma unroll
+      for (int T = 0; T < 2; ++T) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int kk = 2 * T + c;
+          const int p = kpos[kk];
+          const bool ok = p >= 0 && p < pos0;
+          const bool vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
+          const bool vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
+          s[T][c] = vis0 ? s[T][c] * (ksc[kk] * rf0) : -INFINITY;
+          s[T][2 + c] = vis1 ? s[T][2 + c] * (ksc[kk] * rf1) : -INFINITY;
+          mx0 = fmaxf(mx0, s[T][c]);
+          mx1 = fmaxf(mx1, s[T][2 + c]);
+        }
       }
     }
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    // scores are in base-2 units: p = 2^(s - max); a row with nothing visible yet keeps max -inf, corr 1 and p 0
     const float new_m0 = fmaxf(run_m0, mx0), new_m1 = fmaxf(run_m1, mx1);
-    const float corr0 = new_m0 == -INFINITY ? 1.f : __expf(run_m0 - new_m0);
-    const float corr1 = new_m1 == -INFINITY ? 1.f : __expf(run_m1 - new_m1);
+    const float base0 = new_m0 == -INFINITY ? 0.f : new_m0, base1 = new_m1 == -INFINITY ? 0.f : new_m1;
+    const float corr0 = new_m0 == -INFINITY ? 1.f : ex2_approx(run_m0 - new_m0);
+    const float corr1 = new_m1 == -INFINITY ? 1.f : ex2_approx(run_m1 - new_m1);
     run_m0 = new_m0;
     run_m1 = new_m1;
     run_l0 *= corr0;
@@ -408,8 +426,8 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int kk = 2 * T + c;
-        p[c] = s[T][c] == -INFINITY ? 0.f : __expf(s[T][c] - new_m0);
-        p[2 + c] = s[T][2 + c] == -INFINITY ? 0.f : __expf(s[T][2 + c] - new_m1);
+        p[c] = ex2_approx(s[T][c] - base0);   // 2^-inf = 0 for a masked key
+        p[2 + c] = ex2_approx(s[T][2 + c] - base1);
         run_l0 += p[c];
         run_l1 += p[2 + c];
         p[c] *= vsc[kk];
@@ -484,13 +502,13 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
       float w[kQuarters], L = 0.f;
 #pragma unroll
       for (int q = 0; q < kQuarters; ++q) {
-        w[q] = mp[q] == -INFINITY ? 0.f : expf(mp[q] - M);
+        w[q] = mp[q] == -INFINITY ? 0.f : exp2f(mp[q] - M);   // the quarters' maxima are in base 2
         L += w[q] == 0.f ? 0.f : st0[q * ss + r * kStateStride + 1] * w[q];
       }
       const int pidx = a.part_local ? split : sidx;
       float* out = a.part + (int64_t)seq * a.part_seq_stride + (((int64_t)pidx * a.kv_heads + kvh) * kQRows + r) * kPartStride;
       if (j == 0) {
-        out[0] = M;
+        out[0] = M * 0.6931471805599453f;   // natural-log units for the combine
         out[1] = L;
       }
 #pragma unroll

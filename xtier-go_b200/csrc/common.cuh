@@ -267,6 +267,13 @@ __device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1,
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// 2^x on the special-function unit (ex2.approx, flush-to-zero; a few ulp): 2^-inf = 0
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // D = A(16x32, row) * B(32x8, col) + D, signed 8-bit inputs, exact 32-bit integer accumulation.
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
   asm volatile(
