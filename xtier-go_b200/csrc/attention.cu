@@ -12,9 +12,11 @@
 //
 // One CTA per (split of the slots, KV head), 8 warps, two CTAs per SM. Every warp takes part in every 64-slot chunk:
 // warp w takes query rows 16 (w & 1) .. +15 -- a query row is (activation row, q head of this KV head), 8 x 4 = 32
-// rows, so the 4 q heads sharing a KV head read it once -- and the chunk's keys 16 (w >> 1) .. +15, so that a chunk
-// costs each warp a quarter of its products and the chunks stream through a 4-stage ring. Each warp keeps its own
-// online-softmax state over its keys; the 4 key quarters merge at the end.
+// rows, so the 4 q heads sharing a KV head read it once. For the scores it takes the chunk's keys 16 (w >> 1) .. +15;
+// the 4 warps of a row half then share the chunk's row maxima and probabilities through shared memory, and for PV
+// each takes a quarter of the head dims over all 64 keys, so that a chunk costs each warp a quarter of its products,
+// its accumulator holds 16 rows x D / 4 dims, and the online-softmax state (running max, probability sums) is common
+// to the row half: its partial needs no merge. The chunks stream through a 4-stage ring.
 // QK^T over an int8 cache runs on mma.m16n8k32.s8 straight from the cached codes: Q (after RoPE, justnorm, q scale)
 // becomes two signed 8-bit digits per element against its row's max |q| (q = max / 127 * (hi + lo / 254), ~16
 // bits), the two integer products are exact and combine as 254 hi + lo before one conversion to FP32. Over an FP8
@@ -73,11 +75,10 @@ struct Smem {
   uint4 qf[2][2][D / 16][32];
   float qmaxp[kQRows][D / 32];    // int8 cache: a query row's max |q| over the 8-dim pieces of one k32 step
   float qfac[kQRows];             // int8 cache: a query row's digit unit, max |q| / (127 * 254)
+  float cmax[kQuarters][kQRows];  // a chunk's row maxima per key quarter
+  uint2 pbuf[2][16][16];          // a chunk's P' per row half: [row][unit of 4 keys, swizzled] as fp16
+  float lsum[kQuarters][kQRows];  // the probability sums per key quarter, at the end
 };
-// a key quarter's state after the last chunk: per query row m, l, acc[D] (rows D + 4 floats apart)
-static_assert(sizeof(Stage<128>) >= kQRows * (128 + 4) * sizeof(float), "stage too small for a quarter's state");
-static_assert(sizeof(Stage<256>) >= kQRows * (256 + 4) * sizeof(float), "stage too small for a quarter's state");
-static_assert(kStages >= kQuarters, "the quarters' states live in the stages");
 
 // Head dim 256: the same warp roles over twice the dims (16 k16 steps, 32 n8 tiles of the output); the accumulator
 // takes twice the registers and a stage twice the shared memory, so one CTA fits an SM.
@@ -85,7 +86,6 @@ template <int D, bool I8>
 __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(const AttnArgs a) {
   static_assert(D == 128 || D == 256, "head dim 128 or 256");
   constexpr int kSteps = D / 16;                          // k16 steps of QK^T
-  constexpr int kTiles = D / 8;                           // n8 tiles of the output
   constexpr int kPartStride = part_stride(D);
   extern __shared__ __align__(16) unsigned char smem_raw[];
   Smem<D>& sm = *reinterpret_cast<Smem<D>*>(smem_raw);
@@ -279,15 +279,30 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
   const int t0 = pos0 + arow0, t1 = pos0 + arow1;
   const bool live0 = arow0 < m, live1 = arow1 < m;
 
-  float acc[kTiles][4];
+  // PV role of this warp: query rows 16 mt .. + 15, head dims kDq dq .. + kDq - 1 (a quarter of the head)
+  constexpr int kDq = D / 4, kDt = kDq / 8;
+  const int dq = kq;
+  float acc[kDt][4];
 #pragma unroll
-  for (int dt = 0; dt < kTiles; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.f;
+  for (int dt = 0; dt < kDt; ++dt) acc[dt][0] = acc[dt][1] = acc[dt][2] = acc[dt][3] = 0.f;
+  // the running max of rows g and g + 8 (base 2; the same in the 4 warps of a row half, which see the same chunk
+  // maxima) and this lane's part of their probability sums (its 4 keys of every chunk)
   float run_m0 = -INFINITY, run_m1 = -INFINITY, run_l0 = 0.f, run_l1 = 0.f;
+  // the named barrier of the row half's 4 warps (1 or 2; constant ids let the CTA reserve only those)
+  auto half_bar = [&]() {
+    if (mt == 0)
+      named_bar_sync(1, 128);
+    else
+      named_bar_sync(2, 128);
+  };
 
-  // This warp's 16 keys of a chunk (slot base c0) from its stage. The MMA k index of the PV product and the keys
-  // are permuted so that lane tq owns the 4 consecutive keys 16 kq + 4 tq .. + 3: k = 2 tq + {0, 1} are keys
-  // 4 tq + {0, 1}, k = 2 tq + 8 + {0, 1} keys 4 tq + {2, 3}. The score tile T (n8) column 2 tq + c is then key
-  // 4 tq + 2 T + c, and the K row that lane g supplies to tile T is key 4 ((g >> 1) & 3) + 2 T + (g & 1).
+  // One chunk (slot base c0) from its stage. Scores and probabilities: this warp's 16 keys 16 kq .. + 15; the MMA k
+  // index and the keys are permuted so that lane tq owns the 4 consecutive keys 4 tq .. + 3 of a 16-key group:
+  // k = 2 tq + {0, 1} are keys 4 tq + {0, 1}, k = 2 tq + 8 + {0, 1} keys 4 tq + {2, 3}. The score tile T (n8)
+  // column 2 tq + c is then key 4 tq + 2 T + c, and the K row that lane g supplies to tile T is key
+  // 4 ((g >> 1) & 3) + 2 T + (g & 1). The row half's 4 warps meet twice: for the chunk's row maxima, and once every
+  // probability times V scale (P', fp16) is in shared memory, after which each warp multiplies all 64 keys' P' by V
+  // for its quarter of the head dims.
   auto chunk = [&](const Stage<D>& stg, int64_t c0) {
     float s[2][4];   // raw scores of 2 n8 tiles: x rf (row) x the key's K scale below
     if constexpr (I8) {
@@ -400,6 +415,16 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
     mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
     mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    if (tq == 0) {
+      sm.cmax[kq][16 * mt + g] = mx0;
+      sm.cmax[kq][16 * mt + g + 8] = mx1;
+    }
+    half_bar();
+#pragma unroll
+    for (int q = 0; q < kQuarters; ++q) {   // the chunk's row maxima over the 4 key quarters
+      mx0 = fmaxf(mx0, sm.cmax[q][16 * mt + g]);
+      mx1 = fmaxf(mx1, sm.cmax[q][16 * mt + g + 8]);
+    }
     // scores are in base-2 units: p = 2^(s - max); a row with nothing visible yet keeps max -inf, corr 1 and p 0
     const float new_m0 = fmaxf(run_m0, mx0), new_m1 = fmaxf(run_m1, mx1);
     const float base0 = new_m0 == -INFINITY ? 0.f : new_m0, base1 = new_m1 == -INFINITY ? 0.f : new_m1;
@@ -409,16 +434,8 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
     run_m1 = new_m1;
     run_l0 *= corr0;
     run_l1 *= corr1;
-    if (corr0 != 1.f || corr1 != 1.f) {
-#pragma unroll
-      for (int dt = 0; dt < kTiles; ++dt) {
-        acc[dt][0] *= corr0;
-        acc[dt][1] *= corr0;
-        acc[dt][2] *= corr1;
-        acc[dt][3] *= corr1;
-      }
-    }
-    // A fragment of P' (probability times V scale): a0 a1 row g k 2 tq .., a2 a3 row g + 8, a4 .. a7 the same at k + 8
+    // P' (probability times V scale) of this lane's keys 16 kq + 4 tq .. + 3 for rows g, g + 8: 8 bytes each, unit
+    // 4 kq + tq of the row stored at unit (4 kq + tq) ^ 4 (g & 3) (conflict-free stores and loads)
     uint32_t pa[4];
 #pragma unroll
     for (int T = 0; T < 2; ++T) {
@@ -436,14 +453,33 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
       pa[2 * T] = pack_f16x2(p[0], p[1]);
       pa[2 * T + 1] = pack_f16x2(p[2], p[3]);
     }
-    // ---- O += P' V: head dim d = 8 dt + g; lane tq supplies keys 16 kq + 4 tq .. + 3 (one 32-bit word) ----
+    const int pu = (4 * kq + tq) ^ (4 * (g & 3));
+    sm.pbuf[mt][g][pu] = make_uint2(pa[0], pa[2]);
+    sm.pbuf[mt][g + 8][pu] = make_uint2(pa[1], pa[3]);
+    if (corr0 != 1.f || corr1 != 1.f) {
 #pragma unroll
-    for (int dt = 0; dt < kTiles; ++dt) {
-      const int d = 8 * dt + g;
-      const uint32_t w = *reinterpret_cast<const uint32_t*>(stg.v + d * 64 + 16 * (kq ^ ((d >> 1) & 3)) + 4 * tq);
-      uint32_t b0, b1;
-      codes_to_f16(w, I8 ? (int)kKvInt8 : (int)kKvFp8, b0, b1);
-      mma_f16(acc[dt], pa[0], pa[1], pa[2], pa[3], b0, b1);
+      for (int dt = 0; dt < kDt; ++dt) {
+        acc[dt][0] *= corr0;
+        acc[dt][1] *= corr0;
+        acc[dt][2] *= corr1;
+        acc[dt][3] *= corr1;
+      }
+    }
+    half_bar();
+    // ---- O += P' V over the chunk's 64 keys (4 k16 steps) for head dims d = kDq dq + 8 dt + g: lane tq supplies
+    // keys 16 ks + 4 tq .. + 3 (one 32-bit word of V, 8 bytes of P' per row) ----
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const int u = (4 * ks + tq) ^ (4 * (g & 3));
+      const uint2 pg = sm.pbuf[mt][g][u], pg8 = sm.pbuf[mt][g + 8][u];
+#pragma unroll
+      for (int dt = 0; dt < kDt; ++dt) {
+        const int d = kDq * dq + 8 * dt + g;
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(stg.v + d * 64 + 16 * (ks ^ ((d >> 1) & 3)) + 4 * tq);
+        uint32_t b0, b1;
+        codes_to_f16(w, I8 ? (int)kKvInt8 : (int)kKvFp8, b0, b1);
+        mma_f16(acc[dt], pg.x, pg8.x, pg.y, pg8.y, b0, b1);
+      }
     }
   };
 
@@ -460,66 +496,34 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
       issue(i + kStages);
     }
   }
-  // the row sums live spread over the 4 lanes of a row
+  // ---- the CTA's partial: the row sums over the quad and the 4 key-quarter warps; each warp stores its dims ----
   run_l0 += __shfl_xor_sync(0xffffffffu, run_l0, 1);
   run_l0 += __shfl_xor_sync(0xffffffffu, run_l0, 2);
   run_l1 += __shfl_xor_sync(0xffffffffu, run_l1, 1);
   run_l1 += __shfl_xor_sync(0xffffffffu, run_l1, 2);
-
-  // ---- merge the 4 key quarters' states (each in its own stage, every chunk consumed), then the CTA's partial ----
-  // (state rows kStateStride floats apart, so that a warp's stores spread over the banks)
-  constexpr int kStateStride = D + 4;   // m, l, acc[D], pad
-  __syncthreads();
-  {
-    float* st = reinterpret_cast<float*>(&sm.stage[kq]);
-    const int qr0 = 16 * mt + g, qr1 = qr0 + 8;
-    if (tq == 0) {
-      st[qr0 * kStateStride] = run_m0;
-      st[qr0 * kStateStride + 1] = run_l0;
-      st[qr1 * kStateStride] = run_m1;
-      st[qr1 * kStateStride + 1] = run_l1;
-    }
-#pragma unroll
-    for (int dt = 0; dt < kTiles; ++dt) {
-      const int d = 8 * dt + 2 * tq;
-      *reinterpret_cast<float2*>(&st[qr0 * kStateStride + 2 + d]) = make_float2(acc[dt][0], acc[dt][1]);
-      *reinterpret_cast<float2*>(&st[qr1 * kStateStride + 2 + d]) = make_float2(acc[dt][2], acc[dt][3]);
-    }
+  if (active && tq == 0) {
+    sm.lsum[kq][16 * mt + g] = run_l0;
+    sm.lsum[kq][16 * mt + g + 8] = run_l1;
   }
   __syncthreads();
-  {
-    // thread: query row r, head dims j, j + 8, ...: a warp's stores cover 4 rows x 8 consecutive dims
-    const int r = threadIdx.x >> 3, j = threadIdx.x & 7;
-    if (r / group < m) {
-      const float* st0 = reinterpret_cast<const float*>(&sm.stage[0]);
-      const int ss = (int)(sizeof(Stage<D>) / sizeof(float));
-      float mp[kQuarters], M = -INFINITY;
+  if (active) {
+    const int pidx = a.part_local ? split : sidx;
 #pragma unroll
-      for (int q = 0; q < kQuarters; ++q) {
-        mp[q] = st0[q * ss + r * kStateStride];
-        M = fmaxf(M, mp[q]);
-      }
-      float w[kQuarters], L = 0.f;
+    for (int h = 0; h < 2; ++h) {   // rows g and g + 8 of the row half
+      const int r = 16 * mt + g + 8 * h;
+      if (r / group >= m) continue;
+      float L = 0.f;
 #pragma unroll
-      for (int q = 0; q < kQuarters; ++q) {
-        w[q] = mp[q] == -INFINITY ? 0.f : exp2f(mp[q] - M);   // the quarters' maxima are in base 2
-        L += w[q] == 0.f ? 0.f : st0[q * ss + r * kStateStride + 1] * w[q];
-      }
-      const int pidx = a.part_local ? split : sidx;
+      for (int q = 0; q < kQuarters; ++q) L += sm.lsum[q][r];
       float* out = a.part + (int64_t)seq * a.part_seq_stride + (((int64_t)pidx * a.kv_heads + kvh) * kQRows + r) * kPartStride;
-      if (j == 0) {
-        out[0] = M * 0.6931471805599453f;   // natural-log units for the combine
+      if (dq == 0 && tq == 0) {
+        out[0] = (h ? run_m1 : run_m0) * 0.6931471805599453f;   // natural-log units for the combine
         out[1] = L;
       }
 #pragma unroll
-      for (int k = 0; k < D / 8; ++k) {
-        const int d = j + 8 * k;
-        float o = 0.f;
-#pragma unroll
-        for (int q = 0; q < kQuarters; ++q)
-          if (w[q] != 0.f) o += st0[q * ss + r * kStateStride + 2 + d] * w[q];
-        out[4 + d] = o;
-      }
+      for (int dt = 0; dt < kDt; ++dt)
+        *reinterpret_cast<float2*>(out + 4 + kDq * dq + 8 * dt + 2 * tq) =
+            h ? make_float2(acc[dt][2], acc[dt][3]) : make_float2(acc[dt][0], acc[dt][1]);
     }
   }
 }

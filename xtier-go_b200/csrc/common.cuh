@@ -153,6 +153,11 @@ __device__ __forceinline__ float take_seq_word(const uint64_t* p, uint32_t seq, 
   return __uint_as_float((uint32_t)w);
 }
 
+// A named barrier over `threads` threads (a multiple of 32) of the CTA; barrier 0 is __syncthreads'.
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
