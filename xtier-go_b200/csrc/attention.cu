@@ -69,7 +69,8 @@ struct Stage {                    // one 64-slot chunk of one KV head, as it lie
 template <int D>
 struct Smem {
   Stage<D> stage[kStages];        // the chunk ring; after the last chunk, key quarter j's softmax state in stage[j]
-  uint64_t full[kStages], empty[kStages];
+  uint64_t full[kStages];
+  int released[kStages];          // warps done with the stage's current chunk (the last one refills it)
   // Q A fragments. FP8 cache: [m-tile][hi, lo][k16 step][lane], q = hi + lo, both fp16. Int8 cache: the first half
   // as [m-tile][hi, lo][k32 step][lane] of signed 8-bit digits (qi below).
   uint4 qf[2][2][D / 16][32];
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], kThreads / 32);
+      sm.released[s] = 0;
     }
     mbar_init_fence();
   }
@@ -483,17 +484,24 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
     }
   };
 
-  // every warp takes its part of every chunk; warp 0 refills a stage once all 8 warps are done with it
+  // every warp takes its part of every chunk; the last warp done with a stage refills it (nobody waits for it)
   for (int i = 0; i < nc; ++i) {
     const int s = i % kStages;
     mbar_wait_bounded(&sm.full[s], (uint32_t)(i / kStages) & 1u, lane == 0 ? a.err : nullptr);
     if (active) chunk(sm.stage[s], (cb + i) * 64);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sm.empty[s]);
-    if (warp == 0 && i + kStages < nc) {
-      mbar_wait_bounded(&sm.empty[s], (uint32_t)(i / kStages) & 1u, lane == 0 ? a.err : nullptr);
-      fence_proxy_async_smem();
-      issue(i + kStages);
+    if (i + kStages < nc) {
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        __threadfence_block();   // this warp's reads of the stage are ordered before its release
+        last = atomicAdd(&sm.released[s], 1) == kThreads / 32 - 1;
+        if (last) {
+          sm.released[s] = 0;
+          __threadfence_block();
+          fence_proxy_async_smem();   // the other warps' reads before the bulk copies that overwrite the stage
+        }
+      }
+      if (__shfl_sync(0xffffffffu, last, 0)) issue(i + kStages);
     }
   }
   // ---- the CTA's partial: the row sums over the quad and the 4 key-quarter warps; each warp stores its dims ----
