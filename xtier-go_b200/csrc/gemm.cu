@@ -215,15 +215,14 @@ __global__ void __launch_bounds__(kGThreads, 1) gemm_kernel(const __grid_constan
       float y[kActRows];
       const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16);
 #pragma unroll
-      for (int d = 0; d < kGDigits; ++d) {
+      for (int d = 0; d < kGDigits; ++d) {   // a digit's 64 columns in four loads and one wait
+        float v[kActRows];
 #pragma unroll
-        for (int c = 0; c < kActRows; c += 16) {
-          float v[16];
-          tmem_ld16(taddr + (uint32_t)(kActRows * d + c), v);
-          tmem_ld_wait();
+        for (int c = 0; c < kActRows; c += 16)
+          tmem_ld16(taddr + (uint32_t)(kActRows * d + c), *reinterpret_cast<float(*)[16]>(&v[c]));
+        tmem_ld_wait();
 #pragma unroll
-          for (int ii = 0; ii < 16; ++ii) y[c + ii] = d == 0 ? v[ii] : y[c + ii] + v[ii];
-        }
+        for (int ii = 0; ii < kActRows; ++ii) y[ii] = d == 0 ? v[ii] : y[ii] + v[ii];
       }
       tc_fence_before();
       mbar_arrive(&accempty[acc]);   // the next tile's products may start
