@@ -942,12 +942,13 @@ def main():
     ap.add_argument("--ncu-attn", type=int, default=0,
                     help="profiling driver: config-2 global attention (int8 KV, L = 32768, 49 splits) this many "
                          "times, then exit")
+    ap.add_argument("--ncu-attn-len", type=int, default=32768, help="cached positions of --ncu-attn (a multiple of 64)")
     args = ap.parse_args()
     if args.ncu_attn:
         import torch
         x = package()
         g = torch.Generator(device="cuda").manual_seed(2)
-        kvh, heads, slots = 6, 24, 32768
+        kvh, heads, slots = 6, 24, args.ncu_attn_len
         q, k, v = (torch.nn.functional.normalize(torch.randn(8, h, 128, device="cuda", generator=g), dim=-1)
                    for h in (heads, kvh, kvh))
         kc = torch.randint(-127, 128, (kvh * slots * 128,), dtype=torch.int8, device="cuda", generator=g)
