@@ -371,18 +371,20 @@ def test_forward_batch_batched_step(cuda, xtg, cfg, hd):
 
 @pytest.mark.parametrize("hd", [128, 256])
 def test_prompt_chunks_match_oracle_and_verify_steps(cuda, xtg, cfg, hd):
-    """A forward of more than decode_rows tokens runs prompt chunks of up to 64 rows through the batched step: 8-row
-    groups of the session, group g attending the cache up to its own first row (the earlier groups' keys among them,
-    stored by the same step) and its own rows as this call's keys -- the arithmetic of 8-row verify steps. 100 tokens (a
-    chunk of 64, one of 36) within the step tolerance of the oracle stepped 8 rows at a time (identical argmax), and of
-    the same tokens in the session's 8-row verify steps (batch=0); the position and the next verify step agree too.
-    At head_dim 128 and 256."""
+    """A forward of more than decode_rows tokens runs prompt chunks of up to 64 rows through the batched step, with
+    the arithmetic of the reference's multi-row attention (packs/dory/dory.cpp:825-929 attend_rows,
+    engine/src/kv.cpp:166-286): every row attends the cache below the chunk's first position and the chunk's own rows
+    up to itself, unquantized. 100 tokens (a chunk of 64, one of 36) within the step tolerance of the oracle run on
+    the same chunks (identical argmax); the same tokens as the session's 8-row verify steps (batch=0) against the
+    oracle stepped 8 rows at a time; the position and the next verify step agree too. At head_dim 128 and 256."""
     cfg = dict(cfg, head_dim=hd)
     toks = [(37 * i + 11) % cfg["vocab"] for i in range(100)]
-    ref = O.SynthDory(cfg, ctx=512, n_prefill=70)
-    want = np.concatenate([ref.step(toks[o:o + 8]) for o in range(0, 100, 8)])
-    nxt_want = ref.step([5, 6, 7, 8])
-    ref.close()
+    wants, nxts = {}, {}
+    for name, cuts in (("chunks", (0, 64, 100)), ("steps", tuple(range(0, 100, 8)) + (100,))):
+        ref = O.SynthDory(cfg, ctx=512, n_prefill=70)
+        wants[name] = np.concatenate([ref.step(toks[o:e]) for o, e in zip(cuts, cuts[1:])])
+        nxts[name] = ref.step([5, 6, 7, 8])
+        ref.close()
     with xtg.Session(cfg, context=512) as a, xtg.Session(cfg, context=512, batch=0) as b:
         assert a.info()["prefill_ar"] == 64
         a.prefill_synthetic(70)
@@ -390,16 +392,16 @@ def test_prompt_chunks_match_oracle_and_verify_steps(cuda, xtg, cfg, hd):
         ga = logits_of(a.forward(toks, want=2), 100)
         gb = logits_of(b.forward(toks, want=2), 100)
         assert a.pos() == b.pos() == 170
-        for got in (ga, gb):
+        for got, want in ((ga, wants["chunks"]), (gb, wants["steps"])):
             assert np.array_equal(got.argmax(1), want.argmax(1))
             assert np.abs(got - want).max() <= LOGIT_TOL, np.abs(got - want).max()
-        assert a.argmax(8)[:4] == list(want[96:].argmax(1))
+        assert a.argmax(8)[:4] == list(wants["chunks"][96:].argmax(1))
         last = a.forward(toks[:1], want=1)   # one more row: a single verify step after the chunks
         assert sorted(last) == [0]
         assert a.rewind(170) and b.rewind(170)   # the oracle's state: 170 positions
         na = logits_of(a.forward([5, 6, 7, 8], want=2), 4)
         nb = logits_of(b.forward([5, 6, 7, 8], want=2), 4)
-        for got in (na, nb):
-            assert np.array_equal(got.argmax(1), nxt_want.argmax(1))
-            assert np.abs(got - nxt_want).max() <= LOGIT_TOL
+        for got, want in ((na, nxts["chunks"]), (nb, nxts["steps"])):
+            assert np.array_equal(got.argmax(1), want.argmax(1))
+            assert np.abs(got - want).max() <= LOGIT_TOL
         assert a.pos() == 174

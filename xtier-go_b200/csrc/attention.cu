@@ -97,6 +97,8 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
   const KvSeq* sq = a.seqs ? a.seqs + seq : nullptr;
   const int m = prm ? prm->m : a.m;
   const int pos0 = (int)(prm ? prm->pos0 : a.pos0);   // positions stay below 2^31
+  // the cached keys this call reads lie below kend (a prompt chunk's earlier groups come in as own keys instead)
+  const int kend = pos0 - (prm ? prm->own_rows : 0);
   const int64_t slots = sq ? sq->slots : a.slots;
   const int group = a.heads / a.kv_heads;
   const int32_t* ring_pos = sq ? sq->ring_pos : a.ring_pos;
@@ -106,7 +108,7 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
   if (m <= 0) return;
 
   // this CTA's 64-slot chunks: a global cache holds [0, pos0), a ring every slot
-  const int64_t span = a.ring ? slots : pos0;
+  const int64_t span = a.ring ? slots : kend;
   const int64_t nchunks = (span + 63) / 64;
   const int stot = a.splits_total > 0 ? a.splits_total : a.splits, sidx = a.split0 + split;
   const int64_t cb = nchunks * sidx / stot, ce = nchunks * (sidx + 1) / stot;
@@ -375,8 +377,8 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
     const float4 vq4 = *reinterpret_cast<const float4*>(stg.vs + 16 * kq + 4 * tq);
     const float ksc[4] = {kq4.x, kq4.y, kq4.z, kq4.w}, vsc[4] = {vq4.x, vq4.y, vq4.z, vq4.w};
     float mx0 = -INFINITY, mx1 = -INFINITY;
-    if (!a.ring && a.window == 0 && c0 + 64 <= pos0) {
-      // every key of the chunk lies below pos0 and no window applies: visible to every row (rows past m hold zero
+    if (!a.ring && a.window == 0 && c0 + 64 <= kend) {
+      // every key of the chunk lies below kend and no window applies: visible to every row (rows past m hold zero
       // queries and are never written out)
 #pragma unroll
       for (int T = 0; T < 2; ++T)
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(kThreads, D == 128 ? 2 : 1) attention_kernel(c
         for (int c = 0; c < 2; ++c) {
           const int kk = 2 * T + c;
           const int p = kpos[kk];
-          const bool ok = p >= 0 && p < pos0;
+          const bool ok = p >= 0 && p < kend;
           const bool vis0 = live0 && ok && (a.window == 0 || t0 - p < a.window);
           const bool vis1 = live1 && ok && (a.window == 0 || t1 - p < a.window);
           s[T][c] = vis0 ? s[T][c] * (ksc[kk] * rf0) : -INFINITY;
@@ -552,6 +554,7 @@ __global__ void __launch_bounds__(D) attn_combine_kernel(const CombineArgs a) {
   // the gate's scale is a parameter: loaded before the dependency wait
   const float gsc = a.out ? 0.f : a.gscale[col];
   const int m = a.params ? a.params[seq].m : a.m;
+  const int own0 = a.params ? a.params[seq].own_rows : 0;   // the sequence's earlier rows of this step
   const int64_t rows0 = (int64_t)seq * kMaxRows;   // this sequence's first activation row
   if (a.pdl) {
     pdl_wait();
@@ -686,6 +689,44 @@ __global__ void __launch_bounds__(D) attn_combine_kernel(const CombineArgs a) {
     lcached = l;
     o = oo;
   }
+  // a prompt chunk's earlier groups (every row before this one, within the window), scored in FP32 like the own
+  // keys: blocks of 8 keys folded into the cached part (max wgt_max, sum lcached, output o) before this group's keys
+  for (int jb = 0; jb < own0; jb += kMaxRows) {
+    float kb[kMaxRows], vb[kMaxRows], prod[kMaxRows];
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) {
+      const int64_t r = rows0 - own0 + jb + j;
+      kb[j] = a.k[(r * a.kv_heads + kvh) * D + d];
+      vb[j] = a.v[(r * a.kv_heads + kvh) * D + d];
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) prod[j] = warp_sum(qd * kb[j]);
+    __syncthreads();   // every thread has read part_s's previous sums
+    if ((d & 31) == 0)
+#pragma unroll
+      for (int j = 0; j < kMaxRows; ++j) part_s[d >> 5][j] = prod[j];
+    __syncthreads();
+    float sj[kMaxRows], bm = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) {
+      float pr = (part_s[0][j] + part_s[1][j]) + (part_s[2][j] + part_s[3][j]);
+      if constexpr (D == 256) pr += (part_s[4][j] + part_s[5][j]) + (part_s[6][j] + part_s[7][j]);
+      const bool vis = a.window == 0 || own0 + i - (jb + j) < a.window;
+      sj[j] = vis ? pr * a.scale : -INFINITY;
+      bm = fmaxf(bm, sj[j]);
+    }
+    const float nm = fmaxf(wgt_max, bm);
+    const float cw = wgt_max == -INFINITY ? 0.f : expf(wgt_max - nm);
+    lcached *= cw;
+    o *= cw;
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) {
+      const float pj = sj[j] == -INFINITY ? 0.f : expf(sj[j] - nm);
+      lcached += pj;
+      o += pj * vb[j];
+    }
+    wgt_max = nm;
+  }
   const float mall = fmaxf(own_m, wgt_max);
   const float cs = wgt_max == -INFINITY ? 0.f : expf(wgt_max - mall);   // the cached part's weight
   // merge the cached part (relative to wgt_max) and the own keys (relative to mall)
@@ -747,6 +788,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(c
   // the gate's scale is a parameter: loaded before the dependency wait
   const float4 gsc = exists ? ld4g(a.gscale + col) : make_float4(0.f, 0.f, 0.f, 0.f);
   const int m = exists ? (a.params ? a.params[seq].m : a.m) : 0;
+  const int own0 = exists && a.params ? a.params[seq].own_rows : 0;   // the sequence's earlier rows of this step
   const int64_t rows0 = (int64_t)seq * kMaxRows;
   if (a.pdl) {
     pdl_wait();
@@ -785,31 +827,49 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(c
       o.w += acc[s].w * ws;
     }
   }
-  // this call's own keys j <= i, scored in FP32 from the prepared rows (the reference attends to them unquantized)
-  float own_s[kMaxRows], own_m = -INFINITY;
+  // this call's own keys, scored in FP32 from the prepared rows (the reference attends to them unquantized): a
+  // prompt chunk's earlier groups (every row before this one, within the window), then this group's rows j <= i;
+  // each block of 8 keys is folded into the running (max, sum, output), starting from the cached part's
+  float mall = M, lsum = lcached;
+  auto fold = [&](const float4 (&kb)[kMaxRows], const float4 (&vb)[kMaxRows], int jb, int nvis) {
+    // keys jb .. jb + 7 of the sequence's step rows; the first nvis are candidates; this row is own0 + i
+    float sj[kMaxRows], bm = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kMaxRows; ++j) {
-    const float pr = warp_sum(dot4(q4, kj[j]));
-    const bool vis = j < m && j <= i && (a.window == 0 || i - j < a.window);
-    own_s[j] = vis ? pr * a.scale : -INFINITY;
-    own_m = fmaxf(own_m, own_s[j]);
-  }
-  const float mall = fmaxf(own_m, M);
-  const float cs = M == -INFINITY ? 0.f : expf(M - mall);   // the cached part's weight
-  float lsum = lcached * cs;
-  o.x *= cs;
-  o.y *= cs;
-  o.z *= cs;
-  o.w *= cs;
+    for (int j = 0; j < kMaxRows; ++j) {
+      const float pr = warp_sum(dot4(q4, kb[j]));
+      const bool vis = j < nvis && jb + j <= own0 + i && (a.window == 0 || own0 + i - (jb + j) < a.window);
+      sj[j] = vis ? pr * a.scale : -INFINITY;
+      bm = fmaxf(bm, sj[j]);
+    }
+    const float nm = fmaxf(mall, bm);
+    const float cs = mall == -INFINITY ? 0.f : expf(mall - nm);   // the part folded so far
+    lsum *= cs;
+    o.x *= cs;
+    o.y *= cs;
+    o.z *= cs;
+    o.w *= cs;
 #pragma unroll
-  for (int j = 0; j < kMaxRows; ++j) {
-    const float pj = own_s[j] == -INFINITY ? 0.f : expf(own_s[j] - mall);
-    lsum += pj;
-    o.x += pj * vj[j].x;
-    o.y += pj * vj[j].y;
-    o.z += pj * vj[j].z;
-    o.w += pj * vj[j].w;
+    for (int j = 0; j < kMaxRows; ++j) {
+      const float pj = sj[j] == -INFINITY ? 0.f : expf(sj[j] - nm);
+      lsum += pj;
+      o.x += pj * vb[j].x;
+      o.y += pj * vb[j].y;
+      o.z += pj * vb[j].z;
+      o.w += pj * vb[j].w;
+    }
+    mall = nm;
+  };
+  for (int jb = 0; jb < own0; jb += kMaxRows) {   // the earlier groups: whole blocks of 8 rows
+    float4 kb[kMaxRows], vb[kMaxRows];
+#pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) {
+      const int64_t r = rows0 - own0 + jb + j;
+      kb[j] = ld4g(a.k + (r * a.kv_heads + kvh) * kD + d0);
+      vb[j] = ld4g(a.v + (r * a.kv_heads + kvh) * kD + d0);
+    }
+    fold(kb, vb, jb, kMaxRows);
   }
+  fold(kj, vj, own0, m);
   const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
   float v[4] = {o.x * inv, o.y * inv, o.z * inv, o.w * inv};
   const float gtv[4] = {gt.x, gt.y, gt.z, gt.w}, gsv[4] = {gsc.x, gsc.y, gsc.z, gsc.w};

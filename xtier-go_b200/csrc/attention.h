@@ -32,7 +32,9 @@ __host__ __device__ __forceinline__ int64_t v_offset(int h, int d, int64_t slot,
 struct StepParams {
   int32_t tokens[8];
   int32_t m;
-  int32_t pad;
+  // this sequence's rows of the step before these m (a prompt chunk's earlier 8-row groups; 0 in a verify step): the
+  // cache is read below pos0 - own_rows, and those rows' keys are this call's own keys, scored unquantized
+  int32_t own_rows;
   int64_t pos0;
 };
 

@@ -1699,7 +1699,9 @@ struct BatchStep {
       at.err = dev_err;
       at.seqs = kvseq + (size_t)E.cache * S;
       at.nseq = S;
-      at.late_copies = distinct ? 0 : 1;   // a prompt chunk: the earlier groups' keys come from qkv_prep just before
+      // a prompt chunk reads its cache below the chunk's first position only (own_rows): nothing this step writes,
+      // so its copies go out before the dependency wait too
+      at.late_copies = 0;
       at.l2_first = (!ring && c.l2_first) ? 1 : 0;
       at.part_seq_stride = attention_part_floats(c.kv_heads, std::max(splits_g, splits_r), c.head_dim);
       at.head_dim = c.head_dim;
@@ -1818,10 +1820,11 @@ BatchStep* batch_for(const std::vector<xtg_cuda*>& key) {
 
 // Prompt chunks through the batched step: the chunk's rows as kMaxBatch groups of 8 of one session, group g at
 // position n_past + 8 g, every group over the session's own caches. The projections of all the chunk's rows are one
-// GEMM each; the keys and values of all of them are stored before any attention of the step runs, so group g attends
-// the cache up to its own first row (the earlier groups' rows included) and its own rows as this call's keys. A ring
-// holds the window plus its slack: the chunk's new rows overwrite only slots of positions the window has left, so a
-// chunk is at most the slack (64 for the 1088-slot ring over a window of 1024).
+// GEMM each. As attend_rows (packs/dory/dory.cpp:825-929) and the CPU path's multi-row attention (engine/src/kv.cpp:
+// 166-286) do, every row attends the cache below the chunk's first position and the chunk's own rows up to itself,
+// scored unquantized from the prepared rows: group g has own_rows = 8 g, and the combine folds the earlier groups'
+// keys before its own. A ring holds the window plus its slack: the chunk's new rows overwrite only slots of
+// positions the window has left, so a chunk is at most the slack (64 for the 1088-slot ring over a window of 1024).
 int prefill_rows(const xtg_cuda* h) {
   const Config& c = h->c;
   if (!c.batch || !c.graph || c.kv_world != 1 || h->head_w_bf16) return 0;   // the batched step's head is NVFP4
@@ -1840,6 +1843,9 @@ void prefill_chunk(xtg_cuda* h, const int32_t* tokens, int m, int want, int off,
     for (int r = 0; r < mg; ++r) p.tokens[r] = tokens[kMaxRows * g + r];
     p.m = mg;
     p.pos0 = h->n_past + kMaxRows * g;
+    // the chunk's earlier rows are this group's own keys (packs/dory/dory.cpp:825-929, attend_rows: keys below the
+    // chunk's first position from the cache, the chunk's own rows unquantized)
+    p.own_rows = kMaxRows * g;
   }
   b->capture();
   XTG_CUDA(cudaGraphLaunch(b->exec, b->stream));
