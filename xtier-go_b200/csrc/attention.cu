@@ -700,7 +700,8 @@ __global__ void __launch_bounds__(D) attn_combine_kernel(const CombineArgs a) {
       vb[j] = a.v[(r * a.kv_heads + kvh) * D + d];
     }
 #pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) prod[j] = warp_sum(qd * kb[j]);
+    for (int j = 0; j < kMaxRows; ++j) prod[j] = qd * kb[j];
+    warp_sum8(prod);
     __syncthreads();   // every thread has read part_s's previous sums
     if ((d & 31) == 0)
 #pragma unroll
@@ -835,10 +836,12 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(c
     // keys jb .. jb + 7 of the sequence's step rows; the first nvis are candidates; this row is own0 + i
     float sj[kMaxRows], bm = -INFINITY;
 #pragma unroll
+    for (int j = 0; j < kMaxRows; ++j) sj[j] = dot4(q4, kb[j]);
+    warp_sum8(sj);
+#pragma unroll
     for (int j = 0; j < kMaxRows; ++j) {
-      const float pr = warp_sum(dot4(q4, kb[j]));
       const bool vis = j < nvis && jb + j <= own0 + i && (a.window == 0 || own0 + i - (jb + j) < a.window);
-      sj[j] = vis ? pr * a.scale : -INFINITY;
+      sj[j] = vis ? sj[j] * a.scale : -INFINITY;
       bm = fmaxf(bm, sj[j]);
     }
     const float nm = fmaxf(mall, bm);

@@ -325,6 +325,26 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// Sums of 8 values over the warp, each total returned in every lane: a transposing reduction (halves of the set
+// exchanged at lane offsets 16, 8, 4 -- lane l then holds value (l >> 2) & 7 over 8 lanes --, a butterfly over the
+// last 4 lanes, then a broadcast from lane 4 j): 17 shuffles where 8 butterflies take 40.
+__device__ __forceinline__ void warp_sum8(float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+  float a4[4], a2[2];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)   // value k + 4 b4
+    a4[k] = (b4 ? v[k + 4] : v[k]) + __shfl_xor_sync(0xffffffffu, b4 ? v[k] : v[k + 4], 16);
+#pragma unroll
+  for (int k = 0; k < 2; ++k)   // value k + 2 b3 + 4 b4
+    a2[k] = (b3 ? a4[k + 2] : a4[k]) + __shfl_xor_sync(0xffffffffu, b3 ? a4[k] : a4[k + 2], 8);
+  float a1 = (b2 ? a2[1] : a2[0]) + __shfl_xor_sync(0xffffffffu, b2 ? a2[0] : a2[1], 4);   // value (lane >> 2) & 7
+  a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
+  a1 += __shfl_xor_sync(0xffffffffu, a1, 1);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = __shfl_sync(0xffffffffu, a1, 4 * j);
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
