@@ -778,6 +778,7 @@ constexpr int kCombineWarps = 8;
 __device__ __forceinline__ float4 ld4g(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ float dot4(float4 a, float4 b) { return (a.x * b.x + a.y * b.y) + (a.z * b.z + a.w * b.w); }
 
+template <bool kPrompt>
 __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(const CombineArgs a) {
   constexpr int kD = 128, kPartStride = part_stride(kD);   // head dim 128
   const int lane = threadIdx.x & 31;
@@ -789,7 +790,8 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(c
   // the gate's scale is a parameter: loaded before the dependency wait
   const float4 gsc = exists ? ld4g(a.gscale + col) : make_float4(0.f, 0.f, 0.f, 0.f);
   const int m = exists ? (a.params ? a.params[seq].m : a.m) : 0;
-  const int own0 = exists && a.params ? a.params[seq].own_rows : 0;   // the sequence's earlier rows of this step
+  // the sequence's earlier rows of this step (a prompt chunk only: the verify path keeps its registers)
+  const int own0 = kPrompt && exists && a.params ? a.params[seq].own_rows : 0;
   const int64_t rows0 = (int64_t)seq * kMaxRows;
   if (a.pdl) {
     pdl_wait();
@@ -828,51 +830,79 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(c
       o.w += acc[s].w * ws;
     }
   }
-  // this call's own keys, scored in FP32 from the prepared rows (the reference attends to them unquantized): a
-  // prompt chunk's earlier groups (every row before this one, within the window), then this group's rows j <= i;
-  // each block of 8 keys is folded into the running (max, sum, output), starting from the cached part's
   float mall = M, lsum = lcached;
-  auto fold = [&](const float4 (&kb)[kMaxRows], const float4 (&vb)[kMaxRows], int jb, int nvis) {
-    // keys jb .. jb + 7 of the sequence's step rows; the first nvis are candidates; this row is own0 + i
-    float sj[kMaxRows], bm = -INFINITY;
+  if constexpr (kPrompt) {
+    // this call's own keys, scored in FP32 from the prepared rows (the reference attends to them unquantized): a
+    // prompt chunk's earlier groups (every row before this one, within the window), then this group's rows j <= i;
+    // each block of 8 keys is folded into the running (max, sum, output), starting from the cached part's
+    auto fold = [&](const float4 (&kb)[kMaxRows], const float4 (&vb)[kMaxRows], int jb, int nvis) {
+      // keys jb .. jb + 7 of the sequence's step rows; the first nvis are candidates; this row is own0 + i
+      float sj[kMaxRows], bm = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) sj[j] = dot4(q4, kb[j]);
-    warp_sum8(sj);
+      for (int j = 0; j < kMaxRows; ++j) sj[j] = dot4(q4, kb[j]);
+      warp_sum8(sj);
+#pragma unroll
+      for (int j = 0; j < kMaxRows; ++j) {
+        const bool vis = j < nvis && jb + j <= own0 + i && (a.window == 0 || own0 + i - (jb + j) < a.window);
+        sj[j] = vis ? sj[j] * a.scale : -INFINITY;
+        bm = fmaxf(bm, sj[j]);
+      }
+      const float nm = fmaxf(mall, bm);
+      const float cs = mall == -INFINITY ? 0.f : expf(mall - nm);   // the part folded so far
+      lsum *= cs;
+      o.x *= cs;
+      o.y *= cs;
+      o.z *= cs;
+      o.w *= cs;
+#pragma unroll
+      for (int j = 0; j < kMaxRows; ++j) {
+        const float pj = sj[j] == -INFINITY ? 0.f : expf(sj[j] - nm);
+        lsum += pj;
+        o.x += pj * vb[j].x;
+        o.y += pj * vb[j].y;
+        o.z += pj * vb[j].z;
+        o.w += pj * vb[j].w;
+      }
+      mall = nm;
+    };
+    for (int jb = 0; jb < own0; jb += kMaxRows) {   // the earlier groups: whole blocks of 8 rows
+      float4 kb[kMaxRows], vb[kMaxRows];
+#pragma unroll
+      for (int j = 0; j < kMaxRows; ++j) {
+        const int64_t r = rows0 - own0 + jb + j;
+        kb[j] = ld4g(a.k + (r * a.kv_heads + kvh) * kD + d0);
+        vb[j] = ld4g(a.v + (r * a.kv_heads + kvh) * kD + d0);
+      }
+      fold(kb, vb, jb, kMaxRows);
+    }
+    fold(kj, vj, own0, m);
+  } else {
+    // this call's own keys j <= i, scored in FP32 from the prepared rows (the reference attends to them unquantized)
+    float own_s[kMaxRows], own_m = -INFINITY;
 #pragma unroll
     for (int j = 0; j < kMaxRows; ++j) {
-      const bool vis = j < nvis && jb + j <= own0 + i && (a.window == 0 || own0 + i - (jb + j) < a.window);
-      sj[j] = vis ? sj[j] * a.scale : -INFINITY;
-      bm = fmaxf(bm, sj[j]);
+      const float pr = warp_sum(dot4(q4, kj[j]));
+      const bool vis = j < m && j <= i && (a.window == 0 || i - j < a.window);
+      own_s[j] = vis ? pr * a.scale : -INFINITY;
+      own_m = fmaxf(own_m, own_s[j]);
     }
-    const float nm = fmaxf(mall, bm);
-    const float cs = mall == -INFINITY ? 0.f : expf(mall - nm);   // the part folded so far
-    lsum *= cs;
+    mall = fmaxf(own_m, M);
+    const float cs = M == -INFINITY ? 0.f : expf(M - mall);   // the cached part's weight
+    lsum = lcached * cs;
     o.x *= cs;
     o.y *= cs;
     o.z *= cs;
     o.w *= cs;
 #pragma unroll
     for (int j = 0; j < kMaxRows; ++j) {
-      const float pj = sj[j] == -INFINITY ? 0.f : expf(sj[j] - nm);
+      const float pj = own_s[j] == -INFINITY ? 0.f : expf(own_s[j] - mall);
       lsum += pj;
-      o.x += pj * vb[j].x;
-      o.y += pj * vb[j].y;
-      o.z += pj * vb[j].z;
-      o.w += pj * vb[j].w;
+      o.x += pj * vj[j].x;
+      o.y += pj * vj[j].y;
+      o.z += pj * vj[j].z;
+      o.w += pj * vj[j].w;
     }
-    mall = nm;
-  };
-  for (int jb = 0; jb < own0; jb += kMaxRows) {   // the earlier groups: whole blocks of 8 rows
-    float4 kb[kMaxRows], vb[kMaxRows];
-#pragma unroll
-    for (int j = 0; j < kMaxRows; ++j) {
-      const int64_t r = rows0 - own0 + jb + j;
-      kb[j] = ld4g(a.k + (r * a.kv_heads + kvh) * kD + d0);
-      vb[j] = ld4g(a.v + (r * a.kv_heads + kvh) * kD + d0);
-    }
-    fold(kb, vb, jb, kMaxRows);
   }
-  fold(kj, vj, own0, m);
   const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
   float v[4] = {o.x * inv, o.y * inv, o.z * inv, o.w * inv};
   const float gtv[4] = {gt.x, gt.y, gt.z, gt.w}, gsv[4] = {gsc.x, gsc.y, gsc.z, gsc.w};
@@ -957,7 +987,10 @@ void launch_attn_combine(const CombineArgs& a_in, cudaStream_t s, bool pdl) {
     const int wpc = std::max(1, std::min(kCombineWarps, pairs / std::max(1, sms)));
     cfg.gridDim = dim3((unsigned)((pairs + wpc - 1) / wpc));
     cfg.blockDim = dim3(wpc * 32);
-    XTG_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_warp_kernel, a));
+    if (a.prompt)
+      XTG_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_warp_kernel<true>, a));
+    else
+      XTG_CUDA(cudaLaunchKernelEx(&cfg, attn_combine_warp_kernel<false>, a));
     return;
   }
   cfg.gridDim = dim3(kMaxRows, a.heads, a.gated_out ? a.nseq : 1);

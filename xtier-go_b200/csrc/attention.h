@@ -129,6 +129,7 @@ struct CombineArgs {
   int nseq;
   int64_t part_seq_stride;
   int head_dim;             // D: 128 (0 reads as 128) or 256
+  int prompt;               // the batched step of a prompt chunk: the sequences' own_rows may be non-zero
 };
 
 // CTAs of the attention kernel that fit on one SM at head dim D (2 at 128, 1 at 256)

@@ -1724,6 +1724,7 @@ struct BatchStep {
       cb.asum_ld = kRows;
       cb.gated_out = att;
       cb.nseq = S;
+      cb.prompt = distinct ? 0 : 1;
       cb.part_seq_stride = at.part_seq_stride;
       cb.err = dev_err;
       cb.head_dim = c.head_dim;
