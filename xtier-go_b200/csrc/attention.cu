@@ -803,17 +803,24 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(c
   const int64_t sstride = (int64_t)a.kv_heads * kQRows * kPartStride;
   const float ms = lane < a.splits ? base[lane * sstride] : -INFINITY;
   const float ls = lane < a.splits ? base[lane * sstride + 1] : 0.f;
+  // verify rows: every load in one wave up front; a prompt chunk (which also folds the earlier groups' keys) loads
+  // the split partials and its own rows where it uses them, to keep its registers down
   float4 acc[kWarpSplits];
+  if constexpr (!kPrompt) {
 #pragma unroll
-  for (int s = 0; s < kWarpSplits; ++s)
-    acc[s] = s < a.splits ? ld4g(base + s * sstride + 4 + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < kWarpSplits; ++s)
+      acc[s] = s < a.splits ? ld4g(base + s * sstride + 4 + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   const float4 q4 = ld4g(a.q + ((rows0 + i) * a.heads + h) * kD + d0);
   float4 kj[kMaxRows], vj[kMaxRows];
+  auto load_own = [&]() {
 #pragma unroll
-  for (int j = 0; j < kMaxRows; ++j) {
-    kj[j] = j < m ? ld4g(a.k + ((rows0 + j) * a.kv_heads + kvh) * kD + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
-    vj[j] = j < m ? ld4g(a.v + ((rows0 + j) * a.kv_heads + kvh) * kD + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+    for (int j = 0; j < kMaxRows; ++j) {
+      kj[j] = j < m ? ld4g(a.k + ((rows0 + j) * a.kv_heads + kvh) * kD + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
+      vj[j] = j < m ? ld4g(a.v + ((rows0 + j) * a.kv_heads + kvh) * kD + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  if constexpr (!kPrompt) load_own();
   const float4 gt = ld4g(a.gate + (rows0 + i) * a.gate_ld + col);
   // split weights exp(m_s - M) and sum_s l_s exp(m_s - M); the dims' sum in split order
   const float M = warp_max(ms);
@@ -824,10 +831,11 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(c
   for (int s = 0; s < kWarpSplits; ++s) {
     const float ws = __shfl_sync(0xffffffffu, w, s);
     if (s < a.splits) {
-      o.x += acc[s].x * ws;
-      o.y += acc[s].y * ws;
-      o.z += acc[s].z * ws;
-      o.w += acc[s].w * ws;
+      const float4 as = kPrompt ? ld4g(base + s * sstride + 4 + d0) : acc[s];
+      o.x += as.x * ws;
+      o.y += as.y * ws;
+      o.z += as.z * ws;
+      o.w += as.w * ws;
     }
   }
   float mall = M, lsum = lcached;
@@ -875,6 +883,7 @@ __global__ void __launch_bounds__(kCombineWarps * 32) attn_combine_warp_kernel(c
       }
       fold(kb, vb, jb, kMaxRows);
     }
+    load_own();
     fold(kj, vj, own0, m);
   } else {
     // this call's own keys j <= i, scored in FP32 from the prepared rows (the reference attends to them unquantized)
