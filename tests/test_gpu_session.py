@@ -369,15 +369,16 @@ def test_forward_batch_batched_step(cuda, xtg, cfg, hd):
                 s.close()
 
 
-@pytest.mark.parametrize("hd", [128, 256])
-def test_prompt_chunks_match_oracle_and_verify_steps(cuda, xtg, cfg, hd):
+@pytest.mark.parametrize("hd,window", [(128, 64), (256, 64), (128, 24)])
+def test_prompt_chunks_match_oracle_and_verify_steps(cuda, xtg, cfg, hd, window):
     """A forward of more than decode_rows tokens runs prompt chunks of up to 64 rows through the batched step, with
     the arithmetic of the reference's multi-row attention (packs/dory/dory.cpp:825-929 attend_rows,
     engine/src/kv.cpp:166-286): every row attends the cache below the chunk's first position and the chunk's own rows
     up to itself, unquantized. 100 tokens (a chunk of 64, one of 36) within the step tolerance of the oracle run on
     the same chunks (identical argmax); the same tokens as the session's 8-row verify steps (batch=0) against the
-    oracle stepped 8 rows at a time; the position and the next verify step agree too. At head_dim 128 and 256."""
-    cfg = dict(cfg, head_dim=hd)
+    oracle stepped 8 rows at a time; the position and the next verify step agree too. At head_dim 128 and 256, and
+    with a window of 24 (the same 128-slot ring), where a chunk's later rows no longer see its first ones."""
+    cfg = dict(cfg, head_dim=hd, window=window)
     toks = [(37 * i + 11) % cfg["vocab"] for i in range(100)]
     wants, nxts = {}, {}
     for name, cuts in (("chunks", (0, 64, 100)), ("steps", tuple(range(0, 100, 8)) + (100,))):
