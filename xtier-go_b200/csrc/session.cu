@@ -329,6 +329,8 @@ struct xtg_cuda {
   ArgCand* cand = nullptr;
   int* dev_err = nullptr;   // bounded device waits that gave up (never expected)
   int* err_host = nullptr;  // pinned copy of dev_err
+  // forward(): the error word's copy and each logits row's, so that a row's callback runs while later rows copy
+  cudaEvent_t err_ev = nullptr, row_ev[kMaxRows] = {};
   int splits_g = 1, splits_r = 1;
   int proj_ld = 0;
   ncclComm_t comm = nullptr;   // split-KV only
@@ -375,6 +377,9 @@ struct xtg_cuda {
     if (params_host) cudaFreeHost(params_host);
     if (logits_host) cudaFreeHost(logits_host);
     if (err_host) cudaFreeHost(err_host);
+    if (err_ev) cudaEventDestroy(err_ev);
+    for (cudaEvent_t e : row_ev)
+      if (e) cudaEventDestroy(e);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -840,6 +845,8 @@ struct xtg_cuda {
     dev_err = dalloc<int>(1);
     XTG_CUDA(cudaMallocHost(&err_host, sizeof(int)));
     *err_host = 0;
+    XTG_CUDA(cudaEventCreateWithFlags(&err_ev, cudaEventDisableTiming));
+    for (cudaEvent_t& e : row_ev) XTG_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     // the attention runs 2 CTAs per SM (1 at head dim 256): a global cache over every CTA slot, a ring one 64-slot
     // chunk per CTA
     const int per_sm = attention_ctas_per_sm(c.head_dim);
@@ -1258,17 +1265,23 @@ struct xtg_cuda {
     set_params(tokens + off, m);
     launch_step();
     const int r0 = want == 2 ? 0 : (want == 1 && off + m == n ? m - 1 : m);
-    if (r0 < m && copy)
-      XTG_CUDA(cudaMemcpyAsync(logits_host + (size_t)r0 * c.vocab, logits + (size_t)r0 * c.vocab,
-                               (size_t)(m - r0) * c.vocab * sizeof(float), cudaMemcpyDeviceToHost, stream));
+    // the error word first, then each row with its own event: the callback of a row runs while the next copies
     XTG_CUDA(cudaMemcpyAsync(err_host, dev_err, sizeof(int), cudaMemcpyDeviceToHost, stream));
+    XTG_CUDA(cudaEventRecord(err_ev, stream));
+    if (copy)
+      for (int r = r0; r < m; ++r) {
+        XTG_CUDA(cudaMemcpyAsync(logits_host + (size_t)r * c.vocab, logits + (size_t)r * c.vocab,
+                                 (size_t)c.vocab * sizeof(float), cudaMemcpyDeviceToHost, stream));
+        XTG_CUDA(cudaEventRecord(row_ev[r], stream));
+      }
     return Chunk{off, m, r0};
   }
 
-  // false: a bounded device wait gave up, the step's results are not to be trusted (not committed)
+  // false: a bounded device wait gave up, the step's results are not to be trusted (not committed, no callback)
   bool finish_chunk(const Chunk& k, xtg_cuda_logits_fn fn, void* user, int row_base) {
-    XTG_CUDA(cudaStreamSynchronize(stream));
+    XTG_CUDA(cudaEventSynchronize(err_ev));
     if (*err_host) {
+      XTG_CUDA(cudaStreamSynchronize(stream));   // the row copies in flight
       *err_host = 0;
       XTG_CUDA(cudaMemsetAsync(dev_err, 0, sizeof(int), stream));
       return false;
@@ -1276,7 +1289,10 @@ struct xtg_cuda {
     commit(k.m);
     last_rows = k.m;
     if (fn)
-      for (int i = k.r0; i < k.m; ++i) fn(row_base + k.off + i, logits_host + (size_t)i * c.vocab, user);
+      for (int i = k.r0; i < k.m; ++i) {
+        XTG_CUDA(cudaEventSynchronize(row_ev[i]));
+        fn(row_base + k.off + i, logits_host + (size_t)i * c.vocab, user);
+      }
     return true;
   }
 
